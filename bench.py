@@ -1,0 +1,521 @@
+"""bench.py -- KDA / MLA attention hot path on B200, one process per GPU.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--workload decode|prefill|varlen|mla]
+                    [--impl ours|reference]
+
+Default workload (the headline): one KDA recurrent decode token for
+B=256 sequences x H=32 heads, d_k=d_v=128, bf16 q/k/v/o, fp32 state [256,32,128,128]
+resident in HBM (537 MB read and written per step, larger than L2, so no flush is needed
+between steps). A step is one decode token for the whole batch. Metric: tokens/s.
+Multi-GPU: every rank runs its own 256 sequences (weak scaling, no collective);
+value = all ranks' tokens / max-over-ranks device time.
+
+Other workloads (for the per-path records; one JSON line each):
+  prefill  BASELINE config 2: T=32768, H=32, d=128, chunk 64 (tokens/s)
+  varlen   BASELINE config 3: 16 sequences ~U[512,8192], H=64, heads sharded over the
+           ranks, then the all-gather of the [sum T, 64*128] bf16 output (tokens/s)
+  mla      BASELINE config 4: B=64, ctx 8192, 128 heads, latent 512 + rope 64 (tokens/s)
+
+--impl reference times the reference's own C implementation (oracle/_ref/libk3ref.so:
+the unmodified k3_ops.c) on the host cores for the same workload; rank 0 only.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+sys.path.insert(0, os.path.join(ROOT, "kimi-k3-in-c_b200"))
+
+import workloads as W  # noqa: E402
+
+# Algorithmic bytes per unit (one step of each workload); derivation in DESIGN.md.
+DECODE_B, DECODE_H, DECODE_D = 256, 32, 128
+
+
+def decode_bytes(B, H, d):
+    state = 2 * B * H * d * d * 4            # fp32 state read + written
+    qkv = 3 * B * H * d * 2                  # bf16 q, k, v
+    gate = B * H * d * 4 + B * H * 4         # fp32 g and beta
+    out = B * H * d * 2                      # bf16 o
+    return state + qkv + gate + out
+
+
+def prefill_bytes(T, H, d):
+    return 3 * T * H * d * 2 + T * H * d * 4 + T * H * 4 + T * H * d * 2
+
+
+def mla_bytes(B, ctx, H):
+    return (B * ctx * 512 * 2 + B * ctx * 64 * 2 + 2 * H * 128 * 512 * 2 + B * H * 192 * 2
+            + B * H * 128 * 2)
+
+
+def mla_flops(B, ctx, H):
+    return 2 * B * H * (128 * 512 + ctx * 576 + ctx * 512 + 512 * 128)
+
+
+def peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            p = json.load(f)
+        return float(p["hbm_gbs"]), float(p["bf16_tflops"]), "measured"
+    except Exception:
+        return 6650.0, 1590.0, "fallback"
+
+
+def profile_traffic(name):
+    """dram bytes per launch recorded from an ncu capture in profiles/<name> (or None)."""
+    path = os.path.join(ROOT, "profiles", name)
+    try:
+        with open(path) as f:
+            for line in f:
+                if line.strip().startswith("traffic_bytes_per_launch:"):
+                    return float(line.split(":", 1)[1].split()[0])
+    except OSError:
+        pass
+    return None
+
+
+# ------------------------------------------------------------------------ clocks
+class ClockSampler:
+    """nvidia-smi samples of SM clock and throttle reasons during the timed region."""
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device):
+        self.device = device
+        self.proc = None
+        self.lines = []
+        self.t = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "100", "-i", str(self.device)], stdout=subprocess.PIPE,
+                stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except OSError:
+            self.proc = None
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append((time.time(), line.strip()))
+
+    def mark(self):
+        return time.time()
+
+    def stop(self, t0, t1):
+        if not self.proc:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        time.sleep(0.25)
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        rows = [ln for (ts, ln) in self.lines if t0 - 0.15 <= ts <= t1 + 0.15] or \
+            [ln for (_, ln) in self.lines]
+        sm, smax, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in rows:
+            parts = [p.strip() for p in ln.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                smax.append(float(parts[2]))
+            except ValueError:
+                continue
+            for nm, val in zip(names, parts[5:9]):
+                if val.lower().startswith("active"):
+                    reasons.add(nm)
+        return {"sm_mhz": statistics.median(sm) if sm else None,
+                "sm_max_mhz": max(smax) if smax else None, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+# ------------------------------------------------------------------- distributed
+class Dist:
+    def __init__(self):
+        self.world = int(os.environ.get("WORLD_SIZE", "1"))
+        self.rank = int(os.environ.get("RANK", "0"))
+        self.local = int(os.environ.get("LOCAL_RANK", "0"))
+        self.pg = None
+        if self.world > 1:
+            import datetime
+            import torch.distributed as dist
+            dist.init_process_group("gloo", timeout=datetime.timedelta(seconds=300))
+            self.dist = dist
+
+    def barrier(self):
+        if self.world > 1:
+            self.dist.barrier()
+
+    def max(self, x: float) -> float:
+        if self.world == 1:
+            return x
+        import torch
+        t = torch.tensor([x], dtype=torch.float64)
+        self.dist.all_reduce(t, op=self.dist.ReduceOp.MAX)
+        return float(t.item())
+
+    def bcast_bytes(self, b: bytes | None) -> bytes:
+        if self.world == 1:
+            return b
+        obj = [b]
+        self.dist.broadcast_object_list(obj, src=0)
+        return obj[0]
+
+    def close(self):
+        if self.world > 1:
+            self.dist.barrier()
+            self.dist.destroy_process_group()
+
+
+# ---------------------------------------------------------------- cpu baseline
+def cpu_decode_baseline(B, H, d, budget_s=6.0):
+    """The reference's k3_kda_step (oracle/_ref, unmodified k3_ops.c) over the config-1
+    batch on all host cores, repeated for about budget_s seconds."""
+    from oracle import oracle
+    if not oracle.ref_available():
+        return None
+    c = W.kda_config1(B=B, H=H, d=d)
+    nth = oracle.ref().k3ref_max_threads()
+    S = c["state"].copy()
+    oracle.kda_decode(S[:1], c["q"][:1], c["k"][:1], c["v"][:1], c["g"][:1], c["beta"][:1],
+                      use_ref=True, nthreads=nth)
+    steps, t0 = 0, time.perf_counter()
+    while True:
+        _, S = oracle.kda_decode(S, c["q"], c["k"], c["v"], c["g"], c["beta"], use_ref=True,
+                                 nthreads=nth)
+        steps += 1
+        el = time.perf_counter() - t0
+        if el >= budget_s:
+            break
+    return {"value": B * steps / el, "unit": "tokens/s", "cores": nth, "kind": "reference",
+            "sample": f"{steps} full config-1 decode steps (B={B}, H={H}, d={d}) through the "
+                      f"reference k3_kda_step, OpenMP over the {B * H} (sequence, head) streams"}
+
+
+# ----------------------------------------------------------------------- decode
+def bench_decode(args, D: Dist):
+    import k3cuda
+    ctx = k3cuda.Context(D.local)
+    B, H, d = DECODE_B, DECODE_H, DECODE_D
+    c = W.kda_config1(seed=D.rank, B=B, H=H, d=d)
+    qs = 1.0 / np.sqrt(np.float32(d))
+    bf = W.f32_to_bf16
+    dS = ctx.upload(c["state"])
+    dq, dk, dv = ctx.upload(bf(c["q"])), ctx.upload(bf(c["k"])), ctx.upload(bf(c["v"]))
+    dg, db = ctx.upload(c["g"]), ctx.upload(c["beta"])
+    do = ctx.empty((B, H, d), np.uint16)
+
+    def step():
+        ctx.kda_decode(dS, do, dq, dk, dv, dg, db, B, H, d, d, qs)
+
+    for _ in range(args.warmup):
+        step()
+    ctx.sync()
+    clk = ClockSampler(D.local)
+    clk.start()
+    time.sleep(0.3)
+    D.barrier()
+    ctx.sync()
+    l0 = ctx.launches()
+    t0 = clk.mark()
+    ctx.record(0)
+    for _ in range(args.steps):
+        step()
+    ctx.record(1)
+    ctx.sync()
+    t1 = clk.mark()
+    D.barrier()
+    l1 = ctx.launches()
+    ms = ctx.elapsed_ms(0, 1)
+    ms_max = D.max(ms)
+    clocks = clk.stop(t0, t1)
+
+    # e2e: host buffers (page-locked), copies in the timed region every step
+    hq, hk, hv = (ctx.pinned((B, H, d), np.uint16) for _ in range(3))
+    hg = ctx.pinned((B, H, d), np.float32)
+    hb = ctx.pinned((B, H), np.float32)
+    ho = ctx.pinned((B, H, d), np.uint16)
+    hq[...], hk[...], hv[...], hg[...], hb[...] = bf(c["q"]), bf(c["k"]), bf(c["v"]), c["g"], c["beta"]
+    L = k3cuda.lib()
+    h2d = [(dq, hq), (dk, hk), (dv, hv), (dg, hg), (db, hb)]
+    bi = sum(h.nbytes for _, h in h2d)
+    bo = ho.nbytes
+
+    def e2e_step():
+        for dbuf, h in h2d:
+            k3cuda.check(L.k3cuda_memcpy_h2d(ctx.h, dbuf.ptr, h.ctypes.data, h.nbytes))
+        step()
+        k3cuda.check(L.k3cuda_memcpy_d2h(ctx.h, ho.ctypes.data, do.ptr, bo))
+
+    for _ in range(max(1, args.warmup)):
+        e2e_step()
+    ctx.sync()
+    D.barrier()
+    ctx.record(2)
+    for _ in range(args.steps):
+        e2e_step()
+    ctx.record(3)
+    ctx.sync()
+    D.barrier()
+    ms_e2e = D.max(ctx.elapsed_ms(2, 3))
+
+    hbm, tf, src = peaks()
+    per_launch_s = ms_max / 1e3 / args.steps
+    alg = decode_bytes(B, H, d)
+    achieved = alg / per_launch_s / 1e9
+    toks = B * args.steps * D.world
+    line = {
+        "metric": "KDA recurrent decode tokens/s (BASELINE config 1: B=256, H=32, d=128)",
+        "value": toks / (ms_max / 1e3), "unit": "tokens/s", "n_gpus": D.world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_max / args.steps,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "fp32",
+        "data": "synthetic (seeded numpy: BASELINE config-1 distributions)",
+        "config": {"workload": "kda_decode_config1", "batch_per_gpu": B, "heads": H,
+                   "d_k": d, "d_v": d, "io": "bf16 q/k/v/o, fp32 g/beta/state",
+                   "parallelism": f"seq-shard x{D.world} (no collective)",
+                   "l2": "inputs larger than L2 (537 MB fp32 state per GPU)"},
+        "e2e": {"value": toks / (ms_e2e / 1e3), "unit": "tokens/s", "h2d_bytes_per_step": bi,
+                "d2h_bytes_per_step": bo},
+        "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s",
+                     "frac": achieved / hbm, "peak_source": src,
+                     "traffic": profile_traffic("kda_decode_config1.md"),
+                     "algorithmic_bytes_per_launch": alg},
+        "gpu_launches": int(l1 - l0),
+        "clocks": clocks,
+    }
+    ctx.close()
+    return line
+
+
+# ---------------------------------------------------------------------- prefill
+def bench_prefill(args, D: Dist, varlen: bool):
+    import k3cuda
+    ctx = k3cuda.Context(D.local)
+    if varlen:
+        c = W.kda_config3()
+        H_total, d = 64, 128
+    else:
+        c = W.kda_config2()
+        H_total, d = 32, 128
+    cu = c["cu_seqlens"]
+    T = int(cu[-1])
+    R = D.world if varlen else 1
+    Hl = H_total // R
+    hs = slice(D.rank * Hl, (D.rank + 1) * Hl) if varlen else slice(0, H_total)
+    bf = W.f32_to_bf16
+    q, k, v = (np.ascontiguousarray(c[x][:, hs]) for x in ("q", "k", "v"))
+    g, beta = np.ascontiguousarray(c["g"][:, hs]), np.ascontiguousarray(c["beta"][:, hs])
+    dq, dk, dv = ctx.upload(bf(q)), ctx.upload(bf(k)), ctx.upload(bf(v))
+    dg, db = ctx.upload(g), ctx.upload(beta)
+    nseq = len(cu) - 1
+    dS = ctx.empty((nseq, Hl, d, d), np.float32)
+    do = ctx.empty((T, Hl, d), np.uint16)
+    nws = ctx.kda_prefill_workspace(cu, Hl, d, d)
+    ws = ctx.empty((nws,), np.uint8)
+    qs = 1.0 / np.sqrt(np.float32(d))
+    gather = varlen and R > 1
+    if gather:
+        uid = D.bcast_bytes(k3cuda.comm_unique_id() if D.rank == 0 else None)
+        ctx.comm_init(R, D.rank, uid)
+        nag = ctx.allgather_heads_workspace(R, T, Hl, d)
+        agws = ctx.empty((nag,), np.uint8)
+        dfull = ctx.empty((T, H_total, d), np.uint16)
+
+    def step():
+        dS.zero()
+        ctx.kda_prefill(dS, do, dq, dk, dv, dg, db, cu, Hl, d, d, qs, ws, nws)
+        if gather:
+            ctx.allgather_heads(dfull, do, T, Hl, d, agws, nag)
+
+    for _ in range(args.warmup):
+        step()
+    ctx.sync()
+    clk = ClockSampler(D.local)
+    clk.start()
+    time.sleep(0.3)
+    D.barrier()
+    ctx.sync()
+    l0 = ctx.launches()
+    t0 = clk.mark()
+    ctx.record(0)
+    for _ in range(args.steps):
+        step()
+    ctx.record(1)
+    ctx.sync()
+    t1 = clk.mark()
+    D.barrier()
+    ms_max = D.max(ctx.elapsed_ms(0, 1))
+    clocks = clk.stop(t0, t1)
+    hbm, tf, src = peaks()
+    alg = prefill_bytes(T, Hl, d)
+    per = ms_max / 1e3 / args.steps
+    name = "kda_prefill_config3" if varlen else "kda_prefill_config2"
+    line = {
+        "metric": f"KDA chunked prefill tokens/s ({name})", "value": T * args.steps / (ms_max / 1e3),
+        "unit": "tokens/s", "n_gpus": D.world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": ms_max / args.steps, "higher_is_better": True,
+        "scaling": "strong" if varlen else "weak", "vs_baseline": None, "dtype": "fp32",
+        "data": "synthetic (seeded numpy: BASELINE config distributions)",
+        "config": {"workload": name, "tokens": T, "heads_total": H_total, "heads_per_gpu": Hl,
+                   "d": d, "chunk": 64, "parallelism": f"head-shard x{R}" if varlen else "replica",
+                   "allgather": bool(gather), "l2": "inputs larger than L2"},
+        "roofline": {"bound": "hbm", "achieved": alg / per / 1e9, "peak": hbm, "unit": "GB/s",
+                     "frac": alg / per / 1e9 / hbm, "peak_source": src, "traffic": None,
+                     "algorithmic_bytes_per_launch": alg},
+        "gpu_launches": int(ctx.launches() - l0), "clocks": clocks,
+    }
+    ctx.close()
+    return line
+
+
+# -------------------------------------------------------------------------- mla
+def bench_mla(args, D: Dist):
+    import k3cuda
+    ctx = k3cuda.Context(D.local)
+    B, ctxlen, H = 64, 8192, 128
+    c = W.mla_config4(seed=D.rank, B=B, ctx=ctxlen, H=H)
+    d = [ctx.upload(c[x]) for x in ("q_nope", "q_rope", "latent", "rope", "w_uk", "w_uv")]
+    out = ctx.empty((B, H, 128), np.uint16)
+    nws = ctx.mla_decode_workspace(c["ctx_lens"], H)
+    ws = ctx.empty((nws,), np.uint8)
+
+    def step():
+        ctx.mla_decode(out, *d, c["ctx_lens"], ctxlen, H, c["scale"], ws, nws,
+                       out_dtype=k3cuda.BF16)
+
+    for _ in range(args.warmup):
+        step()
+    ctx.sync()
+    clk = ClockSampler(D.local)
+    clk.start()
+    time.sleep(0.3)
+    D.barrier()
+    ctx.sync()
+    l0 = ctx.launches()
+    t0 = clk.mark()
+    ctx.record(0)
+    for _ in range(args.steps):
+        step()
+    ctx.record(1)
+    ctx.sync()
+    t1 = clk.mark()
+    D.barrier()
+    ms_max = D.max(ctx.elapsed_ms(0, 1))
+    clocks = clk.stop(t0, t1)
+    hbm, tf, src = peaks()
+    per = ms_max / 1e3 / args.steps
+    alg = mla_bytes(B, ctxlen, H)
+    line = {
+        "metric": "MLA absorbed decode tokens/s (BASELINE config 4)",
+        "value": B * args.steps * D.world / (ms_max / 1e3), "unit": "tokens/s",
+        "n_gpus": D.world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": ms_max / args.steps, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic (seeded numpy: BASELINE config-4 distributions)",
+        "config": {"workload": "mla_decode_config4", "batch_per_gpu": B, "ctx": ctxlen,
+                   "heads": H, "parallelism": f"batch-shard x{D.world}",
+                   "l2": "inputs larger than L2 (604 MB latent+rope cache)"},
+        "roofline": {"bound": "hbm", "achieved": alg / per / 1e9, "peak": hbm, "unit": "GB/s",
+                     "frac": alg / per / 1e9 / hbm, "peak_source": src, "traffic": None,
+                     "algorithmic_bytes_per_launch": alg,
+                     "tensor_tflops": mla_flops(B, ctxlen, H) / per / 1e12},
+        "gpu_launches": int(ctx.launches() - l0), "clocks": clocks,
+    }
+    ctx.close()
+    return line
+
+
+# -------------------------------------------------------------- reference arm
+def bench_reference(args, D: Dist):
+    """The reference's own C (oracle/_ref/libk3ref.so, unmodified k3_ops.c) on the host
+    cores, same workload, metric and unit as our arm. Rank 0 only."""
+    from oracle import oracle
+    if not oracle.ref_available():
+        return {"impl": "reference", "unavailable": "oracle/_ref/libk3ref.so was not built"}
+    B, H, d = DECODE_B, DECODE_H, DECODE_D
+    c = W.kda_config1(B=B, H=H, d=d)
+    nth = oracle.ref().k3ref_max_threads()
+    S = c["state"].copy()
+    # bound each step to a sample of the batch when a full step would make the run long
+    t0 = time.perf_counter()
+    _, S1 = oracle.kda_decode(S, c["q"], c["k"], c["v"], c["g"], c["beta"], use_ref=True,
+                              nthreads=nth)
+    full = time.perf_counter() - t0
+    total = args.steps + args.warmup
+    frac = min(1.0, 120.0 / max(full * total, 1e-9))
+    nb = max(1, int(B * frac))
+    sub = {x: np.ascontiguousarray(c[x][:nb]) for x in ("q", "k", "v", "g", "beta")}
+    Ss = np.ascontiguousarray(S[:nb])
+    for _ in range(args.warmup):
+        _, Ss = oracle.kda_decode(Ss, sub["q"], sub["k"], sub["v"], sub["g"], sub["beta"],
+                                  use_ref=True, nthreads=nth)
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        _, Ss = oracle.kda_decode(Ss, sub["q"], sub["k"], sub["v"], sub["g"], sub["beta"],
+                                  use_ref=True, nthreads=nth)
+    el = time.perf_counter() - t0
+    value = nb * args.steps / el
+    return {
+        "impl": "reference",
+        "metric": "KDA recurrent decode tokens/s (BASELINE config 1: B=256, H=32, d=128)",
+        "value": value, "unit": "tokens/s", "n_gpus": D.world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": el * 1e3 / args.steps, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "fp32", "data": "synthetic",
+        "config": {"workload": "kda_decode_config1", "batch_per_gpu": B, "heads": H, "d_k": d,
+                   "d_v": d},
+        "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": nth, "kind": "reference",
+                         "sample": f"{nb} of {B} sequences x {H} heads per step through the "
+                                   f"reference k3_kda_step (OpenMP over streams)"},
+        "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=2000)
+    ap.add_argument("--warmup", type=int, default=20)
+    ap.add_argument("--workload", default="decode", choices=["decode", "prefill", "varlen", "mla"])
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3)
+    D = Dist()
+    if args.impl == "reference":
+        if D.rank == 0:
+            print(json.dumps(bench_reference(args, D)), flush=True)
+        D.close()
+        return
+    if args.workload == "decode":
+        line = bench_decode(args, D)
+    elif args.workload in ("prefill", "varlen"):
+        line = bench_prefill(args, D, varlen=args.workload == "varlen")
+    else:
+        line = bench_mla(args, D)
+    if D.rank == 0:
+        if args.workload == "decode" and D.world == 1 and not args.no_cpu_baseline:
+            line["cpu_baseline"] = cpu_decode_baseline(DECODE_B, DECODE_H, DECODE_D)
+        print(json.dumps(line), flush=True)
+    D.close()
+
+
+if __name__ == "__main__":
+    main()

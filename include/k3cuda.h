@@ -1,0 +1,168 @@
+/* k3cuda.h -- libk3cuda: a B200 (sm_100a) attention engine for the kimi-k3-in-c C engine.
+ *
+ * Plain C ABI (extern "C", pointers and sizes, no C++ or framework types). Every entry
+ * point returns an int status (K3CUDA_OK == 0) and never aborts; k3cuda_last_error()
+ * gives the message of the most recent failure on the calling thread. The reference's
+ * abort-on-failure contract (src/core/k3_ops.c:38-78) is kept one level up, by the C99
+ * wrappers of include/k3_gpu.h.
+ *
+ * Device pointers ("d" in the comments) must come from k3cuda_malloc or any other CUDA
+ * allocation on the context's device. All work is issued on the context's stream and is
+ * asynchronous unless stated; k3cuda_sync waits for it.
+ *
+ * Layouts follow the reference (include/k3/k3.h:157-165, src/core/k3_ops.c:864-938):
+ *   per-token tensors      [tokens][heads][dim]       (the reference's [T][H*D])
+ *   KDA recurrent state    [streams][heads][d_k][d_v] fp32, row = key channel
+ *   MLA latent cache       [batch][cap][kv_lora] and rope cache [batch][cap][qk_rope]
+ */
+#ifndef K3CUDA_H
+#define K3CUDA_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ------------------------------------------------------------------ status codes */
+enum {
+    K3CUDA_OK = 0,
+    K3CUDA_ERR_ARG = 1,         /* invalid argument (null pointer, bad size, misaligned) */
+    K3CUDA_ERR_CUDA = 2,        /* a CUDA runtime call failed                              */
+    K3CUDA_ERR_UNSUPPORTED = 3, /* shape or option this build has no kernel for            */
+    K3CUDA_ERR_WORKSPACE = 4,   /* workspace smaller than the *_workspace query returned   */
+    K3CUDA_ERR_NCCL = 5,        /* NCCL missing or a collective failed                     */
+    K3CUDA_ERR_TIMEOUT = 6,     /* a bounded device-side wait gave up (error word set)     */
+    K3CUDA_ERR_STATE = 7        /* call out of order (no communicator, context shut down)  */
+};
+
+/* element types of the per-token tensors */
+enum { K3CUDA_F32 = 0, K3CUDA_BF16 = 1 };
+/* gate semantics: log-decay g (alpha = exp(g), k3_ops.c:182) or alpha itself */
+enum { K3CUDA_GATE_LOG = 0, K3CUDA_GATE_ALPHA = 1 };
+
+typedef struct k3cuda_ctx k3cuda_ctx;
+
+/* ------------------------------------------------------------ context and memory */
+/* Create a context on `device` with its own non-blocking stream. */
+int  k3cuda_init(int device, k3cuda_ctx **ctx);
+/* Synchronise, release the stream, events, communicator and the context. */
+int  k3cuda_shutdown(k3cuda_ctx *ctx);
+/* Message of the last failure on this thread ("" when none). Never NULL. */
+const char *k3cuda_last_error(void);
+int  k3cuda_device_count(int *count);
+/* Wait for all work issued on the context's stream. */
+int  k3cuda_sync(k3cuda_ctx *ctx);
+/* The context's cudaStream_t, as an opaque pointer (for callers that order their own
+ * work against this library's). */
+void *k3cuda_stream(k3cuda_ctx *ctx);
+/* Device memory (256-byte aligned). */
+int  k3cuda_malloc(k3cuda_ctx *ctx, void **dptr, size_t bytes);
+int  k3cuda_free(k3cuda_ctx *ctx, void *dptr);
+/* Page-locked host memory, for the host-buffer entry points' fast copies. */
+int  k3cuda_host_alloc(k3cuda_ctx *ctx, void **hptr, size_t bytes);
+int  k3cuda_host_free(k3cuda_ctx *ctx, void *hptr);
+/* Copies on the context's stream (asynchronous for page-locked host memory). */
+int  k3cuda_memcpy_h2d(k3cuda_ctx *ctx, void *dst, const void *src, size_t bytes);
+int  k3cuda_memcpy_d2h(k3cuda_ctx *ctx, void *dst, const void *src, size_t bytes);
+int  k3cuda_memcpy_d2d(k3cuda_ctx *ctx, void *dst, const void *src, size_t bytes);
+int  k3cuda_memset(k3cuda_ctx *ctx, void *dptr, int value, size_t bytes);
+
+/* ------------------------------------------------------------------------ timing */
+/* Record event `slot` (0..K3CUDA_MAX_EVENTS-1) on the context's stream. */
+#define K3CUDA_MAX_EVENTS 64
+int  k3cuda_event_record(k3cuda_ctx *ctx, int slot);
+/* Milliseconds between two recorded events (waits for the second). */
+int  k3cuda_event_elapsed(k3cuda_ctx *ctx, int slot_a, int slot_b, float *ms);
+/* Number of kernels this context has launched since init (all entry points). */
+long long k3cuda_launch_count(k3cuda_ctx *ctx);
+/* Zero-filled device buffer larger than L2, written once per call to evict L2 between
+ * timed iterations (allocated on first use, freed at shutdown). */
+int  k3cuda_flush_l2(k3cuda_ctx *ctx);
+
+/* ------------------------------------------------------------- KDA decode (T = 1) */
+/* One recurrent token for n_streams independent sequences x H heads. Replaces the
+ * per-head call of k3_kda_step (src/core/k3_ops.c:186-243, contract include/k3/k3.h:
+ * 157-165) that k3_kda_layer makes at T = 1 (k3_ops.c:927-938):
+ *     S <- diag(alpha) S;  u = S^T k;  S <- S + k (beta (v - u))^T;  o = S^T q
+ * with q multiplied by q_scale first (the reference pre-scales by d_k^-0.5,
+ * k3_ops.c:918,934).
+ *   state  d [n_streams][H][dk][dv] fp32, updated in place
+ *   o      d [n_streams][H][dv]   io_dtype
+ *   q, k   d [n_streams][H][dk]   io_dtype;   v d [n_streams][H][dv] io_dtype
+ *   gate   d [n_streams][H][dk]   fp32, g (K3CUDA_GATE_LOG) or alpha (K3CUDA_GATE_ALPHA)
+ *   beta   d [n_streams][H]       fp32
+ * Fast path: dv == 128 and dk in {64, 128}; any other dk, dv <= 256 with
+ * dk*dv <= 32768 runs a general kernel. */
+int k3cuda_kda_decode(k3cuda_ctx *ctx, float *state, void *o, const void *q,
+                      const void *k, const void *v, const float *gate, const float *beta,
+                      int n_streams, int H, int dk, int dv, float q_scale, int io_dtype,
+                      int gate_mode);
+
+/* --------------------------------------------------- KDA chunked prefill (varlen) */
+/* The whole recurrence of k3_kda_layer (src/core/k3_ops.c:908-938) over packed
+ * variable-length sequences, computed chunkwise (WY / UT-transform form of the gated
+ * delta rule) instead of token by token. Results equal the token-by-token recurrence to
+ * floating-point rounding.
+ *   cu_seqlens  HOST [n_seq + 1] token offsets into the packed tensors
+ *   state       d [n_seq][H][dk][dv] fp32: initial state in, final state out; NULL
+ *               means zero initial state and no state out
+ *   o, q, k, v, gate, beta   as k3cuda_kda_decode, with [total_tokens] in place of
+ *               [n_streams]
+ *   chunk       64 (the only chunk size built)
+ * Supported: dk == dv == 64 or 128. workspace must hold k3cuda_kda_prefill_workspace()
+ * bytes (device memory, 256-byte aligned). */
+int k3cuda_kda_prefill_workspace(const int *cu_seqlens, int n_seq, int H, int dk, int dv,
+                                 int chunk, size_t *bytes);
+int k3cuda_kda_prefill(k3cuda_ctx *ctx, float *state, void *o, const void *q,
+                       const void *k, const void *v, const float *gate, const float *beta,
+                       const int *cu_seqlens, int n_seq, int H, int dk, int dv,
+                       float q_scale, int io_dtype, int gate_mode, int chunk,
+                       void *workspace, size_t workspace_bytes);
+
+/* ----------------------------------------------------------- MLA absorbed decode */
+/* One query token per sequence over a compressed latent KV cache. Replaces the
+ * attention loop of k3_mla_cached (src/core/k3_ops.c:381-411) at T = 1, with the
+ * expanded per-head keys/values of the reference's cache (k3_ops.c:351-367) factored
+ * through kv_b's per-head blocks W_UK = kv_b[h*(dn+dv) .. +dn) and
+ * W_UV = kv_b[h*(dn+dv)+dn .. +dv):
+ *     score[s] = (q_nope . (W_UK c_s) + q_rope . r_s) * scale
+ *     out      = W_UV sum_s softmax(score)[s] c_s          (fp32 softmax)
+ *   out       d [B][H][dv]     out_dtype (pre-gate accumulator acc of k3_ops.c:404-410)
+ *   q_nope    d [B][H][dn] bf16;  q_rope d [B][H][dr] bf16
+ *   latent    d [B][cap][dl] bf16; rope d [B][cap][dr] bf16
+ *   w_uk      d [H][dn][dl] bf16;  w_uv d [H][dv][dl] bf16
+ *   ctx_lens  HOST [B], 1 <= ctx_lens[b] <= cap: positions 0..ctx_lens[b]-1 attended
+ * Supported: dn == dv == 128, dr == 64, dl == 512 (the released head geometry, k3.h
+ * comments at :83-90), any H <= 128. */
+int k3cuda_mla_decode_workspace(const int *ctx_lens, int B, int H, int dl, int dv,
+                                size_t *bytes);
+int k3cuda_mla_decode(k3cuda_ctx *ctx, void *out, int out_dtype, const void *q_nope,
+                      const void *q_rope, const void *latent, const void *rope,
+                      const void *w_uk, const void *w_uv, const int *ctx_lens, int B,
+                      int cap, int H, int dn, int dr, int dl, int dv, float scale,
+                      void *workspace, size_t workspace_bytes);
+
+/* ------------------------------------------------- multi-GPU: head-sharded output */
+/* The reference is single-process (no communicator exists in it). Head sharding adds
+ * one exchange: each rank computes H_local = H / nranks heads of [T][H][dv] and the
+ * output is all-gathered over NVLink before o_proj. NCCL is loaded at run time
+ * (libnccl.so.2); without it these return K3CUDA_ERR_NCCL. */
+#define K3CUDA_UNIQUE_ID_BYTES 128
+int k3cuda_comm_unique_id(unsigned char id[K3CUDA_UNIQUE_ID_BYTES]);
+int k3cuda_comm_init(k3cuda_ctx *ctx, int nranks, int rank,
+                     const unsigned char id[K3CUDA_UNIQUE_ID_BYTES]);
+/* full d [T][nranks*H_local][dv] <- every rank's local d [T][H_local][dv] (rank r owns
+ * heads r*H_local .. r*H_local+H_local-1). workspace d >= nranks*T*H_local*dv elements
+ * of `dtype` (k3cuda_allgather_heads_workspace). */
+int k3cuda_allgather_heads_workspace(int nranks, int T, int H_local, int dv, int dtype,
+                                     size_t *bytes);
+int k3cuda_allgather_heads(k3cuda_ctx *ctx, void *full, const void *local, int T,
+                           int H_local, int dv, int dtype, void *workspace,
+                           size_t workspace_bytes);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* K3CUDA_H */

@@ -1,0 +1,70 @@
+// internal.cuh -- shared state and helpers of libk3cuda (not part of the C ABI).
+#pragma once
+
+#include <cuda_runtime.h>
+#include <cuda_bf16.h>
+#include <stdint.h>
+#include <stdio.h>
+
+#include "k3cuda.h"
+
+struct k3cuda_ctx {
+    int device;
+    int sm_count;
+    cudaStream_t stream;
+    cudaEvent_t events[K3CUDA_MAX_EVENTS];
+    long long launches;
+    void *flush_buf;
+    size_t flush_bytes;
+    unsigned int *err_word;     // device word set by bounded waits that gave up
+    // NCCL (opaque; see comm.cu)
+    void *nccl_comm;
+    int nranks, rank;
+};
+
+namespace k3 {
+
+// Record an error message for the calling thread; returns `code`.
+int set_error(int code, const char *fmt, ...);
+void clear_error();
+
+// Make ctx->device current; returns K3CUDA_OK or an error.
+int enter(k3cuda_ctx *ctx);
+
+// Check the last launch, count it, and convert failures.
+int after_launch(k3cuda_ctx *ctx, const char *what);
+
+#define K3_CUDA_TRY(expr)                                                                  \
+    do {                                                                                   \
+        cudaError_t _e = (expr);                                                           \
+        if (_e != cudaSuccess)                                                             \
+            return ::k3::set_error(K3CUDA_ERR_CUDA, "%s failed: %s (%s:%d)", #expr,        \
+                                   cudaGetErrorString(_e), __FILE__, __LINE__);            \
+    } while (0)
+
+#define K3_ARG_CHECK(cond, ...)                                                            \
+    do {                                                                                   \
+        if (!(cond)) return ::k3::set_error(K3CUDA_ERR_ARG, __VA_ARGS__);                  \
+    } while (0)
+
+inline bool aligned(const void *p, size_t a) { return ((uintptr_t)p % a) == 0; }
+
+// ------------------------------------------------------------------ element access
+template <typename T> struct io;
+template <> struct io<float> {
+    static __device__ __forceinline__ float ld(const float *p) { return *p; }
+    static __device__ __forceinline__ void st(float *p, float x) { *p = x; }
+};
+template <> struct io<__nv_bfloat16> {
+    static __device__ __forceinline__ float ld(const __nv_bfloat16 *p) {
+        return __bfloat162float(*p);
+    }
+    static __device__ __forceinline__ void st(__nv_bfloat16 *p, float x) {
+        *p = __float2bfloat16_rn(x);
+    }
+};
+
+__device__ __forceinline__ float bf16lo(uint32_t w) { return __uint_as_float(w << 16); }
+__device__ __forceinline__ float bf16hi(uint32_t w) { return __uint_as_float(w & 0xffff0000u); }
+
+}  // namespace k3

@@ -1,0 +1,394 @@
+// kda_prefill.cu -- KDA chunkwise prefill over packed variable-length sequences.
+//
+// Replaces the token-by-token recurrence of k3_kda_layer (reference src/core/k3_ops.c:
+// 908-938, k3_kda_step at :186-243) with the chunkwise (WY / UT-transform) form of the
+// gated delta rule. Inside a chunk of C = 64 tokens with per-channel cumulative log decay
+// G_t = sum_{u<=t} g_u:
+//     (I + Akk) Delta = diag(beta) (V - Ktil S0)     Akk[t][s] = beta_t sum_i k_ti k_si e^(G_ti - G_si), s < t
+//     O   = Qtil S0 + Aqk Delta                      Aqk[t][s] = sum_i q_ti k_si e^(G_ti - G_si),      s <= t
+//     S_C = diag(e^G_C) S0 + Kbar^T Delta
+// with Ktil_t = e^G_t k_t, Qtil_t = e^G_t q_t (q pre-multiplied by q_scale) and
+// Kbar_s = e^(G_C - G_s) k_s. Every factor above is <= 1, so nothing overflows.
+//
+// Two kernels:
+//   kda_chunk_intra  one CTA per (chunk, head), all chunks in parallel: G, Akk, Aqk with
+//                    16-token sub-block anchors, M = (I + Akk)^-1 diag(beta) by forward
+//                    substitution, and the scaled operands Qtil, Ktil, Kbar, e^G_C.
+//   kda_chunk_scan   one CTA per (sequence, head, 16-column slice of d_v): walks the
+//                    sequence's chunks in order with its state slice in shared memory:
+//                    X = V - Ktil S; Delta = M X; O = Qtil S + Aqk Delta;
+//                    S = e^G_C S + Kbar^T Delta.
+// Columns of the state are independent in every step, which is what lets the scan split
+// d_v across CTAs with no communication.
+//
+// Anchors. e^(G_t - G_s) is formed as e^(G_t - G_r) e^(G_r - G_s) with r the first token
+// of t's 16-token sub-block. For s before the sub-block both factors are <= 1. For s
+// inside it e^(G_r - G_s) >= 1 spans at most 15 decay steps; if any channel's 15-step
+// decay exceeds e^80 the sub-block's diagonal entries are formed directly instead.
+#include <vector>
+
+#include "internal.cuh"
+
+namespace k3 {
+
+constexpr int KC = 64;        // chunk length
+constexpr int KSUB = 16;      // anchor sub-block
+constexpr int SCAN_DVT = 16;  // d_v columns per scan CTA
+
+struct ChunkDesc {
+    int seq;    // sequence index
+    int t0;     // first token (packed index)
+    int len;    // tokens in this chunk (1..64)
+    int pad;
+};
+
+template <int DK>
+struct PrefillLayout {
+    // per (chunk, head) block, in floats
+    static constexpr size_t qt = 0;
+    static constexpr size_t kt = qt + (size_t)KC * DK;
+    static constexpr size_t kb = kt + (size_t)KC * DK;
+    static constexpr size_t gc = kb + (size_t)KC * DK;
+    static constexpr size_t m = gc + DK;
+    static constexpr size_t aqk = m + (size_t)KC * KC;
+    static constexpr size_t floats = aqk + (size_t)KC * KC;
+};
+
+__device__ __forceinline__ float load_gate(const float *p, int gate_is_log) {
+    const float x = *p;
+    return gate_is_log ? x : logf(x);
+}
+
+// ---------------------------------------------------------------------------- intra
+template <typename IO, int DK>
+__global__ void __launch_bounds__(256, 1)
+kda_chunk_intra(const ChunkDesc *__restrict__ chunks, const IO *__restrict__ q,
+                const IO *__restrict__ k, const float *__restrict__ gate,
+                const float *__restrict__ beta, float *__restrict__ ws, int H, float q_scale,
+                int gate_is_log) {
+    using L = PrefillLayout<DK>;
+    extern __shared__ __align__(16) float sm[];
+    float *sk = sm;                     // [KC][DK]  k
+    float *sq = sk + KC * DK;           // [KC][DK]  q * q_scale
+    float *sG = sq + KC * DK;           // [KC][DK]  cumulative log decay
+    float *sKh = sG + KC * DK;          // [KC][DK]  k_s e^(G_r - G_s) for the current anchor r
+    float *sKa = sKh + KC * DK;         // [KSUB][DK] k_t e^(G_t - G_r)
+    float *sQa = sKa + KSUB * DK;       // [KSUB][DK] q_t e^(G_t - G_r)
+    float *sA = sQa + KSUB * DK;        // [KC][KC]  Akk (beta-scaled, strictly lower)
+    float *sAq = sA + KC * KC;          // [KC][KC]  Aqk (lower incl. diagonal)
+    float *sT = sAq + KC * KC;          // [KC][KC]  (I + Akk)^-1
+    float *sb = sT + KC * KC;           // [KC]      beta
+
+    const ChunkDesc cd = chunks[blockIdx.x];
+    const int h = blockIdx.y, tid = threadIdx.x;
+    float *out = ws + ((size_t)blockIdx.x * H + h) * L::floats;
+
+    for (int e = tid; e < KC * DK; e += 256) {
+        const int t = e / DK, i = e - t * DK;
+        float kv = 0.f, qv = 0.f, gv = 0.f;
+        if (t < cd.len) {
+            const size_t off = ((size_t)(cd.t0 + t) * H + h) * DK + i;
+            kv = io<IO>::ld(k + off);
+            qv = io<IO>::ld(q + off) * q_scale;
+            gv = load_gate(gate + off, gate_is_log);
+        }
+        sk[e] = kv;
+        sq[e] = qv;
+        sG[e] = gv;
+    }
+    if (tid < KC) sb[tid] = tid < cd.len ? beta[(size_t)(cd.t0 + tid) * H + h] : 0.f;
+    __syncthreads();
+    if (tid < DK) {
+        float acc = 0.f;
+        for (int t = 0; t < KC; t++) {
+            acc += sG[t * DK + tid];
+            sG[t * DK + tid] = acc;
+        }
+    }
+    __syncthreads();
+
+    // scaled operands for the scan (full-chunk anchor at the chunk start)
+    for (int e = tid; e < KC * DK; e += 256) {
+        const int t = e / DK, i = e - t * DK;
+        const float G = sG[e], GC = sG[(KC - 1) * DK + i];
+        const float eg = expf(G);
+        out[L::qt + e] = sq[e] * eg;
+        out[L::kt + e] = sk[e] * eg;
+        out[L::kb + e] = sk[e] * expf(GC - G);
+    }
+    if (tid < DK) out[L::gc + tid] = expf(sG[(KC - 1) * DK + tid]);
+
+    // Akk / Aqk, one 16-row sub-block at a time
+    for (int a = 0; a < KC / KSUB; a++) {
+        const int r0 = a * KSUB, ncol = r0 + KSUB;
+        int big = 0;
+        for (int e = tid; e < ncol * DK; e += 256) {
+            const int s = e / DK, i = e - s * DK;
+            const float ex = sG[r0 * DK + i] - sG[e];
+            big |= ex > 80.f;
+            sKh[e] = sk[e] * expf(fminf(ex, 80.f));
+        }
+        for (int e = tid; e < KSUB * DK; e += 256) {
+            const int t = r0 + e / DK, i = e % DK;
+            const float f = expf(sG[t * DK + i] - sG[r0 * DK + i]);
+            sKa[e] = sk[t * DK + i] * f;
+            sQa[e] = sq[t * DK + i] * f;
+        }
+        big = __syncthreads_or(big);
+        for (int e = tid; e < KSUB * KC; e += 256) {
+            const int tl = e / KC, s = e - tl * KC, t = r0 + tl;
+            float akk = 0.f, aqk = 0.f;
+            if (s <= t) {
+                if (big && s >= r0) {
+                    for (int i = 0; i < DK; i++) {
+                        const float f = expf(sG[t * DK + i] - sG[s * DK + i]) * sk[s * DK + i];
+                        akk += sk[t * DK + i] * f;
+                        aqk += sq[t * DK + i] * f;
+                    }
+                } else {
+                    const float *ka = sKa + tl * DK, *qa = sQa + tl * DK, *kh = sKh + s * DK;
+                    for (int i = 0; i < DK; i++) {
+                        akk += ka[i] * kh[i];
+                        aqk += qa[i] * kh[i];
+                    }
+                }
+            }
+            sA[t * KC + s] = s < t ? sb[t] * akk : 0.f;
+            sAq[t * KC + s] = aqk;
+        }
+        __syncthreads();
+    }
+
+    // T = (I + Akk)^-1 by forward substitution, row by row; M = T diag(beta)
+    for (int e = tid; e < KC * KC; e += 256) sT[e] = (e / KC == e % KC) ? 1.f : 0.f;
+    __syncthreads();
+    for (int t = 1; t < KC; t++) {
+        if (tid < t) {
+            const int s = tid;
+            float acc = 0.f;
+            for (int j = s; j < t; j++) acc += sA[t * KC + j] * sT[j * KC + s];
+            sT[t * KC + s] = -acc;
+        }
+        __syncthreads();
+    }
+    for (int e = tid; e < KC * KC; e += 256) {
+        const int s = e % KC;
+        out[L::m + e] = sT[e] * sb[s];
+        out[L::aqk + e] = sAq[e];
+    }
+}
+
+// ----------------------------------------------------------------------------- scan
+template <typename IO, int DK>
+__global__ void __launch_bounds__(256, 1)
+kda_chunk_scan(const ChunkDesc *__restrict__ chunks, const int *__restrict__ seq_chunk0,
+               const IO *__restrict__ v, const float *__restrict__ ws, float *__restrict__ state,
+               IO *__restrict__ o, int H) {
+    using L = PrefillLayout<DK>;
+    constexpr int DV = DK, NT = DV / SCAN_DVT;
+    extern __shared__ __align__(16) float sm[];
+    float *sQt = sm;                    // [KC][DK]
+    float *sKt = sQt + KC * DK;         // [KC][DK]
+    float *sKb = sKt + KC * DK;         // [KC][DK]
+    float *sM = sKb + KC * DK;          // [KC][KC]
+    float *sAq = sM + KC * KC;          // [KC][KC]
+    float *sS = sAq + KC * KC;          // [DK][SCAN_DVT]
+    float *sX = sS + DK * SCAN_DVT;     // [KC][SCAN_DVT]
+    float *sD = sX + KC * SCAN_DVT;     // [KC][SCAN_DVT]
+    float *sGc = sD + KC * SCAN_DVT;    // [DK]
+
+    const int tile = blockIdx.x % NT;
+    const int h = (blockIdx.x / NT) % H;
+    const int n = blockIdx.x / (NT * H);
+    const int tid = threadIdx.x, j = tid % SCAN_DVT, r = tid / SCAN_DVT;  // r in 0..15
+    const int c0 = seq_chunk0[n], c1 = seq_chunk0[n + 1];
+    const int col0 = tile * SCAN_DVT;
+    float *Sg = state ? state + ((size_t)n * H + h) * DK * DV : nullptr;
+
+    for (int e = tid; e < DK * SCAN_DVT; e += 256) {
+        const int i = e / SCAN_DVT, jj = e % SCAN_DVT;
+        sS[e] = Sg ? Sg[(size_t)i * DV + col0 + jj] : 0.f;
+    }
+    for (int c = c0; c < c1; c++) {
+        const ChunkDesc cd = chunks[c];
+        const float *blk = ws + ((size_t)c * H + h) * L::floats;
+        __syncthreads();
+        for (int e = tid; e < KC * DK / 4; e += 256) {
+            reinterpret_cast<float4 *>(sQt)[e] = reinterpret_cast<const float4 *>(blk + L::qt)[e];
+            reinterpret_cast<float4 *>(sKt)[e] = reinterpret_cast<const float4 *>(blk + L::kt)[e];
+            reinterpret_cast<float4 *>(sKb)[e] = reinterpret_cast<const float4 *>(blk + L::kb)[e];
+        }
+        for (int e = tid; e < KC * KC / 4; e += 256) {
+            reinterpret_cast<float4 *>(sM)[e] = reinterpret_cast<const float4 *>(blk + L::m)[e];
+            reinterpret_cast<float4 *>(sAq)[e] = reinterpret_cast<const float4 *>(blk + L::aqk)[e];
+        }
+        if (tid < DK) sGc[tid] = blk[L::gc + tid];
+        // X = V - Ktil S
+        for (int t = r; t < KC; t += 16) {
+            float vv = 0.f;
+            if (t < cd.len) vv = io<IO>::ld(v + ((size_t)(cd.t0 + t) * H + h) * DV + col0 + j);
+            sX[t * SCAN_DVT + j] = vv;
+        }
+        __syncthreads();
+        for (int t = r; t < KC; t += 16) {
+            float acc = 0.f;
+            const float *kt = sKt + t * DK;
+            for (int i = 0; i < DK; i++) acc += kt[i] * sS[i * SCAN_DVT + j];
+            sX[t * SCAN_DVT + j] -= acc;
+        }
+        __syncthreads();
+        // Delta = M X  (M lower triangular)
+        for (int t = r; t < KC; t += 16) {
+            float acc = 0.f;
+            const float *m = sM + t * KC;
+            for (int s = 0; s <= t; s++) acc += m[s] * sX[s * SCAN_DVT + j];
+            sD[t * SCAN_DVT + j] = acc;
+        }
+        __syncthreads();
+        // O = Qtil S + Aqk Delta
+        for (int t = r; t < cd.len; t += 16) {
+            float acc = 0.f;
+            const float *qt = sQt + t * DK;
+            for (int i = 0; i < DK; i++) acc += qt[i] * sS[i * SCAN_DVT + j];
+            const float *aq = sAq + t * KC;
+            for (int s = 0; s <= t; s++) acc += aq[s] * sD[s * SCAN_DVT + j];
+            io<IO>::st(o + ((size_t)(cd.t0 + t) * H + h) * DV + col0 + j, acc);
+        }
+        __syncthreads();
+        // S = e^G_C S + Kbar^T Delta
+        for (int i = r; i < DK; i += 16) {
+            float acc = sGc[i] * sS[i * SCAN_DVT + j];
+            for (int s = 0; s < KC; s++) acc += sKb[s * DK + i] * sD[s * SCAN_DVT + j];
+            sS[i * SCAN_DVT + j] = acc;
+        }
+    }
+    __syncthreads();
+    if (Sg)
+        for (int e = tid; e < DK * SCAN_DVT; e += 256) {
+            const int i = e / SCAN_DVT, jj = e % SCAN_DVT;
+            Sg[(size_t)i * DV + col0 + jj] = sS[e];
+        }
+}
+
+static size_t align256(size_t x) { return (x + 255) & ~(size_t)255; }
+
+static int count_chunks(const int *cu, int n_seq, long long *nc) {
+    long long c = 0;
+    for (int n = 0; n < n_seq; n++) {
+        const int len = cu[n + 1] - cu[n];
+        if (len < 0) return set_error(K3CUDA_ERR_ARG, "cu_seqlens not non-decreasing at %d", n);
+        c += (len + KC - 1) / KC;
+    }
+    *nc = c;
+    return K3CUDA_OK;
+}
+
+static size_t table_bytes(long long nc, int n_seq) {
+    return align256((size_t)nc * sizeof(ChunkDesc)) + align256((size_t)(n_seq + 1) * sizeof(int));
+}
+
+template <typename IO, int DK>
+static int run_prefill(k3cuda_ctx *ctx, float *state, void *o, const void *q, const void *k,
+                       const void *v, const float *gate, const float *beta, const int *cu,
+                       int n_seq, int H, float q_scale, int gate_is_log, long long nc,
+                       void *workspace) {
+    using L = PrefillLayout<DK>;
+    std::vector<ChunkDesc> table((size_t)nc);
+    std::vector<int> c0((size_t)n_seq + 1);
+    long long c = 0;
+    for (int n = 0; n < n_seq; n++) {
+        c0[n] = (int)c;
+        for (int t = cu[n]; t < cu[n + 1]; t += KC) {
+            const int len = cu[n + 1] - t < KC ? cu[n + 1] - t : KC;
+            table[(size_t)c++] = ChunkDesc{n, t, len, 0};
+        }
+    }
+    c0[n_seq] = (int)c;
+    char *wsb = (char *)workspace;
+    ChunkDesc *d_table = (ChunkDesc *)wsb;
+    int *d_c0 = (int *)(wsb + align256((size_t)nc * sizeof(ChunkDesc)));
+    float *blocks = (float *)(wsb + table_bytes(nc, n_seq));
+    if (nc > 0)
+        K3_CUDA_TRY(cudaMemcpyAsync(d_table, table.data(), (size_t)nc * sizeof(ChunkDesc),
+                                    cudaMemcpyHostToDevice, ctx->stream));
+    K3_CUDA_TRY(cudaMemcpyAsync(d_c0, c0.data(), (size_t)(n_seq + 1) * sizeof(int),
+                                cudaMemcpyHostToDevice, ctx->stream));
+    if (nc > 0) {
+        const size_t smem1 =
+            ((size_t)4 * KC * DK + 2 * KSUB * DK + 3 * KC * KC + KC) * sizeof(float);
+        K3_CUDA_TRY(cudaFuncSetAttribute(kda_chunk_intra<IO, DK>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem1));
+        dim3 g1((unsigned)nc, (unsigned)H);
+        kda_chunk_intra<IO, DK><<<g1, 256, smem1, ctx->stream>>>(
+            d_table, (const IO *)q, (const IO *)k, gate, beta, blocks, H, q_scale, gate_is_log);
+        int rc = after_launch(ctx, "kda_chunk_intra");
+        if (rc) return rc;
+    }
+    const size_t smem2 = ((size_t)3 * KC * DK + 2 * KC * KC + DK * SCAN_DVT + 2 * KC * SCAN_DVT +
+                          DK) * sizeof(float);
+    K3_CUDA_TRY(cudaFuncSetAttribute(kda_chunk_scan<IO, DK>,
+                                     cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem2));
+    const long long nblk = (long long)n_seq * H * (DK / SCAN_DVT);
+    if (nblk > 0) {
+        kda_chunk_scan<IO, DK><<<(unsigned)nblk, 256, smem2, ctx->stream>>>(
+            d_table, d_c0, (const IO *)v, blocks, state, (IO *)o, H);
+        return after_launch(ctx, "kda_chunk_scan");
+    }
+    (void)L::floats;
+    return K3CUDA_OK;
+}
+
+}  // namespace k3
+
+using namespace k3;
+
+extern "C" int k3cuda_kda_prefill_workspace(const int *cu_seqlens, int n_seq, int H, int dk,
+                                            int dv, int chunk, size_t *bytes) {
+    K3_ARG_CHECK(bytes && cu_seqlens && n_seq >= 0 && H >= 1, "bad prefill workspace query");
+    if (chunk != KC || dk != dv || (dk != 64 && dk != 128))
+        return set_error(K3CUDA_ERR_UNSUPPORTED, "kda_prefill: dk=%d dv=%d chunk=%d not built",
+                         dk, dv, chunk);
+    long long nc = 0;
+    int rc = count_chunks(cu_seqlens, n_seq, &nc);
+    if (rc) return rc;
+    const size_t per = dk == 64 ? PrefillLayout<64>::floats : PrefillLayout<128>::floats;
+    *bytes = table_bytes(nc, n_seq) + (size_t)nc * H * per * sizeof(float);
+    return K3CUDA_OK;
+}
+
+extern "C" int k3cuda_kda_prefill(k3cuda_ctx *ctx, float *state, void *o, const void *q,
+                                  const void *k, const void *v, const float *gate,
+                                  const float *beta, const int *cu_seqlens, int n_seq, int H,
+                                  int dk, int dv, float q_scale, int io_dtype, int gate_mode,
+                                  int chunk, void *workspace, size_t workspace_bytes) {
+    int rc = enter(ctx);
+    if (rc) return rc;
+    K3_ARG_CHECK(io_dtype == K3CUDA_F32 || io_dtype == K3CUDA_BF16, "bad io_dtype %d", io_dtype);
+    K3_ARG_CHECK(gate_mode == K3CUDA_GATE_LOG || gate_mode == K3CUDA_GATE_ALPHA,
+                 "bad gate_mode %d", gate_mode);
+    size_t need = 0;
+    rc = k3cuda_kda_prefill_workspace(cu_seqlens, n_seq, H, dk, dv, chunk, &need);
+    if (rc) return rc;
+    if (cu_seqlens[0] != 0) return set_error(K3CUDA_ERR_ARG, "cu_seqlens[0] must be 0");
+    if (workspace_bytes < need || (need && !workspace))
+        return set_error(K3CUDA_ERR_WORKSPACE, "kda_prefill: workspace %zu < %zu bytes",
+                         workspace_bytes, need);
+    K3_ARG_CHECK(aligned(workspace, 256), "workspace must be 256-byte aligned");
+    if (cu_seqlens[n_seq] == 0 || n_seq == 0) return K3CUDA_OK;
+    K3_ARG_CHECK(o && q && k && v && gate && beta, "kda_prefill: null pointer");
+    long long nc = 0;
+    count_chunks(cu_seqlens, n_seq, &nc);
+    const int gl = gate_mode == K3CUDA_GATE_LOG;
+    if (io_dtype == K3CUDA_BF16) {
+        if (dk == 64)
+            return run_prefill<__nv_bfloat16, 64>(ctx, state, o, q, k, v, gate, beta, cu_seqlens,
+                                                  n_seq, H, q_scale, gl, nc, workspace);
+        return run_prefill<__nv_bfloat16, 128>(ctx, state, o, q, k, v, gate, beta, cu_seqlens,
+                                               n_seq, H, q_scale, gl, nc, workspace);
+    }
+    if (dk == 64)
+        return run_prefill<float, 64>(ctx, state, o, q, k, v, gate, beta, cu_seqlens, n_seq, H,
+                                      q_scale, gl, nc, workspace);
+    return run_prefill<float, 128>(ctx, state, o, q, k, v, gate, beta, cu_seqlens, n_seq, H,
+                                   q_scale, gl, nc, workspace);
+}

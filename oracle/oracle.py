@@ -1,0 +1,168 @@
+"""ctypes bindings for the CPU checkers (TEST INFRASTRUCTURE, not product code).
+
+Only tests/, ``__graft_entry__.smoke()`` and bench.py's ``cpu_baseline`` / ``--impl
+reference`` legs import this module, and only to check or to time the reference. The
+product library (libk3cuda) never calls into it.
+
+Two libraries:
+  * ``liboracle.so``      -- our C restatement (oracle/k3_oracle.c), each function citing
+                             the reference file:line it follows;
+  * ``_ref/libk3ref.so``  -- the reference's unmodified src/core/k3_ops.c compiled by
+                             oracle/Makefile, plus loops in ref_driver.c.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+_LIB = None
+_REF = None
+
+f32p = np.ctypeslib.ndpointer(dtype=np.float32, flags="C_CONTIGUOUS")
+f64p = np.ctypeslib.ndpointer(dtype=np.float64, flags="C_CONTIGUOUS")
+i32p = np.ctypeslib.ndpointer(dtype=np.int32, flags="C_CONTIGUOUS")
+
+
+def _f32(a):
+    return np.ascontiguousarray(a, dtype=np.float32)
+
+
+def lib():
+    """Load (building if needed) the restatement library."""
+    global _LIB
+    if _LIB is None:
+        path = os.path.join(HERE, "liboracle.so")
+        if not os.path.exists(path):
+            build()
+        L = C.CDLL(path)
+        L.orc_kda_step.argtypes = [f32p, f32p, f32p, f32p, f32p, f32p, C.c_float, C.c_int, C.c_int]
+        L.orc_kda_recurrence.argtypes = [C.c_void_p, f32p, f32p, f32p, f32p, f32p, C.c_int, f32p,
+                                         i32p, C.c_int, C.c_int, C.c_int, C.c_int, C.c_float,
+                                         C.c_int]
+        L.orc_kda_decay.argtypes = [f32p, f32p, f32p, f32p, f32p, C.c_int, C.c_int, C.c_float]
+        L.orc_kda_layer.argtypes = ([f32p, f32p] + [C.c_int] * 5 + [C.c_float, C.c_float]
+                                    + [f32p] * 14 + [C.c_void_p])
+        L.orc_mla_absorbed_decode.argtypes = ([f32p] * 7 + [i32p] + [C.c_int] * 7
+                                              + [C.c_float, C.c_int])
+        L.orc_kda_chunked_f64.argtypes = [f32p, f32p, f64p, f64p, f32p, f32p, f32p, f32p, f32p,
+                                          C.c_int, C.c_int, C.c_int, C.c_int, C.c_float]
+        _LIB = L
+    return _LIB
+
+
+def ref_available() -> bool:
+    return os.path.exists(os.path.join(HERE, "_ref", "libk3ref.so"))
+
+
+def ref():
+    """Load the compiled reference (oracle/_ref/libk3ref.so)."""
+    global _REF
+    if _REF is None:
+        path = os.path.join(HERE, "_ref", "libk3ref.so")
+        if not os.path.exists(path):
+            build()
+        R = C.CDLL(path)
+        R.k3_kda_step.argtypes = [f32p, f32p, f32p, f32p, f32p, f32p, C.c_float, C.c_int, C.c_int]
+        R.k3ref_kda_recurrence.argtypes = [f32p, f32p, f32p, f32p, f32p, f32p, C.c_int, f32p,
+                                           i32p, C.c_int, C.c_int, C.c_int, C.c_int, C.c_float,
+                                           C.c_int]
+        R.k3ref_kda_decode.argtypes = [f32p, f32p, f32p, f32p, f32p, f32p, C.c_int, f32p,
+                                       C.c_long, C.c_int, C.c_int, C.c_float, C.c_int]
+        R.k3ref_max_threads.restype = C.c_int
+        R.k3_kda_decay.argtypes = [f32p, f32p, f32p, f32p, f32p, C.c_int, C.c_int, C.c_float]
+        R.k3_rmsnorm.argtypes = [f32p, f32p, f32p, C.c_int, C.c_float]
+        R.k3_matmul.argtypes = [f32p, f32p, f32p, C.c_int, C.c_int]
+        R.k3_mla_scratch_cached.restype = C.c_size_t
+        _REF = R
+    return _REF
+
+
+def build():
+    """Compile liboracle.so and, where the reference sources exist, _ref/libk3ref.so."""
+    import subprocess
+    subprocess.run(["make", "-s", "-C", HERE], check=True)
+
+
+# ----------------------------------------------------------------------------- KDA
+def kda_recurrence(q, k, v, gate, beta, cu_seqlens, *, gate_is_log=True, q_scale=None,
+                   state=None, nthreads=1, use_ref=False):
+    """Packed varlen KDA recurrence. q,k [sumT,H,dk]; v [sumT,H,dv]; gate [sumT,H,dk];
+    beta [sumT,H]; cu_seqlens int32 [nseq+1]. Returns (o [sumT,H,dv], S [nseq,H,dk,dv]).
+    ``use_ref`` runs the reference's own k3_kda_step instead of the restatement."""
+    q, k, v, gate, beta = (_f32(a) for a in (q, k, v, gate, beta))
+    cu = np.ascontiguousarray(cu_seqlens, dtype=np.int32)
+    T, H, dk = q.shape
+    dv = v.shape[2]
+    nseq = len(cu) - 1
+    if q_scale is None:
+        q_scale = 1.0 / float(np.sqrt(np.float32(dk)))
+    S = (np.zeros((nseq, H, dk, dv), np.float32) if state is None
+         else np.array(state, dtype=np.float32, copy=True, order="C"))
+    o = np.zeros((T, H, dv), np.float32)
+    if use_ref:
+        ref().k3ref_kda_recurrence(S, o, q, k, v, gate, int(gate_is_log), beta, cu, nseq, H, dk,
+                                   dv, float(q_scale), int(nthreads))
+    else:
+        lib().orc_kda_recurrence(S.ctypes.data, o, q, k, v, gate, int(gate_is_log), beta, cu,
+                                 nseq, H, dk, dv, float(q_scale), int(nthreads))
+    return o, S
+
+
+def kda_decode(S, q, k, v, gate, beta, *, gate_is_log=True, q_scale=None, nthreads=1,
+               use_ref=False):
+    """One decode token for B sequences: S [B,H,dk,dv] (copied, not modified);
+    q,k [B,H,dk], v [B,H,dv], gate [B,H,dk], beta [B,H]. Returns (o [B,H,dv], S_new)."""
+    B, H, dk = q.shape
+    dv = v.shape[2]
+    if q_scale is None:
+        q_scale = 1.0 / float(np.sqrt(np.float32(dk)))
+    if use_ref:
+        S2 = np.array(S, dtype=np.float32, copy=True, order="C")
+        o = np.zeros((B, H, dv), np.float32)
+        ref().k3ref_kda_decode(S2, o, _f32(q), _f32(k), _f32(v), _f32(gate), int(gate_is_log),
+                               _f32(beta), B * H, dk, dv, float(q_scale), int(nthreads))
+        return o, S2
+    cu = np.arange(B + 1, dtype=np.int32)
+    o, S2 = kda_recurrence(q.reshape(B, H, dk), k, v, gate, beta, cu, gate_is_log=gate_is_log,
+                           q_scale=q_scale, state=S, nthreads=nthreads)
+    return o, S2
+
+
+def kda_chunked_f64(q, k, v, g, beta, C, q_scale):
+    """Chunkwise double-precision restatement for one head: q,k,g [T,dk], v [T,dv], beta [T].
+    Returns (o, S, Akk, Aqk)."""
+    q, k, v, g, beta = (_f32(a) for a in (q, k, v, g, beta))
+    T, dk = q.shape
+    dv = v.shape[1]
+    n = T // C
+    o = np.zeros((T, dv), np.float32)
+    S = np.zeros((dk, dv), np.float32)
+    Akk = np.zeros((n, C, C), np.float64)
+    Aqk = np.zeros((n, C, C), np.float64)
+    lib().orc_kda_chunked_f64(o, S, Akk, Aqk, q, k, v, g, beta, T, C, dk, dv, float(q_scale))
+    return o, S, Akk, Aqk
+
+
+# ----------------------------------------------------------------------------- MLA
+def mla_absorbed_decode(q_nope, q_rope, latent, rope, w_uk, w_uv, ctx_lens, scale,
+                        nthreads=1):
+    """q_nope [B,H,dn], q_rope [B,H,dr], latent [B,cap,dl], rope [B,cap,dr],
+    w_uk [H,dn,dl], w_uv [H,dv,dl], ctx_lens int32 [B]. Returns out [B,H,dv] fp32."""
+    q_nope, q_rope, latent, rope, w_uk, w_uv = (_f32(a) for a in
+                                               (q_nope, q_rope, latent, rope, w_uk, w_uv))
+    B, H, dn = q_nope.shape
+    dr = q_rope.shape[2]
+    cap, dl = latent.shape[1], latent.shape[2]
+    dv = w_uv.shape[1]
+    out = np.zeros((B, H, dv), np.float32)
+    cl = np.ascontiguousarray(ctx_lens, dtype=np.int32)
+    lib().orc_mla_absorbed_decode(out, q_nope, q_rope, latent, rope, w_uk, w_uv, cl, B, cap, H,
+                                  dn, dr, dl, dv, float(scale), int(nthreads))
+    return out
+
+
+def max_threads() -> int:
+    return os.cpu_count() or 1

@@ -1,0 +1,163 @@
+"""Regenerate the golden vectors under tests/golden/ (run here, where the reference exists).
+
+    python tests/golden/make_golden.py [REF_DIR]
+
+Two kinds of fixture, both written as .npz (float32 unless noted):
+
+1. The reference's own op fixtures for the hot path, converted unchanged from
+   REF/tests/fixtures/ops/{kda_recur1,kda_recur8,kda_decay,kda_layer1,kda_layer8,mla}.json
+   (emitted by the reference's tools/emit_fixtures.py from its pure-torch model) and the
+   tolerance of REF/tests/fixtures/ops/MANIFEST.json.
+
+2. Outputs of the reference's own C (oracle/_ref/libk3ref.so, built from
+   REF/src/core/k3_ops.c by oracle/Makefile) on seeded inputs:
+     * cfg0_kda.npz  -- BASELINE config 0: B=1, prefill T=256 then 32 decode steps,
+                        H=4, d_k=d_v=64, seed 0, through k3_kda_step (k3_ops.c:186-243)
+                        driven as k3_ops.c:908-938.
+     * mla_ref.npz   -- k3_mla_cached (k3_ops.c:321-424) with a filled cache, kv_b built
+                        from W_UK/W_UV per head, no gate and an identity o_proj, so its
+                        output is the pre-gate attention accumulator; q and the latent are
+                        recovered exactly as the reference forms them. Small geometry
+                        (H=8, nope 32, rope 16, latent 64, v 32), every causal prefix.
+     * mla_ref_full.npz -- the same at the released head geometry (nope 128, rope 64,
+                        latent 512, v 128) with H=2 and 80 positions, the shape the CUDA
+                        kernel is built for.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import json
+import os
+import sys
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+ROOT = os.path.dirname(os.path.dirname(HERE))
+sys.path.insert(0, ROOT)
+sys.path.insert(0, os.path.join(ROOT, "kimi-k3-in-c_b200"))
+
+from oracle import oracle  # noqa: E402
+import workloads as gen  # noqa: E402
+
+
+def convert_fixture(ref_dir: str, name: str):
+    with open(os.path.join(ref_dir, "tests", "fixtures", "ops", name + ".json")) as f:
+        d = json.load(f)
+    out = {}
+    for key, val in d.items():
+        if isinstance(val, dict) and "data" in val:
+            out[key] = np.asarray(val["data"], dtype=np.float32).reshape(val["shape"])
+        elif isinstance(val, (int, float)) and not isinstance(val, bool):
+            out[key] = np.asarray(val, dtype=np.float64)
+    np.savez_compressed(os.path.join(HERE, name + ".npz"), **out)
+    return out
+
+
+class K3Cfg(C.Structure):
+    """include/k3/k3.h:73-120, field for field."""
+    _fields_ = [("hidden", C.c_int), ("n_layers", C.c_int), ("vocab", C.c_int),
+                ("rms_eps", C.c_float), ("kda_heads", C.c_int), ("kda_head_dim", C.c_int),
+                ("conv_k", C.c_int), ("gate_lb", C.c_float), ("n_heads", C.c_int),
+                ("q_lora", C.c_int), ("kv_lora", C.c_int), ("qk_nope", C.c_int),
+                ("qk_rope", C.c_int), ("v_head", C.c_int), ("mla_out_gate", C.c_int),
+                ("n_experts", C.c_int), ("topk", C.c_int), ("n_shared", C.c_int),
+                ("latent", C.c_int), ("moe_inter", C.c_int), ("routed_scale", C.c_float),
+                ("moe_renorm", C.c_int), ("latent_norm", C.c_int), ("first_dense", C.c_int),
+                ("dense_inter", C.c_int), ("attn_res_block", C.c_int), ("situ_b1", C.c_float),
+                ("situ_b2", C.c_float), ("n_full_attn", C.c_int),
+                ("full_attn", C.POINTER(C.c_int))]
+
+
+class K3MlaW(C.Structure):
+    """include/k3/k3.h:203-211."""
+    _fields_ = [("q_a", C.c_void_p), ("q_b", C.c_void_p), ("kv_a", C.c_void_p),
+                ("kv_b", C.c_void_p), ("o", C.c_void_p), ("g", C.c_void_p),
+                ("q_a_norm", C.c_void_p), ("kv_a_norm", C.c_void_p), ("wdt", C.c_int)]
+
+
+def mla_reference_case(H=8, dn=32, dr=16, dl=64, dv=32, q_lora=48, P=40, seed=3):
+    """Run the reference k3_mla_cached over P tokens with a cache and return the absorbed
+    inputs plus the reference's per-token attention output (token t attends 0..t)."""
+    R = oracle.ref()
+    rng = np.random.default_rng(seed)
+    E = H * dv  # hidden == H*v_head so that o_proj can be the identity
+    x = rng.standard_normal((P, E), dtype=np.float32)
+    q_a = (rng.standard_normal((q_lora, E)) * 0.05).astype(np.float32)
+    q_b = (rng.standard_normal((H * (dn + dr), q_lora)) * 0.2).astype(np.float32)
+    kv_a = (rng.standard_normal((dl + dr, E)) * 0.05).astype(np.float32)
+    w_uk = (rng.standard_normal((H, dn, dl)) * 0.15).astype(np.float32)
+    w_uv = (rng.standard_normal((H, dv, dl)) * 0.15).astype(np.float32)
+    kv_b = np.concatenate([w_uk, w_uv], axis=1).reshape(H * (dn + dv), dl).astype(np.float32)
+    eye = np.eye(E, dtype=np.float32)
+    n1 = np.ones(q_lora, np.float32)
+    n2 = np.ones(dl, np.float32)
+    cfg = K3Cfg()
+    cfg.hidden, cfg.rms_eps, cfg.n_heads = E, 1e-5, H
+    cfg.q_lora, cfg.kv_lora, cfg.qk_nope, cfg.qk_rope, cfg.v_head = q_lora, dl, dn, dr, dv
+    w = K3MlaW()
+    keep = [np.ascontiguousarray(a) for a in (q_a, q_b, kv_a, kv_b, eye, n1, n2)]
+    w.q_a, w.q_b, w.kv_a, w.kv_b, w.o = (a.ctypes.data for a in keep[:5])
+    w.g = None
+    w.q_a_norm, w.kv_a_norm = keep[5].ctypes.data, keep[6].ctypes.data
+    w.wdt = 0
+    R.k3_mla_scratch_cached.argtypes = [C.POINTER(K3Cfg), C.c_int, C.c_int, C.c_int]
+    nscr = R.k3_mla_scratch_cached(C.byref(cfg), P, P, 1)
+    scratch = np.zeros(nscr, np.float32)
+    kvc = np.zeros((P, H * (dn + dv)), np.float32)
+    ropec = np.zeros((P, dr), np.float32)
+    out = np.zeros((P, E), np.float32)
+    R.k3_mla_cached.argtypes = [C.c_void_p, C.c_void_p, C.POINTER(K3MlaW), C.POINTER(K3Cfg),
+                                C.c_int, C.c_void_p, C.c_void_p, C.c_void_p, C.c_int, C.c_int]
+    R.k3_mla_cached(out.ctypes.data, x.ctypes.data, C.byref(w), C.byref(cfg), P,
+                    scratch.ctypes.data, kvc.ctypes.data, ropec.ctypes.data, 0, P)
+    # q as the reference formed it: scratch[0 : P*H*qh] (k3_ops.c:343)
+    q = scratch[: P * H * (dn + dr)].reshape(P, H, dn + dr).copy()
+    # the latent as the reference formed it: rmsnorm(kv_a x)[:dl] (k3_ops.c:363-365)
+    lat = np.zeros((P, dl), np.float32)
+    for t in range(P):
+        ct = np.zeros(dl + dr, np.float32)
+        R.k3_matmul(ct, np.ascontiguousarray(x[t]), kv_a, E, dl + dr)
+        y = np.zeros(dl, np.float32)
+        R.k3_rmsnorm(y, np.ascontiguousarray(ct[:dl]), n2, dl, np.float32(1e-5))
+        lat[t] = y
+    scale = np.float32(1.0 / np.sqrt(np.float32(dn + dr)))
+    return dict(q_nope=q[:, :, :dn], q_rope=q[:, :, dn:], latent=np.broadcast_to(lat, (P, P, dl)),
+                rope=np.broadcast_to(ropec, (P, P, dr)), w_uk=w_uk, w_uv=w_uv,
+                ctx_lens=np.arange(1, P + 1, dtype=np.int32), scale=np.float64(scale),
+                out=out.reshape(P, H, dv))
+
+
+def main():
+    ref_dir = sys.argv[1] if len(sys.argv) > 1 else "/root/reference"
+    for name in ("kda_recur1", "kda_recur8", "kda_decay", "kda_layer1", "kda_layer8", "mla"):
+        convert_fixture(ref_dir, name)
+    with open(os.path.join(ref_dir, "tests", "fixtures", "ops", "MANIFEST.json")) as f:
+        tol = json.load(f)["tolerance"]
+    np.savez(os.path.join(HERE, "manifest_tolerance.npz"), fp32_abs=tol["fp32_abs"],
+             fp32_rel=tol["fp32_rel"])
+
+    # BASELINE config 0 through the reference C.
+    c0 = gen.kda_config0()
+    o, S = oracle.kda_recurrence(c0["q"], c0["k"], c0["v"], c0["g"], c0["beta"],
+                                 np.array([0, c0["q"].shape[0]], np.int32), gate_is_log=True,
+                                 use_ref=True)
+    np.savez_compressed(os.path.join(HERE, "cfg0_kda.npz"), out=o, state_out=S,
+                        **{k: v for k, v in c0.items()})
+
+    m = mla_reference_case()
+    m = {k: np.ascontiguousarray(v) for k, v in m.items()}
+    m["latent"] = m["latent"][0:1].copy()  # stored once; every row of the batch shares it
+    m["rope"] = m["rope"][0:1].copy()
+    np.savez_compressed(os.path.join(HERE, "mla_ref.npz"), **m)
+
+    m = mla_reference_case(H=2, dn=128, dr=64, dl=512, dv=128, q_lora=64, P=80, seed=4)
+    m = {k: np.ascontiguousarray(v) for k, v in m.items()}
+    m["latent"] = m["latent"][0:1].copy()
+    m["rope"] = m["rope"][0:1].copy()
+    np.savez_compressed(os.path.join(HERE, "mla_ref_full.npz"), **m)
+    print("golden vectors written to", HERE)
+
+
+if __name__ == "__main__":
+    main()

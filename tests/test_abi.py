@@ -1,0 +1,102 @@
+"""The C ABI: both libraries load and export every function include/*.h declares (CPU only).
+
+No kernel is launched here. The host-only parts of the ABI (argument checks, workspace
+queries, error reporting) are exercised without a GPU.
+"""
+import ctypes as C
+import glob
+import os
+import re
+
+import numpy as np
+import pytest
+
+import k3cuda
+import workloads as W
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+DECL = re.compile(r"^\s*(?:const\s+)?(?:int|void|char|long\s+long|size_t)\s*\**\s*"
+                  r"(k3cuda_\w+|k3g_\w+)\s*\(", re.M)
+
+
+def declared(header):
+    with open(os.path.join(ROOT, "include", header)) as f:
+        return sorted(set(DECL.findall(f.read())))
+
+
+def test_headers_declare_the_expected_entry_points():
+    names = declared("k3cuda.h")
+    for must in ("k3cuda_init", "k3cuda_kda_decode", "k3cuda_kda_prefill", "k3cuda_mla_decode",
+                 "k3cuda_allgather_heads", "k3cuda_last_error"):
+        assert must in names
+    assert set(declared("k3_gpu.h")) >= {"k3g_kda_step", "k3g_kda_recurrence", "k3g_mla_attend"}
+
+
+def test_every_header_symbol_is_exported_and_bound():
+    L = k3cuda.lib()
+    for h in glob.glob(os.path.join(ROOT, "include", "*.h")):
+        for name in declared(os.path.basename(h)):
+            lib = k3cuda.gpu_lib() if name.startswith("k3g_") else L
+            assert hasattr(lib, name), f"{name} declared in {h} but not exported"
+            table = k3cuda.GPU_SIGNATURES if name.startswith("k3g_") else k3cuda.SIGNATURES
+            assert name in table, f"{name} has no ctypes signature"
+
+
+def test_library_is_sm100a_only():
+    with open(os.path.join(ROOT, "kimi-k3-in-c_b200", "Makefile")) as f:
+        mk = f.read()
+    assert "arch=compute_100a,code=sm_100a" in mk
+
+
+def test_workspace_queries_are_host_only():
+    L = k3cuda.lib()
+    cu = np.array([0, 100, 100, 300], np.int32)
+    n = C.c_size_t()
+    k3cuda.check(L.k3cuda_kda_prefill_workspace(cu.ctypes.data_as(C.POINTER(C.c_int)), 3, 4, 128,
+                                                128, 64, C.byref(n)))
+    nchunks = 2 + 0 + 4
+    per_block = (3 * 64 * 128 + 128 + 2 * 64 * 64) * 4
+    assert n.value >= nchunks * 4 * per_block
+    # unsupported shapes and bad arguments are refused with a message, not a crash
+    rc = L.k3cuda_kda_prefill_workspace(cu.ctypes.data_as(C.POINTER(C.c_int)), 3, 4, 96, 96, 64,
+                                        C.byref(n))
+    assert rc == k3cuda.ERR_UNSUPPORTED
+    assert b"dk=96" in L.k3cuda_last_error()
+    bad = np.array([0, 10, 5], np.int32)
+    rc = L.k3cuda_kda_prefill_workspace(bad.ctypes.data_as(C.POINTER(C.c_int)), 2, 4, 128, 128,
+                                        64, C.byref(n))
+    assert rc == k3cuda.ERR_ARG
+    cl = np.array([8192, 100], np.int32)
+    k3cuda.check(L.k3cuda_mla_decode_workspace(cl.ctypes.data_as(C.POINTER(C.c_int)), 2, 128, 512,
+                                               128, C.byref(n)))
+    assert n.value > 2 * 128 * 576 * 4
+    k3cuda.check(L.k3cuda_allgather_heads_workspace(8, 1000, 8, 128, k3cuda.BF16, C.byref(n)))
+    assert n.value == 8 * 1000 * 8 * 128 * 2
+
+
+def test_init_without_gpu_fails_loudly():
+    L = k3cuda.lib()
+    cnt = C.c_int(0)
+    rc = L.k3cuda_device_count(C.byref(cnt))
+    if rc == 0 and cnt.value > 0:
+        pytest.skip("a GPU is visible; the no-GPU error path is not reachable here")
+    with pytest.raises(k3cuda.K3CudaError):
+        k3cuda.Context(0)
+
+
+def test_null_context_is_an_error_not_a_crash():
+    L = k3cuda.lib()
+    rc = L.k3cuda_kda_decode(None, None, None, None, None, None, None, None, 1, 1, 128, 128, 1.0,
+                             k3cuda.BF16, k3cuda.GATE_LOG)
+    assert rc == k3cuda.ERR_ARG
+    assert L.k3cuda_last_error() == b"null context"
+
+
+def test_workload_shapes():
+    c = W.kda_config3(nseq=4, H=2, d=16, lo=10, hi=40)
+    cu = c["cu_seqlens"]
+    assert cu[0] == 0 and np.all(np.diff(cu) >= 10) and np.all(np.diff(cu) <= 40)
+    assert c["q"].shape == (cu[-1], 2, 16)
+    n = np.linalg.norm(c["q"].astype(np.float64), axis=-1)
+    assert np.all(np.abs(n - 1) < 1e-2)
+    assert np.all(c["g"] <= 0) and np.all((c["beta"] > 0) & (c["beta"] < 1))

@@ -1,0 +1,84 @@
+"""The C99 drop-ins (include/k3_gpu.h) with the reference's own signatures and fixtures.
+
+These are the calls a reference caller switches to: host fp32 buffers, the reference's
+argument order, abort-on-failure. They are checked on the reference's fixtures exactly as
+the reference's tests/unit/test_ops.c drives k3_kda_step (t_recur, :310-350).
+"""
+import ctypes as C
+
+import numpy as np
+import pytest
+
+import k3cuda
+import workloads as W
+
+pytestmark = pytest.mark.gpu
+fp = C.POINTER(C.c_float)
+
+
+def P(a):
+    return a.ctypes.data_as(fp)
+
+
+@pytest.mark.parametrize("name", ["kda_recur1", "kda_recur8"])
+def test_kda_step_dropin_on_reference_fixture(golden, name):
+    G = k3cuda.gpu_lib()
+    d = golden(name)
+    T, H, dk = d["q"].shape
+    qs = np.float32(d["q_scale"])
+    S = np.zeros((H, dk, dk), np.float32)
+    out = np.zeros((T, H, dk), np.float32)
+    for t in range(T):
+        for h in range(H):
+            q = np.ascontiguousarray(d["q"][t, h] * qs)
+            o = np.zeros(dk, np.float32)
+            Sh = np.ascontiguousarray(S[h])
+            G.k3g_kda_step(P(Sh), P(o), P(q), P(np.ascontiguousarray(d["k"][t, h])),
+                           P(np.ascontiguousarray(d["v"][t, h])),
+                           P(np.ascontiguousarray(d["alpha"][t, h])), float(d["beta"][t, h]), dk, dk)
+            S[h] = Sh
+            out[t, h] = o
+    assert W.rel_fro(out, d["out"]) < 1e-5 and W.rel_fro(S, d["state_out"]) < 1e-5
+
+
+def test_kda_recurrence_dropin_config0(golden):
+    """k3_kda_layer's recurrence block (k3_ops.c:908-938) on config 0 through the drop-in:
+    alpha in, q scaled inside, state carried in place; 256 prefill then 32 single steps."""
+    G = k3cuda.gpu_lib()
+    d = golden("cfg0_kda")
+    T, H, D = d["q"].shape
+    alpha = np.exp(d["g"]).astype(np.float32)
+    S = np.zeros((H, D, D), np.float32)
+    out = np.zeros((T, H, D), np.float32)
+    f = lambda a: np.ascontiguousarray(a, np.float32)  # noqa: E731
+    o = np.zeros((256, H, D), np.float32)
+    G.k3g_kda_recurrence(P(S), P(o), P(f(d["q"][:256])), P(f(d["k"][:256])), P(f(d["v"][:256])),
+                         P(f(alpha[:256])), P(f(d["beta"][:256])), 256, H, D)
+    out[:256] = o
+    for t in range(256, T):
+        o1 = np.zeros((1, H, D), np.float32)
+        G.k3g_kda_recurrence(P(S), P(o1), P(f(d["q"][t:t + 1])), P(f(d["k"][t:t + 1])),
+                             P(f(d["v"][t:t + 1])), P(f(alpha[t:t + 1])),
+                             P(f(d["beta"][t:t + 1])), 1, H, D)
+        out[t] = o1[0]
+    assert W.rel_fro(out, d["out"]) < 2e-3 and W.rel_fro(S, d["state_out"]) < 2e-3
+
+
+def test_mla_attend_dropin_on_reference_output(golden):
+    """kv_b in the reference's layout; the drop-in splits W_UK/W_UV itself."""
+    G = k3cuda.gpu_lib()
+    m = golden("mla_ref_full")
+    Pn = m["q_nope"].shape[0]
+    H, qn = m["q_nope"].shape[1:]
+    qr = m["q_rope"].shape[2]
+    dl = m["latent"].shape[2]
+    vh = m["w_uv"].shape[1]
+    kv_b = np.ascontiguousarray(np.concatenate([m["w_uk"], m["w_uv"]], axis=1).reshape(-1, dl))
+    scale = float(m["scale"].ravel()[0])
+    for p in (1, 17, 64, Pn):
+        q = np.ascontiguousarray(np.concatenate([m["q_nope"][p - 1], m["q_rope"][p - 1]], axis=1))
+        acc = np.zeros((H, vh), np.float32)
+        G.k3g_mla_attend(P(acc), P(q), P(np.ascontiguousarray(m["latent"][0, :p])),
+                         P(np.ascontiguousarray(m["rope"][0, :p])), P(kv_b), scale, H, qn, qr, dl,
+                         vh, p)
+        assert W.rel_fro(acc, m["out"][p - 1]) < 5e-3, p

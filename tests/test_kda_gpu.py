@@ -1,0 +1,210 @@
+"""KDA decode and chunked prefill on the B200 against the oracle and the golden vectors.
+
+Tolerances (relative Frobenius error, written per test): 2e-3 for fp32 inputs and for the
+fp32 state, 5e-3 where inputs or outputs are bf16 -- the bar of the hot-path contract.
+Inputs are seeded; bf16 tensors are rounded on the host, and the oracle consumes the exact
+widened values, so both sides see identical numbers.
+"""
+import numpy as np
+import pytest
+
+import k3cuda
+import workloads as W
+from oracle import oracle
+
+pytestmark = pytest.mark.gpu
+
+TOL_F32 = 2e-3
+TOL_BF16 = 5e-3
+
+
+def _bf(x):
+    return W.f32_to_bf16(x)
+
+
+def run_decode(ctx, S, q, k, v, gate, beta, io=k3cuda.BF16, gate_mode=k3cuda.GATE_LOG,
+               q_scale=None):
+    B, H, dk = q.shape
+    dv = v.shape[2]
+    if q_scale is None:
+        q_scale = 1.0 / np.sqrt(np.float32(dk))
+    conv = _bf if io == k3cuda.BF16 else (lambda x: np.ascontiguousarray(x, np.float32))
+    dS = ctx.upload(np.ascontiguousarray(S, np.float32))
+    dq, dk_, dv_ = ctx.upload(conv(q)), ctx.upload(conv(k)), ctx.upload(conv(v))
+    dg, db = ctx.upload(np.ascontiguousarray(gate, np.float32)), ctx.upload(
+        np.ascontiguousarray(beta, np.float32))
+    do = ctx.empty((B, H, dv), np.uint16 if io == k3cuda.BF16 else np.float32)
+    ctx.kda_decode(dS, do, dq, dk_, dv_, dg, db, B, H, dk, dv, q_scale, io, gate_mode)
+    o = do.numpy()
+    if io == k3cuda.BF16:
+        o = W.bf16_to_f32(o)
+    return o, dS.numpy()
+
+
+def run_prefill(ctx, q, k, v, g, beta, cu, S0=None, io=k3cuda.BF16, gate_mode=k3cuda.GATE_LOG,
+                with_state=True):
+    T, H, dk = q.shape
+    dv = v.shape[2]
+    nseq = len(cu) - 1
+    conv = _bf if io == k3cuda.BF16 else (lambda x: np.ascontiguousarray(x, np.float32))
+    dq, dk_, dv_ = ctx.upload(conv(q)), ctx.upload(conv(k)), ctx.upload(conv(v))
+    dg, db = ctx.upload(np.ascontiguousarray(g, np.float32)), ctx.upload(
+        np.ascontiguousarray(beta, np.float32))
+    dS = None
+    if with_state:
+        S0 = np.zeros((nseq, H, dk, dv), np.float32) if S0 is None else S0
+        dS = ctx.upload(np.ascontiguousarray(S0, np.float32))
+    do = ctx.empty((T, H, dv), np.uint16 if io == k3cuda.BF16 else np.float32)
+    nws = ctx.kda_prefill_workspace(cu, H, dk, dv)
+    ws = ctx.empty((max(nws, 1),), np.uint8)
+    ctx.kda_prefill(dS, do, dq, dk_, dv_, dg, db, cu, H, dk, dv, 1.0 / np.sqrt(np.float32(dk)),
+                    ws, nws, io, gate_mode)
+    o = do.numpy()
+    if io == k3cuda.BF16:
+        o = W.bf16_to_f32(o)
+    return o, (dS.numpy() if dS is not None else None)
+
+
+# --------------------------------------------------------------------------- decode
+@pytest.mark.parametrize("name", ["kda_recur1", "kda_recur8"])
+def test_decode_matches_reference_fixture(ctx, golden, name):
+    """The reference's own fixture (H=4, d=16, alpha given, q_scale 0.25), token by token
+    through the general decode kernel, fp32 I/O."""
+    d = golden(name)
+    T, H, dk = d["q"].shape
+    S = np.zeros((1, H, dk, dk), np.float32)
+    outs = []
+    for t in range(T):
+        o, S2 = run_decode(ctx, S, d["q"][t:t + 1], d["k"][t:t + 1], d["v"][t:t + 1],
+                           d["alpha"][t:t + 1], d["beta"][t:t + 1], io=k3cuda.F32,
+                           gate_mode=k3cuda.GATE_ALPHA, q_scale=float(d["q_scale"]))
+        S = S2
+        outs.append(o[0])
+    assert W.rel_fro(np.stack(outs), d["out"]) < 1e-5
+    assert W.rel_fro(S[0], d["state_out"]) < 1e-5
+
+
+@pytest.mark.parametrize("dk", [64, 128])
+@pytest.mark.parametrize("io", [k3cuda.F32, k3cuda.BF16])
+def test_decode_fast_path_vs_reference_c(ctx, dk, io):
+    rng = np.random.default_rng(11 + dk)
+    B, H, dv = 6, 5, 128
+    t = W.kda_tokens(rng, B, H, dk, dv, bf16=(io == k3cuda.BF16))
+    S = rng.standard_normal((B, H, dk, dv), dtype=np.float32) * np.float32(0.02)
+    o, S2 = run_decode(ctx, S, t["q"], t["k"], t["v"], t["g"], t["beta"], io=io)
+    use_ref = oracle.ref_available()
+    o_ref, S_ref = oracle.kda_decode(S, t["q"], t["k"], t["v"], t["g"], t["beta"], use_ref=use_ref)
+    tol = TOL_BF16 if io == k3cuda.BF16 else TOL_F32
+    assert W.rel_fro(o, o_ref) < tol
+    assert W.rel_fro(S2, S_ref) < 1e-5  # the state stays fp32 end to end
+
+
+def test_decode_config1_full_size(ctx):
+    """BASELINE config 1 at full size: B=256, H=32, d=128, bf16 q/k/v/o, fp32 state."""
+    c = W.kda_config1()
+    o, S2 = run_decode(ctx, c["state"], c["q"], c["k"], c["v"], c["g"], c["beta"])
+    o_ref, S_ref = oracle.kda_decode(c["state"], c["q"], c["k"], c["v"], c["g"], c["beta"],
+                                     nthreads=oracle.max_threads())
+    assert W.rel_fro(o, o_ref) < TOL_BF16
+    assert W.rel_fro(S2, S_ref) < TOL_F32
+    # a size-independent property: a second step equals two oracle steps
+    o2, S3 = run_decode(ctx, S2, c["q"], c["k"], c["v"], c["g"], c["beta"])
+    o2_ref, S3_ref = oracle.kda_decode(S_ref, c["q"], c["k"], c["v"], c["g"], c["beta"],
+                                       nthreads=oracle.max_threads())
+    assert W.rel_fro(S3, S3_ref) < TOL_F32 and W.rel_fro(o2, o2_ref) < TOL_BF16
+
+
+def test_decode_alpha_mode_equals_log_mode(ctx):
+    rng = np.random.default_rng(3)
+    t = W.kda_tokens(rng, 4, 3, 128, 128, bf16=False)
+    S = rng.standard_normal((4, 3, 128, 128), dtype=np.float32) * np.float32(0.02)
+    o1, S1 = run_decode(ctx, S, t["q"], t["k"], t["v"], t["g"], t["beta"], io=k3cuda.F32)
+    o2, S2 = run_decode(ctx, S, t["q"], t["k"], t["v"], np.exp(t["g"]), t["beta"], io=k3cuda.F32,
+                        gate_mode=k3cuda.GATE_ALPHA)
+    assert W.rel_fro(o1, o2) < 1e-6 and W.rel_fro(S1, S2) < 1e-6
+
+
+# -------------------------------------------------------------------------- prefill
+def test_config0_prefill_then_decode_matches_reference_c(ctx, golden):
+    """chunked prefill of 256 tokens, then 32 decode steps, against the
+    reference C recurrence over all 288 tokens (fp32, H=4, d=64)."""
+    d = golden("cfg0_kda")
+    Tp = 256
+    o_p, S = run_prefill(ctx, d["q"][:Tp], d["k"][:Tp], d["v"][:Tp], d["g"][:Tp],
+                         d["beta"][:Tp], np.array([0, Tp], np.int32), io=k3cuda.F32)
+    outs = [o_p]
+    for t in range(Tp, Tp + 32):
+        o, S = run_decode(ctx, S, d["q"][t][None], d["k"][t][None], d["v"][t][None],
+                          d["g"][t][None], d["beta"][t][None], io=k3cuda.F32)
+        outs.append(o)
+    out = np.concatenate(outs, axis=0)
+    assert W.rel_fro(out, d["out"]) < TOL_F32
+    assert W.rel_fro(S, d["state_out"]) < TOL_F32
+    assert W.rel_fro(out[:Tp], d["out"][:Tp]) < TOL_F32
+
+
+RAGGED = [0, 1, 63, 64, 65, 0, 130, 7, 200]
+
+
+@pytest.mark.parametrize("d", [64, 128])
+def test_prefill_varlen_ragged_bf16(ctx, d):
+    """Packed sequences with empty, single-token, exact-chunk and partial-chunk lengths,
+    a nonzero initial state, bf16 q/k/v/o."""
+    rng = np.random.default_rng(7 + d)
+    H = 3
+    cu = np.concatenate([[0], np.cumsum(RAGGED)]).astype(np.int32)
+    t = W.kda_tokens(rng, int(cu[-1]), H, d, d, bf16=True)
+    S0 = rng.standard_normal((len(RAGGED), H, d, d), dtype=np.float32) * np.float32(0.05)
+    o, S = run_prefill(ctx, t["q"], t["k"], t["v"], t["g"], t["beta"], cu, S0=S0)
+    o_ref, S_ref = oracle.kda_recurrence(t["q"], t["k"], t["v"], t["g"], t["beta"], cu, state=S0,
+                                         nthreads=oracle.max_threads())
+    assert W.rel_fro(o, o_ref) < TOL_BF16
+    assert W.rel_fro(S, S_ref) < TOL_F32
+    for n in range(len(RAGGED)):  # every sequence on its own, not only in aggregate
+        a, b = cu[n], cu[n + 1]
+        if b > a:
+            assert W.rel_fro(o[a:b], o_ref[a:b]) < TOL_BF16, n
+        assert W.rel_fro(S[n], S_ref[n]) < TOL_F32, n
+    assert np.array_equal(S[0], S0[0]) and np.array_equal(S[5], S0[5])  # empty: untouched
+
+
+def test_prefill_without_state_and_alpha_gate(ctx):
+    rng = np.random.default_rng(21)
+    H, d = 2, 128
+    cu = np.array([0, 150, 300], np.int32)
+    t = W.kda_tokens(rng, 300, H, d, d, bf16=False)
+    o1, _ = run_prefill(ctx, t["q"], t["k"], t["v"], t["g"], t["beta"], cu, io=k3cuda.F32,
+                        with_state=False)
+    o2, _ = run_prefill(ctx, t["q"], t["k"], t["v"], np.exp(t["g"]), t["beta"], cu,
+                        io=k3cuda.F32, gate_mode=k3cuda.GATE_ALPHA, with_state=False)
+    o_ref, _ = oracle.kda_recurrence(t["q"], t["k"], t["v"], t["g"], t["beta"], cu,
+                                     nthreads=oracle.max_threads())
+    assert W.rel_fro(o1, o_ref) < TOL_F32 and W.rel_fro(o2, o_ref) < TOL_F32
+
+
+def test_prefill_extreme_decay_takes_the_exact_path(ctx):
+    """Channels decaying by e^-30 per token overflow a 15-token anchor; the kernel must form
+    those sub-block entries directly and still match."""
+    rng = np.random.default_rng(9)
+    H, d, T = 2, 64, 128
+    t = W.kda_tokens(rng, T, H, d, d, bf16=False)
+    t["g"][:, :, :8] = -30.0
+    t["g"][:, :, 8:16] = 0.0  # alpha == 1 exactly: perfect retention is legitimate
+    cu = np.array([0, T], np.int32)
+    o, S = run_prefill(ctx, t["q"], t["k"], t["v"], t["g"], t["beta"], cu, io=k3cuda.F32)
+    o_ref, S_ref = oracle.kda_recurrence(t["q"], t["k"], t["v"], t["g"], t["beta"], cu)
+    assert np.all(np.isfinite(o)) and np.all(np.isfinite(S))
+    assert W.rel_fro(o, o_ref) < TOL_F32 and W.rel_fro(S, S_ref) < TOL_F32
+
+
+def test_prefill_config2_shape_reduced_heads(ctx):
+    """BASELINE config 2's sequence length (T=32768, 512 chunks in one scan) at 2 heads."""
+    rng = np.random.default_rng(0)
+    T, H, d = 32768, 2, 128
+    t = W.kda_tokens(rng, T, H, d, d, bf16=True)
+    cu = np.array([0, T], np.int32)
+    o, S = run_prefill(ctx, t["q"], t["k"], t["v"], t["g"], t["beta"], cu)
+    o_ref, S_ref = oracle.kda_recurrence(t["q"], t["k"], t["v"], t["g"], t["beta"], cu,
+                                         nthreads=oracle.max_threads())
+    assert W.rel_fro(o, o_ref) < TOL_BF16
+    assert W.rel_fro(S, S_ref) < TOL_F32

@@ -1,0 +1,151 @@
+"""The CPU oracle pinned against the reference's golden vectors (CPU only).
+
+Every check here compares oracle/k3_oracle.c (our restatement) either with the
+reference's own fixtures (tests/fixtures/ops/*.json of the reference, converted by
+tests/golden/make_golden.py) at the reference's MANIFEST tolerance, or with the reference C
+compiled unmodified (oracle/_ref/libk3ref.so), bit for bit where both run the same fp32
+arithmetic.
+"""
+import numpy as np
+import pytest
+
+from oracle import oracle
+import workloads as W
+
+
+def tol(golden):
+    t = golden("manifest_tolerance")
+    return float(t["fp32_abs"]), float(t["fp32_rel"])
+
+
+def close(got, want, atol, rtol):
+    """The reference harness's rule, |got - want| <= atol + rtol |want| (test_ops.c:114-131)."""
+    got = np.asarray(got, np.float64)
+    want = np.asarray(want, np.float64)
+    return bool(np.all(np.abs(got - want) <= atol + rtol * np.abs(want)))
+
+
+@pytest.mark.parametrize("name", ["kda_recur1", "kda_recur8"])
+def test_recurrence_matches_reference_fixture(golden, name):
+    d = golden(name)
+    T = d["q"].shape[0]
+    o, S = oracle.kda_recurrence(d["q"], d["k"], d["v"], d["alpha"], d["beta"],
+                                 np.array([0, T], np.int32), gate_is_log=False,
+                                 q_scale=float(d["q_scale"]))
+    atol, rtol = tol(golden)
+    assert close(o, d["out"], atol, rtol)
+    assert close(S[0], d["state_out"], atol, rtol)
+
+
+@pytest.mark.skipif(not oracle.ref_available(), reason="oracle/_ref not built")
+@pytest.mark.parametrize("name", ["kda_recur1", "kda_recur8"])
+def test_recurrence_bit_exact_with_reference_c(golden, name):
+    d = golden(name)
+    T = d["q"].shape[0]
+    args = (d["q"], d["k"], d["v"], d["alpha"], d["beta"], np.array([0, T], np.int32))
+    o1, S1 = oracle.kda_recurrence(*args, gate_is_log=False, q_scale=float(d["q_scale"]))
+    o2, S2 = oracle.kda_recurrence(*args, gate_is_log=False, q_scale=float(d["q_scale"]),
+                                   use_ref=True)
+    assert np.array_equal(o1, o2) and np.array_equal(S1, S2)
+
+
+def test_config0_golden_from_reference_c(golden):
+    """BASELINE config 0 (T=256 prefill + 32 decode, H=4, d=64), reference C output."""
+    d = golden("cfg0_kda")
+    T = d["q"].shape[0]
+    o, S = oracle.kda_recurrence(d["q"], d["k"], d["v"], d["g"], d["beta"],
+                                 np.array([0, T], np.int32))
+    assert np.array_equal(o, d["out"]) and np.array_equal(S, d["state_out"])
+
+
+def test_config0_inputs_regenerate_from_seed(golden):
+    d = golden("cfg0_kda")
+    c0 = W.kda_config0()
+    for key in ("q", "k", "v", "g", "beta"):
+        assert np.array_equal(c0[key], d[key]), key
+
+
+def test_decay_per_head(golden):
+    d = golden("kda_decay")
+    z = d["z"].reshape(-1, d["z"].shape[-1])
+    H = d["A_log"].shape[0]
+    D = z.shape[1] // H
+    atol, rtol = tol(golden)
+    for r in range(z.shape[0]):
+        g = np.zeros(H * D, np.float32)
+        a = np.zeros(H * D, np.float32)
+        oracle.lib().orc_kda_decay(g, a, np.ascontiguousarray(z[r]), d["A_log"], d["dt_bias"], H,
+                                   D, float(d["lower_bound"]))
+        assert close(g, d["g"].reshape(z.shape[0], -1)[r], atol, rtol)
+        assert close(a, d["alpha"].reshape(z.shape[0], -1)[r], atol, rtol)
+
+
+@pytest.mark.parametrize("name", ["kda_layer1", "kda_layer8"])
+def test_full_kda_layer_matches_reference_fixture(golden, name):
+    d = golden(name)
+    T, E = d["in"].shape[1], d["in"].shape[2]
+    H, D, K = int(d["H"]), int(d["d_k"]), int(d["conv_k"])
+    P = H * D
+    state = np.zeros(H * D * D + 3 * P * (K - 1), np.float32)
+    out = np.zeros((T, E), np.float32)
+    f = lambda k: np.ascontiguousarray(d[k], np.float32)  # noqa: E731
+    oracle.lib().orc_kda_layer(out, f("in"), T, E, H, D, K, float(d["lower_bound"]),
+                               float(d["rms_eps"]), f("q_proj"), f("k_proj"), f("v_proj"),
+                               f("q_conv"), f("k_conv"), f("v_conv"), f("f_a"), f("f_b"),
+                               f("A_log"), f("dt_bias"), f("b_proj"), f("g_proj"), f("o_norm"),
+                               f("o_proj"), state.ctypes.data)
+    atol, rtol = tol(golden)
+    assert close(out, d["out"][0], atol, rtol)
+    assert close(state[: H * D * D], d["state_out"].ravel(), atol, rtol)
+
+
+def test_absorbed_mla_matches_reference_expanded_cache(golden):
+    """k3_mla_cached (expanded fp32 cache) vs the absorbed restatement, every causal prefix."""
+    m = golden("mla_ref")
+    P = m["q_nope"].shape[0]
+    lat = np.broadcast_to(m["latent"], (P,) + m["latent"].shape[1:])
+    rope = np.broadcast_to(m["rope"], (P,) + m["rope"].shape[1:])
+    out = oracle.mla_absorbed_decode(m["q_nope"], m["q_rope"], lat, rope, m["w_uk"], m["w_uv"],
+                                     m["ctx_lens"], float(m["scale"].item()))
+    atol, rtol = tol(golden)
+    assert close(out, m["out"], atol, rtol)
+    assert W.rel_fro(out, m["out"]) < 1e-6
+
+
+def test_chunked_restatement_matches_recurrence(golden):
+    """The WY/UT chunk algebra (double) reproduces the token recurrence; its Akk/Aqk are
+    the intra-chunk known answers the reference itself never forms."""
+    d = golden("cfg0_kda")
+    h = 1
+    T = 256
+    qs = 1.0 / np.sqrt(np.float32(64))
+    oc, Sc, Akk, Aqk = oracle.kda_chunked_f64(d["q"][:T, h], d["k"][:T, h], d["v"][:T, h],
+                                              d["g"][:T, h], d["beta"][:T, h], 64, qs)
+    o1, S1 = oracle.kda_recurrence(d["q"][:T, h:h + 1], d["k"][:T, h:h + 1],
+                                   d["v"][:T, h:h + 1], d["g"][:T, h:h + 1],
+                                   d["beta"][:T, h:h + 1], np.array([0, T], np.int32))
+    assert W.rel_fro(oc, o1[:, 0]) < 1e-5
+    assert W.rel_fro(Sc, S1[0, 0]) < 1e-5
+    # Akk strictly lower, Aqk lower with diagonal q.k
+    assert np.all(np.triu(Akk[0]) == 0)
+    assert np.allclose(np.diag(Aqk[0]),
+                       np.sum(d["q"][:64, h].astype(np.float64) * qs * d["k"][:64, h], axis=1))
+
+
+def test_varlen_streams_are_independent():
+    rng = np.random.default_rng(5)
+    t = W.kda_tokens(rng, 50, 2, 16, 16, bf16=False)
+    cu = np.array([0, 17, 17, 50], np.int32)
+    o, S = oracle.kda_recurrence(t["q"], t["k"], t["v"], t["g"], t["beta"], cu)
+    o2, S2 = oracle.kda_recurrence(t["q"][17:], t["k"][17:], t["v"][17:], t["g"][17:],
+                                   t["beta"][17:], np.array([0, 33], np.int32))
+    assert np.array_equal(o[17:], o2) and np.array_equal(S[2], S2[0])
+    assert np.all(S[1] == 0)  # the empty sequence keeps its (zero) state
+
+
+def test_bf16_round_trip():
+    x = np.array([1.0, -2.5, 3.14159, 1e-30, 65504.0, 0.0], np.float32)
+    b = W.f32_to_bf16(x)
+    y = W.bf16_to_f32(b)
+    assert np.array_equal(W.f32_to_bf16(y), b)
+    assert np.all(np.abs(y - x) <= np.abs(x) * 2.0 ** -8)
