@@ -76,7 +76,7 @@ class K3MlaW(C.Structure):
                 ("q_a_norm", C.c_void_p), ("kv_a_norm", C.c_void_p), ("wdt", C.c_int)]
 
 
-def mla_reference_case(H=8, dn=32, dr=16, dl=64, dv=32, q_lora=48, P=40, seed=3):
+def mla_reference_case(H=8, dn=32, dr=16, dl=64, dv=32, q_lora=48, P=40, seed=3, wstd=0.15):
     """Run the reference k3_mla_cached over P tokens with a cache and return the absorbed
     inputs plus the reference's per-token attention output (token t attends 0..t)."""
     R = oracle.ref()
@@ -86,8 +86,8 @@ def mla_reference_case(H=8, dn=32, dr=16, dl=64, dv=32, q_lora=48, P=40, seed=3)
     q_a = (rng.standard_normal((q_lora, E)) * 0.05).astype(np.float32)
     q_b = (rng.standard_normal((H * (dn + dr), q_lora)) * 0.2).astype(np.float32)
     kv_a = (rng.standard_normal((dl + dr, E)) * 0.05).astype(np.float32)
-    w_uk = (rng.standard_normal((H, dn, dl)) * 0.15).astype(np.float32)
-    w_uv = (rng.standard_normal((H, dv, dl)) * 0.15).astype(np.float32)
+    w_uk = (rng.standard_normal((H, dn, dl)) * wstd).astype(np.float32)
+    w_uv = (rng.standard_normal((H, dv, dl)) * wstd).astype(np.float32)
     kv_b = np.concatenate([w_uk, w_uv], axis=1).reshape(H * (dn + dv), dl).astype(np.float32)
     eye = np.eye(E, dtype=np.float32)
     n1 = np.ones(q_lora, np.float32)
@@ -151,7 +151,10 @@ def main():
     m["rope"] = m["rope"][0:1].copy()
     np.savez_compressed(os.path.join(HERE, "mla_ref.npz"), **m)
 
-    m = mla_reference_case(H=2, dn=128, dr=64, dl=512, dv=128, q_lora=64, P=80, seed=4)
+    # W_UK/W_UV std 0.05 puts the score spread (std ~1.3 logits) where bf16 rounding of the
+    # inputs stays inside the 5e-3 bf16-input bar; the small case above keeps std 0.15.
+    m = mla_reference_case(H=2, dn=128, dr=64, dl=512, dv=128, q_lora=64, P=80, seed=4,
+                           wstd=0.05)
     m = {k: np.ascontiguousarray(v) for k, v in m.items()}
     m["latent"] = m["latent"][0:1].copy()
     m["rope"] = m["rope"][0:1].copy()
