@@ -121,6 +121,25 @@ int k3cuda_kda_prefill(k3cuda_ctx *ctx, float *state, void *o, const void *q,
                        float q_scale, int io_dtype, int gate_mode, int chunk,
                        void *workspace, size_t workspace_bytes);
 
+/* Allocation-free k3cuda_kda_prefill. No counterpart in the reference (whose CPU kernels
+ * need no device memory). It is for callers that cannot call cudaMalloc where they run a
+ * prefill: a host runtime that has already reserved the whole HBM budget through its own
+ * allocator, or a latency-critical path where cudaMalloc's implicit device synchronisation
+ * would stall other streams. The workspace is a static device array of
+ * K3CUDA_NOALLOC_SCRATCH_BYTES that every GPU loading the library holds until exit; a call
+ * whose k3cuda_kda_prefill_workspace() size exceeds it fails with K3CUDA_ERR_WORKSPACE.
+ * Arguments and results are those of k3cuda_kda_prefill. The first call on a device looks
+ * up the array's device address (cudaGetSymbolAddress); make that first call before any
+ * stream capture. All calls share the one array and nothing in it needs to start zeroed
+ * (every byte a call reads it has written first), but two calls whose kernels overlap on
+ * the GPU (different streams or contexts on one device) race on it: serialise them. */
+#define K3CUDA_NOALLOC_SCRATCH_BYTES (64u << 20)
+int k3cuda_kda_prefill_noalloc(k3cuda_ctx *ctx, float *state, void *o, const void *q,
+                               const void *k, const void *v, const float *gate,
+                               const float *beta, const int *cu_seqlens, int n_seq, int H,
+                               int dk, int dv, float q_scale, int io_dtype, int gate_mode,
+                               int chunk);
+
 /* ----------------------------------------------------------- MLA absorbed decode */
 /* One query token per sequence over a compressed latent KV cache. Replaces the
  * attention loop of k3_mla_cached (src/core/k3_ops.c:381-411) at T = 1, with the

@@ -392,3 +392,55 @@ extern "C" int k3cuda_kda_prefill(k3cuda_ctx *ctx, float *state, void *o, const 
     return run_prefill<float, 128>(ctx, state, o, q, k, v, gate, beta, cu_seqlens, n_seq, H,
                                    q_scale, gl, nc, workspace);
 }
+
+// ------------------------------------------------------------- allocation-free variant
+// Some callers cannot allocate device memory at the point they run a prefill: a host
+// runtime that has already reserved the whole HBM budget through its own allocator, or a
+// latency-critical path where cudaMalloc's implicit device synchronisation would stall
+// other streams. For them the workspace of k3cuda_kda_prefill lives in this file-scope
+// array instead, K3CUDA_NOALLOC_SCRATCH_BYTES on every GPU that loads the library, held
+// until the process exits.
+#include <mutex>
+
+static __device__ __align__(256) unsigned char g_prefill_scratch[K3CUDA_NOALLOC_SCRATCH_BYTES];
+
+namespace k3 {
+static std::mutex g_scratch_mu;
+static void *g_scratch_dev[256];  // device address of g_prefill_scratch, per device ordinal
+}  // namespace k3
+
+extern "C" int k3cuda_kda_prefill_noalloc(k3cuda_ctx *ctx, float *state, void *o, const void *q,
+                                          const void *k, const void *v, const float *gate,
+                                          const float *beta, const int *cu_seqlens, int n_seq,
+                                          int H, int dk, int dv, float q_scale, int io_dtype,
+                                          int gate_mode, int chunk) {
+    int rc = enter(ctx);
+    if (rc) return rc;
+    size_t need = 0;
+    rc = k3cuda_kda_prefill_workspace(cu_seqlens, n_seq, H, dk, dv, chunk, &need);
+    if (rc) return rc;
+    if (need > K3CUDA_NOALLOC_SCRATCH_BYTES)
+        return set_error(K3CUDA_ERR_WORKSPACE,
+                         "kda_prefill_noalloc: this call needs %zu bytes of scratch; the static "
+                         "scratch holds %zu (split the batch, or use k3cuda_kda_prefill)",
+                         need, (size_t)K3CUDA_NOALLOC_SCRATCH_BYTES);
+    if (ctx->device < 0 || ctx->device >= 256)
+        return set_error(K3CUDA_ERR_ARG, "device ordinal %d out of range", ctx->device);
+    void *scratch;
+    {
+        std::lock_guard<std::mutex> lock(g_scratch_mu);
+        if (!g_scratch_dev[ctx->device]) {
+            // set-up, once per device, with the device current (enter() made it so)
+            void *p = nullptr;
+            cudaError_t e = cudaGetSymbolAddress(&p, g_prefill_scratch);
+            if (e != cudaSuccess || !p)
+                return set_error(K3CUDA_ERR_CUDA, "cudaGetSymbolAddress(scratch) failed: %s",
+                                 cudaGetErrorString(e));
+            g_scratch_dev[ctx->device] = p;
+        }
+        scratch = g_scratch_dev[ctx->device];
+    }
+    return k3cuda_kda_prefill(ctx, state, o, q, k, v, gate, beta, cu_seqlens, n_seq, H, dk, dv,
+                              q_scale, io_dtype, gate_mode, chunk, scratch,
+                              K3CUDA_NOALLOC_SCRATCH_BYTES);
+}

@@ -50,6 +50,8 @@ SIGNATURES = {
     "k3cuda_kda_prefill_workspace": (_i, [_ip, _i, _i, _i, _i, _i, C.POINTER(_sz)]),
     "k3cuda_kda_prefill": (_i, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _ip, _i, _i, _i, _i, _f,
                                 _i, _i, _i, _vp, _sz]),
+    "k3cuda_kda_prefill_noalloc": (_i, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _ip, _i, _i, _i,
+                                        _i, _f, _i, _i, _i]),
     "k3cuda_mla_decode_workspace": (_i, [_ip, _i, _i, _i, _i, C.POINTER(_sz)]),
     "k3cuda_mla_decode": (_i, [_vp, _vp, _i, _vp, _vp, _vp, _vp, _vp, _vp, _ip, _i, _i, _i, _i,
                                _i, _i, _i, _f, _vp, _sz]),
@@ -216,6 +218,15 @@ class Context:
                                        int(dk), int(dv), float(q_scale), int(io_dtype),
                                        int(gate_mode), int(chunk), _ptr(workspace),
                                        int(workspace_bytes)))
+
+    def kda_prefill_noalloc(self, state, o, q, k, v, gate, beta, cu_seqlens, H, dk, dv, q_scale,
+                            io_dtype=BF16, gate_mode=GATE_LOG, chunk=64):
+        """k3cuda_kda_prefill with the library's static scratch instead of a workspace."""
+        cu, cup = _iarr(cu_seqlens)
+        check(lib().k3cuda_kda_prefill_noalloc(self.h, _ptr(state), _ptr(o), _ptr(q), _ptr(k),
+                                               _ptr(v), _ptr(gate), _ptr(beta), cup, len(cu) - 1,
+                                               int(H), int(dk), int(dv), float(q_scale),
+                                               int(io_dtype), int(gate_mode), int(chunk)))
 
     def mla_decode_workspace(self, ctx_lens, H, dl=512, dv=128) -> int:
         cl, clp = _iarr(ctx_lens)
