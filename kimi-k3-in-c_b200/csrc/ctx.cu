@@ -98,6 +98,13 @@ int k3cuda_sync(k3cuda_ctx *ctx) {
     int rc = enter(ctx);
     if (rc) return rc;
     K3_CUDA_TRY(cudaStreamSynchronize(ctx->stream));
+    // a kernel whose bounded wait gave up leaves its code in the error word
+    unsigned code = 0;
+    K3_CUDA_TRY(cudaMemcpy(&code, ctx->err_word, sizeof code, cudaMemcpyDeviceToHost));
+    if (code) {
+        K3_CUDA_TRY(cudaMemset(ctx->err_word, 0, sizeof code));
+        return set_error(K3CUDA_ERR_TIMEOUT, "a device-side wait timed out (code 0x%x)", code);
+    }
     return K3CUDA_OK;
 }
 

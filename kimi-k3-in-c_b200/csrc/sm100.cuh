@@ -100,6 +100,14 @@ __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, unsign
     return true;
 }
 
+// Bounded wait that reports nothing (used only to drain a CTA's own loads on exit).
+__device__ __forceinline__ bool mbar_wait_quiet(uint64_t *bar, uint32_t parity) {
+    const long long t0 = clock64();
+    while (!mbar_try_wait(bar, parity))
+        if (clock64() - t0 > kWaitCycles) return false;
+    return true;
+}
+
 __device__ __forceinline__ bool mbar_wait_cluster(uint64_t *bar, uint32_t parity, unsigned *err,
                                                   unsigned code) {
     if (mbar_try_wait_cluster(bar, parity)) return true;
@@ -116,7 +124,7 @@ __device__ __forceinline__ bool mbar_wait_cluster(uint64_t *bar, uint32_t parity
 
 // ------------------------------------------------------------------------------ TMA
 // 2-D tiled load of box (c0 = inner, c1 = outer) into shared memory, completing on `bar`
-// (transaction bytes). No cluster multicast: the destination is this CTA's shared memory.
+// (transaction bytes). The destination is this CTA's own shared memory.
 __device__ __forceinline__ void tma_load_2d(void *dst, const CUtensorMap *map, uint64_t *bar,
                                             int c0, int c1) {
     asm volatile(
