@@ -5,31 +5,34 @@
 // values (k3_ops.c:304-315, 351-367); here the cache holds the latent c_s (512 wide) and the
 // shared rope slot r_s (64), and the per-head blocks of kv_b are folded into the query and
 // the output:
-//     q_lat = W_UK^T q_nope                       mla_q_absorb      (bf16 [B][128][576])
+//     q_lat = W_UK^T q_nope                       mla_q_absorb_tc   (tcgen05, bf16 [B][128][576])
 //     S     = [q_lat | q_rope] . [c_s | r_s]^T    mla_attend_tc     (tcgen05, fp32 in TMEM)
 //     P     = softmax(S * scale)                  mla_attend_tc     (fp32 on CUDA cores)
 //     o_lat = P . C                               mla_attend_tc     (tcgen05, fp32 in TMEM)
-//     out   = W_UV o_lat                          mla_merge_project (split-K merge + GEMM)
+//     merge the context splits                    mla_merge         (flash-decoding identity)
+//     out   = W_UV o_lat                          mla_project_tc    (tcgen05)
 //
 // mla_attend_tc runs as clusters of two CTAs (one SM each). All 128 heads are the MMA's M.
 // The 576-wide contraction of S is split across the pair -- rank 0 takes latent dims
 // [0,256) and the 64 rope dims, rank 1 latent dims [256,512) -- and each rank accumulates
 // the output for its own 256 latent dims, which are exactly the dims whose tiles it already
-// holds. Per 64-token tile each rank computes its partial S, the ranks exchange the partials
+// holds. Per 32-token tile each rank computes its partial S, the ranks exchange the partials
 // through distributed shared memory, both add them in the same order (rank 0's + rank 1's),
 // so both derive the same softmax, and each multiplies P by its half of the tile. Per SM:
-//   shared  Q half 80 KB + 2 KV stages x 40 KB + P 16 KB + exchange 32 KB   (~209 KB)
-//   TMEM    S double buffer 2 x 64 columns + O 256 columns                   (of 512)
+//   shared  Q half 80 KB + 4 KV stages x 20 KB + 2 P x 16 KB + 2 exchange x 16 KB (~225 KB)
+//   TMEM    S double buffer 2 x 32 columns + O 256 columns                         (of 512)
+// P and the exchange buffers are double-buffered so that the softmax of tile g overlaps the
+// P.V product of tile g-1.
 // Warp roles: warp 0 issues TMA loads, warp 1 allocates TMEM and issues the MMAs, warps 2-5
 // (one thread per head = TMEM lane) run the exchange, the softmax and the epilogue. The
 // running max is only moved when it grows by more than 2^8 (a lazy rescale: numerator and
 // denominator use the same stale max, so the result is exact), which keeps the O rescale in
 // TMEM off the common path.
 //
-// Work: the (sequence, 64-token tile) list is cut into equal contiguous ranges, one per
+// Work: the (sequence, 32-token tile) list is cut into equal contiguous ranges, one per
 // cluster; a range that crosses sequences becomes several segments, each writing a partial
-// (max, sum, o_lat) per head; mla_merge_project combines the segments of every sequence
-// (the flash-decoding identity) and applies W_UV.
+// (max, sum, o_lat) per head; mla_merge combines the segments of every sequence (the
+// flash-decoding identity) and mla_project_tc applies W_UV.
 //
 // Every wait is bounded (sm100.cuh): on a timeout the kernel records an error word, skips
 // the rest of its work, waits briefly for its own loads and frees TMEM; k3cuda_sync then
@@ -48,16 +51,18 @@ using namespace sm100;
 constexpr int MLA_DN = 128, MLA_DR = 64, MLA_DL = 512, MLA_DV = 128;
 constexpr int MLA_QW = MLA_DL + MLA_DR;    // 576: absorbed query width
 constexpr int MLA_HP = 128;                // heads padded to the MMA's M
-constexpr int MLA_TILE = 64;               // tokens per tile
-constexpr int MLA_NST = 2;                 // KV pipeline stages
+constexpr int MLA_TILE = 32;               // tokens per tile
+constexpr int MLA_NST = 4;                 // KV pipeline stages
 constexpr int MLA_QBLK = MLA_HP * 128;     // bytes of one 64-dim block of Q (128 rows x 128 B)
 constexpr int MLA_KVBLK = MLA_TILE * 128;  // bytes of one 64-dim block of a KV tile
 constexpr int MLA_NBLK = 5;                // dim blocks of rank 0 (4 latent + rope); rank 1: 4
 constexpr int MLA_OFF_Q = 0;
 constexpr int MLA_OFF_KV = MLA_OFF_Q + MLA_NBLK * MLA_QBLK;
 constexpr int MLA_OFF_P = MLA_OFF_KV + MLA_NST * MLA_NBLK * MLA_KVBLK;
-constexpr int MLA_OFF_X = MLA_OFF_P + MLA_HP * 128;
-constexpr int MLA_SMEM = MLA_OFF_X + MLA_HP * MLA_TILE * 4 + 1024;  // + alignment slack
+constexpr int MLA_PBUF = MLA_HP * 128;     // one P buffer: 128 rows x 128 B (K-major, SW128)
+constexpr int MLA_OFF_X = MLA_OFF_P + 2 * MLA_PBUF;
+constexpr int MLA_XBUF = MLA_HP * MLA_TILE * 4;  // one exchange buffer: 128 heads x 32 fp32
+constexpr int MLA_SMEM = MLA_OFF_X + 2 * MLA_XBUF + 1024;  // + alignment slack
 constexpr int MLA_PART = MLA_DL + 4;       // floats per (segment, head): o_lat, max, sum, pad
                                            // (rows stay 16-byte aligned for float4 stores)
 constexpr int MLA_TM_S = 0, MLA_TM_O = 128, MLA_TM_COLS = 512;
@@ -74,48 +79,170 @@ __device__ __forceinline__ bool warp_wait(uint64_t *bar, uint32_t parity, unsign
     return __all_sync(0xffffffffu, ok);
 }
 
-// ------------------------------------------------------------------------- q absorb
-// qlat[b][h][0:512] = W_UK[h]^T q_nope[b][h], qlat[b][h][512:576] = q_rope[b][h], bf16, with
-// rows h >= H zero. One CTA per (padded head, group of 16 sequences); thread l owns latent
-// columns l and l + 256.
-__global__ void __launch_bounds__(256)
-mla_q_absorb(const __nv_bfloat16 *__restrict__ q_nope, const __nv_bfloat16 *__restrict__ q_rope,
-             const __nv_bfloat16 *__restrict__ w_uk, __nv_bfloat16 *__restrict__ qlat, int B,
-             int H) {
-    __shared__ float sq[16][MLA_DN];
-    const int h = blockIdx.x, b0 = blockIdx.y * 16, tid = threadIdx.x;
-    const bool live = h < H;
-    for (int e = tid; e < 16 * MLA_DN; e += 256) {
-        const int bb = e / MLA_DN, i = e % MLA_DN;
-        sq[bb][i] = (live && b0 + bb < B) ? bf(q_nope + ((size_t)(b0 + bb) * H + h) * MLA_DN + i)
-                                          : 0.f;
+// ------------------------------------------------------------------ per-head GEMMs
+// The two small per-head products around the attention, on tcgen05 with the sequences as the
+// MMA's M (128 per CTA; rows past B are zero-filled by TMA and never stored):
+//   mla_q_absorb_tc  qlat[b][h][0:512] = q_nope[b][h] (1 x 128) . W_UK[h] (128 x 512), bf16,
+//                    and qlat[b][h][512:576] = q_rope[b][h]
+//   mla_project_tc   out[b][h][:] = o_lat[b][h] (1 x 512) . W_UV[h]^T (512 x 128), with
+//                    o_lat carried as a bf16 hi/lo pair (K = 1024, W_UV's blocks read twice)
+//                    so the fp32 o_lat reaches the MMA to ~16 mantissa bits
+struct HeadGemmMaps {
+    CUtensorMap a, b;
+};
+
+__global__ void __launch_bounds__(128, 1)
+mla_q_absorb_tc(const __grid_constant__ HeadGemmMaps maps, const __nv_bfloat16 *__restrict__ q_rope,
+                __nv_bfloat16 *__restrict__ qlat, int B, int H, unsigned *__restrict__ err) {
+    extern __shared__ uint8_t smraw[];
+    uint8_t *sm = (uint8_t *)(((uintptr_t)smraw + 1023) & ~(uintptr_t)1023);
+    uint8_t *sA = sm;              // 2 K-blocks x [128 b][128 B]
+    uint8_t *sB = sm + 2 * 16384;  // [2 K-blocks][8 N-blocks] x [64 i][128 B]
+    __shared__ uint64_t bar_ld, bar_mma;
+    __shared__ uint32_t tslot;
+    const int h = blockIdx.x, b0 = blockIdx.y * 128, tid = threadIdx.x, warp = tid >> 5;
+    if (tid == 0) {
+        mbar_init(&bar_ld, 1);
+        mbar_init(&bar_mma, 1);
+        fence_barrier_init();
     }
+    if (warp == 1) tmem_alloc(&tslot, 512);
+    tc_fence_before();
     __syncthreads();
-    float acc0[16], acc1[16];
+    tc_fence_after();
+    const uint32_t tb = tslot;
+    if (tid == 0) {
+        mbar_expect_tx(&bar_ld, 2 * 16384 + 16 * 8192);
+        for (int kb = 0; kb < 2; kb++) tma_load_3d(sA + kb * 16384, &maps.a, &bar_ld, kb * 64, h, b0);
+        for (int kb = 0; kb < 2; kb++)
+            for (int nb = 0; nb < 8; nb++)
+                tma_load_3d(sB + (kb * 8 + nb) * 8192, &maps.b, &bar_ld, nb * 64, kb * 64, h);
+        if (mbar_wait(&bar_ld, 0, err, 0x401)) {
+            tc_fence_after();
+            constexpr uint32_t id = idesc_f16(128, 256, false, true);
+            for (int ks = 0; ks < 8; ks++) {
+                const int kb = ks / 4, kin = ks % 4;
+                const uint64_t ad = sdesc_kmajor(smem_u32(sA + kb * 16384 + kin * 32));
+                for (int half = 0; half < 2; half++) {
+                    const uint64_t bd =
+                        sdesc_mnmajor(smem_u32(sB + (kb * 8 + half * 4) * 8192 + kin * 2048), 8192);
+                    mma_bf16_ss(tb + half * 256, ad, bd, id, ks ? 1u : 0u);
+                }
+            }
+            mma_commit(&bar_mma);
+        }
+    }
+    __syncwarp();
+    const bool ok = warp_wait(&bar_mma, 0, err, 0x402);
+    tc_fence_after();
+    const int b = b0 + 32 * warp + (tid & 31);
+    if (ok) {
+        for (int c = 0; c < 512; c += 16) {
+            float v[16];
+            tmem_ld16(tb + ((uint32_t)(32 * warp) << 16) + c, v);
+            tmem_wait_ld();
+            if (b < B) {
+                uint32_t pk[8];
 #pragma unroll
-    for (int bb = 0; bb < 16; bb++) acc0[bb] = acc1[bb] = 0.f;
-    if (live) {
-        const __nv_bfloat16 *W = w_uk + (size_t)h * MLA_DN * MLA_DL;
-        for (int i = 0; i < MLA_DN; i++) {
-            const float w0 = bf(W + (size_t)i * MLA_DL + tid);
-            const float w1 = bf(W + (size_t)i * MLA_DL + tid + 256);
-#pragma unroll
-            for (int bb = 0; bb < 16; bb++) {
-                acc0[bb] += sq[bb][i] * w0;
-                acc1[bb] += sq[bb][i] * w1;
+                for (int i = 0; i < 8; i++) {
+                    const __nv_bfloat162 t2 = __floats2bfloat162_rn(v[2 * i], v[2 * i + 1]);
+                    pk[i] = *reinterpret_cast<const uint32_t *>(&t2);
+                }
+                uint4 *dst = reinterpret_cast<uint4 *>(qlat + ((size_t)b * MLA_HP + h) * MLA_QW + c);
+                dst[0] = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+                dst[1] = make_uint4(pk[4], pk[5], pk[6], pk[7]);
             }
         }
-    }
+        if (b < B) {
+            const uint4 *src = reinterpret_cast<const uint4 *>(q_rope + ((size_t)b * H + h) * MLA_DR);
+            uint4 *dst = reinterpret_cast<uint4 *>(qlat + ((size_t)b * MLA_HP + h) * MLA_QW + MLA_DL);
 #pragma unroll
-    for (int bb = 0; bb < 16; bb++) {
-        if (b0 + bb < B) {
-            __nv_bfloat16 *dst = qlat + ((size_t)(b0 + bb) * MLA_HP + h) * MLA_QW;
-            dst[tid] = __float2bfloat16_rn(acc0[bb]);
-            dst[tid + 256] = __float2bfloat16_rn(acc1[bb]);
-            if (tid < MLA_DR)
-                dst[MLA_DL + tid] = live ? q_rope[((size_t)(b0 + bb) * H + h) * MLA_DR + tid]
-                                         : __float2bfloat16_rn(0.f);
+            for (int i = 0; i < MLA_DR / 8; i++) dst[i] = src[i];
         }
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        __syncwarp();
+        tmem_dealloc(tb, 512);
+    }
+}
+
+template <typename OUT>
+__global__ void __launch_bounds__(128, 1)
+mla_project_tc(const __grid_constant__ HeadGemmMaps maps, OUT *__restrict__ out, int B, int H,
+               unsigned *__restrict__ err) {
+    constexpr int NS = 4, KB = 16;  // A stages; K blocks of 64 (hi 0..7, lo 8..15)
+    extern __shared__ uint8_t smraw[];
+    uint8_t *sm = (uint8_t *)(((uintptr_t)smraw + 1023) & ~(uintptr_t)1023);
+    uint8_t *sB = sm;               // 8 K-blocks x [128 j][128 B]
+    uint8_t *sA = sm + 8 * 16384;   // NS stages x [128 b][128 B]
+    __shared__ uint64_t bar_b, bar_full[NS], bar_empty[NS], bar_mma;
+    __shared__ uint32_t tslot;
+    const int h = blockIdx.x, b0 = blockIdx.y * 128, tid = threadIdx.x, warp = tid >> 5;
+    if (tid == 0) {
+        mbar_init(&bar_b, 1);
+        mbar_init(&bar_mma, 1);
+        for (int i = 0; i < NS; i++) {
+            mbar_init(&bar_full[i], 1);
+            mbar_init(&bar_empty[i], 1);
+        }
+        fence_barrier_init();
+    }
+    if (warp == 1) tmem_alloc(&tslot, 128);
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tb = tslot;
+    if (tid == 0) {
+        bool ok = true;
+        mbar_expect_tx(&bar_b, 8 * 16384);
+        for (int kb = 0; kb < 8; kb++) tma_load_3d(sB + kb * 16384, &maps.b, &bar_b, kb * 64, 0, h);
+        for (int kb = 0; kb < NS; kb++) {
+            mbar_expect_tx(&bar_full[kb], 16384);
+            tma_load_3d(sA + kb * 16384, &maps.a, &bar_full[kb], kb * 64, h, b0);
+        }
+        ok = mbar_wait(&bar_b, 0, err, 0x411);
+        constexpr uint32_t id = idesc_f16(128, 128, false, false);
+        for (int kb = 0; kb < KB && ok; kb++) {
+            const int st = kb % NS;
+            if (!(ok = mbar_wait(&bar_full[st], (kb / NS) & 1, err, 0x412))) break;
+            tc_fence_after();
+            for (int kin = 0; kin < 4; kin++) {
+                const uint64_t ad = sdesc_kmajor(smem_u32(sA + st * 16384 + kin * 32));
+                const uint64_t bd = sdesc_kmajor(smem_u32(sB + (kb % 8) * 16384 + kin * 32));
+                mma_bf16_ss(tb, ad, bd, id, (kb | kin) ? 1u : 0u);
+            }
+            mma_commit(&bar_empty[st]);
+            if (kb + NS < KB) {
+                if (!(ok = mbar_wait(&bar_empty[st], (kb / NS) & 1, err, 0x413))) break;
+                mbar_expect_tx(&bar_full[st], 16384);
+                tma_load_3d(sA + st * 16384, &maps.a, &bar_full[st], (kb + NS) * 64, h, b0);
+            }
+        }
+        if (ok) mma_commit(&bar_mma);
+        // drain: the last load of every stage has landed before the CTA may exit
+        for (int st = 0; st < NS; st++) mbar_wait_quiet(&bar_full[st], ((KB - NS + st) / NS) & 1);
+    }
+    __syncwarp();
+    const bool ok = warp_wait(&bar_mma, 0, err, 0x414);
+    tc_fence_after();
+    const int b = b0 + 32 * warp + (tid & 31);
+    if (ok) {
+        for (int c = 0; c < 128; c += 16) {
+            float v[16];
+            tmem_ld16(tb + ((uint32_t)(32 * warp) << 16) + c, v);
+            tmem_wait_ld();
+            if (b < B)
+#pragma unroll
+                for (int i = 0; i < 16; i++) io<OUT>::st(out + ((size_t)b * H + h) * MLA_DV + c + i, v[i]);
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        __syncwarp();
+        tmem_dealloc(tb, 128);
     }
 }
 
@@ -132,8 +259,8 @@ struct MlaBars {
     uint64_t kv_full[MLA_NST], kv_empty[MLA_NST];
     uint64_t q_full, q_empty;
     uint64_t s_full[2], s_empty[2];
-    uint64_t p_full, pv_done;
-    uint64_t x_full, x_empty;
+    uint64_t p_full[2], pv_done[2];
+    uint64_t x_full[2], x_empty[2];
     uint32_t tmem_base;
 };
 
@@ -163,10 +290,12 @@ mla_attend_tc(const __grid_constant__ MlaMaps maps, const MlaSeg *__restrict__ s
             mbar_init(&bars.s_full[s], 1);
             mbar_init(&bars.s_empty[s], 128);
         }
-        mbar_init(&bars.p_full, 128);
-        mbar_init(&bars.pv_done, 1);
-        mbar_init(&bars.x_full, 128);
-        mbar_init(&bars.x_empty, 128);
+        for (int s = 0; s < 2; s++) {
+            mbar_init(&bars.p_full[s], 128);
+            mbar_init(&bars.pv_done[s], 1);
+            mbar_init(&bars.x_full[s], 128);
+            mbar_init(&bars.x_empty[s], 128);
+        }
         fence_barrier_init();
     }
     if (warp == 1) tmem_alloc(&bars.tmem_base, MLA_TM_COLS);
@@ -183,7 +312,7 @@ mla_attend_tc(const __grid_constant__ MlaMaps maps, const MlaSeg *__restrict__ s
             prefetch_tmap(&maps.lat);
             prefetch_tmap(&maps.rope);
             int g = 0, nq = 0, prev_b = -1;
-            int last_use[MLA_NST] = {-1, -1};
+            int last_use[MLA_NST] = {-1, -1, -1, -1};
             bool ok = true;
             for (int si = sbeg; si < send && ok; si++) {
                 const MlaSeg sg = segs[si];
@@ -228,10 +357,10 @@ mla_attend_tc(const __grid_constant__ MlaMaps maps, const MlaSeg *__restrict__ s
             int pend = -1;  // tile whose PV is still to be issued
             bool pend_first = false;
             auto issue_pv = [&](int gp, bool first) -> bool {
-                if (!mbar_wait(&bars.p_full, gp & 1, err, 0x203)) return false;
+                if (!mbar_wait(&bars.p_full[gp & 1], (gp >> 1) & 1, err, 0x203)) return false;
                 tc_fence_after();
                 const uint8_t *kv = sm + MLA_OFF_KV + (gp % MLA_NST) * MLA_NBLK * MLA_KVBLK;
-                const uint8_t *P = sm + MLA_OFF_P;
+                const uint8_t *P = sm + MLA_OFF_P + (gp & 1) * MLA_PBUF;
 #pragma unroll
                 for (int ks = 0; ks < MLA_TILE / 16; ks++) {
                     const uint64_t ad = sdesc_kmajor(smem_u32(P + ks * 32));
@@ -239,7 +368,7 @@ mla_attend_tc(const __grid_constant__ MlaMaps maps, const MlaSeg *__restrict__ s
                     mma_bf16_ss(tbase + MLA_TM_O, ad, bd, id_o, (first && ks == 0) ? 0u : 1u);
                 }
                 mma_commit(&bars.kv_empty[gp % MLA_NST]);
-                mma_commit(&bars.pv_done);
+                mma_commit(&bars.pv_done[gp & 1]);
                 return true;
             };
             for (int si = sbeg; si < send && ok; si++) {
@@ -281,9 +410,7 @@ mla_attend_tc(const __grid_constant__ MlaMaps maps, const MlaSeg *__restrict__ s
         // -------------------------------------------- exchange, softmax, epilogue
         const int row = 32 * (warp & 3) + lane;  // head == TMEM lane
         const uint32_t lane_off = (uint32_t)(32 * (warp & 3)) << 16;
-        const float4 *X4 = reinterpret_cast<const float4 *>(sm + MLA_OFF_X);
         const uint32_t xpeer = map_peer(smem_u32(sm + MLA_OFF_X), peer);
-        uint8_t *P = sm + MLA_OFF_P;
         float m_ref = -INFINITY, l = 0.f;
         int g = 0, cur_slot = -1;
         bool ok = true;
@@ -323,14 +450,19 @@ mla_attend_tc(const __grid_constant__ MlaMaps maps, const MlaSeg *__restrict__ s
                 }
                 tc_fence_before();
                 mbar_arrive(&bars.s_empty[sb]);
-                // exchange partial scores with the peer; X4[i * 128 + row] = float4 i of `row`
-                if (g > 0 && !(ok = warp_wait(&bars.x_empty, (g - 1) & 1, err, 0x302, true))) break;
+                // exchange partial scores with the peer through exchange buffer xb;
+                // X4[i * 128 + row] holds float4 i of `row`
+                const int xb = g & 1;
+                const float4 *X4 = reinterpret_cast<const float4 *>(sm + MLA_OFF_X + xb * MLA_XBUF);
+                if (g >= 2 &&
+                    !(ok = warp_wait(&bars.x_empty[xb], ((g >> 1) - 1) & 1, err, 0x302, true)))
+                    break;
 #pragma unroll
                 for (int i = 0; i < MLA_TILE / 4; i++)
-                    st_cluster_v4(xpeer + (uint32_t)((i * MLA_HP + row) * 16), s[4 * i],
-                                  s[4 * i + 1], s[4 * i + 2], s[4 * i + 3]);
-                mbar_arrive_cluster(&bars.x_full, peer);
-                if (!(ok = warp_wait(&bars.x_full, g & 1, err, 0x303, true))) break;
+                    st_cluster_v4(xpeer + (uint32_t)(xb * MLA_XBUF + (i * MLA_HP + row) * 16),
+                                  s[4 * i], s[4 * i + 1], s[4 * i + 2], s[4 * i + 3]);
+                mbar_arrive_cluster(&bars.x_full[xb], peer);
+                if (!(ok = warp_wait(&bars.x_full[xb], (g >> 1) & 1, err, 0x303, true))) break;
                 const int valid = clen - t * MLA_TILE;
                 float mx = -INFINITY;
 #pragma unroll
@@ -345,11 +477,16 @@ mla_attend_tc(const __grid_constant__ MlaMaps maps, const MlaSeg *__restrict__ s
                         mx = fmaxf(mx, s[c]);
                     }
                 }
-                mbar_arrive_cluster(&bars.x_empty, peer);
-                // PV of the previous tile done: P buffer free, O stable
-                if (g > 0 && !(ok = warp_wait(&bars.pv_done, (g - 1) & 1, err, 0x304))) break;
-                tc_fence_after();
+                mbar_arrive_cluster(&bars.x_empty[xb], peer);
                 if (t == sg.t0) {
+                    // a new segment: the previous segment's last P.V must be done before its
+                    // O is read out and the next P.V overwrites it
+                    if (g > 0) {
+                        if (!(ok = warp_wait(&bars.pv_done[(g - 1) & 1], ((g - 1) >> 1) & 1, err,
+                                             0x304)))
+                            break;
+                        tc_fence_after();
+                    }
                     if (cur_slot >= 0) epilogue(cur_slot);
                     cur_slot = sg.slot;
                     m_ref = mx;
@@ -357,6 +494,11 @@ mla_attend_tc(const __grid_constant__ MlaMaps maps, const MlaSeg *__restrict__ s
                 } else {
                     const bool grow = mx > m_ref + MLA_RESCALE_LOG2;
                     if (__any_sync(0xffffffffu, grow)) {
+                        // O is rescaled in place: the previous tile's P.V must be done
+                        if (!(ok = warp_wait(&bars.pv_done[(g - 1) & 1], ((g - 1) >> 1) & 1, err,
+                                             0x306)))
+                            break;
+                        tc_fence_after();
                         const float f = grow ? exp2f(m_ref - mx) : 1.f;
                         for (int c = 0; c < 256; c += 16) {
                             float v[16];
@@ -373,7 +515,14 @@ mla_attend_tc(const __grid_constant__ MlaMaps maps, const MlaSeg *__restrict__ s
                         }
                     }
                 }
-                // P row (bf16, 128-byte swizzle: 16-byte chunk c of row r sits at c ^ (r & 7))
+                // P buffer pb is free once the P.V of tile g-2 is done
+                const int pb = g & 1;
+                uint8_t *P = sm + MLA_OFF_P + pb * MLA_PBUF;
+                if (g >= 2 &&
+                    !(ok = warp_wait(&bars.pv_done[pb], ((g >> 1) - 1) & 1, err, 0x307)))
+                    break;
+                // P row (bf16, 128-byte swizzle: 16-byte chunk c of row r sits at c ^ (r & 7);
+                // a 32-token tile fills chunks 0..3 of each 128-byte row)
                 float rs = 0.f;
                 uint32_t pk[MLA_TILE / 2];
 #pragma unroll
@@ -385,7 +534,7 @@ mla_attend_tc(const __grid_constant__ MlaMaps maps, const MlaSeg *__restrict__ s
                 }
                 l += rs;
 #pragma unroll
-                for (int c = 0; c < 8; c++)
+                for (int c = 0; c < MLA_TILE / 8; c++)
                     *reinterpret_cast<uint4 *>(P + row * 128 + ((c ^ (row & 7)) * 16)) =
                         make_uint4(pk[4 * c], pk[4 * c + 1], pk[4 * c + 2], pk[4 * c + 3]);
                 if (valid < MLA_TILE) {
@@ -401,10 +550,10 @@ mla_attend_tc(const __grid_constant__ MlaMaps maps, const MlaSeg *__restrict__ s
                 }
                 fence_async_shared();
                 tc_fence_before();
-                mbar_arrive(&bars.p_full);
+                mbar_arrive(&bars.p_full[pb]);
             }
         }
-        if (ok && g > 0 && warp_wait(&bars.pv_done, (g - 1) & 1, err, 0x305)) {
+        if (ok && g > 0 && warp_wait(&bars.pv_done[(g - 1) & 1], ((g - 1) >> 1) & 1, err, 0x305)) {
             tc_fence_after();
             epilogue(cur_slot);
         }
@@ -418,77 +567,41 @@ mla_attend_tc(const __grid_constant__ MlaMaps maps, const MlaSeg *__restrict__ s
     }
 }
 
-// ------------------------------------------------------------------ merge + project
-// One CTA per head: merge every sequence's segments (max, sum, o_lat) into o_lat, then
-// out[b][h][:] = W_UV[h] o_lat[b] as a [64 x 512] x [512 x 128] tile product per 64
-// sequences (each thread 4 sequences x 8 outputs).
-template <typename OUT>
-__global__ void __launch_bounds__(256)
-mla_merge_project(const float *__restrict__ part, const int *__restrict__ slot0,
-                  const __nv_bfloat16 *__restrict__ w_uv, OUT *__restrict__ out, int B, int H,
-                  int nslots) {
-    extern __shared__ float msm[];
-    float *wsl = msm;             // [nslots] merge weight of each slot (this head)
-    float *sA = wsl + nslots;     // [64 b][65] o_lat chunk (padded)
-    float *sW = sA + 64 * 65;     // [128 j][65] W_UV chunk (padded)
-    const int h = blockIdx.x, tid = threadIdx.x;
-    const size_t hs = (size_t)h * MLA_PART, sstride = (size_t)H * MLA_PART;
-    for (int b = tid; b < B; b += 256) {
-        float M = -INFINITY;
-        for (int s = slot0[b]; s < slot0[b + 1]; s++) M = fmaxf(M, part[s * sstride + hs + MLA_DL]);
-        float L = 0.f;
-        for (int s = slot0[b]; s < slot0[b + 1]; s++)
-            L += exp2f(part[s * sstride + hs + MLA_DL] - M) * part[s * sstride + hs + MLA_DL + 1];
-        for (int s = slot0[b]; s < slot0[b + 1]; s++)
-            wsl[s] = exp2f(part[s * sstride + hs + MLA_DL] - M) / L;
+// ---------------------------------------------------------------------------- merge
+// One CTA per (head, sequence): combine the sequence's segments (max, sum, o_lat) by the
+// flash-decoding identity and write o_lat as a bf16 hi/lo pair [B][H][hi 512 | lo 512] for
+// mla_project_tc. Thread t owns latent elements 4t .. 4t+3.
+__global__ void __launch_bounds__(128)
+mla_merge(const float *__restrict__ part, const int *__restrict__ slot0,
+          __nv_bfloat16 *__restrict__ olat2, int H) {
+    const int h = blockIdx.x, b = blockIdx.y, tid = threadIdx.x;
+    const int s0 = slot0[b], s1 = slot0[b + 1];
+    const size_t stride = (size_t)H * MLA_PART;
+    const float *base = part + (size_t)h * MLA_PART;
+    float M = -INFINITY;
+    for (int s = s0; s < s1; s++) M = fmaxf(M, base[s * stride + MLA_DL]);
+    float L = 0.f;
+    for (int s = s0; s < s1; s++) L += exp2f(base[s * stride + MLA_DL] - M) * base[s * stride + MLA_DL + 1];
+    const float invL = 1.f / L;
+    float4 o = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int s = s0; s < s1; s++) {
+        const float w = exp2f(base[s * stride + MLA_DL] - M) * invL;
+        const float4 p = reinterpret_cast<const float4 *>(base + s * stride)[tid];
+        o.x += w * p.x; o.y += w * p.y; o.z += w * p.z; o.w += w * p.w;
     }
-    __syncthreads();
-    const int tb = tid / 16, tj = tid % 16;  // 16 x 16 threads: 4 b x 8 j each
-    const __nv_bfloat16 *W = w_uv + (size_t)h * MLA_DV * MLA_DL;
-    for (int b0 = 0; b0 < B; b0 += 64) {
-        float acc[4][8];
+    const float ov[4] = {o.x, o.y, o.z, o.w};
+    uint32_t hi[2], lo[2];
 #pragma unroll
-        for (int i = 0; i < 4; i++)
-#pragma unroll
-            for (int j = 0; j < 8; j++) acc[i][j] = 0.f;
-        for (int k0 = 0; k0 < MLA_DL; k0 += 64) {
-            __syncthreads();
-            for (int e = tid; e < 64 * 64; e += 256) {
-                const int bb = e / 64, kk = e % 64, b = b0 + bb;
-                float a = 0.f;
-                if (b < B)
-                    for (int s = slot0[b]; s < slot0[b + 1]; s++)
-                        a += wsl[s] * part[s * sstride + hs + k0 + kk];
-                sA[bb * 65 + kk] = a;
-            }
-            for (int e = tid; e < 128 * 64; e += 256) {
-                const int j = e / 64, kk = e % 64;
-                sW[j * 65 + kk] = bf(W + (size_t)j * MLA_DL + k0 + kk);
-            }
-            __syncthreads();
-#pragma unroll 4
-            for (int kk = 0; kk < 64; kk++) {
-                float a[4], w[8];
-#pragma unroll
-                for (int i = 0; i < 4; i++) a[i] = sA[(tb * 4 + i) * 65 + kk];
-#pragma unroll
-                for (int j = 0; j < 8; j++) w[j] = sW[(tj + 16 * j) * 65 + kk];
-#pragma unroll
-                for (int i = 0; i < 4; i++)
-#pragma unroll
-                    for (int j = 0; j < 8; j++) acc[i][j] += a[i] * w[j];
-            }
-        }
-#pragma unroll
-        for (int i = 0; i < 4; i++) {
-            const int b = b0 + tb * 4 + i;
-            if (b < B) {
-#pragma unroll
-                for (int j = 0; j < 8; j++)
-                    io<OUT>::st(out + ((size_t)b * H + h) * MLA_DV + tj + 16 * j, acc[i][j]);
-            }
-        }
+    for (int i = 0; i < 2; i++) {
+        const __nv_bfloat162 t = __floats2bfloat162_rn(ov[2 * i], ov[2 * i + 1]);
+        const float2 tf = __bfloat1622float2(t);
+        const __nv_bfloat162 r = __floats2bfloat162_rn(ov[2 * i] - tf.x, ov[2 * i + 1] - tf.y);
+        hi[i] = *reinterpret_cast<const uint32_t *>(&t);
+        lo[i] = *reinterpret_cast<const uint32_t *>(&r);
     }
+    __nv_bfloat16 *dst = olat2 + ((size_t)b * H + h) * 2 * MLA_DL;
+    reinterpret_cast<uint2 *>(dst)[tid] = make_uint2(hi[0], hi[1]);
+    reinterpret_cast<uint2 *>(dst + MLA_DL)[tid] = make_uint2(lo[0], lo[1]);
 }
 
 // ---------------------------------------------------------------------- host side
@@ -533,7 +646,8 @@ static size_t mla_ws_bytes(const MlaPlan &p, int B, int H) {
     return align256(p.segs.size() * sizeof(MlaSeg)) + align256(p.cl_begin.size() * sizeof(int)) +
            align256(((size_t)B + 1) * sizeof(int)) + align256((size_t)B * sizeof(int)) +
            align256((size_t)B * MLA_HP * MLA_QW * 2) +
-           align256(p.segs.size() * (size_t)H * MLA_PART * sizeof(float));
+           align256(p.segs.size() * (size_t)H * MLA_PART * sizeof(float)) +
+           align256((size_t)B * H * 2 * MLA_DL * 2);
 }
 
 constexpr int MLA_MAX_CLUSTERS = 74;  // 148 SMs of a B200, two per cluster
@@ -596,6 +710,8 @@ extern "C" int k3cuda_mla_decode(k3cuda_ctx *ctx, void *out, int out_dtype, cons
     __nv_bfloat16 *qlat = (__nv_bfloat16 *)w;
     w += align256((size_t)B * MLA_HP * MLA_QW * 2);
     float *part = (float *)w;
+    w += align256((size_t)nseg * H * MLA_PART * sizeof(float));
+    __nv_bfloat16 *olat2 = (__nv_bfloat16 *)w;
     K3_CUDA_TRY(cudaMemcpyAsync(d_segs, p.segs.data(), (size_t)nseg * sizeof(MlaSeg),
                                 cudaMemcpyHostToDevice, ctx->stream));
     K3_CUDA_TRY(cudaMemcpyAsync(d_cl, p.cl_begin.data(), p.cl_begin.size() * sizeof(int),
@@ -604,22 +720,44 @@ extern "C" int k3cuda_mla_decode(k3cuda_ctx *ctx, void *out, int out_dtype, cons
                                 cudaMemcpyHostToDevice, ctx->stream));
     K3_CUDA_TRY(cudaMemcpyAsync(d_lens, ctx_lens, (size_t)B * sizeof(int), cudaMemcpyHostToDevice,
                                 ctx->stream));
+    if (H < MLA_HP)  // the padded query rows must score zero
+        K3_CUDA_TRY(cudaMemset2DAsync(qlat + (size_t)H * MLA_QW, (size_t)MLA_HP * MLA_QW * 2, 0,
+                                      (size_t)(MLA_HP - H) * MLA_QW * 2, (size_t)B, ctx->stream));
 
+    const CUtensorMapDataType BF = CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+    HeadGemmMaps qmaps, pmaps;
     MlaMaps maps;
-    rc = make_tmap_2d(&maps.q, qlat, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, MLA_QW,
-                      (uint64_t)B * MLA_HP, MLA_QW * 2, 64, MLA_HP);
+    rc = make_tmap_3d(&qmaps.a, q_nope, BF, 2, MLA_DN, H, B, MLA_DN * 2, (uint64_t)H * MLA_DN * 2,
+                      64, 1, 128);
     if (!rc)
-        rc = make_tmap_2d(&maps.lat, latent, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, MLA_DL,
-                          (uint64_t)B * cap, MLA_DL * 2, 64, MLA_TILE);
+        rc = make_tmap_3d(&qmaps.b, w_uk, BF, 2, MLA_DL, MLA_DN, H, MLA_DL * 2,
+                          (uint64_t)MLA_DN * MLA_DL * 2, 64, 64, 1);
     if (!rc)
-        rc = make_tmap_2d(&maps.rope, rope, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, MLA_DR,
-                          (uint64_t)B * cap, MLA_DR * 2, 64, MLA_TILE);
+        rc = make_tmap_2d(&maps.q, qlat, BF, 2, MLA_QW, (uint64_t)B * MLA_HP, MLA_QW * 2, 64, MLA_HP);
+    if (!rc)
+        rc = make_tmap_2d(&maps.lat, latent, BF, 2, MLA_DL, (uint64_t)B * cap, MLA_DL * 2, 64,
+                          MLA_TILE);
+    if (!rc)
+        rc = make_tmap_2d(&maps.rope, rope, BF, 2, MLA_DR, (uint64_t)B * cap, MLA_DR * 2, 64,
+                          MLA_TILE);
+    if (!rc)
+        rc = make_tmap_3d(&pmaps.a, olat2, BF, 2, 2 * MLA_DL, H, B, 2 * MLA_DL * 2,
+                          (uint64_t)H * 2 * MLA_DL * 2, 64, 1, 128);
+    if (!rc)
+        rc = make_tmap_3d(&pmaps.b, w_uv, BF, 2, MLA_DL, MLA_DV, H, MLA_DL * 2,
+                          (uint64_t)MLA_DV * MLA_DL * 2, 64, 128, 1);
     if (rc) return rc;
+    K3_ARG_CHECK(aligned(q_nope, 16) && aligned(q_rope, 16) && aligned(w_uk, 16) &&
+                     aligned(w_uv, 16),
+                 "MLA inputs must be 16-byte aligned");
 
-    mla_q_absorb<<<dim3(MLA_HP, (B + 15) / 16), 256, 0, ctx->stream>>>(
-        (const __nv_bfloat16 *)q_nope, (const __nv_bfloat16 *)q_rope,
-        (const __nv_bfloat16 *)w_uk, qlat, B, H);
-    rc = after_launch(ctx, "mla_q_absorb");
+    const dim3 hgrid(H, (B + 127) / 128);
+    const int qsmem = 2 * 16384 + 16 * 8192 + 1024;
+    K3_CUDA_TRY(cudaFuncSetAttribute(mla_q_absorb_tc, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     qsmem));
+    mla_q_absorb_tc<<<hgrid, 128, qsmem, ctx->stream>>>(qmaps, (const __nv_bfloat16 *)q_rope, qlat,
+                                                        B, H, ctx->err_word);
+    rc = after_launch(ctx, "mla_q_absorb_tc");
     if (rc) return rc;
 
     K3_CUDA_TRY(cudaFuncSetAttribute(mla_attend_tc, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -630,17 +768,21 @@ extern "C" int k3cuda_mla_decode(k3cuda_ctx *ctx, void *out, int out_dtype, cons
     rc = after_launch(ctx, "mla_attend_tc");
     if (rc) return rc;
 
-    const size_t msmem = ((size_t)nseg + 64 * 65 + 128 * 65) * sizeof(float);
+    mla_merge<<<dim3(H, B), 128, 0, ctx->stream>>>(part, d_slot0, olat2, H);
+    rc = after_launch(ctx, "mla_merge");
+    if (rc) return rc;
+
+    const int psmem = 12 * 16384 + 1024;
     if (out_dtype == K3CUDA_BF16) {
-        K3_CUDA_TRY(cudaFuncSetAttribute(mla_merge_project<__nv_bfloat16>,
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize, (int)msmem));
-        mla_merge_project<__nv_bfloat16><<<H, 256, msmem, ctx->stream>>>(
-            part, d_slot0, (const __nv_bfloat16 *)w_uv, (__nv_bfloat16 *)out, B, H, nseg);
+        K3_CUDA_TRY(cudaFuncSetAttribute(mla_project_tc<__nv_bfloat16>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, psmem));
+        mla_project_tc<__nv_bfloat16><<<hgrid, 128, psmem, ctx->stream>>>(
+            pmaps, (__nv_bfloat16 *)out, B, H, ctx->err_word);
     } else {
-        K3_CUDA_TRY(cudaFuncSetAttribute(mla_merge_project<float>,
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize, (int)msmem));
-        mla_merge_project<float><<<H, 256, msmem, ctx->stream>>>(
-            part, d_slot0, (const __nv_bfloat16 *)w_uv, (float *)out, B, H, nseg);
+        K3_CUDA_TRY(cudaFuncSetAttribute(mla_project_tc<float>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, psmem));
+        mla_project_tc<float><<<hgrid, 128, psmem, ctx->stream>>>(pmaps, (float *)out, B, H,
+                                                                  ctx->err_word);
     }
-    return after_launch(ctx, "mla_merge_project");
+    return after_launch(ctx, "mla_project_tc");
 }

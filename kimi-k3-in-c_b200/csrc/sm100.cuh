@@ -86,18 +86,34 @@ __device__ __forceinline__ bool mbar_try_wait_cluster(uint64_t *bar, uint32_t pa
 constexpr long long kWaitCycles = 1ll << 31;
 
 // Bounded wait; on timeout records `code` in *err (first error wins) and returns false.
-__device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, unsigned *err,
-                                          unsigned code) {
-    if (mbar_try_wait(bar, parity)) return true;
+// try_wait blocks in hardware for a while before returning false, so the loop spins slowly;
+// the error word (another role's timeout) and the clock are only checked every 64 tries,
+// which keeps a global load off the fast path.
+template <bool kCluster>
+__device__ __forceinline__ bool mbar_wait_impl(uint64_t *bar, uint32_t parity, unsigned *err,
+                                               unsigned code) {
+    if (kCluster ? mbar_try_wait_cluster(bar, parity) : mbar_try_wait(bar, parity)) return true;
     const long long t0 = clock64();
-    while (!mbar_try_wait(bar, parity)) {
-        if (*(volatile unsigned *)err) return false;
-        if (clock64() - t0 > kWaitCycles) {
-            atomicCAS(err, 0u, code);
-            return false;
+    for (uint32_t i = 1;; i++) {
+        if (kCluster ? mbar_try_wait_cluster(bar, parity) : mbar_try_wait(bar, parity)) return true;
+        if ((i & 63) == 0) {
+            if (*(volatile unsigned *)err) return false;
+            if (clock64() - t0 > kWaitCycles) {
+                atomicCAS(err, 0u, code);
+                return false;
+            }
         }
     }
-    return true;
+}
+
+__device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, unsigned *err,
+                                          unsigned code) {
+    return mbar_wait_impl<false>(bar, parity, err, code);
+}
+
+__device__ __forceinline__ bool mbar_wait_cluster(uint64_t *bar, uint32_t parity, unsigned *err,
+                                                  unsigned code) {
+    return mbar_wait_impl<true>(bar, parity, err, code);
 }
 
 // Bounded wait that reports nothing (used only to drain a CTA's own loads on exit).
@@ -105,20 +121,6 @@ __device__ __forceinline__ bool mbar_wait_quiet(uint64_t *bar, uint32_t parity) 
     const long long t0 = clock64();
     while (!mbar_try_wait(bar, parity))
         if (clock64() - t0 > kWaitCycles) return false;
-    return true;
-}
-
-__device__ __forceinline__ bool mbar_wait_cluster(uint64_t *bar, uint32_t parity, unsigned *err,
-                                                  unsigned code) {
-    if (mbar_try_wait_cluster(bar, parity)) return true;
-    const long long t0 = clock64();
-    while (!mbar_try_wait_cluster(bar, parity)) {
-        if (*(volatile unsigned *)err) return false;
-        if (clock64() - t0 > kWaitCycles) {
-            atomicCAS(err, 0u, code);
-            return false;
-        }
-    }
     return true;
 }
 
