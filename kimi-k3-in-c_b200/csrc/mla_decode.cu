@@ -16,20 +16,23 @@
 // The 576-wide contraction of S is split across the pair -- rank 0 takes latent dims
 // [0,256) and the 64 rope dims, rank 1 latent dims [256,512) -- and each rank accumulates
 // the output for its own 256 latent dims, which are exactly the dims whose tiles it already
-// holds. Per 32-token tile each rank computes its partial S, the ranks exchange the partials
-// through distributed shared memory, both add them in the same order (rank 0's + rank 1's),
-// so both derive the same softmax, and each multiplies P by its half of the tile. Per SM:
-//   shared  Q half 80 KB + 4 KV stages x 20 KB + 2 P x 16 KB + 2 exchange x 16 KB (~225 KB)
-//   TMEM    S double buffer 2 x 32 columns + O 256 columns                         (of 512)
-// P and the exchange buffers are double-buffered so that the softmax of tile g overlaps the
-// P.V product of tile g-1.
-// Warp roles: warp 0 issues TMA loads, warp 1 allocates TMEM and issues the MMAs, warps 2-5
-// (one thread per head = TMEM lane) run the exchange, the softmax and the epilogue. The
-// running max is only moved when it grows by more than 2^8 (a lazy rescale: numerator and
-// denominator use the same stale max, so the result is exact), which keeps the O rescale in
-// TMEM off the common path.
+// holds. Per 64-token tile each rank computes its partial S, sends it to the peer with
+// asynchronous cluster stores that complete on the peer's mbarrier (no fences on the path),
+// both add the two partials in the same order (rank 0's + rank 1's), so both derive the same
+// softmax, and each multiplies P by its half of the tile. Per SM:
+//   TMEM    S 64 columns + this rank's query half (160 columns, the MMA's A operand read
+//           straight from TMEM) + O 256 columns                                     (of 512)
+//   shared  3 KV stages x 40 KB + 2 P x 16 KB + 2 exchange x 32 KB                 (~217 KB)
+// Keeping the query in TMEM leaves shared memory to the KV pipeline. P and the exchange
+// buffers are double-buffered so that the softmax of tile g overlaps the P.V product of
+// tile g-1.
+// Warp roles: warp 0 issues TMA loads; warp 1 allocates TMEM and issues S = Q.K^T; warp 6
+// issues O += P.V; warps 2-5 (one thread per head = TMEM lane) write the query into TMEM,
+// run the exchange, the softmax and the epilogue. The running max is only moved when it
+// grows by more than 2^8 (a lazy rescale: numerator and denominator use the same stale max,
+// so the result is exact), which keeps the O rescale in TMEM off the common path.
 //
-// Work: the (sequence, 32-token tile) list is cut into equal contiguous ranges, one per
+// Work: the (sequence, 64-token tile) list is cut into equal contiguous ranges, one per
 // cluster; a range that crosses sequences becomes several segments, each writing a partial
 // (max, sum, o_lat) per head; mla_merge combines the segments of every sequence (the
 // flash-decoding identity) and mla_project_tc applies W_UV.
@@ -51,21 +54,21 @@ using namespace sm100;
 constexpr int MLA_DN = 128, MLA_DR = 64, MLA_DL = 512, MLA_DV = 128;
 constexpr int MLA_QW = MLA_DL + MLA_DR;    // 576: absorbed query width
 constexpr int MLA_HP = 128;                // heads padded to the MMA's M
-constexpr int MLA_TILE = 32;               // tokens per tile
-constexpr int MLA_NST = 4;                 // KV pipeline stages
-constexpr int MLA_QBLK = MLA_HP * 128;     // bytes of one 64-dim block of Q (128 rows x 128 B)
+constexpr int MLA_TILE = 64;               // tokens per tile
+constexpr int MLA_NST = 3;                 // KV pipeline stages
 constexpr int MLA_KVBLK = MLA_TILE * 128;  // bytes of one 64-dim block of a KV tile
 constexpr int MLA_NBLK = 5;                // dim blocks of rank 0 (4 latent + rope); rank 1: 4
-constexpr int MLA_OFF_Q = 0;
-constexpr int MLA_OFF_KV = MLA_OFF_Q + MLA_NBLK * MLA_QBLK;
+constexpr int MLA_OFF_KV = 0;
 constexpr int MLA_OFF_P = MLA_OFF_KV + MLA_NST * MLA_NBLK * MLA_KVBLK;
 constexpr int MLA_PBUF = MLA_HP * 128;     // one P buffer: 128 rows x 128 B (K-major, SW128)
 constexpr int MLA_OFF_X = MLA_OFF_P + 2 * MLA_PBUF;
-constexpr int MLA_XBUF = MLA_HP * MLA_TILE * 4;  // one exchange buffer: 128 heads x 32 fp32
+constexpr int MLA_XBUF = MLA_HP * MLA_TILE * 4;  // one exchange buffer: 128 heads x 64 fp32
 constexpr int MLA_SMEM = MLA_OFF_X + 2 * MLA_XBUF + 1024;  // + alignment slack
 constexpr int MLA_PART = MLA_DL + 4;       // floats per (segment, head): o_lat, max, sum, pad
                                            // (rows stay 16-byte aligned for float4 stores)
-constexpr int MLA_TM_S = 0, MLA_TM_O = 128, MLA_TM_COLS = 512;
+// TMEM columns: S [0, 64), this rank's query half [64, 224) (two bf16 per column),
+// O [256, 512)
+constexpr int MLA_TM_S = 0, MLA_TM_Q = 64, MLA_TM_O = 256, MLA_TM_COLS = 512;
 constexpr float MLA_RESCALE_LOG2 = 8.f;    // lazy rescale threshold (factor 256)
 
 __device__ __forceinline__ float bf(const __nv_bfloat16 *p) { return __bfloat162float(*p); }
@@ -252,7 +255,7 @@ struct MlaSeg {
 };
 
 struct MlaMaps {
-    CUtensorMap q, lat, rope;
+    CUtensorMap lat, rope;
 };
 
 struct MlaBars {
@@ -260,15 +263,15 @@ struct MlaBars {
     uint64_t q_full, q_empty;
     uint64_t s_full[2], s_empty[2];
     uint64_t p_full[2], pv_done[2];
-    uint64_t x_full[2], x_empty[2];
+    uint64_t x_full[2], x_empty[2], x_read[2];
     uint32_t tmem_base;
 };
 
-__global__ void __launch_bounds__(192, 1) __cluster_dims__(2, 1, 1)
+__global__ void __launch_bounds__(224, 1) __cluster_dims__(2, 1, 1)
 mla_attend_tc(const __grid_constant__ MlaMaps maps, const MlaSeg *__restrict__ segs,
               const int *__restrict__ cl_begin, const int *__restrict__ ctx_lens,
-              float *__restrict__ part, int H, int cap, float scale_log2e,
-              unsigned *__restrict__ err) {
+              const __nv_bfloat16 *__restrict__ qlat, float *__restrict__ part, int H, int cap,
+              float scale_log2e, unsigned *__restrict__ err) {
     extern __shared__ uint8_t smraw[];
     uint8_t *sm = (uint8_t *)(((uintptr_t)smraw + 1023) & ~(uintptr_t)1023);
     __shared__ MlaBars bars;
@@ -284,17 +287,16 @@ mla_attend_tc(const __grid_constant__ MlaMaps maps, const MlaSeg *__restrict__ s
             mbar_init(&bars.kv_full[s], 1);
             mbar_init(&bars.kv_empty[s], 1);
         }
-        mbar_init(&bars.q_full, 1);
+        mbar_init(&bars.q_full, 128);
         mbar_init(&bars.q_empty, 1);
         for (int s = 0; s < 2; s++) {
             mbar_init(&bars.s_full[s], 1);
             mbar_init(&bars.s_empty[s], 128);
-        }
-        for (int s = 0; s < 2; s++) {
             mbar_init(&bars.p_full[s], 128);
             mbar_init(&bars.pv_done[s], 1);
-            mbar_init(&bars.x_full[s], 128);
-            mbar_init(&bars.x_empty[s], 128);
+            mbar_init(&bars.x_full[s], 1);
+            mbar_init(&bars.x_empty[s], 1);
+            mbar_init(&bars.x_read[s], 128);
         }
         fence_barrier_init();
     }
@@ -308,26 +310,14 @@ mla_attend_tc(const __grid_constant__ MlaMaps maps, const MlaSeg *__restrict__ s
     if (warp == 0) {
         // ------------------------------------------------------------ TMA producer
         if (lane == 0) {
-            prefetch_tmap(&maps.q);
             prefetch_tmap(&maps.lat);
             prefetch_tmap(&maps.rope);
-            int g = 0, nq = 0, prev_b = -1;
-            int last_use[MLA_NST] = {-1, -1, -1, -1};
+            int g = 0;
+            int last_use[MLA_NST];
+            for (int st = 0; st < MLA_NST; st++) last_use[st] = -1;
             bool ok = true;
             for (int si = sbeg; si < send && ok; si++) {
                 const MlaSeg sg = segs[si];
-                if (sg.b != prev_b) {
-                    if (nq > 0) ok = mbar_wait(&bars.q_empty, (nq - 1) & 1, err, 0x101);
-                    if (!ok) break;
-                    mbar_expect_tx(&bars.q_full, nblk * MLA_QBLK);
-                    for (int kb = 0; kb < nblk; kb++) {
-                        const int col = kb < 4 ? dim0 + kb * 64 : MLA_DL;
-                        tma_load_2d(sm + MLA_OFF_Q + kb * MLA_QBLK, &maps.q, &bars.q_full, col,
-                                    sg.b * MLA_HP);
-                    }
-                    nq++;
-                    prev_b = sg.b;
-                }
                 for (int t = sg.t0; t < sg.t1; t++, g++) {
                     const int st = g % MLA_NST, n = g / MLA_NST;
                     if (n > 0 && !(ok = mbar_wait(&bars.kv_empty[st], (n - 1) & 1, err, 0x102)))
@@ -348,71 +338,69 @@ mla_attend_tc(const __grid_constant__ MlaMaps maps, const MlaSeg *__restrict__ s
                 if (last_use[st] >= 0) mbar_wait_quiet(&bars.kv_full[st], last_use[st] & 1);
         }
     } else if (warp == 1) {
-        // ----------------------------------------------------------------- MMA issuer
+        // ------------------------------------------------- S issuer: S = Q . K^T
         if (lane == 0) {
             constexpr uint32_t id_s = idesc_f16(128, MLA_TILE, false, false);
-            constexpr uint32_t id_o = idesc_f16(128, 256, false, true);
             int g = 0, nq = 0, prev_b = -1;
             bool ok = true;
-            int pend = -1;  // tile whose PV is still to be issued
-            bool pend_first = false;
-            auto issue_pv = [&](int gp, bool first) -> bool {
-                if (!mbar_wait(&bars.p_full[gp & 1], (gp >> 1) & 1, err, 0x203)) return false;
-                tc_fence_after();
-                const uint8_t *kv = sm + MLA_OFF_KV + (gp % MLA_NST) * MLA_NBLK * MLA_KVBLK;
-                const uint8_t *P = sm + MLA_OFF_P + (gp & 1) * MLA_PBUF;
-#pragma unroll
-                for (int ks = 0; ks < MLA_TILE / 16; ks++) {
-                    const uint64_t ad = sdesc_kmajor(smem_u32(P + ks * 32));
-                    const uint64_t bd = sdesc_mnmajor(smem_u32(kv + ks * 2048), MLA_KVBLK);
-                    mma_bf16_ss(tbase + MLA_TM_O, ad, bd, id_o, (first && ks == 0) ? 0u : 1u);
-                }
-                mma_commit(&bars.kv_empty[gp % MLA_NST]);
-                mma_commit(&bars.pv_done[gp & 1]);
-                return true;
-            };
             for (int si = sbeg; si < send && ok; si++) {
                 const MlaSeg sg = segs[si];
                 const bool qlast = si + 1 >= send || segs[si + 1].b != sg.b;
-                if (sg.b != prev_b) {
+                if (sg.b != prev_b) {  // the softmax warps have written this batch's Q
                     if (!(ok = mbar_wait(&bars.q_full, nq & 1, err, 0x201))) break;
                     nq++;
                     prev_b = sg.b;
                 }
                 for (int t = sg.t0; t < sg.t1 && ok; t++, g++) {
-                    const int st = g % MLA_NST, sb = g & 1;
+                    const int st = g % MLA_NST, sb = 0;
                     if (!(ok = mbar_wait(&bars.kv_full[st], (g / MLA_NST) & 1, err, 0x202))) break;
-                    if (g >= 2 &&
-                        !(ok = mbar_wait(&bars.s_empty[sb], ((g >> 1) - 1) & 1, err, 0x204)))
+                    if (g >= 1 && !(ok = mbar_wait(&bars.s_empty[0], (g - 1) & 1, err, 0x204)))
                         break;
                     tc_fence_after();
                     const uint8_t *kv = sm + MLA_OFF_KV + st * MLA_NBLK * MLA_KVBLK;
                     for (int kb = 0; kb < nblk; kb++)
 #pragma unroll
-                        for (int ks = 0; ks < 4; ks++) {
-                            const uint64_t ad =
-                                sdesc_kmajor(smem_u32(sm + MLA_OFF_Q + kb * MLA_QBLK + ks * 32));
-                            const uint64_t bd =
-                                sdesc_kmajor(smem_u32(kv + kb * MLA_KVBLK + ks * 32));
-                            mma_bf16_ss(tbase + MLA_TM_S + sb * MLA_TILE, ad, bd, id_s,
+                        for (int ks = 0; ks < 4; ks++)
+                            mma_bf16_ts(tbase + MLA_TM_S + sb * MLA_TILE,
+                                        tbase + MLA_TM_Q + kb * 32 + ks * 8,
+                                        sdesc_kmajor(smem_u32(kv + kb * MLA_KVBLK + ks * 32)), id_s,
                                         (kb | ks) ? 1u : 0u);
-                        }
                     mma_commit(&bars.s_full[sb]);
                     if (qlast && t + 1 == sg.t1) mma_commit(&bars.q_empty);
-                    if (pend >= 0 && !(ok = issue_pv(pend, pend_first))) break;
-                    pend = g;
-                    pend_first = t == sg.t0;
                 }
             }
-            if (ok && pend >= 0) issue_pv(pend, pend_first);
+        }
+    } else if (warp == 6) {
+        // ------------------------------------------ PV issuer: O (+)= P . V_half
+        if (lane == 0) {
+            constexpr uint32_t id_o = idesc_f16(128, 256, false, true);
+            int g = 0;
+            for (int si = sbeg; si < send; si++) {
+                const MlaSeg sg = segs[si];
+                bool ok = true;
+                for (int t = sg.t0; t < sg.t1; t++, g++) {
+                    if (!(ok = mbar_wait(&bars.p_full[g & 1], (g >> 1) & 1, err, 0x203))) break;
+                    tc_fence_after();
+                    const uint8_t *kv = sm + MLA_OFF_KV + (g % MLA_NST) * MLA_NBLK * MLA_KVBLK;
+                    const uint8_t *P = sm + MLA_OFF_P + (g & 1) * MLA_PBUF;
+#pragma unroll
+                    for (int ks = 0; ks < MLA_TILE / 16; ks++)
+                        mma_bf16_ss(tbase + MLA_TM_O, sdesc_kmajor(smem_u32(P + ks * 32)),
+                                    sdesc_mnmajor(smem_u32(kv + ks * 2048), MLA_KVBLK), id_o,
+                                    (t == sg.t0 && ks == 0) ? 0u : 1u);
+                    mma_commit(&bars.kv_empty[g % MLA_NST]);
+                    mma_commit(&bars.pv_done[g & 1]);
+                }
+                if (!ok) break;
+            }
         }
     } else {
-        // -------------------------------------------- exchange, softmax, epilogue
+        // ------------------------------------- Q load, exchange, softmax, epilogue
         const int row = 32 * (warp & 3) + lane;  // head == TMEM lane
         const uint32_t lane_off = (uint32_t)(32 * (warp & 3)) << 16;
         const uint32_t xpeer = map_peer(smem_u32(sm + MLA_OFF_X), peer);
         float m_ref = -INFINITY, l = 0.f;
-        int g = 0, cur_slot = -1;
+        int g = 0, cur_slot = -1, nq = 0, prev_b = -1;
         bool ok = true;
         auto epilogue = [&](int slot) {  // warp-collective: every lane loads its row
             float *dst = part + ((size_t)slot * H + row) * MLA_PART;
@@ -435,10 +423,40 @@ mla_attend_tc(const __grid_constant__ MlaMaps maps, const MlaSeg *__restrict__ s
         for (int si = sbeg; si < send && ok; si++) {
             const MlaSeg sg = segs[si];
             const int clen = ctx_lens[sg.b];
+            if (sg.b != prev_b) {
+                // this rank's query half into TMEM (lane = head, two bf16 per column): the
+                // previous batch's S products must be done with the old one
+                if (nq > 0 && !(ok = warp_wait(&bars.q_empty, (nq - 1) & 1, err, 0x308))) break;
+                tc_fence_after();
+                const uint4 *qrow =
+                    reinterpret_cast<const uint4 *>(qlat + ((size_t)sg.b * MLA_HP + row) * MLA_QW);
+                for (int kb = 0; kb < nblk; kb++) {
+                    const int d0 = kb < 4 ? dim0 + kb * 64 : MLA_DL;  // first dim of block
+#pragma unroll
+                    for (int half = 0; half < 2; half++) {
+                        float v[16];
+#pragma unroll
+                        for (int i = 0; i < 4; i++) {
+                            const uint4 w = qrow[(d0 + half * 32) / 8 + i];
+                            v[4 * i] = __uint_as_float(w.x);
+                            v[4 * i + 1] = __uint_as_float(w.y);
+                            v[4 * i + 2] = __uint_as_float(w.z);
+                            v[4 * i + 3] = __uint_as_float(w.w);
+                        }
+                        tmem_st16(tbase + lane_off + MLA_TM_Q + kb * 32 + half * 16, v);
+                    }
+                }
+                tmem_wait_st();
+                tc_fence_before();
+                mbar_arrive(&bars.q_full);
+                nq++;
+                prev_b = sg.b;
+            }
             for (int t = sg.t0; t < sg.t1; t++, g++) {
-                const int sb = g & 1;
+                const int sb = 0, xb = g & 1, pb = g & 1;
+                if (row == 0) mbar_expect_tx(&bars.x_full[xb], MLA_XBUF);
                 float s[MLA_TILE];
-                if (!(ok = warp_wait(&bars.s_full[sb], (g >> 1) & 1, err, 0x301))) break;
+                if (!(ok = warp_wait(&bars.s_full[0], g & 1, err, 0x301))) break;
                 tc_fence_after();
 #pragma unroll
                 for (int c = 0; c < MLA_TILE; c += 16) {
@@ -450,19 +468,19 @@ mla_attend_tc(const __grid_constant__ MlaMaps maps, const MlaSeg *__restrict__ s
                 }
                 tc_fence_before();
                 mbar_arrive(&bars.s_empty[sb]);
-                // exchange partial scores with the peer through exchange buffer xb;
-                // X4[i * 128 + row] holds float4 i of `row`
-                const int xb = g & 1;
-                const float4 *X4 = reinterpret_cast<const float4 *>(sm + MLA_OFF_X + xb * MLA_XBUF);
+                // send this rank's partial scores into the peer's exchange buffer xb
+                // (X4[i * 128 + row] = float4 i of `row`); the transfer completes on the
+                // peer's x_full[xb]
                 if (g >= 2 &&
                     !(ok = warp_wait(&bars.x_empty[xb], ((g >> 1) - 1) & 1, err, 0x302, true)))
                     break;
+                const uint32_t rbar = map_peer(smem_u32(&bars.x_full[xb]), peer);
 #pragma unroll
                 for (int i = 0; i < MLA_TILE / 4; i++)
-                    st_cluster_v4(xpeer + (uint32_t)(xb * MLA_XBUF + (i * MLA_HP + row) * 16),
-                                  s[4 * i], s[4 * i + 1], s[4 * i + 2], s[4 * i + 3]);
-                mbar_arrive_cluster(&bars.x_full[xb], peer);
+                    st_async_v4(xpeer + (uint32_t)(xb * MLA_XBUF + (i * MLA_HP + row) * 16),
+                                s[4 * i], s[4 * i + 1], s[4 * i + 2], s[4 * i + 3], rbar);
                 if (!(ok = warp_wait(&bars.x_full[xb], (g >> 1) & 1, err, 0x303, true))) break;
+                const float4 *X4 = reinterpret_cast<const float4 *>(sm + MLA_OFF_X + xb * MLA_XBUF);
                 const int valid = clen - t * MLA_TILE;
                 float mx = -INFINITY;
 #pragma unroll
@@ -477,7 +495,10 @@ mla_attend_tc(const __grid_constant__ MlaMaps maps, const MlaSeg *__restrict__ s
                         mx = fmaxf(mx, s[c]);
                     }
                 }
-                mbar_arrive_cluster(&bars.x_empty[xb], peer);
+                // once every row has read exchange buffer xb, row 0 tells the peer it may refill it
+                mbar_arrive(&bars.x_read[xb]);
+                if (row == 0 && mbar_wait(&bars.x_read[xb], (g >> 1) & 1, err, 0x309))
+                    mbar_arrive_cluster_relaxed(&bars.x_empty[xb], peer);
                 if (t == sg.t0) {
                     // a new segment: the previous segment's last P.V must be done before its
                     // O is read out and the next P.V overwrites it
@@ -516,13 +537,11 @@ mla_attend_tc(const __grid_constant__ MlaMaps maps, const MlaSeg *__restrict__ s
                     }
                 }
                 // P buffer pb is free once the P.V of tile g-2 is done
-                const int pb = g & 1;
                 uint8_t *P = sm + MLA_OFF_P + pb * MLA_PBUF;
                 if (g >= 2 &&
                     !(ok = warp_wait(&bars.pv_done[pb], ((g >> 1) - 1) & 1, err, 0x307)))
                     break;
-                // P row (bf16, 128-byte swizzle: 16-byte chunk c of row r sits at c ^ (r & 7);
-                // a 32-token tile fills chunks 0..3 of each 128-byte row)
+                // P row (bf16, 128-byte swizzle: 16-byte chunk c of row r sits at c ^ (r & 7))
                 float rs = 0.f;
                 uint32_t pk[MLA_TILE / 2];
 #pragma unroll
@@ -553,7 +572,8 @@ mla_attend_tc(const __grid_constant__ MlaMaps maps, const MlaSeg *__restrict__ s
                 mbar_arrive(&bars.p_full[pb]);
             }
         }
-        if (ok && g > 0 && warp_wait(&bars.pv_done[(g - 1) & 1], ((g - 1) >> 1) & 1, err, 0x305)) {
+        if (ok && g > 0 &&
+            warp_wait(&bars.pv_done[(g - 1) & 1], ((g - 1) >> 1) & 1, err, 0x305)) {
             tc_fence_after();
             epilogue(cur_slot);
         }
@@ -733,8 +753,6 @@ extern "C" int k3cuda_mla_decode(k3cuda_ctx *ctx, void *out, int out_dtype, cons
         rc = make_tmap_3d(&qmaps.b, w_uk, BF, 2, MLA_DL, MLA_DN, H, MLA_DL * 2,
                           (uint64_t)MLA_DN * MLA_DL * 2, 64, 64, 1);
     if (!rc)
-        rc = make_tmap_2d(&maps.q, qlat, BF, 2, MLA_QW, (uint64_t)B * MLA_HP, MLA_QW * 2, 64, MLA_HP);
-    if (!rc)
         rc = make_tmap_2d(&maps.lat, latent, BF, 2, MLA_DL, (uint64_t)B * cap, MLA_DL * 2, 64,
                           MLA_TILE);
     if (!rc)
@@ -763,8 +781,9 @@ extern "C" int k3cuda_mla_decode(k3cuda_ctx *ctx, void *out, int out_dtype, cons
     K3_CUDA_TRY(cudaFuncSetAttribute(mla_attend_tc, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                      MLA_SMEM));
     const float scale_log2e = scale * 1.4426950408889634f;
-    mla_attend_tc<<<2 * p.ncl, 192, MLA_SMEM, ctx->stream>>>(maps, d_segs, d_cl, d_lens, part, H,
-                                                           cap, scale_log2e, ctx->err_word);
+    mla_attend_tc<<<2 * p.ncl, 224, MLA_SMEM, ctx->stream>>>(maps, d_segs, d_cl, d_lens, qlat,
+                                                           part, H, cap, scale_log2e,
+                                                           ctx->err_word);
     rc = after_launch(ctx, "mla_attend_tc");
     if (rc) return rc;
 

@@ -59,6 +59,17 @@ __device__ __forceinline__ void mbar_arrive_cluster(uint64_t *bar, uint32_t cta)
         : "memory");
 }
 
+// Relaxed remote arrive: for signals that order no data of this thread's (e.g. "I have
+// finished reading your buffer": the reads are complete once their values are consumed).
+__device__ __forceinline__ void mbar_arrive_cluster_relaxed(uint64_t *bar, uint32_t cta) {
+    asm volatile(
+        "{\n\t.reg .b32 ra;\n\t"
+        "mapa.shared::cluster.u32 ra, %0, %1;\n\t"
+        "mbarrier.arrive.relaxed.cluster.shared::cluster.b64 _, [ra];\n\t}" ::"r"(smem_u32(bar)),
+        "r"(cta)
+        : "memory");
+}
+
 __device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
     uint32_t ok;
     asm volatile(
@@ -250,6 +261,18 @@ __device__ __forceinline__ void mma_bf16_ss(uint32_t d_tmem, uint64_t adesc, uin
         : "memory");
 }
 
+// D[tmem] (+)= A[tmem] . B[smem]^T (A K-major in TMEM: row m in lane m, two bf16 per
+// 32-bit column, K ascending), issued by one thread.
+__device__ __forceinline__ void mma_bf16_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t bdesc,
+                                            uint32_t idesc, uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
+        "r"(a_tmem), "l"(bdesc), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+
 __device__ __forceinline__ void mma_tf32_ss(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc,
                                             uint32_t idesc, uint32_t accumulate) {
     asm volatile(
@@ -290,6 +313,21 @@ __device__ __forceinline__ void st_cluster_v4(uint32_t addr, float a, float b, f
     asm volatile("st.shared::cluster.v4.f32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "f"(a), "f"(b),
                  "f"(c), "f"(d)
                  : "memory");
+}
+
+// Asynchronous 16-byte store into cluster CTA shared memory that completes `bytes`
+// transactions on the mbarrier `rbar` of the destination CTA (both addresses from map_peer).
+__device__ __forceinline__ void st_async_v4(uint32_t raddr, float a, float b, float c, float d,
+                                            uint32_t rbar) {
+    asm volatile(
+        "st.async.shared::cluster.mbarrier::complete_tx::bytes.v4.f32 [%0], {%1, %2, %3, %4}, [%5];" ::
+            "r"(raddr), "f"(a), "f"(b), "f"(c), "f"(d), "r"(rbar)
+        : "memory");
+}
+
+// Barrier among `nthreads` threads (a multiple of 32) on hardware barrier `id` (1..15).
+__device__ __forceinline__ void named_sync(uint32_t id, uint32_t nthreads) {
+    asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
 }
 
 }  // namespace sm100
