@@ -25,11 +25,19 @@
 // of t's 16-token sub-block. For s before the sub-block both factors are <= 1. For s
 // inside it e^(G_r - G_s) >= 1 spans at most 15 decay steps; if any channel's 15-step
 // decay exceeds e^80 the sub-block's diagonal entries are formed directly instead.
+#include <type_traits>
 #include <vector>
 
 #include "internal.cuh"
 
 namespace k3 {
+
+// kda_prefill_tc.cu: the tcgen05 form, used for bf16 q/k/v/o with d_k = d_v = 128
+int run_prefill_tc(k3cuda_ctx *ctx, float *state, void *o, const void *q, const void *k,
+                   const void *v, const float *gate, const float *beta, int total_tokens,
+                   int n_seq, int H, float q_scale, int gate_is_log, long long nc,
+                   const void *d_table, const int *d_c0, void *blocks);
+size_t prefill_tc_block_bytes();
 
 constexpr int KC = 64;        // chunk length
 constexpr int KSUB = 16;      // anchor sub-block
@@ -313,6 +321,12 @@ static int run_prefill(k3cuda_ctx *ctx, float *state, void *o, const void *q, co
                                     cudaMemcpyHostToDevice, ctx->stream));
     K3_CUDA_TRY(cudaMemcpyAsync(d_c0, c0.data(), (size_t)(n_seq + 1) * sizeof(int),
                                 cudaMemcpyHostToDevice, ctx->stream));
+    if constexpr (std::is_same<IO, __nv_bfloat16>::value && DK == 128) {
+        // bf16 operands on the tensor cores (every operand bf16, accumulation fp32)
+        if (nc == 0) return K3CUDA_OK;
+        return run_prefill_tc(ctx, state, o, q, k, v, gate, beta, cu[n_seq], n_seq, H, q_scale,
+                              gate_is_log, nc, d_table, d_c0, blocks);
+    }
     if (nc > 0) {
         const size_t smem1 =
             ((size_t)4 * KC * DK + 2 * KSUB * DK + 3 * KC * KC + KC) * sizeof(float);

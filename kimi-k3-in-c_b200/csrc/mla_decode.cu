@@ -64,6 +64,8 @@ constexpr int MLA_PBUF = MLA_HP * 128;     // one P buffer: 128 rows x 128 B (K-
 constexpr int MLA_OFF_X = MLA_OFF_P + 2 * MLA_PBUF;
 constexpr int MLA_XBUF = MLA_HP * MLA_TILE * 4;  // one exchange buffer: 128 heads x 64 fp32
 constexpr int MLA_SMEM = MLA_OFF_X + 2 * MLA_XBUF + 1024;  // + alignment slack
+static_assert(MLA_KVBLK % 1024 == 0 && MLA_OFF_P % 1024 == 0 && MLA_PBUF % 1024 == 0,
+              "swizzled operands need 1024-byte alignment");
 constexpr int MLA_PART = MLA_DL + 4;       // floats per (segment, head): o_lat, max, sum, pad
                                            // (rows stay 16-byte aligned for float4 stores)
 // TMEM columns: S [0, 64), this rank's query half [64, 224) (two bf16 per column),

@@ -158,14 +158,36 @@ def test_prefill_varlen_ragged_bf16(ctx, d):
     o, S = run_prefill(ctx, t["q"], t["k"], t["v"], t["g"], t["beta"], cu, S0=S0)
     o_ref, S_ref = oracle.kda_recurrence(t["q"], t["k"], t["v"], t["g"], t["beta"], cu, state=S0,
                                          nthreads=oracle.max_threads())
+    # bf16 inputs: the 5e-3 bar applies to the outputs and to the final state
     assert W.rel_fro(o, o_ref) < TOL_BF16
-    assert W.rel_fro(S, S_ref) < TOL_F32
+    assert W.rel_fro(S, S_ref) < TOL_BF16
     for n in range(len(RAGGED)):  # every sequence on its own, not only in aggregate
         a, b = cu[n], cu[n + 1]
         if b > a:
             assert W.rel_fro(o[a:b], o_ref[a:b]) < TOL_BF16, n
-        assert W.rel_fro(S[n], S_ref[n]) < TOL_F32, n
+        assert W.rel_fro(S[n], S_ref[n]) < TOL_BF16, n
     assert np.array_equal(S[0], S0[0]) and np.array_equal(S[5], S0[5])  # empty: untouched
+
+
+def test_prefill_many_streams_bf16(ctx):
+    """Enough (sequence, head) streams that the tensor-core scan takes whole 128-column
+    state rows per CTA (the config-3 shape class), ragged lengths, nonzero initial state."""
+    rng = np.random.default_rng(17)
+    H, d = 16, 128
+    lens = [1, 64, 100, 130, 7, 0, 257, 64, 65, 33]
+    cu = np.concatenate([[0], np.cumsum(lens)]).astype(np.int32)
+    t = W.kda_tokens(rng, int(cu[-1]), H, d, d, bf16=True)
+    S0 = rng.standard_normal((len(lens), H, d, d), dtype=np.float32) * np.float32(0.05)
+    o, S = run_prefill(ctx, t["q"], t["k"], t["v"], t["g"], t["beta"], cu, S0=S0)
+    o_ref, S_ref = oracle.kda_recurrence(t["q"], t["k"], t["v"], t["g"], t["beta"], cu, state=S0,
+                                         nthreads=oracle.max_threads())
+    assert W.rel_fro(o, o_ref) < TOL_BF16
+    assert W.rel_fro(S, S_ref) < TOL_BF16
+    for n in range(len(lens)):
+        a, b = cu[n], cu[n + 1]
+        if b > a:
+            assert W.rel_fro(o[a:b], o_ref[a:b]) < TOL_BF16, n
+        assert W.rel_fro(S[n], S_ref[n]) < TOL_BF16, n
 
 
 def test_prefill_without_state_and_alpha_gate(ctx):
@@ -207,4 +229,4 @@ def test_prefill_config2_shape_reduced_heads(ctx):
     o_ref, S_ref = oracle.kda_recurrence(t["q"], t["k"], t["v"], t["g"], t["beta"], cu,
                                          nthreads=oracle.max_threads())
     assert W.rel_fro(o, o_ref) < TOL_BF16
-    assert W.rel_fro(S, S_ref) < TOL_F32
+    assert W.rel_fro(S, S_ref) < TOL_BF16
