@@ -133,15 +133,19 @@ kda_prep_tc(const __grid_constant__ PrepMaps maps, const TcChunk *__restrict__ c
     // G = cumsum(g): thread (i, half) sums rows [32 half, 32 half + 32) of channel i
     {
         const int i = tid & 127, half = tid >> 7;
+        float gv[32];
+#pragma unroll
+        for (int r = 0; r < 32; r++) {  // all 32 loads in flight before the first add
+            const int t = half * 32 + r;
+            gv[r] = t < cd.len ? gate[((size_t)(cd.t0 + t) * H + h) * TC_D + i] : 1.f;
+        }
         float acc = 0.f;
+#pragma unroll
         for (int r = 0; r < 32; r++) {
             const int t = half * 32 + r;
-            float gv = 0.f;
-            if (t < cd.len) {
-                gv = gate[((size_t)(cd.t0 + t) * H + h) * TC_D + i];
-                if (!gate_is_log) gv = logf(gv);
-            }
-            acc += gv;
+            float x = 0.f;
+            if (t < cd.len) x = gate_is_log ? gv[r] : logf(gv[r]);
+            acc += x;
             G[t * 128 + i] = acc;
         }
         if (tid < TC_C) sb[tid] = tid < cd.len ? beta[(size_t)(cd.t0 + tid) * H + h] : 0.f;
@@ -191,7 +195,7 @@ kda_prep_tc(const __grid_constant__ PrepMaps maps, const TcChunk *__restrict__ c
         stbf(outb + PB_Q, (uint32_t)(t * 128 + i) * 2, v);
     }
     for (int e = tid; e < TC_C * 128; e += 256) {
-        const int t = e & 63, i = e >> 6;
+        const int t = e >> 7, i = e & 127;
         float v = 0.f;
         if (t < cd.len) {
             const float kv = ldbf(sK, (i >> 6) * 8192 + sw128(t, i & 63));
@@ -401,7 +405,7 @@ kda_prep_tc(const __grid_constant__ PrepMaps maps, const TcChunk *__restrict__ c
 namespace k3 {
 
 struct ScanMaps {
-    CUtensorMap w, q, kb, a, u;
+    CUtensorMap w, q, kb, a, u, g;
 };
 
 __device__ __forceinline__ bool warp_wait_all(uint64_t *bar, uint32_t parity, unsigned *err,
@@ -419,7 +423,10 @@ kda_scan_tc(const __grid_constant__ ScanMaps maps, const TcChunk *__restrict__ c
             const int *__restrict__ seq_chunk0, const uint8_t *__restrict__ ws,
             float *__restrict__ state, __nv_bfloat16 *__restrict__ o, int H,
             unsigned *__restrict__ err) {
-    constexpr int SB = 57344 + 128 * DVT;         // operand stage: W, Qtil, Kbar^T, Aqk, U
+    // operand stage: W, Qtil, Kbar^T, Aqk, U slice, Gamma (padded to 1 KB)
+    constexpr int OFF_GAM = 57344 + 128 * DVT;
+    constexpr int STAGE_TX = OFF_GAM + 512;
+    constexpr int SB = (STAGE_TX + 1023) & ~1023;
     static_assert(SB % 1024 == 0 && (DVT * 256) % 1024 == 0, "1024-byte aligned operands");
     constexpr int OFF_S16 = 2 * SB;               // bf16 S^T [DVT][128] (2 K-blocks)
     constexpr int OFF_XT = OFF_S16 + DVT * 256;   // bf16 X^T [DVT][64]
@@ -461,7 +468,7 @@ kda_scan_tc(const __grid_constant__ ScanMaps maps, const TcChunk *__restrict__ c
                 const int st = j & 1, ch = (c0 + j) * H + h;
                 if (j >= 2 && !(ok = mbar_wait(&op_empty[st], ((j >> 1) - 1) & 1, err, 0x601))) break;
                 uint8_t *s = sm + st * SB;
-                mbar_expect_tx(&op_full[st], SB);
+                mbar_expect_tx(&op_full[st], STAGE_TX);
                 for (int kb = 0; kb < 2; kb++) {
                     tma_load_3d(s + kb * 8192, &maps.w, &op_full[st], kb * 64, 0, ch);
                     tma_load_3d(s + 16384 + kb * 8192, &maps.q, &op_full[st], kb * 64, 0, ch);
@@ -470,6 +477,7 @@ kda_scan_tc(const __grid_constant__ ScanMaps maps, const TcChunk *__restrict__ c
                 tma_load_3d(s + 49152, &maps.a, &op_full[st], 0, 0, ch);
                 for (int u = 0; u < (DVT + 63) / 64; u++)
                     tma_load_3d(s + 57344 + u * 8192, &maps.u, &op_full[st], col0 + u * 64, 0, ch);
+                tma_load_2d(s + OFF_GAM, &maps.g, &op_full[st], 0, ch);
                 last[st] = j;
             }
             // loads still in flight are waited for (bounded) before the CTA may exit
@@ -534,13 +542,14 @@ kda_scan_tc(const __grid_constant__ ScanMaps maps, const TcChunk *__restrict__ c
         tc_fence_before();
         mbar_arrive(&s16_ready);
         bool ok = true;
+        TcChunk cd_next = nc > 0 ? chunks[c0] : TcChunk{0, 0, 0, 0};
         for (int j = 0; j < nc; j++) {
-            const TcChunk cd = chunks[c0 + j];
-            const int ch = (c0 + j) * H + h;
+            const TcChunk cd = cd_next;
+            if (j + 1 < nc) cd_next = chunks[c0 + j + 1];  // prefetched off the critical path
             const uint8_t *s = sm + (j & 1) * SB;
-            const float gam = reinterpret_cast<const float *>(ws + (size_t)ch * PB_BYTES + PB_G)[i];
             if (!(ok = warp_wait_all(&x_full, j & 1, err, 0x605))) break;
             tc_fence_after();
+            const float gam = reinterpret_cast<const float *>(s + OFF_GAM)[i];
             // X = U - X_acc (rows t < 16 of each warp's quarter) -> X^T in shared memory
             for (int c = 0; c < DVT; c += 16) {
                 float v[16];
@@ -656,17 +665,20 @@ int run_prefill_tc(k3cuda_ctx *ctx, float *state, void *o, const void *q, const 
     if (!rc)
         rc = make_tmap_3d(&sm.u, b + PB_U, BF, 2, 128, 64, nch, 256, PB_BYTES, dvt > 64 ? 64 : dvt,
                           64, 1);
+    if (!rc)
+        rc = make_tmap_2d(&sm.g, b + PB_G, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, 128, nch, PB_BYTES,
+                          128, 1);
     if (rc) return rc;
     const long long nblk = (long long)n_seq * H * (TC_D / dvt);
     if (dvt == 128) {
-        const int smem = 2 * (57344 + 128 * 128) + 128 * 384 + 1024;
+        const int smem = 2 * (((57344 + 128 * 128 + 512) + 1023) & ~1023) + 128 * 384 + 1024;
         K3_CUDA_TRY(cudaFuncSetAttribute(kda_scan_tc<128>,
                                          cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
         kda_scan_tc<128><<<(unsigned)nblk, 192, smem, ctx->stream>>>(
             sm, (const TcChunk *)d_table, d_c0, (const uint8_t *)blocks, state,
             (__nv_bfloat16 *)o, H, ctx->err_word);
     } else {
-        const int smem = 2 * (57344 + 128 * 32) + 32 * 384 + 1024;
+        const int smem = 2 * (((57344 + 128 * 32 + 512) + 1023) & ~1023) + 32 * 384 + 1024;
         K3_CUDA_TRY(cudaFuncSetAttribute(kda_scan_tc<32>,
                                          cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
         kda_scan_tc<32><<<(unsigned)nblk, 192, smem, ctx->stream>>>(
