@@ -1,33 +1,50 @@
 // kda_prefill_tc.cu -- KDA chunkwise prefill on tcgen05 (bf16 operands, fp32 accumulation).
 //
 // The tensor-core form of kda_prefill.cu's algorithm (same chunk algebra, reference
-// src/core/k3_ops.c:908-938 / :186-243), for bf16 q/k/v/o with d_k = d_v = 128:
+// src/core/k3_ops.c:908-938 / :186-243), for bf16 q/k/v/o with d_k = d_v = 128. Per chunk
+// of C = 64 tokens with G_t = sum_{u<=t} g_u (per key channel):
 //
-//   kda_prep_tc   one CTA per (chunk, head), every chunk in parallel:
-//       G = cumsum(g) per key channel; within-sub-block factors F = e^(G_t - G_r),
-//       Finv = e^(G_r - G_t) (r = first token of t's 16-token sub-block) and per-channel
-//       sub-block ratios D(a,b) = e^(G_r(a) - G_r(b)) -- every exponent <= 0 except Finv's,
-//       which spans at most 15 decay steps (a larger one marks its sub-block for the exact
-//       path below).
-//       Akk, Aqk by column sub-block b: A[:, b] = (k F D(a,b)) . (k Finv)_b^T on tcgen05
-//       (M=64 tokens, N=16, K=128 channels), four rounds.
-//       (I + diag(beta) Akk)^-1 by 16x16 blocks in fp32 (forward substitution on the four
-//       diagonal blocks, then the off-diagonal blocks by block products).
-//       W = M Ktil and U = M V on tcgen05 (M = T diag(beta), Ktil = k e^(G_t): the decay
-//       from the chunk start through token t).
-//       Writes W, U, Qtil = q e^(G_t), Kbar^T = (k e^(G_C - G_t))^T, Aqk (bf16) and
-//       Gamma = e^(G_C) (fp32) per (chunk, head).
-//   kda_scan_tc   one CTA per (sequence, head, slice of d_v): the fp32 state slice lives
-//       in TMEM for the whole sequence; per chunk
-//           X = U - W S16          (tcgen05, S16 = bf16 copy of S in shared memory)
-//           O = Qtil S16 + Aqk X   (tcgen05)
-//           S = Gamma S + Kbar^T X (tcgen05, accumulating into the fp32 state in TMEM)
+//   Akk[t][s] = beta_t sum_i k_ti k_si e^(G_ti - G_si)   (s < t)
+//   Aqk[t][s] =        sum_i q_ti k_si e^(G_ti - G_si)   (s <= t, q pre-scaled)
+//   M  = (I + Akk)^-1 diag(beta),  W = M Ktil,  U = M V   (Ktil_t = k_t e^(G_t))
+//   Kbar_t = k_t e^(G_C - G_t),    Qtil_t = q_t e^(G_t),   Gamma = e^(G_C)
 //
-// Operand precision: every tensor-core operand is bf16 and every accumulation fp32. On the
-// synthetic distributions of the workloads this holds the outputs and the final state to
-// about 2.5e-3 relative Frobenius error of the fp32 recurrence (inside the 5e-3 bar for
-// bf16 inputs); fp32 I/O keeps the CUDA-core path of kda_prefill.cu, which is exact to fp32
-// rounding.
+// and the chunk step  X = U - W S,  O = Qtil S + Aqk X,  S' = Gamma S + Kbar^T X  is
+// regrouped into its transition form
+//
+//   S' = Gamma S + P S + Kbar^T U          P  = -Kbar^T W          [d_k x d_k]
+//   O  = Q' S + Aqk U                      Q' = Qtil - Aqk W       [C x d_k]
+//
+// so every product that does not involve S is formed once per (chunk, head) in parallel,
+// and the sequential scan over chunks is one batch of MMAs per chunk.
+//
+//   kda_prep_tc   one CTA per (chunk, head), two CTAs per SM. g, q, k arrive by TMA;
+//       G by a per-channel prefix sum; then one vectorised pass (each thread: one token
+//       of each 16-token sub-block, eight channels) forms every elementwise operand:
+//         A  = [k_t e^(G_t - G_r(t)) ; q_t e^(G_t - G_r(t))]   128 x 128, r(t) = first
+//              token of t's sub-block: exponents <= 0
+//         B_a[s] = k_s e^(G_r(a) - G_s), s < 16(a+1)            exponent > 0 only inside
+//              sub-block a (at most 15 decay steps; a larger one is flagged and that
+//              sub-block's columns are recomputed exactly)
+//         Ktil, Qtil (in place over k, q), Kbar (to the workspace).
+//       Akk and Aqk for row sub-block a come out of one M=128 MMA, A . B_a^T (four
+//       "rounds", N = 16, 32, 48, 64). (I + Akk)^-1 by 16x16 blocks in fp32 on the CUDA
+//       cores; W = M Ktil, U = M V (M as bf16 hi + lo); P = -Kbar^T W (M=128, N=128,
+//       K=64) and Aqk W on tcgen05. Writes P, Kbar, U, Q', Aqk (bf16; Aqk also its
+//       bf16 remainder) and Gamma (fp32).
+//   kda_scan_tc   one CTA per (sequence, head, 64-column half of d_v). The fp32 state
+//       slice lives in TMEM; per chunk the compute warps write its bf16 copy S16 to shared
+//       memory and scale the TMEM copy by Gamma (read two chunks ahead from the workspace),
+//       then one thread issues
+//           S += P . S16 + Kbar^T . U      (M=128, N=64)
+//           O  = Q' . S16 + Aqk . U        (M=64,  N=64, double-buffered in TMEM; Aqk as
+//                                            bf16 hi + lo)
+//       while TMA streams the next chunk's operands (and prefetches later ones into L2).
+//
+// Operand precision: every tensor-core operand is bf16 and every accumulation fp32; the
+// state itself stays fp32 (Gamma is applied in fp32, and only the products with P and Q'
+// see its bf16 copy). fp32 I/O keeps the CUDA-core path of kda_prefill.cu, which is exact
+// to fp32 rounding.
 #include <vector>
 
 #include "internal.cuh"
@@ -41,372 +58,672 @@ using namespace sm100;
 constexpr int TC_C = 64;    // chunk
 constexpr int TC_D = 128;   // d_k = d_v
 
-// Per-(chunk, head) block written by kda_prep_tc, in bytes.
-constexpr int PB_W = 0;                 // W    [64][128] bf16
-constexpr int PB_U = PB_W + 16384;      // U    [64][128] bf16
-constexpr int PB_Q = PB_U + 16384;      // Qtil [64][128] bf16
-constexpr int PB_KB = PB_Q + 16384;     // Kbar^T [128][64] bf16
-constexpr int PB_A = PB_KB + 16384;     // Aqk  [64][64] bf16
-constexpr int PB_G = PB_A + 8192;       // Gamma [128] fp32
-constexpr int PB_BYTES = PB_G + 512;    // 74240 (a multiple of 256)
+// Per-(chunk, head) block written by kda_prep_tc, in bytes (row-major bf16 unless noted).
+constexpr int WB_P = 0;                 // P = -Kbar^T W  [128 i][128 i']
+constexpr int WB_KB = 32768;            // Kbar           [64 t][128 i]
+constexpr int WB_U = 49152;             // U              [64 t][128 j]
+constexpr int WB_QP = 65536;            // Q'             [64 t][128 i]
+constexpr int WB_A = 81920;             // Aqk            [64 t][64 s]
+constexpr int WB_AL = 90112;            // Aqk - bf16(Aqk) [64 t][64 s]
+constexpr int WB_G = 98304;             // Gamma          [128] fp32
+constexpr int WB_BYTES = 98816;         // a multiple of 256
 
 struct TcChunk {
     int seq, t0, len, pad;
 };
 
-// byte offset of element (r, c), c < 64, inside a [rows x 64 bf16] 128-byte-swizzled block
-__device__ __forceinline__ uint32_t sw128(int r, int c) {
-    return (uint32_t)(r * 128 + ((((c >> 3) ^ (r & 7)) & 7) << 4) + (c & 7) * 2);
+// byte offset of the 16-byte chunk `c` (0..7) of row `r` in a 128-byte-swizzled tile whose
+// base is 1024-byte aligned
+__device__ __forceinline__ uint32_t swz(int r, int c) {
+    return (uint32_t)(r * 128 + (((c ^ r) & 7) << 4));
 }
 
-__device__ __forceinline__ float ldbf(const uint8_t *base, uint32_t off) {
-    return __bfloat162float(*reinterpret_cast<const __nv_bfloat16 *>(base + off));
+// fp32 [64][128] G tile, 16-byte units XOR-swizzled within each 128-byte group so that both
+// a channel-per-thread pass (fixed t) and a token-per-thread pass (fixed channels) are free
+// of bank conflicts
+__device__ __forceinline__ int gsw(int t, int i) {
+    const int u = i >> 2;
+    return t * 128 + (((u & ~7) | ((u ^ t) & 7)) << 2) + (i & 3);
 }
-__device__ __forceinline__ void stbf(uint8_t *base, uint32_t off, float x) {
-    *reinterpret_cast<__nv_bfloat16 *>(base + off) = __float2bfloat16_rn(x);
+
+__device__ __forceinline__ uint32_t pack_bf2(float a, float b) {
+    const __nv_bfloat162 p = __floats2bfloat162_rn(a, b);
+    return *reinterpret_cast<const uint32_t *>(&p);
 }
+__device__ __forceinline__ uint4 pack_bf8(const float *v) {
+    return make_uint4(pack_bf2(v[0], v[1]), pack_bf2(v[2], v[3]), pack_bf2(v[4], v[5]),
+                      pack_bf2(v[6], v[7]));
+}
+__device__ __forceinline__ void unpack_bf8(uint4 u, float *v) {
+    const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+    for (int i = 0; i < 4; i++) {
+        v[2 * i] = __uint_as_float(w[i] << 16);
+        v[2 * i + 1] = __uint_as_float(w[i] & 0xffff0000u);
+    }
+}
+__device__ __forceinline__ void ld_g8(const float *Gs, int t, int i0, float *v) {
+    const float4 a = *reinterpret_cast<const float4 *>(Gs + gsw(t, i0));
+    const float4 b = *reinterpret_cast<const float4 *>(Gs + gsw(t, i0 + 4));
+    v[0] = a.x, v[1] = a.y, v[2] = a.z, v[3] = a.w, v[4] = b.x, v[5] = b.y, v[6] = b.z, v[7] = b.w;
+}
+__device__ __forceinline__ void ld_f8(const float *p, float *v) {
+    const float4 a = reinterpret_cast<const float4 *>(p)[0];
+    const float4 b = reinterpret_cast<const float4 *>(p)[1];
+    v[0] = a.x, v[1] = a.y, v[2] = a.z, v[3] = a.w, v[4] = b.x, v[5] = b.y, v[6] = b.z, v[7] = b.w;
+}
+__device__ __forceinline__ void st16s(uint8_t *p, uint4 v) { *reinterpret_cast<uint4 *>(p) = v; }
 
 struct PrepMaps {
-    CUtensorMap q, k, v;
+    CUtensorMap q, k, v, g;
 };
 
-// shared memory of kda_prep_tc (bytes from a 1024-aligned base). The tensor-core operands
-// come first: a 128-byte-swizzled operand must start on a 1024-byte boundary, because the
-// hardware derives the swizzle from the address bits.
-constexpr int PS_Q = 0;                       // q tile  2 x [64 x 64] bf16 SW128
-constexpr int PS_K = PS_Q + 16384;            // k tile
-constexpr int PS_V = PS_K + 16384;            // v tile (MN-major B of U = M V)
-constexpr int PS_R = PS_V + 16384;            // R 16K, Rq 16K, Kh 4K; later M 8K, Ktil 16K
-constexpr int PS_F = PS_R + 36864;            // F    fp32 [64][129] (33 KB padded)
-constexpr int PS_FI = PS_F + 33792;           // Finv fp32 [64][129]
-constexpr int PS_G = PS_FI + 33792;           // G fp32 [64][128]; later T [64][65] + Y
-constexpr int PS_A = PS_G + 32768;            // Akk fp32 [64][65]
-constexpr int PS_D = PS_A + 64 * 65 * 4;      // D(a,b) fp32 [4][4][128]
-constexpr int PS_EC = PS_D + 8192;            // e^(G_C - G_r(a)) fp32 [4][128]
-constexpr int PS_EZ = PS_EC + 2048;           // e^(G_r(a)) fp32 [4][128]
-constexpr int PS_GC = PS_EZ + 2048;           // Gamma fp32 [128]
-constexpr int PS_B = PS_GC + 512;             // beta fp32 [64]
-constexpr int PS_BYTES = PS_B + 256;
+// Shared memory of kda_prep_tc (bytes from a 1024-aligned base); regions are reused as the
+// kernel proceeds. Every swizzled operand starts on a 1024-byte boundary (the hardware
+// derives the swizzle from the address bits).
+constexpr int PS_Q = 0;                  // q -> Qtil                 [64][128] bf16 (2 k-blocks)
+constexpr int PS_K = 16384;              // k -> Ktil -> W            [64][128] bf16
+constexpr int PS_R1 = 32768;             // g/G fp32 -> A [128][128] bf16 -> V | Kbar
+constexpr int PS_V = PS_R1;              //   V    [64][128] bf16 (MN-major B of U = M V)
+constexpr int PS_KBAR = PS_R1 + 16384;   //   Kbar [64][128] bf16 (MN-major A of Kbar^T W)
+constexpr int PS_R2 = 65536;             // B_0 | B_1 | B_3, then B_2; then AT, Y, M
+constexpr int PS_B0 = PS_R2;             //   16 rows, k-blocks of 2 KB
+constexpr int PS_B1 = PS_R2 + 4096;      //   32 rows, k-blocks of 4 KB
+constexpr int PS_B3 = PS_R2 + 12288;     //   64 rows, k-blocks of 8 KB
+constexpr int PS_B2 = PS_R2;             //   48 rows, k-blocks of 6 KB (second phase)
+constexpr int PS_AT = PS_R2;             //   Akk (strictly lower) / T^T (upper) fp32 [64][68]
+constexpr int PS_Y = PS_R2 + 17408;      //   block-product scratch, fp32 [32][36]
+constexpr int PS_M = PS_R2 + 20480;      //   M bf16 [64][64] (over the dead tail of Y)
+constexpr int PS_AQ = 94208;             // Aqk bf16 [64][64] (A of Aqk W)
+constexpr int PS_D = 102400;             // D(a,b) = e^(G_r(a) - G_r(b)) fp32 [6][128]
+constexpr int PS_EZ = PS_D + 3072;       // e^(G_r(a)) fp32 [4][128]
+constexpr int PS_ML = PS_D;              //   then M - bf16(M) bf16 [64][64]
+constexpr int PS_BETA = PS_D + 8192;     // beta [64]
+constexpr int PS_BYTES = PS_BETA + 256;
 constexpr int PS_SMEM = PS_BYTES + 1024;
-static_assert(PS_K % 1024 == 0 && PS_V % 1024 == 0 && PS_R % 1024 == 0,
+constexpr int ATS = 68;                  // AT row stride in floats (16-byte aligned rows)
+static_assert(PS_AT + 64 * ATS * 4 <= PS_Y && PS_Y + 32 * 36 * 4 <= PS_AQ &&
+                  PS_M + 8192 <= PS_AQ && PS_B3 + 16384 <= PS_AQ,
+              "prep shared-memory regions overlap");
+static_assert(PS_M % 1024 == 0 && PS_AQ % 1024 == 0 && PS_B2 % 1024 == 0 && PS_B3 % 1024 == 0 &&
+                  PS_ML % 1024 == 0 && PS_EZ + 2048 <= PS_BETA,
               "swizzled operands need 1024-byte alignment");
-static_assert(64 * 129 * 4 <= 33792, "F padding");
 
-__global__ void __launch_bounds__(256, 1)
+// TMEM column of round a's accumulator (N = 16 (a + 1) columns each)
+__device__ __forceinline__ int round_col(int a) { return 8 * a * (a + 1); }
+// index of D(a, b), b < a
+__host__ __device__ constexpr int dpair(int a, int b) { return a * (a - 1) / 2 + b; }
+
+__global__ void __launch_bounds__(256, 2)
 kda_prep_tc(const __grid_constant__ PrepMaps maps, const TcChunk *__restrict__ chunks,
             const float *__restrict__ gate, const float *__restrict__ beta,
+            const __nv_bfloat16 *__restrict__ qg, const __nv_bfloat16 *__restrict__ kg,
             uint8_t *__restrict__ ws, int H, float q_scale, int gate_is_log,
             unsigned *__restrict__ err) {
     extern __shared__ uint8_t smraw[];
     uint8_t *sm = (uint8_t *)(((uintptr_t)smraw + 1023) & ~(uintptr_t)1023);
-    __shared__ uint64_t bar_ld, bar_mma;
+    __shared__ uint64_t bar_g, bar_qk, bar_v, bar_mma;
     __shared__ uint32_t tslot;
     __shared__ int flags[4];
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const TcChunk cd = chunks[blockIdx.x];
-    const int h = blockIdx.y;
-    uint8_t *outb = ws + ((size_t)blockIdx.x * H + h) * PB_BYTES;
-    float *F = reinterpret_cast<float *>(sm + PS_F);
-    float *Fi = reinterpret_cast<float *>(sm + PS_FI);
-    float *G = reinterpret_cast<float *>(sm + PS_G);
-    float *A = reinterpret_cast<float *>(sm + PS_A);
-    float *Dab = reinterpret_cast<float *>(sm + PS_D);
-    float *Ec = reinterpret_cast<float *>(sm + PS_EC);
+    const int h = blockIdx.y, len = cd.len;
+    uint8_t *outb = ws + ((size_t)blockIdx.x * H + h) * WB_BYTES;
+    float *Gs = reinterpret_cast<float *>(sm + PS_R1);
+    float *Dt = reinterpret_cast<float *>(sm + PS_D);
     float *Ez = reinterpret_cast<float *>(sm + PS_EZ);
-    float *Gc = reinterpret_cast<float *>(sm + PS_GC);
-    float *sb = reinterpret_cast<float *>(sm + PS_B);
-    uint8_t *sQ = sm + PS_Q, *sK = sm + PS_K, *sV = sm + PS_V;
+    float *sb = reinterpret_cast<float *>(sm + PS_BETA);
+    float *AT = reinterpret_cast<float *>(sm + PS_AT);
+    float *Y = reinterpret_cast<float *>(sm + PS_Y);
 
     if (tid == 0) {
-        mbar_init(&bar_ld, 1);
+        mbar_init(&bar_g, 1);
+        mbar_init(&bar_qk, 1);
+        mbar_init(&bar_v, 1);
         mbar_init(&bar_mma, 1);
         fence_barrier_init();
-        mbar_expect_tx(&bar_ld, 3 * 16384);
+        mbar_expect_tx(&bar_g, 32768);
+        tma_load_3d(sm + PS_R1, &maps.g, &bar_g, 0, h, cd.t0);
+        mbar_expect_tx(&bar_qk, 32768);
         for (int kb = 0; kb < 2; kb++) {
-            tma_load_3d(sQ + kb * 8192, &maps.q, &bar_ld, kb * 64, h, cd.t0);
-            tma_load_3d(sK + kb * 8192, &maps.k, &bar_ld, kb * 64, h, cd.t0);
-            tma_load_3d(sV + kb * 8192, &maps.v, &bar_ld, kb * 64, h, cd.t0);
+            tma_load_3d(sm + PS_Q + kb * 8192, &maps.q, &bar_qk, kb * 64, h, cd.t0);
+            tma_load_3d(sm + PS_K + kb * 8192, &maps.k, &bar_qk, kb * 64, h, cd.t0);
         }
     }
     if (tid < 4) flags[tid] = 0;
-    if (warp == 1) tmem_alloc(&tslot, 256);
-    // G = cumsum(g): thread (i, half) sums rows [32 half, 32 half + 32) of channel i
-    {
-        const int i = tid & 127, half = tid >> 7;
-        float gv[32];
-#pragma unroll
-        for (int r = 0; r < 32; r++) {  // all 32 loads in flight before the first add
-            const int t = half * 32 + r;
-            gv[r] = t < cd.len ? gate[((size_t)(cd.t0 + t) * H + h) * TC_D + i] : 1.f;
-        }
-        float acc = 0.f;
-#pragma unroll
-        for (int r = 0; r < 32; r++) {
-            const int t = half * 32 + r;
-            float x = 0.f;
-            if (t < cd.len) x = gate_is_log ? gv[r] : logf(gv[r]);
-            acc += x;
-            G[t * 128 + i] = acc;
-        }
-        if (tid < TC_C) sb[tid] = tid < cd.len ? beta[(size_t)(cd.t0 + tid) * H + h] : 0.f;
-    }
+    if (tid < TC_C) sb[tid] = tid < len ? beta[(size_t)(cd.t0 + tid) * H + h] : 0.f;
+    if (warp == 0) tmem_alloc(&tslot, 256);
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
     const uint32_t tb = tslot;
-    if (tid >= 128) {
-        const int i = tid & 127;
-        const float base = G[31 * 128 + i];
-        for (int t = 32; t < 64; t++) G[t * 128 + i] += base;
+    bool ok = mbar_wait(&bar_g, 0, err, 0x501);
+
+    // ------------------------------------------------------------- G = cumsum(g)
+    {
+        const int i = tid & 127, half = tid >> 7;
+        float gv[32];
+#pragma unroll
+        for (int r = 0; r < 32; r++) gv[r] = Gs[(32 * half + r) * 128 + i];  // dense, as loaded
+        __syncthreads();  // every thread holds its gates: the tile is rewritten swizzled
+        if (!gate_is_log) {
+#pragma unroll
+            for (int r = 0; r < 32; r++) gv[r] = 32 * half + r < len ? logf(gv[r]) : 0.f;
+        }
+        float acc = 0.f;
+#pragma unroll
+        for (int r = 0; r < 32; r++) {
+            acc += 32 * half + r < len ? gv[r] : 0.f;
+            gv[r] = acc;
+        }
+        if (half == 0) {
+#pragma unroll
+            for (int r = 0; r < 32; r++) Gs[gsw(r, i)] = gv[r];
+        }
+        __syncthreads();
+        if (half == 1) {
+            const float base = Gs[gsw(31, i)];
+#pragma unroll
+            for (int r = 0; r < 32; r++) Gs[gsw(32 + r, i)] = gv[r] + base;
+        }
+        __syncthreads();
     }
-    __syncthreads();
-    // factors
-    for (int e = tid; e < TC_C * 128; e += 256) {
-        const int t = e >> 7, i = e & 127, r = t & ~15;
-        const float g = G[e], gr = G[r * 128 + i];
-        F[t * 129 + i] = __expf(g - gr);
-        const float ex = gr - g;
-        if (ex > 80.f) atomicOr(&flags[t >> 4], 1);
-        Fi[t * 129 + i] = __expf(fminf(ex, 80.f));
-    }
+    // per-channel tables: sub-block ratios, decay from the chunk start, Gamma
     if (tid < 128) {
         const int i = tid;
-        for (int a = 0; a < 4; a++) {
-            for (int b = 0; b < a; b++)
-                Dab[(a * 4 + b) * 128 + i] = __expf(G[16 * a * 128 + i] - G[16 * b * 128 + i]);
-            Dab[(a * 4 + a) * 128 + i] = 1.f;
-            Ec[a * 128 + i] = __expf(G[63 * 128 + i] - G[16 * a * 128 + i]);
-            Ez[a * 128 + i] = __expf(G[16 * a * 128 + i]);  // decay from the chunk start
-        }
-        Gc[i] = __expf(G[63 * 128 + i]);
-    }
-    bool ok = true;
-    if (tid == 0) ok = mbar_wait(&bar_ld, 0, err, 0x501);
-    __syncthreads();
-    ok = __syncthreads_and(ok ? 1 : 0) && !*(volatile unsigned *)err;
-    // Qtil = q e^(G_t - G_0), Kbar^T = (k e^(G_C - G_t))^T and Gamma = e^(G_C) to the
-    // workspace (G is still live here for sub-blocks flagged by the overflow guard)
-    for (int e = tid; e < TC_C * 128; e += 256) {
-        const int t = e >> 7, i = e & 127;
-        float v = 0.f;
-        if (t < cd.len)
-            v = ldbf(sQ, (i >> 6) * 8192 + sw128(t, i & 63)) * q_scale * F[t * 129 + i] *
-                Ez[(t >> 4) * 128 + i];
-        stbf(outb + PB_Q, (uint32_t)(t * 128 + i) * 2, v);
-    }
-    for (int e = tid; e < TC_C * 128; e += 256) {
-        const int t = e >> 7, i = e & 127;
-        float v = 0.f;
-        if (t < cd.len) {
-            const float kv = ldbf(sK, (i >> 6) * 8192 + sw128(t, i & 63));
-            v = flags[t >> 4] ? kv * __expf(G[63 * 128 + i] - G[t * 128 + i])
-                              : kv * Fi[t * 129 + i] * Ec[(t >> 4) * 128 + i];
-        }
-        stbf(outb + PB_KB, (uint32_t)(i * 64 + t) * 2, v);
-    }
-    if (tid < 128) reinterpret_cast<float *>(outb + PB_G)[tid] = Gc[tid];
-
-    // ---------------------------------------------------------------- Akk, Aqk
-    uint8_t *sR = sm + PS_R, *sRq = sR + 16384, *sKh = sR + 32768;
-    constexpr uint32_t id_a = idesc_f16(64, 16, false, false);
-    for (int b = 0; b < 4 && ok; b++) {
-        for (int e = tid; e < TC_C * 128; e += 256) {
-            const int t = e >> 7, i = e & 127, a = t >> 4;
-            float rk = 0.f, rq = 0.f;
-            if (a >= b && t < cd.len) {
-                const float f = F[t * 129 + i] * Dab[(a * 4 + b) * 128 + i];
-                const uint32_t off = (i >> 6) * 8192 + sw128(t, i & 63);
-                rk = ldbf(sK, off) * f;
-                rq = ldbf(sQ, off) * q_scale * f;
-            }
-            const uint32_t o = (i >> 6) * 8192 + sw128(t, i & 63);
-            stbf(sR, o, rk);
-            stbf(sRq, o, rq);
-        }
-        for (int e = tid; e < 16 * 128; e += 256) {
-            const int s = e >> 7, i = e & 127, t = 16 * b + s;
-            const float v = t < cd.len ? ldbf(sK, (i >> 6) * 8192 + sw128(t, i & 63)) * Fi[t * 129 + i]
-                                       : 0.f;
-            stbf(sKh, (i >> 6) * 2048 + sw128(s, i & 63), v);
-        }
-        fence_async_shared();
-        tc_fence_before();
-        __syncthreads();
-        if (tid == 0) {
-            tc_fence_after();
-            for (int kb = 0; kb < 2; kb++)
+        float gr[4];
 #pragma unroll
-                for (int ks = 0; ks < 4; ks++) {
-                    const uint64_t bd = sdesc_kmajor(smem_u32(sKh + kb * 2048 + ks * 32));
-                    const uint32_t acc = (kb | ks) ? 1u : 0u;
-                    mma_bf16_ss(tb + 16 * b, sdesc_kmajor(smem_u32(sR + kb * 8192 + ks * 32)), bd,
-                                id_a, acc);
-                    mma_bf16_ss(tb + 64 + 16 * b, sdesc_kmajor(smem_u32(sRq + kb * 8192 + ks * 32)),
-                                bd, id_a, acc);
-                }
-            mma_commit(&bar_mma);
-        }
-        __syncwarp();
-        ok = mbar_wait(&bar_mma, b & 1, err, 0x502);
-        ok = __syncthreads_and(ok ? 1 : 0);
-        tc_fence_after();
-    }
-    // read Akk (beta-scaled, strictly lower) to shared memory, Aqk (lower) to the workspace.
-    // M=64 accumulator: row 16 w + l sits in lane l (< 16) of warp w's TMEM quarter.
-    if (ok && warp < 4) {
-        const int t = 16 * warp + lane;
-        for (int c = 0; c < 64; c += 16) {
-            float vk[16], vq[16];
-            tmem_ld16(tb + ((uint32_t)(32 * warp) << 16) + c, vk);
-            tmem_ld16(tb + ((uint32_t)(32 * warp) << 16) + 64 + c, vq);
-            tmem_wait_ld();
-            if (lane < 16) {
-                uint32_t pk[8];
+        for (int a = 0; a < 4; a++) gr[a] = Gs[gsw(16 * a, i)];
 #pragma unroll
-                for (int j = 0; j < 16; j++) {
-                    const int s = c + j;
-                    A[t * 65 + s] = s < t ? sb[t] * vk[j] : 0.f;
-                    vq[j] = s <= t ? vq[j] : 0.f;
-                }
+        for (int a = 1; a < 4; a++)
 #pragma unroll
-                for (int j = 0; j < 8; j++) {
-                    const __nv_bfloat162 p = __floats2bfloat162_rn(vq[2 * j], vq[2 * j + 1]);
-                    pk[j] = *reinterpret_cast<const uint32_t *>(&p);
-                }
-                uint4 *dst = reinterpret_cast<uint4 *>(outb + PB_A + (t * 64 + c) * 2);
-                dst[0] = make_uint4(pk[0], pk[1], pk[2], pk[3]);
-                dst[1] = make_uint4(pk[4], pk[5], pk[6], pk[7]);
-            }
-        }
+            for (int b = 0; b < a; b++) Dt[dpair(a, b) * 128 + i] = __expf(gr[a] - gr[b]);
+#pragma unroll
+        for (int a = 0; a < 4; a++) Ez[a * 128 + i] = __expf(gr[a]);
+        reinterpret_cast<float *>(outb + WB_G)[i] = __expf(Gs[gsw(63, i)]);
     }
-    tc_fence_before();
-    __syncthreads();
-    // column sub-blocks b whose 15-step decay overflowed the factored form (their Finv was
-    // clamped): every entry with s in b recomputed exactly, e^(G_t - G_s) per element
-    for (int b = 0; b < 4 && ok; b++) {
-        if (!flags[b]) continue;
-        for (int e = tid; e < 16 * TC_C; e += 256) {
-            const int t = e >> 4, s = 16 * b + (e & 15);
-            if (s > t || t >= cd.len) continue;
-            float akk = 0.f, aqk = 0.f;
-            for (int i = 0; i < 128; i++) {
-                const uint32_t ot = (i >> 6) * 8192 + sw128(t, i & 63);
-                const uint32_t os = (i >> 6) * 8192 + sw128(s, i & 63);
-                const float f = __expf(G[t * 128 + i] - G[s * 128 + i]) * ldbf(sK, os);
-                akk += ldbf(sK, ot) * f;
-                aqk += ldbf(sQ, ot) * q_scale * f;
-            }
-            A[t * 65 + s] = s < t ? sb[t] * akk : 0.f;
-            stbf(outb + PB_A, (uint32_t)(t * 64 + s) * 2, aqk);
-        }
-    }
+    ok = mbar_wait(&bar_qk, 0, err, 0x502) && ok;
     __syncthreads();
 
-    // ------------------------------------------------- T = (I + Akk)^-1, M = T diag(beta)
-    float *T = G;                 // [64][65], G is dead from here
-    float *Y = G + 64 * 65;       // [3][16][17] scratch
-    if (warp < 4 && lane < 16) {
-        // diagonal block w, column c = lane: forward substitution, columns independent
-        const int o = 16 * warp, c = lane;
-        for (int r = 0; r < 16; r++) {
-            float v = r == c ? 1.f : 0.f;
-            if (r > c) {
-                float acc = 0.f;
-                for (int j = c; j < r; j++) acc += A[(o + r) * 65 + o + j] * T[(o + j) * 65 + o + c];
-                v = -acc;
+    // -------------------------------------------------- elementwise operands (one pass)
+    // thread: channels [8 cc, 8 cc + 8), token j + 16 m of every sub-block m
+    // The A rows go over G (same region): this pass leaves them in place of k and q, and a
+    // second pass, once every thread has read its G values, moves them into A and scales
+    // them by e^(G_r(t)) into Ktil and Qtil.
+    const int cc = 2 * warp + (lane >> 4), j = lane & 15, kbk = cc >> 3, ch = cc & 7;
+    const int i0 = 8 * cc;
+    uint4 b2[3];  // rows of B_2, written once round 2's buffer is free
+    {
+        float gc[8];
+        ld_g8(Gs, 63, i0, gc);
+        int fl = 0;
+#pragma unroll
+        for (int m = 0; m < 4; m++) {
+            const int t = j + 16 * m;
+            float gt[8], ga[8], kv[8], qv[8];
+            ld_g8(Gs, t, i0, gt);
+            ld_g8(Gs, 16 * m, i0, ga);
+            const uint32_t so = (uint32_t)kbk * 8192 + swz(t, ch);
+            unpack_bf8(*reinterpret_cast<const uint4 *>(sm + PS_K + so), kv);
+            unpack_bf8(*reinterpret_cast<const uint4 *>(sm + PS_Q + so), qv);
+            float ak[8], aq[8], bo[8], kb8[8];
+#pragma unroll
+            for (int x = 0; x < 8; x++) {
+                const float f = __expf(gt[x] - ga[x]);
+                float e = ga[x] - gt[x];
+                if (e > 80.f) {
+                    fl |= 1 << m;
+                    e = 80.f;
+                }
+                ak[x] = kv[x] * f;
+                aq[x] = qv[x] * (q_scale * f);
+                bo[x] = kv[x] * __expf(e);
+                kb8[x] = t < len ? kv[x] * __expf(gc[x] - gt[x]) : 0.f;
             }
-            T[(o + r) * 65 + o + c] = v;
+            st16s(sm + PS_K + so, pack_bf8(ak));
+            st16s(sm + PS_Q + so, pack_bf8(aq));
+            // Kbar to the workspace; the same thread reads it back for the Kbar^T W operand
+            *reinterpret_cast<uint4 *>(outb + WB_KB + (t * 128 + i0) * 2) = pack_bf8(kb8);
+            // B_a rows: own sub-block (exponent >= 0), later sub-blocks via D(a, m) <= 1
+            if (m == 0) st16s(sm + PS_B0 + kbk * 2048 + swz(t, ch), pack_bf8(bo));
+            if (m == 1) st16s(sm + PS_B1 + kbk * 4096 + swz(t, ch), pack_bf8(bo));
+            if (m == 2) b2[2] = pack_bf8(bo);
+            if (m == 3) st16s(sm + PS_B3 + kbk * 8192 + swz(t, ch), pack_bf8(bo));
+#pragma unroll
+            for (int a2 = m + 1; a2 < 4; a2++) {
+                float dd[8], bv[8];
+                ld_f8(Dt + dpair(a2, m) * 128 + i0, dd);
+#pragma unroll
+                for (int x = 0; x < 8; x++) bv[x] = bo[x] * dd[x];
+                if (a2 == 1) st16s(sm + PS_B1 + kbk * 4096 + swz(t, ch), pack_bf8(bv));
+                if (a2 == 2) b2[m] = pack_bf8(bv);
+                if (a2 == 3) st16s(sm + PS_B3 + kbk * 8192 + swz(t, ch), pack_bf8(bv));
+            }
+        }
+        if (fl) {
+#pragma unroll
+            for (int m = 0; m < 4; m++)
+                if ((fl >> m) & 1) atomicOr(&flags[m], 1);
         }
     }
-    __syncthreads();
-    for (int d = 1; d < 4; d++) {
-        const int nb = 4 - d;  // blocks (a, a-d), a = d..3
-        for (int e = tid; e < nb * 256; e += 256) {
-            const int a = d + e / 256, b = a - d, r = (e >> 4) & 15, c = e & 15;
-            float acc = 0.f;
-            for (int m = b; m < a; m++)
-                for (int j = 0; j < 16; j++)
-                    acc += A[(16 * a + r) * 65 + 16 * m + j] * T[(16 * m + j) * 65 + 16 * b + c];
-            Y[(a - d) * 272 + r * 17 + c] = acc;
+    __syncthreads();  // G is dead: the A operand goes over it
+#pragma unroll
+    for (int m = 0; m < 4; m++) {
+        const int t = j + 16 * m;
+        const uint32_t so = (uint32_t)kbk * 8192 + swz(t, ch);
+        const uint4 ak = *reinterpret_cast<const uint4 *>(sm + PS_K + so);
+        const uint4 aq = *reinterpret_cast<const uint4 *>(sm + PS_Q + so);
+        st16s(sm + PS_R1 + kbk * 16384 + swz(t, ch), ak);
+        st16s(sm + PS_R1 + kbk * 16384 + swz(64 + t, ch), aq);
+        float ez[8], kt[8], qt[8];
+        ld_f8(Ez + m * 128 + i0, ez);
+        unpack_bf8(ak, kt);
+        unpack_bf8(aq, qt);
+#pragma unroll
+        for (int x = 0; x < 8; x++) {
+            kt[x] *= ez[x];
+            qt[x] *= ez[x];
         }
-        __syncthreads();
-        for (int e = tid; e < nb * 256; e += 256) {
-            const int a = d + e / 256, b = a - d, r = (e >> 4) & 15, c = e & 15;
-            float acc = 0.f;
-            for (int j = 0; j <= r; j++)
-                acc += T[(16 * a + r) * 65 + 16 * a + j] * Y[(a - d) * 272 + j * 17 + c];
-            T[(16 * a + r) * 65 + 16 * b + c] = -acc;
-        }
-        __syncthreads();
+        st16s(sm + PS_K + so, pack_bf8(kt));
+        st16s(sm + PS_Q + so, pack_bf8(qt));
     }
-    // M (bf16, K-major [t][s]) and Ktil (bf16, MN-major [t][i]) into the freed R region
-    uint8_t *sM = sm + PS_R, *sKt = sm + PS_R + 8192;
-    for (int e = tid; e < TC_C * TC_C; e += 256) {
-        const int t = e >> 6, s = e & 63;
-        stbf(sM, sw128(t, s), s <= t ? T[t * 65 + s] * sb[s] : 0.f);
-    }
-    for (int e = tid; e < TC_C * 128; e += 256) {
-        const int t = e >> 7, i = e & 127;
-        const uint32_t off = (i >> 6) * 8192 + sw128(t, i & 63);
-        float v = 0.f;
-        if (t < cd.len) v = ldbf(sK, off) * F[t * 129 + i] * Ez[(t >> 4) * 128 + i];
-        stbf(sKt, off, v);
-    }
+    // this thread's Kbar rows back from the workspace (its own writes), in flight during the
+    // rounds; they go to shared memory once the first region is free
+    uint4 kbar[4];
+#pragma unroll
+    for (int m = 0; m < 4; m++)
+        kbar[m] = *reinterpret_cast<const uint4 *>(outb + WB_KB + ((j + 16 * m) * 128 + i0) * 2);
     fence_async_shared();
     tc_fence_before();
-    __syncthreads();
+    ok = __syncthreads_and(ok ? 1 : 0);
+
+    // ------------------------------------------------------------- Akk, Aqk rounds
+    // descriptors: one base per operand, the start-address field advanced by offset >> 4
+    const uint64_t dsm = sdesc_kmajor(smem_u32(sm));
+    auto issue_round = [&](int a, int bbase) {
+        const int N = 16 * (a + 1);
+        const uint32_t id = idesc_f16(128, N, false, false);
+#pragma unroll
+        for (int ks = 0; ks < 8; ks++) {
+            const int kb = ks >> 2;
+            mma_bf16_ss(tb + round_col(a), dsm + ((PS_R1 + kb * 16384 + (ks & 3) * 32) >> 4),
+                        dsm + ((bbase + kb * N * 128 + (ks & 3) * 32) >> 4), id, ks ? 1u : 0u);
+        }
+    };
     if (tid == 0 && ok) {
         tc_fence_after();
-        constexpr uint32_t id_w = idesc_f16(64, 128, false, true);
+        issue_round(0, PS_B0);
+        issue_round(1, PS_B1);
+        issue_round(3, PS_B3);
+        mma_commit(&bar_mma);
+    }
+    if (ok) ok = mbar_wait(&bar_mma, 0, err, 0x503);
 #pragma unroll
-        for (int ks = 0; ks < 4; ks++) {
-            const uint64_t ad = sdesc_kmajor(smem_u32(sM + ks * 32));
-            mma_bf16_ss(tb, ad, sdesc_mnmajor(smem_u32(sKt + ks * 2048), 8192), id_w, ks ? 1u : 0u);
-            mma_bf16_ss(tb + 128, ad, sdesc_mnmajor(smem_u32(sV + ks * 2048), 8192), id_w,
-                        ks ? 1u : 0u);
+    for (int m = 0; m < 3; m++) st16s(sm + PS_B2 + kbk * 6144 + swz(j + 16 * m, ch), b2[m]);
+    fence_async_shared();
+    tc_fence_before();
+    ok = __syncthreads_and(ok ? 1 : 0);
+    if (tid == 0 && ok) {
+        tc_fence_after();
+        issue_round(2, PS_B2);
+        mma_commit(&bar_mma);
+    }
+    tc_fence_after();
+
+    // Read-out (M=128: TMEM lane r = row r). Rows 0-63: Akk row t = r; rows 64-127: Aqk row
+    // t = r - 64. Warp w reads columns [32 (w >> 2), +32) of its lane quarter; the two
+    // sub-blocks of its 32 rows have their own rounds.
+    const int q4 = warp & 3, hf = warp >> 2;
+    const uint32_t lb = (uint32_t)(32 * q4) << 16;
+    auto readout = [&]() {
+        const int r = 32 * q4 + lane, t = r & 63;
+        const int alo = 2 * (q4 & 1);
+        const bool kside = r < 64;
+#pragma unroll
+        for (int c16 = 0; c16 < 2; c16++) {
+            const int s0 = 32 * hf + 16 * c16;
+            float vlo[16], vhi[16];
+            if (s0 < 16 * (alo + 1)) {
+                tmem_ld16(tb + lb + round_col(alo) + s0, vlo);
+            } else {
+#pragma unroll
+                for (int x = 0; x < 16; x++) vlo[x] = 0.f;
+            }
+            if (s0 < 16 * (alo + 2)) {
+                tmem_ld16(tb + lb + round_col(alo + 1) + s0, vhi);
+            } else {
+#pragma unroll
+                for (int x = 0; x < 16; x++) vhi[x] = 0.f;
+            }
+            tmem_wait_ld();
+            float v[16];
+#pragma unroll
+            for (int x = 0; x < 16; x++) v[x] = lane >= 16 ? vhi[x] : vlo[x];
+            if (kside) {
+                const float bt = sb[t];
+#pragma unroll
+                for (int x = 0; x < 16; x++)
+                    if (s0 + x < t) AT[t * ATS + s0 + x] = bt * v[x];
+            } else {
+#pragma unroll
+                for (int x = 0; x < 16; x++) v[x] = s0 + x <= t ? v[x] : 0.f;
+                const uint4 p0 = pack_bf8(v), p1 = pack_bf8(v + 8);
+                st16s(sm + PS_AQ + swz(t, s0 >> 3), p0);
+                st16s(sm + PS_AQ + swz(t, (s0 >> 3) + 1), p1);
+                uint4 *dst = reinterpret_cast<uint4 *>(outb + WB_A + (t * 64 + s0) * 2);
+                dst[0] = p0;
+                dst[1] = p1;
+                float lo[16];
+                unpack_bf8(p0, lo);
+                unpack_bf8(p1, lo + 8);
+#pragma unroll
+                for (int x = 0; x < 16; x++) lo[x] = v[x] - lo[x];
+                uint4 *dl = reinterpret_cast<uint4 *>(outb + WB_AL + (t * 64 + s0) * 2);
+                dl[0] = pack_bf8(lo);
+                dl[1] = pack_bf8(lo + 8);
+            }
+        }
+    };
+    // (Akk lands over the B operands, so nothing is read out before round 2 completes)
+    if (ok) ok = mbar_wait(&bar_mma, 1, err, 0x504);
+    tc_fence_after();
+    if (ok) readout();
+    ok = __syncthreads_and(ok ? 1 : 0);
+
+    // Sub-blocks whose 15-step decay overflowed the factored form: every entry of their
+    // columns is recomputed exactly (e^(G_t - G_s) per element), from the inputs in global
+    // memory and G rebuilt in the (now free) first region.
+    if (ok && (flags[0] | flags[1] | flags[2] | flags[3])) {
+        {
+            const int i = tid & 127, half = tid >> 7;
+            float gv[32];
+            float acc = 0.f;
+#pragma unroll
+            for (int r = 0; r < 32; r++) {
+                const int t = 32 * half + r;
+                float x = 0.f;
+                if (t < len) {
+                    const float gg = gate[((size_t)(cd.t0 + t) * H + h) * TC_D + i];
+                    x = gate_is_log ? gg : logf(gg);
+                }
+                acc += x;
+                gv[r] = acc;
+            }
+            if (half == 0)
+                for (int r = 0; r < 32; r++) Gs[gsw(r, i)] = gv[r];
+            __syncthreads();
+            if (half == 1) {
+                const float base = Gs[gsw(31, i)];
+                for (int r = 0; r < 32; r++) Gs[gsw(32 + r, i)] = gv[r] + base;
+            }
+            __syncthreads();
+        }
+        for (int b = 0; b < 4; b++) {
+            if (!flags[b]) continue;
+            for (int e = tid; e < 16 * TC_C; e += 256) {
+                const int t = e >> 4, s = 16 * b + (e & 15);
+                if (s > t || t >= len) continue;
+                const __nv_bfloat16 *kt = kg + ((size_t)(cd.t0 + t) * H + h) * TC_D;
+                const __nv_bfloat16 *qt = qg + ((size_t)(cd.t0 + t) * H + h) * TC_D;
+                const __nv_bfloat16 *ks = kg + ((size_t)(cd.t0 + s) * H + h) * TC_D;
+                float akk = 0.f, aqk = 0.f;
+                for (int i = 0; i < TC_D; i++) {
+                    const float f = __expf(Gs[gsw(t, i)] - Gs[gsw(s, i)]) * __bfloat162float(ks[i]);
+                    akk += __bfloat162float(kt[i]) * f;
+                    aqk += __bfloat162float(qt[i]) * q_scale * f;
+                }
+                if (s < t) AT[t * ATS + s] = sb[t] * akk;
+                const __nv_bfloat16 a16 = __float2bfloat16_rn(aqk);
+                *reinterpret_cast<__nv_bfloat16 *>(sm + PS_AQ + swz(t, s >> 3) + (s & 7) * 2) = a16;
+                *reinterpret_cast<__nv_bfloat16 *>(outb + WB_A + (t * 64 + s) * 2) = a16;
+                *reinterpret_cast<__nv_bfloat16 *>(outb + WB_AL + (t * 64 + s) * 2) =
+                    __float2bfloat16_rn(aqk - __bfloat162float(a16));
+            }
+        }
+        __syncthreads();
+    }
+    // V into the first region (its generic-proxy uses are complete), Kbar beside it
+    fence_async_shared();
+    __syncthreads();
+    if (tid == 0 && ok) {
+        mbar_expect_tx(&bar_v, 16384);
+        for (int kb = 0; kb < 2; kb++)
+            tma_load_3d(sm + PS_V + kb * 8192, &maps.v, &bar_v, kb * 64, h, cd.t0);
+    }
+#pragma unroll
+    for (int m = 0; m < 4; m++) st16s(sm + PS_KBAR + kbk * 8192 + swz(j + 16 * m, ch), kbar[m]);
+
+    // ------------------------------------------- T = (I + Akk)^-1: 16x16 blocks, merged
+    // Akk (beta-scaled) sits strictly below the diagonal of AT; T (unit lower triangular)
+    // is stored transposed above it: T[x][y] (x > y) at AT[y][x]. Both L rows and T columns
+    // are then contiguous in shared memory. Diagonal 16x16 blocks by forward substitution;
+    // then T_10 = -T_11 L_10 T_00 merges 16 -> 32 (twice) and 32 -> 64 (once).
+    if (warp < 4 && lane < 16) {
+        const int o = 16 * warp, c = lane;
+        float tc[16];
+#pragma unroll
+        for (int r = 0; r < 16; r++) tc[r] = r == c ? 1.f : 0.f;
+#pragma unroll
+        for (int r = 1; r < 16; r++) {
+            float lr[16];
+#pragma unroll
+            for (int q = 0; q < (r + 3) / 4; q++) {
+                const float4 l4 = *reinterpret_cast<const float4 *>(AT + (o + r) * ATS + o + 4 * q);
+                lr[4 * q] = l4.x, lr[4 * q + 1] = l4.y, lr[4 * q + 2] = l4.z, lr[4 * q + 3] = l4.w;
+            }
+            float acc = 0.f;
+#pragma unroll
+            for (int jj = 0; jj < r; jj++) acc += lr[jj] * tc[jj];
+            if (r > c) tc[r] = -acc;
+        }
+#pragma unroll
+        for (int r = 1; r < 16; r++)
+            if (r > c) AT[(o + c) * ATS + o + r] = tc[r];
+    }
+    __syncthreads();
+    {   // 16 -> 32, both halves: Y = L_10 T_00, then T_10 = -T_11 Y
+        const int hb = tid >> 7, r = (tid >> 3) & 15, c0 = (tid & 7) * 2, B = 32 * hb;
+        float y0 = 0.f, y1 = 0.f;
+#pragma unroll
+        for (int q = 0; q < 4; q++) {
+            if (4 * q + 3 < c0) continue;  // T_00[j][c] = 0 for j < c
+            const float4 l4 = *reinterpret_cast<const float4 *>(AT + (B + 16 + r) * ATS + B + 4 * q);
+            const float4 a4 = *reinterpret_cast<const float4 *>(AT + (B + c0) * ATS + B + 4 * q);
+            const float4 b4 = *reinterpret_cast<const float4 *>(AT + (B + c0 + 1) * ATS + B + 4 * q);
+            const float lv[4] = {l4.x, l4.y, l4.z, l4.w}, av[4] = {a4.x, a4.y, a4.z, a4.w},
+                        bv[4] = {b4.x, b4.y, b4.z, b4.w};
+#pragma unroll
+            for (int x = 0; x < 4; x++) {
+                const int jj = 4 * q + x;
+                y0 += lv[x] * (jj > c0 ? av[x] : (jj == c0 ? 1.f : 0.f));
+                y1 += lv[x] * (jj > c0 + 1 ? bv[x] : (jj == c0 + 1 ? 1.f : 0.f));
+            }
+        }
+        Y[(16 * hb + r) * 36 + c0] = y0;
+        Y[(16 * hb + r) * 36 + c0 + 1] = y1;
+        __syncthreads();
+        float t0 = y0, t1 = y1;
+#pragma unroll
+        for (int jj = 0; jj < 15; jj++) {
+            if (jj < r) {
+                const float tv = AT[(B + 16 + jj) * ATS + B + 16 + r];
+                const float2 yv = *reinterpret_cast<const float2 *>(Y + (16 * hb + jj) * 36 + c0);
+                t0 += tv * yv.x;
+                t1 += tv * yv.y;
+            }
+        }
+        AT[(B + c0) * ATS + B + 16 + r] = -t0;
+        AT[(B + c0 + 1) * ATS + B + 16 + r] = -t1;
+    }
+    __syncthreads();
+    {   // 32 -> 64: Y = L_BA T_AA (rows 32..63, columns 0..31), then T_BA = -T_BB Y
+        const int r = tid >> 3, c4 = (tid & 7) * 4;
+        float y[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+        for (int q = 0; q < 8; q++) {
+            if (4 * q + 3 < c4) continue;
+            const float4 l4 = *reinterpret_cast<const float4 *>(AT + (32 + r) * ATS + 4 * q);
+            const float lv[4] = {l4.x, l4.y, l4.z, l4.w};
+#pragma unroll
+            for (int u = 0; u < 4; u++) {
+                const float4 t4 = *reinterpret_cast<const float4 *>(AT + (c4 + u) * ATS + 4 * q);
+                const float tv[4] = {t4.x, t4.y, t4.z, t4.w};
+#pragma unroll
+                for (int x = 0; x < 4; x++) {
+                    const int jj = 4 * q + x;
+                    y[u] += lv[x] * (jj > c4 + u ? tv[x] : (jj == c4 + u ? 1.f : 0.f));
+                }
+            }
+        }
+        *reinterpret_cast<float4 *>(Y + r * 36 + c4) = make_float4(y[0], y[1], y[2], y[3]);
+        __syncthreads();
+#pragma unroll
+        for (int jj = 0; jj < 31; jj++) {
+            if (jj < r) {
+                const float tv = AT[(32 + jj) * ATS + 32 + r];
+                const float4 yv = *reinterpret_cast<const float4 *>(Y + jj * 36 + c4);
+                y[0] += tv * yv.x;
+                y[1] += tv * yv.y;
+                y[2] += tv * yv.z;
+                y[3] += tv * yv.w;
+            }
+        }
+#pragma unroll
+        for (int u = 0; u < 4; u++) AT[(c4 + u) * ATS + 32 + r] = -y[u];
+    }
+    __syncthreads();
+    // M = T diag(beta) as bf16 hi + lo, K-major [t][s]
+    for (int u = tid; u < 512; u += 256) {
+        const int t = u >> 3, c8 = u & 7;
+        float mv[8], hi[8];
+#pragma unroll
+        for (int x = 0; x < 8; x++) {
+            const int s = 8 * c8 + x;
+            mv[x] = (s < t ? AT[s * ATS + t] : (s == t ? 1.f : 0.f)) * sb[s];
+        }
+        const uint4 ph = pack_bf8(mv);
+        unpack_bf8(ph, hi);
+#pragma unroll
+        for (int x = 0; x < 8; x++) mv[x] -= hi[x];
+        st16s(sm + PS_M + swz(t, c8), ph);
+        st16s(sm + PS_ML + swz(t, c8), pack_bf8(mv));
+    }
+    if (ok) ok = mbar_wait(&bar_v, 0, err, 0x505);
+    fence_async_shared();
+    tc_fence_before();
+    ok = __syncthreads_and(ok ? 1 : 0);
+
+    // ------------------------------------------------------- W = M Ktil, U = M V
+    if (tid == 0 && ok) {
+        tc_fence_after();
+        constexpr uint32_t idw = idesc_f16(64, 128, false, true);
+        const uint64_t dmn = sdesc_mnmajor(smem_u32(sm), 8192);
+#pragma unroll
+        for (int ks = 0; ks < 8; ks++) {
+            const uint64_t ad = dsm + (((ks < 4 ? PS_M : PS_ML) + (ks & 3) * 32) >> 4);
+            mma_bf16_ss(tb, ad, dmn + ((PS_K + (ks & 3) * 2048) >> 4), idw, ks ? 1u : 0u);
+            mma_bf16_ss(tb + 128, ad, dmn + ((PS_V + (ks & 3) * 2048) >> 4), idw, ks ? 1u : 0u);
         }
         mma_commit(&bar_mma);
     }
-    __syncwarp();
-    if (ok) ok = mbar_wait(&bar_mma, 0, err, 0x503);  // 5th commit: phase 0 of round parity
-    ok = __syncthreads_and(ok ? 1 : 0);
+    if (ok) ok = mbar_wait(&bar_mma, 0, err, 0x506);
     tc_fence_after();
-    if (ok && warp < 4) {
-        const int t = 16 * warp + lane;
-        for (int which = 0; which < 2; which++)
-            for (int c = 0; c < 128; c += 16) {
-                float v[16];
-                tmem_ld16(tb + ((uint32_t)(32 * warp) << 16) + which * 128 + c, v);
-                tmem_wait_ld();
-                if (lane < 16) {
-                    uint32_t pk[8];
+    // M=64 accumulators: row 16 q + l in lane l (< 16) of quarter q; warp w reads columns
+    // [64 (w >> 2), +64). W goes to shared memory (over Ktil, consumed), U to the workspace.
+    if (ok) {
+        const int t = 16 * q4 + lane;
 #pragma unroll
-                    for (int j = 0; j < 8; j++) {
-                        const __nv_bfloat162 p = __floats2bfloat162_rn(v[2 * j], v[2 * j + 1]);
-                        pk[j] = *reinterpret_cast<const uint32_t *>(&p);
-                    }
-                    uint4 *dst = reinterpret_cast<uint4 *>(outb + (which ? PB_U : PB_W) +
-                                                           (t * 128 + c) * 2);
-                    dst[0] = make_uint4(pk[0], pk[1], pk[2], pk[3]);
-                    dst[1] = make_uint4(pk[4], pk[5], pk[6], pk[7]);
-                }
+        for (int c16 = 0; c16 < 4; c16++) {
+            float wv[16], uv[16];
+            tmem_ld16(tb + lb + 64 * hf + 16 * c16, wv);
+            tmem_ld16(tb + lb + 128 + 64 * hf + 16 * c16, uv);
+            tmem_wait_ld();
+            if (lane < 16) {
+                st16s(sm + PS_K + hf * 8192 + swz(t, 2 * c16), pack_bf8(wv));
+                st16s(sm + PS_K + hf * 8192 + swz(t, 2 * c16 + 1), pack_bf8(wv + 8));
+                uint4 *dst =
+                    reinterpret_cast<uint4 *>(outb + WB_U + (t * 128 + 64 * hf + 16 * c16) * 2);
+                dst[0] = pack_bf8(uv);
+                dst[1] = pack_bf8(uv + 8);
             }
+        }
+    }
+    fence_async_shared();
+    tc_fence_before();
+    ok = __syncthreads_and(ok ? 1 : 0);
+
+    // --------------------------------------------- Kbar^T W (M=128) and Aqk W (M=64)
+    if (tid == 0 && ok) {
+        tc_fence_after();
+        constexpr uint32_t idp = idesc_f16(128, 128, true, true);
+        constexpr uint32_t ida = idesc_f16(64, 128, false, true);
+        const uint64_t dmn = sdesc_mnmajor(smem_u32(sm), 8192);
+#pragma unroll
+        for (int ks = 0; ks < 4; ks++) {
+            const uint64_t bw = dmn + ((PS_K + ks * 2048) >> 4);
+            mma_bf16_ss(tb, dmn + ((PS_KBAR + ks * 2048) >> 4), bw, idp, ks ? 1u : 0u);
+            mma_bf16_ss(tb + 128, dsm + ((PS_AQ + ks * 32) >> 4), bw, ida, ks ? 1u : 0u);
+        }
+        mma_commit(&bar_mma);
+    }
+    if (ok) ok = mbar_wait(&bar_mma, 1, err, 0x507);
+    tc_fence_after();
+    if (ok) {
+        const int i = 32 * q4 + lane;  // row of P
+        const int t = 16 * q4 + lane;  // row of Q' (lane < 16)
+#pragma unroll
+        for (int c16 = 0; c16 < 4; c16++) {
+            float pv[16], dv[16];
+            tmem_ld16(tb + lb + 64 * hf + 16 * c16, pv);
+            tmem_ld16(tb + lb + 128 + 64 * hf + 16 * c16, dv);
+            tmem_wait_ld();
+#pragma unroll
+            for (int x = 0; x < 16; x++) pv[x] = -pv[x];
+            uint4 *dp = reinterpret_cast<uint4 *>(outb + WB_P + (i * 128 + 64 * hf + 16 * c16) * 2);
+            dp[0] = pack_bf8(pv);
+            dp[1] = pack_bf8(pv + 8);
+            if (lane < 16) {
+                float qt[16];
+                unpack_bf8(*reinterpret_cast<const uint4 *>(sm + PS_Q + hf * 8192 + swz(t, 2 * c16)),
+                           qt);
+                unpack_bf8(
+                    *reinterpret_cast<const uint4 *>(sm + PS_Q + hf * 8192 + swz(t, 2 * c16 + 1)),
+                    qt + 8);
+#pragma unroll
+                for (int x = 0; x < 16; x++) qt[x] -= dv[x];
+                uint4 *dq =
+                    reinterpret_cast<uint4 *>(outb + WB_QP + (t * 128 + 64 * hf + 16 * c16) * 2);
+                dq[0] = pack_bf8(qt);
+                dq[1] = pack_bf8(qt + 8);
+            }
+        }
     }
     tc_fence_before();
     __syncthreads();
-    if (warp == 1) {
+    if (warp == 0) {
         __syncwarp();
         tmem_dealloc(tb, 256);
     }
 }
 
-}  // namespace k3
-
-namespace k3 {
-
+// ------------------------------------------------------------------------------ scan
 struct ScanMaps {
-    CUtensorMap w, q, kb, a, u, g;
+    CUtensorMap p, kb, u, qp, a, al;
 };
+
+// operand stage (bytes from a 1024-aligned base)
+constexpr int SS_P = 0;            // P    [128][128]: 2 k-blocks of [128][64]
+constexpr int SS_KB = 32768;       // Kbar [64][128]:  2 blocks of [64 t][64 i]
+constexpr int SS_QP = 49152;       // Q'   [64][128]:  2 k-blocks
+constexpr int SS_U = 65536;        // U    [64 t][64 j] (this CTA's half of d_v)
+constexpr int SS_A = 73728;        // Aqk  [64][64]
+constexpr int SS_AL = 81920;       // Aqk - bf16(Aqk) [64][64]
+constexpr int SS_TX = SS_AL + 8192;
+constexpr int SS_STAGE = (SS_TX + 1023) & ~1023;
+constexpr int SS_S16 = 2 * SS_STAGE;            // 2 x bf16 S [128 i][64 j] (MN-major B)
+constexpr int SS_BYTES = SS_S16 + 2 * 16384;
+constexpr int SS_SMEM = SS_BYTES + 1024;
+constexpr int SCAN_DV = 64;                     // d_v columns per CTA
 
 __device__ __forceinline__ bool warp_wait_all(uint64_t *bar, uint32_t parity, unsigned *err,
                                               unsigned code) {
@@ -414,47 +731,35 @@ __device__ __forceinline__ bool warp_wait_all(uint64_t *bar, uint32_t parity, un
     return __all_sync(0xffffffffu, ok);
 }
 
-// One CTA per (sequence, head, DVT-column slice of d_v). Warps 0-3: one thread per TMEM
-// lane (state row i; for the M=64 products, token row 16 w + lane of lanes 0-15); warp 4:
-// TMA producer; warp 5: TMEM allocation and MMA issue.
-template <int DVT>
+// One CTA per (sequence, head, half of d_v). Warps 0-3: thread i owns state row i (TMEM lane
+// i) and, for the M=64 output tile, token row 16 w + lane of lanes 0-15; warp 4: TMA
+// producer; warp 5: TMEM allocation and MMA issue.
 __global__ void __launch_bounds__(192, 1)
 kda_scan_tc(const __grid_constant__ ScanMaps maps, const TcChunk *__restrict__ chunks,
             const int *__restrict__ seq_chunk0, const uint8_t *__restrict__ ws,
             float *__restrict__ state, __nv_bfloat16 *__restrict__ o, int H,
             unsigned *__restrict__ err) {
-    // operand stage: W, Qtil, Kbar^T, Aqk, U slice, Gamma (padded to 1 KB)
-    constexpr int OFF_GAM = 57344 + 128 * DVT;
-    constexpr int STAGE_TX = OFF_GAM + 512;
-    constexpr int SB = (STAGE_TX + 1023) & ~1023;
-    static_assert(SB % 1024 == 0 && (DVT * 256) % 1024 == 0, "1024-byte aligned operands");
-    constexpr int OFF_S16 = 2 * SB;               // bf16 S^T [DVT][128] (2 K-blocks)
-    constexpr int OFF_XT = OFF_S16 + DVT * 256;   // bf16 X^T [DVT][64]
-    constexpr int TM_S = 0, TM_X = DVT, TM_O = 2 * DVT;
-    constexpr uint32_t TM_COLS = DVT <= 32 ? 128 : 512;
-    constexpr int NT = TC_D / DVT;
     extern __shared__ uint8_t smraw[];
     uint8_t *sm = (uint8_t *)(((uintptr_t)smraw + 1023) & ~(uintptr_t)1023);
-    __shared__ uint64_t op_full[2], op_empty[2], x_full, xt_ready, done, s16_ready;
+    __shared__ uint64_t op_full[2], op_empty[2], s_done, o_done[2], s16_ready;
     __shared__ uint32_t tslot;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const int tile = blockIdx.x % NT, h = (blockIdx.x / NT) % H, n = blockIdx.x / (NT * H);
+    const int half = blockIdx.x & 1, h = (blockIdx.x >> 1) % H, n = blockIdx.x / (2 * H);
     const int c0 = seq_chunk0[n], nc = seq_chunk0[n + 1] - c0;
-    const int col0 = tile * DVT;
-    uint8_t *S16 = sm + OFF_S16, *XT = sm + OFF_XT;
+    const int col0 = SCAN_DV * half;
+    constexpr uint32_t TM_S = 0, TM_O = 64;
 
     if (tid == 0) {
         for (int s = 0; s < 2; s++) {
             mbar_init(&op_full[s], 1);
             mbar_init(&op_empty[s], 1);
+            mbar_init(&o_done[s], 1);
         }
-        mbar_init(&x_full, 1);
-        mbar_init(&xt_ready, 128);
-        mbar_init(&done, 1);
+        mbar_init(&s_done, 1);
         mbar_init(&s16_ready, 128);
         fence_barrier_init();
     }
-    if (warp == 5) tmem_alloc(&tslot, TM_COLS);
+    if (warp == 5) tmem_alloc(&tslot, 256);
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
@@ -464,20 +769,34 @@ kda_scan_tc(const __grid_constant__ ScanMaps maps, const TcChunk *__restrict__ c
         if (lane == 0) {
             bool ok = true;
             int last[2] = {-1, -1};
-            for (int j = 0; j < nc && ok; j++) {
-                const int st = j & 1, ch = (c0 + j) * H + h;
-                if (j >= 2 && !(ok = mbar_wait(&op_empty[st], ((j >> 1) - 1) & 1, err, 0x601))) break;
-                uint8_t *s = sm + st * SB;
-                mbar_expect_tx(&op_full[st], STAGE_TX);
+            // chunk j + 3 is brought into L2 while chunk j is loaded (two stages cover only
+            // one chunk of look-ahead in shared memory)
+            auto prefetch = [&](int jj) {
+                const int chh = (c0 + jj) * H + h;
                 for (int kb = 0; kb < 2; kb++) {
-                    tma_load_3d(s + kb * 8192, &maps.w, &op_full[st], kb * 64, 0, ch);
-                    tma_load_3d(s + 16384 + kb * 8192, &maps.q, &op_full[st], kb * 64, 0, ch);
+                    tma_prefetch_3d(&maps.p, kb * 64, 0, chh);
+                    tma_prefetch_3d(&maps.kb, kb * 64, 0, chh);
+                    tma_prefetch_3d(&maps.qp, kb * 64, 0, chh);
                 }
-                tma_load_3d(s + 32768, &maps.kb, &op_full[st], 0, 0, ch);
-                tma_load_3d(s + 49152, &maps.a, &op_full[st], 0, 0, ch);
-                for (int u = 0; u < (DVT + 63) / 64; u++)
-                    tma_load_3d(s + 57344 + u * 8192, &maps.u, &op_full[st], col0 + u * 64, 0, ch);
-                tma_load_2d(s + OFF_GAM, &maps.g, &op_full[st], 0, ch);
+                tma_prefetch_3d(&maps.u, col0, 0, chh);
+                tma_prefetch_3d(&maps.a, 0, 0, chh);
+                tma_prefetch_3d(&maps.al, 0, 0, chh);
+            };
+            if (nc > 2) prefetch(2);
+            for (int j = 0; j < nc && ok; j++) {
+                const int st = j & 1, chh = (c0 + j) * H + h;
+                if (j + 3 < nc) prefetch(j + 3);
+                if (j >= 2 && !(ok = mbar_wait(&op_empty[st], ((j >> 1) - 1) & 1, err, 0x601))) break;
+                uint8_t *s = sm + st * SS_STAGE;
+                mbar_expect_tx(&op_full[st], SS_TX);
+                for (int kb = 0; kb < 2; kb++) {
+                    tma_load_3d(s + SS_P + kb * 16384, &maps.p, &op_full[st], kb * 64, 0, chh);
+                    tma_load_3d(s + SS_KB + kb * 8192, &maps.kb, &op_full[st], kb * 64, 0, chh);
+                    tma_load_3d(s + SS_QP + kb * 8192, &maps.qp, &op_full[st], kb * 64, 0, chh);
+                }
+                tma_load_3d(s + SS_U, &maps.u, &op_full[st], col0, 0, chh);
+                tma_load_3d(s + SS_A, &maps.a, &op_full[st], 0, 0, chh);
+                tma_load_3d(s + SS_AL, &maps.al, &op_full[st], 0, 0, chh);
                 last[st] = j;
             }
             // loads still in flight are waited for (bounded) before the CTA may exit
@@ -486,205 +805,181 @@ kda_scan_tc(const __grid_constant__ ScanMaps maps, const TcChunk *__restrict__ c
         }
     } else if (warp == 5) {
         if (lane == 0) {
-            constexpr uint32_t id64 = idesc_f16(64, DVT, false, false);
-            constexpr uint32_t id128 = idesc_f16(128, DVT, false, false);
+            constexpr uint32_t id_s = idesc_f16(128, SCAN_DV, false, true);
+            constexpr uint32_t id_k = idesc_f16(128, SCAN_DV, true, true);
+            constexpr uint32_t id_o = idesc_f16(64, SCAN_DV, false, true);
             for (int j = 0; j < nc; j++) {
                 const int st = j & 1;
-                const uint8_t *s = sm + st * SB;
+                const uint8_t *s = sm + st * SS_STAGE;
+                const uint8_t *S16 = sm + SS_S16 + (j & 1) * 16384;
                 if (!mbar_wait(&op_full[st], (j >> 1) & 1, err, 0x602)) break;
                 if (!mbar_wait(&s16_ready, j & 1, err, 0x603)) break;
                 tc_fence_after();
-                // X_acc = W . S16 ; O = Qtil . S16
-                for (int kb = 0; kb < 2; kb++)
+                // S (already Gamma S) += P . S16 + Kbar^T . U
 #pragma unroll
-                    for (int ks = 0; ks < 4; ks++)
-                        mma_bf16_ss(tb + TM_X, sdesc_kmajor(smem_u32(s + kb * 8192 + ks * 32)),
-                                    sdesc_kmajor(smem_u32(S16 + kb * DVT * 128 + ks * 32)), id64,
-                                    (kb | ks) ? 1u : 0u);
-                mma_commit(&x_full);
-                for (int kb = 0; kb < 2; kb++)
+                for (int ks = 0; ks < 8; ks++)
+                    mma_bf16_ss(tb + TM_S,
+                                sdesc_kmajor(smem_u32(s + SS_P + (ks >> 2) * 16384 + (ks & 3) * 32)),
+                                sdesc_mnmajor(smem_u32(S16 + ks * 2048), 8192), id_s, 1u);
 #pragma unroll
-                    for (int ks = 0; ks < 4; ks++)
-                        mma_bf16_ss(tb + TM_O, sdesc_kmajor(smem_u32(s + 16384 + kb * 8192 + ks * 32)),
-                                    sdesc_kmajor(smem_u32(S16 + kb * DVT * 128 + ks * 32)), id64,
-                                    (kb | ks) ? 1u : 0u);
-                if (!mbar_wait(&xt_ready, j & 1, err, 0x604)) break;
-                tc_fence_after();
-                // S += Kbar^T . X ; O += Aqk . X
+                for (int ks = 0; ks < 4; ks++)
+                    mma_bf16_ss(tb + TM_S, sdesc_mnmajor(smem_u32(s + SS_KB + ks * 2048), 8192),
+                                sdesc_mnmajor(smem_u32(s + SS_U + ks * 2048), 8192), id_k, 1u);
+                mma_commit(&s_done);
+                // O = Q' . S16 + Aqk . U
+                const uint32_t od = tb + TM_O + 64 * (j & 1);
 #pragma unroll
-                for (int ks = 0; ks < 4; ks++) {
-                    const uint64_t bx = sdesc_kmajor(smem_u32(XT + ks * 32));
-                    mma_bf16_ss(tb + TM_S, sdesc_kmajor(smem_u32(s + 32768 + ks * 32)), bx, id128, 1u);
-                    mma_bf16_ss(tb + TM_O, sdesc_kmajor(smem_u32(s + 49152 + ks * 32)), bx, id64, 1u);
-                }
-                mma_commit(&done);
+                for (int ks = 0; ks < 8; ks++)
+                    mma_bf16_ss(od,
+                                sdesc_kmajor(smem_u32(s + SS_QP + (ks >> 2) * 8192 + (ks & 3) * 32)),
+                                sdesc_mnmajor(smem_u32(S16 + ks * 2048), 8192), id_o, ks ? 1u : 0u);
+#pragma unroll
+                for (int ks = 0; ks < 8; ks++)
+                    mma_bf16_ss(od, sdesc_kmajor(smem_u32(s + (ks < 4 ? SS_A : SS_AL) + (ks & 3) * 32)),
+                                sdesc_mnmajor(smem_u32(s + SS_U + (ks & 3) * 2048), 8192), id_o, 1u);
+                mma_commit(&o_done[j & 1]);
                 mma_commit(&op_empty[st]);
             }
         }
-    } else {
+    } else if (nc > 0) {
         // ----------------------------------------------------------- compute warps
-        const int i = 32 * warp + lane;                 // state row / TMEM lane
-        const int t = 16 * warp + lane;                 // token row of the M=64 products
+        const int i = tid;                                // state row / TMEM lane
+        const int t = 16 * warp + lane;                   // token row of O (lanes < 16)
         const uint32_t lo = (uint32_t)(32 * warp) << 16;
-        float *Sg = state ? state + ((size_t)n * H + h) * TC_D * TC_D : nullptr;
-        // initial state slice -> TMEM (fp32) and S16 (bf16, S^T K-major)
-        for (int c = 0; c < DVT; c += 16) {
-            float v[16];
+        float *Sg = state ? state + (((size_t)n * H + h) * TC_D + i) * TC_D + col0 : nullptr;
+        float s[SCAN_DV];
+        auto write_s16 = [&](int buf) {
+            uint8_t *S16 = sm + SS_S16 + buf * 16384;
 #pragma unroll
-            for (int q = 0; q < 16; q++) v[q] = Sg ? Sg[(size_t)i * TC_D + col0 + c + q] : 0.f;
-            tmem_st16(tb + lo + TM_S + c, v);
+            for (int c = 0; c < 8; c++) st16s(S16 + swz(i, c), pack_bf8(s + 8 * c));
+        };
+        auto scale_store = [&](float gam) {
 #pragma unroll
-            for (int q = 0; q < 16; q++)
-                stbf(S16, (uint32_t)((i >> 6) * DVT * 128) + sw128(c + q, i & 63), v[q]);
+            for (int c = 0; c < SCAN_DV; c += 16) {
+                float v[16];
+#pragma unroll
+                for (int x = 0; x < 16; x++) v[x] = s[c + x] * gam;
+                tmem_st16(tb + lo + TM_S + c, v);
+            }
+            tmem_wait_st();
+        };
+        // Gamma of chunk jj for this state row, from the workspace (loaded two chunks ahead)
+        auto gamma = [&](int jj) {
+            return jj < nc ? *reinterpret_cast<const float *>(
+                                 ws + ((size_t)(c0 + jj) * H + h) * WB_BYTES + WB_G + 4 * i)
+                           : 0.f;
+        };
+        float gam1 = gamma(1), gam2 = gamma(2);
+        // initial state: bf16 copy for the first products, Gamma_0 S_0 into TMEM
+#pragma unroll
+        for (int c = 0; c < SCAN_DV; c += 4) {
+            const float4 v =
+                Sg ? *reinterpret_cast<const float4 *>(Sg + c) : make_float4(0.f, 0.f, 0.f, 0.f);
+            s[c] = v.x, s[c + 1] = v.y, s[c + 2] = v.z, s[c + 3] = v.w;
         }
-        tmem_wait_st();
+        write_s16(0);
+        scale_store(gamma(0));
         fence_async_shared();
         tc_fence_before();
         mbar_arrive(&s16_ready);
         bool ok = true;
-        TcChunk cd_next = nc > 0 ? chunks[c0] : TcChunk{0, 0, 0, 0};
-        for (int j = 0; j < nc; j++) {
+        TcChunk cd_next = chunks[c0];
+        for (int j = 0; j < nc && ok; j++) {
             const TcChunk cd = cd_next;
             if (j + 1 < nc) cd_next = chunks[c0 + j + 1];  // prefetched off the critical path
-            const uint8_t *s = sm + (j & 1) * SB;
-            if (!(ok = warp_wait_all(&x_full, j & 1, err, 0x605))) break;
+            if (!(ok = warp_wait_all(&s_done, j & 1, err, 0x605))) break;
             tc_fence_after();
-            const float gam = reinterpret_cast<const float *>(s + OFF_GAM)[i];
-            // X = U - X_acc (rows t < 16 of each warp's quarter) -> X^T in shared memory
-            for (int c = 0; c < DVT; c += 16) {
-                float v[16];
-                tmem_ld16(tb + lo + TM_X + c, v);
-                tmem_wait_ld();
-                if (lane < 16) {
 #pragma unroll
-                    for (int q = 0; q < 16; q++) {
-                        const int jj = c + q;
-                        const float u = DVT == 32 ? ldbf(s + 57344, (uint32_t)(t * 64 + jj * 2))
-                                                  : ldbf(s + 57344, (uint32_t)((jj >> 6) * 8192) +
-                                                                        sw128(t, jj & 63));
-                        stbf(XT, sw128(jj, t), u - v[q]);
-                    }
-                }
-            }
-            // S <- Gamma S, before S += Kbar^T X accumulates into it
-            for (int c = 0; c < DVT; c += 16) {
+            for (int c = 0; c < SCAN_DV; c += 16) {
                 float v[16];
                 tmem_ld16(tb + lo + TM_S + c, v);
-                tmem_wait_ld();
 #pragma unroll
-                for (int q = 0; q < 16; q++) v[q] *= gam;
-                tmem_st16(tb + lo + TM_S + c, v);
+                for (int x = 0; x < 16; x++) s[c + x] = v[x];
             }
-            tmem_wait_st();
-            fence_async_shared();
-            tc_fence_before();
-            mbar_arrive(&xt_ready);
-            if (!(ok = warp_wait_all(&done, j & 1, err, 0x606))) break;
+            tmem_wait_ld();
+            if (j + 1 < nc) {
+                write_s16((j + 1) & 1);
+                scale_store(gam1);
+                gam1 = gam2;
+                gam2 = gamma(j + 3);
+                fence_async_shared();
+                tc_fence_before();
+                mbar_arrive(&s16_ready);
+            } else if (Sg) {
+#pragma unroll
+                for (int c = 0; c < SCAN_DV; c += 4)
+                    *reinterpret_cast<float4 *>(Sg + c) =
+                        make_float4(s[c], s[c + 1], s[c + 2], s[c + 3]);
+            }
+            // outputs of chunk j (overlapping the next chunk's products)
+            if (!(ok = warp_wait_all(&o_done[j & 1], (j >> 1) & 1, err, 0x607))) break;
             tc_fence_after();
-            // outputs of this chunk, then the new S16
-            for (int c = 0; c < DVT; c += 16) {
+#pragma unroll
+            for (int c = 0; c < SCAN_DV; c += 16) {
                 float v[16];
-                tmem_ld16(tb + lo + TM_O + c, v);
+                tmem_ld16(tb + lo + TM_O + 64 * (j & 1) + c, v);
                 tmem_wait_ld();
                 if (lane < 16 && t < cd.len) {
-                    uint32_t pk[8];
-#pragma unroll
-                    for (int q = 0; q < 8; q++) {
-                        const __nv_bfloat162 p = __floats2bfloat162_rn(v[2 * q], v[2 * q + 1]);
-                        pk[q] = *reinterpret_cast<const uint32_t *>(&p);
-                    }
-                    uint4 *dst = reinterpret_cast<uint4 *>(o + ((size_t)(cd.t0 + t) * H + h) * TC_D +
-                                                           col0 + c);
-                    dst[0] = make_uint4(pk[0], pk[1], pk[2], pk[3]);
-                    dst[1] = make_uint4(pk[4], pk[5], pk[6], pk[7]);
+                    uint4 *dst = reinterpret_cast<uint4 *>(
+                        o + ((size_t)(cd.t0 + t) * H + h) * TC_D + col0 + c);
+                    dst[0] = pack_bf8(v);
+                    dst[1] = pack_bf8(v + 8);
                 }
             }
-            for (int c = 0; c < DVT; c += 16) {
-                float v[16];
-                tmem_ld16(tb + lo + TM_S + c, v);
-                tmem_wait_ld();
-#pragma unroll
-                for (int q = 0; q < 16; q++)
-                    stbf(S16, (uint32_t)((i >> 6) * DVT * 128) + sw128(c + q, i & 63), v[q]);
-            }
-            fence_async_shared();
             tc_fence_before();
-            mbar_arrive(&s16_ready);
-        }
-        if (ok && Sg) {
-            for (int c = 0; c < DVT; c += 16) {
-                float v[16];
-                tmem_ld16(tb + lo + TM_S + c, v);
-                tmem_wait_ld();
-#pragma unroll
-                for (int q = 0; q < 16; q++) Sg[(size_t)i * TC_D + col0 + c + q] = v[q];
-            }
         }
     }
     tc_fence_before();
     __syncthreads();
     if (warp == 5) {
         __syncwarp();
-        tmem_dealloc(tb, TM_COLS);
+        tmem_dealloc(tb, 256);
     }
 }
 
 // -------------------------------------------------------------------------- host side
-size_t prefill_tc_block_bytes() { return PB_BYTES; }
+size_t prefill_tc_block_bytes() { return WB_BYTES; }
 
-// Launch both phases. `blocks` has room for nc * H blocks of PB_BYTES; d_table / d_c0 are
+// Launch both phases. `blocks` has room for nc * H blocks of WB_BYTES; d_table / d_c0 are
 // the device copies of the chunk table and of the per-sequence first-chunk index.
 int run_prefill_tc(k3cuda_ctx *ctx, float *state, void *o, const void *q, const void *k,
                    const void *v, const float *gate, const float *beta, int total_tokens,
                    int n_seq, int H, float q_scale, int gate_is_log, long long nc,
                    const void *d_table, const int *d_c0, void *blocks) {
     const CUtensorMapDataType BF = CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+    const CUtensorMapDataType F32 = CU_TENSOR_MAP_DATA_TYPE_FLOAT32;
     PrepMaps pm;
     const uint64_t rs = (uint64_t)H * TC_D * 2;  // bytes per token row of q/k/v
     int rc = make_tmap_3d(&pm.q, q, BF, 2, TC_D, H, total_tokens, TC_D * 2, rs, 64, 1, 64);
     if (!rc) rc = make_tmap_3d(&pm.k, k, BF, 2, TC_D, H, total_tokens, TC_D * 2, rs, 64, 1, 64);
     if (!rc) rc = make_tmap_3d(&pm.v, v, BF, 2, TC_D, H, total_tokens, TC_D * 2, rs, 64, 1, 64);
+    if (!rc)
+        rc = make_tmap_3d(&pm.g, gate, F32, 4, TC_D, H, total_tokens, TC_D * 4, 2 * rs, 128, 1,
+                          64);
     if (rc) return rc;
     K3_CUDA_TRY(cudaFuncSetAttribute(kda_prep_tc, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                      PS_SMEM));
     kda_prep_tc<<<dim3((unsigned)nc, (unsigned)H), 256, PS_SMEM, ctx->stream>>>(
-        pm, (const TcChunk *)d_table, gate, beta, (uint8_t *)blocks, H, q_scale, gate_is_log,
-        ctx->err_word);
+        pm, (const TcChunk *)d_table, gate, beta, (const __nv_bfloat16 *)q,
+        (const __nv_bfloat16 *)k, (uint8_t *)blocks, H, q_scale, gate_is_log, ctx->err_word);
     rc = after_launch(ctx, "kda_prep_tc");
     if (rc) return rc;
 
     const uint64_t nch = (uint64_t)nc * H;
-    const bool wide = (long long)n_seq * H >= ctx->sm_count;
-    const int dvt = wide ? 128 : 32;
     ScanMaps sm;
     uint8_t *b = (uint8_t *)blocks;
-    rc = make_tmap_3d(&sm.w, b + PB_W, BF, 2, 128, 64, nch, 256, PB_BYTES, 64, 64, 1);
-    if (!rc) rc = make_tmap_3d(&sm.q, b + PB_Q, BF, 2, 128, 64, nch, 256, PB_BYTES, 64, 64, 1);
-    if (!rc) rc = make_tmap_3d(&sm.kb, b + PB_KB, BF, 2, 64, 128, nch, 128, PB_BYTES, 64, 128, 1);
-    if (!rc) rc = make_tmap_3d(&sm.a, b + PB_A, BF, 2, 64, 64, nch, 128, PB_BYTES, 64, 64, 1);
-    if (!rc)
-        rc = make_tmap_3d(&sm.u, b + PB_U, BF, 2, 128, 64, nch, 256, PB_BYTES, dvt > 64 ? 64 : dvt,
-                          64, 1);
-    if (!rc)
-        rc = make_tmap_2d(&sm.g, b + PB_G, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, 128, nch, PB_BYTES,
-                          128, 1);
+    rc = make_tmap_3d(&sm.p, b + WB_P, BF, 2, 128, 128, nch, 256, WB_BYTES, 64, 128, 1);
+    if (!rc) rc = make_tmap_3d(&sm.kb, b + WB_KB, BF, 2, 128, 64, nch, 256, WB_BYTES, 64, 64, 1);
+    if (!rc) rc = make_tmap_3d(&sm.u, b + WB_U, BF, 2, 128, 64, nch, 256, WB_BYTES, 64, 64, 1);
+    if (!rc) rc = make_tmap_3d(&sm.qp, b + WB_QP, BF, 2, 128, 64, nch, 256, WB_BYTES, 64, 64, 1);
+    if (!rc) rc = make_tmap_3d(&sm.a, b + WB_A, BF, 2, 64, 64, nch, 128, WB_BYTES, 64, 64, 1);
+    if (!rc) rc = make_tmap_3d(&sm.al, b + WB_AL, BF, 2, 64, 64, nch, 128, WB_BYTES, 64, 64, 1);
     if (rc) return rc;
-    const long long nblk = (long long)n_seq * H * (TC_D / dvt);
-    if (dvt == 128) {
-        const int smem = 2 * (((57344 + 128 * 128 + 512) + 1023) & ~1023) + 128 * 384 + 1024;
-        K3_CUDA_TRY(cudaFuncSetAttribute(kda_scan_tc<128>,
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
-        kda_scan_tc<128><<<(unsigned)nblk, 192, smem, ctx->stream>>>(
-            sm, (const TcChunk *)d_table, d_c0, (const uint8_t *)blocks, state,
-            (__nv_bfloat16 *)o, H, ctx->err_word);
-    } else {
-        const int smem = 2 * (((57344 + 128 * 32 + 512) + 1023) & ~1023) + 32 * 384 + 1024;
-        K3_CUDA_TRY(cudaFuncSetAttribute(kda_scan_tc<32>,
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
-        kda_scan_tc<32><<<(unsigned)nblk, 192, smem, ctx->stream>>>(
-            sm, (const TcChunk *)d_table, d_c0, (const uint8_t *)blocks, state,
-            (__nv_bfloat16 *)o, H, ctx->err_word);
-    }
+    const long long nblk = (long long)n_seq * H * (TC_D / SCAN_DV);
+    K3_CUDA_TRY(cudaFuncSetAttribute(kda_scan_tc, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     SS_SMEM));
+    kda_scan_tc<<<(unsigned)nblk, 192, SS_SMEM, ctx->stream>>>(
+        sm, (const TcChunk *)d_table, d_c0, b, state, (__nv_bfloat16 *)o, H, ctx->err_word);
     return after_launch(ctx, "kda_scan_tc");
 }
 
