@@ -86,6 +86,14 @@ __device__ __forceinline__ int gsw(int t, int i) {
     return t * 128 + (((u & ~7) | ((u ^ t) & 7)) << 2) + (i & 3);
 }
 
+// 2^x on the special-function unit (the intra-chunk kernel keeps G in log2 units)
+__device__ __forceinline__ float ex2(float x) {
+    float y;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
+constexpr float kLog2e = 1.4426950408889634f;
+
 __device__ __forceinline__ uint32_t pack_bf2(float a, float b) {
     const __nv_bfloat162 p = __floats2bfloat162_rn(a, b);
     return *reinterpret_cast<const uint32_t *>(&p);
@@ -115,7 +123,8 @@ __device__ __forceinline__ void ld_f8(const float *p, float *v) {
 __device__ __forceinline__ void st16s(uint8_t *p, uint4 v) { *reinterpret_cast<uint4 *>(p) = v; }
 
 struct PrepMaps {
-    CUtensorMap q, k, v, g;
+    CUtensorMap q, k, v, g;         // inputs (loads)
+    CUtensorMap p, kb, u, qp, a, al;  // workspace (stores), the scan's maps
 };
 
 // Shared memory of kda_prep_tc (bytes from a 1024-aligned base); regions are reused as the
@@ -137,6 +146,7 @@ constexpr int PS_M = PS_R2 + 20480;      //   M bf16 [64][64] (over the dead tai
 constexpr int PS_AQ = 94208;             // Aqk bf16 [64][64] (A of Aqk W)
 constexpr int PS_D = 102400;             // D(a,b) = e^(G_r(a) - G_r(b)) fp32 [6][128]
 constexpr int PS_EZ = PS_D + 3072;       // e^(G_r(a)) fp32 [4][128]
+constexpr int PS_AL = PS_D;              //   then Aqk - bf16(Aqk) bf16 [64][64] (stored out)
 constexpr int PS_ML = PS_D;              //   then M - bf16(M) bf16 [64][64]
 constexpr int PS_BETA = PS_D + 8192;     // beta [64]
 constexpr int PS_BYTES = PS_BETA + 256;
@@ -151,6 +161,9 @@ static_assert(PS_M % 1024 == 0 && PS_AQ % 1024 == 0 && PS_B2 % 1024 == 0 && PS_B
 
 // TMEM column of round a's accumulator (N = 16 (a + 1) columns each)
 __device__ __forceinline__ int round_col(int a) { return 8 * a * (a + 1); }
+// largest sub-block growth factor 2^x the factored form admits (e^80); beyond it the
+// sub-block's columns take the exact path
+constexpr float kOverflowLog2 = 80.f * kLog2e;
 // index of D(a, b), b < a
 __host__ __device__ constexpr int dpair(int a, int b) { return a * (a - 1) / 2 + b; }
 
@@ -206,9 +219,13 @@ kda_prep_tc(const __grid_constant__ PrepMaps maps, const TcChunk *__restrict__ c
 #pragma unroll
         for (int r = 0; r < 32; r++) gv[r] = Gs[(32 * half + r) * 128 + i];  // dense, as loaded
         __syncthreads();  // every thread holds its gates: the tile is rewritten swizzled
-        if (!gate_is_log) {
+        // G in log2 units: every use below is 2^(difference of G values)
+        if (gate_is_log) {
 #pragma unroll
-            for (int r = 0; r < 32; r++) gv[r] = 32 * half + r < len ? logf(gv[r]) : 0.f;
+            for (int r = 0; r < 32; r++) gv[r] *= kLog2e;
+        } else {
+#pragma unroll
+            for (int r = 0; r < 32; r++) gv[r] = 32 * half + r < len ? log2f(gv[r]) : 0.f;
         }
         float acc = 0.f;
 #pragma unroll
@@ -237,10 +254,10 @@ kda_prep_tc(const __grid_constant__ PrepMaps maps, const TcChunk *__restrict__ c
 #pragma unroll
         for (int a = 1; a < 4; a++)
 #pragma unroll
-            for (int b = 0; b < a; b++) Dt[dpair(a, b) * 128 + i] = __expf(gr[a] - gr[b]);
+            for (int b = 0; b < a; b++) Dt[dpair(a, b) * 128 + i] = ex2(gr[a] - gr[b]);
 #pragma unroll
-        for (int a = 0; a < 4; a++) Ez[a * 128 + i] = __expf(gr[a]);
-        reinterpret_cast<float *>(outb + WB_G)[i] = __expf(Gs[gsw(63, i)]);
+        for (int a = 0; a < 4; a++) Ez[a * 128 + i] = ex2(gr[a]);
+        reinterpret_cast<float *>(outb + WB_G)[i] = ex2(Gs[gsw(63, i)]);
     }
     ok = mbar_wait(&bar_qk, 0, err, 0x502) && ok;
     __syncthreads();
@@ -252,7 +269,8 @@ kda_prep_tc(const __grid_constant__ PrepMaps maps, const TcChunk *__restrict__ c
     // them by e^(G_r(t)) into Ktil and Qtil.
     const int cc = 2 * warp + (lane >> 4), j = lane & 15, kbk = cc >> 3, ch = cc & 7;
     const int i0 = 8 * cc;
-    uint4 b2[3];  // rows of B_2, written once round 2's buffer is free
+    uint4 b2[3];    // rows of B_2, written once round 2's buffer is free
+    uint4 kbar[4];  // Kbar rows, stored once the first region is free
     {
         float gc[8];
         ld_g8(Gs, 63, i0, gc);
@@ -267,23 +285,21 @@ kda_prep_tc(const __grid_constant__ PrepMaps maps, const TcChunk *__restrict__ c
             unpack_bf8(*reinterpret_cast<const uint4 *>(sm + PS_K + so), kv);
             unpack_bf8(*reinterpret_cast<const uint4 *>(sm + PS_Q + so), qv);
             float ak[8], aq[8], bo[8], kb8[8];
+            float emax = 0.f;
 #pragma unroll
             for (int x = 0; x < 8; x++) {
-                const float f = __expf(gt[x] - ga[x]);
-                float e = ga[x] - gt[x];
-                if (e > 80.f) {
-                    fl |= 1 << m;
-                    e = 80.f;
-                }
+                const float f = ex2(gt[x] - ga[x]);
+                const float e = ga[x] - gt[x];  // >= 0: at most 15 decay steps, in log2 units
+                emax = fmaxf(emax, e);
                 ak[x] = kv[x] * f;
                 aq[x] = qv[x] * (q_scale * f);
-                bo[x] = kv[x] * __expf(e);
-                kb8[x] = t < len ? kv[x] * __expf(gc[x] - gt[x]) : 0.f;
+                bo[x] = kv[x] * ex2(fminf(e, kOverflowLog2));
+                kb8[x] = t < len ? kv[x] * ex2(gc[x] - gt[x]) : 0.f;
             }
+            if (emax > kOverflowLog2) fl |= 1 << m;
             st16s(sm + PS_K + so, pack_bf8(ak));
             st16s(sm + PS_Q + so, pack_bf8(aq));
-            // Kbar to the workspace; the same thread reads it back for the Kbar^T W operand
-            *reinterpret_cast<uint4 *>(outb + WB_KB + (t * 128 + i0) * 2) = pack_bf8(kb8);
+            kbar[m] = pack_bf8(kb8);
             // B_a rows: own sub-block (exponent >= 0), later sub-blocks via D(a, m) <= 1
             if (m == 0) st16s(sm + PS_B0 + kbk * 2048 + swz(t, ch), pack_bf8(bo));
             if (m == 1) st16s(sm + PS_B1 + kbk * 4096 + swz(t, ch), pack_bf8(bo));
@@ -327,12 +343,6 @@ kda_prep_tc(const __grid_constant__ PrepMaps maps, const TcChunk *__restrict__ c
         st16s(sm + PS_K + so, pack_bf8(kt));
         st16s(sm + PS_Q + so, pack_bf8(qt));
     }
-    // this thread's Kbar rows back from the workspace (its own writes), in flight during the
-    // rounds; they go to shared memory once the first region is free
-    uint4 kbar[4];
-#pragma unroll
-    for (int m = 0; m < 4; m++)
-        kbar[m] = *reinterpret_cast<const uint4 *>(outb + WB_KB + ((j + 16 * m) * 128 + i0) * 2);
     fence_async_shared();
     tc_fence_before();
     ok = __syncthreads_and(ok ? 1 : 0);
@@ -410,17 +420,13 @@ kda_prep_tc(const __grid_constant__ PrepMaps maps, const TcChunk *__restrict__ c
                 const uint4 p0 = pack_bf8(v), p1 = pack_bf8(v + 8);
                 st16s(sm + PS_AQ + swz(t, s0 >> 3), p0);
                 st16s(sm + PS_AQ + swz(t, (s0 >> 3) + 1), p1);
-                uint4 *dst = reinterpret_cast<uint4 *>(outb + WB_A + (t * 64 + s0) * 2);
-                dst[0] = p0;
-                dst[1] = p1;
                 float lo[16];
                 unpack_bf8(p0, lo);
                 unpack_bf8(p1, lo + 8);
 #pragma unroll
                 for (int x = 0; x < 16; x++) lo[x] = v[x] - lo[x];
-                uint4 *dl = reinterpret_cast<uint4 *>(outb + WB_AL + (t * 64 + s0) * 2);
-                dl[0] = pack_bf8(lo);
-                dl[1] = pack_bf8(lo + 8);
+                st16s(sm + PS_AL + swz(t, s0 >> 3), pack_bf8(lo));
+                st16s(sm + PS_AL + swz(t, (s0 >> 3) + 1), pack_bf8(lo + 8));
             }
         }
     };
@@ -474,24 +480,30 @@ kda_prep_tc(const __grid_constant__ PrepMaps maps, const TcChunk *__restrict__ c
                 }
                 if (s < t) AT[t * ATS + s] = sb[t] * akk;
                 const __nv_bfloat16 a16 = __float2bfloat16_rn(aqk);
-                *reinterpret_cast<__nv_bfloat16 *>(sm + PS_AQ + swz(t, s >> 3) + (s & 7) * 2) = a16;
-                *reinterpret_cast<__nv_bfloat16 *>(outb + WB_A + (t * 64 + s) * 2) = a16;
-                *reinterpret_cast<__nv_bfloat16 *>(outb + WB_AL + (t * 64 + s) * 2) =
+                const uint32_t so = swz(t, s >> 3) + (s & 7) * 2;
+                *reinterpret_cast<__nv_bfloat16 *>(sm + PS_AQ + so) = a16;
+                *reinterpret_cast<__nv_bfloat16 *>(sm + PS_AL + so) =
                     __float2bfloat16_rn(aqk - __bfloat162float(a16));
             }
         }
         __syncthreads();
     }
-    // V into the first region (its generic-proxy uses are complete), Kbar beside it
+    // V into the first region (its generic-proxy uses are complete), Kbar beside it; Aqk and
+    // its remainder out to the workspace
+    const int chh = blockIdx.x * H + h;  // this block's index in the workspace
     fence_async_shared();
     __syncthreads();
     if (tid == 0 && ok) {
         mbar_expect_tx(&bar_v, 16384);
         for (int kb = 0; kb < 2; kb++)
             tma_load_3d(sm + PS_V + kb * 8192, &maps.v, &bar_v, kb * 64, h, cd.t0);
+        tma_store_3d(&maps.a, sm + PS_AQ, 0, 0, chh);
+        tma_store_3d(&maps.al, sm + PS_AL, 0, 0, chh);
+        bulk_commit();
     }
 #pragma unroll
     for (int m = 0; m < 4; m++) st16s(sm + PS_KBAR + kbk * 8192 + swz(j + 16 * m, ch), kbar[m]);
+    fence_async_shared();
 
     // ------------------------------------------- T = (I + Akk)^-1: 16x16 blocks, merged
     // Akk (beta-scaled) sits strictly below the diagonal of AT; T (unit lower triangular)
@@ -521,8 +533,15 @@ kda_prep_tc(const __grid_constant__ PrepMaps maps, const TcChunk *__restrict__ c
             if (r > c) AT[(o + c) * ATS + o + r] = tc[r];
     }
     __syncthreads();
-    {   // 16 -> 32, both halves: Y = L_10 T_00, then T_10 = -T_11 Y
-        const int hb = tid >> 7, r = (tid >> 3) & 15, c0 = (tid & 7) * 2, B = 32 * hb;
+    if (tid == 0 && ok) {
+        for (int kb = 0; kb < 2; kb++)
+            tma_store_3d(&maps.kb, sm + PS_KBAR + kb * 8192, kb * 64, 0, chh);
+        bulk_commit();
+    }
+    {   // 16 -> 32, both halves: Y = L_10 T_00, then T_10 = -T_11 Y. Lane: row r; the
+        // two columns c0, c0 + 1 are shared by a half-warp (T loads broadcast).
+        const int hb = warp >> 2, r = lane & 15, c0 = 4 * (warp & 3) + 2 * (lane >> 4);
+        const int B = 32 * hb;
         float y0 = 0.f, y1 = 0.f;
 #pragma unroll
         for (int q = 0; q < 4; q++) {
@@ -539,58 +558,55 @@ kda_prep_tc(const __grid_constant__ PrepMaps maps, const TcChunk *__restrict__ c
                 y1 += lv[x] * (jj > c0 + 1 ? bv[x] : (jj == c0 + 1 ? 1.f : 0.f));
             }
         }
-        Y[(16 * hb + r) * 36 + c0] = y0;
-        Y[(16 * hb + r) * 36 + c0 + 1] = y1;
+        *reinterpret_cast<float2 *>(Y + (16 * hb + r) * 36 + c0) = make_float2(y0, y1);
         __syncthreads();
-        float t0 = y0, t1 = y1;
 #pragma unroll
         for (int jj = 0; jj < 15; jj++) {
-            if (jj < r) {
-                const float tv = AT[(B + 16 + jj) * ATS + B + 16 + r];
-                const float2 yv = *reinterpret_cast<const float2 *>(Y + (16 * hb + jj) * 36 + c0);
-                t0 += tv * yv.x;
-                t1 += tv * yv.y;
-            }
+            const float tv = jj < r ? AT[(B + 16 + jj) * ATS + B + 16 + r] : 0.f;
+            const float2 yv = *reinterpret_cast<const float2 *>(Y + (16 * hb + jj) * 36 + c0);
+            y0 += tv * yv.x;
+            y1 += tv * yv.y;
         }
-        AT[(B + c0) * ATS + B + 16 + r] = -t0;
-        AT[(B + c0 + 1) * ATS + B + 16 + r] = -t1;
+        AT[(B + c0) * ATS + B + 16 + r] = -y0;
+        AT[(B + c0 + 1) * ATS + B + 16 + r] = -y1;
     }
     __syncthreads();
-    {   // 32 -> 64: Y = L_BA T_AA (rows 32..63, columns 0..31), then T_BA = -T_BB Y
-        const int r = tid >> 3, c4 = (tid & 7) * 4;
+    {   // 32 -> 64: Y = L_BA T_AA (rows 32..63, columns 0..31), then T_BA = -T_BB Y.
+        // Lane: row r; warp w: columns 4w..4w+3 (warp-uniform: T loads broadcast).
+        const int r = lane, c4 = 4 * warp;
         float y[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
         for (int q = 0; q < 8; q++) {
-            if (4 * q + 3 < c4) continue;
+            if (q < warp) continue;  // T_AA[j][c] = 0 for j < c
             const float4 l4 = *reinterpret_cast<const float4 *>(AT + (32 + r) * ATS + 4 * q);
             const float lv[4] = {l4.x, l4.y, l4.z, l4.w};
 #pragma unroll
             for (int u = 0; u < 4; u++) {
                 const float4 t4 = *reinterpret_cast<const float4 *>(AT + (c4 + u) * ATS + 4 * q);
-                const float tv[4] = {t4.x, t4.y, t4.z, t4.w};
+                float tv[4] = {t4.x, t4.y, t4.z, t4.w};
+                if (q == warp) {
 #pragma unroll
-                for (int x = 0; x < 4; x++) {
-                    const int jj = 4 * q + x;
-                    y[u] += lv[x] * (jj > c4 + u ? tv[x] : (jj == c4 + u ? 1.f : 0.f));
+                    for (int x = 0; x < 4; x++) tv[x] = x > u ? tv[x] : (x == u ? 1.f : 0.f);
                 }
+#pragma unroll
+                for (int x = 0; x < 4; x++) y[u] += lv[x] * tv[x];
             }
         }
         *reinterpret_cast<float4 *>(Y + r * 36 + c4) = make_float4(y[0], y[1], y[2], y[3]);
         __syncthreads();
 #pragma unroll
         for (int jj = 0; jj < 31; jj++) {
-            if (jj < r) {
-                const float tv = AT[(32 + jj) * ATS + 32 + r];
-                const float4 yv = *reinterpret_cast<const float4 *>(Y + jj * 36 + c4);
-                y[0] += tv * yv.x;
-                y[1] += tv * yv.y;
-                y[2] += tv * yv.z;
-                y[3] += tv * yv.w;
-            }
+            const float tv = jj < r ? AT[(32 + jj) * ATS + 32 + r] : 0.f;
+            const float4 yv = *reinterpret_cast<const float4 *>(Y + jj * 36 + c4);
+            y[0] += tv * yv.x;
+            y[1] += tv * yv.y;
+            y[2] += tv * yv.z;
+            y[3] += tv * yv.w;
         }
 #pragma unroll
         for (int u = 0; u < 4; u++) AT[(c4 + u) * ATS + 32 + r] = -y[u];
     }
+    if (tid == 0) bulk_wait_read<0>();  // the remainder of M goes over the stored-out Aqk
     __syncthreads();
     // M = T diag(beta) as bf16 hi + lo, K-major [t][s]
     for (int u = tid; u < 512; u += 256) {
@@ -633,18 +649,17 @@ kda_prep_tc(const __grid_constant__ PrepMaps maps, const TcChunk *__restrict__ c
     if (ok) {
         const int t = 16 * q4 + lane;
 #pragma unroll
-        for (int c16 = 0; c16 < 4; c16++) {
-            float wv[16], uv[16];
-            tmem_ld16(tb + lb + 64 * hf + 16 * c16, wv);
-            tmem_ld16(tb + lb + 128 + 64 * hf + 16 * c16, uv);
+        for (int c32 = 0; c32 < 2; c32++) {
+            float wv[32], uv[32];
+            tmem_ld32(tb + lb + 64 * hf + 32 * c32, wv);
+            tmem_ld32(tb + lb + 128 + 64 * hf + 32 * c32, uv);
             tmem_wait_ld();
             if (lane < 16) {
-                st16s(sm + PS_K + hf * 8192 + swz(t, 2 * c16), pack_bf8(wv));
-                st16s(sm + PS_K + hf * 8192 + swz(t, 2 * c16 + 1), pack_bf8(wv + 8));
-                uint4 *dst =
-                    reinterpret_cast<uint4 *>(outb + WB_U + (t * 128 + 64 * hf + 16 * c16) * 2);
-                dst[0] = pack_bf8(uv);
-                dst[1] = pack_bf8(uv + 8);
+#pragma unroll
+                for (int c = 0; c < 4; c++) {
+                    st16s(sm + PS_K + hf * 8192 + swz(t, 4 * c32 + c), pack_bf8(wv + 8 * c));
+                    st16s(sm + PS_V + hf * 8192 + swz(t, 4 * c32 + c), pack_bf8(uv + 8 * c));
+                }
             }
         }
     }
@@ -655,6 +670,8 @@ kda_prep_tc(const __grid_constant__ PrepMaps maps, const TcChunk *__restrict__ c
     // --------------------------------------------- Kbar^T W (M=128) and Aqk W (M=64)
     if (tid == 0 && ok) {
         tc_fence_after();
+        for (int kb = 0; kb < 2; kb++) tma_store_3d(&maps.u, sm + PS_V + kb * 8192, kb * 64, 0, chh);
+        bulk_commit();
         constexpr uint32_t idp = idesc_f16(128, 128, true, true);
         constexpr uint32_t ida = idesc_f16(64, 128, false, true);
         const uint64_t dmn = sdesc_mnmajor(smem_u32(sm), 8192);
@@ -672,33 +689,43 @@ kda_prep_tc(const __grid_constant__ PrepMaps maps, const TcChunk *__restrict__ c
         const int i = 32 * q4 + lane;  // row of P
         const int t = 16 * q4 + lane;  // row of Q' (lane < 16)
 #pragma unroll
-        for (int c16 = 0; c16 < 4; c16++) {
-            float pv[16], dv[16];
-            tmem_ld16(tb + lb + 64 * hf + 16 * c16, pv);
-            tmem_ld16(tb + lb + 128 + 64 * hf + 16 * c16, dv);
+        for (int c32 = 0; c32 < 2; c32++) {
+            float pv[32], dv[32];
+            tmem_ld32(tb + lb + 64 * hf + 32 * c32, pv);
+            tmem_ld32(tb + lb + 128 + 64 * hf + 32 * c32, dv);
             tmem_wait_ld();
 #pragma unroll
-            for (int x = 0; x < 16; x++) pv[x] = -pv[x];
-            uint4 *dp = reinterpret_cast<uint4 *>(outb + WB_P + (i * 128 + 64 * hf + 16 * c16) * 2);
-            dp[0] = pack_bf8(pv);
-            dp[1] = pack_bf8(pv + 8);
-            if (lane < 16) {
-                float qt[16];
-                unpack_bf8(*reinterpret_cast<const uint4 *>(sm + PS_Q + hf * 8192 + swz(t, 2 * c16)),
-                           qt);
-                unpack_bf8(
-                    *reinterpret_cast<const uint4 *>(sm + PS_Q + hf * 8192 + swz(t, 2 * c16 + 1)),
-                    qt + 8);
+            for (int x = 0; x < 32; x++) pv[x] = -pv[x];
+            // P half hf ([128][64]) over the dead AT/M (hf 0) or Kbar (hf 1) tiles
+            uint8_t *pb = sm + (hf ? PS_KBAR : PS_R2);
 #pragma unroll
-                for (int x = 0; x < 16; x++) qt[x] -= dv[x];
-                uint4 *dq =
-                    reinterpret_cast<uint4 *>(outb + WB_QP + (t * 128 + 64 * hf + 16 * c16) * 2);
-                dq[0] = pack_bf8(qt);
-                dq[1] = pack_bf8(qt + 8);
+            for (int c = 0; c < 4; c++) st16s(pb + swz(i, 4 * c32 + c), pack_bf8(pv + 8 * c));
+            if (lane < 16) {
+#pragma unroll
+                for (int c = 0; c < 4; c++) {
+                    uint8_t *qa = sm + PS_Q + hf * 8192 + swz(t, 4 * c32 + c);
+                    float qt[8];
+                    unpack_bf8(*reinterpret_cast<const uint4 *>(qa), qt);
+#pragma unroll
+                    for (int x = 0; x < 8; x++) qt[x] -= dv[8 * c + x];
+                    st16s(qa, pack_bf8(qt));  // Q' over Qtil
+                }
             }
         }
     }
+    fence_async_shared();
     tc_fence_before();
+    __syncthreads();
+    if (tid == 0) {
+        if (ok) {
+            tma_store_3d(&maps.p, sm + PS_R2, 0, 0, chh);
+            tma_store_3d(&maps.p, sm + PS_KBAR, 64, 0, chh);
+            for (int kb = 0; kb < 2; kb++)
+                tma_store_3d(&maps.qp, sm + PS_Q + kb * 8192, kb * 64, 0, chh);
+            bulk_commit();
+        }
+        bulk_wait_read<0>();  // shared memory stays valid until the stores have read it
+    }
     __syncthreads();
     if (warp == 0) {
         __syncwarp();
@@ -956,6 +983,15 @@ int run_prefill_tc(k3cuda_ctx *ctx, float *state, void *o, const void *q, const 
     if (!rc)
         rc = make_tmap_3d(&pm.g, gate, F32, 4, TC_D, H, total_tokens, TC_D * 4, 2 * rs, 128, 1,
                           64);
+    // workspace maps: stores of the intra-chunk kernel, loads of the scan
+    const uint64_t nch = (uint64_t)nc * H;
+    uint8_t *b = (uint8_t *)blocks;
+    if (!rc) rc = make_tmap_3d(&pm.p, b + WB_P, BF, 2, 128, 128, nch, 256, WB_BYTES, 64, 128, 1);
+    if (!rc) rc = make_tmap_3d(&pm.kb, b + WB_KB, BF, 2, 128, 64, nch, 256, WB_BYTES, 64, 64, 1);
+    if (!rc) rc = make_tmap_3d(&pm.u, b + WB_U, BF, 2, 128, 64, nch, 256, WB_BYTES, 64, 64, 1);
+    if (!rc) rc = make_tmap_3d(&pm.qp, b + WB_QP, BF, 2, 128, 64, nch, 256, WB_BYTES, 64, 64, 1);
+    if (!rc) rc = make_tmap_3d(&pm.a, b + WB_A, BF, 2, 64, 64, nch, 128, WB_BYTES, 64, 64, 1);
+    if (!rc) rc = make_tmap_3d(&pm.al, b + WB_AL, BF, 2, 64, 64, nch, 128, WB_BYTES, 64, 64, 1);
     if (rc) return rc;
     K3_CUDA_TRY(cudaFuncSetAttribute(kda_prep_tc, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                      PS_SMEM));
@@ -965,16 +1001,7 @@ int run_prefill_tc(k3cuda_ctx *ctx, float *state, void *o, const void *q, const 
     rc = after_launch(ctx, "kda_prep_tc");
     if (rc) return rc;
 
-    const uint64_t nch = (uint64_t)nc * H;
-    ScanMaps sm;
-    uint8_t *b = (uint8_t *)blocks;
-    rc = make_tmap_3d(&sm.p, b + WB_P, BF, 2, 128, 128, nch, 256, WB_BYTES, 64, 128, 1);
-    if (!rc) rc = make_tmap_3d(&sm.kb, b + WB_KB, BF, 2, 128, 64, nch, 256, WB_BYTES, 64, 64, 1);
-    if (!rc) rc = make_tmap_3d(&sm.u, b + WB_U, BF, 2, 128, 64, nch, 256, WB_BYTES, 64, 64, 1);
-    if (!rc) rc = make_tmap_3d(&sm.qp, b + WB_QP, BF, 2, 128, 64, nch, 256, WB_BYTES, 64, 64, 1);
-    if (!rc) rc = make_tmap_3d(&sm.a, b + WB_A, BF, 2, 64, 64, nch, 128, WB_BYTES, 64, 64, 1);
-    if (!rc) rc = make_tmap_3d(&sm.al, b + WB_AL, BF, 2, 64, 64, nch, 128, WB_BYTES, 64, 64, 1);
-    if (rc) return rc;
+    ScanMaps sm{pm.p, pm.kb, pm.u, pm.qp, pm.a, pm.al};
     const long long nblk = (long long)n_seq * H * (TC_D / SCAN_DV);
     K3_CUDA_TRY(cudaFuncSetAttribute(kda_scan_tc, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                      SS_SMEM));
