@@ -32,7 +32,7 @@
 //       cores; W = M Ktil, U = M V (M as bf16 hi + lo); P = -Kbar^T W (M=128, N=128,
 //       K=64) and Aqk W on tcgen05. Writes P, Kbar, U, Q', Aqk (bf16; Aqk also its
 //       bf16 remainder) and Gamma (fp32).
-//   kda_scan_tc   one CTA per (sequence, head, 64-column half of d_v). The fp32 state
+//   kda_scan_tc   one CTA per (sequence, head, 64- or 128-column slice of d_v). The fp32 state
 //       slice lives in TMEM; per chunk the compute warps write its bf16 copy S16 to shared
 //       memory and scale the TMEM copy by Gamma (read two chunks ahead from the workspace),
 //       then one thread issues
@@ -738,19 +738,27 @@ struct ScanMaps {
     CUtensorMap p, kb, u, qp, a, al;
 };
 
-// operand stage (bytes from a 1024-aligned base)
-constexpr int SS_P = 0;            // P    [128][128]: 2 k-blocks of [128][64]
-constexpr int SS_KB = 32768;       // Kbar [64][128]:  2 blocks of [64 t][64 i]
-constexpr int SS_QP = 49152;       // Q'   [64][128]:  2 k-blocks
-constexpr int SS_U = 65536;        // U    [64 t][64 j] (this CTA's half of d_v)
-constexpr int SS_A = 73728;        // Aqk  [64][64]
-constexpr int SS_AL = 81920;       // Aqk - bf16(Aqk) [64][64]
-constexpr int SS_TX = SS_AL + 8192;
-constexpr int SS_STAGE = (SS_TX + 1023) & ~1023;
-constexpr int SS_S16 = 2 * SS_STAGE;            // 2 x bf16 S [128 i][64 j] (MN-major B)
-constexpr int SS_BYTES = SS_S16 + 2 * 16384;
-constexpr int SS_SMEM = SS_BYTES + 1024;
-constexpr int SCAN_DV = 64;                     // d_v columns per CTA
+// Shared-memory plan of kda_scan_tc for DVT state columns per CTA (64: two CTAs per head,
+// 128: one). Operand stage (bytes from a 1024-aligned base):
+template <int DVT>
+struct ScanCfg {
+    static constexpr int P = 0;                      // P    [128][128]: 2 k-blocks [128][64]
+    static constexpr int KB = 32768;                 // Kbar [64][128]:  2 blocks [64 t][64 i]
+    static constexpr int QP = 49152;                 // Q'   [64][128]:  2 k-blocks
+    static constexpr int U = 65536;                  // U    DVT/64 blocks [64 t][64 j]
+    static constexpr int A = U + DVT * 128;          // Aqk  [64][64]
+    static constexpr int AL = A + 8192;              // Aqk - bf16(Aqk)
+    static constexpr int TX = AL + 8192;             // bytes per stage
+    static constexpr int STAGE = (TX + 1023) & ~1023;
+    // bf16 copy of the state, [128 i][DVT j] MN-major (64-column atoms of 16 KB); two copies
+    // at DVT = 64, one at DVT = 128 (whose next copy then waits for the output products)
+    static constexpr int NS16 = DVT == 64 ? 2 : 1;
+    static constexpr int S16B = 128 * DVT * 2;
+    static constexpr int S16 = 2 * STAGE;
+    static constexpr int SMEM = S16 + NS16 * S16B + 1024;
+    static constexpr uint32_t TM_COLS = DVT == 64 ? 256 : 512;  // S, O (x2)
+};
+static_assert(ScanCfg<128>::SMEM <= 232448 && ScanCfg<64>::SMEM <= 232448, "scan shared memory");
 
 __device__ __forceinline__ bool warp_wait_all(uint64_t *bar, uint32_t parity, unsigned *err,
                                               unsigned code) {
@@ -758,23 +766,26 @@ __device__ __forceinline__ bool warp_wait_all(uint64_t *bar, uint32_t parity, un
     return __all_sync(0xffffffffu, ok);
 }
 
-// One CTA per (sequence, head, half of d_v). Warps 0-3: thread i owns state row i (TMEM lane
-// i) and, for the M=64 output tile, token row 16 w + lane of lanes 0-15; warp 4: TMA
-// producer; warp 5: TMEM allocation and MMA issue.
+// One CTA per (sequence, head, DVT-column slice of d_v). Warps 0-3: thread i owns state row i
+// (TMEM lane i) and, for the M=64 output tile, token row 16 w + lane of lanes 0-15; warp 4:
+// TMA producer; warp 5: TMEM allocation and MMA issue.
+template <int DVT>
 __global__ void __launch_bounds__(192, 1)
 kda_scan_tc(const __grid_constant__ ScanMaps maps, const TcChunk *__restrict__ chunks,
             const int *__restrict__ seq_chunk0, const uint8_t *__restrict__ ws,
             float *__restrict__ state, __nv_bfloat16 *__restrict__ o, int H,
             unsigned *__restrict__ err) {
+    using C = ScanCfg<DVT>;
+    constexpr int NT = TC_D / DVT;
     extern __shared__ uint8_t smraw[];
     uint8_t *sm = (uint8_t *)(((uintptr_t)smraw + 1023) & ~(uintptr_t)1023);
     __shared__ uint64_t op_full[2], op_empty[2], s_done, o_done[2], s16_ready;
     __shared__ uint32_t tslot;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const int half = blockIdx.x & 1, h = (blockIdx.x >> 1) % H, n = blockIdx.x / (2 * H);
+    const int slice = blockIdx.x % NT, h = (blockIdx.x / NT) % H, n = blockIdx.x / (NT * H);
     const int c0 = seq_chunk0[n], nc = seq_chunk0[n + 1] - c0;
-    const int col0 = SCAN_DV * half;
-    constexpr uint32_t TM_S = 0, TM_O = 64;
+    const int col0 = DVT * slice;
+    constexpr uint32_t TM_S = 0, TM_O = DVT;
 
     if (tid == 0) {
         for (int s = 0; s < 2; s++) {
@@ -786,7 +797,7 @@ kda_scan_tc(const __grid_constant__ ScanMaps maps, const TcChunk *__restrict__ c
         mbar_init(&s16_ready, 128);
         fence_barrier_init();
     }
-    if (warp == 5) tmem_alloc(&tslot, 256);
+    if (warp == 5) tmem_alloc(&tslot, C::TM_COLS);
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
@@ -805,7 +816,7 @@ kda_scan_tc(const __grid_constant__ ScanMaps maps, const TcChunk *__restrict__ c
                     tma_prefetch_3d(&maps.kb, kb * 64, 0, chh);
                     tma_prefetch_3d(&maps.qp, kb * 64, 0, chh);
                 }
-                tma_prefetch_3d(&maps.u, col0, 0, chh);
+                for (int u = 0; u < DVT / 64; u++) tma_prefetch_3d(&maps.u, col0 + 64 * u, 0, chh);
                 tma_prefetch_3d(&maps.a, 0, 0, chh);
                 tma_prefetch_3d(&maps.al, 0, 0, chh);
             };
@@ -814,16 +825,17 @@ kda_scan_tc(const __grid_constant__ ScanMaps maps, const TcChunk *__restrict__ c
                 const int st = j & 1, chh = (c0 + j) * H + h;
                 if (j + 3 < nc) prefetch(j + 3);
                 if (j >= 2 && !(ok = mbar_wait(&op_empty[st], ((j >> 1) - 1) & 1, err, 0x601))) break;
-                uint8_t *s = sm + st * SS_STAGE;
-                mbar_expect_tx(&op_full[st], SS_TX);
+                uint8_t *s = sm + st * C::STAGE;
+                mbar_expect_tx(&op_full[st], C::TX);
                 for (int kb = 0; kb < 2; kb++) {
-                    tma_load_3d(s + SS_P + kb * 16384, &maps.p, &op_full[st], kb * 64, 0, chh);
-                    tma_load_3d(s + SS_KB + kb * 8192, &maps.kb, &op_full[st], kb * 64, 0, chh);
-                    tma_load_3d(s + SS_QP + kb * 8192, &maps.qp, &op_full[st], kb * 64, 0, chh);
+                    tma_load_3d(s + C::P + kb * 16384, &maps.p, &op_full[st], kb * 64, 0, chh);
+                    tma_load_3d(s + C::KB + kb * 8192, &maps.kb, &op_full[st], kb * 64, 0, chh);
+                    tma_load_3d(s + C::QP + kb * 8192, &maps.qp, &op_full[st], kb * 64, 0, chh);
                 }
-                tma_load_3d(s + SS_U, &maps.u, &op_full[st], col0, 0, chh);
-                tma_load_3d(s + SS_A, &maps.a, &op_full[st], 0, 0, chh);
-                tma_load_3d(s + SS_AL, &maps.al, &op_full[st], 0, 0, chh);
+                for (int u = 0; u < DVT / 64; u++)
+                    tma_load_3d(s + C::U + u * 8192, &maps.u, &op_full[st], col0 + 64 * u, 0, chh);
+                tma_load_3d(s + C::A, &maps.a, &op_full[st], 0, 0, chh);
+                tma_load_3d(s + C::AL, &maps.al, &op_full[st], 0, 0, chh);
                 last[st] = j;
             }
             // loads still in flight are waited for (bounded) before the CTA may exit
@@ -832,38 +844,39 @@ kda_scan_tc(const __grid_constant__ ScanMaps maps, const TcChunk *__restrict__ c
         }
     } else if (warp == 5) {
         if (lane == 0) {
-            constexpr uint32_t id_s = idesc_f16(128, SCAN_DV, false, true);
-            constexpr uint32_t id_k = idesc_f16(128, SCAN_DV, true, true);
-            constexpr uint32_t id_o = idesc_f16(64, SCAN_DV, false, true);
+            constexpr uint32_t id_s = idesc_f16(128, DVT, false, true);
+            constexpr uint32_t id_k = idesc_f16(128, DVT, true, true);
+            constexpr uint32_t id_o = idesc_f16(64, DVT, false, true);
+            const uint64_t dk = sdesc_kmajor(smem_u32(sm));
+            const uint64_t d8 = sdesc_mnmajor(smem_u32(sm), 8192);     // U, Kbar: 8 KB atoms
+            const uint64_t d16 = sdesc_mnmajor(smem_u32(sm), 16384);   // S16: 16 KB atoms
             for (int j = 0; j < nc; j++) {
                 const int st = j & 1;
-                const uint8_t *s = sm + st * SS_STAGE;
-                const uint8_t *S16 = sm + SS_S16 + (j & 1) * 16384;
+                const int s = st * C::STAGE;
+                const int s16 = C::S16 + (C::NS16 == 2 ? (j & 1) * C::S16B : 0);
                 if (!mbar_wait(&op_full[st], (j >> 1) & 1, err, 0x602)) break;
                 if (!mbar_wait(&s16_ready, j & 1, err, 0x603)) break;
                 tc_fence_after();
                 // S (already Gamma S) += P . S16 + Kbar^T . U
 #pragma unroll
                 for (int ks = 0; ks < 8; ks++)
-                    mma_bf16_ss(tb + TM_S,
-                                sdesc_kmajor(smem_u32(s + SS_P + (ks >> 2) * 16384 + (ks & 3) * 32)),
-                                sdesc_mnmajor(smem_u32(S16 + ks * 2048), 8192), id_s, 1u);
+                    mma_bf16_ss(tb + TM_S, dk + ((s + C::P + (ks >> 2) * 16384 + (ks & 3) * 32) >> 4),
+                                d16 + ((s16 + ks * 2048) >> 4), id_s, 1u);
 #pragma unroll
                 for (int ks = 0; ks < 4; ks++)
-                    mma_bf16_ss(tb + TM_S, sdesc_mnmajor(smem_u32(s + SS_KB + ks * 2048), 8192),
-                                sdesc_mnmajor(smem_u32(s + SS_U + ks * 2048), 8192), id_k, 1u);
+                    mma_bf16_ss(tb + TM_S, d8 + ((s + C::KB + ks * 2048) >> 4),
+                                d8 + ((s + C::U + ks * 2048) >> 4), id_k, 1u);
                 mma_commit(&s_done);
                 // O = Q' . S16 + Aqk . U
-                const uint32_t od = tb + TM_O + 64 * (j & 1);
+                const uint32_t od = tb + TM_O + DVT * (j & 1);
 #pragma unroll
                 for (int ks = 0; ks < 8; ks++)
-                    mma_bf16_ss(od,
-                                sdesc_kmajor(smem_u32(s + SS_QP + (ks >> 2) * 8192 + (ks & 3) * 32)),
-                                sdesc_mnmajor(smem_u32(S16 + ks * 2048), 8192), id_o, ks ? 1u : 0u);
+                    mma_bf16_ss(od, dk + ((s + C::QP + (ks >> 2) * 8192 + (ks & 3) * 32) >> 4),
+                                d16 + ((s16 + ks * 2048) >> 4), id_o, ks ? 1u : 0u);
 #pragma unroll
                 for (int ks = 0; ks < 8; ks++)
-                    mma_bf16_ss(od, sdesc_kmajor(smem_u32(s + (ks < 4 ? SS_A : SS_AL) + (ks & 3) * 32)),
-                                sdesc_mnmajor(smem_u32(s + SS_U + (ks & 3) * 2048), 8192), id_o, 1u);
+                    mma_bf16_ss(od, dk + ((s + (ks < 4 ? C::A : C::AL) + (ks & 3) * 32) >> 4),
+                                d8 + ((s + C::U + (ks & 3) * 2048) >> 4), id_o, 1u);
                 mma_commit(&o_done[j & 1]);
                 mma_commit(&op_empty[st]);
             }
@@ -874,21 +887,26 @@ kda_scan_tc(const __grid_constant__ ScanMaps maps, const TcChunk *__restrict__ c
         const int t = 16 * warp + lane;                   // token row of O (lanes < 16)
         const uint32_t lo = (uint32_t)(32 * warp) << 16;
         float *Sg = state ? state + (((size_t)n * H + h) * TC_D + i) * TC_D + col0 : nullptr;
-        float s[SCAN_DV];
-        auto write_s16 = [&](int buf) {
-            uint8_t *S16 = sm + SS_S16 + buf * 16384;
+        float s[64];  // 64 columns of the state row at a time
+        // bf16 copy of columns [64 a, +64) of this row into buffer `buf`
+        auto write_s16 = [&](int buf, int a) {
+            uint8_t *S16 = sm + C::S16 + buf * C::S16B + a * 16384;
 #pragma unroll
             for (int c = 0; c < 8; c++) st16s(S16 + swz(i, c), pack_bf8(s + 8 * c));
         };
-        auto scale_store = [&](float gam) {
+        auto scale_store = [&](float gam, int a) {
 #pragma unroll
-            for (int c = 0; c < SCAN_DV; c += 16) {
+            for (int c = 0; c < 64; c += 16) {
                 float v[16];
 #pragma unroll
                 for (int x = 0; x < 16; x++) v[x] = s[c + x] * gam;
-                tmem_st16(tb + lo + TM_S + c, v);
+                tmem_st16(tb + lo + TM_S + 64 * a + c, v);
             }
-            tmem_wait_st();
+        };
+        auto load_s = [&](int a) {
+#pragma unroll
+            for (int c = 0; c < 64; c += 32) tmem_ld32(tb + lo + TM_S + 64 * a + c, s + c);
+            tmem_wait_ld();
         };
         // Gamma of chunk jj for this state row, from the workspace (loaded two chunks ahead)
         auto gamma = [&](int jj) {
@@ -898,14 +916,19 @@ kda_scan_tc(const __grid_constant__ ScanMaps maps, const TcChunk *__restrict__ c
         };
         float gam1 = gamma(1), gam2 = gamma(2);
         // initial state: bf16 copy for the first products, Gamma_0 S_0 into TMEM
+        const float gam0 = gamma(0);
 #pragma unroll
-        for (int c = 0; c < SCAN_DV; c += 4) {
-            const float4 v =
-                Sg ? *reinterpret_cast<const float4 *>(Sg + c) : make_float4(0.f, 0.f, 0.f, 0.f);
-            s[c] = v.x, s[c + 1] = v.y, s[c + 2] = v.z, s[c + 3] = v.w;
+        for (int a = 0; a < DVT / 64; a++) {
+#pragma unroll
+            for (int c = 0; c < 64; c += 4) {
+                const float4 v = Sg ? *reinterpret_cast<const float4 *>(Sg + 64 * a + c)
+                                    : make_float4(0.f, 0.f, 0.f, 0.f);
+                s[c] = v.x, s[c + 1] = v.y, s[c + 2] = v.z, s[c + 3] = v.w;
+            }
+            write_s16(0, a);
+            scale_store(gam0, a);
         }
-        write_s16(0);
-        scale_store(gamma(0));
+        tmem_wait_st();
         fence_async_shared();
         tc_fence_before();
         mbar_arrive(&s16_ready);
@@ -915,18 +938,18 @@ kda_scan_tc(const __grid_constant__ ScanMaps maps, const TcChunk *__restrict__ c
             const TcChunk cd = cd_next;
             if (j + 1 < nc) cd_next = chunks[c0 + j + 1];  // prefetched off the critical path
             if (!(ok = warp_wait_all(&s_done, j & 1, err, 0x605))) break;
+            // one copy of S16 (DVT = 128): the output products of chunk j read it too
+            if (C::NS16 == 1 && !(ok = warp_wait_all(&o_done[j & 1], (j >> 1) & 1, err, 0x606)))
+                break;
             tc_fence_after();
-#pragma unroll
-            for (int c = 0; c < SCAN_DV; c += 16) {
-                float v[16];
-                tmem_ld16(tb + lo + TM_S + c, v);
-#pragma unroll
-                for (int x = 0; x < 16; x++) s[c + x] = v[x];
-            }
-            tmem_wait_ld();
             if (j + 1 < nc) {
-                write_s16((j + 1) & 1);
-                scale_store(gam1);
+#pragma unroll
+                for (int a = 0; a < DVT / 64; a++) {
+                    load_s(a);
+                    write_s16(C::NS16 == 2 ? (j + 1) & 1 : 0, a);
+                    scale_store(gam1, a);
+                }
+                tmem_wait_st();
                 gam1 = gam2;
                 gam2 = gamma(j + 3);
                 fence_async_shared();
@@ -934,23 +957,28 @@ kda_scan_tc(const __grid_constant__ ScanMaps maps, const TcChunk *__restrict__ c
                 mbar_arrive(&s16_ready);
             } else if (Sg) {
 #pragma unroll
-                for (int c = 0; c < SCAN_DV; c += 4)
-                    *reinterpret_cast<float4 *>(Sg + c) =
-                        make_float4(s[c], s[c + 1], s[c + 2], s[c + 3]);
+                for (int a = 0; a < DVT / 64; a++) {
+                    load_s(a);
+#pragma unroll
+                    for (int c = 0; c < 64; c += 4)
+                        *reinterpret_cast<float4 *>(Sg + 64 * a + c) =
+                            make_float4(s[c], s[c + 1], s[c + 2], s[c + 3]);
+                }
             }
             // outputs of chunk j (overlapping the next chunk's products)
-            if (!(ok = warp_wait_all(&o_done[j & 1], (j >> 1) & 1, err, 0x607))) break;
+            if (C::NS16 == 2 && !(ok = warp_wait_all(&o_done[j & 1], (j >> 1) & 1, err, 0x607)))
+                break;
             tc_fence_after();
 #pragma unroll
-            for (int c = 0; c < SCAN_DV; c += 16) {
-                float v[16];
-                tmem_ld16(tb + lo + TM_O + 64 * (j & 1) + c, v);
+            for (int c = 0; c < DVT; c += 32) {
+                float v[32];
+                tmem_ld32(tb + lo + TM_O + DVT * (j & 1) + c, v);
                 tmem_wait_ld();
                 if (lane < 16 && t < cd.len) {
                     uint4 *dst = reinterpret_cast<uint4 *>(
                         o + ((size_t)(cd.t0 + t) * H + h) * TC_D + col0 + c);
-                    dst[0] = pack_bf8(v);
-                    dst[1] = pack_bf8(v + 8);
+#pragma unroll
+                    for (int q = 0; q < 4; q++) dst[q] = pack_bf8(v + 8 * q);
                 }
             }
             tc_fence_before();
@@ -960,7 +988,7 @@ kda_scan_tc(const __grid_constant__ ScanMaps maps, const TcChunk *__restrict__ c
     __syncthreads();
     if (warp == 5) {
         __syncwarp();
-        tmem_dealloc(tb, 256);
+        tmem_dealloc(tb, C::TM_COLS);
     }
 }
 
@@ -1002,11 +1030,22 @@ int run_prefill_tc(k3cuda_ctx *ctx, float *state, void *o, const void *q, const 
     if (rc) return rc;
 
     ScanMaps sm{pm.p, pm.kb, pm.u, pm.qp, pm.a, pm.al};
-    const long long nblk = (long long)n_seq * H * (TC_D / SCAN_DV);
-    K3_CUDA_TRY(cudaFuncSetAttribute(kda_scan_tc, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                     SS_SMEM));
-    kda_scan_tc<<<(unsigned)nblk, 192, SS_SMEM, ctx->stream>>>(
-        sm, (const TcChunk *)d_table, d_c0, b, state, (__nv_bfloat16 *)o, H, ctx->err_word);
+    // Few (sequence, head) pairs: two CTAs per head halve each chunk's chain; enough of them
+    // to fill the GPU: one CTA per head, half the operand traffic.
+    const bool wide = (long long)n_seq * H >= ctx->sm_count;
+    if (wide) {
+        using C = ScanCfg<128>;
+        K3_CUDA_TRY(cudaFuncSetAttribute(kda_scan_tc<128>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM));
+        kda_scan_tc<128><<<(unsigned)((long long)n_seq * H), 192, C::SMEM, ctx->stream>>>(
+            sm, (const TcChunk *)d_table, d_c0, b, state, (__nv_bfloat16 *)o, H, ctx->err_word);
+    } else {
+        using C = ScanCfg<64>;
+        K3_CUDA_TRY(cudaFuncSetAttribute(kda_scan_tc<64>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM));
+        kda_scan_tc<64><<<(unsigned)((long long)n_seq * H * 2), 192, C::SMEM, ctx->stream>>>(
+            sm, (const TcChunk *)d_table, d_c0, b, state, (__nv_bfloat16 *)o, H, ctx->err_word);
+    }
     return after_launch(ctx, "kda_scan_tc");
 }
 

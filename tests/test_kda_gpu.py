@@ -219,6 +219,37 @@ def test_prefill_extreme_decay_takes_the_exact_path(ctx):
     assert W.rel_fro(o, o_ref) < TOL_F32 and W.rel_fro(S, S_ref) < TOL_F32
 
 
+def test_prefill_extreme_decay_bf16_tensor_core(ctx):
+    """The same overflow case through the tensor-core path (bf16, d=128): the flagged
+    sub-blocks' columns of Akk/Aqk are recomputed exactly inside the intra-chunk kernel."""
+    rng = np.random.default_rng(10)
+    H, d, T = 2, 128, 200
+    t = W.kda_tokens(rng, T, H, d, d, bf16=True)
+    t["g"][:, :, :8] = -30.0
+    t["g"][:, :, 8:16] = 0.0
+    cu = np.array([0, 70, T], np.int32)
+    S0 = rng.standard_normal((2, H, d, d), dtype=np.float32) * np.float32(0.05)
+    o, S = run_prefill(ctx, t["q"], t["k"], t["v"], t["g"], t["beta"], cu, S0=S0)
+    o_ref, S_ref = oracle.kda_recurrence(t["q"], t["k"], t["v"], t["g"], t["beta"], cu, state=S0,
+                                         nthreads=oracle.max_threads())
+    assert np.all(np.isfinite(o)) and np.all(np.isfinite(S))
+    assert W.rel_fro(o, o_ref) < TOL_BF16 and W.rel_fro(S, S_ref) < TOL_BF16
+
+
+def test_prefill_alpha_gate_bf16_tensor_core(ctx):
+    """Gates given as decay factors alpha (not log-decay) through the tensor-core path."""
+    rng = np.random.default_rng(23)
+    H, d = 4, 128
+    cu = np.array([0, 37, 200, 330], np.int32)
+    t = W.kda_tokens(rng, 330, H, d, d, bf16=True)
+    o, S = run_prefill(ctx, t["q"], t["k"], t["v"], np.exp(t["g"]), t["beta"], cu,
+                       gate_mode=k3cuda.GATE_ALPHA)
+    o_ref, S_ref = oracle.kda_recurrence(t["q"], t["k"], t["v"], t["g"], t["beta"], cu,
+                                         state=np.zeros((3, H, d, d), np.float32),
+                                         nthreads=oracle.max_threads())
+    assert W.rel_fro(o, o_ref) < TOL_BF16 and W.rel_fro(S, S_ref) < TOL_BF16
+
+
 def test_prefill_config2_shape_reduced_heads(ctx):
     """BASELINE config 2's sequence length (T=32768, 512 chunks in one scan) at 2 heads."""
     rng = np.random.default_rng(0)
