@@ -371,7 +371,7 @@ def bench_prefill(args, D: Dist, varlen: bool):
         "metric": f"KDA chunked prefill tokens/s ({name})", "value": T * args.steps / (ms_max / 1e3),
         "unit": "tokens/s", "n_gpus": D.world, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": ms_max / args.steps, "higher_is_better": True,
-        "scaling": "strong" if varlen else "weak", "vs_baseline": None, "dtype": "fp32",
+        "scaling": "strong" if varlen else "weak", "vs_baseline": None, "dtype": "bf16",
         "data": "synthetic (seeded numpy: BASELINE config distributions)",
         "config": {"workload": name, "tokens": T, "heads_total": H_total, "heads_per_gpu": Hl,
                    "d": d, "chunk": 64, "parallelism": f"head-shard x{R}" if varlen else "replica",

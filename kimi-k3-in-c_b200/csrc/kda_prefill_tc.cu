@@ -87,11 +87,7 @@ __device__ __forceinline__ int gsw(int t, int i) {
 }
 
 // 2^x on the special-function unit (the intra-chunk kernel keeps G in log2 units)
-__device__ __forceinline__ float ex2(float x) {
-    float y;
-    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
-    return y;
-}
+__device__ __forceinline__ float ex2(float x) { return ex2_approx(x); }
 constexpr float kLog2e = 1.4426950408889634f;
 
 __device__ __forceinline__ uint32_t pack_bf2(float a, float b) {

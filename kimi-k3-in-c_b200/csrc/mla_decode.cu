@@ -26,11 +26,14 @@
 // Keeping the query in TMEM leaves shared memory to the KV pipeline. P and the exchange
 // buffers are double-buffered so that the softmax of tile g overlaps the P.V product of
 // tile g-1.
-// Warp roles: warp 0 issues TMA loads; warp 1 allocates TMEM and issues S = Q.K^T; warp 6
-// issues O += P.V; warps 2-5 (one thread per head = TMEM lane) write the query into TMEM,
-// run the exchange, the softmax and the epilogue. The running max is only moved when it
-// grows by more than 2^8 (a lazy rescale: numerator and denominator use the same stale max,
-// so the result is exact), which keeps the O rescale in TMEM off the common path.
+// Warp roles: warp 0 issues TMA loads; warp 1 allocates TMEM and issues S = Q.K^T; warp 10
+// issues O += P.V; warps 2-9 (two threads per head = TMEM lane, 32 score columns each) write
+// the query into TMEM, run the exchange, the softmax and the epilogue; the two threads of a
+// head combine their row max and row sum through an mbarrier of the warp pair. The running
+// max is only moved when it grows by more than 2^8 (a lazy rescale: numerator and
+// denominator use the same stale max, so the result is exact), which keeps the O rescale in
+// TMEM off the common path. The score exchange of tile g overlaps the softmax of tile g-1:
+// tile g's partial is sent first, then tile g-1 is finished.
 //
 // Work: the (sequence, 64-token tile) list is cut into equal contiguous ranges, one per
 // cluster; a range that crosses sequences becomes several segments, each writing a partial
@@ -265,11 +268,16 @@ struct MlaBars {
     uint64_t q_full, q_empty;
     uint64_t s_full[2], s_empty[2];
     uint64_t p_full[2], pv_done[2];
-    uint64_t x_full[2], x_empty[2], x_read[2];
+    uint64_t x_full[2], x_empty[2];
+    uint64_t pair[4];           // per lane quarter: the two softmax warps of those rows
+    float pair_val[2][2][128];  // [phase parity][column half][head]
     uint32_t tmem_base;
 };
 
-__global__ void __launch_bounds__(224, 1) __cluster_dims__(2, 1, 1)
+constexpr int MLA_THREADS = 352;  // 11 warps: TMA, S issuer, 8 softmax, PV issuer
+constexpr int MLA_SOFT = 256;     // softmax threads: two per head (32 score columns each)
+
+__global__ void __launch_bounds__(MLA_THREADS, 1) __cluster_dims__(2, 1, 1)
 mla_attend_tc(const __grid_constant__ MlaMaps maps, const MlaSeg *__restrict__ segs,
               const int *__restrict__ cl_begin, const int *__restrict__ ctx_lens,
               const __nv_bfloat16 *__restrict__ qlat, float *__restrict__ part, int H, int cap,
@@ -289,17 +297,17 @@ mla_attend_tc(const __grid_constant__ MlaMaps maps, const MlaSeg *__restrict__ s
             mbar_init(&bars.kv_full[s], 1);
             mbar_init(&bars.kv_empty[s], 1);
         }
-        mbar_init(&bars.q_full, 128);
+        mbar_init(&bars.q_full, MLA_SOFT);
         mbar_init(&bars.q_empty, 1);
         for (int s = 0; s < 2; s++) {
             mbar_init(&bars.s_full[s], 1);
-            mbar_init(&bars.s_empty[s], 128);
-            mbar_init(&bars.p_full[s], 128);
+            mbar_init(&bars.s_empty[s], MLA_SOFT);
+            mbar_init(&bars.p_full[s], MLA_SOFT);
             mbar_init(&bars.pv_done[s], 1);
             mbar_init(&bars.x_full[s], 1);
-            mbar_init(&bars.x_empty[s], 1);
-            mbar_init(&bars.x_read[s], 128);
+            mbar_init(&bars.x_empty[s], 8);  // one arrive per softmax warp of the peer
         }
+        for (int q = 0; q < 4; q++) mbar_init(&bars.pair[q], 64);
         fence_barrier_init();
     }
     if (warp == 1) tmem_alloc(&bars.tmem_base, MLA_TM_COLS);
@@ -372,7 +380,7 @@ mla_attend_tc(const __grid_constant__ MlaMaps maps, const MlaSeg *__restrict__ s
                 }
             }
         }
-    } else if (warp == 6) {
+    } else if (warp == 10) {
         // ------------------------------------------ PV issuer: O (+)= P . V_half
         if (lane == 0) {
             constexpr uint32_t id_o = idesc_f16(128, 256, false, true);
@@ -398,15 +406,32 @@ mla_attend_tc(const __grid_constant__ MlaMaps maps, const MlaSeg *__restrict__ s
         }
     } else {
         // ------------------------------------- Q load, exchange, softmax, epilogue
-        const int row = 32 * (warp & 3) + lane;  // head == TMEM lane
-        const uint32_t lane_off = (uint32_t)(32 * (warp & 3)) << 16;
+        // Two warps per lane quarter: warp 2 + q and warp 6 + q own heads 32 q .. 32 q + 31
+        // (TMEM lanes) and score columns [32 hc, 32 hc + 32) of every tile; the row max and
+        // the row sum are combined through the pair's mbarrier.
+        const int q4 = warp & 3, hc = (warp - 2) >> 2, sw = warp - 2;
+        const int row = 32 * q4 + lane;  // head == TMEM lane
+        const int c0 = 32 * hc;          // first score column of this thread
+        const uint32_t lane_off = (uint32_t)(32 * q4) << 16;
         const uint32_t xpeer = map_peer(smem_u32(sm + MLA_OFF_X), peer);
-        float m_ref = -INFINITY, l = 0.f;
-        int g = 0, cur_slot = -1, nq = 0, prev_b = -1;
+        float m_ref = -INFINITY, l = 0.f;  // l: this thread's half of the row sum
+        int g = 0, cur_slot = -1, nq = 0, prev_b = -1, np = 0;
         bool ok = true;
-        auto epilogue = [&](int slot) {  // warp-collective: every lane loads its row
+        // the partner warp's value for this row (bounded wait on the pair's mbarrier); both
+        // warps of a pair call this at the same points, so their phases stay in step
+        auto pair_value = [&](float v, bool &good) -> float {
+            bars.pair_val[np & 1][hc][row] = v;
+            mbar_arrive(&bars.pair[q4]);
+            good = warp_wait(&bars.pair[q4], np & 1, err, 0x30a) && good;
+            const float o = bars.pair_val[np & 1][hc ^ 1][row];
+            np++;
+            return o;
+        };
+        auto epilogue = [&](int slot) -> bool {  // warp-collective: every lane loads its row
+            bool good = true;
+            const float lt = l + pair_value(l, good);
             float *dst = part + ((size_t)slot * H + row) * MLA_PART;
-            for (int c = 0; c < 256; c += 16) {
+            for (int c = 128 * hc; c < 128 * hc + 128; c += 16) {
                 float v[16];
                 tmem_ld16(tbase + lane_off + MLA_TM_O + c, v);
                 tmem_wait_ld();
@@ -417,10 +442,118 @@ mla_attend_tc(const __grid_constant__ MlaMaps maps, const MlaSeg *__restrict__ s
                         d4[i] = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
                 }
             }
-            if (rank == 0 && row < H) {
+            if (rank == 0 && hc == 0 && row < H) {
                 dst[MLA_DL] = m_ref;
-                dst[MLA_DL + 1] = l;
+                dst[MLA_DL + 1] = lt;
             }
+            return good;
+        };
+        // Tiles are handled with a one-tile skew: tile g's partial scores are sent to the
+        // peer, then tile g-1 -- whose peer partial arrived meanwhile -- is finished (softmax,
+        // P). The exchange latency overlaps the next tile's score read-out.
+        struct Pending {
+            int g, valid, slot;
+            bool newseg;
+        };
+        constexpr int HT = MLA_TILE / 2;  // score columns per thread
+        float sp[HT];  // this rank's partial scores of the pending tile (this thread's columns)
+        Pending pd{-1, 0, -1, false};
+        auto finish = [&](const Pending &q) -> bool {
+            const int xb = q.g & 1, pb = q.g & 1;
+            if (!warp_wait(&bars.x_full[xb], (q.g >> 1) & 1, err, 0x303, true)) return false;
+            const float4 *X4 = reinterpret_cast<const float4 *>(sm + MLA_OFF_X + xb * MLA_XBUF);
+            float m4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+#pragma unroll
+            for (int i = 0; i < HT / 4; i++) {
+                const float4 o = X4[(c0 / 4 + i) * MLA_HP + row];
+                const float ov[4] = {o.x, o.y, o.z, o.w};
+#pragma unroll
+                for (int j = 0; j < 4; j++) {
+                    const int c = 4 * i + j;
+                    const float tot = rank == 0 ? sp[c] + ov[j] : ov[j] + sp[c];
+                    sp[c] = c0 + c < q.valid ? tot * scale_log2e : -INFINITY;
+                    m4[j] = fmaxf(m4[j], sp[c]);
+                }
+            }
+            // this warp's part of exchange buffer xb is read (the values are consumed above):
+            // lane 0 tells the peer that it may be refilled
+            __syncwarp();
+            if (lane == 0) mbar_arrive_cluster_relaxed(&bars.x_empty[xb], peer);
+            bool good = true;
+            float mx = fmaxf(fmaxf(m4[0], m4[1]), fmaxf(m4[2], m4[3]));
+            mx = fmaxf(mx, pair_value(mx, good));
+            if (!good) return false;
+            if (q.newseg) {
+                // a new segment: the previous segment's last P.V must be done before its O is
+                // read out and the next P.V overwrites it
+                if (q.g > 0) {
+                    if (!warp_wait(&bars.pv_done[(q.g - 1) & 1], ((q.g - 1) >> 1) & 1, err, 0x304))
+                        return false;
+                    tc_fence_after();
+                }
+                if (cur_slot >= 0 && !epilogue(cur_slot)) return false;
+                cur_slot = q.slot;
+                m_ref = mx;
+                l = 0.f;
+            } else {
+                const bool grow = mx > m_ref + MLA_RESCALE_LOG2;
+                if (__any_sync(0xffffffffu, grow)) {
+                    // O is rescaled in place: the previous tile's P.V must be done
+                    if (!warp_wait(&bars.pv_done[(q.g - 1) & 1], ((q.g - 1) >> 1) & 1, err, 0x306))
+                        return false;
+                    tc_fence_after();
+                    const float f = grow ? exp2f(m_ref - mx) : 1.f;
+                    for (int c = 128 * hc; c < 128 * hc + 128; c += 16) {
+                        float v[16];
+                        tmem_ld16(tbase + lane_off + MLA_TM_O + c, v);
+                        tmem_wait_ld();
+#pragma unroll
+                        for (int i = 0; i < 16; i++) v[i] *= f;
+                        tmem_st16(tbase + lane_off + MLA_TM_O + c, v);
+                    }
+                    tmem_wait_st();
+                    if (grow) {
+                        l *= f;
+                        m_ref = mx;
+                    }
+                }
+            }
+            // P buffer pb is free once the P.V of tile g-2 is done
+            uint8_t *P = sm + MLA_OFF_P + pb * MLA_PBUF;
+            if (q.g >= 2 && !warp_wait(&bars.pv_done[pb], ((q.g >> 1) - 1) & 1, err, 0x307))
+                return false;
+            // P row (bf16, 128-byte swizzle: 16-byte chunk c of row r sits at c ^ (r & 7))
+            float rs[4] = {0.f, 0.f, 0.f, 0.f};
+            uint32_t pk[HT / 2];
+#pragma unroll
+            for (int c = 0; c < HT; c += 2) {
+                const float p0 = ex2_approx(sp[c] - m_ref), p1 = ex2_approx(sp[c + 1] - m_ref);
+                rs[(c >> 1) & 3] += p0 + p1;
+                const __nv_bfloat162 h2 = __floats2bfloat162_rn(p0, p1);
+                pk[c / 2] = *reinterpret_cast<const uint32_t *>(&h2);
+            }
+            l += (rs[0] + rs[1]) + (rs[2] + rs[3]);
+#pragma unroll
+            for (int c = 0; c < HT / 8; c++) {
+                const int ch = c0 / 8 + c;  // 16-byte chunk of the 128-byte P row
+                *reinterpret_cast<uint4 *>(P + row * 128 + ((ch ^ (row & 7)) * 16)) =
+                    make_uint4(pk[4 * c], pk[4 * c + 1], pk[4 * c + 2], pk[4 * c + 3]);
+            }
+            if (q.valid < MLA_TILE) {
+                // rows past the context may hold anything (even NaN): zero this rank's value
+                // rows there so that P = 0 times them stays 0
+                uint8_t *kv = sm + MLA_OFF_KV + (q.g % MLA_NST) * MLA_NBLK * MLA_KVBLK;
+                const int nz = (MLA_TILE - q.valid) * 8;  // 16-byte chunks per block
+                for (int e = 32 * sw + lane; e < 4 * nz; e += MLA_SOFT) {
+                    const int kb = e / nz, r = q.valid + (e % nz) / 8, c = e % 8;
+                    *reinterpret_cast<uint4 *>(kv + kb * MLA_KVBLK + r * 128 + c * 16) =
+                        make_uint4(0, 0, 0, 0);
+                }
+            }
+            fence_async_shared();
+            tc_fence_before();
+            mbar_arrive(&bars.p_full[pb]);
+            return true;
         };
         for (int si = sbeg; si < send && ok; si++) {
             const MlaSeg sg = segs[si];
@@ -434,19 +567,16 @@ mla_attend_tc(const __grid_constant__ MlaMaps maps, const MlaSeg *__restrict__ s
                     reinterpret_cast<const uint4 *>(qlat + ((size_t)sg.b * MLA_HP + row) * MLA_QW);
                 for (int kb = 0; kb < nblk; kb++) {
                     const int d0 = kb < 4 ? dim0 + kb * 64 : MLA_DL;  // first dim of block
+                    float v[16];  // this warp's 32 dims of the block (16 columns)
 #pragma unroll
-                    for (int half = 0; half < 2; half++) {
-                        float v[16];
-#pragma unroll
-                        for (int i = 0; i < 4; i++) {
-                            const uint4 w = qrow[(d0 + half * 32) / 8 + i];
-                            v[4 * i] = __uint_as_float(w.x);
-                            v[4 * i + 1] = __uint_as_float(w.y);
-                            v[4 * i + 2] = __uint_as_float(w.z);
-                            v[4 * i + 3] = __uint_as_float(w.w);
-                        }
-                        tmem_st16(tbase + lane_off + MLA_TM_Q + kb * 32 + half * 16, v);
+                    for (int i = 0; i < 4; i++) {
+                        const uint4 w = qrow[(d0 + hc * 32) / 8 + i];
+                        v[4 * i] = __uint_as_float(w.x);
+                        v[4 * i + 1] = __uint_as_float(w.y);
+                        v[4 * i + 2] = __uint_as_float(w.z);
+                        v[4 * i + 3] = __uint_as_float(w.w);
                     }
+                    tmem_st16(tbase + lane_off + MLA_TM_Q + kb * 32 + hc * 16, v);
                 }
                 tmem_wait_st();
                 tc_fence_before();
@@ -455,22 +585,16 @@ mla_attend_tc(const __grid_constant__ MlaMaps maps, const MlaSeg *__restrict__ s
                 prev_b = sg.b;
             }
             for (int t = sg.t0; t < sg.t1; t++, g++) {
-                const int sb = 0, xb = g & 1, pb = g & 1;
-                if (row == 0) mbar_expect_tx(&bars.x_full[xb], MLA_XBUF);
-                float s[MLA_TILE];
+                const int xb = g & 1;
+                if (sw == 0 && lane == 0) mbar_expect_tx(&bars.x_full[xb], MLA_XBUF);
+                float s[HT];
                 if (!(ok = warp_wait(&bars.s_full[0], g & 1, err, 0x301))) break;
                 tc_fence_after();
-#pragma unroll
-                for (int c = 0; c < MLA_TILE; c += 16) {
-                    float v[16];
-                    tmem_ld16(tbase + lane_off + MLA_TM_S + sb * MLA_TILE + c, v);
-                    tmem_wait_ld();
-#pragma unroll
-                    for (int i = 0; i < 16; i++) s[c + i] = v[i];
-                }
+                tmem_ld32(tbase + lane_off + MLA_TM_S + c0, s);
+                tmem_wait_ld();
                 tc_fence_before();
-                mbar_arrive(&bars.s_empty[sb]);
-                // send this rank's partial scores into the peer's exchange buffer xb
+                mbar_arrive(&bars.s_empty[0]);
+                // send this thread's partial scores into the peer's exchange buffer xb
                 // (X4[i * 128 + row] = float4 i of `row`); the transfer completes on the
                 // peer's x_full[xb]
                 if (g >= 2 &&
@@ -478,102 +602,16 @@ mla_attend_tc(const __grid_constant__ MlaMaps maps, const MlaSeg *__restrict__ s
                     break;
                 const uint32_t rbar = map_peer(smem_u32(&bars.x_full[xb]), peer);
 #pragma unroll
-                for (int i = 0; i < MLA_TILE / 4; i++)
-                    st_async_v4(xpeer + (uint32_t)(xb * MLA_XBUF + (i * MLA_HP + row) * 16),
+                for (int i = 0; i < HT / 4; i++)
+                    st_async_v4(xpeer + (uint32_t)(xb * MLA_XBUF + ((c0 / 4 + i) * MLA_HP + row) * 16),
                                 s[4 * i], s[4 * i + 1], s[4 * i + 2], s[4 * i + 3], rbar);
-                if (!(ok = warp_wait(&bars.x_full[xb], (g >> 1) & 1, err, 0x303, true))) break;
-                const float4 *X4 = reinterpret_cast<const float4 *>(sm + MLA_OFF_X + xb * MLA_XBUF);
-                const int valid = clen - t * MLA_TILE;
-                float mx = -INFINITY;
+                if (pd.g >= 0 && !(ok = finish(pd))) break;
 #pragma unroll
-                for (int i = 0; i < MLA_TILE / 4; i++) {
-                    const float4 o = X4[i * MLA_HP + row];
-                    const float ov[4] = {o.x, o.y, o.z, o.w};
-#pragma unroll
-                    for (int j = 0; j < 4; j++) {
-                        const int c = 4 * i + j;
-                        const float tot = rank == 0 ? s[c] + ov[j] : ov[j] + s[c];
-                        s[c] = c < valid ? tot * scale_log2e : -INFINITY;
-                        mx = fmaxf(mx, s[c]);
-                    }
-                }
-                // once every row has read exchange buffer xb, row 0 tells the peer it may refill it
-                mbar_arrive(&bars.x_read[xb]);
-                if (row == 0 && mbar_wait(&bars.x_read[xb], (g >> 1) & 1, err, 0x309))
-                    mbar_arrive_cluster_relaxed(&bars.x_empty[xb], peer);
-                if (t == sg.t0) {
-                    // a new segment: the previous segment's last P.V must be done before its
-                    // O is read out and the next P.V overwrites it
-                    if (g > 0) {
-                        if (!(ok = warp_wait(&bars.pv_done[(g - 1) & 1], ((g - 1) >> 1) & 1, err,
-                                             0x304)))
-                            break;
-                        tc_fence_after();
-                    }
-                    if (cur_slot >= 0) epilogue(cur_slot);
-                    cur_slot = sg.slot;
-                    m_ref = mx;
-                    l = 0.f;
-                } else {
-                    const bool grow = mx > m_ref + MLA_RESCALE_LOG2;
-                    if (__any_sync(0xffffffffu, grow)) {
-                        // O is rescaled in place: the previous tile's P.V must be done
-                        if (!(ok = warp_wait(&bars.pv_done[(g - 1) & 1], ((g - 1) >> 1) & 1, err,
-                                             0x306)))
-                            break;
-                        tc_fence_after();
-                        const float f = grow ? exp2f(m_ref - mx) : 1.f;
-                        for (int c = 0; c < 256; c += 16) {
-                            float v[16];
-                            tmem_ld16(tbase + lane_off + MLA_TM_O + c, v);
-                            tmem_wait_ld();
-#pragma unroll
-                            for (int i = 0; i < 16; i++) v[i] *= f;
-                            tmem_st16(tbase + lane_off + MLA_TM_O + c, v);
-                        }
-                        tmem_wait_st();
-                        if (grow) {
-                            l *= f;
-                            m_ref = mx;
-                        }
-                    }
-                }
-                // P buffer pb is free once the P.V of tile g-2 is done
-                uint8_t *P = sm + MLA_OFF_P + pb * MLA_PBUF;
-                if (g >= 2 &&
-                    !(ok = warp_wait(&bars.pv_done[pb], ((g >> 1) - 1) & 1, err, 0x307)))
-                    break;
-                // P row (bf16, 128-byte swizzle: 16-byte chunk c of row r sits at c ^ (r & 7))
-                float rs = 0.f;
-                uint32_t pk[MLA_TILE / 2];
-#pragma unroll
-                for (int c = 0; c < MLA_TILE; c += 2) {
-                    const float p0 = exp2f(s[c] - m_ref), p1 = exp2f(s[c + 1] - m_ref);
-                    rs += p0 + p1;
-                    const __nv_bfloat162 h2 = __floats2bfloat162_rn(p0, p1);
-                    pk[c / 2] = *reinterpret_cast<const uint32_t *>(&h2);
-                }
-                l += rs;
-#pragma unroll
-                for (int c = 0; c < MLA_TILE / 8; c++)
-                    *reinterpret_cast<uint4 *>(P + row * 128 + ((c ^ (row & 7)) * 16)) =
-                        make_uint4(pk[4 * c], pk[4 * c + 1], pk[4 * c + 2], pk[4 * c + 3]);
-                if (valid < MLA_TILE) {
-                    // rows past the context may hold anything (even NaN): zero this rank's
-                    // value rows there so that P = 0 times them stays 0
-                    uint8_t *kv = sm + MLA_OFF_KV + (g % MLA_NST) * MLA_NBLK * MLA_KVBLK;
-                    const int nz = (MLA_TILE - valid) * 8;  // 16-byte chunks per block
-                    for (int e = row; e < 4 * nz; e += 128) {
-                        const int kb = e / nz, r = valid + (e % nz) / 8, c = e % 8;
-                        *reinterpret_cast<uint4 *>(kv + kb * MLA_KVBLK + r * 128 + c * 16) =
-                            make_uint4(0, 0, 0, 0);
-                    }
-                }
-                fence_async_shared();
-                tc_fence_before();
-                mbar_arrive(&bars.p_full[pb]);
+                for (int c = 0; c < HT; c++) sp[c] = s[c];
+                pd = Pending{g, clen - t * MLA_TILE, sg.slot, t == sg.t0};
             }
         }
+        if (ok && pd.g >= 0) ok = finish(pd);
         if (ok && g > 0 &&
             warp_wait(&bars.pv_done[(g - 1) & 1], ((g - 1) >> 1) & 1, err, 0x305)) {
             tc_fence_after();
@@ -783,7 +821,7 @@ extern "C" int k3cuda_mla_decode(k3cuda_ctx *ctx, void *out, int out_dtype, cons
     K3_CUDA_TRY(cudaFuncSetAttribute(mla_attend_tc, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                      MLA_SMEM));
     const float scale_log2e = scale * 1.4426950408889634f;
-    mla_attend_tc<<<2 * p.ncl, 224, MLA_SMEM, ctx->stream>>>(maps, d_segs, d_cl, d_lens, qlat,
+    mla_attend_tc<<<2 * p.ncl, MLA_THREADS, MLA_SMEM, ctx->stream>>>(maps, d_segs, d_cl, d_lens, qlat,
                                                            part, H, cap, scale_log2e,
                                                            ctx->err_word);
     rc = after_launch(ctx, "mla_attend_tc");
