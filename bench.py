@@ -316,9 +316,10 @@ def bench_prefill(args, D: Dist, varlen: bool):
         H_total, d = 32, 128
     cu = c["cu_seqlens"]
     T = int(cu[-1])
+    import sharding
     R = D.world if varlen else 1
-    Hl = H_total // R
-    hs = slice(D.rank * Hl, (D.rank + 1) * Hl) if varlen else slice(0, H_total)
+    hs = sharding.head_shard(H_total, R, D.rank if varlen else 0)
+    Hl = hs.stop - hs.start
     bf = W.f32_to_bf16
     q, k, v = (np.ascontiguousarray(c[x][:, hs]) for x in ("q", "k", "v"))
     g, beta = np.ascontiguousarray(c["g"][:, hs]), np.ascontiguousarray(c["beta"][:, hs])
