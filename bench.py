@@ -312,7 +312,7 @@ def bench_prefill(args, D: Dist, varlen: bool):
         c = W.kda_config3()
         H_total, d = 64, 128
     else:
-        c = W.kda_config2()
+        c = W.kda_config2(T=args.tokens) if args.tokens else W.kda_config2()
         H_total, d = 32, 128
     cu = c["cu_seqlens"]
     T = int(cu[-1])
@@ -368,6 +368,8 @@ def bench_prefill(args, D: Dist, varlen: bool):
     alg = prefill_bytes(T, Hl, d)
     per = ms_max / 1e3 / args.steps
     name = "kda_prefill_config3" if varlen else "kda_prefill_config2"
+    if not varlen and args.tokens:
+        name = f"kda_prefill_T{T}_reduced"
     line = {
         "metric": f"KDA chunked prefill tokens/s ({name})", "value": T * args.steps / (ms_max / 1e3),
         "unit": "tokens/s", "n_gpus": D.world, "steps": args.steps, "warmup": args.warmup,
@@ -378,7 +380,9 @@ def bench_prefill(args, D: Dist, varlen: bool):
                    "d": d, "chunk": 64, "parallelism": f"head-shard x{R}" if varlen else "replica",
                    "allgather": bool(gather), "l2": "inputs larger than L2"},
         "roofline": {"bound": "hbm", "achieved": alg / per / 1e9, "peak": hbm, "unit": "GB/s",
-                     "frac": alg / per / 1e9 / hbm, "peak_source": src, "traffic": None,
+                     "frac": alg / per / 1e9 / hbm, "peak_source": src,
+                     "traffic": (profile_traffic("kda_prefill_config2.md")
+                                 if not varlen and not args.tokens else None),
                      "algorithmic_bytes_per_launch": alg},
         "gpu_launches": int(ctx.launches() - l0), "clocks": clocks,
     }
@@ -434,7 +438,7 @@ def bench_mla(args, D: Dist):
                    "heads": H, "parallelism": f"batch-shard x{D.world}",
                    "l2": "inputs larger than L2 (604 MB latent+rope cache)"},
         "roofline": {"bound": "hbm", "achieved": alg / per / 1e9, "peak": hbm, "unit": "GB/s",
-                     "frac": alg / per / 1e9 / hbm, "peak_source": src, "traffic": None,
+                     "frac": alg / per / 1e9 / hbm, "peak_source": src, "traffic": profile_traffic("mla_attend_config4.md"),
                      "algorithmic_bytes_per_launch": alg,
                      "tensor_tflops": mla_flops(B, ctxlen, H) / per / 1e12},
         "gpu_launches": int(ctx.launches() - l0), "clocks": clocks,
@@ -497,6 +501,9 @@ def main():
     ap.add_argument("--workload", default="decode", choices=["decode", "prefill", "varlen", "mla"])
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--tokens", type=int, default=None,
+                    help="prefill workload only: sequence length in place of config 2's 32768 "
+                         "(a small case for kernel profiling; not a headline number)")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     D = Dist()
