@@ -333,17 +333,19 @@ def bench_prefill(args, D: Dist, varlen: bool):
     qs = 1.0 / np.sqrt(np.float32(d))
     gather = varlen and R > 1
     if gather:
+        # the prefill writes every rank's full [T][H][d] output directly (peer memory over
+        # NVLink): no separate all-gather or interleave pass
         uid = D.bcast_bytes(k3cuda.comm_unique_id() if D.rank == 0 else None)
         ctx.comm_init(R, D.rank, uid)
-        nag = ctx.allgather_heads_workspace(R, T, Hl, d)
-        agws = ctx.empty((nag,), np.uint8)
         dfull = ctx.empty((T, H_total, d), np.uint16)
+        ctx.comm_register_full(dfull)
 
     def step():
         dS.zero()
-        ctx.kda_prefill(dS, do, dq, dk, dv, dg, db, cu, Hl, d, d, qs, ws, nws)
         if gather:
-            ctx.allgather_heads(dfull, do, T, Hl, d, agws, nag)
+            ctx.kda_prefill_gathered(dS, dq, dk, dv, dg, db, cu, Hl, d, d, qs, ws, nws)
+        else:
+            ctx.kda_prefill(dS, do, dq, dk, dv, dg, db, cu, Hl, d, d, qs, ws, nws)
 
     for _ in range(args.warmup):
         step()
@@ -378,7 +380,8 @@ def bench_prefill(args, D: Dist, varlen: bool):
         "data": "synthetic (seeded numpy: BASELINE config distributions)",
         "config": {"workload": name, "tokens": T, "heads_total": H_total, "heads_per_gpu": Hl,
                    "d": d, "chunk": 64, "parallelism": f"head-shard x{R}" if varlen else "replica",
-                   "allgather": bool(gather), "l2": "inputs larger than L2"},
+                   "allgather": "fused into the prefill (peer stores)" if gather else False,
+                   "l2": "inputs larger than L2"},
         "roofline": {"bound": "hbm", "achieved": alg / per / 1e9, "peak": hbm, "unit": "GB/s",
                      "frac": alg / per / 1e9 / hbm, "peak_source": src,
                      "traffic": (profile_traffic("kda_prefill_config2.md")

@@ -181,6 +181,29 @@ int k3cuda_allgather_heads(k3cuda_ctx *ctx, void *full, const void *local, int T
                            int H_local, int dv, int dtype, void *workspace,
                            size_t workspace_bytes);
 
+/* The prefill and the exchange in one call, without the all-gather's staging copy and
+ * interleave pass: the head-sharded KDA prefill writes this rank's heads straight into
+ * its own full [T][nranks*H_local][dv] bf16 buffer at their final place, and one
+ * coalesced pass stores that head span into every peer's full buffer (peer memory over
+ * NVLink, mapped by k3cuda_comm_register_full). It replaces k3cuda_kda_prefill +
+ * k3cuda_allgather_heads at the head-sharded call site of k3_kda_layer
+ * (src/core/k3_ops.c:908-949: recurrence, then the o_proj input).
+ *
+ * k3cuda_comm_register_full  collective (every rank, after k3cuda_comm_init): maps every
+ *     rank's `full` (device memory from k3cuda_malloc/cudaMalloc, `bytes` long) into every
+ *     process (CUDA IPC). Once per buffer; the mapping lives until k3cuda_shutdown.
+ * k3cuda_kda_prefill_gathered  collective: arguments as k3cuda_kda_prefill with H_local
+ *     heads per rank and no local output; bf16, dk == dv == 128. On return (in stream
+ *     order) every rank's full buffer holds all heads: the call orders itself against the
+ *     other ranks with two one-int all-reduces, before its writes and after them. */
+#define K3CUDA_MAX_RANKS 8
+int k3cuda_comm_register_full(k3cuda_ctx *ctx, void *full, size_t bytes);
+int k3cuda_kda_prefill_gathered(k3cuda_ctx *ctx, float *state, const void *q, const void *k,
+                                const void *v, const float *gate, const float *beta,
+                                const int *cu_seqlens, int n_seq, int H_local, int dk,
+                                int dv, float q_scale, int gate_mode, int chunk,
+                                void *workspace, size_t workspace_bytes);
+
 #ifdef __cplusplus
 }
 #endif

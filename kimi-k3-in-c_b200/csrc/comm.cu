@@ -8,9 +8,12 @@
 //
 // NCCL is opened with dlopen at first use (libnccl.so.2, whichever copy the process
 // already has or the system one), so the library loads and runs single-GPU without it.
+#include <cuda.h>
 #include <dlfcn.h>
 #include <nccl.h>
 #include <string.h>
+
+#include <vector>
 
 #include "internal.cuh"
 
@@ -23,6 +26,8 @@ struct NcclApi {
     ncclResult_t (*CommDestroy)(ncclComm_t) = nullptr;
     ncclResult_t (*CommAbort)(ncclComm_t) = nullptr;
     ncclResult_t (*CommGetAsyncError)(ncclComm_t, ncclResult_t *) = nullptr;
+    ncclResult_t (*AllReduce)(const void *, void *, size_t, ncclDataType_t, ncclRedOp_t,
+                              ncclComm_t, cudaStream_t) = nullptr;
     ncclResult_t (*AllGather)(const void *, void *, size_t, ncclDataType_t, ncclComm_t,
                               cudaStream_t) = nullptr;
     const char *(*GetErrorString)(ncclResult_t) = nullptr;
@@ -44,6 +49,7 @@ static int nccl_load() {
     K3_SYM(CommAbort, "ncclCommAbort");
     K3_SYM(CommGetAsyncError, "ncclCommGetAsyncError");
     K3_SYM(AllGather, "ncclAllGather");
+    K3_SYM(AllReduce, "ncclAllReduce");
     K3_SYM(GetErrorString, "ncclGetErrorString");
 #undef K3_SYM
     g_nccl.handle = h;
@@ -64,6 +70,55 @@ __global__ void head_interleave(uint4 *__restrict__ full, const uint4 *__restric
     }
 }
 
+// Copy rows [t][head0 .. head0 + H_local) of this rank's full buffer into the same place of
+// every peer's full buffer (peer memory over NVLink). Consecutive threads move consecutive
+// 16-byte pieces of a token's contiguous head span, so each warp store is 512 B contiguous.
+__global__ void push_heads(const uint4 *__restrict__ own, uint4 *const *__restrict__ peers,
+                           int npeers, int T, long long row16, long long span16,
+                           long long off16) {
+    const long long total = (long long)T * span16;
+    for (long long e = blockIdx.x * (long long)blockDim.x + threadIdx.x; e < total;
+         e += (long long)gridDim.x * blockDim.x) {
+        const long long t = e / span16, x = e % span16;
+        const long long at = t * row16 + off16 + x;
+        const uint4 v = own[at];
+        for (int r = 0; r < npeers; r++) peers[r][at] = v;
+    }
+}
+
+int comm_push_heads(k3cuda_ctx *ctx, int T, int head0, int H_local, int H_total, int dv) {
+    if (ctx->nranks <= 1 || T == 0) return K3CUDA_OK;
+    uint4 *peers[K3CUDA_MAX_RANKS];
+    int np = 0;
+    for (int r = 0; r < ctx->nranks; r++)
+        if (r != ctx->rank) peers[np++] = (uint4 *)ctx->full_out[r];
+    if (!ctx->peer_table)
+        K3_CUDA_TRY(cudaMalloc((void **)&ctx->peer_table, sizeof(void *) * K3CUDA_MAX_RANKS));
+    K3_CUDA_TRY(cudaMemcpyAsync(ctx->peer_table, peers, sizeof(void *) * np,
+                                cudaMemcpyHostToDevice, ctx->stream));
+    const long long row16 = (long long)H_total * dv * 2 / 16;
+    const long long span16 = (long long)H_local * dv * 2 / 16;
+    const long long off16 = (long long)head0 * dv * 2 / 16;
+    const long long total = (long long)T * span16;
+    const int blocks = (int)((total + 255) / 256 < ctx->sm_count * 8 ? (total + 255) / 256
+                                                                     : ctx->sm_count * 8);
+    push_heads<<<blocks, 256, 0, ctx->stream>>>((const uint4 *)ctx->full_out[ctx->rank],
+                                                (uint4 *const *)ctx->peer_table, np, T, row16,
+                                                span16, off16);
+    return after_launch(ctx, "push_heads");
+}
+
+// Stream-ordered fence across the ranks: a one-int all-reduce completes on every rank only
+// after every rank has reached it (so all work enqueued before it, on every rank, is done).
+int comm_fence(k3cuda_ctx *ctx) {
+    if (ctx->nranks <= 1) return K3CUDA_OK;
+    ncclResult_t r = g_nccl.AllReduce(ctx->sync_word, ctx->sync_word, 1, ncclInt32, ncclSum,
+                                      (ncclComm_t)ctx->nccl_comm, ctx->stream);
+    if (r != ncclSuccess)
+        return set_error(K3CUDA_ERR_NCCL, "ncclAllReduce: %s", g_nccl.GetErrorString(r));
+    return K3CUDA_OK;
+}
+
 }  // namespace k3
 
 using namespace k3;
@@ -71,7 +126,17 @@ using namespace k3;
 extern "C" {
 
 int k3cuda_comm_destroy_internal(k3cuda_ctx *ctx) {
-    if (ctx && ctx->nccl_comm && g_nccl.handle) {
+    if (!ctx) return K3CUDA_OK;
+    for (int r = 0; r < K3CUDA_MAX_RANKS; r++) {
+        if (ctx->full_out[r] && r != ctx->rank) cudaIpcCloseMemHandle(ctx->full_base[r]);
+        ctx->full_out[r] = nullptr;
+        ctx->full_base[r] = nullptr;
+    }
+    if (ctx->sync_word) cudaFree(ctx->sync_word);
+    ctx->sync_word = nullptr;
+    if (ctx->peer_table) cudaFree(ctx->peer_table);
+    ctx->peer_table = nullptr;
+    if (ctx->nccl_comm && g_nccl.handle) {
         g_nccl.CommDestroy((ncclComm_t)ctx->nccl_comm);
         ctx->nccl_comm = nullptr;
     }
@@ -108,6 +173,87 @@ int k3cuda_comm_init(k3cuda_ctx *ctx, int nranks, int rank,
     ctx->nccl_comm = comm;
     ctx->nranks = nranks;
     ctx->rank = rank;
+    return K3CUDA_OK;
+}
+
+int k3cuda_comm_register_full(k3cuda_ctx *ctx, void *full, size_t bytes) {
+    int rc = enter(ctx);
+    if (rc) return rc;
+    if (!ctx->nccl_comm) return set_error(K3CUDA_ERR_STATE, "k3cuda_comm_init not called");
+    K3_ARG_CHECK(full && bytes && aligned(full, 16), "register_full: bad buffer");
+    K3_ARG_CHECK(ctx->nranks <= K3CUDA_MAX_RANKS, "register_full: at most %d ranks",
+                 K3CUDA_MAX_RANKS);
+    if (ctx->full_out[ctx->rank])
+        return set_error(K3CUDA_ERR_STATE, "register_full: a buffer is already registered");
+    // this rank's record: IPC handle of the allocation holding `full`, offset of `full` in it
+    struct Rec {
+        cudaIpcMemHandle_t h;
+        unsigned long long off, bytes;
+    };
+    static_assert(sizeof(Rec) % 16 == 0, "record size");
+    Rec mine{};
+    if (ctx->nranks > 1) {
+        void *base = nullptr;
+        size_t range = 0;
+        CUdeviceptr b = 0;
+        // allocation base through the driver entry point (no libcuda link)
+        static CUresult (*get_range)(CUdeviceptr *, size_t *, CUdeviceptr) = nullptr;
+        if (!get_range) {
+            void *fp = nullptr;
+            cudaDriverEntryPointQueryResult qr;
+            if (cudaGetDriverEntryPoint("cuMemGetAddressRange", &fp, cudaEnableDefault, &qr) !=
+                    cudaSuccess ||
+                qr != cudaDriverEntryPointSuccess)
+                return set_error(K3CUDA_ERR_CUDA, "cuMemGetAddressRange unavailable");
+            get_range = (CUresult(*)(CUdeviceptr *, size_t *, CUdeviceptr))fp;
+        }
+        if (get_range(&b, &range, (CUdeviceptr)full) != CUDA_SUCCESS)
+            return set_error(K3CUDA_ERR_ARG, "register_full: not device memory");
+        base = (void *)b;
+        K3_CUDA_TRY(cudaIpcGetMemHandle(&mine.h, base));
+        mine.off = (unsigned long long)((char *)full - (char *)base);
+    }
+    mine.bytes = bytes;
+    std::vector<Rec> all(ctx->nranks);
+    if (ctx->nranks > 1) {
+        Rec *d = nullptr;
+        K3_CUDA_TRY(cudaMalloc((void **)&d, sizeof(Rec) * (ctx->nranks + 1)));
+        K3_CUDA_TRY(cudaMemcpyAsync(d + ctx->nranks, &mine, sizeof mine, cudaMemcpyHostToDevice,
+                                    ctx->stream));
+        ncclResult_t r = g_nccl.AllGather(d + ctx->nranks, d, sizeof(Rec), ncclUint8,
+                                          (ncclComm_t)ctx->nccl_comm, ctx->stream);
+        if (r != ncclSuccess) {
+            cudaFree(d);
+            return set_error(K3CUDA_ERR_NCCL, "register_full: ncclAllGather: %s",
+                             g_nccl.GetErrorString(r));
+        }
+        K3_CUDA_TRY(cudaMemcpyAsync(all.data(), d, sizeof(Rec) * ctx->nranks,
+                                    cudaMemcpyDeviceToHost, ctx->stream));
+        K3_CUDA_TRY(cudaStreamSynchronize(ctx->stream));
+        cudaFree(d);
+    } else {
+        all[0] = mine;
+    }
+    size_t common = bytes;
+    for (int r = 0; r < ctx->nranks; r++) common = all[r].bytes < common ? all[r].bytes : common;
+    for (int r = 0; r < ctx->nranks; r++) {
+        if (r == ctx->rank) {
+            ctx->full_out[r] = full;
+            continue;
+        }
+        void *p = nullptr;
+        cudaError_t e = cudaIpcOpenMemHandle(&p, all[r].h, cudaIpcMemLazyEnablePeerAccess);
+        if (e != cudaSuccess) {
+            for (int q = 0; q < r; q++)
+                if (q != ctx->rank && ctx->full_base[q]) cudaIpcCloseMemHandle(ctx->full_base[q]);
+            return set_error(K3CUDA_ERR_CUDA, "register_full: opening rank %d's buffer: %s", r,
+                             cudaGetErrorString(e));
+        }
+        ctx->full_base[r] = p;
+        ctx->full_out[r] = (char *)p + all[r].off;
+    }
+    ctx->full_bytes = common;
+    if (!ctx->sync_word) K3_CUDA_TRY(cudaMalloc((void **)&ctx->sync_word, sizeof(int)));
     return K3CUDA_OK;
 }
 

@@ -20,7 +20,24 @@ struct k3cuda_ctx {
     // NCCL (opaque; see comm.cu)
     void *nccl_comm;
     int nranks, rank;
+    // every rank's registered [T][H][dv] output, mapped into this process (comm.cu)
+    void *full_out[K3CUDA_MAX_RANKS];
+    void *full_base[K3CUDA_MAX_RANKS];   // peer allocations opened by IPC (to close)
+    size_t full_bytes;
+    int *sync_word;             // device int for the cross-rank ordering all-reduce
+    void *peer_table;           // device copy of the peers' full-buffer addresses
 };
+
+namespace k3 {
+// Output of a head-sharded prefill written straight into every rank's full
+// [T][H_total][dv] bf16 buffer (rank-local heads at head0..head0+H_local-1).
+struct GatherOut {
+    __nv_bfloat16 *ptr[K3CUDA_MAX_RANKS];
+    int n;        // ranks (0: write the local output instead)
+    int head0;    // first head of this rank in the full layout
+    int H_total;
+};
+}  // namespace k3
 
 namespace k3 {
 

@@ -36,7 +36,7 @@ namespace k3 {
 int run_prefill_tc(k3cuda_ctx *ctx, float *state, void *o, const void *q, const void *k,
                    const void *v, const float *gate, const float *beta, int total_tokens,
                    int n_seq, int H, float q_scale, int gate_is_log, long long nc,
-                   const void *d_table, const int *d_c0, void *blocks);
+                   const void *d_table, const int *d_c0, void *blocks, const GatherOut *go);
 size_t prefill_tc_block_bytes();
 
 constexpr int KC = 64;        // chunk length
@@ -299,7 +299,7 @@ template <typename IO, int DK>
 static int run_prefill(k3cuda_ctx *ctx, float *state, void *o, const void *q, const void *k,
                        const void *v, const float *gate, const float *beta, const int *cu,
                        int n_seq, int H, float q_scale, int gate_is_log, long long nc,
-                       void *workspace) {
+                       void *workspace, const GatherOut *go = nullptr) {
     using L = PrefillLayout<DK>;
     std::vector<ChunkDesc> table((size_t)nc);
     std::vector<int> c0((size_t)n_seq + 1);
@@ -325,7 +325,7 @@ static int run_prefill(k3cuda_ctx *ctx, float *state, void *o, const void *q, co
         // bf16 operands on the tensor cores (every operand bf16, accumulation fp32)
         if (nc == 0) return K3CUDA_OK;
         return run_prefill_tc(ctx, state, o, q, k, v, gate, beta, cu[n_seq], n_seq, H, q_scale,
-                              gate_is_log, nc, d_table, d_c0, blocks);
+                              gate_is_log, nc, d_table, d_c0, blocks, go);
     }
     if (nc > 0) {
         const size_t smem1 =
@@ -405,6 +405,67 @@ extern "C" int k3cuda_kda_prefill(k3cuda_ctx *ctx, float *state, void *o, const 
                                       q_scale, gl, nc, workspace);
     return run_prefill<float, 128>(ctx, state, o, q, k, v, gate, beta, cu_seqlens, n_seq, H,
                                    q_scale, gl, nc, workspace);
+}
+
+// ------------------------------------------------- head-sharded prefill, gathered output
+namespace k3 {
+int comm_fence(k3cuda_ctx *ctx);  // comm.cu: a one-int all-reduce ordering all ranks
+// comm.cu: copy this rank's heads of its full buffer into every peer's full buffer
+int comm_push_heads(k3cuda_ctx *ctx, int T, int head0, int H_local, int H_total, int dv);
+}
+
+extern "C" int k3cuda_kda_prefill_gathered(k3cuda_ctx *ctx, float *state, const void *q,
+                                           const void *k, const void *v, const float *gate,
+                                           const float *beta, const int *cu_seqlens, int n_seq,
+                                           int H_local, int dk, int dv, float q_scale,
+                                           int gate_mode, int chunk, void *workspace,
+                                           size_t workspace_bytes) {
+    int rc = enter(ctx);
+    if (rc) return rc;
+    if (!ctx->nccl_comm || !ctx->full_out[ctx->rank])
+        return set_error(K3CUDA_ERR_STATE,
+                         "kda_prefill_gathered: k3cuda_comm_init and k3cuda_comm_register_full "
+                         "first");
+    K3_ARG_CHECK(dk == 128 && dv == 128, "kda_prefill_gathered: built for dk = dv = 128 only");
+    K3_ARG_CHECK(gate_mode == K3CUDA_GATE_LOG || gate_mode == K3CUDA_GATE_ALPHA,
+                 "bad gate_mode %d", gate_mode);
+    size_t need = 0;
+    rc = k3cuda_kda_prefill_workspace(cu_seqlens, n_seq, H_local, dk, dv, chunk, &need);
+    if (rc) return rc;
+    if (cu_seqlens[0] != 0) return set_error(K3CUDA_ERR_ARG, "cu_seqlens[0] must be 0");
+    if (workspace_bytes < need || (need && !workspace))
+        return set_error(K3CUDA_ERR_WORKSPACE, "kda_prefill_gathered: workspace %zu < %zu bytes",
+                         workspace_bytes, need);
+    K3_ARG_CHECK(aligned(workspace, 256), "workspace must be 256-byte aligned");
+    const int T = cu_seqlens[n_seq];
+    const size_t full_need = (size_t)T * ctx->nranks * H_local * dv * 2;
+    if (full_need > ctx->full_bytes)
+        return set_error(K3CUDA_ERR_ARG,
+                         "kda_prefill_gathered: output needs %zu bytes, registered buffer has %zu",
+                         full_need, ctx->full_bytes);
+    K3_ARG_CHECK(T == 0 || (q && k && v && gate && beta), "kda_prefill_gathered: null pointer");
+    // the scan writes this rank's heads straight into its own full buffer (final layout);
+    // one coalesced pass then pushes that head span into every peer's buffer over NVLink
+    GatherOut go{};
+    go.ptr[0] = (__nv_bfloat16 *)ctx->full_out[ctx->rank];
+    go.n = 1;
+    go.head0 = ctx->rank * H_local;
+    go.H_total = ctx->nranks * H_local;
+    // every rank is done with the previous contents of its buffer before anyone writes
+    rc = comm_fence(ctx);
+    if (rc) return rc;
+    if (T > 0 && n_seq > 0) {
+        long long nc = 0;
+        count_chunks(cu_seqlens, n_seq, &nc);
+        rc = run_prefill<__nv_bfloat16, 128>(ctx, state, nullptr, q, k, v, gate, beta,
+                                             cu_seqlens, n_seq, H_local, q_scale,
+                                             gate_mode == K3CUDA_GATE_LOG, nc, workspace, &go);
+        if (rc) return rc;
+        rc = comm_push_heads(ctx, T, go.head0, H_local, go.H_total, dv);
+        if (rc) return rc;
+    }
+    // and every rank's writes into every buffer are complete before anyone reads one
+    return comm_fence(ctx);
 }
 
 // ------------------------------------------------------------- allocation-free variant

@@ -770,7 +770,7 @@ __global__ void __launch_bounds__(192, 1)
 kda_scan_tc(const __grid_constant__ ScanMaps maps, const TcChunk *__restrict__ chunks,
             const int *__restrict__ seq_chunk0, const uint8_t *__restrict__ ws,
             float *__restrict__ state, __nv_bfloat16 *__restrict__ o, int H,
-            unsigned *__restrict__ err) {
+            const __grid_constant__ GatherOut go, unsigned *__restrict__ err) {
     using C = ScanCfg<DVT>;
     constexpr int NT = TC_D / DVT;
     extern __shared__ uint8_t smraw[];
@@ -971,10 +971,25 @@ kda_scan_tc(const __grid_constant__ ScanMaps maps, const TcChunk *__restrict__ c
                 tmem_ld32(tb + lo + TM_O + DVT * (j & 1) + c, v);
                 tmem_wait_ld();
                 if (lane < 16 && t < cd.len) {
-                    uint4 *dst = reinterpret_cast<uint4 *>(
-                        o + ((size_t)(cd.t0 + t) * H + h) * TC_D + col0 + c);
+                    uint4 pk[4];
 #pragma unroll
-                    for (int q = 0; q < 4; q++) dst[q] = pack_bf8(v + 8 * q);
+                    for (int q = 0; q < 4; q++) pk[q] = pack_bf8(v + 8 * q);
+                    if (go.n == 0) {
+                        uint4 *dst = reinterpret_cast<uint4 *>(
+                            o + ((size_t)(cd.t0 + t) * H + h) * TC_D + col0 + c);
+#pragma unroll
+                        for (int q = 0; q < 4; q++) dst[q] = pk[q];
+                    } else {
+                        // the row goes straight into every rank's full output (peer memory
+                        // over NVLink), at this rank's heads of the [T][H_total][dv] layout
+                        const size_t off =
+                            ((size_t)(cd.t0 + t) * go.H_total + go.head0 + h) * TC_D + col0 + c;
+                        for (int r = 0; r < go.n; r++) {
+                            uint4 *dst = reinterpret_cast<uint4 *>(go.ptr[r] + off);
+#pragma unroll
+                            for (int q = 0; q < 4; q++) dst[q] = pk[q];
+                        }
+                    }
                 }
             }
             tc_fence_before();
@@ -996,7 +1011,8 @@ size_t prefill_tc_block_bytes() { return WB_BYTES; }
 int run_prefill_tc(k3cuda_ctx *ctx, float *state, void *o, const void *q, const void *k,
                    const void *v, const float *gate, const float *beta, int total_tokens,
                    int n_seq, int H, float q_scale, int gate_is_log, long long nc,
-                   const void *d_table, const int *d_c0, void *blocks) {
+                   const void *d_table, const int *d_c0, void *blocks, const GatherOut *go) {
+    const GatherOut gout = go ? *go : GatherOut{};
     const CUtensorMapDataType BF = CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
     const CUtensorMapDataType F32 = CU_TENSOR_MAP_DATA_TYPE_FLOAT32;
     PrepMaps pm;
@@ -1034,13 +1050,15 @@ int run_prefill_tc(k3cuda_ctx *ctx, float *state, void *o, const void *q, const 
         K3_CUDA_TRY(cudaFuncSetAttribute(kda_scan_tc<128>,
                                          cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM));
         kda_scan_tc<128><<<(unsigned)((long long)n_seq * H), 192, C::SMEM, ctx->stream>>>(
-            sm, (const TcChunk *)d_table, d_c0, b, state, (__nv_bfloat16 *)o, H, ctx->err_word);
+            sm, (const TcChunk *)d_table, d_c0, b, state, (__nv_bfloat16 *)o, H, gout,
+            ctx->err_word);
     } else {
         using C = ScanCfg<64>;
         K3_CUDA_TRY(cudaFuncSetAttribute(kda_scan_tc<64>,
                                          cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM));
         kda_scan_tc<64><<<(unsigned)((long long)n_seq * H * 2), 192, C::SMEM, ctx->stream>>>(
-            sm, (const TcChunk *)d_table, d_c0, b, state, (__nv_bfloat16 *)o, H, ctx->err_word);
+            sm, (const TcChunk *)d_table, d_c0, b, state, (__nv_bfloat16 *)o, H, gout,
+            ctx->err_word);
     }
     return after_launch(ctx, "kda_scan_tc");
 }

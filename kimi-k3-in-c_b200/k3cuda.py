@@ -59,6 +59,9 @@ SIGNATURES = {
     "k3cuda_comm_init": (_i, [_vp, _i, _i, C.c_char_p]),
     "k3cuda_allgather_heads_workspace": (_i, [_i, _i, _i, _i, _i, C.POINTER(_sz)]),
     "k3cuda_allgather_heads": (_i, [_vp, _vp, _vp, _i, _i, _i, _i, _vp, _sz]),
+    "k3cuda_comm_register_full": (_i, [_vp, _vp, _sz]),
+    "k3cuda_kda_prefill_gathered": (_i, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _ip, _i, _i, _i, _i,
+                                         _f, _i, _i, _vp, _sz]),
 }
 
 # include/k3_gpu.h: the reference-signature C99 wrappers (host fp32 buffers).
@@ -260,6 +263,20 @@ class Context:
         check(lib().k3cuda_allgather_heads(self.h, _ptr(full), _ptr(local), int(T), int(H_local),
                                            int(dv), int(dtype), _ptr(workspace),
                                            int(workspace_bytes)))
+
+    def comm_register_full(self, full):
+        """Map every rank's full-output buffer into every process (collective)."""
+        check(lib().k3cuda_comm_register_full(self.h, _ptr(full), int(full.nbytes)))
+
+    def kda_prefill_gathered(self, state, q, k, v, gate, beta, cu_seqlens, H_local, dk, dv,
+                             q_scale, workspace, workspace_bytes, gate_mode=GATE_LOG, chunk=64):
+        """Head-sharded prefill writing into every rank's registered full buffer (collective)."""
+        cu, cup = _iarr(cu_seqlens)
+        check(lib().k3cuda_kda_prefill_gathered(self.h, _ptr(state), _ptr(q), _ptr(k), _ptr(v),
+                                                _ptr(gate), _ptr(beta), cup, len(cu) - 1,
+                                                int(H_local), int(dk), int(dv), float(q_scale),
+                                                int(gate_mode), int(chunk), _ptr(workspace),
+                                                int(workspace_bytes)))
 
 
 def comm_unique_id() -> bytes:
