@@ -590,17 +590,24 @@ kda_prep_tc(const __grid_constant__ PrepMaps maps, const TcChunk *__restrict__ c
         }
         *reinterpret_cast<float4 *>(Y + r * 36 + c4) = make_float4(y[0], y[1], y[2], y[3]);
         __syncthreads();
+        // T_BA = -T_BB Y with lane = column c and warp w = rows 4w..4w+3: the triangular bound
+        // is warp-uniform and the four T_BB entries of a step are one broadcast float4
+        const int c = lane, r0 = 4 * warp;
+        float a4[4];
+#pragma unroll
+        for (int u = 0; u < 4; u++) a4[u] = Y[(r0 + u) * 36 + c];
 #pragma unroll
         for (int jj = 0; jj < 31; jj++) {
-            const float tv = jj < r ? AT[(32 + jj) * ATS + 32 + r] : 0.f;
-            const float4 yv = *reinterpret_cast<const float4 *>(Y + jj * 36 + c4);
-            y[0] += tv * yv.x;
-            y[1] += tv * yv.y;
-            y[2] += tv * yv.z;
-            y[3] += tv * yv.w;
-        }
+            if (jj < r0 + 3) {
+                const float4 t4 = *reinterpret_cast<const float4 *>(AT + (32 + jj) * ATS + 32 + r0);
+                const float tv[4] = {t4.x, t4.y, t4.z, t4.w};
+                const float yv = Y[jj * 36 + c];
 #pragma unroll
-        for (int u = 0; u < 4; u++) AT[(c4 + u) * ATS + 32 + r] = -y[u];
+                for (int u = 0; u < 4; u++) a4[u] += (jj < r0 + u ? tv[u] : 0.f) * yv;
+            }
+        }
+        *reinterpret_cast<float4 *>(AT + c * ATS + 32 + r0) =
+            make_float4(-a4[0], -a4[1], -a4[2], -a4[3]);
     }
     if (tid == 0) bulk_wait_read<0>();  // the remainder of M goes over the stored-out Aqk
     __syncthreads();
