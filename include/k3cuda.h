@@ -204,6 +204,57 @@ int k3cuda_kda_prefill_gathered(k3cuda_ctx *ctx, float *state, const void *q, co
                                 int dv, float q_scale, int gate_mode, int chunk,
                                 void *workspace, size_t workspace_bytes);
 
+/* --------------------------------------------------- projections (k3_mmw on device) */
+/* y d [T][out] fp32 = x d [T][in] fp32 times W d [out][in]^T, W fp32 (K3CUDA_F32) or bf16
+ * (K3CUDA_BF16). The T-row form of k3_mmw (include/k3/k3.h:290-296: k3_matmul, k3_ops.c:
+ * 265-291, and k3_matmul_bf16, :1122-1227, each one row). Products of the fp32 activation
+ * and the weight are exact and summed in fp32 (the reference sums in double; the
+ * difference is inside fp32 rounding of the result). T <= 8 streams every weight row once
+ * (HBM-bound); T > 8 is a cuBLAS GEMM (loaded at run time), and for bf16 weights x is split
+ * into bf16 hi + lo halves so the product keeps near-fp32 accuracy. Requires in % 8 == 0
+ * and 16-byte aligned x, W, y. workspace d: k3cuda_matmul_workspace() bytes (0 when
+ * T <= 8 or W is fp32). */
+int k3cuda_matmul_workspace(int T, int in, int wdt, size_t *bytes);
+int k3cuda_matmul(k3cuda_ctx *ctx, float *y, const float *x, const void *W, int wdt, int in,
+                  int out, int T, void *workspace, size_t workspace_bytes);
+
+/* --------------------------------------------------------- KDA layer forward */
+/* Device weights of one KDA layer, field for field K3KdaW (include/k3/k3.h:449-463):
+ * q, k, v, g [H*D][E], f_a [D][E], f_b [H*D][D], b [H][E], o [E][H*D] are tagged by wdt
+ * (K3CUDA_F32 == K3_WF32, K3CUDA_BF16 == K3_WBF16); the conv kernels [H*D][K], A_log [H],
+ * dt_bias [H*D] and o_norm [D] are fp32. Every pointer is device memory. */
+typedef struct {
+    const void  *q, *k, *v;
+    const float *q_conv, *k_conv, *v_conv;
+    const void  *f_a, *f_b;
+    const float *A_log;
+    const float *dt_bias;
+    const void  *b;
+    const void  *g;
+    const float *o_norm;
+    const void  *o;
+    int          wdt;
+} k3cuda_kda_weights;
+
+/* k3_kda_layer (src/core/k3_ops.c:864-951) for one sequence of T tokens, every activation
+ * on the device: projections, ShortConv + SiLU with the carried history, L2 on q and k,
+ * beta, the decay chain, the recurrence (the decode kernel at T == 1, the chunked prefill
+ * at T > 1 for D in {64, 128}, else the decode kernel once per token), head RMSNorm, the
+ * sigmoid gate and o_proj, in the reference's order.
+ *   out    d [T][E] fp32;  x d [T][E] fp32
+ *   state  d [H*D*D + 3*H*D*(K-1)] fp32 (recurrent state, then the q, k, v conv
+ *          histories), updated in place; NULL = fresh sequence, nothing written back
+ *   io_dtype  the recurrence's q, k, v and output type: K3CUDA_BF16 runs the prefill on
+ *          the tensor cores (D == 128), K3CUDA_F32 keeps every operand fp32
+ * Supported: E % 8 == 0, D % 16 == 0, D <= 128, 1 <= K <= 8. workspace d:
+ * k3cuda_kda_layer_workspace() bytes, 256-byte aligned. */
+int k3cuda_kda_layer_workspace(int T, int E, int H, int D, int K, int wdt, int io_dtype,
+                               size_t *bytes);
+int k3cuda_kda_layer(k3cuda_ctx *ctx, float *out, const float *x,
+                     const k3cuda_kda_weights *w, int T, int E, int H, int D, int K,
+                     float gate_lb, float rms_eps, float *state, int io_dtype,
+                     void *workspace, size_t workspace_bytes);
+
 #ifdef __cplusplus
 }
 #endif

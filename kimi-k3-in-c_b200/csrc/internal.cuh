@@ -26,6 +26,7 @@ struct k3cuda_ctx {
     size_t full_bytes;
     int *sync_word;             // device int for the cross-rank ordering all-reduce
     void *peer_table;           // device copy of the peers' full-buffer addresses
+    void *blas;                 // cuBLAS handle of the projections (kda_layer.cu), lazily made
 };
 
 namespace k3 {

@@ -1,0 +1,653 @@
+// kda_layer.cu -- the KDA layer forward of k3_kda_layer (src/core/k3_ops.c:864-951) with
+// every activation resident on the device, and the projection primitive k3cuda_matmul
+// (k3_mmw, include/k3/k3.h:290-296) it is built from.
+//
+//   step (reference line)                         where it runs here
+//   1   q, k, v, b, f_a, f_b projections (:877-886)  matvec_rows (T <= 8) or cuBLAS (T > 8)
+//   2   ShortConv + SiLU, history carried (:889-892)  kda_layer_pre, one launch for
+//   3   L2 on q and k per head, eps 1e-6 (:895-899)   steps 2-5
+//   4/5 beta = sigmoid, decay chain (:902-906)
+//   6   recurrence, q * D^-0.5 (:908-938)           k3cuda_kda_decode / k3cuda_kda_prefill
+//   7/8 head RMSNorm, then * sigmoid(g x) (:941-947) kda_layer_post (g x is formed in step 1)
+//   9   o_proj (:948)                               matvec_rows or cuBLAS
+//
+// Projections. Activations are fp32 as in the reference, weights fp32 or bf16 (the wdt tag).
+// With T <= 8 tokens every weight is used at most 8 times, so a projection is weight
+// streaming: matvec_rows reads each weight row once with 16-byte streaming loads and forms
+// the T dot products from exact fp32 products summed in fp32, bound by HBM. The first
+// projections of the layer (q, k, v, g, b, f_a all read the same x) go out as ONE launch
+// over a table of weight matrices. With T > 8 a projection is a GEMM and goes to cuBLAS
+// (opened with dlopen, like NCCL): fp32 weights through SGEMM; bf16 weights with the fp32
+// activations split into bf16 hi + lo halves (x = hi + lo to 2^-16 relative), two bf16
+// GEMMs accumulating into one fp32 result, so x is not rounded to bf16.
+#include <cublas_v2.h>  // types and enumerators only: the library is opened with dlopen
+#include <dlfcn.h>
+
+#include <mutex>
+
+#include "internal.cuh"
+
+namespace k3 {
+
+// ------------------------------------------------------------------------- cuBLAS
+struct BlasApi {
+    void *handle = nullptr;
+    cublasStatus_t (*Create)(cublasHandle_t *) = nullptr;
+    cublasStatus_t (*Destroy)(cublasHandle_t) = nullptr;
+    cublasStatus_t (*SetStream)(cublasHandle_t, cudaStream_t) = nullptr;
+    cublasStatus_t (*Sgemm)(cublasHandle_t, cublasOperation_t, cublasOperation_t, int, int,
+                            int, const float *, const float *, int, const float *, int,
+                            const float *, float *, int) = nullptr;
+    cublasStatus_t (*GemmEx)(cublasHandle_t, cublasOperation_t, cublasOperation_t, int, int,
+                             int, const void *, const void *, cudaDataType, int, const void *,
+                             cudaDataType, int, const void *, void *, cudaDataType, int,
+                             cublasComputeType_t, cublasGemmAlgo_t) = nullptr;
+};
+static BlasApi g_blas;
+static std::mutex g_blas_mu;
+
+static int blas_load() {
+    std::lock_guard<std::mutex> lk(g_blas_mu);
+    if (g_blas.handle) return K3CUDA_OK;
+    void *h = dlopen("libcublas.so.12", RTLD_NOW | RTLD_GLOBAL);
+    if (!h) h = dlopen("/usr/local/cuda/lib64/libcublas.so.12", RTLD_NOW | RTLD_GLOBAL);
+    if (!h) return set_error(K3CUDA_ERR_UNSUPPORTED, "cannot load libcublas.so.12: %s", dlerror());
+#define K3_SYM(field, name)                                                              \
+    g_blas.field = (decltype(g_blas.field))dlsym(h, name);                               \
+    if (!g_blas.field) return set_error(K3CUDA_ERR_UNSUPPORTED, "libcublas lacks %s", name);
+    K3_SYM(Create, "cublasCreate_v2");
+    K3_SYM(Destroy, "cublasDestroy_v2");
+    K3_SYM(SetStream, "cublasSetStream_v2");
+    K3_SYM(Sgemm, "cublasSgemm_v2");
+    K3_SYM(GemmEx, "cublasGemmEx");
+#undef K3_SYM
+    g_blas.handle = h;
+    return K3CUDA_OK;
+}
+
+static int blas_handle(k3cuda_ctx *ctx, cublasHandle_t *out) {
+    int rc = blas_load();
+    if (rc) return rc;
+    if (!ctx->blas) {
+        cublasHandle_t hd = nullptr;
+        if (g_blas.Create(&hd) != CUBLAS_STATUS_SUCCESS)
+            return set_error(K3CUDA_ERR_CUDA, "cublasCreate failed");
+        ctx->blas = hd;
+    }
+    if (g_blas.SetStream((cublasHandle_t)ctx->blas, ctx->stream) != CUBLAS_STATUS_SUCCESS)
+        return set_error(K3CUDA_ERR_CUDA, "cublasSetStream failed");
+    *out = (cublasHandle_t)ctx->blas;
+    return K3CUDA_OK;
+}
+
+__device__ __forceinline__ float dsigm(float x) { return 1.0f / (1.0f + expf(-x)); }
+
+// ------------------------------------------------------------------- matvec_rows
+// y_s[t][r] = sum_i W_s[r][i] x[t][i] for up to MV_MAXSEG weight matrices W_s that share x
+// and `in`. A warp owns MV_ROWS rows and one of `ks` slices of `in`; its lanes read 16-byte
+// pieces (8 weights) of every row, so a warp load is 512 contiguous bytes per row. The `ks`
+// slices of a row group are summed through shared memory in a fixed order.
+constexpr int MV_THREADS = 256, MV_WARPS = 8, MV_ROWS = 4, MV_MAXT = 8, MV_MAXSEG = 8;
+
+struct MatvecSeg {
+    const void *W;  // [rows][in]
+    float *y;       // [T][rows]
+    int rows;
+    int blocks;
+};
+struct MatvecArgs {
+    MatvecSeg seg[MV_MAXSEG];
+    int nseg;
+    const float *x;  // [T][in]
+    int in;
+    int ks;
+};
+
+__device__ __forceinline__ void load8(const __nv_bfloat16 *p, float w[8]) {
+    const uint4 u = __ldcs(reinterpret_cast<const uint4 *>(p));
+    const unsigned int q[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+    for (int j = 0; j < 4; j++) {
+        w[2 * j] = __uint_as_float(q[j] << 16);
+        w[2 * j + 1] = __uint_as_float(q[j] & 0xffff0000u);
+    }
+}
+__device__ __forceinline__ void load8(const float *p, float w[8]) {
+    const float4 a = __ldcs(reinterpret_cast<const float4 *>(p));
+    const float4 b = __ldcs(reinterpret_cast<const float4 *>(p) + 1);
+    w[0] = a.x; w[1] = a.y; w[2] = a.z; w[3] = a.w;
+    w[4] = b.x; w[5] = b.y; w[6] = b.z; w[7] = b.w;
+}
+
+template <int NT, typename WT>
+__global__ void __launch_bounds__(MV_THREADS) matvec_rows(const __grid_constant__ MatvecArgs a) {
+    __shared__ float part[MV_WARPS][MV_ROWS * NT];
+    int b = blockIdx.x, s = 0;
+    while (s + 1 < a.nseg && b >= a.seg[s].blocks) b -= a.seg[s++].blocks;
+    const MatvecSeg &sg = a.seg[s];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int ks = a.ks, rg = warp / ks, sl = warp - rg * ks;
+    const int row0 = (b * (MV_WARPS / ks) + rg) * MV_ROWS;
+    const int n8 = a.in >> 3, per = (n8 + ks - 1) / ks;
+    const int b8 = sl * per, e8 = min(n8, b8 + per);
+    const WT *wr[MV_ROWS];
+#pragma unroll
+    for (int r = 0; r < MV_ROWS; r++)  // rows past the end re-read the last row, never stored
+        wr[r] = (const WT *)sg.W + (size_t)min(row0 + r, sg.rows - 1) * a.in;
+    float acc[MV_ROWS][NT];
+#pragma unroll
+    for (int r = 0; r < MV_ROWS; r++)
+#pragma unroll
+        for (int t = 0; t < NT; t++) acc[r][t] = 0.f;
+#pragma unroll 2
+    for (int i8 = b8 + lane; i8 < e8; i8 += 32) {
+        float w[MV_ROWS][8];
+#pragma unroll
+        for (int r = 0; r < MV_ROWS; r++) load8(wr[r] + (size_t)i8 * 8, w[r]);
+#pragma unroll
+        for (int t = 0; t < NT; t++) {
+            const float4 *xp = reinterpret_cast<const float4 *>(a.x + (size_t)t * a.in) + 2 * i8;
+            const float4 x0 = __ldg(xp), x1 = __ldg(xp + 1);
+            const float xv[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
+#pragma unroll
+            for (int r = 0; r < MV_ROWS; r++)
+#pragma unroll
+                for (int j = 0; j < 8; j++) acc[r][t] = fmaf(w[r][j], xv[j], acc[r][t]);
+        }
+    }
+#pragma unroll
+    for (int r = 0; r < MV_ROWS; r++)
+#pragma unroll
+        for (int t = 0; t < NT; t++) {
+            float v = acc[r][t];
+#pragma unroll
+            for (int o = 16; o; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+            if (lane == 0) part[warp][r * NT + t] = v;
+        }
+    __syncthreads();
+    if (sl == 0 && lane < MV_ROWS * NT) {
+        const int r = lane / NT, t = lane - r * NT;
+        float v = 0.f;
+        for (int j = 0; j < ks; j++) v += part[rg * ks + j][lane];
+        if (row0 + r < sg.rows) sg.y[(size_t)t * sg.rows + row0 + r] = v;
+    }
+}
+
+template <int NT>
+static void launch_matvec(const MatvecArgs &a, int wdt, int blocks, cudaStream_t st) {
+    if (wdt == K3CUDA_BF16)
+        matvec_rows<NT, __nv_bfloat16><<<blocks, MV_THREADS, 0, st>>>(a);
+    else
+        matvec_rows<NT, float><<<blocks, MV_THREADS, 0, st>>>(a);
+}
+
+struct Proj {
+    const void *W;
+    float *y;
+    int rows;
+};
+
+// One launch of matvec_rows over `n` projections of the same x [T][in] (T <= MV_MAXT).
+static int matvec(k3cuda_ctx *ctx, const float *x, int T, int in, const Proj *p, int n, int wdt) {
+    if (T < 1 || T > MV_MAXT || n < 1 || n > MV_MAXSEG)
+        return set_error(K3CUDA_ERR_ARG, "matvec: T=%d n=%d", T, n);
+    MatvecArgs a{};
+    a.nseg = n;
+    a.x = x;
+    a.in = in;
+    const int n8 = in / 8;
+    auto blocks_for = [&](int ks) {
+        long long tot = 0;
+        const int per_block = (MV_WARPS / ks) * MV_ROWS;
+        for (int i = 0; i < n; i++) tot += (p[i].rows + per_block - 1) / per_block;
+        return tot;
+    };
+    // split `in` over more warps only while the grid is short of two waves and every
+    // slice still gives each lane at least one 16-byte piece
+    int ks = 1;
+    while (ks < MV_WARPS && blocks_for(ks) < 2LL * ctx->sm_count && n8 / (2 * ks) >= 32) ks *= 2;
+    a.ks = ks;
+    const int per_block = (MV_WARPS / ks) * MV_ROWS;
+    long long tot = 0;
+    for (int i = 0; i < n; i++) {
+        a.seg[i] = MatvecSeg{p[i].W, p[i].y, p[i].rows, (p[i].rows + per_block - 1) / per_block};
+        tot += a.seg[i].blocks;
+    }
+    if (tot == 0) return K3CUDA_OK;
+    if (tot > 0x7fffffffLL) return set_error(K3CUDA_ERR_ARG, "matvec: grid too large");
+    switch (T) {
+        case 1: launch_matvec<1>(a, wdt, (int)tot, ctx->stream); break;
+        case 2: launch_matvec<2>(a, wdt, (int)tot, ctx->stream); break;
+        case 3: launch_matvec<3>(a, wdt, (int)tot, ctx->stream); break;
+        case 4: launch_matvec<4>(a, wdt, (int)tot, ctx->stream); break;
+        case 5: launch_matvec<5>(a, wdt, (int)tot, ctx->stream); break;
+        case 6: launch_matvec<6>(a, wdt, (int)tot, ctx->stream); break;
+        case 7: launch_matvec<7>(a, wdt, (int)tot, ctx->stream); break;
+        default: launch_matvec<8>(a, wdt, (int)tot, ctx->stream); break;
+    }
+    return after_launch(ctx, "matvec_rows");
+}
+
+// hi = bf16(x), lo = bf16(x - hi): x = hi + lo to within 2^-16 |x|.
+__global__ void split_bf16(__nv_bfloat16 *__restrict__ hi, __nv_bfloat16 *__restrict__ lo,
+                           const float *__restrict__ x, long long n) {
+    for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n;
+         i += (long long)gridDim.x * blockDim.x) {
+        const float v = x[i];
+        const __nv_bfloat16 h = __float2bfloat16_rn(v);
+        hi[i] = h;
+        lo[i] = __float2bfloat16_rn(v - __bfloat162float(h));
+    }
+}
+
+static int split(k3cuda_ctx *ctx, __nv_bfloat16 *xs, const float *x, long long n) {
+    const long long want = (n + 255) / 256;
+    const int blocks = (int)(want < 8LL * ctx->sm_count ? want : 8LL * ctx->sm_count);
+    split_bf16<<<blocks, 256, 0, ctx->stream>>>(xs, xs + n, x, n);
+    return after_launch(ctx, "split_bf16");
+}
+
+// y [T][out] = x [T][in] W^T through cuBLAS (column-major: y^T = W^T' x^T with W read
+// transposed). xs = the bf16 hi/lo split of x ([2][T][in]) when W is bf16.
+static int gemm(k3cuda_ctx *ctx, float *y, const float *x, const __nv_bfloat16 *xs,
+                const void *W, int wdt, int T, int in, int out) {
+    cublasHandle_t h = nullptr;
+    int rc = blas_handle(ctx, &h);
+    if (rc) return rc;
+    const float one = 1.f, zero = 0.f;
+    cublasStatus_t st;
+    if (wdt == K3CUDA_F32) {
+        st = g_blas.Sgemm(h, CUBLAS_OP_T, CUBLAS_OP_N, out, T, in, &one, (const float *)W, in, x,
+                          in, &zero, y, out);
+    } else {
+        st = g_blas.GemmEx(h, CUBLAS_OP_T, CUBLAS_OP_N, out, T, in, &one, W, CUDA_R_16BF, in, xs,
+                           CUDA_R_16BF, in, &zero, y, CUDA_R_32F, out, CUBLAS_COMPUTE_32F,
+                           CUBLAS_GEMM_DEFAULT);
+        if (st == CUBLAS_STATUS_SUCCESS)
+            st = g_blas.GemmEx(h, CUBLAS_OP_T, CUBLAS_OP_N, out, T, in, &one, W, CUDA_R_16BF, in,
+                               xs + (size_t)T * in, CUDA_R_16BF, in, &one, y, CUDA_R_32F, out,
+                               CUBLAS_COMPUTE_32F, CUBLAS_GEMM_DEFAULT);
+    }
+    if (st != CUBLAS_STATUS_SUCCESS)
+        return set_error(K3CUDA_ERR_CUDA, "cuBLAS GEMM %dx%dx%d failed (status %d)", T, out, in,
+                         (int)st);
+    return K3CUDA_OK;
+}
+
+// ------------------------------------------------------------------ kda_layer_pre
+// Grid (token tiles of LT, H, 4). z = 0, 1, 2: ShortConv + SiLU of the raw q, k, v
+// projections of head h (k3_shortconv, k3_ops.c:133-165: taps oldest..newest, w[K-1] on the
+// current input), then for q and k the L2 norm over the head's D channels (l2norm_,
+// :845-851). z = 3: the decay chain g = lb * sigmoid(exp(A_log[h]) (z + dt_bias))
+// (k3_kda_decay, :167-183, kept as log-decay) and beta = sigmoid(b x) (:902-903).
+// A block stages the raw rows t0-K+1 .. t0+LT-1 of its head (older rows from the conv
+// history) and the conv taps in shared memory; warps take tokens, lanes take channels. The
+// block of the first tile, which alone reads the old history, writes the new one (the raw
+// inputs of the last K-1 tokens) after its staging.
+constexpr int LT = 32, LAYER_THREADS = 256;
+
+template <typename IO>
+struct PreArgs {
+    const float *y[3];   // raw projections q, k, v [T][P]
+    const float *cw[3];  // conv taps [P][K]
+    float *hist;         // conv histories [3][P][K-1], or null
+    const float *z;      // low-rank decay input [T][P]
+    const float *yb;     // beta logits [T][H]
+    const float *A_log, *dt_bias;
+    IO *out[3];          // recurrence q, k, v [T][P]
+    float *g;            // log decay [T][P]
+    float *beta;         // [T][H]
+    int T, H, D, K;
+    float lb;
+};
+
+template <typename IO, int CPL>
+__global__ void __launch_bounds__(LAYER_THREADS) kda_layer_pre(const __grid_constant__ PreArgs<IO> a) {
+    extern __shared__ float sm[];
+    const int s = blockIdx.z, h = blockIdx.y, t0 = blockIdx.x * LT;
+    const int D = a.D, P = a.H * D, K = a.K, hist = K - 1;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int nt = min(LT, a.T - t0);
+    if (s == 3) {
+        const float ea = expf(a.A_log[h]);
+        for (int tt = warp; tt < nt; tt += LAYER_THREADS / 32) {
+            const size_t row = (size_t)(t0 + tt) * P + (size_t)h * D;
+            for (int c = lane; c < D; c += 32)
+                a.g[row + c] = a.lb * dsigm(ea * (a.z[row + c] + a.dt_bias[h * D + c]));
+            if (lane == 0) {
+                const size_t i = (size_t)(t0 + tt) * a.H + h;
+                a.beta[i] = dsigm(a.yb[i]);
+            }
+        }
+        return;
+    }
+    float *raw = sm;                   // [nt + hist][D]: row r is token t0 - hist + r
+    float *cw = sm + (LT + hist) * D;  // [K][D]
+    const float *y = a.y[s];
+    float *hs = a.hist ? a.hist + ((size_t)s * P + (size_t)h * D) * hist : nullptr;  // [D][hist]
+    const int rows = nt + hist;
+    for (int i = threadIdx.x; i < rows * D; i += LAYER_THREADS) {
+        const int r = i / D, c = i - r * D, tok = t0 - hist + r;
+        float v = 0.f;
+        if (tok >= 0) v = y[(size_t)tok * P + (size_t)h * D + c];
+        else if (hs) v = hs[(size_t)c * hist + (tok + hist)];
+        raw[i] = v;
+    }
+    for (int i = threadIdx.x; i < D * K; i += LAYER_THREADS) {
+        const int c = i / K, j = i - c * K;
+        cw[j * D + c] = a.cw[s][(size_t)h * D * K + i];
+    }
+    __syncthreads();
+    if (blockIdx.x == 0 && hs) {
+        for (int i = threadIdx.x; i < D * hist; i += LAYER_THREADS) {
+            const int c = i / hist, j = i - c * hist, tok = a.T - hist + j;
+            hs[i] = tok < nt ? raw[(tok + hist) * D + c] : y[(size_t)tok * P + (size_t)h * D + c];
+        }
+    }
+    IO *out = a.out[s];
+    for (int tt = warp; tt < nt; tt += LAYER_THREADS / 32) {
+        float v[CPL], ss = 0.f;
+#pragma unroll
+        for (int m = 0; m < CPL; m++) {
+            const int c = lane + 32 * m;
+            v[m] = 0.f;
+            if (c < D) {
+                float acc = cw[hist * D + c] * raw[(tt + hist) * D + c];
+                for (int j = 0; j < hist; j++) acc += cw[j * D + c] * raw[(tt + j) * D + c];
+                v[m] = acc * dsigm(acc);
+                ss += v[m] * v[m];
+            }
+        }
+        if (s < 2) {
+#pragma unroll
+            for (int o = 16; o; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+            const float inv = 1.0f / sqrtf(ss + 1e-6f);
+#pragma unroll
+            for (int m = 0; m < CPL; m++) v[m] *= inv;
+        }
+        const size_t row = (size_t)(t0 + tt) * P + (size_t)h * D;
+#pragma unroll
+        for (int m = 0; m < CPL; m++) {
+            const int c = lane + 32 * m;
+            if (c < D) io<IO>::st(out + row + c, v[m]);
+        }
+    }
+}
+
+// ----------------------------------------------------------------- kda_layer_post
+// ot = RMSNorm_head(o) * o_norm * sigmoid(g x) (k3_rmsnorm per head then the gate,
+// k3_ops.c:941-947), optionally also split into bf16 hi/lo for the o_proj GEMM.
+template <typename IO>
+struct PostArgs {
+    const IO *o;       // recurrence output [T][P]
+    const float *gb;   // gate logits [T][P]
+    const float *w;    // o_norm [D]
+    float *ot;         // [T][P]
+    __nv_bfloat16 *hi, *lo;
+    int T, H, D;
+    float eps;
+};
+
+template <typename IO, int CPL>
+__global__ void __launch_bounds__(LAYER_THREADS) kda_layer_post(const __grid_constant__ PostArgs<IO> a) {
+    const int h = blockIdx.y, t0 = blockIdx.x * LT;
+    const int D = a.D, P = a.H * D;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int nt = min(LT, a.T - t0);
+    for (int tt = warp; tt < nt; tt += LAYER_THREADS / 32) {
+        const size_t row = (size_t)(t0 + tt) * P + (size_t)h * D;
+        float v[CPL], ss = 0.f;
+#pragma unroll
+        for (int m = 0; m < CPL; m++) {
+            const int c = lane + 32 * m;
+            v[m] = c < D ? io<IO>::ld(a.o + row + c) : 0.f;
+            ss += v[m] * v[m];
+        }
+#pragma unroll
+        for (int o = 16; o; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+        const float inv = 1.0f / sqrtf(ss / (float)D + a.eps);
+#pragma unroll
+        for (int m = 0; m < CPL; m++) {
+            const int c = lane + 32 * m;
+            if (c < D) {
+                float r = a.w[c] * v[m] * inv;
+                r *= dsigm(a.gb[row + c]);
+                a.ot[row + c] = r;
+                if (a.hi) {
+                    const __nv_bfloat16 hb = __float2bfloat16_rn(r);
+                    a.hi[row + c] = hb;
+                    a.lo[row + c] = __float2bfloat16_rn(r - __bfloat162float(hb));
+                }
+            }
+        }
+    }
+}
+
+// ----------------------------------------------------------------- workspace plan
+static size_t al256(size_t x) { return (x + 255) & ~(size_t)255; }
+
+struct LayerPlan {
+    // byte offsets into the workspace
+    size_t yq, yk, yv, z, gb, yb, fa, rq, rk, rv, g, beta, o, xs, fas, s0, pre, total;
+    size_t pre_bytes;
+    bool gemm_path, split;
+    int io_size;
+};
+
+static int plan_layer(int T, int E, int H, int D, int K, int wdt, int io_dtype, LayerPlan *p) {
+    (void)K;
+    const size_t P = (size_t)H * D, TP = (size_t)T * P;
+    const int es = io_dtype == K3CUDA_BF16 ? 2 : 4;
+    size_t off = 0;
+    auto take = [&](size_t bytes) { const size_t o = off; off += al256(bytes); return o; };
+    p->gemm_path = T > MV_MAXT;
+    p->split = p->gemm_path && wdt == K3CUDA_BF16;
+    p->io_size = es;
+    p->yq = take(TP * 4);  // later the post kernel's ot
+    p->yk = take(TP * 4);  // later ot's bf16 hi/lo split (same bytes)
+    p->yv = take(TP * 4);
+    p->z = take(TP * 4);
+    p->gb = take(TP * 4);
+    p->yb = take((size_t)T * H * 4);
+    p->fa = take((size_t)T * D * 4);
+    p->rq = take(TP * es);
+    p->rk = take(TP * es);
+    p->rv = take(TP * es);
+    p->g = take(TP * 4);
+    p->beta = take((size_t)T * H * 4);
+    p->o = take(TP * es);
+    p->xs = p->split ? take((size_t)2 * T * E * 2) : 0;
+    p->fas = p->split ? take((size_t)2 * T * D * 2) : 0;
+    p->s0 = take(P * D * 4);
+    p->pre_bytes = 0;
+    if (T > 1 && (D == 64 || D == 128)) {
+        const int cu[2] = {0, T};
+        int rc = k3cuda_kda_prefill_workspace(cu, 1, H, D, D, 64, &p->pre_bytes);
+        if (rc) return rc;
+    }
+    p->pre = take(p->pre_bytes);
+    p->total = off;
+    return K3CUDA_OK;
+}
+
+static int layer_shape_ok(int T, int E, int H, int D, int K, int wdt, int io_dtype) {
+    K3_ARG_CHECK(T >= 0 && E >= 8 && H >= 1 && D >= 16 && K >= 1, "kda_layer: bad shape T=%d "
+                 "E=%d H=%d D=%d K=%d", T, E, H, D, K);
+    K3_ARG_CHECK(wdt == K3CUDA_F32 || wdt == K3CUDA_BF16, "kda_layer: bad wdt %d", wdt);
+    K3_ARG_CHECK(io_dtype == K3CUDA_F32 || io_dtype == K3CUDA_BF16, "kda_layer: bad io_dtype %d",
+                 io_dtype);
+    if (E % 8 || D % 16 || D > 128 || K > 8)
+        return set_error(K3CUDA_ERR_UNSUPPORTED, "kda_layer: E=%d D=%d K=%d not built (E %% 8 "
+                         "== 0, D %% 16 == 0, D <= 128, K <= 8)", E, D, K);
+    return K3CUDA_OK;
+}
+
+// One projection: matvec (T <= 8) or GEMM; xs is x's bf16 split when the GEMM needs it.
+static int project(k3cuda_ctx *ctx, float *y, const float *x, const __nv_bfloat16 *xs,
+                   const void *W, int wdt, int T, int in, int out) {
+    if (T <= MV_MAXT) {
+        const Proj p{W, y, out};
+        return matvec(ctx, x, T, in, &p, 1, wdt);
+    }
+    return gemm(ctx, y, x, xs, W, wdt, T, in, out);
+}
+
+template <typename IO>
+static int layer_core(k3cuda_ctx *ctx, float *out, const float *x, const k3cuda_kda_weights *w,
+                      int T, int E, int H, int D, int K, float lb, float eps, float *state,
+                      int io_dtype, char *ws, const LayerPlan &pl) {
+    const int P = H * D, hist = K - 1, wdt = w->wdt;
+    float *yq = (float *)(ws + pl.yq), *yk = (float *)(ws + pl.yk), *yv = (float *)(ws + pl.yv);
+    float *z = (float *)(ws + pl.z), *gb = (float *)(ws + pl.gb), *yb = (float *)(ws + pl.yb);
+    float *fa = (float *)(ws + pl.fa), *g = (float *)(ws + pl.g), *beta = (float *)(ws + pl.beta);
+    IO *rq = (IO *)(ws + pl.rq), *rk = (IO *)(ws + pl.rk), *rv = (IO *)(ws + pl.rv);
+    IO *o = (IO *)(ws + pl.o);
+    __nv_bfloat16 *xs = pl.split ? (__nv_bfloat16 *)(ws + pl.xs) : nullptr;
+    __nv_bfloat16 *fas = pl.split ? (__nv_bfloat16 *)(ws + pl.fas) : nullptr;
+    int rc;
+    // 1. projections (and the gate's g x, which reads the same x)
+    if (!pl.gemm_path) {
+        const Proj first[6] = {{w->q, yq, P}, {w->k, yk, P}, {w->v, yv, P},
+                               {w->g, gb, P}, {w->b, yb, H}, {w->f_a, fa, D}};
+        if ((rc = matvec(ctx, x, T, E, first, 6, wdt))) return rc;
+    } else {
+        if (pl.split && (rc = split(ctx, xs, x, (long long)T * E))) return rc;
+        const Proj first[6] = {{w->q, yq, P}, {w->k, yk, P}, {w->v, yv, P},
+                               {w->g, gb, P}, {w->b, yb, H}, {w->f_a, fa, D}};
+        for (const Proj &p : first)
+            if ((rc = gemm(ctx, p.y, x, xs, p.W, wdt, T, E, p.rows))) return rc;
+        if (pl.split && (rc = split(ctx, fas, fa, (long long)T * D))) return rc;
+    }
+    if ((rc = project(ctx, z, fa, fas, w->f_b, wdt, T, D, P))) return rc;
+    // 2-5. conv + SiLU, L2, decay, beta
+    {
+        PreArgs<IO> a{};
+        a.y[0] = yq; a.y[1] = yk; a.y[2] = yv;
+        a.cw[0] = w->q_conv; a.cw[1] = w->k_conv; a.cw[2] = w->v_conv;
+        a.hist = state && hist > 0 ? state + (size_t)H * D * D : nullptr;
+        a.z = z; a.yb = yb; a.A_log = w->A_log; a.dt_bias = w->dt_bias;
+        a.out[0] = rq; a.out[1] = rk; a.out[2] = rv;
+        a.g = g; a.beta = beta;
+        a.T = T; a.H = H; a.D = D; a.K = K; a.lb = lb;
+        const size_t smem = ((size_t)(LT + hist) * D + (size_t)K * D) * sizeof(float);
+        dim3 grid((unsigned)((T + LT - 1) / LT), (unsigned)H, 4);
+        if (D <= 32) kda_layer_pre<IO, 1><<<grid, LAYER_THREADS, smem, ctx->stream>>>(a);
+        else if (D <= 64) kda_layer_pre<IO, 2><<<grid, LAYER_THREADS, smem, ctx->stream>>>(a);
+        else kda_layer_pre<IO, 4><<<grid, LAYER_THREADS, smem, ctx->stream>>>(a);
+        if ((rc = after_launch(ctx, "kda_layer_pre"))) return rc;
+    }
+    // 6. recurrence
+    float *S = state;
+    if (!S) {
+        S = (float *)(ws + pl.s0);
+        K3_CUDA_TRY(cudaMemsetAsync(S, 0, (size_t)P * D * sizeof(float), ctx->stream));
+    }
+    const float qs = 1.0f / sqrtf((float)D);
+    if (T == 1 || pl.pre_bytes == 0) {
+        for (int t = 0; t < T; t++) {
+            const size_t off = (size_t)t * P;
+            rc = k3cuda_kda_decode(ctx, S, o + off, rq + off, rk + off, rv + off, g + off,
+                                   beta + (size_t)t * H, 1, H, D, D, qs, io_dtype,
+                                   K3CUDA_GATE_LOG);
+            if (rc) return rc;
+        }
+    } else {
+        const int cu[2] = {0, T};
+        rc = k3cuda_kda_prefill(ctx, S, o, rq, rk, rv, g, beta, cu, 1, H, D, D, qs, io_dtype,
+                                K3CUDA_GATE_LOG, 64, ws + pl.pre, pl.pre_bytes);
+        if (rc) return rc;
+    }
+    // 7/8. head RMSNorm, then the gate (ot reuses yq, its split reuses yk)
+    float *ot = yq;
+    __nv_bfloat16 *ots = pl.split ? (__nv_bfloat16 *)yk : nullptr;
+    {
+        PostArgs<IO> a{};
+        a.o = o; a.gb = gb; a.w = w->o_norm; a.ot = ot;
+        a.hi = ots; a.lo = ots ? ots + (size_t)T * P : nullptr;
+        a.T = T; a.H = H; a.D = D; a.eps = eps;
+        dim3 grid((unsigned)((T + LT - 1) / LT), (unsigned)H);
+        if (D <= 32) kda_layer_post<IO, 1><<<grid, LAYER_THREADS, 0, ctx->stream>>>(a);
+        else if (D <= 64) kda_layer_post<IO, 2><<<grid, LAYER_THREADS, 0, ctx->stream>>>(a);
+        else kda_layer_post<IO, 4><<<grid, LAYER_THREADS, 0, ctx->stream>>>(a);
+        if ((rc = after_launch(ctx, "kda_layer_post"))) return rc;
+    }
+    // 9. o_proj
+    return project(ctx, out, ot, ots, w->o, wdt, T, P, E);
+}
+
+}  // namespace k3
+
+using namespace k3;
+
+extern "C" void k3cuda_blas_destroy_internal(k3cuda_ctx *ctx) {
+    if (ctx && ctx->blas && g_blas.Destroy) g_blas.Destroy((cublasHandle_t)ctx->blas);
+    if (ctx) ctx->blas = nullptr;
+}
+
+extern "C" int k3cuda_matmul_workspace(int T, int in, int wdt, size_t *bytes) {
+    K3_ARG_CHECK(bytes && T >= 0 && in >= 0, "bad matmul workspace query");
+    K3_ARG_CHECK(wdt == K3CUDA_F32 || wdt == K3CUDA_BF16, "matmul: bad wdt %d", wdt);
+    *bytes = (T > MV_MAXT && wdt == K3CUDA_BF16) ? al256((size_t)2 * T * in * 2) : 0;
+    return K3CUDA_OK;
+}
+
+extern "C" int k3cuda_matmul(k3cuda_ctx *ctx, float *y, const float *x, const void *W, int wdt,
+                             int in, int out, int T, void *workspace, size_t workspace_bytes) {
+    int rc = enter(ctx);
+    if (rc) return rc;
+    size_t need = 0;
+    if ((rc = k3cuda_matmul_workspace(T, in, wdt, &need))) return rc;
+    K3_ARG_CHECK(out >= 0, "matmul: out=%d", out);
+    if (T == 0 || out == 0) return K3CUDA_OK;
+    K3_ARG_CHECK(y && x && W, "matmul: null pointer");
+    if (in % 8) return set_error(K3CUDA_ERR_UNSUPPORTED, "matmul: in=%d not a multiple of 8", in);
+    K3_ARG_CHECK(aligned(y, 16) && aligned(x, 16) && aligned(W, 16),
+                 "matmul: x, W, y must be 16-byte aligned");
+    if (workspace_bytes < need || (need && !workspace))
+        return set_error(K3CUDA_ERR_WORKSPACE, "matmul: workspace %zu < %zu bytes",
+                         workspace_bytes, need);
+    __nv_bfloat16 *xs = need ? (__nv_bfloat16 *)workspace : nullptr;
+    if (xs && (rc = split(ctx, xs, x, (long long)T * in))) return rc;
+    return project(ctx, y, x, xs, W, wdt, T, in, out);
+}
+
+extern "C" int k3cuda_kda_layer_workspace(int T, int E, int H, int D, int K, int wdt,
+                                          int io_dtype, size_t *bytes) {
+    K3_ARG_CHECK(bytes, "null bytes");
+    int rc = layer_shape_ok(T, E, H, D, K, wdt, io_dtype);
+    if (rc) return rc;
+    LayerPlan p;
+    if ((rc = plan_layer(T, E, H, D, K, wdt, io_dtype, &p))) return rc;
+    *bytes = p.total;
+    return K3CUDA_OK;
+}
+
+extern "C" int k3cuda_kda_layer(k3cuda_ctx *ctx, float *out, const float *x,
+                                const k3cuda_kda_weights *w, int T, int E, int H, int D, int K,
+                                float gate_lb, float rms_eps, float *state, int io_dtype,
+                                void *workspace, size_t workspace_bytes) {
+    int rc = enter(ctx);
+    if (rc) return rc;
+    K3_ARG_CHECK(w, "kda_layer: null weights");
+    if ((rc = layer_shape_ok(T, E, H, D, K, w->wdt, io_dtype))) return rc;
+    if (T == 0) return K3CUDA_OK;
+    K3_ARG_CHECK(out && x && w->q && w->k && w->v && w->q_conv && w->k_conv && w->v_conv &&
+                 w->f_a && w->f_b && w->A_log && w->dt_bias && w->b && w->g && w->o_norm &&
+                 w->o, "kda_layer: null pointer");
+    const void *vec[] = {out, x, w->q, w->k, w->v, w->f_a, w->f_b, w->b, w->g, w->o};
+    for (const void *p : vec)
+        K3_ARG_CHECK(aligned(p, 16), "kda_layer: x, out and the projection weights must be "
+                     "16-byte aligned");
+    K3_ARG_CHECK(aligned(state, 16), "kda_layer: state must be 16-byte aligned");
+    LayerPlan pl;
+    if ((rc = plan_layer(T, E, H, D, K, w->wdt, io_dtype, &pl))) return rc;
+    if (workspace_bytes < pl.total || !workspace)
+        return set_error(K3CUDA_ERR_WORKSPACE, "kda_layer: workspace %zu < %zu bytes",
+                         workspace_bytes, pl.total);
+    K3_ARG_CHECK(aligned(workspace, 256), "kda_layer: workspace must be 256-byte aligned");
+    if (io_dtype == K3CUDA_BF16)
+        return layer_core<__nv_bfloat16>(ctx, out, x, w, T, E, H, D, K, gate_lb, rms_eps, state,
+                                         io_dtype, (char *)workspace, pl);
+    return layer_core<float>(ctx, out, x, w, T, E, H, D, K, gate_lb, rms_eps, state, io_dtype,
+                             (char *)workspace, pl);
+}

@@ -62,7 +62,22 @@ SIGNATURES = {
     "k3cuda_comm_register_full": (_i, [_vp, _vp, _sz]),
     "k3cuda_kda_prefill_gathered": (_i, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _ip, _i, _i, _i, _i,
                                          _f, _i, _i, _vp, _sz]),
+    "k3cuda_matmul_workspace": (_i, [_i, _i, _i, C.POINTER(_sz)]),
+    "k3cuda_matmul": (_i, [_vp, _vp, _vp, _vp, _i, _i, _i, _i, _vp, _sz]),
+    "k3cuda_kda_layer_workspace": (_i, [_i, _i, _i, _i, _i, _i, _i, C.POINTER(_sz)]),
+    "k3cuda_kda_layer": (_i, [_vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _f, _f, _vp, _i, _vp, _sz]),
 }
+
+
+class KdaWeights(C.Structure):
+    """k3cuda_kda_weights: device pointers of one KDA layer, in K3KdaW's field order."""
+    _fields_ = [("q", _vp), ("k", _vp), ("v", _vp), ("q_conv", _vp), ("k_conv", _vp),
+                ("v_conv", _vp), ("f_a", _vp), ("f_b", _vp), ("A_log", _vp), ("dt_bias", _vp),
+                ("b", _vp), ("g", _vp), ("o_norm", _vp), ("o", _vp), ("wdt", _i)]
+
+
+KDA_WEIGHT_NAMES = ("q", "k", "v", "q_conv", "k_conv", "v_conv", "f_a", "f_b", "A_log",
+                    "dt_bias", "b", "g", "o_norm", "o")
 
 # include/k3_gpu.h: the reference-signature C99 wrappers (host fp32 buffers).
 _fp = C.POINTER(C.c_float)
@@ -249,6 +264,27 @@ class Context:
                                       int(workspace_bytes)))
 
     # multi-GPU -------------------------------------------------------------------
+    # projections and the KDA layer ------------------------------------------------
+    def matmul_workspace(self, T, n_in, wdt) -> int:
+        return _ws_query(lib().k3cuda_matmul_workspace, int(T), int(n_in), int(wdt))
+
+    def matmul(self, y, x, W, wdt, n_in, n_out, T, workspace=None, workspace_bytes=0):
+        check(lib().k3cuda_matmul(self.h, _ptr(y), _ptr(x), _ptr(W), int(wdt), int(n_in),
+                                  int(n_out), int(T), _ptr(workspace), int(workspace_bytes)))
+
+    def kda_layer_workspace(self, T, E, H, D, K, wdt, io_dtype) -> int:
+        return _ws_query(lib().k3cuda_kda_layer_workspace, int(T), int(E), int(H), int(D),
+                         int(K), int(wdt), int(io_dtype))
+
+    def kda_layer(self, out, x, weights, wdt, T, E, H, D, K, gate_lb, rms_eps, state,
+                  io_dtype, workspace, workspace_bytes):
+        """weights: mapping of KDA_WEIGHT_NAMES to device buffers (or device addresses)."""
+        w = KdaWeights(**{n: _ptr(weights[n]) for n in KDA_WEIGHT_NAMES}, wdt=int(wdt))
+        check(lib().k3cuda_kda_layer(self.h, _ptr(out), _ptr(x), C.byref(w), int(T), int(E),
+                                     int(H), int(D), int(K), float(gate_lb), float(rms_eps),
+                                     _ptr(state), int(io_dtype), _ptr(workspace),
+                                     int(workspace_bytes)))
+
     def comm_init(self, nranks: int, rank: int, uid: bytes):
         check(lib().k3cuda_comm_init(self.h, int(nranks), int(rank), uid))
 
@@ -277,6 +313,12 @@ class Context:
                                                 int(H_local), int(dk), int(dv), float(q_scale),
                                                 int(gate_mode), int(chunk), _ptr(workspace),
                                                 int(workspace_bytes)))
+
+
+def _ws_query(fn, *args) -> int:
+    n = C.c_size_t()
+    check(fn(*args, C.byref(n)))
+    return int(n.value)
 
 
 def comm_unique_id() -> bytes:

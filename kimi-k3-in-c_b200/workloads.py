@@ -122,6 +122,26 @@ def mla_config4(seed: int = 0, B: int = 64, ctx: int = 8192, H: int = 128, dn: i
     return out
 
 
+def kda_layer_weights(rng, E: int, H: int, D: int, K: int = 4) -> dict:
+    """Random fp32 weights of one KDA layer under the reference fixtures' names and shapes
+    (tests/golden/kda_layer*.npz): entries N(0, 0.3) at fan-in 128, scaled by
+    sqrt(128 / fan-in) so activations keep the fixtures' magnitude at any width; A_log in
+    [-0.4, 1.2], dt_bias N(0.1, 0.45), o_norm 1 + N(0, 0.1)."""
+    P = H * D
+    f = lambda *s: rng.standard_normal(s).astype(np.float32)  # noqa: E731
+    sc = lambda fan: np.float32(0.3 * np.sqrt(128.0 / fan))  # noqa: E731
+    return {
+        "q_proj": f(P, E) * sc(E), "k_proj": f(P, E) * sc(E), "v_proj": f(P, E) * sc(E),
+        "g_proj": f(P, E) * sc(E), "o_proj": f(E, P) * sc(P), "f_a": f(D, E) * sc(E),
+        "f_b": f(P, D) * sc(D), "b_proj": f(H, E) * sc(E),
+        "q_conv": f(P, 1, K) * np.float32(0.3), "k_conv": f(P, 1, K) * np.float32(0.3),
+        "v_conv": f(P, 1, K) * np.float32(0.3),
+        "A_log": rng.uniform(-0.4, 1.2, H).astype(np.float32),
+        "dt_bias": (0.1 + 0.45 * f(P)).astype(np.float32),
+        "o_norm": (1.0 + 0.1 * f(D)).astype(np.float32),
+    }
+
+
 def rel_fro(a: np.ndarray, b: np.ndarray) -> float:
     """Relative Frobenius error ||a - b||_F / ||b||_F in double."""
     a = np.asarray(a, dtype=np.float64)

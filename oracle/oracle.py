@@ -76,6 +76,10 @@ def ref():
         R.k3_rmsnorm.argtypes = [f32p, f32p, f32p, C.c_int, C.c_float]
         R.k3_matmul.argtypes = [f32p, f32p, f32p, C.c_int, C.c_int]
         R.k3_mla_scratch_cached.restype = C.c_size_t
+        R.k3ref_kda_layer.argtypes = ([f32p, f32p] + [C.c_int] * 5 + [C.c_float, C.c_float]
+                                      + [C.c_void_p] * 3 + [f32p] * 3 + [C.c_void_p] * 2
+                                      + [f32p] * 2 + [C.c_void_p] * 2 + [f32p, C.c_void_p,
+                                                                         C.c_int, C.c_void_p])
         _REF = R
     return _REF
 
@@ -161,6 +165,46 @@ def mla_absorbed_decode(q_nope, q_rope, latent, rope, w_uk, w_uv, ctx_lens, scal
     cl = np.ascontiguousarray(ctx_lens, dtype=np.int32)
     lib().orc_mla_absorbed_decode(out, q_nope, q_rope, latent, rope, w_uk, w_uv, cl, B, cap, H,
                                   dn, dr, dl, dv, float(scale), int(nthreads))
+    return out
+
+
+# ------------------------------------------------------------------------ KDA layer
+# Weight names as the reference's layer fixtures store them (tests/golden/kda_layer*.npz),
+# in the argument order of orc_kda_layer / K3KdaW.
+LAYER_WEIGHTS = ("q_proj", "k_proj", "v_proj", "q_conv", "k_conv", "v_conv", "f_a", "f_b",
+                 "A_log", "dt_bias", "b_proj", "g_proj", "o_norm", "o_proj")
+LAYER_PROJ = ("q_proj", "k_proj", "v_proj", "f_a", "f_b", "b_proj", "g_proj", "o_proj")
+
+
+def kda_layer(x, w, H, D, K, lb, eps, state=None):
+    """orc_kda_layer (restatement of k3_kda_layer, src/core/k3_ops.c:864-951) on x [T][E]
+    with fp32 weights `w` (LAYER_WEIGHTS). state: flat fp32 [H*D*D + 3*H*D*(K-1)], updated
+    in place, or None."""
+    x = _f32(x)
+    T, E = x.shape
+    out = np.zeros((T, E), np.float32)
+    args = [_f32(w[n]) for n in LAYER_WEIGHTS]
+    lib().orc_kda_layer(out, x, T, E, H, D, K, float(lb), float(eps), *args,
+                        None if state is None else state.ctypes.data)
+    return out
+
+
+def ref_kda_layer(x, w, H, D, K, lb, eps, state=None, wdt=0):
+    """The reference's own k3_kda_layer (oracle/_ref). wdt 1: the projection weights in `w`
+    are bf16 bit patterns (uint16), as the real checkpoint stores them."""
+    x = _f32(x)
+    T, E = x.shape
+    out = np.zeros((T, E), np.float32)
+    keep, args = [], []
+    for n in LAYER_WEIGHTS:
+        if n in LAYER_PROJ:
+            a = np.ascontiguousarray(w[n], np.uint16 if wdt == 1 else np.float32)
+            keep.append(a)
+            args.append(a.ctypes.data)
+        else:
+            args.append(_f32(w[n]))
+    ref().k3ref_kda_layer(out, x, T, E, H, D, K, float(lb), float(eps), *args, int(wdt),
+                          None if state is None else state.ctypes.data)
     return out
 
 

@@ -6,10 +6,12 @@
  * tests/unit/test_ops.c:324-337 and src/core/k3_ops.c:918-938 do, then calls the
  * reference's k3_kda_step once per (stream, token). Streams (sequence x head) run in
  * parallel on OpenMP threads, each in its own serial token order, as k3_kda_layer runs
- * its heads (k3_ops.c:927-938).
+ * its heads (k3_ops.c:927-938). k3ref_kda_layer fills the configuration and weight
+ * structs and calls the reference's k3_kda_layer once.
  */
 #include <math.h>
 #include <stdlib.h>
+#include <string.h>
 #ifdef _OPENMP
 #include <omp.h>
 #endif
@@ -83,4 +85,31 @@ int k3ref_max_threads(void)
 #else
     return 1;
 #endif
+}
+
+/* One k3_kda_layer call (src/core/k3_ops.c:864-951) on x [T][E]. The config fields it reads
+ * (hidden, kda_heads, kda_head_dim, conv_k, gate_lb, rms_eps) are set, the rest zero; the
+ * projection weights are fp32 (wdt 0) or bf16 bit patterns (wdt 1); state is the
+ * reference's layout (H*D*D recurrent, then 3*H*D*(K-1) conv) or NULL. */
+void k3ref_kda_layer(float *out, const float *x, int T, int E, int H, int D, int K,
+                     float lb, float eps, const void *Wq, const void *Wk, const void *Wv,
+                     const float *q_conv, const float *k_conv, const float *v_conv,
+                     const void *f_a, const void *f_b, const float *A_log,
+                     const float *dt_bias, const void *Wb, const void *Wg,
+                     const float *o_norm, const void *Wo, int wdt, float *state)
+{
+    K3Cfg c;
+    memset(&c, 0, sizeof c);
+    c.hidden = E; c.kda_heads = H; c.kda_head_dim = D; c.conv_k = K;
+    c.gate_lb = lb; c.rms_eps = eps;
+    K3KdaW w;
+    memset(&w, 0, sizeof w);
+    w.q = Wq; w.k = Wk; w.v = Wv;
+    w.q_conv = q_conv; w.k_conv = k_conv; w.v_conv = v_conv;
+    w.f_a = f_a; w.f_b = f_b; w.A_log = A_log; w.dt_bias = dt_bias;
+    w.b = Wb; w.g = Wg; w.o_norm = o_norm; w.o = Wo; w.wdt = wdt;
+    float *scratch = (float *)malloc(k3_kda_scratch(&c, T) * sizeof(float));
+    if (!scratch) abort();
+    k3_kda_layer(out, x, &w, &c, T, state, scratch);
+    free(scratch);
 }

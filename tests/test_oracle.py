@@ -99,6 +99,32 @@ def test_full_kda_layer_matches_reference_fixture(golden, name):
     assert close(state[: H * D * D], d["state_out"].ravel(), atol, rtol)
 
 
+@pytest.mark.skipif(not oracle.ref_available(), reason="oracle/_ref not built")
+@pytest.mark.parametrize("wdt", [0, 1])
+def test_kda_layer_bit_exact_with_reference_c(wdt):
+    """orc_kda_layer against the reference's own k3_kda_layer (compiled from its sources) on
+    a carried state: nonzero recurrent state and conv history, then calls of T = 1, 2 (both
+    shorter than the conv history), 5 and 9 tokens, every output and the whole state
+    bit-identical. wdt 1: bf16 projection weights (the real checkpoint's type) against the
+    restatement run on the same weights widened to fp32."""
+    rng = np.random.default_rng(40 + wdt)
+    E, H, D, K = 256, 2, 128, 4
+    w = W.kda_layer_weights(rng, E, H, D, K)
+    if wdt:
+        wr = {n: W.f32_to_bf16(w[n]) if n in oracle.LAYER_PROJ else w[n] for n in w}
+        w = {n: W.bf16_to_f32(wr[n]) if n in oracle.LAYER_PROJ else w[n] for n in w}
+    else:
+        wr = w
+    s_orc = (0.1 * rng.standard_normal(H * D * D + 3 * H * D * (K - 1))).astype(np.float32)
+    s_ref = s_orc.copy()
+    for T in (1, 2, 5, 9):
+        x = rng.standard_normal((T, E)).astype(np.float32)
+        a = oracle.kda_layer(x, w, H, D, K, -5.0, 1e-5, s_orc)
+        b = oracle.ref_kda_layer(x, wr, H, D, K, -5.0, 1e-5, s_ref, wdt=wdt)
+        assert np.array_equal(a, b), T
+        assert np.array_equal(s_orc, s_ref), T
+
+
 def test_absorbed_mla_matches_reference_expanded_cache(golden):
     """k3_mla_cached (expanded fp32 cache) vs the absorbed restatement, every causal prefix."""
     m = golden("mla_ref")
