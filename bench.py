@@ -15,6 +15,9 @@ Other workloads (for the per-path records; one JSON line each):
   varlen   BASELINE config 3: 16 sequences ~U[512,8192], H=64, heads sharded over the
            ranks, then the all-gather of the [sum T, 64*128] bf16 output (tokens/s)
   mla      BASELINE config 4: B=64, ctx 8192, 128 heads, latent 512 + rope 64 (tokens/s)
+  layer    the whole KDA layer forward (k3_kda_layer) at the model's shape: hidden 7168,
+           96 heads of 128, conv 4, bf16 projection weights; --tokens T per call (default
+           1: a decode step, weight streaming; e.g. 4096: a prefill chunk) (tokens/s)
 
 --impl reference times the reference's own C implementation (oracle/_ref/libk3ref.so:
 the unmodified k3_ops.c) on the host cores for the same workload; rank 0 only.
@@ -61,6 +64,28 @@ def mla_bytes(B, ctx, H):
 
 def mla_flops(B, ctx, H):
     return 2 * B * H * (128 * 512 + ctx * 576 + ctx * 512 + 512 * 128)
+
+
+LAYER_E, LAYER_H, LAYER_D, LAYER_K = 7168, 96, 128, 4
+
+
+def layer_weight_bytes(E, H, D):
+    P = H * D
+    return 2 * (4 * P * E + H * E + D * E + P * D + E * P)   # bf16 q,k,v,g,b,f_a,f_b,o
+
+
+def layer_bytes(T, E, H, D, K):
+    """HBM bytes one layer call must move at least: every weight once, the recurrent and
+    conv state read and written, x in and out (activations between steps excluded)."""
+    P = H * D
+    return (layer_weight_bytes(E, H, D) + 2 * (H * D * D + 3 * P * (K - 1)) * 4
+            + 2 * T * E * 4)
+
+
+def layer_flops(T, E, H, D):
+    """Projection FLOPs of one call (the recurrence adds < 3% at T = 4096)."""
+    P = H * D
+    return 2 * T * (4 * P * E + H * E + D * E + D * P + P * E)
 
 
 def peaks():
@@ -450,6 +475,142 @@ def bench_mla(args, D: Dist):
     return line
 
 
+# ------------------------------------------------------------------------ layer
+def layer_inputs(seed, T, E=LAYER_E, H=LAYER_H, D=LAYER_D, K=LAYER_K):
+    rng = np.random.default_rng(seed)
+    w = W.kda_layer_weights(rng, E, H, D, K, pool=1 << 22, bf16=True)
+    x = rng.standard_normal((T, E)).astype(np.float32)
+    state = (0.05 * rng.standard_normal(H * D * D + 3 * H * D * (K - 1))).astype(np.float32)
+    return w, x, state
+
+
+def bench_layer(args, D: Dist):
+    import k3cuda
+    ctx = k3cuda.Context(D.local)
+    E, H, Dh, K = LAYER_E, LAYER_H, LAYER_D, LAYER_K
+    T = args.tokens or 1
+    w, x, state = layer_inputs(D.rank, T)
+    dev = {}
+    for kn, on in zip(k3cuda.KDA_WEIGHT_NAMES, W.LAYER_WEIGHTS):
+        a = w[on]
+        if on in W.LAYER_PROJ:
+            dev[kn] = ctx.upload(a)  # bf16 bits
+        else:
+            dev[kn] = ctx.upload(np.ascontiguousarray(a.reshape(a.shape[0], -1) if a.ndim == 3
+                                                      else a))
+    del w
+    dS = ctx.upload(state)
+    dx = ctx.upload(x)
+    dout = ctx.empty((T, E), np.float32)
+    nws = ctx.kda_layer_workspace(T, E, H, Dh, K, k3cuda.BF16, k3cuda.BF16)
+    ws = ctx.empty((nws,), np.uint8)
+
+    def step():
+        ctx.kda_layer(dout, dx, dev, k3cuda.BF16, T, E, H, Dh, K, -5.0, 1e-5, dS, k3cuda.BF16,
+                      ws, nws)
+
+    for _ in range(args.warmup):
+        step()
+    ctx.sync()
+    clk = ClockSampler(D.local)
+    clk.start()
+    time.sleep(0.3)
+    D.barrier()
+    ctx.sync()
+    l0 = ctx.launches()
+    t0 = clk.mark()
+    ctx.record(0)
+    for _ in range(args.steps):
+        step()
+    ctx.record(1)
+    ctx.sync()
+    t1 = clk.mark()
+    D.barrier()
+    l1 = ctx.launches()
+    ms_max = D.max(ctx.elapsed_ms(0, 1))
+    clocks = clk.stop(t0, t1)
+
+    # e2e: x from page-locked host memory in, the layer output back, every step
+    hx = ctx.pinned((T, E), np.float32)
+    hx[...] = x
+    ho = ctx.pinned((T, E), np.float32)
+    L = k3cuda.lib()
+
+    def e2e_step():
+        k3cuda.check(L.k3cuda_memcpy_h2d(ctx.h, dx.ptr, hx.ctypes.data, hx.nbytes))
+        step()
+        k3cuda.check(L.k3cuda_memcpy_d2h(ctx.h, ho.ctypes.data, dout.ptr, ho.nbytes))
+
+    for _ in range(3):
+        e2e_step()
+    ctx.sync()
+    D.barrier()
+    ctx.record(2)
+    for _ in range(args.steps):
+        e2e_step()
+    ctx.record(3)
+    ctx.sync()
+    D.barrier()
+    ms_e2e = D.max(ctx.elapsed_ms(2, 3))
+
+    hbm, tf, src = peaks()
+    per = ms_max / 1e3 / args.steps
+    toks = T * args.steps * D.world
+    name = f"kda_layer_T{T}"
+    if T <= 8:
+        alg = layer_bytes(T, E, H, Dh, K)
+        roof = {"bound": "hbm", "achieved": alg / per / 1e9, "peak": hbm, "unit": "GB/s",
+                "frac": alg / per / 1e9 / hbm, "peak_source": src, "traffic": None,
+                "algorithmic_bytes_per_launch": alg}
+    else:
+        fl = layer_flops(T, E, H, Dh)
+        roof = {"bound": "tensor", "achieved": fl / per / 1e12, "peak": tf, "unit": "TFLOP/s",
+                "frac": fl / per / 1e12 / tf, "peak_source": src, "traffic": None,
+                "algorithmic_flops_per_launch": fl}
+    line = {
+        "metric": f"KDA layer forward tokens/s ({name}: hidden {E}, {H} heads x {Dh}, "
+                  f"bf16 weights)",
+        "value": toks / (ms_max / 1e3), "unit": "tokens/s", "n_gpus": D.world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_max / args.steps,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "fp32",
+        "data": "synthetic (seeded numpy weights and activations at the model's layer shape)",
+        "config": {"workload": name, "tokens_per_call": T, "hidden": E, "heads": H,
+                   "head_dim": Dh, "conv_k": K, "weights": "bf16",
+                   "recurrence_io": "bf16", "parallelism": f"replica x{D.world}",
+                   "l2": f"weights larger than L2 ({layer_weight_bytes(E, H, Dh) / 1e6:.0f} MB)"},
+        "e2e": {"value": toks / (ms_e2e / 1e3), "unit": "tokens/s", "h2d_bytes_per_step": hx.nbytes,
+                "d2h_bytes_per_step": ho.nbytes},
+        "roofline": roof,
+        "gpu_launches": int(l1 - l0),
+        "clocks": clocks,
+    }
+    ctx.close()
+    return line
+
+
+def cpu_layer_baseline(T, budget_s=10.0):
+    """The reference's own k3_kda_layer (oracle/_ref) with bf16 weights on all host cores,
+    on min(T, 16) tokens per call, repeated for about budget_s seconds."""
+    from oracle import oracle
+    if not oracle.ref_available():
+        return None
+    t = min(T, 16)
+    wr, x, state = layer_inputs(0, t)
+    E, H, Dh, K = LAYER_E, LAYER_H, LAYER_D, LAYER_K
+    oracle.ref_kda_layer(x, wr, H, Dh, K, -5.0, 1e-5, state, wdt=1)
+    calls, t0 = 0, time.perf_counter()
+    while True:
+        oracle.ref_kda_layer(x, wr, H, Dh, K, -5.0, 1e-5, state, wdt=1)
+        calls += 1
+        el = time.perf_counter() - t0
+        if el >= budget_s:
+            break
+    nth = oracle.ref().k3ref_max_threads()
+    return {"value": t * calls / el, "unit": "tokens/s", "cores": nth, "kind": "reference",
+            "sample": f"{calls} calls of the reference k3_kda_layer on {t} tokens each "
+                      f"(bf16 weights, OpenMP matmuls and heads)"}
+
+
 # -------------------------------------------------------------- reference arm
 def bench_reference(args, D: Dist):
     """The reference's own C (oracle/_ref/libk3ref.so, unmodified k3_ops.c) on the host
@@ -501,12 +662,13 @@ def main():
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=2000)
     ap.add_argument("--warmup", type=int, default=20)
-    ap.add_argument("--workload", default="decode", choices=["decode", "prefill", "varlen", "mla"])
+    ap.add_argument("--workload", default="decode",
+                    choices=["decode", "prefill", "varlen", "mla", "layer"])
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--tokens", type=int, default=None,
-                    help="prefill workload only: sequence length in place of config 2's 32768 "
-                         "(a small case for kernel profiling; not a headline number)")
+                    help="prefill: sequence length in place of config 2's 32768 (a small case "
+                         "for kernel profiling; not a headline number); layer: tokens per call")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     D = Dist()
@@ -519,11 +681,15 @@ def main():
         line = bench_decode(args, D)
     elif args.workload in ("prefill", "varlen"):
         line = bench_prefill(args, D, varlen=args.workload == "varlen")
+    elif args.workload == "layer":
+        line = bench_layer(args, D)
     else:
         line = bench_mla(args, D)
     if D.rank == 0:
         if args.workload == "decode" and D.world == 1 and not args.no_cpu_baseline:
             line["cpu_baseline"] = cpu_decode_baseline(DECODE_B, DECODE_H, DECODE_D)
+        if args.workload == "layer" and D.world == 1 and not args.no_cpu_baseline:
+            line["cpu_baseline"] = cpu_layer_baseline(args.tokens or 1)
         print(json.dumps(line), flush=True)
     D.close()
 

@@ -246,7 +246,7 @@ typedef struct {
  *          histories), updated in place; NULL = fresh sequence, nothing written back
  *   io_dtype  the recurrence's q, k, v and output type: K3CUDA_BF16 runs the prefill on
  *          the tensor cores (D == 128), K3CUDA_F32 keeps every operand fp32
- * Supported: E % 8 == 0, D % 16 == 0, D <= 128, 1 <= K <= 8. workspace d:
+ * Supported: E % 8 == 0, D % 16 == 0, D <= 128, 1 <= K <= 4. workspace d:
  * k3cuda_kda_layer_workspace() bytes, 256-byte aligned. */
 int k3cuda_kda_layer_workspace(int T, int E, int H, int D, int K, int wdt, int io_dtype,
                                size_t *bytes);

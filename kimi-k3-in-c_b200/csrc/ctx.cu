@@ -67,6 +67,9 @@ int k3cuda_init(int device, k3cuda_ctx **out) {
     cudaError_t e = cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking);
     for (int i = 0; e == cudaSuccess && i < K3CUDA_MAX_EVENTS; i++)
         e = cudaEventCreate(&c->events[i]);
+    if (e == cudaSuccess) e = cudaStreamCreateWithFlags(&c->aux, cudaStreamNonBlocking);
+    if (e == cudaSuccess) e = cudaEventCreateWithFlags(&c->ev_fork, cudaEventDisableTiming);
+    if (e == cudaSuccess) e = cudaEventCreateWithFlags(&c->ev_join, cudaEventDisableTiming);
     if (e == cudaSuccess) e = cudaMalloc((void **)&c->err_word, 256);
     if (e == cudaSuccess) e = cudaMemset(c->err_word, 0, 256);
     if (e != cudaSuccess) {
@@ -91,6 +94,9 @@ int k3cuda_shutdown(k3cuda_ctx *ctx) {
         if (ctx->events[i]) cudaEventDestroy(ctx->events[i]);
     if (ctx->flush_buf) cudaFree(ctx->flush_buf);
     if (ctx->err_word) cudaFree(ctx->err_word);
+    if (ctx->ev_fork) cudaEventDestroy(ctx->ev_fork);
+    if (ctx->ev_join) cudaEventDestroy(ctx->ev_join);
+    if (ctx->aux) cudaStreamDestroy(ctx->aux);
     cudaStreamDestroy(ctx->stream);
     free(ctx);
     return K3CUDA_OK;

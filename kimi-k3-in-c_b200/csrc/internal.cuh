@@ -27,6 +27,8 @@ struct k3cuda_ctx {
     int *sync_word;             // device int for the cross-rank ordering all-reduce
     void *peer_table;           // device copy of the peers' full-buffer addresses
     void *blas;                 // cuBLAS handle of the projections (kda_layer.cu), lazily made
+    cudaStream_t aux;           // side stream for work that overlaps the main stream's
+    cudaEvent_t ev_fork, ev_join;  // (forked from and joined back into `stream`)
 };
 
 namespace k3 {

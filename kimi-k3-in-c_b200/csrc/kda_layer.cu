@@ -80,14 +80,19 @@ static int blas_handle(k3cuda_ctx *ctx, cublasHandle_t *out) {
     return K3CUDA_OK;
 }
 
-__device__ __forceinline__ float dsigm(float x) { return 1.0f / (1.0f + expf(-x)); }
+// sigmoid with the fast exponential and divide intrinsics: within a few ulp of
+// 1 / (1 + expf(-x)) (the reference's sigmoidf_), and exactly 0 where exp(-x) overflows
+__device__ __forceinline__ float dsigm(float x) { return __fdividef(1.0f, 1.0f + __expf(-x)); }
 
 // ------------------------------------------------------------------- matvec_rows
 // y_s[t][r] = sum_i W_s[r][i] x[t][i] for up to MV_MAXSEG weight matrices W_s that share x
 // and `in`. A warp owns MV_ROWS rows and one of `ks` slices of `in`; its lanes read 16-byte
 // pieces (8 weights) of every row, so a warp load is 512 contiguous bytes per row. The `ks`
 // slices of a row group are summed through shared memory in a fixed order.
-constexpr int MV_THREADS = 256, MV_WARPS = 8, MV_ROWS = 4, MV_MAXT = 8, MV_MAXSEG = 8;
+constexpr int MV_THREADS = 256, MV_WARPS = 8, MV_MAXT = 8, MV_MAXSEG = 8;
+// rows per warp: 2 for one token (more warps in flight), 4 for more tokens (each x load
+// feeds more rows)
+template <int NT> constexpr int mv_rows() { return NT == 1 ? 2 : 4; }
 
 struct MatvecSeg {
     const void *W;  // [rows][in]
@@ -103,8 +108,16 @@ struct MatvecArgs {
     int ks;
 };
 
+// weights are read once per call: no L1 allocation, 256-byte L2 sectors
+__device__ __forceinline__ uint4 ld_stream(const void *p) {
+    uint4 r;
+    asm volatile("ld.global.nc.L1::no_allocate.L2::256B.v4.u32 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w) : "l"(p));
+    return r;
+}
+
 __device__ __forceinline__ void load8(const __nv_bfloat16 *p, float w[8]) {
-    const uint4 u = __ldcs(reinterpret_cast<const uint4 *>(p));
+    const uint4 u = ld_stream(p);
     const unsigned int q[4] = {u.x, u.y, u.z, u.w};
 #pragma unroll
     for (int j = 0; j < 4; j++) {
@@ -113,14 +126,16 @@ __device__ __forceinline__ void load8(const __nv_bfloat16 *p, float w[8]) {
     }
 }
 __device__ __forceinline__ void load8(const float *p, float w[8]) {
-    const float4 a = __ldcs(reinterpret_cast<const float4 *>(p));
-    const float4 b = __ldcs(reinterpret_cast<const float4 *>(p) + 1);
-    w[0] = a.x; w[1] = a.y; w[2] = a.z; w[3] = a.w;
-    w[4] = b.x; w[5] = b.y; w[6] = b.z; w[7] = b.w;
+    const uint4 a = ld_stream(p), b = ld_stream(p + 4);
+    w[0] = __uint_as_float(a.x); w[1] = __uint_as_float(a.y);
+    w[2] = __uint_as_float(a.z); w[3] = __uint_as_float(a.w);
+    w[4] = __uint_as_float(b.x); w[5] = __uint_as_float(b.y);
+    w[6] = __uint_as_float(b.z); w[7] = __uint_as_float(b.w);
 }
 
 template <int NT, typename WT>
 __global__ void __launch_bounds__(MV_THREADS) matvec_rows(const __grid_constant__ MatvecArgs a) {
+    constexpr int MV_ROWS = mv_rows<NT>();
     __shared__ float part[MV_WARPS][MV_ROWS * NT];
     int b = blockIdx.x, s = 0;
     while (s + 1 < a.nseg && b >= a.seg[s].blocks) b -= a.seg[s++].blocks;
@@ -196,18 +211,20 @@ static int matvec(k3cuda_ctx *ctx, const float *x, int T, int in, const Proj *p,
     a.x = x;
     a.in = in;
     const int n8 = in / 8;
+    const int R = T == 1 ? mv_rows<1>() : mv_rows<2>();
     auto blocks_for = [&](int ks) {
         long long tot = 0;
-        const int per_block = (MV_WARPS / ks) * MV_ROWS;
+        const int per_block = (MV_WARPS / ks) * R;
         for (int i = 0; i < n; i++) tot += (p[i].rows + per_block - 1) / per_block;
         return tot;
     };
-    // split `in` over more warps only while the grid is short of two waves and every
-    // slice still gives each lane at least one 16-byte piece
+    // split `in` over up to 4 warps while the grid is short of about 8 blocks per SM (a
+    // measured optimum for streaming) and every slice still gives each lane at least two
+    // 16-byte pieces
     int ks = 1;
-    while (ks < MV_WARPS && blocks_for(ks) < 2LL * ctx->sm_count && n8 / (2 * ks) >= 32) ks *= 2;
+    while (ks < 4 && blocks_for(ks) < 8LL * ctx->sm_count && n8 / (2 * ks) >= 64) ks *= 2;
     a.ks = ks;
-    const int per_block = (MV_WARPS / ks) * MV_ROWS;
+    const int per_block = (MV_WARPS / ks) * R;
     long long tot = 0;
     for (int i = 0; i < n; i++) {
         a.seg[i] = MatvecSeg{p[i].W, p[i].y, p[i].rows, (p[i].rows + per_block - 1) / per_block};
@@ -274,17 +291,86 @@ static int gemm(k3cuda_ctx *ctx, float *y, const float *x, const __nv_bfloat16 *
     return K3CUDA_OK;
 }
 
+// ------------------------------------------------------------ vector lane access
+// A lane holds CPL consecutive channels of a head (D = 32 CPL, or D = 16 with lanes 16-31
+// idle), moved with one CPL-wide load or store.
+template <int CPL> struct fvec;
+template <> struct fvec<1> {
+    static __device__ __forceinline__ void ld(float v[1], const float *p) { v[0] = __ldg(p); }
+    static __device__ __forceinline__ void st(float *p, const float v[1]) { *p = v[0]; }
+};
+template <> struct fvec<2> {
+    static __device__ __forceinline__ void ld(float v[2], const float *p) {
+        const float2 t = __ldg(reinterpret_cast<const float2 *>(p));
+        v[0] = t.x; v[1] = t.y;
+    }
+    static __device__ __forceinline__ void st(float *p, const float v[2]) {
+        *reinterpret_cast<float2 *>(p) = make_float2(v[0], v[1]);
+    }
+};
+template <> struct fvec<4> {
+    static __device__ __forceinline__ void ld(float v[4], const float *p) {
+        const float4 t = __ldg(reinterpret_cast<const float4 *>(p));
+        v[0] = t.x; v[1] = t.y; v[2] = t.z; v[3] = t.w;
+    }
+    static __device__ __forceinline__ void st(float *p, const float v[4]) {
+        *reinterpret_cast<float4 *>(p) = make_float4(v[0], v[1], v[2], v[3]);
+    }
+};
+// the same for the recurrence's io type (fp32, or bf16 packed in pairs)
+template <typename IO, int CPL> struct iovec {
+    static __device__ __forceinline__ void ld(float v[CPL], const IO *p) { fvec<CPL>::ld(v, p); }
+    static __device__ __forceinline__ void st(IO *p, const float v[CPL]) { fvec<CPL>::st(p, v); }
+};
+template <int CPL> struct iovec<__nv_bfloat16, CPL> {
+    static __device__ __forceinline__ void ld(float v[CPL], const __nv_bfloat16 *p) {
+        if constexpr (CPL == 1) {
+            v[0] = __bfloat162float(*p);
+        } else {
+            unsigned int u[CPL / 2];
+            if constexpr (CPL == 2) u[0] = *reinterpret_cast<const unsigned int *>(p);
+            else { const uint2 t = *reinterpret_cast<const uint2 *>(p); u[0] = t.x; u[1] = t.y; }
+#pragma unroll
+            for (int m = 0; m < CPL / 2; m++) {
+                v[2 * m] = __uint_as_float(u[m] << 16);
+                v[2 * m + 1] = __uint_as_float(u[m] & 0xffff0000u);
+            }
+        }
+    }
+    static __device__ __forceinline__ void st(__nv_bfloat16 *p, const float v[CPL]) {
+        if constexpr (CPL == 1) {
+            *p = __float2bfloat16_rn(v[0]);
+        } else {
+            unsigned int u[CPL / 2];
+#pragma unroll
+            for (int m = 0; m < CPL / 2; m++) {
+                const __nv_bfloat162 b2 = __floats2bfloat162_rn(v[2 * m], v[2 * m + 1]);
+                u[m] = *reinterpret_cast<const unsigned int *>(&b2);
+            }
+            if constexpr (CPL == 2) *reinterpret_cast<unsigned int *>(p) = u[0];
+            else *reinterpret_cast<uint2 *>(p) = make_uint2(u[0], u[1]);
+        }
+    }
+};
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+    for (int o = 16; o; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+}
+
 // ------------------------------------------------------------------ kda_layer_pre
 // Grid (token tiles of LT, H, 4). z = 0, 1, 2: ShortConv + SiLU of the raw q, k, v
 // projections of head h (k3_shortconv, k3_ops.c:133-165: taps oldest..newest, w[K-1] on the
 // current input), then for q and k the L2 norm over the head's D channels (l2norm_,
 // :845-851). z = 3: the decay chain g = lb * sigmoid(exp(A_log[h]) (z + dt_bias))
 // (k3_kda_decay, :167-183, kept as log-decay) and beta = sigmoid(b x) (:902-903).
-// A block stages the raw rows t0-K+1 .. t0+LT-1 of its head (older rows from the conv
-// history) and the conv taps in shared memory; warps take tokens, lanes take channels. The
-// block of the first tile, which alone reads the old history, writes the new one (the raw
-// inputs of the last K-1 tokens) after its staging.
-constexpr int LT = 32, LAYER_THREADS = 256;
+// Each warp owns TPW consecutive tokens and slides a window of K-1 + TPW raw rows through
+// registers: K-1 history rows (older ones from the carried conv history) and its TPW rows,
+// every load issued before the arithmetic. Lanes hold CPL channels each. The warp that owns
+// token 0 is the only reader of the old conv history; it also writes the new one (the raw
+// inputs of tokens T-K+1 .. T-1), after its reads.
+constexpr int TPW = 8, LAYER_WARPS = 8, LT = TPW * LAYER_WARPS, LAYER_THREADS = 32 * LAYER_WARPS;
 
 template <typename IO>
 struct PreArgs {
@@ -297,128 +383,162 @@ struct PreArgs {
     IO *out[3];          // recurrence q, k, v [T][P]
     float *g;            // log decay [T][P]
     float *beta;         // [T][H]
-    int T, H, D, K;
+    int T, H, D;
     float lb;
 };
 
-template <typename IO, int CPL>
+template <typename IO, int CPL, int K>
 __global__ void __launch_bounds__(LAYER_THREADS) kda_layer_pre(const __grid_constant__ PreArgs<IO> a) {
-    extern __shared__ float sm[];
-    const int s = blockIdx.z, h = blockIdx.y, t0 = blockIdx.x * LT;
-    const int D = a.D, P = a.H * D, K = a.K, hist = K - 1;
+    constexpr int HIST = K - 1;
+    const int s = blockIdx.z, h = blockIdx.y;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int nt = min(LT, a.T - t0);
+    const int t_a = blockIdx.x * LT + warp * TPW;
+    const int D = a.D, P = a.H * D, c0 = lane * CPL;
+    if (t_a >= a.T) return;  // whole warps only: no block-level synchronisation below
+    const int nt = min(TPW, a.T - t_a);
+    const bool on = c0 < D;  // lanes past the head's channels stay for the L2 reduction
+    const size_t col = (size_t)h * D + (on ? c0 : 0);
     if (s == 3) {
+        if (lane < nt) {
+            const size_t i = (size_t)(t_a + lane) * a.H + h;
+            a.beta[i] = dsigm(a.yb[i]);
+        }
+        if (!on) return;
+        float dt[CPL], zv[TPW][CPL];
+        fvec<CPL>::ld(dt, a.dt_bias + col);
+#pragma unroll
+        for (int tt = 0; tt < TPW; tt++)
+            if (tt < nt) fvec<CPL>::ld(zv[tt], a.z + (size_t)(t_a + tt) * P + col);
         const float ea = expf(a.A_log[h]);
-        for (int tt = warp; tt < nt; tt += LAYER_THREADS / 32) {
-            const size_t row = (size_t)(t0 + tt) * P + (size_t)h * D;
-            for (int c = lane; c < D; c += 32)
-                a.g[row + c] = a.lb * dsigm(ea * (a.z[row + c] + a.dt_bias[h * D + c]));
-            if (lane == 0) {
-                const size_t i = (size_t)(t0 + tt) * a.H + h;
-                a.beta[i] = dsigm(a.yb[i]);
+#pragma unroll
+        for (int tt = 0; tt < TPW; tt++) {
+            if (tt < nt) {
+                float gv[CPL];
+#pragma unroll
+                for (int m = 0; m < CPL; m++) gv[m] = a.lb * dsigm(ea * (zv[tt][m] + dt[m]));
+                fvec<CPL>::st(a.g + (size_t)(t_a + tt) * P + col, gv);
             }
         }
         return;
     }
-    float *raw = sm;                   // [nt + hist][D]: row r is token t0 - hist + r
-    float *cw = sm + (LT + hist) * D;  // [K][D]
-    const float *y = a.y[s];
-    float *hs = a.hist ? a.hist + ((size_t)s * P + (size_t)h * D) * hist : nullptr;  // [D][hist]
-    const int rows = nt + hist;
-    for (int i = threadIdx.x; i < rows * D; i += LAYER_THREADS) {
-        const int r = i / D, c = i - r * D, tok = t0 - hist + r;
-        float v = 0.f;
-        if (tok >= 0) v = y[(size_t)tok * P + (size_t)h * D + c];
-        else if (hs) v = hs[(size_t)c * hist + (tok + hist)];
-        raw[i] = v;
-    }
-    for (int i = threadIdx.x; i < D * K; i += LAYER_THREADS) {
-        const int c = i / K, j = i - c * K;
-        cw[j * D + c] = a.cw[s][(size_t)h * D * K + i];
-    }
-    __syncthreads();
-    if (blockIdx.x == 0 && hs) {
-        for (int i = threadIdx.x; i < D * hist; i += LAYER_THREADS) {
-            const int c = i / hist, j = i - c * hist, tok = a.T - hist + j;
-            hs[i] = tok < nt ? raw[(tok + hist) * D + c] : y[(size_t)tok * P + (size_t)h * D + c];
+    const float *y = a.y[s] + col;
+    float *hs = (HIST > 0 && a.hist) ? a.hist + ((size_t)s * P + col) * HIST : nullptr;  // [CPL][HIST]
+    // rows[r] = raw input of token t_a - HIST + r
+    float rows[HIST + TPW][CPL];
+#pragma unroll
+    for (int r = 0; r < HIST + TPW; r++) {
+        const int tok = t_a - HIST + r;
+        if (tok >= 0) {
+            if (tok < t_a + nt) fvec<CPL>::ld(rows[r], y + (size_t)tok * P);
+        } else {
+#pragma unroll
+            for (int m = 0; m < CPL; m++) rows[r][m] = hs ? hs[m * HIST + (tok + HIST)] : 0.f;
         }
     }
-    IO *out = a.out[s];
-    for (int tt = warp; tt < nt; tt += LAYER_THREADS / 32) {
+    float wt[K][CPL];
+#pragma unroll
+    for (int m = 0; m < CPL; m++)
+#pragma unroll
+        for (int j = 0; j < K; j++) wt[j][m] = __ldg(a.cw[s] + (col + m) * K + j);
+    if (t_a == 0 && hs && on) {
+        // the new history: tokens T-HIST .. T-1, older than token 0 from the old history.
+        // Slot j is written after slot T+j > j is read, so the shift is in place.
+#pragma unroll
+        for (int j = 0; j < HIST; j++) {
+            const int tok = a.T - HIST + j;
+            float v[CPL];
+            if (tok >= 0) {
+                fvec<CPL>::ld(v, y + (size_t)tok * P);
+            } else {
+#pragma unroll
+                for (int m = 0; m < CPL; m++) v[m] = hs[m * HIST + (tok + HIST)];
+            }
+#pragma unroll
+            for (int m = 0; m < CPL; m++) hs[m * HIST + j] = v[m];
+        }
+    }
+    IO *out = a.out[s] + col;
+#pragma unroll
+    for (int tt = 0; tt < TPW; tt++) {
+        if (tt >= nt) continue;
         float v[CPL], ss = 0.f;
 #pragma unroll
         for (int m = 0; m < CPL; m++) {
-            const int c = lane + 32 * m;
-            v[m] = 0.f;
-            if (c < D) {
-                float acc = cw[hist * D + c] * raw[(tt + hist) * D + c];
-                for (int j = 0; j < hist; j++) acc += cw[j * D + c] * raw[(tt + j) * D + c];
-                v[m] = acc * dsigm(acc);
-                ss += v[m] * v[m];
-            }
+            float acc = wt[HIST][m] * rows[tt + HIST][m];
+#pragma unroll
+            for (int j = 0; j < HIST; j++) acc += wt[j][m] * rows[tt + j][m];
+            v[m] = acc * dsigm(acc);
+            ss += on ? v[m] * v[m] : 0.f;
         }
         if (s < 2) {
-#pragma unroll
-            for (int o = 16; o; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
-            const float inv = 1.0f / sqrtf(ss + 1e-6f);
+            const float inv = 1.0f / sqrtf(warp_sum(ss) + 1e-6f);
 #pragma unroll
             for (int m = 0; m < CPL; m++) v[m] *= inv;
         }
-        const size_t row = (size_t)(t0 + tt) * P + (size_t)h * D;
-#pragma unroll
-        for (int m = 0; m < CPL; m++) {
-            const int c = lane + 32 * m;
-            if (c < D) io<IO>::st(out + row + c, v[m]);
-        }
+        if (on) iovec<IO, CPL>::st(out + (size_t)(t_a + tt) * P, v);
     }
 }
 
 // ----------------------------------------------------------------- kda_layer_post
-// ot = RMSNorm_head(o) * o_norm * sigmoid(g x) (k3_rmsnorm per head then the gate,
-// k3_ops.c:941-947), optionally also split into bf16 hi/lo for the o_proj GEMM.
+// ot = RMSNorm_head(o) * o_norm * sigmoid(g x) (k3_rmsnorm per head, then the gate,
+// k3_ops.c:941-947), written as fp32 (the matvec input) and/or as the bf16 hi/lo split (the
+// GEMM input). Warps own TPW tokens of one head, lanes CPL channels; loads first.
 template <typename IO>
 struct PostArgs {
     const IO *o;       // recurrence output [T][P]
     const float *gb;   // gate logits [T][P]
     const float *w;    // o_norm [D]
-    float *ot;         // [T][P]
-    __nv_bfloat16 *hi, *lo;
+    float *ot;         // [T][P], or null
+    __nv_bfloat16 *hi, *lo;  // [T][P] each, or null
     int T, H, D;
     float eps;
 };
 
 template <typename IO, int CPL>
 __global__ void __launch_bounds__(LAYER_THREADS) kda_layer_post(const __grid_constant__ PostArgs<IO> a) {
-    const int h = blockIdx.y, t0 = blockIdx.x * LT;
-    const int D = a.D, P = a.H * D;
+    const int h = blockIdx.y;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int nt = min(LT, a.T - t0);
-    for (int tt = warp; tt < nt; tt += LAYER_THREADS / 32) {
-        const size_t row = (size_t)(t0 + tt) * P + (size_t)h * D;
-        float v[CPL], ss = 0.f;
+    const int t_a = blockIdx.x * LT + warp * TPW;
+    const int D = a.D, P = a.H * D, c0 = lane * CPL;
+    if (t_a >= a.T) return;
+    const bool on = c0 < D;  // idle lanes still take part in the reductions
+    const int nt = min(TPW, a.T - t_a);
+    const size_t col = (size_t)h * D + (on ? c0 : 0);
+    float wn[CPL], ov[TPW][CPL], gv[TPW][CPL];
+    fvec<CPL>::ld(wn, a.w + (on ? c0 : 0));
 #pragma unroll
-        for (int m = 0; m < CPL; m++) {
-            const int c = lane + 32 * m;
-            v[m] = c < D ? io<IO>::ld(a.o + row + c) : 0.f;
-            ss += v[m] * v[m];
+    for (int tt = 0; tt < TPW; tt++) {
+        if (tt < nt) {
+            const size_t row = (size_t)(t_a + tt) * P + col;
+            iovec<IO, CPL>::ld(ov[tt], a.o + row);
+            fvec<CPL>::ld(gv[tt], a.gb + row);
         }
+    }
 #pragma unroll
-        for (int o = 16; o; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
-        const float inv = 1.0f / sqrtf(ss / (float)D + a.eps);
+    for (int tt = 0; tt < TPW; tt++) {
+        if (tt >= nt) continue;
+        float ss = 0.f;
+#pragma unroll
+        for (int m = 0; m < CPL; m++) ss += on ? ov[tt][m] * ov[tt][m] : 0.f;
+        const float inv = 1.0f / sqrtf(warp_sum(ss) / (float)D + a.eps);
+        if (!on) continue;
+        float r[CPL];
 #pragma unroll
         for (int m = 0; m < CPL; m++) {
-            const int c = lane + 32 * m;
-            if (c < D) {
-                float r = a.w[c] * v[m] * inv;
-                r *= dsigm(a.gb[row + c]);
-                a.ot[row + c] = r;
-                if (a.hi) {
-                    const __nv_bfloat16 hb = __float2bfloat16_rn(r);
-                    a.hi[row + c] = hb;
-                    a.lo[row + c] = __float2bfloat16_rn(r - __bfloat162float(hb));
-                }
+            r[m] = wn[m] * ov[tt][m] * inv;
+            r[m] *= dsigm(gv[tt][m]);
+        }
+        const size_t row = (size_t)(t_a + tt) * P + col;
+        if (a.ot) fvec<CPL>::st(a.ot + row, r);
+        if (a.hi) {
+            float hv[CPL], lv[CPL];
+#pragma unroll
+            for (int m = 0; m < CPL; m++) {
+                hv[m] = __bfloat162float(__float2bfloat16_rn(r[m]));
+                lv[m] = r[m] - hv[m];
             }
+            iovec<__nv_bfloat16, CPL>::st(a.hi + row, hv);
+            iovec<__nv_bfloat16, CPL>::st(a.lo + row, lv);
         }
     }
 }
@@ -476,10 +596,27 @@ static int layer_shape_ok(int T, int E, int H, int D, int K, int wdt, int io_dty
     K3_ARG_CHECK(wdt == K3CUDA_F32 || wdt == K3CUDA_BF16, "kda_layer: bad wdt %d", wdt);
     K3_ARG_CHECK(io_dtype == K3CUDA_F32 || io_dtype == K3CUDA_BF16, "kda_layer: bad io_dtype %d",
                  io_dtype);
-    if (E % 8 || D % 16 || D > 128 || K > 8)
+    if (E % 8 || D % 16 || D > 128 || K > 4)
         return set_error(K3CUDA_ERR_UNSUPPORTED, "kda_layer: E=%d D=%d K=%d not built (E %% 8 "
-                         "== 0, D %% 16 == 0, D <= 128, K <= 8)", E, D, K);
+                         "== 0, D %% 16 == 0, D <= 128, K <= 4)", E, D, K);
     return K3CUDA_OK;
+}
+
+template <typename IO, int CPL>
+static void launch_pre_k(const PreArgs<IO> &a, int K, dim3 grid, cudaStream_t st) {
+    switch (K) {
+        case 1: kda_layer_pre<IO, CPL, 1><<<grid, LAYER_THREADS, 0, st>>>(a); break;
+        case 2: kda_layer_pre<IO, CPL, 2><<<grid, LAYER_THREADS, 0, st>>>(a); break;
+        case 3: kda_layer_pre<IO, CPL, 3><<<grid, LAYER_THREADS, 0, st>>>(a); break;
+        default: kda_layer_pre<IO, CPL, 4><<<grid, LAYER_THREADS, 0, st>>>(a); break;
+    }
+}
+
+template <typename IO>
+static void launch_pre(const PreArgs<IO> &a, int D, int K, dim3 grid, cudaStream_t st) {
+    if (D <= 32) launch_pre_k<IO, 1>(a, K, grid, st);
+    else if (D <= 64) launch_pre_k<IO, 2>(a, K, grid, st);
+    else launch_pre_k<IO, 4>(a, K, grid, st);
 }
 
 // One projection: matvec (T <= 8) or GEMM; xs is x's bf16 split when the GEMM needs it.
@@ -506,10 +643,23 @@ static int layer_core(k3cuda_ctx *ctx, float *out, const float *x, const k3cuda_
     __nv_bfloat16 *fas = pl.split ? (__nv_bfloat16 *)(ws + pl.fas) : nullptr;
     int rc;
     // 1. projections (and the gate's g x, which reads the same x)
+    bool forked = false;
     if (!pl.gemm_path) {
-        const Proj first[6] = {{w->q, yq, P}, {w->k, yk, P}, {w->v, yv, P},
-                               {w->g, gb, P}, {w->b, yb, H}, {w->f_a, fa, D}};
-        if ((rc = matvec(ctx, x, T, E, first, 6, wdt))) return rc;
+        const Proj first[5] = {{w->q, yq, P}, {w->k, yk, P}, {w->v, yv, P},
+                               {w->b, yb, H}, {w->f_a, fa, D}};
+        if ((rc = matvec(ctx, x, T, E, first, 5, wdt))) return rc;
+        // The gate projection (needed at step 8) streams on the side stream while the chain
+        // of small kernels of steps 2-6 runs on the main one.
+        K3_CUDA_TRY(cudaEventRecord(ctx->ev_fork, ctx->stream));
+        K3_CUDA_TRY(cudaStreamWaitEvent(ctx->aux, ctx->ev_fork, 0));
+        cudaStream_t main_stream = ctx->stream;
+        ctx->stream = ctx->aux;
+        const Proj gate{w->g, gb, P};
+        rc = matvec(ctx, x, T, E, &gate, 1, wdt);
+        ctx->stream = main_stream;
+        if (rc) return rc;
+        K3_CUDA_TRY(cudaEventRecord(ctx->ev_join, ctx->aux));
+        forked = true;
     } else {
         if (pl.split && (rc = split(ctx, xs, x, (long long)T * E))) return rc;
         const Proj first[6] = {{w->q, yq, P}, {w->k, yk, P}, {w->v, yv, P},
@@ -528,12 +678,9 @@ static int layer_core(k3cuda_ctx *ctx, float *out, const float *x, const k3cuda_
         a.z = z; a.yb = yb; a.A_log = w->A_log; a.dt_bias = w->dt_bias;
         a.out[0] = rq; a.out[1] = rk; a.out[2] = rv;
         a.g = g; a.beta = beta;
-        a.T = T; a.H = H; a.D = D; a.K = K; a.lb = lb;
-        const size_t smem = ((size_t)(LT + hist) * D + (size_t)K * D) * sizeof(float);
+        a.T = T; a.H = H; a.D = D; a.lb = lb;
         dim3 grid((unsigned)((T + LT - 1) / LT), (unsigned)H, 4);
-        if (D <= 32) kda_layer_pre<IO, 1><<<grid, LAYER_THREADS, smem, ctx->stream>>>(a);
-        else if (D <= 64) kda_layer_pre<IO, 2><<<grid, LAYER_THREADS, smem, ctx->stream>>>(a);
-        else kda_layer_pre<IO, 4><<<grid, LAYER_THREADS, smem, ctx->stream>>>(a);
+        launch_pre(a, D, K, grid, ctx->stream);
         if ((rc = after_launch(ctx, "kda_layer_pre"))) return rc;
     }
     // 6. recurrence
@@ -558,11 +705,12 @@ static int layer_core(k3cuda_ctx *ctx, float *out, const float *x, const k3cuda_
         if (rc) return rc;
     }
     // 7/8. head RMSNorm, then the gate (ot reuses yq, its split reuses yk)
+    if (forked) K3_CUDA_TRY(cudaStreamWaitEvent(ctx->stream, ctx->ev_join, 0));
     float *ot = yq;
     __nv_bfloat16 *ots = pl.split ? (__nv_bfloat16 *)yk : nullptr;
     {
         PostArgs<IO> a{};
-        a.o = o; a.gb = gb; a.w = w->o_norm; a.ot = ot;
+        a.o = o; a.gb = gb; a.w = w->o_norm; a.ot = pl.split ? nullptr : ot;
         a.hi = ots; a.lo = ots ? ots + (size_t)T * P : nullptr;
         a.T = T; a.H = H; a.D = D; a.eps = eps;
         dim3 grid((unsigned)((T + LT - 1) / LT), (unsigned)H);
@@ -634,10 +782,11 @@ extern "C" int k3cuda_kda_layer(k3cuda_ctx *ctx, float *out, const float *x,
     K3_ARG_CHECK(out && x && w->q && w->k && w->v && w->q_conv && w->k_conv && w->v_conv &&
                  w->f_a && w->f_b && w->A_log && w->dt_bias && w->b && w->g && w->o_norm &&
                  w->o, "kda_layer: null pointer");
-    const void *vec[] = {out, x, w->q, w->k, w->v, w->f_a, w->f_b, w->b, w->g, w->o};
+    const void *vec[] = {out, x, w->q, w->k, w->v, w->f_a, w->f_b, w->b, w->g, w->o,
+                         w->dt_bias, w->o_norm};
     for (const void *p : vec)
-        K3_ARG_CHECK(aligned(p, 16), "kda_layer: x, out and the projection weights must be "
-                     "16-byte aligned");
+        K3_ARG_CHECK(aligned(p, 16), "kda_layer: x, out, the projection weights, dt_bias and "
+                     "o_norm must be 16-byte aligned");
     K3_ARG_CHECK(aligned(state, 16), "kda_layer: state must be 16-byte aligned");
     LayerPlan pl;
     if ((rc = plan_layer(T, E, H, D, K, w->wdt, io_dtype, &pl))) return rc;

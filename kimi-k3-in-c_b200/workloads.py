@@ -122,18 +122,35 @@ def mla_config4(seed: int = 0, B: int = 64, ctx: int = 8192, H: int = 128, dn: i
     return out
 
 
-def kda_layer_weights(rng, E: int, H: int, D: int, K: int = 4) -> dict:
-    """Random fp32 weights of one KDA layer under the reference fixtures' names and shapes
+# KDA layer weight names as the reference's layer fixtures store them, in K3KdaW's field
+# order (include/k3/k3.h:449-463), and the projections among them (the wdt-tagged ones).
+LAYER_WEIGHTS = ("q_proj", "k_proj", "v_proj", "q_conv", "k_conv", "v_conv", "f_a", "f_b",
+                 "A_log", "dt_bias", "b_proj", "g_proj", "o_norm", "o_proj")
+LAYER_PROJ = ("q_proj", "k_proj", "v_proj", "f_a", "f_b", "b_proj", "g_proj", "o_proj")
+
+
+def kda_layer_weights(rng, E: int, H: int, D: int, K: int = 4, pool: int = 0,
+                      bf16: bool = False) -> dict:
+    """Random weights of one KDA layer under the reference fixtures' names and shapes
     (tests/golden/kda_layer*.npz): entries N(0, 0.3) at fan-in 128, scaled by
     sqrt(128 / fan-in) so activations keep the fixtures' magnitude at any width; A_log in
-    [-0.4, 1.2], dt_bias N(0.1, 0.45), o_norm 1 + N(0, 0.1)."""
+    [-0.4, 1.2], dt_bias N(0.1, 0.45), o_norm 1 + N(0, 0.1). bf16: the projections are
+    returned as bf16 bit patterns. pool > 0: each projection repeats one draw of `pool`
+    values (model-size weights in seconds, for timing runs)."""
     P = H * D
-    f = lambda *s: rng.standard_normal(s).astype(np.float32)  # noqa: E731
-    sc = lambda fan: np.float32(0.3 * np.sqrt(128.0 / fan))  # noqa: E731
+    f = lambda *s: rng.standard_normal(s, dtype=np.float32)  # noqa: E731
+
+    def proj(rows, fan):
+        n = rows * fan
+        a = f(min(pool, n) if pool else n) * np.float32(0.3 * np.sqrt(128.0 / fan))
+        if bf16:
+            a = f32_to_bf16(a)
+        return np.resize(a, (rows, fan)) if pool else a.reshape(rows, fan)
+
     return {
-        "q_proj": f(P, E) * sc(E), "k_proj": f(P, E) * sc(E), "v_proj": f(P, E) * sc(E),
-        "g_proj": f(P, E) * sc(E), "o_proj": f(E, P) * sc(P), "f_a": f(D, E) * sc(E),
-        "f_b": f(P, D) * sc(D), "b_proj": f(H, E) * sc(E),
+        "q_proj": proj(P, E), "k_proj": proj(P, E), "v_proj": proj(P, E),
+        "g_proj": proj(P, E), "o_proj": proj(E, P), "f_a": proj(D, E),
+        "f_b": proj(P, D), "b_proj": proj(H, E),
         "q_conv": f(P, 1, K) * np.float32(0.3), "k_conv": f(P, 1, K) * np.float32(0.3),
         "v_conv": f(P, 1, K) * np.float32(0.3),
         "A_log": rng.uniform(-0.4, 1.2, H).astype(np.float32),
