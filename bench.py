@@ -15,6 +15,9 @@ Other workloads (for the per-path records; one JSON line each):
   varlen   BASELINE config 3: 16 sequences ~U[512,8192], H=64, heads sharded over the
            ranks, then the all-gather of the [sum T, 64*128] bf16 output (tokens/s)
   mla      BASELINE config 4: B=64, ctx 8192, 128 heads, latent 512 + rope 64 (tokens/s)
+  mla_prefill  causal MLA prefill chunk over the latent cache: --tokens T (default 4096)
+           new tokens of one sequence appended to the cache (kv_a_norm rows) and attended
+           causally from position 0, 128 heads (tokens/s)
   layer    the whole KDA layer forward (k3_kda_layer) at the model's shape: hidden 7168,
            96 heads of 128, conv 4, bf16 projection weights; --tokens T per call (default
            1: a decode step, weight streaming; e.g. 4096: a prefill chunk) (tokens/s)
@@ -611,6 +614,114 @@ def cpu_layer_baseline(T, budget_s=10.0):
                       f"(bf16 weights, OpenMP matmuls and heads)"}
 
 
+# ------------------------------------------------------------------ mla prefill
+def mla_prefill_flops(T, H):
+    """Absorbed-form FLOPs of a causal chunk from position 0: scores over 576 dims and the
+    latent accumulation over 512 per (head, query, key), plus W_UK / W_UV absorption."""
+    pairs = T * (T + 1) // 2
+    return 2 * H * pairs * (576 + 512) + 2 * 2 * T * H * 128 * 512
+
+
+def bench_mla_prefill(args, D: Dist):
+    import k3cuda
+    ctx = k3cuda.Context(D.local)
+    T, H = args.tokens or 4096, 128
+    cap = T
+    c = W.mla_config4(seed=D.rank, B=1, ctx=cap, H=H)
+    rng = np.random.default_rng(D.rank + 11)
+    qn = W.f32_to_bf16(rng.standard_normal((T, H, 128), dtype=np.float32))
+    qr = W.f32_to_bf16(rng.standard_normal((T, H, 64), dtype=np.float32))
+    ct = rng.standard_normal((T, 576), dtype=np.float32)
+    wn = (1.0 + 0.1 * rng.standard_normal(512)).astype(np.float32)
+    d_qn, d_qr, d_ct, d_wn = ctx.upload(qn), ctx.upload(qr), ctx.upload(ct), ctx.upload(wn)
+    d_lat, d_rope = ctx.upload(c["latent"]), ctx.upload(c["rope"])
+    d_uk, d_uv = ctx.upload(c["w_uk"]), ctx.upload(c["w_uv"])
+    seq = np.zeros(T, np.int32)
+    lens = (np.arange(T) + 1).astype(np.int32)
+    out = ctx.empty((T, H, 128), np.uint16)
+    nws = ctx.mla_decode_workspace(lens, H)
+    ws = ctx.empty((nws,), np.uint8)
+
+    def step():
+        ctx.mla_cache_append(d_lat, d_rope, d_ct, d_wn, 1e-5, 0, 0, T, 1, cap)
+        ctx.mla_attend(out, d_qn, d_qr, d_lat, d_rope, d_uk, d_uv, seq, lens, 1, cap, H,
+                       c["scale"], ws, nws, out_dtype=k3cuda.BF16)
+
+    for _ in range(args.warmup):
+        step()
+    ctx.sync()
+    clk = ClockSampler(D.local)
+    clk.start()
+    time.sleep(0.3)
+    D.barrier()
+    ctx.sync()
+    l0 = ctx.launches()
+    t0 = clk.mark()
+    ctx.record(0)
+    for _ in range(args.steps):
+        ctx.flush_l2()
+        step()
+    ctx.record(1)
+    ctx.sync()
+    t1 = clk.mark()
+    D.barrier()
+    l1 = ctx.launches()
+    ms_max = D.max(ctx.elapsed_ms(0, 1))
+    clocks = clk.stop(t0, t1)
+
+    hq, hr, hc = ctx.pinned(qn.shape, np.uint16), ctx.pinned(qr.shape, np.uint16), \
+        ctx.pinned(ct.shape, np.float32)
+    hq[...], hr[...], hc[...] = qn, qr, ct
+    ho = ctx.pinned((T, H, 128), np.uint16)
+    L = k3cuda.lib()
+    h2d = [(d_qn, hq), (d_qr, hr), (d_ct, hc)]
+
+    def e2e_step():
+        for dbuf, h in h2d:
+            k3cuda.check(L.k3cuda_memcpy_h2d(ctx.h, dbuf.ptr, h.ctypes.data, h.nbytes))
+        step()
+        k3cuda.check(L.k3cuda_memcpy_d2h(ctx.h, ho.ctypes.data, out.ptr, ho.nbytes))
+
+    for _ in range(2):
+        e2e_step()
+    ctx.sync()
+    D.barrier()
+    ctx.record(2)
+    for _ in range(args.steps):
+        e2e_step()
+    ctx.record(3)
+    ctx.sync()
+    D.barrier()
+    ms_e2e = D.max(ctx.elapsed_ms(2, 3))
+    hbm, tf, src = peaks()
+    per = ms_max / 1e3 / args.steps
+    fl = mla_prefill_flops(T, H)
+    line = {
+        "metric": f"MLA causal prefill tokens/s (chunk of {T} tokens from position 0, 128 heads)",
+        "value": T * args.steps * D.world / (ms_max / 1e3), "unit": "tokens/s",
+        "n_gpus": D.world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": ms_max / args.steps, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic (seeded numpy, config-4 distributions)",
+        "config": {"workload": f"mla_prefill_T{T}", "tokens": T, "heads": H,
+                   "cache": "latent 512 + rope 64 bf16, appended in the step",
+                   "parallelism": f"replica x{D.world}",
+                   "l2": "flushed before every step, flush inside the timed region (the cache "
+                         "itself is L2-sized)"},
+        "e2e": {"value": T * args.steps * D.world / (ms_e2e / 1e3), "unit": "tokens/s",
+                "h2d_bytes_per_step": int(sum(h.nbytes for _, h in h2d)),
+                "d2h_bytes_per_step": int(ho.nbytes)},
+        "roofline": {"bound": "tensor", "achieved": fl / per / 1e12, "peak": tf,
+                     "unit": "TFLOP/s", "frac": fl / per / 1e12 / tf, "peak_source": src,
+                     "traffic": None, "algorithmic_flops_per_launch": fl,
+                     "flops_form": "absorbed (latent) form"},
+        "gpu_launches": int(l1 - l0),  # the L2 flush is a memset, not a kernel
+        "clocks": clocks,
+    }
+    ctx.close()
+    return line
+
+
 # -------------------------------------------------------------- reference arm
 def bench_reference(args, D: Dist):
     """The reference's own C (oracle/_ref/libk3ref.so, unmodified k3_ops.c) on the host
@@ -663,7 +774,7 @@ def main():
     ap.add_argument("--steps", type=int, default=2000)
     ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--workload", default="decode",
-                    choices=["decode", "prefill", "varlen", "mla", "layer"])
+                    choices=["decode", "prefill", "varlen", "mla", "mla_prefill", "layer"])
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--tokens", type=int, default=None,
@@ -683,6 +794,8 @@ def main():
         line = bench_prefill(args, D, varlen=args.workload == "varlen")
     elif args.workload == "layer":
         line = bench_layer(args, D)
+    elif args.workload == "mla_prefill":
+        line = bench_mla_prefill(args, D)
     else:
         line = bench_mla(args, D)
     if D.rank == 0:

@@ -163,6 +163,31 @@ int k3cuda_mla_decode(k3cuda_ctx *ctx, void *out, int out_dtype, const void *q_n
                       int cap, int H, int dn, int dr, int dl, int dv, float scale,
                       void *workspace, size_t workspace_bytes);
 
+/* The same attention with the query-to-cache map explicit: query b attends positions
+ * [0, ctx_lens[b]) of cache sequence cache_seq[b] of a latent d [n_cache][cap][dl] / rope
+ * d [n_cache][cap][dr] cache. A causal prefill chunk of T tokens at positions pos0 ..
+ * pos0+T-1 of sequence s (after their rows are appended) is B = T queries with
+ * cache_seq[b] = s and ctx_lens[b] = pos0 + b + 1: the attention of k3_mla_cached for
+ * T > 1 (src/core/k3_ops.c:381-411, causal s <= p). k3cuda_mla_decode is the case
+ * cache_seq[b] = b. cache_seq and ctx_lens are HOST arrays [B]; the workspace is
+ * k3cuda_mla_decode_workspace(ctx_lens, B, ...). */
+int k3cuda_mla_attend(k3cuda_ctx *ctx, void *out, int out_dtype, const void *q_nope,
+                      const void *q_rope, const void *latent, const void *rope,
+                      const void *w_uk, const void *w_uv, const int *cache_seq,
+                      const int *ctx_lens, int B, int n_cache, int cap, int H, int dn, int dr,
+                      int dl, int dv, float scale, void *workspace, size_t workspace_bytes);
+
+/* Latent-cache append: the rows of T new tokens of sequence seq at positions pos0 ..
+ * pos0+T-1, from the kv_a projection ct d [T][dl + dr] fp32 (k3_ops.c:363-366):
+ *     latent[seq][pos0+t] = bf16(RMSNorm(ct[t][0:dl]) * kv_a_norm)   (norm over the latent
+ *     rope[seq][pos0+t]   = bf16(ct[t][dl:dl+dr])                     only, eps = rms_eps)
+ * latent d [n_cache][cap][dl] bf16, rope d [n_cache][cap][dr] bf16, kv_a_norm d [dl] fp32.
+ * The reference expands each row through kv_b here; the absorbed attention above reads the
+ * latent row instead. Supported: dl == 512, dr == 64. */
+int k3cuda_mla_cache_append(k3cuda_ctx *ctx, void *latent, void *rope, const float *ct,
+                            const float *kv_a_norm, float eps, int seq, int pos0, int T,
+                            int n_cache, int cap, int dl, int dr);
+
 /* ------------------------------------------------- multi-GPU: head-sharded output */
 /* The reference is single-process (no communicator exists in it). Head sharding adds
  * one exchange: each rank computes H_local = H / nranks heads of [T][H][dv] and the

@@ -80,9 +80,14 @@ static int blas_handle(k3cuda_ctx *ctx, cublasHandle_t *out) {
     return K3CUDA_OK;
 }
 
-// sigmoid with the fast exponential and divide intrinsics: within a few ulp of
-// 1 / (1 + expf(-x)) (the reference's sigmoidf_), and exactly 0 where exp(-x) overflows
-__device__ __forceinline__ float dsigm(float x) { return __fdividef(1.0f, 1.0f + __expf(-x)); }
+// sigmoid with the fast exponential and the hardware reciprocal (rcp.approx, no slow
+// path): within a few ulp of 1 / (1 + expf(-x)) (the reference's sigmoidf_), and exactly 0
+// where exp(-x) overflows
+__device__ __forceinline__ float dsigm(float x) {
+    float r;
+    asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(1.0f + __expf(-x)));
+    return r;
+}
 
 // ------------------------------------------------------------------- matvec_rows
 // y_s[t][r] = sum_i W_s[r][i] x[t][i] for up to MV_MAXSEG weight matrices W_s that share x
@@ -471,7 +476,7 @@ __global__ void __launch_bounds__(LAYER_THREADS) kda_layer_pre(const __grid_cons
             ss += on ? v[m] * v[m] : 0.f;
         }
         if (s < 2) {
-            const float inv = 1.0f / sqrtf(warp_sum(ss) + 1e-6f);
+            const float inv = rsqrtf(warp_sum(ss) + 1e-6f);
 #pragma unroll
             for (int m = 0; m < CPL; m++) v[m] *= inv;
         }
@@ -520,7 +525,7 @@ __global__ void __launch_bounds__(LAYER_THREADS) kda_layer_post(const __grid_con
         float ss = 0.f;
 #pragma unroll
         for (int m = 0; m < CPL; m++) ss += on ? ov[tt][m] * ov[tt][m] : 0.f;
-        const float inv = 1.0f / sqrtf(warp_sum(ss) / (float)D + a.eps);
+        const float inv = rsqrtf(warp_sum(ss) / (float)D + a.eps);
         if (!on) continue;
         float r[CPL];
 #pragma unroll

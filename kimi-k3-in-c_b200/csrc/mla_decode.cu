@@ -280,8 +280,8 @@ constexpr int MLA_SOFT = 256;     // softmax threads: two per head (32 score col
 __global__ void __launch_bounds__(MLA_THREADS, 1) __cluster_dims__(2, 1, 1)
 mla_attend_tc(const __grid_constant__ MlaMaps maps, const MlaSeg *__restrict__ segs,
               const int *__restrict__ cl_begin, const int *__restrict__ ctx_lens,
-              const __nv_bfloat16 *__restrict__ qlat, float *__restrict__ part, int H, int cap,
-              float scale_log2e, unsigned *__restrict__ err) {
+              const __nv_bfloat16 *__restrict__ qlat, float *__restrict__ part, int H,
+              const int *__restrict__ row0, float scale_log2e, unsigned *__restrict__ err) {
     extern __shared__ uint8_t smraw[];
     uint8_t *sm = (uint8_t *)(((uintptr_t)smraw + 1023) & ~(uintptr_t)1023);
     __shared__ MlaBars bars;
@@ -334,7 +334,7 @@ mla_attend_tc(const __grid_constant__ MlaMaps maps, const MlaSeg *__restrict__ s
                         break;
                     mbar_expect_tx(&bars.kv_full[st], nblk * MLA_KVBLK);
                     uint8_t *dst = sm + MLA_OFF_KV + st * MLA_NBLK * MLA_KVBLK;
-                    const int row = sg.b * cap + t * MLA_TILE;
+                    const int row = row0[sg.b] + t * MLA_TILE;
                     for (int kb = 0; kb < 4; kb++)
                         tma_load_2d(dst + kb * MLA_KVBLK, &maps.lat, &bars.kv_full[st],
                                     dim0 + kb * 64, row);
@@ -704,7 +704,7 @@ static void mla_plan(const int *ctx_lens, int B, int max_clusters, MlaPlan &p) {
 
 static size_t mla_ws_bytes(const MlaPlan &p, int B, int H) {
     return align256(p.segs.size() * sizeof(MlaSeg)) + align256(p.cl_begin.size() * sizeof(int)) +
-           align256(((size_t)B + 1) * sizeof(int)) + align256((size_t)B * sizeof(int)) +
+           align256(((size_t)B + 1) * sizeof(int)) + 2 * align256((size_t)B * sizeof(int)) +
            align256((size_t)B * MLA_HP * MLA_QW * 2) +
            align256(p.segs.size() * (size_t)H * MLA_PART * sizeof(float)) +
            align256((size_t)B * H * 2 * MLA_DL * 2);
@@ -729,26 +729,34 @@ extern "C" int k3cuda_mla_decode_workspace(const int *ctx_lens, int B, int H, in
     return K3CUDA_OK;
 }
 
-extern "C" int k3cuda_mla_decode(k3cuda_ctx *ctx, void *out, int out_dtype, const void *q_nope,
-                                 const void *q_rope, const void *latent, const void *rope,
-                                 const void *w_uk, const void *w_uv, const int *ctx_lens, int B,
-                                 int cap, int H, int dn, int dr, int dl, int dv, float scale,
-                                 void *workspace, size_t workspace_bytes) {
+// Every query b attends positions [0, ctx_lens[b]) of cache sequence cache_seq[b] (NULL:
+// b itself) of an [n_cache][cap] latent / rope cache.
+static int mla_run(k3cuda_ctx *ctx, void *out, int out_dtype, const void *q_nope,
+                   const void *q_rope, const void *latent, const void *rope, const void *w_uk,
+                   const void *w_uv, const int *cache_seq, const int *ctx_lens, int B,
+                   int n_cache, int cap, int H, int dn, int dr, int dl, int dv, float scale,
+                   void *workspace, size_t workspace_bytes) {
     int rc = enter(ctx);
     if (rc) return rc;
     if (dn != MLA_DN || dr != MLA_DR || dl != MLA_DL || dv != MLA_DV)
         return set_error(K3CUDA_ERR_UNSUPPORTED, "mla_decode: dn=%d dr=%d dl=%d dv=%d not built",
                          dn, dr, dl, dv);
     K3_ARG_CHECK(out_dtype == K3CUDA_F32 || out_dtype == K3CUDA_BF16, "bad out_dtype");
-    K3_ARG_CHECK(H >= 1 && H <= MLA_HP && B >= 0 && cap >= 1, "bad H=%d B=%d cap=%d", H, B, cap);
+    K3_ARG_CHECK(H >= 1 && H <= MLA_HP && B >= 0 && cap >= 1 && n_cache >= 1,
+                 "bad H=%d B=%d cap=%d n_cache=%d", H, B, cap, n_cache);
     if (B == 0) return K3CUDA_OK;
     K3_ARG_CHECK(ctx_lens, "null ctx_lens");
-    for (int b = 0; b < B; b++)
+    std::vector<int> row0((size_t)B);
+    for (int b = 0; b < B; b++) {
         K3_ARG_CHECK(ctx_lens[b] >= 1 && ctx_lens[b] <= cap, "ctx_lens[%d]=%d outside [1, %d]", b,
                      ctx_lens[b], cap);
+        const int cs = cache_seq ? cache_seq[b] : b;
+        K3_ARG_CHECK(cs >= 0 && cs < n_cache, "cache_seq[%d]=%d outside [0, %d)", b, cs, n_cache);
+        row0[(size_t)b] = cs * cap;
+    }
     K3_ARG_CHECK(out && q_nope && q_rope && latent && rope && w_uk && w_uv, "null pointer");
     K3_ARG_CHECK(aligned(latent, 16) && aligned(rope, 16), "caches must be 16-byte aligned");
-    K3_ARG_CHECK((long long)B * cap < (1ll << 31) && (long long)B * MLA_HP < (1ll << 31),
+    K3_ARG_CHECK((long long)n_cache * cap < (1ll << 31) && (long long)B * MLA_HP < (1ll << 31),
                  "cache too large for 32-bit TMA row coordinates");
     MlaPlan p;
     mla_plan(ctx_lens, B, std::min(MLA_MAX_CLUSTERS, std::max(1, ctx->sm_count / 2)), p);
@@ -767,6 +775,8 @@ extern "C" int k3cuda_mla_decode(k3cuda_ctx *ctx, void *out, int out_dtype, cons
     w += align256(((size_t)B + 1) * sizeof(int));
     int *d_lens = (int *)w;
     w += align256((size_t)B * sizeof(int));
+    int *d_row0 = (int *)w;
+    w += align256((size_t)B * sizeof(int));
     __nv_bfloat16 *qlat = (__nv_bfloat16 *)w;
     w += align256((size_t)B * MLA_HP * MLA_QW * 2);
     float *part = (float *)w;
@@ -780,6 +790,8 @@ extern "C" int k3cuda_mla_decode(k3cuda_ctx *ctx, void *out, int out_dtype, cons
                                 cudaMemcpyHostToDevice, ctx->stream));
     K3_CUDA_TRY(cudaMemcpyAsync(d_lens, ctx_lens, (size_t)B * sizeof(int), cudaMemcpyHostToDevice,
                                 ctx->stream));
+    K3_CUDA_TRY(cudaMemcpyAsync(d_row0, row0.data(), (size_t)B * sizeof(int),
+                                cudaMemcpyHostToDevice, ctx->stream));
     if (H < MLA_HP)  // the padded query rows must score zero
         K3_CUDA_TRY(cudaMemset2DAsync(qlat + (size_t)H * MLA_QW, (size_t)MLA_HP * MLA_QW * 2, 0,
                                       (size_t)(MLA_HP - H) * MLA_QW * 2, (size_t)B, ctx->stream));
@@ -793,11 +805,11 @@ extern "C" int k3cuda_mla_decode(k3cuda_ctx *ctx, void *out, int out_dtype, cons
         rc = make_tmap_3d(&qmaps.b, w_uk, BF, 2, MLA_DL, MLA_DN, H, MLA_DL * 2,
                           (uint64_t)MLA_DN * MLA_DL * 2, 64, 64, 1);
     if (!rc)
-        rc = make_tmap_2d(&maps.lat, latent, BF, 2, MLA_DL, (uint64_t)B * cap, MLA_DL * 2, 64,
-                          MLA_TILE);
+        rc = make_tmap_2d(&maps.lat, latent, BF, 2, MLA_DL, (uint64_t)n_cache * cap, MLA_DL * 2,
+                          64, MLA_TILE);
     if (!rc)
-        rc = make_tmap_2d(&maps.rope, rope, BF, 2, MLA_DR, (uint64_t)B * cap, MLA_DR * 2, 64,
-                          MLA_TILE);
+        rc = make_tmap_2d(&maps.rope, rope, BF, 2, MLA_DR, (uint64_t)n_cache * cap, MLA_DR * 2,
+                          64, MLA_TILE);
     if (!rc)
         rc = make_tmap_3d(&pmaps.a, olat2, BF, 2, 2 * MLA_DL, H, B, 2 * MLA_DL * 2,
                           (uint64_t)H * 2 * MLA_DL * 2, 64, 1, 128);
@@ -822,7 +834,7 @@ extern "C" int k3cuda_mla_decode(k3cuda_ctx *ctx, void *out, int out_dtype, cons
                                      MLA_SMEM));
     const float scale_log2e = scale * 1.4426950408889634f;
     mla_attend_tc<<<2 * p.ncl, MLA_THREADS, MLA_SMEM, ctx->stream>>>(maps, d_segs, d_cl, d_lens, qlat,
-                                                           part, H, cap, scale_log2e,
+                                                           part, H, d_row0, scale_log2e,
                                                            ctx->err_word);
     rc = after_launch(ctx, "mla_attend_tc");
     if (rc) return rc;
@@ -844,4 +856,80 @@ extern "C" int k3cuda_mla_decode(k3cuda_ctx *ctx, void *out, int out_dtype, cons
                                                                   ctx->err_word);
     }
     return after_launch(ctx, "mla_project_tc");
+}
+
+extern "C" int k3cuda_mla_decode(k3cuda_ctx *ctx, void *out, int out_dtype, const void *q_nope,
+                                 const void *q_rope, const void *latent, const void *rope,
+                                 const void *w_uk, const void *w_uv, const int *ctx_lens, int B,
+                                 int cap, int H, int dn, int dr, int dl, int dv, float scale,
+                                 void *workspace, size_t workspace_bytes) {
+    return mla_run(ctx, out, out_dtype, q_nope, q_rope, latent, rope, w_uk, w_uv, nullptr,
+                   ctx_lens, B, B, cap, H, dn, dr, dl, dv, scale, workspace, workspace_bytes);
+}
+
+extern "C" int k3cuda_mla_attend(k3cuda_ctx *ctx, void *out, int out_dtype, const void *q_nope,
+                                 const void *q_rope, const void *latent, const void *rope,
+                                 const void *w_uk, const void *w_uv, const int *cache_seq,
+                                 const int *ctx_lens, int B, int n_cache, int cap, int H, int dn,
+                                 int dr, int dl, int dv, float scale, void *workspace,
+                                 size_t workspace_bytes) {
+    K3_ARG_CHECK(cache_seq || B == 0, "mla_attend: null cache_seq");
+    return mla_run(ctx, out, out_dtype, q_nope, q_rope, latent, rope, w_uk, w_uv, cache_seq,
+                   ctx_lens, B, n_cache, cap, H, dn, dr, dl, dv, scale, workspace,
+                   workspace_bytes);
+}
+
+// ------------------------------------------------------------------- cache append
+// One row per token: latent[seq][pos0 + t] = bf16(kv_a_norm(ct[t][0:512])) and
+// rope[seq][pos0 + t] = bf16(ct[t][512:576]) (k3_ops.c:363-366: the norm covers the latent
+// only). The sum of squares is taken in double and the scale formed in double, as
+// k3_rmsnorm does (k3_ops.c:94-101), so the normalised fp32 values match the reference's
+// before the bf16 rounding. 128 threads, 4 latent values and half a rope value each.
+__global__ void __launch_bounds__(128) mla_cache_append_k(
+    __nv_bfloat16 *__restrict__ latent, __nv_bfloat16 *__restrict__ rope,
+    const float *__restrict__ ct, const float *__restrict__ w, float eps, long long row_base) {
+    __shared__ double red[4];
+    const int t = blockIdx.x, tid = threadIdx.x;
+    const float *src = ct + (size_t)t * MLA_QW;
+    const float4 x = reinterpret_cast<const float4 *>(src)[tid];
+    double ss = (double)x.x * x.x + (double)x.y * x.y + (double)x.z * x.z + (double)x.w * x.w;
+#pragma unroll
+    for (int o = 16; o; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+    if ((tid & 31) == 0) red[tid >> 5] = ss;
+    __syncthreads();
+    ss = (red[0] + red[1]) + (red[2] + red[3]);
+    const float inv = (float)(1.0 / sqrt(ss / (double)MLA_DL + (double)eps));
+    const float4 g = reinterpret_cast<const float4 *>(w)[tid];
+    const size_t row = (size_t)(row_base + t);
+    __nv_bfloat16 *dl = latent + row * MLA_DL + 4 * tid;
+    const __nv_bfloat162 a = __floats2bfloat162_rn(g.x * x.x * inv, g.y * x.y * inv);
+    const __nv_bfloat162 b = __floats2bfloat162_rn(g.z * x.z * inv, g.w * x.w * inv);
+    reinterpret_cast<__nv_bfloat162 *>(dl)[0] = a;
+    reinterpret_cast<__nv_bfloat162 *>(dl)[1] = b;
+    if (tid < MLA_DR / 2) {
+        const float2 r = reinterpret_cast<const float2 *>(src + MLA_DL)[tid];
+        reinterpret_cast<__nv_bfloat162 *>(rope + row * MLA_DR)[tid] = __floats2bfloat162_rn(r.x, r.y);
+    }
+}
+
+extern "C" int k3cuda_mla_cache_append(k3cuda_ctx *ctx, void *latent, void *rope,
+                                       const float *ct, const float *kv_a_norm, float eps,
+                                       int seq, int pos0, int T, int n_cache, int cap, int dl,
+                                       int dr) {
+    int rc = enter(ctx);
+    if (rc) return rc;
+    if (dl != MLA_DL || dr != MLA_DR)
+        return set_error(K3CUDA_ERR_UNSUPPORTED, "mla_cache_append: dl=%d dr=%d not built", dl, dr);
+    K3_ARG_CHECK(T >= 0 && seq >= 0 && seq < n_cache && pos0 >= 0 && (long long)pos0 + T <= cap,
+                 "mla_cache_append: seq=%d pos0=%d T=%d outside [%d][%d]", seq, pos0, T, n_cache,
+                 cap);
+    if (T == 0) return K3CUDA_OK;
+    K3_ARG_CHECK(latent && rope && ct && kv_a_norm, "mla_cache_append: null pointer");
+    K3_ARG_CHECK(aligned(latent, 16) && aligned(rope, 16) && aligned(ct, 16) &&
+                     aligned(kv_a_norm, 16),
+                 "mla_cache_append: pointers must be 16-byte aligned");
+    mla_cache_append_k<<<T, 128, 0, ctx->stream>>>((__nv_bfloat16 *)latent, (__nv_bfloat16 *)rope,
+                                                   ct, kv_a_norm, eps,
+                                                   (long long)seq * cap + pos0);
+    return after_launch(ctx, "mla_cache_append");
 }

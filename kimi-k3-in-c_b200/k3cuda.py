@@ -55,6 +55,9 @@ SIGNATURES = {
     "k3cuda_mla_decode_workspace": (_i, [_ip, _i, _i, _i, _i, C.POINTER(_sz)]),
     "k3cuda_mla_decode": (_i, [_vp, _vp, _i, _vp, _vp, _vp, _vp, _vp, _vp, _ip, _i, _i, _i, _i,
                                _i, _i, _i, _f, _vp, _sz]),
+    "k3cuda_mla_attend": (_i, [_vp, _vp, _i, _vp, _vp, _vp, _vp, _vp, _vp, _ip, _ip, _i, _i, _i,
+                               _i, _i, _i, _i, _i, _f, _vp, _sz]),
+    "k3cuda_mla_cache_append": (_i, [_vp, _vp, _vp, _vp, _vp, _f, _i, _i, _i, _i, _i, _i, _i]),
     "k3cuda_comm_unique_id": (_i, [C.c_char_p]),
     "k3cuda_comm_init": (_i, [_vp, _i, _i, C.c_char_p]),
     "k3cuda_allgather_heads_workspace": (_i, [_i, _i, _i, _i, _i, C.POINTER(_sz)]),
@@ -263,7 +266,6 @@ class Context:
                                       int(dr), int(dl), int(dv), float(scale), _ptr(workspace),
                                       int(workspace_bytes)))
 
-    # multi-GPU -------------------------------------------------------------------
     # projections and the KDA layer ------------------------------------------------
     def matmul_workspace(self, T, n_in, wdt) -> int:
         return _ws_query(lib().k3cuda_matmul_workspace, int(T), int(n_in), int(wdt))
@@ -285,6 +287,22 @@ class Context:
                                      _ptr(state), int(io_dtype), _ptr(workspace),
                                      int(workspace_bytes)))
 
+    def mla_attend(self, out, q_nope, q_rope, latent, rope, w_uk, w_uv, cache_seq, ctx_lens,
+                   n_cache, cap, H, scale, workspace, workspace_bytes, out_dtype=F32):
+        cs, csp = _iarr(cache_seq)
+        cl, clp = _iarr(ctx_lens)
+        check(lib().k3cuda_mla_attend(self.h, _ptr(out), int(out_dtype), _ptr(q_nope),
+                                      _ptr(q_rope), _ptr(latent), _ptr(rope), _ptr(w_uk),
+                                      _ptr(w_uv), csp, clp, len(cl), int(n_cache), int(cap),
+                                      int(H), 128, 64, 512, 128, float(scale), _ptr(workspace),
+                                      int(workspace_bytes)))
+
+    def mla_cache_append(self, latent, rope, ct, kv_a_norm, eps, seq, pos0, T, n_cache, cap):
+        check(lib().k3cuda_mla_cache_append(self.h, _ptr(latent), _ptr(rope), _ptr(ct),
+                                            _ptr(kv_a_norm), float(eps), int(seq), int(pos0),
+                                            int(T), int(n_cache), int(cap), 512, 64))
+
+    # multi-GPU -------------------------------------------------------------------
     def comm_init(self, nranks: int, rank: int, uid: bytes):
         check(lib().k3cuda_comm_init(self.h, int(nranks), int(rank), uid))
 

@@ -80,3 +80,91 @@ def test_rejects_bad_lengths(ctx):
     with pytest.raises(k3cuda.K3CudaError):
         run_mla(ctx, c["q_nope"], c["q_rope"], c["latent"], c["rope"], c["w_uk"], c["w_uv"],
                 np.array([0, 5], np.int32), c["scale"])
+
+
+# --------------------------------------------------------- prefill over a shared cache
+def run_attend(ctx, q_nope, q_rope, latent, rope, w_uk, w_uv, cache_seq, ctx_lens, scale):
+    """k3cuda_mla_attend: query b over cache sequence cache_seq[b], positions < ctx_lens[b]."""
+    B, H, _ = q_nope.shape
+    n_cache, cap = latent.shape[0], latent.shape[1]
+    d = [ctx.upload(np.ascontiguousarray(a)) for a in (q_nope, q_rope, latent, rope, w_uk, w_uv)]
+    out = ctx.empty((B, H, 128), np.float32)
+    nws = ctx.mla_decode_workspace(ctx_lens, H)
+    ws = ctx.empty((nws,), np.uint8)
+    ctx.mla_attend(out, *d, cache_seq, ctx_lens, n_cache, cap, H, scale, ws, nws)
+    return out.numpy()
+
+
+def test_reference_prefixes_through_one_shared_cache(ctx, golden):
+    """The reference's k3_mla_cached fixture (every causal prefix of one sequence) with all
+    queries reading the same cache rows instead of per-query copies."""
+    m = golden("mla_ref_full")
+    P = m["q_nope"].shape[0]
+    b = W.f32_to_bf16
+    out = run_attend(ctx, b(m["q_nope"]), b(m["q_rope"]), b(m["latent"][:1]), b(m["rope"][:1]),
+                     b(m["w_uk"]), b(m["w_uv"]), np.zeros(P, np.int32), m["ctx_lens"],
+                     float(m["scale"].ravel()[0]))
+    assert W.rel_fro(out, m["out"]) < TOL_BF16_INPUTS
+
+
+@pytest.mark.parametrize("H", [128, 96])
+def test_causal_prefill_chunks_of_two_sequences(ctx, H):
+    """Prefill chunks of two sequences in one call, each query over its causal prefix of its
+    own sequence (k3_ops.c:381-411, s <= p): sequence 0 at positions 70..269 (a chunk after
+    a cached prefix), sequence 1 at 0..99 (a fresh sequence)."""
+    cap = 288
+    c = W.mla_config4(seed=H + 1, B=2, ctx=cap, H=H)
+    seq = np.concatenate([np.zeros(200, np.int32), np.ones(100, np.int32)])
+    lens = np.concatenate([70 + np.arange(200) + 1, np.arange(100) + 1]).astype(np.int32)
+    rng = np.random.default_rng(H)
+    qn = W.f32_to_bf16(rng.standard_normal((len(seq), H, 128), dtype=np.float32))
+    qr = W.f32_to_bf16(rng.standard_normal((len(seq), H, 64), dtype=np.float32))
+    out = run_attend(ctx, qn, qr, c["latent"], c["rope"], c["w_uk"], c["w_uv"], seq, lens,
+                     c["scale"])
+    ref = oracle_bf16(qn, qr, c["latent"][seq], c["rope"][seq], c["w_uk"], c["w_uv"], lens,
+                      c["scale"])
+    assert W.rel_fro(out, ref) < TOL_SAME_INPUTS
+
+
+def _append_expected(ct, w, eps):
+    """k3_rmsnorm (k3_ops.c:94-101) over the latent part: sum of squares and scale in double,
+    y = w * x * inv in fp32; then bf16. The rope part is copied (k3_ops.c:366)."""
+    x = ct[:, :512]
+    ss = np.sum(x.astype(np.float64) ** 2, axis=1, keepdims=True)
+    inv = (1.0 / np.sqrt(ss / 512.0 + np.float64(eps))).astype(np.float32)
+    y = (w[None, :] * x).astype(np.float32) * inv
+    return W.f32_to_bf16(y), W.f32_to_bf16(ct[:, 512:])
+
+
+def test_cache_append_then_attend(ctx):
+    """A prefill chunk end to end: kv_a rows appended to the latent cache at positions
+    40..119 of sequence 1 (sequence 0 untouched), then the chunk's causal attention."""
+    n_cache, cap, H, pos0, T = 2, 160, 128, 40, 80
+    c = W.mla_config4(seed=3, B=n_cache, ctx=cap, H=H)
+    rng = np.random.default_rng(9)
+    ct = rng.standard_normal((T, 576), dtype=np.float32) * np.float32(2.0)
+    wn = (1.0 + 0.1 * rng.standard_normal(512)).astype(np.float32)
+    lat, rope = ctx.upload(c["latent"]), ctx.upload(c["rope"])
+    dct, dwn = ctx.upload(ct), ctx.upload(wn)
+    ctx.mla_cache_append(lat, rope, dct, dwn, 1e-5, 1, pos0, T, n_cache, cap)
+    got_lat, got_rope = lat.numpy(), rope.numpy()
+    want_lat, want_rope = c["latent"].copy(), c["rope"].copy()
+    want_lat[1, pos0:pos0 + T], want_rope[1, pos0:pos0 + T] = _append_expected(ct, wn, 1e-5)
+    assert np.array_equal(got_rope, want_rope)
+    diff = got_lat.astype(np.int32) - want_lat.astype(np.int32)
+    assert np.abs(diff).max() <= 1 and np.count_nonzero(diff) <= 4  # bf16 ulp at ties at most
+    seq = np.ones(T, np.int32)
+    lens = (pos0 + np.arange(T) + 1).astype(np.int32)
+    qn = W.f32_to_bf16(rng.standard_normal((T, H, 128), dtype=np.float32))
+    qr = W.f32_to_bf16(rng.standard_normal((T, H, 64), dtype=np.float32))
+    out = run_attend(ctx, qn, qr, got_lat, got_rope, c["w_uk"], c["w_uv"], seq, lens, c["scale"])
+    ref = oracle_bf16(qn, qr, got_lat[seq], got_rope[seq], c["w_uk"], c["w_uv"], lens, c["scale"])
+    assert W.rel_fro(out, ref) < TOL_SAME_INPUTS
+
+
+def test_attend_rejects_bad_cache_index(ctx):
+    c = W.mla_config4(seed=1, B=1, ctx=64, H=16)
+    with pytest.raises(k3cuda.K3CudaError) as e:
+        run_attend(ctx, c["q_nope"], c["q_rope"], c["latent"], c["rope"], c["w_uk"], c["w_uv"],
+                   np.array([1], np.int32), np.array([10], np.int32), c["scale"])
+    assert e.value.code == k3cuda.ERR_ARG
