@@ -41,7 +41,33 @@ void k3g_mla_attend(float *acc, const float *q, const float *latent, const float
                     const float *kv_b, float scale, int H, int qn, int qr, int kv_lora,
                     int vh, int P);
 
-/* Release the process-wide context and staging buffers (optional, at exit). */
+/* Host weights of one KDA layer, field for field K3KdaW (include/k3/k3.h:449-463): same
+ * order, same types, so a K3KdaW pointer can be passed by cast. wdt: 0 fp32, 1 bf16. */
+typedef struct {
+    const void  *q, *k, *v;
+    const float *q_conv, *k_conv, *v_conv;
+    const void  *f_a, *f_b;
+    const float *A_log;
+    const float *dt_bias;
+    const void  *b;
+    const void  *g;
+    const float *o_norm;
+    const void  *o;
+    int          wdt;
+} k3g_kda_weights;
+
+/* Replaces k3_kda_layer (src/core/k3_ops.c:864-951) for host buffers: out, x [T][E]; state
+ * [H*D*D + 3*H*D*(K-1)] updated in place (NULL: fresh sequence, as the reference). E, H, D,
+ * K, gate_lb and rms_eps are the K3Cfg fields hidden, kda_heads, kda_head_dim, conv_k,
+ * gate_lb and rms_eps. The recurrence runs on fp32 operands. The layer's weights are copied
+ * to the device on the first call that sees them (keyed by the address of w->q) and kept
+ * until k3g_shutdown: the reference never changes a loaded layer's weights. A caller that
+ * frees a layer and loads another (whose q may land at the same address) calls
+ * k3g_shutdown in between. */
+void k3g_kda_layer(float *out, const float *x, const k3g_kda_weights *w, int T, int E, int H,
+                   int D, int K, float gate_lb, float rms_eps, float *state);
+
+/* Release the process-wide context, staging buffers and cached weights (optional, at exit). */
 void k3g_shutdown(void);
 
 #ifdef __cplusplus

@@ -187,9 +187,86 @@ void k3g_mla_attend(float *acc, const float *q, const float *latent, const float
     free(hlat); free(hrope);
 }
 
+/* Device copies of KDA layer weights, one allocation per layer, keyed by the host w->q. */
+#define K3G_MAX_LAYERS 256
+typedef struct {
+    const void *key;
+    void *block;
+    k3cuda_kda_weights d;
+} LayerW;
+static LayerW g_lw[K3G_MAX_LAYERS];
+static int g_nlw = 0;
+
+static size_t a256(size_t x) { return (x + 255) & ~(size_t)255; }
+
+static const k3cuda_kda_weights *layer_weights(const k3g_kda_weights *w, int E, int H, int D,
+                                               int K)
+{
+    for (int i = 0; i < g_nlw; i++)
+        if (g_lw[i].key == w->q) return &g_lw[i].d;
+    if (g_nlw == K3G_MAX_LAYERS) {
+        fprintf(stderr, "k3_gpu: FATAL, more than %d KDA layers\n", K3G_MAX_LAYERS);
+        abort();
+    }
+    const size_t P = (size_t)H * D, es = w->wdt == 1 ? 2 : 4;
+    const void *src[14] = {w->q, w->k, w->v, w->q_conv, w->k_conv, w->v_conv, w->f_a, w->f_b,
+                           w->A_log, w->dt_bias, w->b, w->g, w->o_norm, w->o};
+    const size_t bytes[14] = {P * E * es, P * E * es, P * E * es, P * K * 4, P * K * 4,
+                              P * K * 4, (size_t)D * E * es, P * D * es, (size_t)H * 4, P * 4,
+                              (size_t)H * E * es, P * E * es, (size_t)D * 4, (size_t)E * P * es};
+    size_t total = 0;
+    for (int i = 0; i < 14; i++) total += a256(bytes[i]);
+    LayerW *L = &g_lw[g_nlw];
+    ok(k3cuda_malloc(ctx(), &L->block, total), "k3cuda_malloc (layer weights)");
+    const void *dst[14];
+    size_t off = 0;
+    for (int i = 0; i < 14; i++) {
+        if (!src[i]) {
+            fprintf(stderr, "k3_gpu: FATAL, KDA layer weight %d is NULL\n", i);
+            abort();
+        }
+        dst[i] = (char *)L->block + off;
+        ok(k3cuda_memcpy_h2d(ctx(), (void *)dst[i], src[i], bytes[i]), "upload layer weights");
+        off += a256(bytes[i]);
+    }
+    L->d.q = dst[0]; L->d.k = dst[1]; L->d.v = dst[2];
+    L->d.q_conv = (const float *)dst[3]; L->d.k_conv = (const float *)dst[4];
+    L->d.v_conv = (const float *)dst[5];
+    L->d.f_a = dst[6]; L->d.f_b = dst[7];
+    L->d.A_log = (const float *)dst[8]; L->d.dt_bias = (const float *)dst[9];
+    L->d.b = dst[10]; L->d.g = dst[11]; L->d.o_norm = (const float *)dst[12]; L->d.o = dst[13];
+    L->d.wdt = w->wdt == 1 ? K3CUDA_BF16 : K3CUDA_F32;
+    L->key = w->q;
+    g_nlw++;
+    return &L->d;
+}
+
+void k3g_kda_layer(float *out, const float *x, const k3g_kda_weights *w, int T, int E, int H,
+                   int D, int K, float gate_lb, float rms_eps, float *state)
+{
+    if (T <= 0) return;
+    const k3cuda_kda_weights *dw = layer_weights(w, E, H, D, K);
+    const size_t xb = (size_t)T * E * 4;
+    const size_t sb = ((size_t)H * D * D + 3 * (size_t)H * D * (K - 1)) * 4;
+    float *dx = (float *)put(B_Q, x, xb);
+    float *dout = (float *)dev(B_O, xb);
+    float *dS = NULL;
+    if (state) dS = (float *)put(B_S, state, sb);
+    size_t ws = 0;
+    ok(k3cuda_kda_layer_workspace(T, E, H, D, K, dw->wdt, K3CUDA_F32, &ws), "layer workspace");
+    void *dws = dev(B_WS, ws);
+    ok(k3cuda_kda_layer(ctx(), dout, dx, dw, T, E, H, D, K, gate_lb, rms_eps, dS, K3CUDA_F32,
+                        dws, ws),
+       "k3cuda_kda_layer");
+    get(out, dout, xb);
+    if (state) get(state, dS, sb);
+}
+
 void k3g_shutdown(void)
 {
     if (!g_ctx) return;
+    for (int i = 0; i < g_nlw; i++) k3cuda_free(g_ctx, g_lw[i].block);
+    g_nlw = 0;
     for (int i = 0; i < B_N; i++) {
         if (g_buf[i].ptr) k3cuda_free(g_ctx, g_buf[i].ptr);
         g_buf[i].ptr = NULL;

@@ -88,6 +88,7 @@ GPU_SIGNATURES = {
     "k3g_kda_step": (None, [_fp, _fp, _fp, _fp, _fp, _fp, _f, _i, _i]),
     "k3g_kda_recurrence": (None, [_fp, _fp, _fp, _fp, _fp, _fp, _fp, _i, _i, _i]),
     "k3g_mla_attend": (None, [_fp, _fp, _fp, _fp, _fp, _f, _i, _i, _i, _i, _i, _i]),
+    "k3g_kda_layer": (None, [_fp, _fp, _vp, _i, _i, _i, _i, _i, _f, _f, _fp]),
     "k3g_shutdown": (None, []),
 }
 

@@ -82,3 +82,64 @@ def test_mla_attend_dropin_on_reference_output(golden):
                          P(np.ascontiguousarray(m["rope"][0, :p])), P(kv_b), scale, H, qn, qr, dl,
                          vh, p)
         assert W.rel_fro(acc, m["out"][p - 1]) < 5e-3, p
+
+
+def _host_weights(w, wdt):
+    """k3g_kda_weights over host arrays (fixture names), projections as bf16 bits when wdt=1.
+    Returns the struct, the arrays it points into (kept alive), and the fp32 weights the
+    oracle must use."""
+    from oracle import oracle
+    keep, used, ptrs = [], {}, {}
+    for kn, on in zip(k3cuda.KDA_WEIGHT_NAMES, oracle.LAYER_WEIGHTS):
+        a = np.ascontiguousarray(w[on], np.float32)
+        if on in oracle.LAYER_PROJ and wdt == 1:
+            bits = W.f32_to_bf16(a)
+            keep.append(bits)
+            used[on] = W.bf16_to_f32(bits)
+            ptrs[kn] = bits.ctypes.data
+        else:
+            keep.append(a)
+            used[on] = a
+            ptrs[kn] = a.ctypes.data
+    return k3cuda.KdaWeights(**ptrs, wdt=wdt), keep, used
+
+
+@pytest.mark.parametrize("name", ["kda_layer1", "kda_layer8"])
+def test_kda_layer_dropin_on_reference_fixture(golden, name):
+    """k3g_kda_layer with the reference fixture's K3KdaW-ordered host weights: output and the
+    final recurrent state, as tests/unit/test_ops.c checks k3_kda_layer."""
+    G = k3cuda.gpu_lib()
+    G.k3g_shutdown()  # the weight cache is keyed by host address: start from an empty one
+    d = golden(name)
+    T, E = d["in"].shape[1], d["in"].shape[2]
+    H, D, K = int(d["H"]), int(d["d_k"]), int(d["conv_k"])
+    w, keep, _ = _host_weights(d, 0)
+    x = np.ascontiguousarray(d["in"][0], np.float32)
+    out = np.zeros((T, E), np.float32)
+    state = np.zeros(H * D * D + 3 * H * D * (K - 1), np.float32)
+    G.k3g_kda_layer(P(out), P(x), C.byref(w), T, E, H, D, K, float(d["lower_bound"]),
+                    float(d["rms_eps"]), P(state))
+    G.k3g_shutdown()
+    assert W.rel_fro(out, d["out"][0]) < 2e-3
+    assert W.rel_fro(state[: H * D * D], d["state_out"].ravel()) < 2e-3
+
+
+def test_kda_layer_dropin_bf16_weights_decode_loop():
+    """bf16 weights (the real checkpoint's type), D = 128: a 12-token prefill then four
+    decode calls carrying the host state, against the oracle step by step."""
+    from oracle import oracle
+    G = k3cuda.gpu_lib()
+    G.k3g_shutdown()
+    rng = np.random.default_rng(77)
+    E, H, D, K = 256, 2, 128, 4
+    w, keep, used = _host_weights(W.kda_layer_weights(rng, E, H, D, K), 1)
+    s_gpu = (0.1 * rng.standard_normal(H * D * D + 3 * H * D * (K - 1))).astype(np.float32)
+    s_orc = s_gpu.copy()
+    for T in (12, 1, 1, 1, 1):
+        x = rng.standard_normal((T, E)).astype(np.float32)
+        out = np.zeros((T, E), np.float32)
+        G.k3g_kda_layer(P(out), P(x), C.byref(w), T, E, H, D, K, -5.0, 1e-5, P(s_gpu))
+        want = oracle.kda_layer(x, used, H, D, K, -5.0, 1e-5, s_orc)
+        assert W.rel_fro(out, want) < 2e-3, T
+    G.k3g_shutdown()
+    assert W.rel_fro(s_gpu, s_orc) < 2e-3
