@@ -18,6 +18,9 @@ Other workloads (for the per-path records; one JSON line each):
   mla_prefill  causal MLA prefill chunk over the latent cache: --tokens T (default 4096)
            new tokens of one sequence appended to the cache (kv_a_norm rows) and attended
            causally from position 0, 128 heads (tokens/s)
+  moe_experts  one decode token through 16 routed experts' MXFP4 weights (k3_moe's expert
+           step): w1 and w3 (3072 x 3584) on z, then w2 (3584 x 3072) on each expert's
+           activation, as two batched launches (tokens/s)
   layer    the whole KDA layer forward (k3_kda_layer) at the model's shape: hidden 7168,
            96 heads of 128, conv 4, bf16 projection weights; --tokens T per call (default
            1: a decode step, weight streaming; e.g. 4096: a prefill chunk) (tokens/s)
@@ -614,6 +617,140 @@ def cpu_layer_baseline(T, budget_s=10.0):
                       f"(bf16 weights, OpenMP matmuls and heads)"}
 
 
+# ----------------------------------------------------------------- moe experts
+MOE_TOPK, MOE_I, MOE_L = 16, 3072, 3584
+
+
+def moe_expert_bytes(k=MOE_TOPK, I=MOE_I, L=MOE_L):
+    per = I * (L // 2 + L // 32)                   # one [I][L] or [L][I] MXFP4 matrix
+    return 3 * k * per + k * (L + I) * 4 * 2       # + activations in and out
+
+
+def moe_inputs(seed, k=MOE_TOPK, I=MOE_I, L=MOE_L):
+    rng = np.random.default_rng(seed)
+    pool = rng.integers(0, 256, 1 << 22, dtype=np.uint8)   # codes (values do not change time)
+    w13 = [np.resize(np.roll(pool, 97 * e), (I, L // 2)) for e in range(2 * k)]
+    s13 = [rng.integers(118, 128, (I, L // 32), dtype=np.uint8) for _ in range(2 * k)]
+    w2 = [np.resize(np.roll(pool, 31 * e), (L, I // 2)) for e in range(k)]
+    s2 = [rng.integers(118, 128, (L, I // 32), dtype=np.uint8) for _ in range(k)]
+    z = rng.standard_normal((1, L)).astype(np.float32)
+    act = rng.standard_normal((k, I)).astype(np.float32)
+    return w13, s13, w2, s2, z, act
+
+
+def bench_moe_experts(args, D: Dist):
+    import k3cuda
+    ctx = k3cuda.Context(D.local)
+    k, I, L = MOE_TOPK, MOE_I, MOE_L
+    w13, s13, w2, s2, z, act = moe_inputs(D.rank)
+    d13, ds13 = [ctx.upload(a) for a in w13], [ctx.upload(a) for a in s13]
+    d2, ds2 = [ctx.upload(a) for a in w2], [ctx.upload(a) for a in s2]
+    dz = ctx.upload(z)
+    dact = [ctx.upload(act[e:e + 1]) for e in range(k)]
+    y13 = [ctx.empty((1, I), np.float32) for _ in range(2 * k)]
+    y2 = [ctx.empty((1, L), np.float32) for _ in range(k)]
+
+    def step():
+        ctx.matmul_mxfp4_batch(y13, [dz] * (2 * k), d13, ds13, L, I, 1)
+        ctx.matmul_mxfp4_batch(y2, dact, d2, ds2, I, L, 1)
+
+    for _ in range(args.warmup):
+        step()
+    ctx.sync()
+    clk = ClockSampler(D.local)
+    clk.start()
+    time.sleep(0.3)
+    D.barrier()
+    ctx.sync()
+    l0 = ctx.launches()
+    t0 = clk.mark()
+    ctx.record(0)
+    for _ in range(args.steps):
+        step()
+    ctx.record(1)
+    ctx.sync()
+    t1 = clk.mark()
+    D.barrier()
+    l1 = ctx.launches()
+    ms_max = D.max(ctx.elapsed_ms(0, 1))
+    clocks = clk.stop(t0, t1)
+    # e2e: z and the activations in from page-locked memory, every output back
+    hz = ctx.pinned(z.shape, np.float32)
+    hz[...] = z
+    ha = ctx.pinned(act.shape, np.float32)
+    ha[...] = act
+    ho = ctx.pinned((3 * k, max(I, L)), np.float32)
+    L_ = k3cuda.lib()
+
+    def e2e_step():
+        k3cuda.check(L_.k3cuda_memcpy_h2d(ctx.h, dz.ptr, hz.ctypes.data, hz.nbytes))
+        for e in range(k):
+            k3cuda.check(L_.k3cuda_memcpy_h2d(ctx.h, dact[e].ptr, ha[e:e + 1].ctypes.data, I * 4))
+        step()
+        for e, y in enumerate(y13 + y2):
+            k3cuda.check(L_.k3cuda_memcpy_d2h(ctx.h, ho[e].ctypes.data, y.ptr, y.nbytes))
+
+    for _ in range(3):
+        e2e_step()
+    ctx.sync()
+    D.barrier()
+    ctx.record(2)
+    for _ in range(args.steps):
+        e2e_step()
+    ctx.record(3)
+    ctx.sync()
+    D.barrier()
+    ms_e2e = D.max(ctx.elapsed_ms(2, 3))
+    hbm, tf, src = peaks()
+    per = ms_max / 1e3 / args.steps
+    alg = moe_expert_bytes()
+    line = {
+        "metric": "MoE routed-expert decode tokens/s (16 experts x w1, w3, w2 in MXFP4)",
+        "value": args.steps * D.world / (ms_max / 1e3), "unit": "tokens/s", "n_gpus": D.world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_max / args.steps,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "fp32",
+        "data": "synthetic MXFP4 codes (pooled) and scales, seeded activations",
+        "config": {"workload": "moe_experts_decode", "experts": k, "moe_inter": I,
+                   "latent": L, "group": 32, "parallelism": f"replica x{D.world}",
+                   "l2": f"weights larger than L2 ({alg / 1e6:.0f} MB per step)"},
+        "e2e": {"value": args.steps * D.world / (ms_e2e / 1e3), "unit": "tokens/s",
+                "h2d_bytes_per_step": int(hz.nbytes + ha.nbytes),
+                "d2h_bytes_per_step": int(sum(y.nbytes for y in y13 + y2))},
+        "roofline": {"bound": "hbm", "achieved": alg / per / 1e9, "peak": hbm, "unit": "GB/s",
+                     "frac": alg / per / 1e9 / hbm, "peak_source": src, "traffic": None,
+                     "algorithmic_bytes_per_launch": alg},
+        "gpu_launches": int(l1 - l0), "clocks": clocks,
+    }
+    ctx.close()
+    return line
+
+
+def cpu_moe_baseline(budget_s=10.0):
+    """The reference's k3_matmul_mxfp4 (oracle/_ref) over the same 48 expert matrices for one
+    token, OpenMP over rows on all host cores, repeated for about budget_s seconds."""
+    from oracle import oracle
+    if not oracle.ref_available():
+        return None
+    k, I, L = MOE_TOPK, MOE_I, MOE_L
+    w13, s13, w2, s2, z, act = moe_inputs(0)
+
+    def one():
+        for e in range(2 * k):
+            oracle.matmul_mxfp4(z, w13[e], s13[e], use_ref=True)
+        for e in range(k):
+            oracle.matmul_mxfp4(act[e:e + 1], w2[e], s2[e], use_ref=True)
+
+    one()
+    n, t0 = 0, time.perf_counter()
+    while time.perf_counter() - t0 < budget_s:
+        one()
+        n += 1
+    el = time.perf_counter() - t0
+    return {"value": n / el, "unit": "tokens/s", "cores": oracle.ref().k3ref_max_threads(),
+            "kind": "reference", "sample": f"{n} tokens x 48 expert matrices through the "
+                                            f"reference k3_matmul_mxfp4"}
+
+
 # ------------------------------------------------------------------ mla prefill
 def mla_prefill_flops(T, H):
     """Absorbed-form FLOPs of a causal chunk from position 0: scores over 576 dims and the
@@ -774,7 +911,8 @@ def main():
     ap.add_argument("--steps", type=int, default=2000)
     ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--workload", default="decode",
-                    choices=["decode", "prefill", "varlen", "mla", "mla_prefill", "layer"])
+                    choices=["decode", "prefill", "varlen", "mla", "mla_prefill", "layer",
+                             "moe_experts"])
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--tokens", type=int, default=None,
@@ -796,6 +934,8 @@ def main():
         line = bench_layer(args, D)
     elif args.workload == "mla_prefill":
         line = bench_mla_prefill(args, D)
+    elif args.workload == "moe_experts":
+        line = bench_moe_experts(args, D)
     else:
         line = bench_mla(args, D)
     if D.rank == 0:
@@ -803,6 +943,8 @@ def main():
             line["cpu_baseline"] = cpu_decode_baseline(DECODE_B, DECODE_H, DECODE_D)
         if args.workload == "layer" and D.world == 1 and not args.no_cpu_baseline:
             line["cpu_baseline"] = cpu_layer_baseline(args.tokens or 1)
+        if args.workload == "moe_experts" and D.world == 1 and not args.no_cpu_baseline:
+            line["cpu_baseline"] = cpu_moe_baseline()
         print(json.dumps(line), flush=True)
     D.close()
 

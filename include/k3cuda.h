@@ -243,6 +243,34 @@ int k3cuda_matmul_workspace(int T, int in, int wdt, size_t *bytes);
 int k3cuda_matmul(k3cuda_ctx *ctx, float *y, const float *x, const void *W, int wdt, int in,
                   int out, int T, void *workspace, size_t workspace_bytes);
 
+/* ------------------------------------------------- MXFP4 expert projections */
+/* The routed experts' weights in OCP MX FP4 (include/k3/k3.h:523-569): packed d
+ * [rows][in/2] bytes, two E2M1 codes per byte, the LOW nibble the even element; scales d
+ * [rows][in/group] E8M0 bytes; w = E2M1[code] * 2^(scale - 127), scale 255 read as 0.
+ *
+ * k3cuda_mxfp4_dequant replaces k3_mxfp4_dequant (src/core/k3_ops.c:1801-1831): out d
+ * [rows][in] fp32 or bf16 (both exact). k3cuda_matmul_mxfp4 replaces k3_matmul_mxfp4
+ * (:1394-1799) for T activation rows: y d [T][rows] fp32 = x d [T][in] fp32 times W^T,
+ * never materialising W when T <= 4, group == 32 and in % 32 == 0 (products exact, each
+ * 32-element group summed in fp32 then scaled, groups summed in fp32); otherwise W is
+ * expanded to bf16 in the workspace and multiplied by cuBLAS against x's bf16 hi + lo
+ * halves. Requirements of the reference: in even, group <= 64. */
+int k3cuda_mxfp4_dequant(k3cuda_ctx *ctx, void *out, int out_dtype,
+                         const unsigned char *packed, const unsigned char *scales, int rows,
+                         int in, int group);
+int k3cuda_matmul_mxfp4_workspace(int T, int in, int rows, int group, size_t *bytes);
+int k3cuda_matmul_mxfp4(k3cuda_ctx *ctx, float *y, const float *x, const unsigned char *packed,
+                        const unsigned char *scales, int in, int rows, int group, int T,
+                        void *workspace, size_t workspace_bytes);
+/* n (<= 64) matrices of one shape in one launch, each with its own x and y: the decode
+ * step of k3_moe (k3_ops.c:640-645), where every selected expert's w1 and w3 multiply the
+ * same z, or each expert's w2 its own activation. HOST arrays of device pointers; group
+ * 32, T <= 4, in % 32 == 0. */
+int k3cuda_matmul_mxfp4_batch(k3cuda_ctx *ctx, float *const *y, const float *const *x,
+                              const unsigned char *const *packed,
+                              const unsigned char *const *scales, int n, int in, int rows,
+                              int T);
+
 /* --------------------------------------------------------- KDA layer forward */
 /* Device weights of one KDA layer, field for field K3KdaW (include/k3/k3.h:449-463):
  * q, k, v, g [H*D][E], f_a [D][E], f_b [H*D][D], b [H][E], o [E][H*D] are tagged by wdt

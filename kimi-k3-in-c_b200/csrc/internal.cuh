@@ -44,6 +44,13 @@ struct GatherOut {
 
 namespace k3 {
 
+// Projections (kda_layer.cu). split: hi = bf16(x), lo = bf16(x - hi) into xs [2][n].
+// gemm: y [T][out] = x [T][in] W^T through cuBLAS; W fp32 (SGEMM) or bf16 (two bf16
+// GEMMs over xs, the bf16 split of x).
+int split(k3cuda_ctx *ctx, __nv_bfloat16 *xs, const float *x, long long n);
+int gemm(k3cuda_ctx *ctx, float *y, const float *x, const __nv_bfloat16 *xs, const void *W,
+         int wdt, int T, int in, int out);
+
 // Record an error message for the calling thread; returns `code`.
 int set_error(int code, const char *fmt, ...);
 void clear_error();

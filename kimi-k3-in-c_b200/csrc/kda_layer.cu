@@ -262,7 +262,7 @@ __global__ void split_bf16(__nv_bfloat16 *__restrict__ hi, __nv_bfloat16 *__rest
     }
 }
 
-static int split(k3cuda_ctx *ctx, __nv_bfloat16 *xs, const float *x, long long n) {
+int split(k3cuda_ctx *ctx, __nv_bfloat16 *xs, const float *x, long long n) {
     const long long want = (n + 255) / 256;
     const int blocks = (int)(want < 8LL * ctx->sm_count ? want : 8LL * ctx->sm_count);
     split_bf16<<<blocks, 256, 0, ctx->stream>>>(xs, xs + n, x, n);
@@ -271,7 +271,7 @@ static int split(k3cuda_ctx *ctx, __nv_bfloat16 *xs, const float *x, long long n
 
 // y [T][out] = x [T][in] W^T through cuBLAS (column-major: y^T = W^T' x^T with W read
 // transposed). xs = the bf16 hi/lo split of x ([2][T][in]) when W is bf16.
-static int gemm(k3cuda_ctx *ctx, float *y, const float *x, const __nv_bfloat16 *xs,
+int gemm(k3cuda_ctx *ctx, float *y, const float *x, const __nv_bfloat16 *xs,
                 const void *W, int wdt, int T, int in, int out) {
     cublasHandle_t h = nullptr;
     int rc = blas_handle(ctx, &h);

@@ -67,6 +67,11 @@ SIGNATURES = {
                                          _f, _i, _i, _vp, _sz]),
     "k3cuda_matmul_workspace": (_i, [_i, _i, _i, C.POINTER(_sz)]),
     "k3cuda_matmul": (_i, [_vp, _vp, _vp, _vp, _i, _i, _i, _i, _vp, _sz]),
+    "k3cuda_mxfp4_dequant": (_i, [_vp, _vp, _i, _vp, _vp, _i, _i, _i]),
+    "k3cuda_matmul_mxfp4_workspace": (_i, [_i, _i, _i, _i, C.POINTER(_sz)]),
+    "k3cuda_matmul_mxfp4": (_i, [_vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _vp, _sz]),
+    "k3cuda_matmul_mxfp4_batch": (_i, [_vp, C.POINTER(_vp), C.POINTER(_vp), C.POINTER(_vp),
+                                       C.POINTER(_vp), _i, _i, _i, _i]),
     "k3cuda_kda_layer_workspace": (_i, [_i, _i, _i, _i, _i, _i, _i, C.POINTER(_sz)]),
     "k3cuda_kda_layer": (_i, [_vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _f, _f, _vp, _i, _vp, _sz]),
 }
@@ -274,6 +279,26 @@ class Context:
     def matmul(self, y, x, W, wdt, n_in, n_out, T, workspace=None, workspace_bytes=0):
         check(lib().k3cuda_matmul(self.h, _ptr(y), _ptr(x), _ptr(W), int(wdt), int(n_in),
                                   int(n_out), int(T), _ptr(workspace), int(workspace_bytes)))
+
+    def mxfp4_dequant(self, out, packed, scales, rows, n_in, group=32, out_dtype=F32):
+        check(lib().k3cuda_mxfp4_dequant(self.h, _ptr(out), int(out_dtype), _ptr(packed),
+                                         _ptr(scales), int(rows), int(n_in), int(group)))
+
+    def matmul_mxfp4_workspace(self, T, n_in, rows, group=32) -> int:
+        return _ws_query(lib().k3cuda_matmul_mxfp4_workspace, int(T), int(n_in), int(rows),
+                         int(group))
+
+    def matmul_mxfp4(self, y, x, packed, scales, n_in, rows, T, group=32, workspace=None,
+                     workspace_bytes=0):
+        check(lib().k3cuda_matmul_mxfp4(self.h, _ptr(y), _ptr(x), _ptr(packed), _ptr(scales),
+                                        int(n_in), int(rows), int(group), int(T),
+                                        _ptr(workspace), int(workspace_bytes)))
+
+    def matmul_mxfp4_batch(self, ys, xs, packeds, scaless, n_in, rows, T):
+        n = len(ys)
+        arr = lambda bufs: (_vp * max(n, 1))(*[_ptr(b) for b in bufs])  # noqa: E731
+        check(lib().k3cuda_matmul_mxfp4_batch(self.h, arr(ys), arr(xs), arr(packeds),
+                                              arr(scaless), n, int(n_in), int(rows), int(T)))
 
     def kda_layer_workspace(self, T, E, H, D, K, wdt, io_dtype) -> int:
         return _ws_query(lib().k3cuda_kda_layer_workspace, int(T), int(E), int(H), int(D),

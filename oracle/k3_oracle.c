@@ -377,3 +377,45 @@ void orc_kda_chunked_f64(float *o, float *S, double *Akk, double *Aqk,
     for (size_t i = 0; i < (size_t)dk * dv; i++) S[i] = (float)S0[i];
     free(S0); free(G); free(R); free(Dl);
 }
+
+/* ------------------------------------------------------------------------------------
+ * MXFP4. E2M1 is 1 sign, 2 exponent, 1 mantissa bits: magnitudes 0, .5, 1, 1.5, 2, 3, 4, 6
+ * by the low three bits, bit 3 the sign (code 8 is -0). E8M0 is a bare biased exponent. */
+static float e2m1(unsigned nib)
+{
+    static const float mag[8] = {0.0f, 0.5f, 1.0f, 1.5f, 2.0f, 3.0f, 4.0f, 6.0f};
+    const float m = mag[nib & 7u];
+    return (nib & 8u) ? -m : m;
+}
+
+static float e8m0(unsigned char s) { return s == 255 ? 0.0f : ldexpf(1.0f, (int)s - 127); }
+
+void orc_mxfp4_dequant(float *out, const unsigned char *packed, const unsigned char *scales,
+                       int rows, int in, int group)
+{
+    const int ngrp = (in + group - 1) / group;
+    for (int r = 0; r < rows; r++)
+        for (int i = 0; i < in; i++) {
+            const unsigned char byte = packed[(size_t)r * (in / 2) + i / 2];
+            const unsigned nib = (i & 1) ? (unsigned)(byte >> 4) : (unsigned)(byte & 15);
+            out[(size_t)r * in + i] = e2m1(nib) * e8m0(scales[(size_t)r * ngrp + i / group]);
+        }
+}
+
+void orc_matmul_mxfp4(float *y, const float *x, const unsigned char *packed,
+                      const unsigned char *scales, int in, int rows, int T, int group)
+{
+    const int ngrp = (in + group - 1) / group;
+    for (int t = 0; t < T; t++)
+        for (int r = 0; r < rows; r++) {
+            double acc = 0.0;
+            for (int i = 0; i < in; i++) {
+                const unsigned char byte = packed[(size_t)r * (in / 2) + i / 2];
+                const unsigned nib = (i & 1) ? (unsigned)(byte >> 4) : (unsigned)(byte & 15);
+                const double w = (double)e2m1(nib) *
+                                 (double)e8m0(scales[(size_t)r * ngrp + i / group]);
+                acc += w * (double)x[(size_t)t * in + i];
+            }
+            y[(size_t)t * rows + r] = (float)acc;
+        }
+}

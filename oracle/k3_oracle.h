@@ -92,6 +92,18 @@ void orc_kda_chunked_f64(float *o, float *S, double *Akk, double *Aqk,
                          const float *g, const float *beta, int T, int C, int dk,
                          int dv, float q_scale);
 
+/* MXFP4 (OCP MX FP4, include/k3/k3.h:523-569): packed [rows][in/2] bytes, the LOW nibble
+ * the even element; scales [rows][in/group] E8M0 bytes; value = E2M1[nibble] *
+ * 2^(scale - 127), scale 255 read as 0. k3_mxfp4_dequant (src/core/k3_ops.c:1801-1831). */
+void orc_mxfp4_dequant(float *out, const unsigned char *packed, const unsigned char *scales,
+                       int rows, int in, int group);
+
+/* y[t][r] = sum_i W[r][i] x[t][i] with W read as MXFP4, every product and the row sum in
+ * double: the arithmetic k3_matmul_mxfp4 (src/core/k3_ops.c:1394-1799) is held to (its
+ * test: dequantise-then-matmul within 1e-6 relative). */
+void orc_matmul_mxfp4(float *y, const float *x, const unsigned char *packed,
+                      const unsigned char *scales, int in, int rows, int T, int group);
+
 #ifdef __cplusplus
 }
 #endif

@@ -49,6 +49,9 @@ def lib():
                                               + [C.c_float, C.c_int])
         L.orc_kda_chunked_f64.argtypes = [f32p, f32p, f64p, f64p, f32p, f32p, f32p, f32p, f32p,
                                           C.c_int, C.c_int, C.c_int, C.c_int, C.c_float]
+        u8p = np.ctypeslib.ndpointer(dtype=np.uint8, flags="C_CONTIGUOUS")
+        L.orc_mxfp4_dequant.argtypes = [f32p, u8p, u8p, C.c_int, C.c_int, C.c_int]
+        L.orc_matmul_mxfp4.argtypes = [f32p, f32p, u8p, u8p, C.c_int, C.c_int, C.c_int, C.c_int]
         _LIB = L
     return _LIB
 
@@ -76,6 +79,9 @@ def ref():
         R.k3_rmsnorm.argtypes = [f32p, f32p, f32p, C.c_int, C.c_float]
         R.k3_matmul.argtypes = [f32p, f32p, f32p, C.c_int, C.c_int]
         R.k3_mla_scratch_cached.restype = C.c_size_t
+        u8p = np.ctypeslib.ndpointer(dtype=np.uint8, flags="C_CONTIGUOUS")
+        R.k3_mxfp4_dequant.argtypes = [f32p, u8p, u8p, C.c_int, C.c_int, C.c_int]
+        R.k3_matmul_mxfp4.argtypes = [f32p, f32p, u8p, u8p, C.c_int, C.c_int, C.c_int]
         R.k3ref_kda_layer.argtypes = ([f32p, f32p] + [C.c_int] * 5 + [C.c_float, C.c_float]
                                       + [C.c_void_p] * 3 + [f32p] * 3 + [C.c_void_p] * 2
                                       + [f32p] * 2 + [C.c_void_p] * 2 + [f32p, C.c_void_p,
@@ -206,6 +212,37 @@ def ref_kda_layer(x, w, H, D, K, lb, eps, state=None, wdt=0):
     ref().k3ref_kda_layer(out, x, T, E, H, D, K, float(lb), float(eps), *args, int(wdt),
                           None if state is None else state.ctypes.data)
     return out
+
+
+# --------------------------------------------------------------------------- MXFP4
+def mxfp4_dequant(packed, scales, group=32):
+    """orc_mxfp4_dequant: packed uint8 [rows][in/2], scales uint8 [rows][in/group]."""
+    packed = np.ascontiguousarray(packed, np.uint8)
+    scales = np.ascontiguousarray(scales, np.uint8)
+    rows, in_ = packed.shape[0], 2 * packed.shape[1]
+    out = np.zeros((rows, in_), np.float32)
+    lib().orc_mxfp4_dequant(out, packed, scales, rows, in_, group)
+    return out
+
+
+def matmul_mxfp4(x, packed, scales, group=32, use_ref=False):
+    """y [T][rows] = x [T][in] W^T with W as MXFP4: the restatement (double products and
+    sums), or with use_ref the reference's own k3_matmul_mxfp4 once per row of x."""
+    x = _f32(np.atleast_2d(x))
+    packed = np.ascontiguousarray(packed, np.uint8)
+    scales = np.ascontiguousarray(scales, np.uint8)
+    T, in_ = x.shape
+    rows = packed.shape[0]
+    y = np.zeros((T, rows), np.float32)
+    if use_ref:
+        for t in range(T):
+            yt = np.zeros(rows, np.float32)
+            ref().k3_matmul_mxfp4(yt, np.ascontiguousarray(x[t]), packed, scales, in_, rows,
+                                  group)
+            y[t] = yt
+    else:
+        lib().orc_matmul_mxfp4(y, x, packed, scales, in_, rows, T, group)
+    return y
 
 
 def max_threads() -> int:

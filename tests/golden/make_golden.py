@@ -22,6 +22,8 @@ Two kinds of fixture, both written as .npz (float32 unless noted):
      * mla_ref_full.npz -- the same at the released head geometry (nope 128, rope 64,
                         latent 512, v 128) with H=2 and 80 positions, the shape the CUDA
                         kernel is built for.
+     * mxfp4.npz     -- REF/tests/fixtures/mxfp4.json converted (real checkpoint MXFP4
+                        bytes and their dequantised values), plus k3_matmul_mxfp4 on them.
 """
 from __future__ import annotations
 
@@ -128,6 +130,25 @@ def mla_reference_case(H=8, dn=32, dr=16, dl=64, dv=32, q_lora=48, P=40, seed=3,
                 out=out.reshape(P, H, dv))
 
 
+def convert_mxfp4(ref_dir: str):
+    """REF/tests/fixtures/mxfp4.json (real checkpoint MXFP4 bytes, 64 rows x 3584, with the
+    expected dequantised values and the swapped-nibble trap) -> mxfp4.npz, plus the
+    reference's own k3_matmul_mxfp4 (oracle/_ref) on those bytes for two seeded activation
+    rows (y_ref)."""
+    with open(os.path.join(ref_dir, "tests", "fixtures", "mxfp4.json")) as f:
+        d = json.load(f)
+    arr = lambda k, t: np.asarray(d[k]["data"], t).reshape(d[k]["shape"])  # noqa: E731
+    packed, scales = arr("packed", np.uint8), arr("scales", np.uint8)
+    x = np.random.default_rng(21).standard_normal((2, int(d["logical_width"]))).astype(np.float32)
+    y_ref = oracle.matmul_mxfp4(x, packed, scales, int(d["group_size"]), use_ref=True)
+    np.savez_compressed(os.path.join(HERE, "mxfp4.npz"), packed=packed, scales=scales,
+                        expected=arr("expected", np.float32),
+                        expected_swapped_first64=np.asarray(
+                            d["expected_swapped_nibbles"]["first64"], np.float32),
+                        e2m1_lut=np.asarray(d["e2m1_lut"], np.float32),
+                        group=np.asarray(int(d["group_size"])), x=x, y_ref=y_ref)
+
+
 def main():
     ref_dir = sys.argv[1] if len(sys.argv) > 1 else "/root/reference"
     for name in ("kda_recur1", "kda_recur8", "kda_decay", "kda_layer1", "kda_layer8", "mla"):
@@ -159,6 +180,7 @@ def main():
     m["latent"] = m["latent"][0:1].copy()
     m["rope"] = m["rope"][0:1].copy()
     np.savez_compressed(os.path.join(HERE, "mla_ref_full.npz"), **m)
+    convert_mxfp4(ref_dir)
     print("golden vectors written to", HERE)
 
 

@@ -175,3 +175,48 @@ def test_bf16_round_trip():
     y = W.bf16_to_f32(b)
     assert np.array_equal(W.f32_to_bf16(y), b)
     assert np.all(np.abs(y - x) <= np.abs(x) * 2.0 ** -8)
+
+
+def test_mxfp4_dequant_is_exact_on_checkpoint_bytes(golden):
+    """orc_mxfp4_dequant on the reference's real checkpoint bytes (tests/fixtures/mxfp4.json):
+    every value bit-exact (signed zeros too); the swapped nibble order gives the fixture's
+    recorded wrong answer, so the order is really tested."""
+    d = golden("mxfp4")
+    got = oracle.mxfp4_dequant(d["packed"], d["scales"], int(d["group"]))
+    assert np.array_equal(got.view(np.uint32), d["expected"].view(np.uint32))
+    p = d["packed"]
+    swapped = ((p & 15) << 4 | (p >> 4)).astype(np.uint8)
+    wrong = oracle.mxfp4_dequant(swapped, d["scales"], int(d["group"]))
+    assert np.array_equal(wrong[0, :64], d["expected_swapped_first64"])
+    assert not np.array_equal(wrong, got)
+
+
+def test_mxfp4_matmul_matches_reference(golden):
+    """orc_matmul_mxfp4 against the reference's k3_matmul_mxfp4 output stored with the
+    fixture (its own test bar: 1e-6 relative to dequantise-then-matmul)."""
+    d = golden("mxfp4")
+    y = oracle.matmul_mxfp4(d["x"], d["packed"], d["scales"], int(d["group"]))
+    rel = np.abs(y - d["y_ref"]) / np.maximum(np.abs(d["y_ref"]), 1e-30)
+    assert rel.max() < 1e-6
+
+
+@pytest.mark.skipif(not oracle.ref_available(), reason="oracle/_ref not built")
+@pytest.mark.parametrize("group,n_in", [(32, 256), (16, 96), (64, 130)])
+def test_mxfp4_matmul_matches_reference_c_on_extreme_scales(group, n_in):
+    """Random codes with scales at the extremes (0: subnormal 2^-127, 255: read as 0, up to
+    2^100) and a partial last group, against the reference C directly."""
+    rng = np.random.default_rng(group + n_in)
+    rows = 37
+    packed = rng.integers(0, 256, (rows, n_in // 2), dtype=np.uint8)
+    ngrp = (n_in + group - 1) // group
+    scales = rng.choice(np.array([0, 1, 100, 120, 127, 130, 200, 227, 255], np.uint8),
+                        (rows, ngrp)).astype(np.uint8)
+    x = rng.standard_normal((3, n_in)).astype(np.float32)
+    want = oracle.matmul_mxfp4(x, packed, scales, group, use_ref=True)
+    got = oracle.matmul_mxfp4(x, packed, scales, group)
+    rel = np.abs(got - want) / np.maximum(np.abs(want), 1e-30)
+    assert rel.max() < 1e-6
+    deq = oracle.mxfp4_dequant(packed, scales, group)
+    ref = np.zeros_like(deq)
+    oracle.ref().k3_mxfp4_dequant(ref, packed, scales, rows, n_in // 2, group)
+    assert np.array_equal(deq.view(np.uint32), ref.view(np.uint32))
