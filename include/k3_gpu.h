@@ -11,6 +11,8 @@
 #ifndef K3_GPU_H
 #define K3_GPU_H
 
+#include <stdint.h>
+
 #ifdef __cplusplus
 extern "C" {
 #endif
@@ -66,6 +68,33 @@ typedef struct {
  * k3g_shutdown in between. */
 void k3g_kda_layer(float *out, const float *x, const k3g_kda_weights *w, int T, int E, int H,
                    int D, int K, float gate_lb, float rms_eps, float *state);
+
+/* State file for device-resident state (--save-state / --load-state of the reference,
+ * src/cli/k3_state.c:102-270). The header is the reference's K3StateHdr byte for byte
+ * (magic "K3ST", then version, config fingerprint, counts, per-layer geometry, FNV-1a
+ * payload hash over the header with the hash zeroed and then the payload), with version
+ * K3G_STATE_VER: the reference's loader refuses it by version rather than misreading it.
+ * What changes is the MLA part: the device keeps the latent cache, so kvpp is the latent
+ * width (kv_lora) and ropepp the rope width, and those slices are bf16.
+ *   payload: seq [nseq] int32; ks [n_bound][kper] fp32; latent [n_mla][cached][kv_lora]
+ *            bf16; rope [n_mla][cached][rope_w] bf16 (position-major per layer, only the
+ *            occupied positions, so a resumed run may size its cache differently)
+ *   device:  ks d [n_bound][kper]; latent d [n_mla][kv_cap][kv_lora]; rope d
+ *            [n_mla][kv_cap][rope_w]
+ * fp is the reference's 12-int config fingerprint (k3_state_fp). Both return 0, or -1
+ * with a message on stderr (the reference's contract): save writes a temporary file
+ * beside `path`, fsyncs it and renames it over `path`; load refuses a file of another
+ * version, architecture (fp), geometry, layer count or capacity, a truncated or longer
+ * file, or one whose hash does not match. On load *nseq and *cached receive the counts
+ * and seq must hold seq_cap ints. */
+#define K3G_STATE_VER 4
+int k3g_state_save(const char *path, const int32_t fp[12], const int *seq, int nseq,
+                   const float *d_ks, int64_t kper, int n_bound, const void *d_latent,
+                   const void *d_rope, int n_mla, int kv_cap, int kv_lora, int rope_w,
+                   int cached);
+int k3g_state_load(const char *path, const int32_t fp[12], int *seq, int seq_cap, int *nseq,
+                   float *d_ks, int64_t kper, int n_bound, void *d_latent, void *d_rope,
+                   int n_mla, int kv_cap, int kv_lora, int rope_w, int *cached);
 
 /* Release the process-wide context, staging buffers and cached weights (optional, at exit). */
 void k3g_shutdown(void);

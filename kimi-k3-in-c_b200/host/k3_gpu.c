@@ -14,6 +14,7 @@
 #include <string.h>
 
 #include "k3cuda.h"
+#include "k3_gpu_internal.h"
 
 static k3cuda_ctx *g_ctx = NULL;
 
@@ -47,6 +48,8 @@ static k3cuda_ctx *ctx(void)
     }
     return g_ctx;
 }
+
+k3cuda_ctx *k3g_ctx(void) { return ctx(); }
 
 static void *dev(int slot, size_t bytes)
 {

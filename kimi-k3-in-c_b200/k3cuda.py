@@ -94,6 +94,10 @@ GPU_SIGNATURES = {
     "k3g_kda_recurrence": (None, [_fp, _fp, _fp, _fp, _fp, _fp, _fp, _i, _i, _i]),
     "k3g_mla_attend": (None, [_fp, _fp, _fp, _fp, _fp, _f, _i, _i, _i, _i, _i, _i]),
     "k3g_kda_layer": (None, [_fp, _fp, _vp, _i, _i, _i, _i, _i, _f, _f, _fp]),
+    "k3g_state_save": (_i, [C.c_char_p, _ip, _ip, _i, _vp, C.c_int64, _i, _vp, _vp, _i, _i, _i,
+                            _i, _i]),
+    "k3g_state_load": (_i, [C.c_char_p, _ip, _ip, _i, _ip, _vp, C.c_int64, _i, _vp, _vp, _i, _i,
+                            _i, _i, _ip]),
     "k3g_shutdown": (None, []),
 }
 
