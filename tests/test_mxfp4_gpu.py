@@ -1,5 +1,6 @@
 """MXFP4 expert projections on the B200 (k3cuda_mxfp4_dequant, k3cuda_matmul_mxfp4,
-k3cuda_matmul_mxfp4_batch) against the reference's checkpoint fixture and the oracle.
+k3cuda_matmul_mxfp4_batch) against the reference's checkpoint fixture and the oracle. Up to
+four activation rows take the streaming kernel, anything else the bf16 GEMM path.
 
 Dequantisation is exact, so it is compared bit for bit. The matmul sums in fp32 where the
 reference sums in double: relative Frobenius error 1e-6 on the streaming path and 2e-5 on
@@ -52,6 +53,8 @@ def test_matmul_on_checkpoint_bytes_matches_reference(ctx, golden, T):
     (1, 3072, 3584, 32, 1e-6),    # an expert's w1 / w3 at the model's shape, decode
     (3, 3584, 3072, 32, 1e-6),    # w2, three tokens
     (4, 301, 1024, 32, 1e-6),     # rows not a multiple of the warp's 4
+    (1, 1000, 3584, 32, 1e-6),    # many row groups, the last one partial
+    (2, 45, 7168, 32, 1e-6),      # longer rows
     (9, 300, 1024, 32, 2e-5),     # GEMM path
     (2, 40, 96, 16, 2e-5),        # group 16: GEMM path
     (1, 33, 100, 32, 2e-5),       # partial last group: GEMM path
