@@ -188,6 +188,33 @@ int k3cuda_mla_cache_append(k3cuda_ctx *ctx, void *latent, void *rope, const flo
                             const float *kv_a_norm, float eps, int seq, int pos0, int T,
                             int n_cache, int cap, int dl, int dr);
 
+/* ------------------------------------------------------- MLA layer forward */
+/* Device weights of one MLA layer, field for field K3MlaW (include/k3/k3.h:203-210):
+ * q_a [q_lora][E], q_b [H*(dn+dr)][q_lora], kv_a [dl+dr][E], kv_b [H*(dn+dv)][dl] (per head
+ * dn W_UK rows then dv W_UV rows), o [E][H*dv], g [H*dv][E] or NULL (no gate), tagged by
+ * wdt; q_a_norm [q_lora], kv_a_norm [dl] fp32. Every pointer is device memory. */
+typedef struct {
+    const void  *q_a, *q_b;
+    const void  *kv_a, *kv_b;
+    const void  *o, *g;
+    const float *q_a_norm, *kv_a_norm;
+    int          wdt;
+} k3cuda_mla_weights;
+
+/* k3_mla_cached (src/core/k3_ops.c:321-424) for T tokens of one sequence at positions
+ * cached .. cached+T-1, with the cache on the device as the latent: latent d [cap][dl] bf16
+ * and rope d [cap][dr] bf16 take the place of the reference's expanded kvc / ropec (the
+ * layer writes the T new rows, then attends causally). out, x d [T][E] fp32. Attention
+ * operands are bf16, accumulation fp32. Supported: the released geometry dn = 128, dr = 64,
+ * dl = 512, dv = 128, H <= 128, E and q_lora multiples of 8, cached + T <= cap. workspace d:
+ * k3cuda_mla_layer_workspace() bytes. */
+int k3cuda_mla_layer_workspace(int T, int E, int H, int q_lora, int cached, int wdt,
+                               size_t *bytes);
+int k3cuda_mla_layer(k3cuda_ctx *ctx, float *out, const float *x, const k3cuda_mla_weights *w,
+                     int T, int E, int H, int q_lora, int dn, int dr, int dl, int dv,
+                     float rms_eps, void *latent, void *rope, int cached, int cap,
+                     void *workspace, size_t workspace_bytes);
+
 /* ------------------------------------------------- multi-GPU: head-sharded output */
 /* The reference is single-process (no communicator exists in it). Head sharding adds
  * one exchange: each rank computes H_local = H / nranks heads of [T][H][dv] and the

@@ -50,6 +50,24 @@ namespace k3 {
 int split(k3cuda_ctx *ctx, __nv_bfloat16 *xs, const float *x, long long n);
 int gemm(k3cuda_ctx *ctx, float *y, const float *x, const __nv_bfloat16 *xs, const void *W,
          int wdt, int T, int in, int out);
+// One weight matrix [rows][in] of a projection table and its output [T][rows].
+struct Proj {
+    const void *W;
+    float *y;
+    int rows;
+};
+constexpr int PROJ_MAXT = 8;  // up to this many activation rows the projections stream W
+// n (<= 8) projections of the same x [T][in], T <= PROJ_MAXT, in one launch
+int matvec(k3cuda_ctx *ctx, const float *x, int T, int in, const Proj *p, int n, int wdt);
+// one projection: streaming (T <= PROJ_MAXT) or GEMM (xs: x's bf16 split for bf16 W)
+int project(k3cuda_ctx *ctx, float *y, const float *x, const __nv_bfloat16 *xs, const void *W,
+            int wdt, int T, int in, int out);
+// MLA attention of T queries at positions cached.. of one sequence, W_UK/W_UV in kv_b
+// (mla_decode.cu)
+int mla_attend_kvb(k3cuda_ctx *ctx, float *acc, const void *q_nope, const void *q_rope,
+                   const void *latent, const void *rope, const void *kv_b, int T, int cached,
+                   int cap, int H, float scale, void *workspace, size_t workspace_bytes);
+size_t mla_attend_kvb_workspace(int T, int cached, int H);
 
 // Record an error message for the calling thread; returns `code`.
 int set_error(int code, const char *fmt, ...);

@@ -201,14 +201,8 @@ static void launch_matvec(const MatvecArgs &a, int wdt, int blocks, cudaStream_t
         matvec_rows<NT, float><<<blocks, MV_THREADS, 0, st>>>(a);
 }
 
-struct Proj {
-    const void *W;
-    float *y;
-    int rows;
-};
-
 // One launch of matvec_rows over `n` projections of the same x [T][in] (T <= MV_MAXT).
-static int matvec(k3cuda_ctx *ctx, const float *x, int T, int in, const Proj *p, int n, int wdt) {
+int matvec(k3cuda_ctx *ctx, const float *x, int T, int in, const Proj *p, int n, int wdt) {
     if (T < 1 || T > MV_MAXT || n < 1 || n > MV_MAXSEG)
         return set_error(K3CUDA_ERR_ARG, "matvec: T=%d n=%d", T, n);
     MatvecArgs a{};
@@ -625,7 +619,7 @@ static void launch_pre(const PreArgs<IO> &a, int D, int K, dim3 grid, cudaStream
 }
 
 // One projection: matvec (T <= 8) or GEMM; xs is x's bf16 split when the GEMM needs it.
-static int project(k3cuda_ctx *ctx, float *y, const float *x, const __nv_bfloat16 *xs,
+int project(k3cuda_ctx *ctx, float *y, const float *x, const __nv_bfloat16 *xs,
                    const void *W, int wdt, int T, int in, int out) {
     if (T <= MV_MAXT) {
         const Proj p{W, y, out};

@@ -733,7 +733,8 @@ extern "C" int k3cuda_mla_decode_workspace(const int *ctx_lens, int B, int H, in
 // b itself) of an [n_cache][cap] latent / rope cache.
 static int mla_run(k3cuda_ctx *ctx, void *out, int out_dtype, const void *q_nope,
                    const void *q_rope, const void *latent, const void *rope, const void *w_uk,
-                   const void *w_uv, const int *cache_seq, const int *ctx_lens, int B,
+                   const void *w_uv, int uk_head_rows, int uv_head_rows,
+                   const int *cache_seq, const int *ctx_lens, int B,
                    int n_cache, int cap, int H, int dn, int dr, int dl, int dv, float scale,
                    void *workspace, size_t workspace_bytes) {
     int rc = enter(ctx);
@@ -803,7 +804,7 @@ static int mla_run(k3cuda_ctx *ctx, void *out, int out_dtype, const void *q_nope
                       64, 1, 128);
     if (!rc)
         rc = make_tmap_3d(&qmaps.b, w_uk, BF, 2, MLA_DL, MLA_DN, H, MLA_DL * 2,
-                          (uint64_t)MLA_DN * MLA_DL * 2, 64, 64, 1);
+                          (uint64_t)uk_head_rows * MLA_DL * 2, 64, 64, 1);
     if (!rc)
         rc = make_tmap_2d(&maps.lat, latent, BF, 2, MLA_DL, (uint64_t)n_cache * cap, MLA_DL * 2,
                           64, MLA_TILE);
@@ -815,7 +816,7 @@ static int mla_run(k3cuda_ctx *ctx, void *out, int out_dtype, const void *q_nope
                           (uint64_t)H * 2 * MLA_DL * 2, 64, 1, 128);
     if (!rc)
         rc = make_tmap_3d(&pmaps.b, w_uv, BF, 2, MLA_DL, MLA_DV, H, MLA_DL * 2,
-                          (uint64_t)MLA_DV * MLA_DL * 2, 64, 128, 1);
+                          (uint64_t)uv_head_rows * MLA_DL * 2, 64, 128, 1);
     if (rc) return rc;
     K3_ARG_CHECK(aligned(q_nope, 16) && aligned(q_rope, 16) && aligned(w_uk, 16) &&
                      aligned(w_uv, 16),
@@ -858,13 +859,39 @@ static int mla_run(k3cuda_ctx *ctx, void *out, int out_dtype, const void *q_nope
     return after_launch(ctx, "mla_project_tc");
 }
 
+namespace k3 {
+// The causal attention of one prefill chunk / decode token of one sequence for the MLA layer:
+// queries b = 0..T-1 at positions cached + b over the sequence's cache, with W_UK and W_UV
+// read in place from kv_b [H][256][512] bf16 (per head 128 W_UK rows, then 128 W_UV rows).
+int mla_attend_kvb(k3cuda_ctx *ctx, float *acc, const void *q_nope, const void *q_rope,
+                   const void *latent, const void *rope, const void *kv_b, int T, int cached,
+                   int cap, int H, float scale, void *workspace, size_t workspace_bytes) {
+    std::vector<int> seq((size_t)T, 0), lens((size_t)T);
+    for (int t = 0; t < T; t++) lens[(size_t)t] = cached + t + 1;
+    const char *kb = (const char *)kv_b;
+    return mla_run(ctx, acc, K3CUDA_F32, q_nope, q_rope, latent, rope, kb,
+                   kb + (size_t)MLA_DN * MLA_DL * 2, MLA_DN + MLA_DV, MLA_DN + MLA_DV,
+                   seq.data(), lens.data(), T, 1, cap, H, MLA_DN, MLA_DR, MLA_DL, MLA_DV, scale,
+                   workspace, workspace_bytes);
+}
+
+size_t mla_attend_kvb_workspace(int T, int cached, int H) {
+    std::vector<int> lens((size_t)T);
+    for (int t = 0; t < T; t++) lens[(size_t)t] = cached + t + 1;
+    MlaPlan p;
+    mla_plan(lens.data(), T, MLA_MAX_CLUSTERS, p);
+    return mla_ws_bytes(p, T, H);
+}
+}  // namespace k3
+
 extern "C" int k3cuda_mla_decode(k3cuda_ctx *ctx, void *out, int out_dtype, const void *q_nope,
                                  const void *q_rope, const void *latent, const void *rope,
                                  const void *w_uk, const void *w_uv, const int *ctx_lens, int B,
                                  int cap, int H, int dn, int dr, int dl, int dv, float scale,
                                  void *workspace, size_t workspace_bytes) {
-    return mla_run(ctx, out, out_dtype, q_nope, q_rope, latent, rope, w_uk, w_uv, nullptr,
-                   ctx_lens, B, B, cap, H, dn, dr, dl, dv, scale, workspace, workspace_bytes);
+    return mla_run(ctx, out, out_dtype, q_nope, q_rope, latent, rope, w_uk, w_uv, MLA_DN, MLA_DV,
+                   nullptr, ctx_lens, B, B, cap, H, dn, dr, dl, dv, scale, workspace,
+                   workspace_bytes);
 }
 
 extern "C" int k3cuda_mla_attend(k3cuda_ctx *ctx, void *out, int out_dtype, const void *q_nope,
@@ -874,8 +901,8 @@ extern "C" int k3cuda_mla_attend(k3cuda_ctx *ctx, void *out, int out_dtype, cons
                                  int dr, int dl, int dv, float scale, void *workspace,
                                  size_t workspace_bytes) {
     K3_ARG_CHECK(cache_seq || B == 0, "mla_attend: null cache_seq");
-    return mla_run(ctx, out, out_dtype, q_nope, q_rope, latent, rope, w_uk, w_uv, cache_seq,
-                   ctx_lens, B, n_cache, cap, H, dn, dr, dl, dv, scale, workspace,
+    return mla_run(ctx, out, out_dtype, q_nope, q_rope, latent, rope, w_uk, w_uv, MLA_DN, MLA_DV,
+                   cache_seq, ctx_lens, B, n_cache, cap, H, dn, dr, dl, dv, scale, workspace,
                    workspace_bytes);
 }
 

@@ -1,0 +1,215 @@
+// mla_layer.cu -- the MLA layer forward of k3_mla_cached (src/core/k3_ops.c:321-424) with its
+// KV cache on the device as the compressed latent (+ the shared rope slot) instead of the
+// expanded per-head keys and values.
+//
+//   step (reference line)                                  here
+//   ql = RMSNorm(q_a x) (q_a_norm); q = q_b ql   (:358-360)  projections; rmsnorm_rows
+//   ct = kv_a x; RMSNorm(ct[:kv_lora]) (kv_a_norm);           projection; k3cuda_mla_cache_append
+//       rope slot ct[kv_lora:] copied unrotated (:363-366)     (writes the latent / rope rows)
+//   kv = kv_b ct[:kv_lora] into the cache (:367)             not formed: W_UK, W_UV stay in kv_b
+//   causal attention, scale (qk_nope+qk_rope)^-0.5 (:381-411) mla_attend_kvb (absorbed form)
+//   acc *= sigmoid(g x) (when g), out = o acc (:413-420)      mla_gate; projection
+//
+// Projections go through the same streaming / cuBLAS paths as the KDA layer (kda_layer.cu).
+#include "internal.cuh"
+
+namespace k3 {
+
+constexpr int ML_DN = 128, ML_DR = 64, ML_DL = 512, ML_DV = 128;
+
+// y[r] = w * x[r] * inv, inv = 1/sqrt(mean(x^2) + eps) with the sum in double (k3_rmsnorm,
+// k3_ops.c:94-101), one row per block, in place.
+__global__ void rmsnorm_rows(float *__restrict__ x, const float *__restrict__ w, int n,
+                             float eps) {
+    __shared__ double red[32];
+    float *row = x + (size_t)blockIdx.x * n;
+    double ss = 0.0;
+    for (int i = threadIdx.x; i < n; i += blockDim.x) ss += (double)row[i] * (double)row[i];
+#pragma unroll
+    for (int o = 16; o; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
+    __syncthreads();
+    if (threadIdx.x < 32) {
+        double v = threadIdx.x < blockDim.x / 32 ? red[threadIdx.x] : 0.0;
+#pragma unroll
+        for (int o = 16; o; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+        if (threadIdx.x == 0) red[0] = v;
+    }
+    __syncthreads();
+    const float inv = (float)(1.0 / sqrt(red[0] / (double)n + (double)eps));
+    for (int i = threadIdx.x; i < n; i += blockDim.x) row[i] = w[i] * row[i] * inv;
+}
+
+// q [T][H][dn + dr] fp32 -> q_nope [T][H][dn], q_rope [T][H][dr] bf16
+__global__ void mla_q_split(__nv_bfloat16 *__restrict__ qn, __nv_bfloat16 *__restrict__ qr,
+                            const float *__restrict__ q, int H) {
+    const int t = blockIdx.x;
+    for (int i = threadIdx.x; i < H * (ML_DN + ML_DR); i += blockDim.x) {
+        const int h = i / (ML_DN + ML_DR), c = i - h * (ML_DN + ML_DR);
+        const __nv_bfloat16 v = __float2bfloat16_rn(q[(size_t)t * H * (ML_DN + ML_DR) + i]);
+        if (c < ML_DN) qn[((size_t)t * H + h) * ML_DN + c] = v;
+        else qr[((size_t)t * H + h) * ML_DR + c - ML_DN] = v;
+    }
+}
+
+__global__ void f32_to_bf16(__nv_bfloat16 *__restrict__ y, const float *__restrict__ x,
+                            long long n) {
+    for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n;
+         i += (long long)gridDim.x * blockDim.x)
+        y[i] = __float2bfloat16_rn(x[i]);
+}
+
+// ot = acc * sigmoid(g x) (or acc when there is no gate), also as the bf16 hi/lo split when
+// o_proj is a bf16 GEMM
+__global__ void mla_gate(float *__restrict__ ot, __nv_bfloat16 *__restrict__ hi,
+                         __nv_bfloat16 *__restrict__ lo, const float *__restrict__ acc,
+                         const float *__restrict__ gb, long long n) {
+    for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n;
+         i += (long long)gridDim.x * blockDim.x) {
+        float v = acc[i];
+        if (gb) v *= 1.0f / (1.0f + expf(-gb[i]));
+        ot[i] = v;
+        if (hi) {
+            const __nv_bfloat16 h = __float2bfloat16_rn(v);
+            hi[i] = h;
+            lo[i] = __float2bfloat16_rn(v - __bfloat162float(h));
+        }
+    }
+}
+
+static size_t al256(size_t x) { return (x + 255) & ~(size_t)255; }
+
+struct MlaLayerPlan {
+    size_t ql, ct, gb, q, qn, qr, acc, ot, xs, qls, ots, kvb, att, total;
+    bool gemm, split;
+};
+
+static void plan(int T, int E, int H, int q_lora, int cached, int wdt, MlaLayerPlan *p) {
+    size_t off = 0;
+    auto take = [&](size_t b) { const size_t o = off; off += al256(b); return o; };
+    const size_t HV = (size_t)H * ML_DV, HQ = (size_t)H * (ML_DN + ML_DR);
+    p->gemm = T > PROJ_MAXT;
+    p->split = p->gemm && wdt == K3CUDA_BF16;
+    p->ql = take((size_t)T * q_lora * 4);
+    p->ct = take((size_t)T * (ML_DL + ML_DR) * 4);
+    p->gb = take((size_t)T * HV * 4);
+    p->q = take((size_t)T * HQ * 4);
+    p->qn = take((size_t)T * H * ML_DN * 2);
+    p->qr = take((size_t)T * H * ML_DR * 2);
+    p->acc = take((size_t)T * HV * 4);
+    p->ot = take((size_t)T * HV * 4);
+    p->xs = p->split ? take((size_t)2 * T * E * 2) : 0;
+    p->qls = p->split ? take((size_t)2 * T * q_lora * 2) : 0;
+    p->ots = p->split ? take((size_t)2 * T * HV * 2) : 0;
+    p->kvb = wdt == K3CUDA_F32 ? take((size_t)H * (ML_DN + ML_DV) * ML_DL * 2) : 0;
+    p->att = take(mla_attend_kvb_workspace(T, cached, H));
+    p->total = off;
+}
+
+static int shape_ok(int T, int E, int H, int q_lora, int dn, int dr, int dl, int dv, int wdt,
+                    int cached, int cap) {
+    K3_ARG_CHECK(T >= 0 && E >= 8 && H >= 1 && q_lora >= 8 && cached >= 0 && cap >= 1,
+                 "mla_layer: bad shape T=%d E=%d H=%d q_lora=%d cached=%d cap=%d", T, E, H,
+                 q_lora, cached, cap);
+    K3_ARG_CHECK(wdt == K3CUDA_F32 || wdt == K3CUDA_BF16, "mla_layer: bad wdt %d", wdt);
+    if (dn != ML_DN || dr != ML_DR || dl != ML_DL || dv != ML_DV || H > 128 || E % 8 ||
+        q_lora % 8)
+        return set_error(K3CUDA_ERR_UNSUPPORTED, "mla_layer: dn=%d dr=%d dl=%d dv=%d H=%d E=%d "
+                         "q_lora=%d not built (the released head geometry 128/64/512/128, "
+                         "H <= 128, E and q_lora multiples of 8)", dn, dr, dl, dv, H, E, q_lora);
+    if ((long long)cached + T > cap)
+        return set_error(K3CUDA_ERR_ARG, "mla_layer: position %lld past the cache (cap %d)",
+                         (long long)cached + T - 1, cap);
+    return K3CUDA_OK;
+}
+
+static int grid_for(k3cuda_ctx *ctx, long long n) {
+    const long long want = (n + 255) / 256;
+    return (int)(want < 8LL * ctx->sm_count ? (want > 0 ? want : 1) : 8LL * ctx->sm_count);
+}
+
+}  // namespace k3
+
+using namespace k3;
+
+extern "C" int k3cuda_mla_layer_workspace(int T, int E, int H, int q_lora, int cached, int wdt,
+                                          size_t *bytes) {
+    K3_ARG_CHECK(bytes, "null bytes");
+    int rc = shape_ok(T, E, H, q_lora, ML_DN, ML_DR, ML_DL, ML_DV, wdt, cached, cached + T);
+    if (rc) return rc;
+    MlaLayerPlan p;
+    plan(T, E, H, q_lora, cached, wdt, &p);
+    *bytes = p.total;
+    return K3CUDA_OK;
+}
+
+extern "C" int k3cuda_mla_layer(k3cuda_ctx *ctx, float *out, const float *x,
+                                const k3cuda_mla_weights *w, int T, int E, int H, int q_lora,
+                                int dn, int dr, int dl, int dv, float rms_eps, void *latent,
+                                void *rope, int cached, int cap, void *workspace,
+                                size_t workspace_bytes) {
+    int rc = enter(ctx);
+    if (rc) return rc;
+    K3_ARG_CHECK(w, "mla_layer: null weights");
+    if ((rc = shape_ok(T, E, H, q_lora, dn, dr, dl, dv, w->wdt, cached, cap))) return rc;
+    if (T == 0) return K3CUDA_OK;
+    K3_ARG_CHECK(out && x && w->q_a && w->q_b && w->kv_a && w->kv_b && w->o && w->q_a_norm &&
+                 w->kv_a_norm && latent && rope, "mla_layer: null pointer");
+    const void *al[] = {out, x, w->q_a, w->q_b, w->kv_a, w->kv_b, w->o, w->q_a_norm,
+                        w->kv_a_norm, latent, rope};
+    for (const void *p : al)
+        K3_ARG_CHECK(aligned(p, 16), "mla_layer: pointers must be 16-byte aligned");
+    K3_ARG_CHECK(!w->g || aligned(w->g, 16), "mla_layer: g must be 16-byte aligned");
+    MlaLayerPlan pl;
+    plan(T, E, H, q_lora, cached, w->wdt, &pl);
+    if (workspace_bytes < pl.total || !workspace)
+        return set_error(K3CUDA_ERR_WORKSPACE, "mla_layer: workspace %zu < %zu bytes",
+                         workspace_bytes, pl.total);
+    K3_ARG_CHECK(aligned(workspace, 256), "mla_layer: workspace must be 256-byte aligned");
+    char *ws = (char *)workspace;
+    const int wdt = w->wdt, HV = H * ML_DV, HQ = H * (ML_DN + ML_DR), KW = ML_DL + ML_DR;
+    float *ql = (float *)(ws + pl.ql), *ct = (float *)(ws + pl.ct), *gb = (float *)(ws + pl.gb);
+    float *q = (float *)(ws + pl.q), *acc = (float *)(ws + pl.acc), *ot = (float *)(ws + pl.ot);
+    __nv_bfloat16 *qn = (__nv_bfloat16 *)(ws + pl.qn), *qr = (__nv_bfloat16 *)(ws + pl.qr);
+    __nv_bfloat16 *xs = pl.split ? (__nv_bfloat16 *)(ws + pl.xs) : nullptr;
+    __nv_bfloat16 *qls = pl.split ? (__nv_bfloat16 *)(ws + pl.qls) : nullptr;
+    __nv_bfloat16 *ots = pl.split ? (__nv_bfloat16 *)(ws + pl.ots) : nullptr;
+    // projections of x: q_a, kv_a and the gate
+    if (!pl.gemm) {
+        Proj pr[3] = {{w->q_a, ql, q_lora}, {w->kv_a, ct, KW}, {w->g, gb, HV}};
+        if ((rc = matvec(ctx, x, T, E, pr, w->g ? 3 : 2, wdt))) return rc;
+    } else {
+        if (pl.split && (rc = split(ctx, xs, x, (long long)T * E))) return rc;
+        if ((rc = gemm(ctx, ql, x, xs, w->q_a, wdt, T, E, q_lora))) return rc;
+        if ((rc = gemm(ctx, ct, x, xs, w->kv_a, wdt, T, E, KW))) return rc;
+        if (w->g && (rc = gemm(ctx, gb, x, xs, w->g, wdt, T, E, HV))) return rc;
+    }
+    // q = q_b(RMSNorm(ql))
+    rmsnorm_rows<<<T, 256, 0, ctx->stream>>>(ql, w->q_a_norm, q_lora, rms_eps);
+    if ((rc = after_launch(ctx, "rmsnorm_rows"))) return rc;
+    if (pl.split && (rc = split(ctx, qls, ql, (long long)T * q_lora))) return rc;
+    if ((rc = project(ctx, q, ql, qls, w->q_b, wdt, T, q_lora, HQ))) return rc;
+    // the new latent / rope rows (kv_a_norm over the latent only)
+    if ((rc = k3cuda_mla_cache_append(ctx, latent, rope, ct, w->kv_a_norm, rms_eps, 0, cached, T,
+                                      1, cap, ML_DL, ML_DR)))
+        return rc;
+    mla_q_split<<<T, 256, 0, ctx->stream>>>(qn, qr, q, H);
+    if ((rc = after_launch(ctx, "mla_q_split"))) return rc;
+    const void *kvb = w->kv_b;
+    if (wdt == K3CUDA_F32) {
+        const long long n = (long long)H * (ML_DN + ML_DV) * ML_DL;
+        f32_to_bf16<<<grid_for(ctx, n), 256, 0, ctx->stream>>>((__nv_bfloat16 *)(ws + pl.kvb),
+                                                              (const float *)w->kv_b, n);
+        if ((rc = after_launch(ctx, "f32_to_bf16"))) return rc;
+        kvb = ws + pl.kvb;
+    }
+    const float scale = 1.0f / sqrtf((float)(ML_DN + ML_DR));
+    if ((rc = mla_attend_kvb(ctx, acc, qn, qr, latent, rope, kvb, T, cached, cap, H, scale,
+                             ws + pl.att, pl.total - pl.att)))
+        return rc;
+    const long long n = (long long)T * HV;
+    mla_gate<<<grid_for(ctx, n), 256, 0, ctx->stream>>>(ot, ots, ots ? ots + n : nullptr, acc,
+                                                       w->g ? gb : nullptr, n);
+    if ((rc = after_launch(ctx, "mla_gate"))) return rc;
+    return project(ctx, out, ot, ots, w->o, wdt, T, HV, E);
+}

@@ -58,6 +58,9 @@ SIGNATURES = {
     "k3cuda_mla_attend": (_i, [_vp, _vp, _i, _vp, _vp, _vp, _vp, _vp, _vp, _ip, _ip, _i, _i, _i,
                                _i, _i, _i, _i, _i, _f, _vp, _sz]),
     "k3cuda_mla_cache_append": (_i, [_vp, _vp, _vp, _vp, _vp, _f, _i, _i, _i, _i, _i, _i, _i]),
+    "k3cuda_mla_layer_workspace": (_i, [_i, _i, _i, _i, _i, _i, C.POINTER(_sz)]),
+    "k3cuda_mla_layer": (_i, [_vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _i, _i, _f, _vp, _vp,
+                              _i, _i, _vp, _sz]),
     "k3cuda_comm_unique_id": (_i, [C.c_char_p]),
     "k3cuda_comm_init": (_i, [_vp, _i, _i, C.c_char_p]),
     "k3cuda_allgather_heads_workspace": (_i, [_i, _i, _i, _i, _i, C.POINTER(_sz)]),
@@ -82,6 +85,12 @@ class KdaWeights(C.Structure):
     _fields_ = [("q", _vp), ("k", _vp), ("v", _vp), ("q_conv", _vp), ("k_conv", _vp),
                 ("v_conv", _vp), ("f_a", _vp), ("f_b", _vp), ("A_log", _vp), ("dt_bias", _vp),
                 ("b", _vp), ("g", _vp), ("o_norm", _vp), ("o", _vp), ("wdt", _i)]
+
+
+class MlaWeights(C.Structure):
+    """k3cuda_mla_weights: device pointers of one MLA layer, in K3MlaW's field order."""
+    _fields_ = [("q_a", _vp), ("q_b", _vp), ("kv_a", _vp), ("kv_b", _vp), ("o", _vp),
+                ("g", _vp), ("q_a_norm", _vp), ("kv_a_norm", _vp), ("wdt", _i)]
 
 
 KDA_WEIGHT_NAMES = ("q", "k", "v", "q_conv", "k_conv", "v_conv", "f_a", "f_b", "A_log",
@@ -331,6 +340,20 @@ class Context:
         check(lib().k3cuda_mla_cache_append(self.h, _ptr(latent), _ptr(rope), _ptr(ct),
                                             _ptr(kv_a_norm), float(eps), int(seq), int(pos0),
                                             int(T), int(n_cache), int(cap), 512, 64))
+
+    def mla_layer_workspace(self, T, E, H, q_lora, cached, wdt) -> int:
+        return _ws_query(lib().k3cuda_mla_layer_workspace, int(T), int(E), int(H), int(q_lora),
+                         int(cached), int(wdt))
+
+    def mla_layer(self, out, x, weights, wdt, T, E, H, q_lora, rms_eps, latent, rope, cached,
+                  cap, workspace, workspace_bytes):
+        """weights: mapping of MlaWeights field names to device buffers ("g" may be None)."""
+        w = MlaWeights(**{n: _ptr(weights.get(n)) for n, _ in MlaWeights._fields_[:-1]},
+                       wdt=int(wdt))
+        check(lib().k3cuda_mla_layer(self.h, _ptr(out), _ptr(x), C.byref(w), int(T), int(E),
+                                     int(H), int(q_lora), 128, 64, 512, 128, float(rms_eps),
+                                     _ptr(latent), _ptr(rope), int(cached), int(cap),
+                                     _ptr(workspace), int(workspace_bytes)))
 
     # multi-GPU -------------------------------------------------------------------
     def comm_init(self, nranks: int, rank: int, uid: bytes):

@@ -82,6 +82,9 @@ def ref():
         u8p = np.ctypeslib.ndpointer(dtype=np.uint8, flags="C_CONTIGUOUS")
         R.k3_mxfp4_dequant.argtypes = [f32p, u8p, u8p, C.c_int, C.c_int, C.c_int]
         R.k3_matmul_mxfp4.argtypes = [f32p, f32p, u8p, u8p, C.c_int, C.c_int, C.c_int]
+        R.k3ref_mla_cached.argtypes = ([f32p, f32p] + [C.c_int] * 8 + [C.c_float]
+                                       + [C.c_void_p] * 6 + [f32p, f32p, C.c_int, f32p, f32p,
+                                                             C.c_int, C.c_int])
         R.k3ref_kda_layer.argtypes = ([f32p, f32p] + [C.c_int] * 5 + [C.c_float, C.c_float]
                                       + [C.c_void_p] * 3 + [f32p] * 3 + [C.c_void_p] * 2
                                       + [f32p] * 2 + [C.c_void_p] * 2 + [f32p, C.c_void_p,
@@ -211,6 +214,34 @@ def ref_kda_layer(x, w, H, D, K, lb, eps, state=None, wdt=0):
             args.append(_f32(w[n]))
     ref().k3ref_kda_layer(out, x, T, E, H, D, K, float(lb), float(eps), *args, int(wdt),
                           None if state is None else state.ctypes.data)
+    return out
+
+
+# ------------------------------------------------------------------------ MLA layer
+MLA_WEIGHTS = ("q_a", "q_b", "kv_a", "kv_b", "o", "g", "q_a_norm", "kv_a_norm")
+
+
+def ref_mla_cached(x, w, H, q_lora, eps, kvc, ropec, cached, wdt=0, kv_lora=512, qk_nope=128,
+                   qk_rope=64, v_head=128):
+    """The reference's own k3_mla_cached (oracle/_ref) on x [T][E] with its EXPANDED caches
+    kvc [cap][H*(qk_nope+v_head)] and ropec [cap][qk_rope] (updated in place). w: host
+    weights by MLA_WEIGHTS name (projections fp32, or bf16 bits when wdt=1; "g" may be
+    None)."""
+    x = _f32(x)
+    T, E = x.shape
+    out = np.zeros((T, E), np.float32)
+    keep, ptrs = [], []
+    for n in ("q_a", "q_b", "kv_a", "kv_b", "o", "g"):
+        if w.get(n) is None:
+            ptrs.append(None)
+            continue
+        a = np.ascontiguousarray(w[n], np.uint16 if wdt == 1 else np.float32)
+        keep.append(a)
+        ptrs.append(a.ctypes.data)
+    cap = kvc.shape[0]
+    ref().k3ref_mla_cached(out, x, T, E, H, q_lora, kv_lora, qk_nope, qk_rope, v_head,
+                           float(eps), *ptrs, _f32(w["q_a_norm"]), _f32(w["kv_a_norm"]),
+                           int(wdt), kvc, ropec, int(cached), int(cap))
     return out
 
 

@@ -113,3 +113,28 @@ void k3ref_kda_layer(float *out, const float *x, int T, int E, int H, int D, int
     k3_kda_layer(out, x, &w, &c, T, state, scratch);
     free(scratch);
 }
+
+/* One k3_mla_cached call (src/core/k3_ops.c:321-424) with the config fields it reads set
+ * (hidden, n_heads, qk_nope, qk_rope, v_head, q_lora, kv_lora, rms_eps) and its cached-mode
+ * scratch (k3_mla_scratch_cached). kvc [cap][H*(qk_nope+v_head)] and ropec [cap][qk_rope]
+ * are the reference's expanded caches; g may be NULL (no gate). */
+void k3ref_mla_cached(float *out, const float *x, int T, int E, int H, int q_lora,
+                      int kv_lora, int qk_nope, int qk_rope, int v_head, float eps,
+                      const void *q_a, const void *q_b, const void *kv_a, const void *kv_b,
+                      const void *o, const void *g, const float *q_a_norm,
+                      const float *kv_a_norm, int wdt, float *kvc, float *ropec, int cached,
+                      int cap)
+{
+    K3Cfg c;
+    memset(&c, 0, sizeof c);
+    c.hidden = E; c.n_heads = H; c.qk_nope = qk_nope; c.qk_rope = qk_rope; c.v_head = v_head;
+    c.q_lora = q_lora; c.kv_lora = kv_lora; c.rms_eps = eps;
+    K3MlaW w;
+    memset(&w, 0, sizeof w);
+    w.q_a = q_a; w.q_b = q_b; w.kv_a = kv_a; w.kv_b = kv_b; w.o = o; w.g = g;
+    w.q_a_norm = q_a_norm; w.kv_a_norm = kv_a_norm; w.wdt = wdt;
+    float *scratch = (float *)malloc(k3_mla_scratch_cached(&c, T, cap, 1) * sizeof(float));
+    if (!scratch) abort();
+    k3_mla_cached(out, x, &w, &c, T, scratch, kvc, ropec, cached, cap);
+    free(scratch);
+}
