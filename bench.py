@@ -21,6 +21,9 @@ Other workloads (for the per-path records; one JSON line each):
   moe_experts  one decode token through 16 routed experts' MXFP4 weights (k3_moe's expert
            step): w1 and w3 (3072 x 3584) on z, then w2 (3584 x 3072) on each expert's
            activation, as two batched launches (tokens/s)
+  mla_layer  the whole MLA layer forward (k3_mla_cached) at the model's shape: hidden
+           7168, 96 heads, q_lora 1536, latent 512 + rope 64, bf16 weights; --tokens T new
+           tokens after --context positions already cached (default 1 after 8191)
   layer    the whole KDA layer forward (k3_kda_layer) at the model's shape: hidden 7168,
            96 heads of 128, conv 4, bf16 projection weights; --tokens T per call (default
            1: a decode step, weight streaming; e.g. 4096: a prefill chunk) (tokens/s)
@@ -617,6 +620,114 @@ def cpu_layer_baseline(T, budget_s=10.0):
                       f"(bf16 weights, OpenMP matmuls and heads)"}
 
 
+# ------------------------------------------------------------------- mla layer
+MLA_E, MLA_H, MLA_QL = 7168, 96, 1536
+
+
+def mla_layer_bytes(T, ctx_len, E=MLA_E, H=MLA_H, QL=MLA_QL):
+    """bf16 weights once, the latent + rope cache of every attended position once, x/out."""
+    weights = 2 * (QL * E + H * 192 * QL + 576 * E + H * 256 * 512 + E * H * 128 + H * 128 * E)
+    return weights + ctx_len * 576 * 2 + 2 * T * E * 4
+
+
+def mla_layer_inputs(seed, T, ctx_len, E=MLA_E, H=MLA_H, QL=MLA_QL):
+    rng = np.random.default_rng(seed)
+    pool = W.f32_to_bf16(rng.standard_normal(1 << 22, dtype=np.float32) * np.float32(0.02))
+    mk = lambda r, c: np.resize(np.roll(pool, r), (r, c))  # noqa: E731
+    w = dict(q_a=mk(QL, E), q_b=mk(H * 192, QL), kv_a=mk(576, E), kv_b=mk(H * 256, 512),
+             o=mk(E, H * 128), g=mk(H * 128, E),
+             q_a_norm=np.ones(QL, np.float32), kv_a_norm=np.ones(512, np.float32))
+    lat = W.f32_to_bf16(rng.standard_normal((ctx_len, 512), dtype=np.float32) * np.float32(0.5))
+    rope = W.f32_to_bf16(rng.standard_normal((ctx_len, 64), dtype=np.float32))
+    x = rng.standard_normal((T, E), dtype=np.float32)
+    return w, lat, rope, x
+
+
+def bench_mla_layer(args, D: Dist):
+    import k3cuda
+    ctx = k3cuda.Context(D.local)
+    T = args.tokens or 1
+    cached = args.context if args.context is not None else 8192 - T
+    cap = cached + T
+    w, lat, rope, x = mla_layer_inputs(D.rank, T, cap)
+    dev = {n: ctx.upload(a) for n, a in w.items()}
+    dlat, drope, dx = ctx.upload(lat), ctx.upload(rope), ctx.upload(x)
+    dout = ctx.empty((T, MLA_E), np.float32)
+    nws = ctx.mla_layer_workspace(T, MLA_E, MLA_H, MLA_QL, cached, k3cuda.BF16)
+    ws = ctx.empty((nws,), np.uint8)
+
+    def step():  # rewrites the same T rows at cached.. every step
+        ctx.mla_layer(dout, dx, dev, k3cuda.BF16, T, MLA_E, MLA_H, MLA_QL, 1e-5, dlat, drope,
+                      cached, cap, ws, nws)
+
+    for _ in range(args.warmup):
+        step()
+    ctx.sync()
+    clk = ClockSampler(D.local)
+    clk.start()
+    time.sleep(0.3)
+    D.barrier()
+    ctx.sync()
+    l0 = ctx.launches()
+    t0 = clk.mark()
+    ctx.record(0)
+    for _ in range(args.steps):
+        step()
+    ctx.record(1)
+    ctx.sync()
+    t1 = clk.mark()
+    D.barrier()
+    l1 = ctx.launches()
+    ms_max = D.max(ctx.elapsed_ms(0, 1))
+    clocks = clk.stop(t0, t1)
+    hx = ctx.pinned((T, MLA_E), np.float32)
+    hx[...] = x
+    ho = ctx.pinned((T, MLA_E), np.float32)
+    L = k3cuda.lib()
+
+    def e2e_step():
+        k3cuda.check(L.k3cuda_memcpy_h2d(ctx.h, dx.ptr, hx.ctypes.data, hx.nbytes))
+        step()
+        k3cuda.check(L.k3cuda_memcpy_d2h(ctx.h, ho.ctypes.data, dout.ptr, ho.nbytes))
+
+    for _ in range(3):
+        e2e_step()
+    ctx.sync()
+    D.barrier()
+    ctx.record(2)
+    for _ in range(args.steps):
+        e2e_step()
+    ctx.record(3)
+    ctx.sync()
+    D.barrier()
+    ms_e2e = D.max(ctx.elapsed_ms(2, 3))
+    hbm, tf, src = peaks()
+    per = ms_max / 1e3 / args.steps
+    alg = mla_layer_bytes(T, cap)
+    line = {
+        "metric": f"MLA layer forward tokens/s (mla_layer_T{T}_ctx{cap}: hidden {MLA_E}, "
+                  f"{MLA_H} heads, bf16 weights)",
+        "value": T * args.steps * D.world / (ms_max / 1e3), "unit": "tokens/s",
+        "n_gpus": D.world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": ms_max / args.steps, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "fp32",
+        "data": "synthetic (pooled bf16 weights, seeded latent cache and activations)",
+        "config": {"workload": f"mla_layer_T{T}_ctx{cap}", "tokens_per_call": T,
+                   "context": cap, "hidden": MLA_E, "heads": MLA_H, "q_lora": MLA_QL,
+                   "kv_lora": 512, "qk_rope": 64, "weights": "bf16",
+                   "parallelism": f"replica x{D.world}",
+                   "l2": f"weights larger than L2 ({alg / 1e6:.0f} MB per call)"},
+        "e2e": {"value": T * args.steps * D.world / (ms_e2e / 1e3), "unit": "tokens/s",
+                "h2d_bytes_per_step": hx.nbytes, "d2h_bytes_per_step": ho.nbytes},
+        "roofline": {"bound": "hbm", "achieved": alg / per / 1e9, "peak": hbm, "unit": "GB/s",
+                     "frac": alg / per / 1e9 / hbm, "peak_source": src, "traffic": None,
+                     "algorithmic_bytes_per_launch": alg},
+        "gpu_launches": int(l1 - l0), "clocks": clocks,
+    }
+    ctx.close()
+    return line
+
+
 # ----------------------------------------------------------------- moe experts
 MOE_TOPK, MOE_I, MOE_L = 16, 3072, 3584
 
@@ -912,7 +1023,9 @@ def main():
     ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--workload", default="decode",
                     choices=["decode", "prefill", "varlen", "mla", "mla_prefill", "layer",
-                             "moe_experts"])
+                             "moe_experts", "mla_layer"])
+    ap.add_argument("--context", type=int, default=None,
+                    help="mla_layer: positions already in the cache before the new tokens")
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--tokens", type=int, default=None,
@@ -936,6 +1049,8 @@ def main():
         line = bench_mla_prefill(args, D)
     elif args.workload == "moe_experts":
         line = bench_moe_experts(args, D)
+    elif args.workload == "mla_layer":
+        line = bench_mla_layer(args, D)
     else:
         line = bench_mla(args, D)
     if D.rank == 0:

@@ -3,6 +3,8 @@
 #include <stdlib.h>
 #include <string.h>
 
+#include <mutex>
+
 #include "internal.cuh"
 
 namespace k3 {
@@ -30,6 +32,48 @@ int after_launch(k3cuda_ctx *ctx, const char *what) {
     if (e != cudaSuccess)
         return set_error(K3CUDA_ERR_CUDA, "%s launch failed: %s", what, cudaGetErrorString(e));
     ctx->launches++;
+    return K3CUDA_OK;
+}
+
+int set_smem(const void *func, int bytes) {
+    struct Ent { const void *f; int dev, bytes; };
+    static Ent tab[128];
+    static int n = 0;
+    static std::mutex mu;
+    int dev = 0;
+    K3_CUDA_TRY(cudaGetDevice(&dev));
+    std::lock_guard<std::mutex> lk(mu);
+    for (int i = 0; i < n; i++)
+        if (tab[i].f == func && tab[i].dev == dev && tab[i].bytes >= bytes) return K3CUDA_OK;
+    K3_CUDA_TRY(cudaFuncSetAttribute(func, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes));
+    if (n < 128) tab[n++] = Ent{func, dev, bytes};
+    return K3CUDA_OK;
+}
+
+constexpr int PIN_SLOTS = 16;
+constexpr size_t PIN_SLOT = 512u << 10;
+
+int stage_h2d(k3cuda_ctx *ctx, void *dst, const void *src, size_t bytes) {
+    if (bytes == 0) return K3CUDA_OK;
+    if (bytes > PIN_SLOT) {
+        K3_CUDA_TRY(cudaMemcpyAsync(dst, src, bytes, cudaMemcpyHostToDevice, ctx->stream));
+        return K3CUDA_OK;
+    }
+    if (!ctx->pin) {
+        K3_CUDA_TRY(cudaMallocHost((void **)&ctx->pin, PIN_SLOTS * PIN_SLOT));
+        for (int i = 0; i < PIN_SLOTS; i++) {
+            K3_CUDA_TRY(cudaEventCreateWithFlags(&ctx->pin_ev[i], cudaEventDisableTiming));
+            ctx->pin_used[i] = false;
+        }
+    }
+    const int slot = ctx->pin_next;
+    ctx->pin_next = (slot + 1) % PIN_SLOTS;
+    if (ctx->pin_used[slot]) K3_CUDA_TRY(cudaEventSynchronize(ctx->pin_ev[slot]));
+    unsigned char *buf = ctx->pin + (size_t)slot * PIN_SLOT;
+    memcpy(buf, src, bytes);
+    K3_CUDA_TRY(cudaMemcpyAsync(dst, buf, bytes, cudaMemcpyHostToDevice, ctx->stream));
+    K3_CUDA_TRY(cudaEventRecord(ctx->pin_ev[slot], ctx->stream));
+    ctx->pin_used[slot] = true;
     return K3CUDA_OK;
 }
 
@@ -94,6 +138,11 @@ int k3cuda_shutdown(k3cuda_ctx *ctx) {
         if (ctx->events[i]) cudaEventDestroy(ctx->events[i]);
     if (ctx->flush_buf) cudaFree(ctx->flush_buf);
     if (ctx->err_word) cudaFree(ctx->err_word);
+    if (ctx->pin) {
+        for (int i = 0; i < PIN_SLOTS; i++)
+            if (ctx->pin_ev[i]) cudaEventDestroy(ctx->pin_ev[i]);
+        cudaFreeHost(ctx->pin);
+    }
     if (ctx->ev_fork) cudaEventDestroy(ctx->ev_fork);
     if (ctx->ev_join) cudaEventDestroy(ctx->ev_join);
     if (ctx->aux) cudaStreamDestroy(ctx->aux);

@@ -29,6 +29,11 @@ struct k3cuda_ctx {
     void *blas;                 // cuBLAS handle of the projections (kda_layer.cu), lazily made
     cudaStream_t aux;           // side stream for work that overlaps the main stream's
     cudaEvent_t ev_fork, ev_join;  // (forked from and joined back into `stream`)
+    // page-locked ring for the small per-call host tables (stage_h2d)
+    unsigned char *pin;
+    int pin_next;
+    cudaEvent_t pin_ev[16];
+    bool pin_used[16];
 };
 
 namespace k3 {
@@ -68,6 +73,19 @@ int mla_attend_kvb(k3cuda_ctx *ctx, float *acc, const void *q_nope, const void *
                    const void *latent, const void *rope, const void *kv_b, int T, int cached,
                    int cap, int H, float scale, void *workspace, size_t workspace_bytes);
 size_t mla_attend_kvb_workspace(int T, int cached, int H);
+
+// Host -> device copy of a small per-call table on the context's stream without the
+// stream synchronisation a pageable source may cost: the bytes go through a slot of a
+// page-locked ring (16 slots of 512 KB; a slot is reused once the copy that last read it
+// has completed). Larger tables fall back to a plain copy.
+int stage_h2d(k3cuda_ctx *ctx, void *dst, const void *src, size_t bytes);
+
+// cudaFuncSetAttribute(func, MaxDynamicSharedMemorySize, bytes) on the current device,
+// skipped when this (function, device) pair already has at least `bytes`.
+int set_smem(const void *func, int bytes);
+template <typename F> inline int set_smem(F *func, int bytes) {
+    return set_smem(reinterpret_cast<const void *>(func), bytes);
+}
 
 // Record an error message for the calling thread; returns `code`.
 int set_error(int code, const char *fmt, ...);

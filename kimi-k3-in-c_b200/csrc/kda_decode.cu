@@ -169,8 +169,7 @@ static int launch_decode(k3cuda_ctx *ctx, float *state, void *o, const void *q, 
     }
     const size_t smem = ((size_t)dk * dv + 3 * dk + 2 * dv) * sizeof(float);
     if (smem > 48 * 1024)
-        K3_CUDA_TRY(cudaFuncSetAttribute(kda_decode_general<IO>,
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+        if (int rc_ = set_smem(kda_decode_general<IO>, (int)smem)) return rc_;
     kda_decode_general<IO><<<nstream, 256, smem, ctx->stream>>>(state, op, qp, kp, vp, gate, beta,
                                                                 dk, dv, q_scale, gate_is_log);
     return after_launch(ctx, "kda_decode_general");

@@ -28,6 +28,8 @@
 #include <type_traits>
 #include <vector>
 
+#include <string.h>
+
 #include "internal.cuh"
 
 namespace k3 {
@@ -316,11 +318,13 @@ static int run_prefill(k3cuda_ctx *ctx, float *state, void *o, const void *q, co
     ChunkDesc *d_table = (ChunkDesc *)wsb;
     int *d_c0 = (int *)(wsb + align256((size_t)nc * sizeof(ChunkDesc)));
     float *blocks = (float *)(wsb + table_bytes(nc, n_seq));
-    if (nc > 0)
-        K3_CUDA_TRY(cudaMemcpyAsync(d_table, table.data(), (size_t)nc * sizeof(ChunkDesc),
-                                    cudaMemcpyHostToDevice, ctx->stream));
-    K3_CUDA_TRY(cudaMemcpyAsync(d_c0, c0.data(), (size_t)(n_seq + 1) * sizeof(int),
-                                cudaMemcpyHostToDevice, ctx->stream));
+    {
+        // the chunk table and the sequence offsets are adjacent: one image, one copy
+        std::vector<unsigned char> img(table_bytes(nc, n_seq), 0);
+        if (nc > 0) memcpy(img.data(), table.data(), (size_t)nc * sizeof(ChunkDesc));
+        memcpy(img.data() + ((char *)d_c0 - wsb), c0.data(), (size_t)(n_seq + 1) * sizeof(int));
+        if (int rc = stage_h2d(ctx, wsb, img.data(), img.size())) return rc;
+    }
     if constexpr (std::is_same<IO, __nv_bfloat16>::value && DK == 128) {
         // bf16 operands on the tensor cores (every operand bf16, accumulation fp32)
         if (nc == 0) return K3CUDA_OK;
@@ -330,8 +334,7 @@ static int run_prefill(k3cuda_ctx *ctx, float *state, void *o, const void *q, co
     if (nc > 0) {
         const size_t smem1 =
             ((size_t)4 * KC * DK + 2 * KSUB * DK + 3 * KC * KC + KC) * sizeof(float);
-        K3_CUDA_TRY(cudaFuncSetAttribute(kda_chunk_intra<IO, DK>,
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem1));
+        if (int rc_ = set_smem(kda_chunk_intra<IO, DK>, (int)smem1)) return rc_;
         dim3 g1((unsigned)nc, (unsigned)H);
         kda_chunk_intra<IO, DK><<<g1, 256, smem1, ctx->stream>>>(
             d_table, (const IO *)q, (const IO *)k, gate, beta, blocks, H, q_scale, gate_is_log);
@@ -340,8 +343,7 @@ static int run_prefill(k3cuda_ctx *ctx, float *state, void *o, const void *q, co
     }
     const size_t smem2 = ((size_t)3 * KC * DK + 2 * KC * KC + DK * SCAN_DVT + 2 * KC * SCAN_DVT +
                           DK) * sizeof(float);
-    K3_CUDA_TRY(cudaFuncSetAttribute(kda_chunk_scan<IO, DK>,
-                                     cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem2));
+    if (int rc_ = set_smem(kda_chunk_scan<IO, DK>, (int)smem2)) return rc_;
     const long long nblk = (long long)n_seq * H * (DK / SCAN_DVT);
     if (nblk > 0) {
         kda_chunk_scan<IO, DK><<<(unsigned)nblk, 256, smem2, ctx->stream>>>(

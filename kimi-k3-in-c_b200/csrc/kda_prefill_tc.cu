@@ -1040,8 +1040,7 @@ int run_prefill_tc(k3cuda_ctx *ctx, float *state, void *o, const void *q, const 
     if (!rc) rc = make_tmap_3d(&pm.a, b + WB_A, BF, 2, 64, 64, nch, 128, WB_BYTES, 64, 64, 1);
     if (!rc) rc = make_tmap_3d(&pm.al, b + WB_AL, BF, 2, 64, 64, nch, 128, WB_BYTES, 64, 64, 1);
     if (rc) return rc;
-    K3_CUDA_TRY(cudaFuncSetAttribute(kda_prep_tc, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                     PS_SMEM));
+    if (int rc_ = set_smem(kda_prep_tc, PS_SMEM)) return rc_;
     kda_prep_tc<<<dim3((unsigned)nc, (unsigned)H), 256, PS_SMEM, ctx->stream>>>(
         pm, (const TcChunk *)d_table, gate, beta, (const __nv_bfloat16 *)q,
         (const __nv_bfloat16 *)k, (uint8_t *)blocks, H, q_scale, gate_is_log, ctx->err_word);
@@ -1054,15 +1053,13 @@ int run_prefill_tc(k3cuda_ctx *ctx, float *state, void *o, const void *q, const 
     const bool wide = (long long)n_seq * H >= ctx->sm_count;
     if (wide) {
         using C = ScanCfg<128>;
-        K3_CUDA_TRY(cudaFuncSetAttribute(kda_scan_tc<128>,
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM));
+        if (int rc_ = set_smem(kda_scan_tc<128>, C::SMEM)) return rc_;
         kda_scan_tc<128><<<(unsigned)((long long)n_seq * H), 192, C::SMEM, ctx->stream>>>(
             sm, (const TcChunk *)d_table, d_c0, b, state, (__nv_bfloat16 *)o, H, gout,
             ctx->err_word);
     } else {
         using C = ScanCfg<64>;
-        K3_CUDA_TRY(cudaFuncSetAttribute(kda_scan_tc<64>,
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM));
+        if (int rc_ = set_smem(kda_scan_tc<64>, C::SMEM)) return rc_;
         kda_scan_tc<64><<<(unsigned)((long long)n_seq * H * 2), 192, C::SMEM, ctx->stream>>>(
             sm, (const TcChunk *)d_table, d_c0, b, state, (__nv_bfloat16 *)o, H, gout,
             ctx->err_word);

@@ -43,6 +43,8 @@
 // Every wait is bounded (sm100.cuh): on a timeout the kernel records an error word, skips
 // the rest of its work, waits briefly for its own loads and frees TMEM; k3cuda_sync then
 // reports K3CUDA_ERR_TIMEOUT.
+#include <string.h>
+
 #include <algorithm>
 #include <vector>
 
@@ -58,6 +60,7 @@ constexpr int MLA_DN = 128, MLA_DR = 64, MLA_DL = 512, MLA_DV = 128;
 constexpr int MLA_QW = MLA_DL + MLA_DR;    // 576: absorbed query width
 constexpr int MLA_HP = 128;                // heads padded to the MMA's M
 constexpr int MLA_TILE = 64;               // tokens per tile
+constexpr int MLA_MIN_TILES = 4;           // fewest tiles the work plan gives a cluster
 constexpr int MLA_NST = 3;                 // KV pipeline stages
 constexpr int MLA_KVBLK = MLA_TILE * 128;  // bytes of one 64-dim block of a KV tile
 constexpr int MLA_NBLK = 5;                // dim blocks of rank 0 (4 latent + rope); rank 1: 4
@@ -677,7 +680,10 @@ static void mla_plan(const int *ctx_lens, int B, int max_clusters, MlaPlan &p) {
     std::vector<long long> tstart((size_t)B + 1, 0);
     for (int b = 0; b < B; b++) tstart[b + 1] = tstart[b] + (ctx_lens[b] + MLA_TILE - 1) / MLA_TILE;
     const long long nt = tstart[B];
-    p.ncl = (int)std::max<long long>(1, std::min<long long>(max_clusters, nt));
+    // at least MLA_MIN_TILES tiles per cluster: a cluster's fixed cost (TMEM, barriers, the
+    // query load) and the merge of its partial outweigh a single tile
+    p.ncl = (int)std::max<long long>(
+        1, std::min<long long>(max_clusters, (nt + MLA_MIN_TILES - 1) / MLA_MIN_TILES));
     p.segs.clear();
     p.cl_begin.assign((size_t)p.ncl + 1, 0);
     p.slot0.assign((size_t)B + 1, 0);
@@ -783,16 +789,20 @@ static int mla_run(k3cuda_ctx *ctx, void *out, int out_dtype, const void *q_nope
     float *part = (float *)w;
     w += align256((size_t)nseg * H * MLA_PART * sizeof(float));
     __nv_bfloat16 *olat2 = (__nv_bfloat16 *)w;
-    K3_CUDA_TRY(cudaMemcpyAsync(d_segs, p.segs.data(), (size_t)nseg * sizeof(MlaSeg),
-                                cudaMemcpyHostToDevice, ctx->stream));
-    K3_CUDA_TRY(cudaMemcpyAsync(d_cl, p.cl_begin.data(), p.cl_begin.size() * sizeof(int),
-                                cudaMemcpyHostToDevice, ctx->stream));
-    K3_CUDA_TRY(cudaMemcpyAsync(d_slot0, p.slot0.data(), ((size_t)B + 1) * sizeof(int),
-                                cudaMemcpyHostToDevice, ctx->stream));
-    K3_CUDA_TRY(cudaMemcpyAsync(d_lens, ctx_lens, (size_t)B * sizeof(int), cudaMemcpyHostToDevice,
-                                ctx->stream));
-    K3_CUDA_TRY(cudaMemcpyAsync(d_row0, row0.data(), (size_t)B * sizeof(int),
-                                cudaMemcpyHostToDevice, ctx->stream));
+    {
+        // the five tables sit back to back at the start of the workspace: one image, one copy
+        const size_t tbytes = (size_t)((char *)qlat - (char *)workspace);
+        std::vector<unsigned char> img(tbytes, 0);
+        auto put = [&](const void *dptr, const void *src, size_t n) {
+            memcpy(img.data() + ((const char *)dptr - (const char *)workspace), src, n);
+        };
+        put(d_segs, p.segs.data(), (size_t)nseg * sizeof(MlaSeg));
+        put(d_cl, p.cl_begin.data(), p.cl_begin.size() * sizeof(int));
+        put(d_slot0, p.slot0.data(), ((size_t)B + 1) * sizeof(int));
+        put(d_lens, ctx_lens, (size_t)B * sizeof(int));
+        put(d_row0, row0.data(), (size_t)B * sizeof(int));
+        if ((rc = stage_h2d(ctx, workspace, img.data(), tbytes))) return rc;
+    }
     if (H < MLA_HP)  // the padded query rows must score zero
         K3_CUDA_TRY(cudaMemset2DAsync(qlat + (size_t)H * MLA_QW, (size_t)MLA_HP * MLA_QW * 2, 0,
                                       (size_t)(MLA_HP - H) * MLA_QW * 2, (size_t)B, ctx->stream));
@@ -824,15 +834,13 @@ static int mla_run(k3cuda_ctx *ctx, void *out, int out_dtype, const void *q_nope
 
     const dim3 hgrid(H, (B + 127) / 128);
     const int qsmem = 2 * 16384 + 16 * 8192 + 1024;
-    K3_CUDA_TRY(cudaFuncSetAttribute(mla_q_absorb_tc, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                     qsmem));
+    if (int rc_ = set_smem(mla_q_absorb_tc, qsmem)) return rc_;
     mla_q_absorb_tc<<<hgrid, 128, qsmem, ctx->stream>>>(qmaps, (const __nv_bfloat16 *)q_rope, qlat,
                                                         B, H, ctx->err_word);
     rc = after_launch(ctx, "mla_q_absorb_tc");
     if (rc) return rc;
 
-    K3_CUDA_TRY(cudaFuncSetAttribute(mla_attend_tc, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                     MLA_SMEM));
+    if (int rc_ = set_smem(mla_attend_tc, MLA_SMEM)) return rc_;
     const float scale_log2e = scale * 1.4426950408889634f;
     mla_attend_tc<<<2 * p.ncl, MLA_THREADS, MLA_SMEM, ctx->stream>>>(maps, d_segs, d_cl, d_lens, qlat,
                                                            part, H, d_row0, scale_log2e,
@@ -846,13 +854,11 @@ static int mla_run(k3cuda_ctx *ctx, void *out, int out_dtype, const void *q_nope
 
     const int psmem = 12 * 16384 + 1024;
     if (out_dtype == K3CUDA_BF16) {
-        K3_CUDA_TRY(cudaFuncSetAttribute(mla_project_tc<__nv_bfloat16>,
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize, psmem));
+        if (int rc_ = set_smem(mla_project_tc<__nv_bfloat16>, psmem)) return rc_;
         mla_project_tc<__nv_bfloat16><<<hgrid, 128, psmem, ctx->stream>>>(
             pmaps, (__nv_bfloat16 *)out, B, H, ctx->err_word);
     } else {
-        K3_CUDA_TRY(cudaFuncSetAttribute(mla_project_tc<float>,
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize, psmem));
+        if (int rc_ = set_smem(mla_project_tc<float>, psmem)) return rc_;
         mla_project_tc<float><<<hgrid, 128, psmem, ctx->stream>>>(pmaps, (float *)out, B, H,
                                                                   ctx->err_word);
     }

@@ -24,7 +24,7 @@ __global__ void rmsnorm_rows(float *__restrict__ x, const float *__restrict__ w,
     __shared__ double red[32];
     float *row = x + (size_t)blockIdx.x * n;
     double ss = 0.0;
-    for (int i = threadIdx.x; i < n; i += blockDim.x) ss += (double)row[i] * (double)row[i];
+    for (int i = threadIdx.x; i < n; i += blockDim.x) ss = fma((double)row[i], (double)row[i], ss);
 #pragma unroll
     for (int o = 16; o; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
     if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
@@ -40,15 +40,17 @@ __global__ void rmsnorm_rows(float *__restrict__ x, const float *__restrict__ w,
     for (int i = threadIdx.x; i < n; i += blockDim.x) row[i] = w[i] * row[i] * inv;
 }
 
-// q [T][H][dn + dr] fp32 -> q_nope [T][H][dn], q_rope [T][H][dr] bf16
+// q [T][H][dn + dr] fp32 -> q_nope [T][H][dn], q_rope [T][H][dr] bf16 (grid-stride over
+// all T*H*(dn+dr) elements)
 __global__ void mla_q_split(__nv_bfloat16 *__restrict__ qn, __nv_bfloat16 *__restrict__ qr,
-                            const float *__restrict__ q, int H) {
-    const int t = blockIdx.x;
-    for (int i = threadIdx.x; i < H * (ML_DN + ML_DR); i += blockDim.x) {
-        const int h = i / (ML_DN + ML_DR), c = i - h * (ML_DN + ML_DR);
-        const __nv_bfloat16 v = __float2bfloat16_rn(q[(size_t)t * H * (ML_DN + ML_DR) + i]);
-        if (c < ML_DN) qn[((size_t)t * H + h) * ML_DN + c] = v;
-        else qr[((size_t)t * H + h) * ML_DR + c - ML_DN] = v;
+                            const float *__restrict__ q, long long n) {
+    for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n;
+         i += (long long)gridDim.x * blockDim.x) {
+        const long long th = i / (ML_DN + ML_DR);  // (token, head) row
+        const int c = (int)(i - th * (ML_DN + ML_DR));
+        const __nv_bfloat16 v = __float2bfloat16_rn(q[i]);
+        if (c < ML_DN) qn[th * ML_DN + c] = v;
+        else qr[th * ML_DR + c - ML_DN] = v;
     }
 }
 
@@ -175,9 +177,24 @@ extern "C" int k3cuda_mla_layer(k3cuda_ctx *ctx, float *out, const float *x,
     __nv_bfloat16 *qls = pl.split ? (__nv_bfloat16 *)(ws + pl.qls) : nullptr;
     __nv_bfloat16 *ots = pl.split ? (__nv_bfloat16 *)(ws + pl.ots) : nullptr;
     // projections of x: q_a, kv_a and the gate
+    bool forked = false;
     if (!pl.gemm) {
-        Proj pr[3] = {{w->q_a, ql, q_lora}, {w->kv_a, ct, KW}, {w->g, gb, HV}};
-        if ((rc = matvec(ctx, x, T, E, pr, w->g ? 3 : 2, wdt))) return rc;
+        Proj pr[2] = {{w->q_a, ql, q_lora}, {w->kv_a, ct, KW}};
+        if ((rc = matvec(ctx, x, T, E, pr, 2, wdt))) return rc;
+        if (w->g) {
+            // the gate projection (needed only at the gate) streams on the side stream while
+            // the chain of small, latency-bound steps up to the attention runs on the main one
+            K3_CUDA_TRY(cudaEventRecord(ctx->ev_fork, ctx->stream));
+            K3_CUDA_TRY(cudaStreamWaitEvent(ctx->aux, ctx->ev_fork, 0));
+            cudaStream_t main_stream = ctx->stream;
+            ctx->stream = ctx->aux;
+            const Proj gate{w->g, gb, HV};
+            rc = matvec(ctx, x, T, E, &gate, 1, wdt);
+            ctx->stream = main_stream;
+            if (rc) return rc;
+            K3_CUDA_TRY(cudaEventRecord(ctx->ev_join, ctx->aux));
+            forked = true;
+        }
     } else {
         if (pl.split && (rc = split(ctx, xs, x, (long long)T * E))) return rc;
         if ((rc = gemm(ctx, ql, x, xs, w->q_a, wdt, T, E, q_lora))) return rc;
@@ -193,7 +210,10 @@ extern "C" int k3cuda_mla_layer(k3cuda_ctx *ctx, float *out, const float *x,
     if ((rc = k3cuda_mla_cache_append(ctx, latent, rope, ct, w->kv_a_norm, rms_eps, 0, cached, T,
                                       1, cap, ML_DL, ML_DR)))
         return rc;
-    mla_q_split<<<T, 256, 0, ctx->stream>>>(qn, qr, q, H);
+    {
+        const long long n = (long long)T * HQ;
+        mla_q_split<<<grid_for(ctx, n), 256, 0, ctx->stream>>>(qn, qr, q, n);
+    }
     if ((rc = after_launch(ctx, "mla_q_split"))) return rc;
     const void *kvb = w->kv_b;
     if (wdt == K3CUDA_F32) {
@@ -208,6 +228,7 @@ extern "C" int k3cuda_mla_layer(k3cuda_ctx *ctx, float *out, const float *x,
                              ws + pl.att, pl.total - pl.att)))
         return rc;
     const long long n = (long long)T * HV;
+    if (forked) K3_CUDA_TRY(cudaStreamWaitEvent(ctx->stream, ctx->ev_join, 0));
     mla_gate<<<grid_for(ctx, n), 256, 0, ctx->stream>>>(ot, ots, ots ? ots + n : nullptr, acc,
                                                        w->g ? gb : nullptr, n);
     if ((rc = after_launch(ctx, "mla_gate"))) return rc;
