@@ -100,6 +100,31 @@ int k3cuda_kda_decode(k3cuda_ctx *ctx, float *state, void *o, const void *q,
                       int n_streams, int H, int dk, int dv, float q_scale, int io_dtype,
                       int gate_mode);
 
+/* The same step with the per-token tensors in HOST memory and the state on the device
+ * (the caller's view of k3_kda_step: token in, output back): o, q, k, v, gate, beta are
+ * host pointers with k3cuda_kda_decode's layouts, state a device pointer. Two ways across
+ * PCIe, chosen by `slices`:
+ *   K3CUDA_HOST_IN_PLACE (-1): the buffers must be page-locked (k3cuda_host_alloc, which
+ *       maps them into the device's address space); the kernel reads the inputs and writes
+ *       o in place over PCIe: one launch, no copy, the transfer overlapping the step.
+ *   0: chosen from the size: in place for small steps (up to 640 KB of inputs) when all
+ *       six buffers are page-locked, else copies in one slice, or two from 4 MB up.
+ *   1..K3CUDA_HOST_SLICES: copies through `staging`, the streams cut into that many batch
+ *       slices; slice s's inputs come in on one copy stream while the kernel runs on slice
+ *       s-1 and slice s-2's output goes back on another. Pageable memory works here but
+ *       serialises the copies.
+ * staging: a device buffer of k3cuda_kda_decode_host_workspace() bytes, 256-byte aligned
+ * (may be NULL in place). Asynchronous like every entry point: o is complete when the
+ * context's stream is (k3cuda_sync). */
+#define K3CUDA_HOST_SLICES 16
+#define K3CUDA_HOST_IN_PLACE (-1)
+int k3cuda_kda_decode_host_workspace(int n_streams, int H, int dk, int dv, int io_dtype,
+                                     size_t *bytes);
+int k3cuda_kda_decode_host(k3cuda_ctx *ctx, float *state, void *o, const void *q,
+                           const void *k, const void *v, const float *gate, const float *beta,
+                           int n_streams, int H, int dk, int dv, float q_scale, int io_dtype,
+                           int gate_mode, int slices, void *staging, size_t staging_bytes);
+
 /* --------------------------------------------------- KDA chunked prefill (varlen) */
 /* The whole recurrence of k3_kda_layer (src/core/k3_ops.c:908-938) over packed
  * variable-length sequences, computed chunkwise (WY / UT-transform form of the gated

@@ -3,6 +3,7 @@
 #include <stdlib.h>
 #include <string.h>
 
+#include <initializer_list>
 #include <mutex>
 
 #include "internal.cuh"
@@ -114,6 +115,15 @@ int k3cuda_init(int device, k3cuda_ctx **out) {
     if (e == cudaSuccess) e = cudaStreamCreateWithFlags(&c->aux, cudaStreamNonBlocking);
     if (e == cudaSuccess) e = cudaEventCreateWithFlags(&c->ev_fork, cudaEventDisableTiming);
     if (e == cudaSuccess) e = cudaEventCreateWithFlags(&c->ev_join, cudaEventDisableTiming);
+    if (e == cudaSuccess) e = cudaStreamCreateWithFlags(&c->cp_in, cudaStreamNonBlocking);
+    if (e == cudaSuccess) e = cudaStreamCreateWithFlags(&c->cp_out, cudaStreamNonBlocking);
+    cudaEvent_t *evs[] = {&c->ev_cp_start, &c->ev_cp_in_done, &c->ev_cp_out_done};
+    for (cudaEvent_t *ev : evs)
+        if (e == cudaSuccess) e = cudaEventCreateWithFlags(ev, cudaEventDisableTiming);
+    for (int i = 0; e == cudaSuccess && i < K3CUDA_HOST_SLICES; i++) {
+        e = cudaEventCreateWithFlags(&c->ev_in[i], cudaEventDisableTiming);
+        if (e == cudaSuccess) e = cudaEventCreateWithFlags(&c->ev_k[i], cudaEventDisableTiming);
+    }
     if (e == cudaSuccess) e = cudaMalloc((void **)&c->err_word, 256);
     if (e == cudaSuccess) e = cudaMemset(c->err_word, 0, 256);
     if (e != cudaSuccess) {
@@ -146,6 +156,17 @@ int k3cuda_shutdown(k3cuda_ctx *ctx) {
     if (ctx->ev_fork) cudaEventDestroy(ctx->ev_fork);
     if (ctx->ev_join) cudaEventDestroy(ctx->ev_join);
     if (ctx->aux) cudaStreamDestroy(ctx->aux);
+    for (cudaStream_t cs : {ctx->cp_in, ctx->cp_out})
+        if (cs) {
+            cudaStreamSynchronize(cs);
+            cudaStreamDestroy(cs);
+        }
+    for (cudaEvent_t ev : {ctx->ev_cp_start, ctx->ev_cp_in_done, ctx->ev_cp_out_done})
+        if (ev) cudaEventDestroy(ev);
+    for (int i = 0; i < K3CUDA_HOST_SLICES; i++) {
+        if (ctx->ev_in[i]) cudaEventDestroy(ctx->ev_in[i]);
+        if (ctx->ev_k[i]) cudaEventDestroy(ctx->ev_k[i]);
+    }
     cudaStreamDestroy(ctx->stream);
     free(ctx);
     return K3CUDA_OK;

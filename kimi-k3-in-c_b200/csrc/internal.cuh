@@ -34,6 +34,11 @@ struct k3cuda_ctx {
     int pin_next;
     cudaEvent_t pin_ev[16];
     bool pin_used[16];
+    // host-buffer entry points: inputs come in on cp_in, results go out on cp_out, slice by
+    // slice, both forked from and joined back into `stream`
+    cudaStream_t cp_in, cp_out;
+    cudaEvent_t ev_cp_start, ev_cp_in_done, ev_cp_out_done;
+    cudaEvent_t ev_in[K3CUDA_HOST_SLICES], ev_k[K3CUDA_HOST_SLICES];
 };
 
 namespace k3 {

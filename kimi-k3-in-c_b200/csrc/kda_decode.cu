@@ -15,6 +15,8 @@
 // dk/8 128-bit loads of S before anything else, so each SM has up to 2 x 64 KB of state
 // reads in flight; the two column reductions (u and S'^T q) cross the 8 warps through
 // 8 KB of shared memory; the state goes back with 128-bit streaming stores.
+#include <algorithm>
+
 #include "internal.cuh"
 
 namespace k3 {
@@ -200,4 +202,138 @@ extern "C" int k3cuda_kda_decode(k3cuda_ctx *ctx, float *state, void *o, const v
         return launch_decode<__nv_bfloat16>(ctx, state, o, q, k, v, gate, beta, (int)ns, dk, dv,
                                             q_scale, gl);
     return launch_decode<float>(ctx, state, o, q, k, v, gate, beta, (int)ns, dk, dv, q_scale, gl);
+}
+
+// ------------------------------------------------------------ host-buffer decode step
+namespace {
+size_t al256(size_t x) { return (x + 255) & ~(size_t)255; }
+
+// Device staging image of one step: q, k [ns][dk] and v, o [ns][dv] in io dtype, gate
+// [ns][dk] and beta [ns] fp32, each region 256-byte aligned.
+struct HostStage {
+    size_t q, k, v, o, g, b, total;
+    HostStage(long long ns, int dk, int dv, size_t es) {
+        q = 0;
+        k = q + al256((size_t)ns * dk * es);
+        v = k + al256((size_t)ns * dk * es);
+        o = v + al256((size_t)ns * dv * es);
+        g = o + al256((size_t)ns * dv * es);
+        b = g + al256((size_t)ns * dk * 4);
+        total = b + al256((size_t)ns * 4);
+    }
+};
+}  // namespace
+
+extern "C" int k3cuda_kda_decode_host_workspace(int n_streams, int H, int dk, int dv,
+                                                int io_dtype, size_t *bytes) {
+    K3_ARG_CHECK(bytes, "null output pointer");
+    *bytes = 0;
+    K3_ARG_CHECK(n_streams >= 0 && H >= 1 && dk >= 1 && dv >= 1, "bad n_streams=%d H=%d dk=%d dv=%d",
+                 n_streams, H, dk, dv);
+    K3_ARG_CHECK(io_dtype == K3CUDA_F32 || io_dtype == K3CUDA_BF16, "bad io_dtype %d", io_dtype);
+    *bytes = HostStage((long long)n_streams * H, dk, dv, io_dtype == K3CUDA_BF16 ? 2 : 4).total;
+    return K3CUDA_OK;
+}
+
+extern "C" int k3cuda_kda_decode_host(k3cuda_ctx *ctx, float *state, void *o, const void *q,
+                                      const void *k, const void *v, const float *gate,
+                                      const float *beta, int n_streams, int H, int dk, int dv,
+                                      float q_scale, int io_dtype, int gate_mode, int slices,
+                                      void *staging, size_t staging_bytes) {
+    int rc = enter(ctx);
+    if (rc) return rc;
+    K3_ARG_CHECK(n_streams >= 0 && H >= 1, "bad n_streams=%d H=%d", n_streams, H);
+    K3_ARG_CHECK(io_dtype == K3CUDA_F32 || io_dtype == K3CUDA_BF16, "bad io_dtype %d", io_dtype);
+    K3_ARG_CHECK(gate_mode == K3CUDA_GATE_LOG || gate_mode == K3CUDA_GATE_ALPHA,
+                 "bad gate_mode %d", gate_mode);
+    K3_ARG_CHECK(slices >= K3CUDA_HOST_IN_PLACE, "bad slices %d", slices);
+    if (dk < 1 || dv < 1 || dk > 256 || dv > 256 || (size_t)dk * dv > 32768)
+        return set_error(K3CUDA_ERR_UNSUPPORTED, "kda_decode_host: dk=%d dv=%d not built", dk, dv);
+    if (n_streams == 0) return K3CUDA_OK;
+    K3_ARG_CHECK(state && o && q && k && v && gate && beta, "kda_decode_host: null pointer");
+    const long long ns = (long long)n_streams * H;
+    K3_ARG_CHECK(ns <= 0x7fffffffLL, "too many streams");
+    const size_t es = io_dtype == K3CUDA_BF16 ? 2 : 4;
+    const size_t in_bytes = (size_t)ns * ((2 * (size_t)dk + dv) * es + 4 * (size_t)dk + 4);
+    // Measured on the B200 (H = 32, d = 128, bf16): in place costs ~15 us + 2.6 us per
+    // sequence (the kernel's PCIe reads are small and latency-bound, ~14 GB/s), the copies
+    // ~36 us + 1.35 us per sequence at ~49 GB/s: in place wins below ~17 sequences (~700 KB
+    // of inputs); above ~4 MB two slices beat one, and more slices lose to per-copy costs.
+    constexpr size_t kInPlaceMax = 640 << 10, kTwoSlices = 4 << 20;
+    if (slices == K3CUDA_HOST_IN_PLACE || (slices == 0 && in_bytes <= kInPlaceMax)) {
+        // page-locked host memory is mapped into the device's address space: the kernel reads
+        // the inputs and writes the output in place over PCIe, with no copy and one launch
+        const void *hp[6] = {o, q, k, v, gate, beta};
+        void *dp[6];
+        bool all = true;
+        for (int i = 0; i < 6; i++) {
+            cudaPointerAttributes a;
+            if (cudaPointerGetAttributes(&a, hp[i]) != cudaSuccess) {
+                cudaGetLastError();  // not a CUDA-known pointer: pageable memory
+                a.type = cudaMemoryTypeUnregistered;
+                a.devicePointer = nullptr;
+            }
+            dp[i] = a.type == cudaMemoryTypeHost ? a.devicePointer : nullptr;
+            all = all && dp[i];
+        }
+        if (all)
+            return k3cuda_kda_decode(ctx, state, dp[0], dp[1], dp[2], dp[3], (const float *)dp[4],
+                                     (const float *)dp[5], n_streams, H, dk, dv, q_scale, io_dtype,
+                                     gate_mode);
+        K3_ARG_CHECK(slices == 0, "kda_decode_host: in-place mode needs page-locked host buffers");
+    }
+    K3_ARG_CHECK(staging, "kda_decode_host: null staging buffer");
+    const HostStage L(ns, dk, dv, es);
+    if (staging_bytes < L.total)
+        return set_error(K3CUDA_ERR_WORKSPACE, "kda_decode_host: staging %zu < %zu bytes",
+                         staging_bytes, L.total);
+    K3_ARG_CHECK(aligned(staging, 256), "kda_decode_host: staging must be 256-byte aligned");
+    int S = slices > 0 ? slices : (in_bytes >= kTwoSlices ? 2 : 1);
+    S = std::min(S, std::min(n_streams, K3CUDA_HOST_SLICES));
+    uint8_t *st = (uint8_t *)staging;
+    const uint8_t *hq = (const uint8_t *)q, *hk = (const uint8_t *)k, *hv = (const uint8_t *)v;
+    const uint8_t *hg = (const uint8_t *)gate, *hb = (const uint8_t *)beta;
+    uint8_t *ho = (uint8_t *)o;
+
+    K3_CUDA_TRY(cudaEventRecord(ctx->ev_cp_start, ctx->stream));
+    K3_CUDA_TRY(cudaStreamWaitEvent(ctx->cp_in, ctx->ev_cp_start, 0));
+    K3_CUDA_TRY(cudaStreamWaitEvent(ctx->cp_out, ctx->ev_cp_start, 0));
+    cudaError_t e = cudaSuccess;
+    for (int s = 0; s < S && rc == K3CUDA_OK && e == cudaSuccess; s++) {
+        const long long b0 = (long long)n_streams * s / S, b1 = (long long)n_streams * (s + 1) / S;
+        const long long r0 = b0 * H, nr = (b1 - b0) * H;  // (sequence, head) rows of the slice
+        if (nr == 0) continue;
+        const size_t qo = (size_t)r0 * dk * es, qn = (size_t)nr * dk * es;
+        const size_t vo = (size_t)r0 * dv * es, vn = (size_t)nr * dv * es;
+        const size_t go = (size_t)r0 * dk * 4, gn = (size_t)nr * dk * 4;
+        const cudaMemcpyKind H2D = cudaMemcpyHostToDevice;
+        e = cudaMemcpyAsync(st + L.q + qo, hq + qo, qn, H2D, ctx->cp_in);
+        if (e == cudaSuccess) e = cudaMemcpyAsync(st + L.k + qo, hk + qo, qn, H2D, ctx->cp_in);
+        if (e == cudaSuccess) e = cudaMemcpyAsync(st + L.v + vo, hv + vo, vn, H2D, ctx->cp_in);
+        if (e == cudaSuccess) e = cudaMemcpyAsync(st + L.g + go, hg + go, gn, H2D, ctx->cp_in);
+        if (e == cudaSuccess)
+            e = cudaMemcpyAsync(st + L.b + r0 * 4, hb + r0 * 4, (size_t)nr * 4, H2D, ctx->cp_in);
+        if (e == cudaSuccess) e = cudaEventRecord(ctx->ev_in[s], ctx->cp_in);
+        if (e == cudaSuccess) e = cudaStreamWaitEvent(ctx->stream, ctx->ev_in[s], 0);
+        if (e != cudaSuccess) break;
+        rc = k3cuda_kda_decode(ctx, state + (size_t)r0 * dk * dv, st + L.o + vo, st + L.q + qo,
+                               st + L.k + qo, st + L.v + vo, (const float *)(st + L.g + go),
+                               (const float *)(st + L.b + r0 * 4), (int)(b1 - b0), H, dk, dv,
+                               q_scale, io_dtype, gate_mode);
+        if (rc) break;
+        e = cudaEventRecord(ctx->ev_k[s], ctx->stream);
+        if (e == cudaSuccess) e = cudaStreamWaitEvent(ctx->cp_out, ctx->ev_k[s], 0);
+        if (e == cudaSuccess)
+            e = cudaMemcpyAsync(ho + vo, st + L.o + vo, vn, cudaMemcpyDeviceToHost, ctx->cp_out);
+    }
+    // both copy streams join the context's stream whatever happened above
+    cudaError_t e2 = cudaEventRecord(ctx->ev_cp_in_done, ctx->cp_in);
+    if (e2 == cudaSuccess) e2 = cudaStreamWaitEvent(ctx->stream, ctx->ev_cp_in_done, 0);
+    cudaError_t e3 = cudaEventRecord(ctx->ev_cp_out_done, ctx->cp_out);
+    if (e3 == cudaSuccess) e3 = cudaStreamWaitEvent(ctx->stream, ctx->ev_cp_out_done, 0);
+    if (rc) return rc;
+    if (e == cudaSuccess) e = e2 != cudaSuccess ? e2 : e3;
+    if (e != cudaSuccess)
+        return set_error(K3CUDA_ERR_CUDA, "kda_decode_host: %s", cudaGetErrorString(e));
+    return K3CUDA_OK;
 }

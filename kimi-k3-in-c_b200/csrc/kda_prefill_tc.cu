@@ -613,7 +613,7 @@ kda_prep_tc(const __grid_constant__ PrepMaps maps, const TcChunk *__restrict__ c
     __syncthreads();
     // M = T diag(beta) as bf16 hi + lo, K-major [t][s]
     for (int u = tid; u < 512; u += 256) {
-        const int t = u >> 3, c8 = u & 7;
+        const int t = u & 63, c8 = u >> 6;  // a warp: 32 consecutive tokens, one 8-column group
         float mv[8], hi[8];
 #pragma unroll
         for (int x = 0; x < 8; x++) {

@@ -47,6 +47,9 @@ SIGNATURES = {
     "k3cuda_flush_l2": (_i, [_vp]),
     "k3cuda_kda_decode": (_i, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _f, _i,
                                _i]),
+    "k3cuda_kda_decode_host_workspace": (_i, [_i, _i, _i, _i, _i, C.POINTER(_sz)]),
+    "k3cuda_kda_decode_host": (_i, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _f,
+                                    _i, _i, _i, _vp, _sz]),
     "k3cuda_kda_prefill_workspace": (_i, [_ip, _i, _i, _i, _i, _i, C.POINTER(_sz)]),
     "k3cuda_kda_prefill": (_i, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _ip, _i, _i, _i, _i, _f,
                                 _i, _i, _i, _vp, _sz]),
@@ -242,6 +245,24 @@ class Context:
         check(lib().k3cuda_kda_decode(self.h, _ptr(state), _ptr(o), _ptr(q), _ptr(k), _ptr(v),
                                       _ptr(gate), _ptr(beta), int(n_streams), int(H), int(dk),
                                       int(dv), float(q_scale), int(io_dtype), int(gate_mode)))
+
+    def kda_decode_host_workspace(self, n_streams, H, dk, dv, io_dtype=BF16) -> int:
+        n = C.c_size_t()
+        check(lib().k3cuda_kda_decode_host_workspace(int(n_streams), int(H), int(dk), int(dv),
+                                                     int(io_dtype), C.byref(n)))
+        return int(n.value)
+
+    def kda_decode_host(self, state, o, q, k, v, gate, beta, n_streams, H, dk, dv, q_scale,
+                        staging, staging_bytes, io_dtype=BF16, gate_mode=GATE_LOG, slices=0):
+        """k3cuda_kda_decode_host: o, q, k, v, gate, beta are host numpy arrays (C-contiguous,
+        ideally from pinned()), state and staging device buffers. o is complete after sync()."""
+        for a in (o, q, k, v, gate, beta):
+            assert isinstance(a, np.ndarray) and a.flags["C_CONTIGUOUS"]
+        check(lib().k3cuda_kda_decode_host(self.h, _ptr(state), _ptr(o), _ptr(q), _ptr(k),
+                                           _ptr(v), _ptr(gate), _ptr(beta), int(n_streams),
+                                           int(H), int(dk), int(dv), float(q_scale),
+                                           int(io_dtype), int(gate_mode), int(slices),
+                                           _ptr(staging), int(staging_bytes)))
 
     def kda_prefill_workspace(self, cu_seqlens, H, dk, dv, chunk=64) -> int:
         cu, cup = _iarr(cu_seqlens)

@@ -124,6 +124,89 @@ def test_decode_alpha_mode_equals_log_mode(ctx):
     assert W.rel_fro(o1, o2) < 1e-6 and W.rel_fro(S1, S2) < 1e-6
 
 
+def _host_step(ctx, dS, t, io, gate_mode, slices, pinned, n_streams, H, dk, dv, st=None):
+    """One k3cuda_kda_decode_host call from host arrays (staging `st`, or a new buffer);
+    returns the host output array and the staging buffer. Valid after ctx.sync()."""
+    conv = _bf if io == k3cuda.BF16 else (lambda x: np.ascontiguousarray(x, np.float32))
+    ety = np.uint16 if io == k3cuda.BF16 else np.float32
+    src = {"q": conv(t["q"]), "k": conv(t["k"]), "v": conv(t["v"]),
+           "g": np.ascontiguousarray(t["g"], np.float32),
+           "beta": np.ascontiguousarray(t["beta"], np.float32)}
+    if pinned:
+        for name in list(src):
+            a = ctx.pinned(src[name].shape, src[name].dtype)
+            a[...] = src[name]
+            src[name] = a
+        ho = ctx.pinned((n_streams, H, dv), ety)
+    else:
+        ho = np.empty((n_streams, H, dv), ety)
+    n = ctx.kda_decode_host_workspace(n_streams, H, dk, dv, io)
+    st = ctx.empty((n,), np.uint8) if st is None else st
+    ctx.kda_decode_host(dS, ho, src["q"], src["k"], src["v"], src["g"], src["beta"], n_streams,
+                        H, dk, dv, 1.0 / np.sqrt(np.float32(dk)), st, n, io, gate_mode,
+                        slices=slices)
+    return ho, st
+
+
+@pytest.mark.parametrize("slices", [-1, 0, 1, 3, 7, 16])
+def test_decode_host_buffers_equal_device_path(ctx, slices):
+    """k3cuda_kda_decode_host (host tensors in and out) gives the device-buffer step bit for
+    bit: in place over PCIe (-1, and 0 with page-locked buffers), and through copies
+    pipelined over batch slices on every split (uneven, more slices than sequences)."""
+    rng = np.random.default_rng(41 + slices)
+    B, H, d = 37, 4, 128
+    t = W.kda_tokens(rng, B, H, d, d, bf16=True)
+    S = rng.standard_normal((B, H, d, d), dtype=np.float32) * np.float32(0.02)
+    o_dev, S_dev = run_decode(ctx, S, t["q"], t["k"], t["v"], t["g"], t["beta"])
+    dS = ctx.upload(S)
+    ho, _ = _host_step(ctx, dS, t, k3cuda.BF16, k3cuda.GATE_LOG, slices, True, B, H, d, d)
+    ctx.sync()
+    assert np.array_equal(W.bf16_to_f32(np.array(ho)), o_dev)
+    assert np.array_equal(dS.numpy(), S_dev)
+
+
+def test_decode_host_in_place_refuses_pageable_memory(ctx):
+    """In-place mode needs page-locked buffers: pageable ones are an argument error, with
+    nothing launched."""
+    rng = np.random.default_rng(8)
+    B, H, d = 2, 2, 128
+    t = W.kda_tokens(rng, B, H, d, d, bf16=True)
+    dS = ctx.upload(np.zeros((B, H, d, d), np.float32))
+    n0 = ctx.launches()
+    with pytest.raises(k3cuda.K3CudaError):
+        _host_step(ctx, dS, t, k3cuda.BF16, k3cuda.GATE_LOG, -1, False, B, H, d, d)
+    assert ctx.launches() == n0
+
+
+def test_decode_host_pageable_fp32_alpha_consecutive_steps(ctx):
+    """Pageable host arrays, fp32 I/O, alpha gate, dk=64, two host steps enqueued back to
+    back (the second's copies must wait for the first's kernels): equal to two device steps
+    bit for bit, and to the oracle within the fp32 bar."""
+    rng = np.random.default_rng(5)
+    B, H, dk, dv = 9, 3, 64, 128
+    S = rng.standard_normal((B, H, dk, dv), dtype=np.float32) * np.float32(0.02)
+    ts = [W.kda_tokens(rng, B, H, dk, dv, bf16=False) for _ in range(2)]
+    logg = [t["g"] for t in ts]
+    for t in ts:
+        t["g"] = np.exp(t["g"])
+    S_dev, o_dev = S, []
+    for t in ts:
+        o, S_dev = run_decode(ctx, S_dev, t["q"], t["k"], t["v"], t["g"], t["beta"],
+                              io=k3cuda.F32, gate_mode=k3cuda.GATE_ALPHA)
+        o_dev.append(o)
+    dS = ctx.upload(S)
+    ho1, st = _host_step(ctx, dS, ts[0], k3cuda.F32, k3cuda.GATE_ALPHA, 2, False, B, H, dk, dv)
+    ho2, _ = _host_step(ctx, dS, ts[1], k3cuda.F32, k3cuda.GATE_ALPHA, 3, False, B, H, dk, dv,
+                        st=st)  # the same staging buffer: ordered behind the first step
+    ctx.sync()
+    assert np.array_equal(ho1, o_dev[0]) and np.array_equal(ho2, o_dev[1])
+    assert np.array_equal(dS.numpy(), S_dev)
+    S_ref = S
+    for t, g, ho in zip(ts, logg, (ho1, ho2)):
+        o_ref, S_ref = oracle.kda_decode(S_ref, t["q"], t["k"], t["v"], g, t["beta"])
+        assert W.rel_fro(ho, o_ref) < TOL_F32
+
+
 # -------------------------------------------------------------------------- prefill
 def test_config0_prefill_then_decode_matches_reference_c(ctx, golden):
     """chunked prefill of 256 tokens, then 32 decode steps, against the
