@@ -117,6 +117,38 @@ int after_launch(k3cuda_ctx *ctx, const char *what);
 
 inline bool aligned(const void *p, size_t a) { return ((uintptr_t)p % a) == 0; }
 
+// ------------------------------------------------ programmatic dependent launch (PDL)
+// The kernels of a dependent chain (a layer's T <= 8 path) are launched with programmatic
+// stream serialization: the next kernel's CTAs are scheduled while the current one
+// finishes, run their independent prologue (weight loads), and wait in pdl_wait() until the
+// previous kernel has completed and its writes are visible. A kernel calls pdl_wait() before
+// it reads anything an earlier kernel wrote and before its first global write; launched
+// without the attribute, pdl_wait() returns at once. pdl_trigger() lets the next kernel be
+// scheduled once every CTA of this one has issued it (its pdl_wait still waits for the end).
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() {
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
+template <typename... KArgs, typename... Args>
+int launch_pdl(k3cuda_ctx *ctx, cudaStream_t st, const char *what, void (*kern)(KArgs...),
+               dim3 grid, dim3 block, size_t smem, Args... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute at[1];
+    at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    at[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = at;
+    cfg.numAttrs = 1;
+    const cudaError_t e = cudaLaunchKernelEx(&cfg, kern, args...);
+    if (e != cudaSuccess)
+        return set_error(K3CUDA_ERR_CUDA, "%s launch failed: %s", what, cudaGetErrorString(e));
+    return after_launch(ctx, what);
+}
+
 // ------------------------------------------------------------------ element access
 template <typename T> struct io;
 template <> struct io<float> {

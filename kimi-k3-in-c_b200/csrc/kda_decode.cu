@@ -27,6 +27,8 @@ kda_decode_dv128(float *__restrict__ state, IO *__restrict__ o, const IO *__rest
                  const IO *__restrict__ k, const IO *__restrict__ v,
                  const float *__restrict__ gate, const float *__restrict__ beta,
                  float q_scale, int gate_is_log) {
+    pdl_trigger();
+    pdl_wait();  // the state and the inputs may come from the previous kernel
     constexpr int DV = 128;
     constexpr int RPW = DK / 8;  // rows per warp
     const int sh = blockIdx.x;
@@ -114,6 +116,8 @@ kda_decode_general(float *__restrict__ state, IO *__restrict__ o, const IO *__re
                    const IO *__restrict__ k, const IO *__restrict__ v,
                    const float *__restrict__ gate, const float *__restrict__ beta, int dk,
                    int dv, float q_scale, int gate_is_log) {
+    pdl_trigger();
+    pdl_wait();  // the state and the inputs may come from the previous kernel
     extern __shared__ float smem[];
     float *S = smem;                       // [dk][dv]
     float *al = S + (size_t)dk * dv;       // [dk]
@@ -159,22 +163,20 @@ static int launch_decode(k3cuda_ctx *ctx, float *state, void *o, const void *q, 
                          int dk, int dv, float q_scale, int gate_is_log) {
     const IO *qp = (const IO *)q, *kp = (const IO *)k, *vp = (const IO *)v;
     IO *op = (IO *)o;
-    if (dv == 128 && dk == 128 && aligned(state, 16)) {
-        kda_decode_dv128<IO, 128><<<nstream, 256, 0, ctx->stream>>>(state, op, qp, kp, vp, gate,
-                                                                    beta, q_scale, gate_is_log);
-        return after_launch(ctx, "kda_decode_dv128<128>");
-    }
-    if (dv == 128 && dk == 64 && aligned(state, 16)) {
-        kda_decode_dv128<IO, 64><<<nstream, 256, 0, ctx->stream>>>(state, op, qp, kp, vp, gate,
-                                                                   beta, q_scale, gate_is_log);
-        return after_launch(ctx, "kda_decode_dv128<64>");
-    }
+    if (dv == 128 && dk == 128 && aligned(state, 16))
+        return launch_pdl(ctx, ctx->stream, "kda_decode_dv128<128>", kda_decode_dv128<IO, 128>,
+                          dim3(nstream), dim3(256), 0, state, op, qp, kp, vp, gate, beta, q_scale,
+                          gate_is_log);
+    if (dv == 128 && dk == 64 && aligned(state, 16))
+        return launch_pdl(ctx, ctx->stream, "kda_decode_dv128<64>", kda_decode_dv128<IO, 64>,
+                          dim3(nstream), dim3(256), 0, state, op, qp, kp, vp, gate, beta, q_scale,
+                          gate_is_log);
     const size_t smem = ((size_t)dk * dv + 3 * dk + 2 * dv) * sizeof(float);
     if (smem > 48 * 1024)
         if (int rc_ = set_smem(kda_decode_general<IO>, (int)smem)) return rc_;
-    kda_decode_general<IO><<<nstream, 256, smem, ctx->stream>>>(state, op, qp, kp, vp, gate, beta,
-                                                                dk, dv, q_scale, gate_is_log);
-    return after_launch(ctx, "kda_decode_general");
+    return launch_pdl(ctx, ctx->stream, "kda_decode_general", kda_decode_general<IO>,
+                      dim3(nstream), dim3(256), smem, state, op, qp, kp, vp, gate, beta, dk, dv,
+                      q_scale, gate_is_log);
 }
 
 }  // namespace k3

@@ -142,6 +142,7 @@ template <int NT, typename WT>
 __global__ void __launch_bounds__(MV_THREADS) matvec_rows(const __grid_constant__ MatvecArgs a) {
     constexpr int MV_ROWS = mv_rows<NT>();
     __shared__ float part[MV_WARPS][MV_ROWS * NT];
+    pdl_trigger();
     int b = blockIdx.x, s = 0;
     while (s + 1 < a.nseg && b >= a.seg[s].blocks) b -= a.seg[s++].blocks;
     const MatvecSeg &sg = a.seg[s];
@@ -159,6 +160,7 @@ __global__ void __launch_bounds__(MV_THREADS) matvec_rows(const __grid_constant_
     for (int r = 0; r < MV_ROWS; r++)
 #pragma unroll
         for (int t = 0; t < NT; t++) acc[r][t] = 0.f;
+    pdl_wait();  // x comes from the previous kernel
 #pragma unroll 2
     for (int i8 = b8 + lane; i8 < e8; i8 += 32) {
         float w[MV_ROWS][8];
@@ -193,12 +195,22 @@ __global__ void __launch_bounds__(MV_THREADS) matvec_rows(const __grid_constant_
     }
 }
 
+// On the context's stream the launch overlaps the previous kernel's tail (PDL); on the side
+// stream, whose work is ordered by events, it is a plain launch.
 template <int NT>
-static void launch_matvec(const MatvecArgs &a, int wdt, int blocks, cudaStream_t st) {
+static int launch_matvec(k3cuda_ctx *ctx, const MatvecArgs &a, int wdt, int blocks) {
+    if (ctx->stream == ctx->aux) {
+        if (wdt == K3CUDA_BF16)
+            matvec_rows<NT, __nv_bfloat16><<<blocks, MV_THREADS, 0, ctx->stream>>>(a);
+        else
+            matvec_rows<NT, float><<<blocks, MV_THREADS, 0, ctx->stream>>>(a);
+        return after_launch(ctx, "matvec_rows");
+    }
     if (wdt == K3CUDA_BF16)
-        matvec_rows<NT, __nv_bfloat16><<<blocks, MV_THREADS, 0, st>>>(a);
-    else
-        matvec_rows<NT, float><<<blocks, MV_THREADS, 0, st>>>(a);
+        return launch_pdl(ctx, ctx->stream, "matvec_rows", matvec_rows<NT, __nv_bfloat16>,
+                          dim3(blocks), dim3(MV_THREADS), 0, a);
+    return launch_pdl(ctx, ctx->stream, "matvec_rows", matvec_rows<NT, float>, dim3(blocks),
+                      dim3(MV_THREADS), 0, a);
 }
 
 // One launch of matvec_rows over `n` projections of the same x [T][in] (T <= MV_MAXT).
@@ -232,16 +244,15 @@ int matvec(k3cuda_ctx *ctx, const float *x, int T, int in, const Proj *p, int n,
     if (tot == 0) return K3CUDA_OK;
     if (tot > 0x7fffffffLL) return set_error(K3CUDA_ERR_ARG, "matvec: grid too large");
     switch (T) {
-        case 1: launch_matvec<1>(a, wdt, (int)tot, ctx->stream); break;
-        case 2: launch_matvec<2>(a, wdt, (int)tot, ctx->stream); break;
-        case 3: launch_matvec<3>(a, wdt, (int)tot, ctx->stream); break;
-        case 4: launch_matvec<4>(a, wdt, (int)tot, ctx->stream); break;
-        case 5: launch_matvec<5>(a, wdt, (int)tot, ctx->stream); break;
-        case 6: launch_matvec<6>(a, wdt, (int)tot, ctx->stream); break;
-        case 7: launch_matvec<7>(a, wdt, (int)tot, ctx->stream); break;
-        default: launch_matvec<8>(a, wdt, (int)tot, ctx->stream); break;
+        case 1: return launch_matvec<1>(ctx, a, wdt, (int)tot);
+        case 2: return launch_matvec<2>(ctx, a, wdt, (int)tot);
+        case 3: return launch_matvec<3>(ctx, a, wdt, (int)tot);
+        case 4: return launch_matvec<4>(ctx, a, wdt, (int)tot);
+        case 5: return launch_matvec<5>(ctx, a, wdt, (int)tot);
+        case 6: return launch_matvec<6>(ctx, a, wdt, (int)tot);
+        case 7: return launch_matvec<7>(ctx, a, wdt, (int)tot);
+        default: return launch_matvec<8>(ctx, a, wdt, (int)tot);
     }
-    return after_launch(ctx, "matvec_rows");
 }
 
 // hi = bf16(x), lo = bf16(x - hi): x = hi + lo to within 2^-16 |x|.
@@ -388,6 +399,8 @@ struct PreArgs {
 
 template <typename IO, int CPL, int K>
 __global__ void __launch_bounds__(LAYER_THREADS) kda_layer_pre(const __grid_constant__ PreArgs<IO> a) {
+    pdl_trigger();
+    pdl_wait();  // the projections come from the previous kernels
     constexpr int HIST = K - 1;
     const int s = blockIdx.z, h = blockIdx.y;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -495,6 +508,8 @@ struct PostArgs {
 
 template <typename IO, int CPL>
 __global__ void __launch_bounds__(LAYER_THREADS) kda_layer_post(const __grid_constant__ PostArgs<IO> a) {
+    pdl_trigger();  // o_proj's CTAs may be scheduled while this kernel runs
+    pdl_wait();
     const int h = blockIdx.y;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int t_a = blockIdx.x * LT + warp * TPW;
@@ -602,20 +617,22 @@ static int layer_shape_ok(int T, int E, int H, int D, int K, int wdt, int io_dty
 }
 
 template <typename IO, int CPL>
-static void launch_pre_k(const PreArgs<IO> &a, int K, dim3 grid, cudaStream_t st) {
+static int launch_pre_k(k3cuda_ctx *ctx, const PreArgs<IO> &a, int K, dim3 grid) {
+    const dim3 blk(LAYER_THREADS);
+    const char *nm = "kda_layer_pre";
     switch (K) {
-        case 1: kda_layer_pre<IO, CPL, 1><<<grid, LAYER_THREADS, 0, st>>>(a); break;
-        case 2: kda_layer_pre<IO, CPL, 2><<<grid, LAYER_THREADS, 0, st>>>(a); break;
-        case 3: kda_layer_pre<IO, CPL, 3><<<grid, LAYER_THREADS, 0, st>>>(a); break;
-        default: kda_layer_pre<IO, CPL, 4><<<grid, LAYER_THREADS, 0, st>>>(a); break;
+        case 1: return launch_pdl(ctx, ctx->stream, nm, kda_layer_pre<IO, CPL, 1>, grid, blk, 0, a);
+        case 2: return launch_pdl(ctx, ctx->stream, nm, kda_layer_pre<IO, CPL, 2>, grid, blk, 0, a);
+        case 3: return launch_pdl(ctx, ctx->stream, nm, kda_layer_pre<IO, CPL, 3>, grid, blk, 0, a);
+        default: return launch_pdl(ctx, ctx->stream, nm, kda_layer_pre<IO, CPL, 4>, grid, blk, 0, a);
     }
 }
 
 template <typename IO>
-static void launch_pre(const PreArgs<IO> &a, int D, int K, dim3 grid, cudaStream_t st) {
-    if (D <= 32) launch_pre_k<IO, 1>(a, K, grid, st);
-    else if (D <= 64) launch_pre_k<IO, 2>(a, K, grid, st);
-    else launch_pre_k<IO, 4>(a, K, grid, st);
+static int launch_pre(k3cuda_ctx *ctx, const PreArgs<IO> &a, int D, int K, dim3 grid) {
+    if (D <= 32) return launch_pre_k<IO, 1>(ctx, a, K, grid);
+    if (D <= 64) return launch_pre_k<IO, 2>(ctx, a, K, grid);
+    return launch_pre_k<IO, 4>(ctx, a, K, grid);
 }
 
 // One projection: matvec (T <= 8) or GEMM; xs is x's bf16 split when the GEMM needs it.
@@ -679,8 +696,7 @@ static int layer_core(k3cuda_ctx *ctx, float *out, const float *x, const k3cuda_
         a.g = g; a.beta = beta;
         a.T = T; a.H = H; a.D = D; a.lb = lb;
         dim3 grid((unsigned)((T + LT - 1) / LT), (unsigned)H, 4);
-        launch_pre(a, D, K, grid, ctx->stream);
-        if ((rc = after_launch(ctx, "kda_layer_pre"))) return rc;
+        if ((rc = launch_pre(ctx, a, D, K, grid))) return rc;
     }
     // 6. recurrence
     float *S = state;

@@ -646,27 +646,189 @@ mla_attend_tc(const __grid_constant__ MlaMaps maps, const MlaSeg *__restrict__ s
     }
 }
 
+// ------------------------------------------------- per-head products for a few sequences
+// With B <= MLA_SMALL_B sequences the tcgen05 kernels above run one CTA per head whose time
+// is the latency of streaming its 128 KB weight block through one SM. These spread each
+// head's block over several CTAs instead, every thread issuing all its 16-byte weight loads
+// before any arithmetic, with fp32 accumulation on the CUDA cores.
+constexpr int MLA_SMALL_B = 8;
+
+// qlat[b][h][c] = sum_i q_nope[b][h][i] W_UK[h][i][c] (bf16 out) for the 128 columns
+// c in [128 z, +128) of CTA (h, z); z == 0 also copies q_rope into qlat[b][h][512:576].
+// Thread t: columns 128 z + 8 (t % 16) .. +8, rows i = t / 16 + 16 j (j < 8). NB >= B is
+// the register budget for the sequences.
+template <int NB>
+__global__ void __launch_bounds__(256)
+mla_q_absorb_small(const __nv_bfloat16 *__restrict__ q_nope,
+                   const __nv_bfloat16 *__restrict__ q_rope, const __nv_bfloat16 *__restrict__ w_uk,
+                   long long uk_head_elems, __nv_bfloat16 *__restrict__ qlat, int B, int H) {
+    __shared__ float qs[NB][MLA_DN];
+    __shared__ float red[8][NB][128];
+    pdl_trigger();
+    const int h = blockIdx.x, z = blockIdx.y, tid = threadIdx.x, warp = tid >> 5;
+    const int cg = tid & 15, r0 = tid >> 4, c0 = 128 * z + 8 * cg;
+    const __nv_bfloat16 *W = w_uk + (size_t)h * uk_head_elems + c0;
+    uint4 wv[8];
+#pragma unroll
+    for (int j = 0; j < 8; j++)
+        wv[j] = __ldg(reinterpret_cast<const uint4 *>(W + (size_t)(r0 + 16 * j) * MLA_DL));
+    pdl_wait();  // the weights above are never written by the chain; q_nope is
+    for (int e = tid; e < NB * MLA_DN; e += 256) {
+        const int b = e / MLA_DN, i = e % MLA_DN;
+        qs[b][i] = b < B ? __bfloat162float(q_nope[((size_t)b * H + h) * MLA_DN + i]) : 0.f;
+    }
+    __syncthreads();
+    float acc[NB][8];
+#pragma unroll
+    for (int b = 0; b < NB; b++)
+#pragma unroll
+        for (int x = 0; x < 8; x++) acc[b][x] = 0.f;
+#pragma unroll
+    for (int j = 0; j < 8; j++) {
+        const uint32_t u[4] = {wv[j].x, wv[j].y, wv[j].z, wv[j].w};
+        float wf[8];
+#pragma unroll
+        for (int x = 0; x < 4; x++) {
+            wf[2 * x] = __uint_as_float(u[x] << 16);
+            wf[2 * x + 1] = __uint_as_float(u[x] & 0xffff0000u);
+        }
+#pragma unroll
+        for (int b = 0; b < NB; b++) {
+            const float qv = qs[b][r0 + 16 * j];
+#pragma unroll
+            for (int x = 0; x < 8; x++) acc[b][x] = fmaf(qv, wf[x], acc[b][x]);
+        }
+    }
+    // the two row sets of a warp (lanes l and l + 16) first, then the eight warps
+#pragma unroll
+    for (int b = 0; b < NB; b++)
+#pragma unroll
+        for (int x = 0; x < 8; x++) acc[b][x] += __shfl_xor_sync(0xffffffffu, acc[b][x], 16);
+    if ((tid & 31) < 16) {
+#pragma unroll
+        for (int b = 0; b < NB; b++)
+#pragma unroll
+            for (int x = 0; x < 8; x++) red[warp][b][8 * cg + x] = acc[b][x];
+    }
+    __syncthreads();
+    for (int e = tid; e < B * 128; e += 256) {
+        const int b = e >> 7, c = e & 127;
+        float v = 0.f;
+#pragma unroll
+        for (int w = 0; w < 8; w++) v += red[w][b][c];
+        qlat[((size_t)b * MLA_HP + h) * MLA_QW + 128 * z + c] = __float2bfloat16_rn(v);
+    }
+    if (z == 0)
+        for (int e = tid; e < B * MLA_DR; e += 256)
+            qlat[((size_t)(e / MLA_DR) * MLA_HP + h) * MLA_QW + MLA_DL + e % MLA_DR] =
+                q_rope[((size_t)(e / MLA_DR) * H + h) * MLA_DR + e % MLA_DR];
+}
+
+// out[b][h][j] = sum_k o_lat[b][h][k] W_UV[h][j][k] for the 16 rows j in [16 z, +16) of
+// CTA (h, z), o_lat = hi + lo of the merge's bf16 pair. Warp w: rows 16 z + 2 w, +1; lane:
+// k in [16 lane, +16).
+template <typename OUT>
+__global__ void __launch_bounds__(256)
+mla_project_small(const __nv_bfloat16 *__restrict__ olat2, const __nv_bfloat16 *__restrict__ w_uv,
+                  long long uv_head_elems, OUT *__restrict__ out, int B, int H) {
+    __shared__ float os[MLA_SMALL_B][MLA_DL];
+    pdl_trigger();
+    const int h = blockIdx.x, z = blockIdx.y, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int j0 = 16 * z + 2 * warp;
+    const __nv_bfloat16 *W = w_uv + (size_t)h * uv_head_elems + (size_t)j0 * MLA_DL + 16 * lane;
+    uint4 wv[2][2];
+#pragma unroll
+    for (int r = 0; r < 2; r++)
+#pragma unroll
+        for (int q = 0; q < 2; q++)
+            wv[r][q] = __ldg(reinterpret_cast<const uint4 *>(W + (size_t)r * MLA_DL + 8 * q));
+    pdl_wait();  // the weights above are never written by the chain; o_lat is
+    for (int e = tid; e < B * MLA_DL; e += 256) {
+        const __nv_bfloat16 *src = olat2 + ((size_t)(e / MLA_DL) * H + h) * 2 * MLA_DL;
+        os[e / MLA_DL][e % MLA_DL] =
+            __bfloat162float(src[e % MLA_DL]) + __bfloat162float(src[MLA_DL + e % MLA_DL]);
+    }
+    __syncthreads();
+#pragma unroll
+    for (int r = 0; r < 2; r++) {
+        float wf[16];
+#pragma unroll
+        for (int q = 0; q < 2; q++) {
+            const uint32_t u[4] = {wv[r][q].x, wv[r][q].y, wv[r][q].z, wv[r][q].w};
+#pragma unroll
+            for (int x = 0; x < 4; x++) {
+                wf[8 * q + 2 * x] = __uint_as_float(u[x] << 16);
+                wf[8 * q + 2 * x + 1] = __uint_as_float(u[x] & 0xffff0000u);
+            }
+        }
+        for (int b = 0; b < B; b++) {
+            float v = 0.f;
+#pragma unroll
+            for (int x = 0; x < 16; x++) v = fmaf(os[b][16 * lane + x], wf[x], v);
+#pragma unroll
+            for (int o = 16; o; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+            if (lane == 0) io<OUT>::st(out + ((size_t)b * H + h) * MLA_DV + j0 + r, v);
+        }
+    }
+}
+
 // ---------------------------------------------------------------------------- merge
 // One CTA per (head, sequence): combine the sequence's segments (max, sum, o_lat) by the
 // flash-decoding identity and write o_lat as a bf16 hi/lo pair [B][H][hi 512 | lo 512] for
-// mla_project_tc. Thread t owns latent elements 4t .. 4t+3.
+// mla_project_tc. Thread t owns latent elements 4t .. 4t+3. The segments' (max, sum) pairs
+// are read in parallel (one per thread) and the partials eight at a time, so a sequence
+// split over many clusters costs a few memory latencies, not one per segment.
 __global__ void __launch_bounds__(128)
 mla_merge(const float *__restrict__ part, const int *__restrict__ slot0,
           __nv_bfloat16 *__restrict__ olat2, int H) {
+    constexpr int MS = 128;  // segments whose weights are staged at a time
+    __shared__ float wsh[MS];
+    __shared__ float red[2][4];
+    pdl_trigger();
+    pdl_wait();  // the partials come from the attention kernel
     const int h = blockIdx.x, b = blockIdx.y, tid = threadIdx.x;
     const int s0 = slot0[b], s1 = slot0[b + 1];
     const size_t stride = (size_t)H * MLA_PART;
     const float *base = part + (size_t)h * MLA_PART;
+    // global max and sum over all segments, one segment per thread per round
     float M = -INFINITY;
-    for (int s = s0; s < s1; s++) M = fmaxf(M, base[s * stride + MLA_DL]);
+    for (int s = s0 + tid; s < s1; s += 128) M = fmaxf(M, base[s * stride + MLA_DL]);
+#pragma unroll
+    for (int o = 16; o; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
+    if ((tid & 31) == 0) red[0][tid >> 5] = M;
+    __syncthreads();
+    M = fmaxf(fmaxf(red[0][0], red[0][1]), fmaxf(red[0][2], red[0][3]));
     float L = 0.f;
-    for (int s = s0; s < s1; s++) L += exp2f(base[s * stride + MLA_DL] - M) * base[s * stride + MLA_DL + 1];
-    const float invL = 1.f / L;
+    for (int s = s0 + tid; s < s1; s += 128)
+        L += exp2f(base[s * stride + MLA_DL] - M) * base[s * stride + MLA_DL + 1];
+#pragma unroll
+    for (int o = 16; o; o >>= 1) L += __shfl_xor_sync(0xffffffffu, L, o);
+    if ((tid & 31) == 0) red[1][tid >> 5] = L;
+    __syncthreads();
+    const float invL = 1.f / ((red[1][0] + red[1][1]) + (red[1][2] + red[1][3]));
     float4 o = make_float4(0.f, 0.f, 0.f, 0.f);
-    for (int s = s0; s < s1; s++) {
-        const float w = exp2f(base[s * stride + MLA_DL] - M) * invL;
-        const float4 p = reinterpret_cast<const float4 *>(base + s * stride)[tid];
-        o.x += w * p.x; o.y += w * p.y; o.z += w * p.z; o.w += w * p.w;
+    for (int c0 = s0; c0 < s1; c0 += MS) {
+        const int nc = min(MS, s1 - c0);
+        if (tid < nc) wsh[tid] = exp2f(base[(c0 + tid) * stride + MLA_DL] - M) * invL;
+        __syncthreads();
+        int s = 0;
+        for (; s + 8 <= nc; s += 8) {
+            float4 p[8];
+#pragma unroll
+            for (int u = 0; u < 8; u++)
+                p[u] = reinterpret_cast<const float4 *>(base + (c0 + s + u) * stride)[tid];
+#pragma unroll
+            for (int u = 0; u < 8; u++) {
+                const float w = wsh[s + u];
+                o.x += w * p[u].x; o.y += w * p[u].y; o.z += w * p[u].z; o.w += w * p[u].w;
+            }
+        }
+        for (; s < nc; s++) {
+            const float w = wsh[s];
+            const float4 p = reinterpret_cast<const float4 *>(base + (c0 + s) * stride)[tid];
+            o.x += w * p.x; o.y += w * p.y; o.z += w * p.z; o.w += w * p.w;
+        }
+        __syncthreads();  // wsh is rewritten by the next round
     }
     const float ov[4] = {o.x, o.y, o.z, o.w};
     uint32_t hi[2], lo[2];
@@ -849,11 +1011,33 @@ static int mla_run(k3cuda_ctx *ctx, void *out, int out_dtype, const void *q_nope
                  "MLA inputs must be 16-byte aligned");
 
     const dim3 hgrid(H, (B + 127) / 128);
-    const int qsmem = 2 * 16384 + 16 * 8192 + 1024;
-    if (int rc_ = set_smem(mla_q_absorb_tc, qsmem)) return rc_;
-    mla_q_absorb_tc<<<hgrid, 128, qsmem, ctx->stream>>>(qmaps, (const __nv_bfloat16 *)q_rope, qlat,
-                                                        B, H, ctx->err_word);
-    rc = after_launch(ctx, "mla_q_absorb_tc");
+    const bool small = B <= MLA_SMALL_B;
+    if (small) {
+        const dim3 g(H, MLA_DL / 128);
+        const __nv_bfloat16 *qn = (const __nv_bfloat16 *)q_nope, *qr = (const __nv_bfloat16 *)q_rope,
+                            *wk = (const __nv_bfloat16 *)w_uk;
+        const long long uk = (long long)uk_head_rows * MLA_DL;
+        const char *nm = "mla_q_absorb_small";
+        const dim3 blk(256);
+        if (B <= 1)
+            rc = launch_pdl(ctx, ctx->stream, nm, mla_q_absorb_small<1>, g, blk, 0, qn, qr, wk, uk,
+                            qlat, B, H);
+        else if (B <= 2)
+            rc = launch_pdl(ctx, ctx->stream, nm, mla_q_absorb_small<2>, g, blk, 0, qn, qr, wk, uk,
+                            qlat, B, H);
+        else if (B <= 4)
+            rc = launch_pdl(ctx, ctx->stream, nm, mla_q_absorb_small<4>, g, blk, 0, qn, qr, wk, uk,
+                            qlat, B, H);
+        else
+            rc = launch_pdl(ctx, ctx->stream, nm, mla_q_absorb_small<8>, g, blk, 0, qn, qr, wk, uk,
+                            qlat, B, H);
+    } else {
+        const int qsmem = 2 * 16384 + 16 * 8192 + 1024;
+        if (int rc_ = set_smem(mla_q_absorb_tc, qsmem)) return rc_;
+        mla_q_absorb_tc<<<hgrid, 128, qsmem, ctx->stream>>>(qmaps, (const __nv_bfloat16 *)q_rope,
+                                                            qlat, B, H, ctx->err_word);
+        rc = after_launch(ctx, "mla_q_absorb_tc");
+    }
     if (rc) return rc;
 
     if (int rc_ = set_smem(mla_attend_tc, MLA_SMEM)) return rc_;
@@ -864,10 +1048,21 @@ static int mla_run(k3cuda_ctx *ctx, void *out, int out_dtype, const void *q_nope
     rc = after_launch(ctx, "mla_attend_tc");
     if (rc) return rc;
 
-    mla_merge<<<dim3(H, B), 128, 0, ctx->stream>>>(part, d_slot0, olat2, H);
-    rc = after_launch(ctx, "mla_merge");
+    rc = launch_pdl(ctx, ctx->stream, "mla_merge", mla_merge, dim3(H, B), dim3(128), 0,
+                    (const float *)part, (const int *)d_slot0, olat2, H);
     if (rc) return rc;
 
+    if (small) {
+        const dim3 pgrid(H, MLA_DV / 16);
+        const long long uv = (long long)uv_head_rows * MLA_DL;
+        const __nv_bfloat16 *o2 = olat2, *wu = (const __nv_bfloat16 *)w_uv;
+        if (out_dtype == K3CUDA_BF16)
+            return launch_pdl(ctx, ctx->stream, "mla_project_small",
+                              mla_project_small<__nv_bfloat16>, pgrid, dim3(256), 0, o2, wu, uv,
+                              (__nv_bfloat16 *)out, B, H);
+        return launch_pdl(ctx, ctx->stream, "mla_project_small", mla_project_small<float>, pgrid,
+                          dim3(256), 0, o2, wu, uv, (float *)out, B, H);
+    }
     const int psmem = 12 * 16384 + 1024;
     if (out_dtype == K3CUDA_BF16) {
         if (int rc_ = set_smem(mla_project_tc<__nv_bfloat16>, psmem)) return rc_;
@@ -937,6 +1132,8 @@ extern "C" int k3cuda_mla_attend(k3cuda_ctx *ctx, void *out, int out_dtype, cons
 __global__ void __launch_bounds__(128) mla_cache_append_k(
     __nv_bfloat16 *__restrict__ latent, __nv_bfloat16 *__restrict__ rope,
     const float *__restrict__ ct, const float *__restrict__ w, float eps, long long row_base) {
+    pdl_trigger();
+    pdl_wait();
     __shared__ double red[4];
     const int t = blockIdx.x, tid = threadIdx.x;
     const float *src = ct + (size_t)t * MLA_QW;
@@ -977,8 +1174,7 @@ extern "C" int k3cuda_mla_cache_append(k3cuda_ctx *ctx, void *latent, void *rope
     K3_ARG_CHECK(aligned(latent, 16) && aligned(rope, 16) && aligned(ct, 16) &&
                      aligned(kv_a_norm, 16),
                  "mla_cache_append: pointers must be 16-byte aligned");
-    mla_cache_append_k<<<T, 128, 0, ctx->stream>>>((__nv_bfloat16 *)latent, (__nv_bfloat16 *)rope,
-                                                   ct, kv_a_norm, eps,
-                                                   (long long)seq * cap + pos0);
-    return after_launch(ctx, "mla_cache_append");
+    return launch_pdl(ctx, ctx->stream, "mla_cache_append", mla_cache_append_k, dim3(T),
+                      dim3(128), 0, (__nv_bfloat16 *)latent, (__nv_bfloat16 *)rope, ct, kv_a_norm,
+                      eps, (long long)seq * cap + pos0);
 }

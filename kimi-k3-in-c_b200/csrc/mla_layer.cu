@@ -18,12 +18,45 @@ namespace k3 {
 constexpr int ML_DN = 128, ML_DR = 64, ML_DL = 512, ML_DV = 128;
 
 // y[r] = w * x[r] * inv, inv = 1/sqrt(mean(x^2) + eps) with the sum in double (k3_rmsnorm,
-// k3_ops.c:94-101), one row per block, in place.
+// k3_ops.c:94-101), one row per block, in place. Rows up to RN_CACHE * blockDim elements
+// are read once, all loads in flight together, and kept in registers for the scaling.
+constexpr int RN_CACHE = 8;
 __global__ void rmsnorm_rows(float *__restrict__ x, const float *__restrict__ w, int n,
                              float eps) {
+    pdl_trigger();
+    pdl_wait();
     __shared__ double red[32];
     float *row = x + (size_t)blockIdx.x * n;
     double ss = 0.0;
+    if (n <= RN_CACHE * (int)blockDim.x) {
+        float v[RN_CACHE], wv[RN_CACHE];
+#pragma unroll
+        for (int j = 0; j < RN_CACHE; j++) {
+            const int i = threadIdx.x + j * blockDim.x;
+            v[j] = i < n ? row[i] : 0.f;
+            wv[j] = i < n ? w[i] : 0.f;
+        }
+#pragma unroll
+        for (int j = 0; j < RN_CACHE; j++) ss = fma((double)v[j], (double)v[j], ss);
+#pragma unroll
+        for (int o = 16; o; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+        if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
+        __syncthreads();
+        if (threadIdx.x < 32) {
+            double t = threadIdx.x < blockDim.x / 32 ? red[threadIdx.x] : 0.0;
+#pragma unroll
+            for (int o = 16; o; o >>= 1) t += __shfl_xor_sync(0xffffffffu, t, o);
+            if (threadIdx.x == 0) red[0] = t;
+        }
+        __syncthreads();
+        const float inv = (float)(1.0 / sqrt(red[0] / (double)n + (double)eps));
+#pragma unroll
+        for (int j = 0; j < RN_CACHE; j++) {
+            const int i = threadIdx.x + j * blockDim.x;
+            if (i < n) row[i] = wv[j] * v[j] * inv;
+        }
+        return;
+    }
     for (int i = threadIdx.x; i < n; i += blockDim.x) ss = fma((double)row[i], (double)row[i], ss);
 #pragma unroll
     for (int o = 16; o; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
@@ -44,6 +77,8 @@ __global__ void rmsnorm_rows(float *__restrict__ x, const float *__restrict__ w,
 // all T*H*(dn+dr) elements)
 __global__ void mla_q_split(__nv_bfloat16 *__restrict__ qn, __nv_bfloat16 *__restrict__ qr,
                             const float *__restrict__ q, long long n) {
+    pdl_trigger();
+    pdl_wait();
     for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n;
          i += (long long)gridDim.x * blockDim.x) {
         const long long th = i / (ML_DN + ML_DR);  // (token, head) row
@@ -66,6 +101,8 @@ __global__ void f32_to_bf16(__nv_bfloat16 *__restrict__ y, const float *__restri
 __global__ void mla_gate(float *__restrict__ ot, __nv_bfloat16 *__restrict__ hi,
                          __nv_bfloat16 *__restrict__ lo, const float *__restrict__ acc,
                          const float *__restrict__ gb, long long n) {
+    pdl_trigger();  // o_proj's CTAs may be scheduled while this kernel runs
+    pdl_wait();
     for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n;
          i += (long long)gridDim.x * blockDim.x) {
         float v = acc[i];
@@ -202,8 +239,9 @@ extern "C" int k3cuda_mla_layer(k3cuda_ctx *ctx, float *out, const float *x,
         if (w->g && (rc = gemm(ctx, gb, x, xs, w->g, wdt, T, E, HV))) return rc;
     }
     // q = q_b(RMSNorm(ql))
-    rmsnorm_rows<<<T, 256, 0, ctx->stream>>>(ql, w->q_a_norm, q_lora, rms_eps);
-    if ((rc = after_launch(ctx, "rmsnorm_rows"))) return rc;
+    if ((rc = launch_pdl(ctx, ctx->stream, "rmsnorm_rows", rmsnorm_rows, dim3(T), dim3(256), 0,
+                         ql, (const float *)w->q_a_norm, q_lora, rms_eps)))
+        return rc;
     if (pl.split && (rc = split(ctx, qls, ql, (long long)T * q_lora))) return rc;
     if ((rc = project(ctx, q, ql, qls, w->q_b, wdt, T, q_lora, HQ))) return rc;
     // the new latent / rope rows (kv_a_norm over the latent only)
@@ -212,9 +250,10 @@ extern "C" int k3cuda_mla_layer(k3cuda_ctx *ctx, float *out, const float *x,
         return rc;
     {
         const long long n = (long long)T * HQ;
-        mla_q_split<<<grid_for(ctx, n), 256, 0, ctx->stream>>>(qn, qr, q, n);
+        if ((rc = launch_pdl(ctx, ctx->stream, "mla_q_split", mla_q_split, dim3(grid_for(ctx, n)),
+                             dim3(256), 0, qn, qr, (const float *)q, n)))
+            return rc;
     }
-    if ((rc = after_launch(ctx, "mla_q_split"))) return rc;
     const void *kvb = w->kv_b;
     if (wdt == K3CUDA_F32) {
         const long long n = (long long)H * (ML_DN + ML_DV) * ML_DL;
