@@ -663,9 +663,10 @@ static int layer_core(k3cuda_ctx *ctx, float *out, const float *x, const k3cuda_
     if (!pl.gemm_path) {
         const Proj first[5] = {{w->q, yq, P}, {w->k, yk, P}, {w->v, yv, P},
                                {w->b, yb, H}, {w->f_a, fa, D}};
-        if ((rc = matvec(ctx, x, T, E, first, 5, wdt))) return rc;
-        // The gate projection (needed at step 8) streams on the side stream while the chain
-        // of small kernels of steps 2-6 runs on the main one.
+        // The gate projection (needed at step 8) streams on the side stream from the start:
+        // its blocks fill the tail of the main projection launch and it finishes while the
+        // chain of small kernels of steps 2-6 runs on the main stream (forking it after the
+        // main projection instead left step 7 waiting for it: 0.172 vs 0.161 ms per token).
         K3_CUDA_TRY(cudaEventRecord(ctx->ev_fork, ctx->stream));
         K3_CUDA_TRY(cudaStreamWaitEvent(ctx->aux, ctx->ev_fork, 0));
         cudaStream_t main_stream = ctx->stream;
@@ -676,6 +677,7 @@ static int layer_core(k3cuda_ctx *ctx, float *out, const float *x, const k3cuda_
         if (rc) return rc;
         K3_CUDA_TRY(cudaEventRecord(ctx->ev_join, ctx->aux));
         forked = true;
+        if ((rc = matvec(ctx, x, T, E, first, 5, wdt))) return rc;
     } else {
         if (pl.split && (rc = split(ctx, xs, x, (long long)T * E))) return rc;
         const Proj first[6] = {{w->q, yq, P}, {w->k, yk, P}, {w->v, yv, P},
