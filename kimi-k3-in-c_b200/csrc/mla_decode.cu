@@ -289,6 +289,8 @@ mla_attend_tc(const __grid_constant__ MlaMaps maps, const MlaSeg *__restrict__ s
     extern __shared__ uint8_t smraw[];
     uint8_t *sm = (uint8_t *)(((uintptr_t)smraw + 1023) & ~(uintptr_t)1023);
     __shared__ MlaBars bars;
+    pdl_trigger();
+    pdl_wait();  // the work plan, q_lat and the cache come from earlier work
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const uint32_t rank = cluster_rank(), peer = rank ^ 1u;
     const int cl = blockIdx.x >> 1;
@@ -667,12 +669,25 @@ mla_q_absorb_small(const __nv_bfloat16 *__restrict__ q_nope,
     pdl_trigger();
     const int h = blockIdx.x, z = blockIdx.y, tid = threadIdx.x, warp = tid >> 5;
     const int cg = tid & 15, r0 = tid >> 4, c0 = 128 * z + 8 * cg;
-    const __nv_bfloat16 *W = w_uk + (size_t)h * uk_head_elems + c0;
     uint4 wv[8];
+    if (h < H) {
+        const __nv_bfloat16 *W = w_uk + (size_t)h * uk_head_elems + c0;
 #pragma unroll
-    for (int j = 0; j < 8; j++)
-        wv[j] = __ldg(reinterpret_cast<const uint4 *>(W + (size_t)(r0 + 16 * j) * MLA_DL));
+        for (int j = 0; j < 8; j++)
+            wv[j] = __ldg(reinterpret_cast<const uint4 *>(W + (size_t)(r0 + 16 * j) * MLA_DL));
+    }
     pdl_wait();  // the weights above are never written by the chain; q_nope is
+    if (h >= H) {
+        // a padding head of the MMA's M: its query row must score zero
+        for (int e = tid; e < B * 128; e += 256)
+            qlat[((size_t)(e >> 7) * MLA_HP + h) * MLA_QW + 128 * z + (e & 127)] =
+                __float2bfloat16_rn(0.f);
+        if (z == 0)
+            for (int e = tid; e < B * MLA_DR; e += 256)
+                qlat[((size_t)(e / MLA_DR) * MLA_HP + h) * MLA_QW + MLA_DL + e % MLA_DR] =
+                    __float2bfloat16_rn(0.f);
+        return;
+    }
     for (int e = tid; e < NB * MLA_DN; e += 256) {
         const int b = e / MLA_DN, i = e % MLA_DN;
         qs[b][i] = b < B ? __bfloat162float(q_nope[((size_t)b * H + h) * MLA_DN + i]) : 0.f;
@@ -981,7 +996,8 @@ static int mla_run(k3cuda_ctx *ctx, void *out, int out_dtype, const void *q_nope
         put(d_row0, row0.data(), (size_t)B * sizeof(int));
         if ((rc = stage_h2d(ctx, workspace, img.data(), tbytes))) return rc;
     }
-    if (H < MLA_HP)  // the padded query rows must score zero
+    const bool small = B <= MLA_SMALL_B;  // the small absorb kernel zeroes the padded rows
+    if (H < MLA_HP && !small)  // the padded query rows must score zero
         K3_CUDA_TRY(cudaMemset2DAsync(qlat + (size_t)H * MLA_QW, (size_t)MLA_HP * MLA_QW * 2, 0,
                                       (size_t)(MLA_HP - H) * MLA_QW * 2, (size_t)B, ctx->stream));
 
@@ -1011,9 +1027,8 @@ static int mla_run(k3cuda_ctx *ctx, void *out, int out_dtype, const void *q_nope
                  "MLA inputs must be 16-byte aligned");
 
     const dim3 hgrid(H, (B + 127) / 128);
-    const bool small = B <= MLA_SMALL_B;
     if (small) {
-        const dim3 g(H, MLA_DL / 128);
+        const dim3 g(MLA_HP, MLA_DL / 128);
         const __nv_bfloat16 *qn = (const __nv_bfloat16 *)q_nope, *qr = (const __nv_bfloat16 *)q_rope,
                             *wk = (const __nv_bfloat16 *)w_uk;
         const long long uk = (long long)uk_head_rows * MLA_DL;
@@ -1042,10 +1057,10 @@ static int mla_run(k3cuda_ctx *ctx, void *out, int out_dtype, const void *q_nope
 
     if (int rc_ = set_smem(mla_attend_tc, MLA_SMEM)) return rc_;
     const float scale_log2e = scale * 1.4426950408889634f;
-    mla_attend_tc<<<2 * p.ncl, MLA_THREADS, MLA_SMEM, ctx->stream>>>(maps, d_segs, d_cl, d_lens, qlat,
-                                                           part, H, d_row0, scale_log2e,
-                                                           ctx->err_word);
-    rc = after_launch(ctx, "mla_attend_tc");
+    rc = launch_pdl(ctx, ctx->stream, "mla_attend_tc", mla_attend_tc, dim3(2 * p.ncl),
+                    dim3(MLA_THREADS), MLA_SMEM, maps, (const MlaSeg *)d_segs, (const int *)d_cl,
+                    (const int *)d_lens, (const __nv_bfloat16 *)qlat, part, H, (const int *)d_row0,
+                    scale_log2e, ctx->err_word);
     if (rc) return rc;
 
     rc = launch_pdl(ctx, ctx->stream, "mla_merge", mla_merge, dim3(H, B), dim3(128), 0,
