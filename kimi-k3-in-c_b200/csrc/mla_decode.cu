@@ -809,45 +809,78 @@ mla_merge(const float *__restrict__ part, const int *__restrict__ slot0,
     const int s0 = slot0[b], s1 = slot0[b + 1];
     const size_t stride = (size_t)H * MLA_PART;
     const float *base = part + (size_t)h * MLA_PART;
-    // global max and sum over all segments, one segment per thread per round
-    float M = -INFINITY;
-    for (int s = s0 + tid; s < s1; s += 128) M = fmaxf(M, base[s * stride + MLA_DL]);
-#pragma unroll
-    for (int o = 16; o; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
-    if ((tid & 31) == 0) red[0][tid >> 5] = M;
-    __syncthreads();
-    M = fmaxf(fmaxf(red[0][0], red[0][1]), fmaxf(red[0][2], red[0][3]));
-    float L = 0.f;
-    for (int s = s0 + tid; s < s1; s += 128)
-        L += exp2f(base[s * stride + MLA_DL] - M) * base[s * stride + MLA_DL + 1];
-#pragma unroll
-    for (int o = 16; o; o >>= 1) L += __shfl_xor_sync(0xffffffffu, L, o);
-    if ((tid & 31) == 0) red[1][tid >> 5] = L;
-    __syncthreads();
-    const float invL = 1.f / ((red[1][0] + red[1][1]) + (red[1][2] + red[1][3]));
     float4 o = make_float4(0.f, 0.f, 0.f, 0.f);
-    for (int c0 = s0; c0 < s1; c0 += MS) {
-        const int nc = min(MS, s1 - c0);
-        if (tid < nc) wsh[tid] = exp2f(base[(c0 + tid) * stride + MLA_DL] - M) * invL;
-        __syncthreads();
-        int s = 0;
-        for (; s + 8 <= nc; s += 8) {
-            float4 p[8];
+    constexpr int FEW = 4;
+    if (s1 - s0 <= FEW) {
+        // a few segments (the common case): every thread reads their (max, sum) pairs and
+        // partial rows at once, no shared memory
+        float mv[FEW], lv[FEW];
+        float4 pv[FEW];
 #pragma unroll
-            for (int u = 0; u < 8; u++)
-                p[u] = reinterpret_cast<const float4 *>(base + (c0 + s + u) * stride)[tid];
-#pragma unroll
-            for (int u = 0; u < 8; u++) {
-                const float w = wsh[s + u];
-                o.x += w * p[u].x; o.y += w * p[u].y; o.z += w * p[u].z; o.w += w * p[u].w;
+        for (int i = 0; i < FEW; i++) {
+            if (s0 + i < s1) {
+                const float *sp = base + (size_t)(s0 + i) * stride;
+                mv[i] = sp[MLA_DL];
+                lv[i] = sp[MLA_DL + 1];
+                pv[i] = reinterpret_cast<const float4 *>(sp)[tid];
             }
         }
-        for (; s < nc; s++) {
-            const float w = wsh[s];
-            const float4 p = reinterpret_cast<const float4 *>(base + (c0 + s) * stride)[tid];
-            o.x += w * p.x; o.y += w * p.y; o.z += w * p.z; o.w += w * p.w;
+        float M = -INFINITY;
+#pragma unroll
+        for (int i = 0; i < FEW; i++)
+            if (s0 + i < s1) M = fmaxf(M, mv[i]);
+        float L = 0.f;
+#pragma unroll
+        for (int i = 0; i < FEW; i++)
+            if (s0 + i < s1) L += exp2f(mv[i] - M) * lv[i];
+        const float invL = 1.f / L;
+#pragma unroll
+        for (int i = 0; i < FEW; i++) {
+            if (s0 + i < s1) {
+                const float w = exp2f(mv[i] - M) * invL;
+                o.x += w * pv[i].x; o.y += w * pv[i].y; o.z += w * pv[i].z; o.w += w * pv[i].w;
+            }
         }
-        __syncthreads();  // wsh is rewritten by the next round
+    } else {
+        // global max and sum over all segments, one segment per thread per round
+        float M = -INFINITY;
+        for (int s = s0 + tid; s < s1; s += 128) M = fmaxf(M, base[s * stride + MLA_DL]);
+#pragma unroll
+        for (int o = 16; o; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
+        if ((tid & 31) == 0) red[0][tid >> 5] = M;
+        __syncthreads();
+        M = fmaxf(fmaxf(red[0][0], red[0][1]), fmaxf(red[0][2], red[0][3]));
+        float L = 0.f;
+        for (int s = s0 + tid; s < s1; s += 128)
+            L += exp2f(base[s * stride + MLA_DL] - M) * base[s * stride + MLA_DL + 1];
+#pragma unroll
+        for (int o = 16; o; o >>= 1) L += __shfl_xor_sync(0xffffffffu, L, o);
+        if ((tid & 31) == 0) red[1][tid >> 5] = L;
+        __syncthreads();
+        const float invL = 1.f / ((red[1][0] + red[1][1]) + (red[1][2] + red[1][3]));
+        for (int c0 = s0; c0 < s1; c0 += MS) {
+            const int nc = min(MS, s1 - c0);
+            if (tid < nc) wsh[tid] = exp2f(base[(c0 + tid) * stride + MLA_DL] - M) * invL;
+            __syncthreads();
+            int s = 0;
+            for (; s + 8 <= nc; s += 8) {
+                float4 p[8];
+#pragma unroll
+                for (int u = 0; u < 8; u++)
+                    p[u] = reinterpret_cast<const float4 *>(base + (c0 + s + u) * stride)[tid];
+#pragma unroll
+                for (int u = 0; u < 8; u++) {
+                    const float w = wsh[s + u];
+                    o.x += w * p[u].x; o.y += w * p[u].y; o.z += w * p[u].z; o.w += w * p[u].w;
+                }
+            }
+            for (; s < nc; s++) {
+                const float w = wsh[s];
+                const float4 p = reinterpret_cast<const float4 *>(base + (c0 + s) * stride)[tid];
+                o.x += w * p.x; o.y += w * p.y; o.z += w * p.z; o.w += w * p.w;
+            }
+            __syncthreads();  // wsh is rewritten by the next round
+        }
     }
     const float ov[4] = {o.x, o.y, o.z, o.w};
     uint32_t hi[2], lo[2];
