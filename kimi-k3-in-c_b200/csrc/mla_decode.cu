@@ -230,10 +230,14 @@ mla_project_tc(const __grid_constant__ HeadGemmMaps maps, OUT *__restrict__ out,
                 mma_bf16_ss(tb, ad, bd, id, (kb | kin) ? 1u : 0u);
             }
             mma_commit(&bar_empty[st]);
-            if (kb + NS < KB) {
-                if (!(ok = mbar_wait(&bar_empty[st], (kb / NS) & 1, err, 0x413))) break;
-                mbar_expect_tx(&bar_full[st], 16384);
-                tma_load_3d(sA + st * 16384, &maps.a, &bar_full[st], (kb + NS) * 64, h, b0);
+            // refill the previous block's stage while this block's MMAs run (waiting for this
+            // block's own stage here would leave the tensor pipe idle at every step)
+            const int pk = kb - 1;
+            if (pk >= 0 && pk + NS < KB) {
+                const int ps = pk % NS;
+                if (!(ok = mbar_wait(&bar_empty[ps], (pk / NS) & 1, err, 0x413))) break;
+                mbar_expect_tx(&bar_full[ps], 16384);
+                tma_load_3d(sA + ps * 16384, &maps.a, &bar_full[ps], (pk + NS) * 64, h, b0);
             }
         }
         if (ok) mma_commit(&bar_mma);
