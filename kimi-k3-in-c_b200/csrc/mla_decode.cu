@@ -99,7 +99,7 @@ __device__ __forceinline__ bool warp_wait(uint64_t *bar, uint32_t parity, unsign
 // The two small per-head products around the attention, on tcgen05 with the sequences as the
 // MMA's M (128 per CTA; rows past B are zero-filled by TMA and never stored):
 //   mla_q_absorb_tc  qlat[b][h][0:512] = q_nope[b][h] (1 x 128) . W_UK[h] (128 x 512), bf16,
-//                    and qlat[b][h][512:576] = q_rope[b][h]
+//                    and qlat[b][h][512:576] = q_rope[b][h]; two CTAs per head (256 columns)
 //   mla_project_tc   out[b][h][:] = o_lat[b][h] (1 x 512) . W_UV[h]^T (512 x 128), with
 //                    o_lat carried as a bf16 hi/lo pair (K = 1024, W_UV's blocks read twice)
 //                    so the fp32 o_lat reaches the MMA to ~16 mantissa bits
@@ -107,43 +107,44 @@ struct HeadGemmMaps {
     CUtensorMap a, b;
 };
 
-__global__ void __launch_bounds__(128, 1)
+// CTA (h, y, z) computes columns [256 z, +256) of q_lat for 128 sequences: a head's 128 KB
+// W_UK block is split over two CTAs, and two CTAs (97 KB of shared memory each) share an SM.
+__global__ void __launch_bounds__(128, 2)
 mla_q_absorb_tc(const __grid_constant__ HeadGemmMaps maps, const __nv_bfloat16 *__restrict__ q_rope,
                 __nv_bfloat16 *__restrict__ qlat, int B, int H, unsigned *__restrict__ err) {
     extern __shared__ uint8_t smraw[];
     uint8_t *sm = (uint8_t *)(((uintptr_t)smraw + 1023) & ~(uintptr_t)1023);
     uint8_t *sA = sm;              // 2 K-blocks x [128 b][128 B]
-    uint8_t *sB = sm + 2 * 16384;  // [2 K-blocks][8 N-blocks] x [64 i][128 B]
+    uint8_t *sB = sm + 2 * 16384;  // [2 K-blocks][4 N-blocks] x [64 i][128 B]
     __shared__ uint64_t bar_ld, bar_mma;
     __shared__ uint32_t tslot;
-    const int h = blockIdx.x, b0 = blockIdx.y * 128, tid = threadIdx.x, warp = tid >> 5;
+    const int h = blockIdx.x, b0 = blockIdx.y * 128, z = blockIdx.z, tid = threadIdx.x,
+              warp = tid >> 5;
     if (tid == 0) {
         mbar_init(&bar_ld, 1);
         mbar_init(&bar_mma, 1);
         fence_barrier_init();
     }
-    if (warp == 1) tmem_alloc(&tslot, 512);
+    if (warp == 1) tmem_alloc(&tslot, 256);
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
     const uint32_t tb = tslot;
     if (tid == 0) {
-        mbar_expect_tx(&bar_ld, 2 * 16384 + 16 * 8192);
+        mbar_expect_tx(&bar_ld, 2 * 16384 + 8 * 8192);
         for (int kb = 0; kb < 2; kb++) tma_load_3d(sA + kb * 16384, &maps.a, &bar_ld, kb * 64, h, b0);
         for (int kb = 0; kb < 2; kb++)
-            for (int nb = 0; nb < 8; nb++)
-                tma_load_3d(sB + (kb * 8 + nb) * 8192, &maps.b, &bar_ld, nb * 64, kb * 64, h);
+            for (int nb = 0; nb < 4; nb++)
+                tma_load_3d(sB + (kb * 4 + nb) * 8192, &maps.b, &bar_ld, (4 * z + nb) * 64, kb * 64,
+                            h);
         if (mbar_wait(&bar_ld, 0, err, 0x401)) {
             tc_fence_after();
             constexpr uint32_t id = idesc_f16(128, 256, false, true);
             for (int ks = 0; ks < 8; ks++) {
                 const int kb = ks / 4, kin = ks % 4;
                 const uint64_t ad = sdesc_kmajor(smem_u32(sA + kb * 16384 + kin * 32));
-                for (int half = 0; half < 2; half++) {
-                    const uint64_t bd =
-                        sdesc_mnmajor(smem_u32(sB + (kb * 8 + half * 4) * 8192 + kin * 2048), 8192);
-                    mma_bf16_ss(tb + half * 256, ad, bd, id, ks ? 1u : 0u);
-                }
+                const uint64_t bd = sdesc_mnmajor(smem_u32(sB + kb * 4 * 8192 + kin * 2048), 8192);
+                mma_bf16_ss(tb, ad, bd, id, ks ? 1u : 0u);
             }
             mma_commit(&bar_mma);
         }
@@ -153,7 +154,7 @@ mla_q_absorb_tc(const __grid_constant__ HeadGemmMaps maps, const __nv_bfloat16 *
     tc_fence_after();
     const int b = b0 + 32 * warp + (tid & 31);
     if (ok) {
-        for (int c = 0; c < 512; c += 16) {
+        for (int c = 0; c < 256; c += 16) {
             float v[16];
             tmem_ld16(tb + ((uint32_t)(32 * warp) << 16) + c, v);
             tmem_wait_ld();
@@ -164,12 +165,13 @@ mla_q_absorb_tc(const __grid_constant__ HeadGemmMaps maps, const __nv_bfloat16 *
                     const __nv_bfloat162 t2 = __floats2bfloat162_rn(v[2 * i], v[2 * i + 1]);
                     pk[i] = *reinterpret_cast<const uint32_t *>(&t2);
                 }
-                uint4 *dst = reinterpret_cast<uint4 *>(qlat + ((size_t)b * MLA_HP + h) * MLA_QW + c);
+                uint4 *dst = reinterpret_cast<uint4 *>(qlat + ((size_t)b * MLA_HP + h) * MLA_QW +
+                                                       256 * z + c);
                 dst[0] = make_uint4(pk[0], pk[1], pk[2], pk[3]);
                 dst[1] = make_uint4(pk[4], pk[5], pk[6], pk[7]);
             }
         }
-        if (b < B) {
+        if (b < B && z == 0) {
             const uint4 *src = reinterpret_cast<const uint4 *>(q_rope + ((size_t)b * H + h) * MLA_DR);
             uint4 *dst = reinterpret_cast<uint4 *>(qlat + ((size_t)b * MLA_HP + h) * MLA_QW + MLA_DL);
 #pragma unroll
@@ -180,24 +182,23 @@ mla_q_absorb_tc(const __grid_constant__ HeadGemmMaps maps, const __nv_bfloat16 *
     __syncthreads();
     if (warp == 1) {
         __syncwarp();
-        tmem_dealloc(tb, 512);
+        tmem_dealloc(tb, 256);
     }
 }
 
 template <typename OUT>
-__global__ void __launch_bounds__(128, 1)
+__global__ void __launch_bounds__(128, 2)
 mla_project_tc(const __grid_constant__ HeadGemmMaps maps, OUT *__restrict__ out, int B, int H,
                unsigned *__restrict__ err) {
-    constexpr int NS = 4, KB = 16;  // A stages; K blocks of 64 (hi 0..7, lo 8..15)
+    // K blocks of 64 (hi 0..7, lo 8..15); each stage holds one A block (o_lat rows) and the
+    // W_UV block it meets, so a CTA needs 97 KB of shared memory and two share an SM
+    constexpr int NS = 3, KB = 16, STAGE = 2 * 16384;
     extern __shared__ uint8_t smraw[];
     uint8_t *sm = (uint8_t *)(((uintptr_t)smraw + 1023) & ~(uintptr_t)1023);
-    uint8_t *sB = sm;               // 8 K-blocks x [128 j][128 B]
-    uint8_t *sA = sm + 8 * 16384;   // NS stages x [128 b][128 B]
-    __shared__ uint64_t bar_b, bar_full[NS], bar_empty[NS], bar_mma;
+    __shared__ uint64_t bar_full[NS], bar_empty[NS], bar_mma;
     __shared__ uint32_t tslot;
     const int h = blockIdx.x, b0 = blockIdx.y * 128, tid = threadIdx.x, warp = tid >> 5;
     if (tid == 0) {
-        mbar_init(&bar_b, 1);
         mbar_init(&bar_mma, 1);
         for (int i = 0; i < NS; i++) {
             mbar_init(&bar_full[i], 1);
@@ -211,38 +212,38 @@ mla_project_tc(const __grid_constant__ HeadGemmMaps maps, OUT *__restrict__ out,
     tc_fence_after();
     const uint32_t tb = tslot;
     if (tid == 0) {
+        auto load = [&](int kb) {  // block kb into stage kb % NS
+            uint8_t *st = sm + (kb % NS) * STAGE;
+            mbar_expect_tx(&bar_full[kb % NS], STAGE);
+            tma_load_3d(st, &maps.a, &bar_full[kb % NS], kb * 64, h, b0);
+            tma_load_3d(st + 16384, &maps.b, &bar_full[kb % NS], (kb % 8) * 64, 0, h);
+        };
+        for (int kb = 0; kb < NS; kb++) load(kb);
         bool ok = true;
-        mbar_expect_tx(&bar_b, 8 * 16384);
-        for (int kb = 0; kb < 8; kb++) tma_load_3d(sB + kb * 16384, &maps.b, &bar_b, kb * 64, 0, h);
-        for (int kb = 0; kb < NS; kb++) {
-            mbar_expect_tx(&bar_full[kb], 16384);
-            tma_load_3d(sA + kb * 16384, &maps.a, &bar_full[kb], kb * 64, h, b0);
-        }
-        ok = mbar_wait(&bar_b, 0, err, 0x411);
         constexpr uint32_t id = idesc_f16(128, 128, false, false);
         for (int kb = 0; kb < KB && ok; kb++) {
             const int st = kb % NS;
             if (!(ok = mbar_wait(&bar_full[st], (kb / NS) & 1, err, 0x412))) break;
             tc_fence_after();
             for (int kin = 0; kin < 4; kin++) {
-                const uint64_t ad = sdesc_kmajor(smem_u32(sA + st * 16384 + kin * 32));
-                const uint64_t bd = sdesc_kmajor(smem_u32(sB + (kb % 8) * 16384 + kin * 32));
+                const uint64_t ad = sdesc_kmajor(smem_u32(sm + st * STAGE + kin * 32));
+                const uint64_t bd = sdesc_kmajor(smem_u32(sm + st * STAGE + 16384 + kin * 32));
                 mma_bf16_ss(tb, ad, bd, id, (kb | kin) ? 1u : 0u);
             }
             mma_commit(&bar_empty[st]);
-            // refill the previous block's stage while this block's MMAs run (waiting for this
-            // block's own stage here would leave the tensor pipe idle at every step)
+            // refill the previous block's stage while this block's MMAs run
             const int pk = kb - 1;
             if (pk >= 0 && pk + NS < KB) {
-                const int ps = pk % NS;
-                if (!(ok = mbar_wait(&bar_empty[ps], (pk / NS) & 1, err, 0x413))) break;
-                mbar_expect_tx(&bar_full[ps], 16384);
-                tma_load_3d(sA + ps * 16384, &maps.a, &bar_full[ps], (pk + NS) * 64, h, b0);
+                if (!(ok = mbar_wait(&bar_empty[pk % NS], (pk / NS) & 1, err, 0x413))) break;
+                load(pk + NS);
             }
         }
         if (ok) mma_commit(&bar_mma);
         // drain: the last load of every stage has landed before the CTA may exit
-        for (int st = 0; st < NS; st++) mbar_wait_quiet(&bar_full[st], ((KB - NS + st) / NS) & 1);
+        for (int st = 0; st < NS; st++) {
+            const int jl = st + NS * ((KB - 1 - st) / NS);  // the last block of stage st
+            mbar_wait_quiet(&bar_full[st], (jl / NS) & 1);
+        }
     }
     __syncwarp();
     const bool ok = warp_wait(&bar_mma, 0, err, 0x414);
@@ -1104,9 +1105,10 @@ static int mla_run(k3cuda_ctx *ctx, void *out, int out_dtype, const void *q_nope
             rc = launch_pdl(ctx, ctx->stream, nm, mla_q_absorb_small<8>, g, blk, 0, qn, qr, wk, uk,
                             qlat, B, H);
     } else {
-        const int qsmem = 2 * 16384 + 16 * 8192 + 1024;
+        const int qsmem = 2 * 16384 + 8 * 8192 + 1024;
         if (int rc_ = set_smem(mla_q_absorb_tc, qsmem)) return rc_;
-        mla_q_absorb_tc<<<hgrid, 128, qsmem, ctx->stream>>>(qmaps, (const __nv_bfloat16 *)q_rope,
+        const dim3 qgrid(H, (B + 127) / 128, 2);  // two 256-column halves of q_lat per head
+        mla_q_absorb_tc<<<qgrid, 128, qsmem, ctx->stream>>>(qmaps, (const __nv_bfloat16 *)q_rope,
                                                             qlat, B, H, ctx->err_word);
         rc = after_launch(ctx, "mla_q_absorb_tc");
     }
@@ -1135,7 +1137,7 @@ static int mla_run(k3cuda_ctx *ctx, void *out, int out_dtype, const void *q_nope
         return launch_pdl(ctx, ctx->stream, "mla_project_small", mla_project_small<float>, pgrid,
                           dim3(256), 0, o2, wu, uv, (float *)out, B, H);
     }
-    const int psmem = 12 * 16384 + 1024;
+    const int psmem = 3 * 2 * 16384 + 1024;
     if (out_dtype == K3CUDA_BF16) {
         if (int rc_ = set_smem(mla_project_tc<__nv_bfloat16>, psmem)) return rc_;
         mla_project_tc<__nv_bfloat16><<<hgrid, 128, psmem, ctx->stream>>>(
