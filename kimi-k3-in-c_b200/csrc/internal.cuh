@@ -125,6 +125,10 @@ inline bool aligned(const void *p, size_t a) { return ((uintptr_t)p % a) == 0; }
 // it reads anything an earlier kernel wrote and before its first global write; launched
 // without the attribute, pdl_wait() returns at once. pdl_trigger() lets the next kernel be
 // scheduled once every CTA of this one has issued it (its pdl_wait still waits for the end).
+// A kernel that does not call pdl_trigger lets its successor start only when it has finished,
+// as a plain launch would. The projections read weights before their pdl_wait, which is safe
+// because no kernel that calls pdl_trigger writes a weight matrix; a kernel that produces
+// weights (the MXFP4 expansion, the kv_b conversion) must keep not calling it.
 __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 __device__ __forceinline__ void pdl_trigger() {
     asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
