@@ -50,7 +50,8 @@ sys.path.insert(0, os.path.join(ROOT, "kimi-k3-in-c_b200"))
 
 import workloads as W  # noqa: E402
 
-# Algorithmic bytes per unit (one step of each workload); derivation in DESIGN.md.
+# Algorithmic bytes per unit (one step of each workload): every tensor the step must read or
+# write once, counted by the *_bytes functions below.
 DECODE_B, DECODE_H, DECODE_D = 256, 32, 128
 
 

@@ -265,7 +265,7 @@ kda_prep_tc(const __grid_constant__ PrepMaps maps, const TcChunk *__restrict__ c
     // them by e^(G_r(t)) into Ktil and Qtil.
     const int cc = 2 * warp + (lane >> 4), j = lane & 15, kbk = cc >> 3, ch = cc & 7;
     const int i0 = 8 * cc;
-    uint4 b2[3];    // rows of B_2, written once round 2's buffer is free
+    uint4 b2[3];    // rows of B_2, written once MMA round 2's buffer is free
     uint4 kbar[4];  // Kbar rows, stored once the first region is free
     {
         float gc[8];
@@ -426,7 +426,7 @@ kda_prep_tc(const __grid_constant__ PrepMaps maps, const TcChunk *__restrict__ c
             }
         }
     };
-    // (Akk lands over the B operands, so nothing is read out before round 2 completes)
+    // (Akk lands over the B operands, so nothing is read out before MMA round 2 completes)
     if (ok) ok = mbar_wait(&bar_mma, 1, err, 0x504);
     tc_fence_after();
     if (ok) readout();

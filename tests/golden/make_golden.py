@@ -150,7 +150,9 @@ def convert_mxfp4(ref_dir: str):
 
 
 def main():
-    ref_dir = sys.argv[1] if len(sys.argv) > 1 else "/root/reference"
+    if len(sys.argv) < 2:
+        sys.exit("usage: make_golden.py <reference checkout (FareedKhan-dev/kimi-k3-in-c)>")
+    ref_dir = sys.argv[1]
     for name in ("kda_recur1", "kda_recur8", "kda_decay", "kda_layer1", "kda_layer8", "mla"):
         convert_fixture(ref_dir, name)
     with open(os.path.join(ref_dir, "tests", "fixtures", "ops", "MANIFEST.json")) as f:
