@@ -74,6 +74,24 @@ def test_workspace_queries_are_host_only():
     assert n.value == 8 * 1000 * 8 * 128 * 2
 
 
+def test_host_decode_staging_query():
+    """The staging image of k3cuda_kda_decode_host: q, k, v, o in the io dtype, gate and beta in
+    fp32, each region rounded up to 256 bytes; bad arguments are refused, not crashed on."""
+    L = k3cuda.lib()
+    n = C.c_size_t()
+    ns = 256 * 32
+    k3cuda.check(L.k3cuda_kda_decode_host_workspace(256, 32, 128, 128, k3cuda.BF16, C.byref(n)))
+    assert n.value == 4 * ns * 128 * 2 + ns * 128 * 4 + ns * 4
+    k3cuda.check(L.k3cuda_kda_decode_host_workspace(256, 32, 128, 128, k3cuda.F32, C.byref(n)))
+    assert n.value == 5 * ns * 128 * 4 + ns * 4
+    k3cuda.check(L.k3cuda_kda_decode_host_workspace(3, 1, 16, 16, k3cuda.BF16, C.byref(n)))
+    assert n.value == 6 * 256  # every region of 3 x 16 values rounds up to 256 bytes
+    assert L.k3cuda_kda_decode_host_workspace(3, 1, 16, 16, 7, C.byref(n)) == k3cuda.ERR_ARG
+    assert L.k3cuda_kda_decode_host_workspace(-1, 1, 16, 16, k3cuda.BF16, C.byref(n)) == \
+        k3cuda.ERR_ARG
+    assert L.k3cuda_kda_decode_host_workspace(3, 1, 16, 16, k3cuda.BF16, None) == k3cuda.ERR_ARG
+
+
 def test_init_without_gpu_fails_loudly():
     L = k3cuda.lib()
     cnt = C.c_int(0)
