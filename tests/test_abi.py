@@ -118,3 +118,26 @@ def test_workload_shapes():
     n = np.linalg.norm(c["q"].astype(np.float64), axis=-1)
     assert np.all(np.abs(n - 1) < 1e-2)
     assert np.all(c["g"] <= 0) and np.all((c["beta"] > 0) & (c["beta"] < 1))
+
+
+def test_bench_unit_counts():
+    """The algorithmic bytes and FLOPs that bench.py divides by (the roofline numerators) for the
+    headline configurations, written out: each tensor a step must read or write once."""
+    import importlib.util
+    import os
+    spec = importlib.util.spec_from_file_location(
+        "bench_mod", os.path.join(os.path.dirname(__file__), "..", "bench.py"))
+    b = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(b)
+    # config 1: fp32 state read + written, bf16 q, k, v, o, fp32 g and beta
+    assert b.decode_bytes(256, 32, 128) == 1_086_357_504
+    # config 2: 1536 B per (token, head)
+    assert b.prefill_bytes(32768, 32, 128) == 1_614_807_040 == 32768 * 32 * 1536 + 32768 * 32 * 4
+    assert b.mla_bytes(64, 8192, 128) == 642_777_088
+    assert b.layer_bytes(1, 7168, 96, 128, 4) == 900_685_824
+    assert b.layer_flops(4096, 7168, 96, 128) == 2 * 4096 * (4 * 12288 * 7168 + 96 * 7168 +
+                                                              128 * 7168 + 128 * 12288 +
+                                                              12288 * 7168)
+    assert b.mla_layer_bytes(1, 8192) == 473_882_624
+    assert b.moe_expert_bytes() == 281_608_192
+    assert b.mla_prefill_flops(4096, 128) == 2_474_471_587_840
