@@ -71,6 +71,7 @@ struct Fp4Args {
 template <int NT, int R>
 __global__ void __launch_bounds__(FP4_THREADS) mxfp4_rows(const __grid_constant__ Fp4Args a) {
     __shared__ float part[FP4_WARPS][R * NT];
+    pdl_trigger();
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int seg = blockIdx.x / a.blocks_per_seg, b = blockIdx.x - seg * a.blocks_per_seg;
     const float *xs = a.x[seg];
@@ -88,16 +89,23 @@ __global__ void __launch_bounds__(FP4_THREADS) mxfp4_rows(const __grid_constant_
     for (int r = 0; r < R; r++)
 #pragma unroll
         for (int t = 0; t < NT; t++) acc[r][t] = 0.f;
-#pragma unroll 1
-    for (int g = g0 + lane; g < g1; g += 32) {
-        uint4 pk[R];
-        float sf[R];
+    uint4 pk[R];
+    float sf[R];
+    auto load_w = [&](int g) {  // this lane's group g of every row: codes and scale
 #pragma unroll
         for (int r = 0; r < R; r++) {
             const int rr = r < nr ? r : nr - 1;
             pk[r] = ld_stream16(pbase + rr * pstride + (size_t)g * 16);
             sf[r] = e8m0(__ldg(sbase + (size_t)rr * ngrp + g));
         }
+    };
+    // the first group's weights are fetched before waiting for the previous kernel (which
+    // produced x, never the weights)
+    if (g0 + lane < g1) load_w(g0 + lane);
+    pdl_wait();
+#pragma unroll 1
+    for (int g = g0 + lane; g < g1; g += 32) {
+        if (g != g0 + lane) load_w(g);
         float gs[R][NT];
 #pragma unroll
         for (int r = 0; r < R; r++)
@@ -232,8 +240,9 @@ extern "C" int k3cuda_matmul_mxfp4_workspace(int T, int in, int rows, int group,
 template <int NT> constexpr int fp4_rows() { return NT <= 2 ? 8 : 4; }
 
 template <int NT>
-static void launch_fp4(const Fp4Args &a, int blocks, cudaStream_t st) {
-    mxfp4_rows<NT, fp4_rows<NT>()><<<blocks, FP4_THREADS, 0, st>>>(a);
+static int launch_fp4(k3cuda_ctx *ctx, const Fp4Args &a, int blocks) {
+    return launch_pdl(ctx, ctx->stream, "mxfp4_rows", mxfp4_rows<NT, fp4_rows<NT>()>,
+                      dim3(blocks), dim3(FP4_THREADS), 0, a);
 }
 
 // The streaming kernel over n matrices of one shape (T <= 4, group 32, in % 32 == 0).
@@ -265,12 +274,11 @@ static int stream_fp4(k3cuda_ctx *ctx, const unsigned char *const *packed,
     const long long blocks = (long long)n * a.blocks_per_seg;
     if (blocks > 0x7fffffffLL) return set_error(K3CUDA_ERR_ARG, "matmul_mxfp4: grid too large");
     switch (T) {
-        case 1: launch_fp4<1>(a, (int)blocks, ctx->stream); break;
-        case 2: launch_fp4<2>(a, (int)blocks, ctx->stream); break;
-        case 3: launch_fp4<3>(a, (int)blocks, ctx->stream); break;
-        default: launch_fp4<4>(a, (int)blocks, ctx->stream); break;
+        case 1: return launch_fp4<1>(ctx, a, (int)blocks);
+        case 2: return launch_fp4<2>(ctx, a, (int)blocks);
+        case 3: return launch_fp4<3>(ctx, a, (int)blocks);
+        default: return launch_fp4<4>(ctx, a, (int)blocks);
     }
-    return after_launch(ctx, "mxfp4_rows");
 }
 
 extern "C" int k3cuda_matmul_mxfp4(k3cuda_ctx *ctx, float *y, const float *x,
