@@ -327,8 +327,9 @@ def bench_decode(args, D: Dist):
                    "l2": "inputs larger than L2 (537 MB fp32 state per GPU)"},
         "e2e": {"value": toks / (ms_e2e / 1e3), "unit": "tokens/s", "h2d_bytes_per_step": bi,
                 "d2h_bytes_per_step": bo,
-                "path": "k3cuda_kda_decode_host: page-locked host tensors, copies pipelined "
-                        "against the kernel over batch slices"},
+                "path": "k3cuda_kda_decode_host: page-locked host tensors, input copies "
+                        "pipelined against the kernel over batch slices, output written to the "
+                        "host by the kernel"},
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s",
                      "frac": achieved / hbm, "peak_source": src,
                      "traffic": profile_traffic("kda_decode_config1.md"),

@@ -111,7 +111,8 @@ int k3cuda_kda_decode(k3cuda_ctx *ctx, float *state, void *o, const void *q,
  *       six buffers are page-locked, else copies in one slice, or two from 4 MB up.
  *   1..K3CUDA_HOST_SLICES: copies through `staging`, the streams cut into that many batch
  *       slices; slice s's inputs come in on one copy stream while the kernel runs on slice
- *       s-1 and slice s-2's output goes back on another. Pageable memory works here but
+ *       s-1 and slice s-2's output goes back on another (a page-locked o is instead written
+ *       by the kernels in place, with no copy back). Pageable memory works here but
  *       serialises the copies.
  * staging: a device buffer of k3cuda_kda_decode_host_workspace() bytes, 256-byte aligned
  * (may be NULL in place). Asynchronous like every entry point: o is complete when the

@@ -296,6 +296,17 @@ extern "C" int k3cuda_kda_decode_host(k3cuda_ctx *ctx, float *state, void *o, co
     const uint8_t *hq = (const uint8_t *)q, *hk = (const uint8_t *)k, *hv = (const uint8_t *)v;
     const uint8_t *hg = (const uint8_t *)gate, *hb = (const uint8_t *)beta;
     uint8_t *ho = (uint8_t *)o;
+    // A page-locked output is written by the kernels in place: the GPU's writes to host memory
+    // are posted and overlap the step, and the device-to-host copies disappear.
+    uint8_t *od = nullptr;
+    {
+        cudaPointerAttributes a;
+        const cudaError_t pe = cudaPointerGetAttributes(&a, o);
+        if (pe != cudaSuccess)
+            cudaGetLastError();  // not a CUDA-known pointer: pageable memory
+        else if (a.type == cudaMemoryTypeHost)
+            od = (uint8_t *)a.devicePointer;
+    }
 
     K3_CUDA_TRY(cudaEventRecord(ctx->ev_cp_start, ctx->stream));
     K3_CUDA_TRY(cudaStreamWaitEvent(ctx->cp_in, ctx->ev_cp_start, 0));
@@ -318,11 +329,13 @@ extern "C" int k3cuda_kda_decode_host(k3cuda_ctx *ctx, float *state, void *o, co
         if (e == cudaSuccess) e = cudaEventRecord(ctx->ev_in[s], ctx->cp_in);
         if (e == cudaSuccess) e = cudaStreamWaitEvent(ctx->stream, ctx->ev_in[s], 0);
         if (e != cudaSuccess) break;
-        rc = k3cuda_kda_decode(ctx, state + (size_t)r0 * dk * dv, st + L.o + vo, st + L.q + qo,
-                               st + L.k + qo, st + L.v + vo, (const float *)(st + L.g + go),
+        rc = k3cuda_kda_decode(ctx, state + (size_t)r0 * dk * dv, od ? od + vo : st + L.o + vo,
+                               st + L.q + qo, st + L.k + qo, st + L.v + vo,
+                               (const float *)(st + L.g + go),
                                (const float *)(st + L.b + r0 * 4), (int)(b1 - b0), H, dk, dv,
                                q_scale, io_dtype, gate_mode);
         if (rc) break;
+        if (od) continue;  // the output went straight to the host
         e = cudaEventRecord(ctx->ev_k[s], ctx->stream);
         if (e == cudaSuccess) e = cudaStreamWaitEvent(ctx->cp_out, ctx->ev_k[s], 0);
         if (e == cudaSuccess)
