@@ -10,6 +10,10 @@
  * allocation on the context's device. All work is issued on the context's stream and is
  * asynchronous unless stated; k3cuda_sync waits for it.
  *
+ * A context belongs to one host thread at a time: its stream, side streams, events and
+ * staging ring are not locked. Threads that drive the GPU concurrently each create their
+ * own context (the process-wide caches of tensor maps and kernel attributes are locked).
+ *
  * Layouts follow the reference (include/k3/k3.h:157-165, src/core/k3_ops.c:864-938):
  *   per-token tensors      [tokens][heads][dim]       (the reference's [T][H*D])
  *   KDA recurrent state    [streams][heads][d_k][d_v] fp32, row = key channel
