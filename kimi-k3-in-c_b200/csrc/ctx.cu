@@ -127,7 +127,7 @@ int k3cuda_init(int device, k3cuda_ctx **out) {
     if (e == cudaSuccess) e = cudaMalloc((void **)&c->err_word, 256);
     if (e == cudaSuccess) e = cudaMemset(c->err_word, 0, 256);
     if (e != cudaSuccess) {
-        free(c);
+        k3cuda_shutdown(c);  // releases whatever was created (every member starts out null)
         return set_error(K3CUDA_ERR_CUDA, "context creation failed: %s", cudaGetErrorString(e));
     }
     *out = c;
@@ -141,7 +141,7 @@ void k3cuda_blas_destroy_internal(k3cuda_ctx *ctx);  // kda_layer.cu
 int k3cuda_shutdown(k3cuda_ctx *ctx) {
     if (!ctx) return K3CUDA_OK;
     cudaSetDevice(ctx->device);
-    cudaStreamSynchronize(ctx->stream);
+    if (ctx->stream) cudaStreamSynchronize(ctx->stream);
     k3cuda_comm_destroy_internal(ctx);
     k3cuda_blas_destroy_internal(ctx);
     for (int i = 0; i < K3CUDA_MAX_EVENTS; i++)
@@ -167,7 +167,7 @@ int k3cuda_shutdown(k3cuda_ctx *ctx) {
         if (ctx->ev_in[i]) cudaEventDestroy(ctx->ev_in[i]);
         if (ctx->ev_k[i]) cudaEventDestroy(ctx->ev_k[i]);
     }
-    cudaStreamDestroy(ctx->stream);
+    if (ctx->stream) cudaStreamDestroy(ctx->stream);
     free(ctx);
     return K3CUDA_OK;
 }
