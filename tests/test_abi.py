@@ -141,3 +141,38 @@ def test_bench_unit_counts():
     assert b.mla_layer_bytes(1, 8192) == 473_882_624
     assert b.moe_expert_bytes() == 281_608_192
     assert b.mla_prefill_flops(4096, 128) == 2_474_471_587_840
+
+
+def _mla_plan_segments(lens, H=128):
+    """Segments of the MLA attention work plan, recovered from the workspace query (host-only):
+    the partial buffer holds one [H][516] fp32 block per segment."""
+    L = k3cuda.lib()
+    arr = np.ascontiguousarray(lens, np.int32)
+    n = C.c_size_t()
+    k3cuda.check(L.k3cuda_mla_decode_workspace(arr.ctypes.data_as(C.POINTER(C.c_int)), len(arr),
+                                               H, 512, 128, C.byref(n)))
+    B = len(arr)
+    a = lambda x: (x + 255) // 256 * 256  # noqa: E731
+    nt = int(sum((int(v) + 63) // 64 for v in arr))
+    ncl = max(1, min(74, (nt + 3) // 4))
+    fixed = a((ncl + 1) * 4) + a((B + 1) * 4) + 2 * a(B * 4) + a(B * 128 * 576 * 2) + \
+        a(B * H * 2 * 512 * 2)
+    rest = n.value - fixed
+    per = H * 516 * 4
+    for nseg in range(max(0, rest // (per + 16) - 2), rest // per + 2):
+        if a(nseg * 16) + a(nseg * per) == rest:
+            return nseg, ncl
+    raise AssertionError(f"workspace {n.value} does not decompose")
+
+
+def test_mla_work_plan_segments():
+    """The attention work plan cuts the (query, tile) list into one contiguous run per cluster:
+    every query gets at least one segment and a cluster boundary splits at most one query, so
+    B <= segments <= B + clusters - 1 -- for a causal prefill (4096 queries of 1..4096
+    positions, where the plan weighs each segment as extra tiles), for config 4 and for one
+    long query (spread over 32 clusters by equal tile counts)."""
+    for lens in (np.arange(1, 4097), np.full(64, 8192), np.array([8192])):
+        nseg, ncl = _mla_plan_segments(lens)
+        assert len(lens) <= nseg <= len(lens) + ncl - 1, (len(lens), nseg, ncl)
+    nseg, ncl = _mla_plan_segments(np.array([8192]))
+    assert ncl == 32 and nseg == 32
