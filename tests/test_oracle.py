@@ -158,6 +158,24 @@ def test_chunked_restatement_matches_recurrence(golden):
                        np.sum(d["q"][:64, h].astype(np.float64) * qs * d["k"][:64, h], axis=1))
 
 
+@pytest.mark.parametrize("d,decay", [(64, 1.0), (128, 1.0), (128, 6.0)])
+def test_chunked_restatement_on_random_heads(d, decay):
+    """The chunk algebra against the token recurrence on seeded random heads: both head widths
+    the prefill kernels build, five chunks, and a decay strong enough (up to ~e^-6 per token)
+    that the within-chunk factors span many orders of magnitude."""
+    rng = np.random.default_rng(31 + d + int(decay))
+    T = 5 * 64
+    t = W.kda_tokens(rng, T, 1, d, d, bf16=False)
+    g = (t["g"] * np.float32(decay)).astype(np.float32)
+    qs = 1.0 / np.sqrt(np.float32(d))
+    oc, Sc, _, _ = oracle.kda_chunked_f64(t["q"][:, 0], t["k"][:, 0], t["v"][:, 0], g[:, 0],
+                                          t["beta"][:, 0], 64, qs)
+    o1, S1 = oracle.kda_recurrence(t["q"], t["k"], t["v"], g, t["beta"],
+                                   np.array([0, T], np.int32))
+    assert W.rel_fro(oc, o1[:, 0]) < 1e-5
+    assert W.rel_fro(Sc, S1[0, 0]) < 1e-5
+
+
 def test_varlen_streams_are_independent():
     rng = np.random.default_rng(5)
     t = W.kda_tokens(rng, 50, 2, 16, 16, bf16=False)
