@@ -107,19 +107,6 @@ def peaks():
         return 6650.0, 1590.0, "fallback"
 
 
-def profile_traffic(name):
-    """dram bytes per launch recorded from an ncu capture in profiles/<name> (or None)."""
-    path = os.path.join(ROOT, "profiles", name)
-    try:
-        with open(path) as f:
-            for line in f:
-                if line.strip().startswith("traffic_bytes_per_launch:"):
-                    return float(line.split(":", 1)[1].split()[0])
-    except OSError:
-        pass
-    return None
-
-
 # ------------------------------------------------------------------------ clocks
 class ClockSampler:
     """nvidia-smi samples of SM clock and throttle reasons during the timed region."""
@@ -206,6 +193,13 @@ class Dist:
         self.dist.all_reduce(t, op=self.dist.ReduceOp.MAX)
         return float(t.item())
 
+    def allgather_obj(self, x):
+        if self.world == 1:
+            return [x]
+        out = [None] * self.world
+        self.dist.all_gather_object(out, x)
+        return out
+
     def bcast_bytes(self, b: bytes | None) -> bytes:
         if self.world == 1:
             return b
@@ -245,6 +239,14 @@ def cpu_decode_baseline(B, H, d, budget_s=6.0):
 
 
 # ----------------------------------------------------------------------- decode
+def decode_config(B, H, d):
+    """The config-1 workload description, identical in both arms."""
+    return {"workload": "kda_decode_config1", "batch_per_gpu": B, "heads": H, "d_k": d,
+            "d_v": d, "io": "bf16 q/k/v/o, fp32 g/beta/state",
+            "parallelism": "sequence-shard (no collective)",
+            "l2": "inputs larger than L2 (537 MB fp32 state per GPU)"}
+
+
 def bench_decode(args, D: Dist):
     import k3cuda
     ctx = k3cuda.Context(D.local)
@@ -319,12 +321,9 @@ def bench_decode(args, D: Dist):
         "metric": "KDA recurrent decode tokens/s (BASELINE config 1: B=256, H=32, d=128)",
         "value": toks / (ms_max / 1e3), "unit": "tokens/s", "n_gpus": D.world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_max / args.steps,
-        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "fp32",
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "mixed",
         "data": "synthetic (seeded numpy: BASELINE config-1 distributions)",
-        "config": {"workload": "kda_decode_config1", "batch_per_gpu": B, "heads": H,
-                   "d_k": d, "d_v": d, "io": "bf16 q/k/v/o, fp32 g/beta/state",
-                   "parallelism": f"seq-shard x{D.world} (no collective)",
-                   "l2": "inputs larger than L2 (537 MB fp32 state per GPU)"},
+        "config": decode_config(B, H, d),
         "e2e": {"value": toks / (ms_e2e / 1e3), "unit": "tokens/s", "h2d_bytes_per_step": bi,
                 "d2h_bytes_per_step": bo,
                 "path": "k3cuda_kda_decode_host: page-locked host tensors, input copies "
@@ -332,7 +331,7 @@ def bench_decode(args, D: Dist):
                         "host by the kernel"},
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s",
                      "frac": achieved / hbm, "peak_source": src,
-                     "traffic": profile_traffic("kda_decode_config1.md"),
+                     "traffic": None,
                      "algorithmic_bytes_per_launch": alg},
         "gpu_launches": int(l1 - l0),
         "clocks": clocks,
@@ -341,50 +340,11 @@ def bench_decode(args, D: Dist):
     return line
 
 
-# ---------------------------------------------------------------------- prefill
-def bench_prefill(args, D: Dist, varlen: bool):
-    import k3cuda
-    ctx = k3cuda.Context(D.local)
-    if varlen:
-        c = W.kda_config3()
-        H_total, d = 64, 128
-    else:
-        c = W.kda_config2(T=args.tokens) if args.tokens else W.kda_config2()
-        H_total, d = 32, 128
-    cu = c["cu_seqlens"]
-    T = int(cu[-1])
-    import sharding
-    R = D.world if varlen else 1
-    hs = sharding.head_shard(H_total, R, D.rank if varlen else 0)
-    Hl = hs.stop - hs.start
-    bf = W.f32_to_bf16
-    q, k, v = (np.ascontiguousarray(c[x][:, hs]) for x in ("q", "k", "v"))
-    g, beta = np.ascontiguousarray(c["g"][:, hs]), np.ascontiguousarray(c["beta"][:, hs])
-    dq, dk, dv = ctx.upload(bf(q)), ctx.upload(bf(k)), ctx.upload(bf(v))
-    dg, db = ctx.upload(g), ctx.upload(beta)
-    nseq = len(cu) - 1
-    dS = ctx.empty((nseq, Hl, d, d), np.float32)
-    do = ctx.empty((T, Hl, d), np.uint16)
-    nws = ctx.kda_prefill_workspace(cu, Hl, d, d)
-    ws = ctx.empty((nws,), np.uint8)
-    qs = 1.0 / np.sqrt(np.float32(d))
-    gather = varlen and R > 1
-    if gather:
-        # the prefill writes every rank's full [T][H][d] output directly (peer memory over
-        # NVLink): no separate all-gather or interleave pass
-        uid = D.bcast_bytes(k3cuda.comm_unique_id() if D.rank == 0 else None)
-        ctx.comm_init(R, D.rank, uid)
-        dfull = ctx.empty((T, H_total, d), np.uint16)
-        ctx.comm_register_full(dfull)
-
-    def step():
-        dS.zero()
-        if gather:
-            ctx.kda_prefill_gathered(dS, dq, dk, dv, dg, db, cu, Hl, d, d, qs, ws, nws)
-        else:
-            ctx.kda_prefill(dS, do, dq, dk, dv, dg, db, cu, Hl, d, d, qs, ws, nws)
-
-    for _ in range(args.warmup):
+# ------------------------------------------------------------------ timing helpers
+def timed(ctx, D: Dist, step, steps, warmup, slots=(0, 1)):
+    """W untimed steps, then K steps between CUDA events on the context's stream, bracketed by
+    barrier + synchronize; returns (max-over-ranks ms, kernels launched, clocks)."""
+    for _ in range(warmup):
         step()
     ctx.sync()
     clk = ClockSampler(D.local)
@@ -394,48 +354,232 @@ def bench_prefill(args, D: Dist, varlen: bool):
     ctx.sync()
     l0 = ctx.launches()
     t0 = clk.mark()
-    ctx.record(0)
-    for _ in range(args.steps):
+    ctx.record(slots[0])
+    for _ in range(steps):
         step()
-    ctx.record(1)
+    ctx.record(slots[1])
     ctx.sync()
     t1 = clk.mark()
     D.barrier()
-    ms_max = D.max(ctx.elapsed_ms(0, 1))
-    clocks = clk.stop(t0, t1)
+    l1 = ctx.launches()
+    ms = D.max(ctx.elapsed_ms(*slots))
+    return ms, int(l1 - l0), clk.stop(t0, t1)
+
+
+def timed_e2e(ctx, D: Dist, step, steps, warmup):
+    """Same bracket without the clock sampler, for the host-buffer (end-to-end) leg."""
+    for _ in range(max(1, warmup)):
+        step()
+    ctx.sync()
+    D.barrier()
+    ctx.record(2)
+    for _ in range(steps):
+        step()
+    ctx.record(3)
+    ctx.sync()
+    D.barrier()
+    return D.max(ctx.elapsed_ms(2, 3))
+
+
+# ---------------------------------------------------------------------- prefill
+PREFILL = {"cfg2": dict(H=32, name="kda_prefill_config2"),
+           "cfg3": dict(H=64, name="kda_prefill_config3")}
+
+
+def prefill_inputs(which, heads=None, tokens=None):
+    if which == "cfg2":
+        return W.kda_config2(T=tokens, heads=heads) if tokens else W.kda_config2(heads=heads)
+    return W.kda_config3(heads=heads)
+
+
+def prefill_sample(which, n=1024):
+    """The first n tokens of config 2 or 3 at all heads, for the CPU baseline's sample (the
+    reference's time per token and head does not depend on the values)."""
+    H = PREFILL[which]["H"]
+    t = W.kda_tokens_by_head(0 if which == "cfg2" else 1, n, H, 128, 128, True)
+    t["cu_seqlens"] = np.array([0, n], np.int32)
+    return t
+
+
+def cpu_prefill_baseline(c, H, budget_s=5.0, tokens=1024):
+    """The reference's own k3_kda_step (oracle/_ref) driven as its k3_kda_layer recurrence
+    (k3_ops.c:908-938) over the first `tokens` tokens of the packed batch, all H heads,
+    OpenMP over heads on every host core, repeated for about budget_s seconds."""
+    from oracle import oracle
+    if not oracle.ref_available():
+        return None
+    nth = oracle.ref().k3ref_max_threads()
+    n = min(tokens, int(c["cu_seqlens"][-1]))
+    sub = {x: np.ascontiguousarray(c[x][:n]) for x in ("q", "k", "v", "g", "beta")}
+    cu = np.array([0, n], np.int32)
+    calls, t0 = 0, time.perf_counter()
+    while True:
+        oracle.kda_recurrence(sub["q"], sub["k"], sub["v"], sub["g"], sub["beta"], cu,
+                              use_ref=True, nthreads=nth)
+        calls += 1
+        el = time.perf_counter() - t0
+        if el >= budget_s:
+            break
+    return {"value": n * calls / el, "unit": "tokens/s", "cores": nth, "kind": "reference",
+            "sample": f"{calls} passes over the first {n} tokens x {H} heads (d=128) through "
+                      f"the reference k3_kda_step, OpenMP over heads"}
+
+
+def prefill_record(args, D: Dist, which, tokens=None, cpu=True):
+    """BASELINE config 2 or 3. One rank: the whole batch. N ranks: heads split evenly, each
+    rank's prefill writing its heads straight into every rank's full [T][H][d] output over
+    NVLink (k3cuda_kda_prefill_gathered); timed both with the exchange and compute-only."""
+    import k3cuda
+    import sharding
+    cfg = PREFILL[which]
+    H_total, d = cfg["H"], 128
+    R = D.world
+    hs = sharding.head_shard(H_total, R, D.rank)
+    Hl = hs.stop - hs.start
+    c = prefill_inputs(which, heads=hs, tokens=tokens)
+    cu = c["cu_seqlens"]
+    T, nseq = int(cu[-1]), len(cu) - 1
+    ctx = k3cuda.Context(D.local)
+    bf = W.f32_to_bf16
+    hq, hk, hv = (ctx.pinned((T, Hl, d), np.uint16) for _ in range(3))
+    hg = ctx.pinned((T, Hl, d), np.float32)
+    hb = ctx.pinned((T, Hl), np.float32)
+    hq[...], hk[...], hv[...], hg[...], hb[...] = bf(c["q"]), bf(c["k"]), bf(c["v"]), c["g"], c["beta"]
+    cpu_c = c if (cpu and R == 1 and D.rank == 0 and not args.no_cpu_baseline) else None
+    del c
+    dq, dk, dv = (ctx.empty((T, Hl, d), np.uint16) for _ in range(3))
+    dg, db = ctx.empty((T, Hl, d), np.float32), ctx.empty((T, Hl), np.float32)
+    h2d = [(dq, hq), (dk, hk), (dv, hv), (dg, hg), (db, hb)]
+    L = k3cuda.lib()
+    for dbuf, h in h2d:
+        k3cuda.check(L.k3cuda_memcpy_h2d(ctx.h, dbuf.ptr, h.ctypes.data, h.nbytes))
+    dS = ctx.empty((nseq, Hl, d, d), np.float32)
+    dloc = ctx.empty((T, Hl, d), np.uint16)
+    nws = ctx.kda_prefill_workspace(cu, Hl, d, d)
+    ws = ctx.empty((nws,), np.uint8)
+    qs = 1.0 / np.sqrt(np.float32(d))
+    gather = R > 1
+    if gather:
+        uid = D.bcast_bytes(k3cuda.comm_unique_id() if D.rank == 0 else None)
+        ctx.comm_init(R, D.rank, uid)
+        dfull = ctx.empty((T, H_total, d), np.uint16)
+        ctx.comm_register_full(dfull)
+
+    def step_local():
+        dS.zero()
+        ctx.kda_prefill(dS, dloc, dq, dk, dv, dg, db, cu, Hl, d, d, qs, ws, nws)
+
+    def step_gather():
+        dS.zero()
+        ctx.kda_prefill_gathered(dS, dq, dk, dv, dg, db, cu, Hl, d, d, qs, ws, nws)
+
+    step = step_gather if gather else step_local
+    ms, launches, clocks = timed(ctx, D, step, args.steps, args.warmup)
+    ms_compute = timed(ctx, D, step_local, args.steps, args.warmup)[0] if gather else ms
+
+    check = None
+    if gather:
+        # (1) this rank's heads in its gathered buffer equal an unsharded run of the same heads
+        # on this GPU; (2) every rank's gathered buffer holds the same bytes. Together: every
+        # rank holds every rank's heads, bit for bit as computed by their owners.
+        full = dfull.numpy()
+        step_local()
+        own = dloc.numpy()
+        ok_own = bool(np.array_equal(full[:, hs], own))
+        import hashlib
+        digest = hashlib.blake2b(full.tobytes(), digest_size=16).hexdigest()
+        digests = D.allgather_obj(digest)
+        ok_same = len(set(digests)) == 1
+        check = {"result": "pass" if (ok_own and ok_same) else "fail",
+                 "own_heads_equal_unsharded": ok_own, "all_ranks_same_output": ok_same,
+                 "what": "gathered [sum T, H, 128] output on every rank: its own heads vs an "
+                         "unsharded prefill of them, and a blake2b digest compared across "
+                         "ranks"}
+        del full
+
+    # e2e: this rank's inputs from page-locked host memory in, and the output back (with the
+    # exchange, each rank reads back its 1/R share of the gathered rows, all heads)
+    if gather:
+        r0, r1 = D.rank * T // R, (D.rank + 1) * T // R
+        row_bytes = H_total * d * 2
+        src_ptr, nb = dfull.ptr + r0 * row_bytes, (r1 - r0) * row_bytes
+    else:
+        src_ptr, nb = dloc.ptr, dloc.nbytes
+    ho = ctx.pinned((max(nb, 2) // 2,), np.uint16)
+
+    def e2e_step():
+        for dbuf, h in h2d:
+            k3cuda.check(L.k3cuda_memcpy_h2d(ctx.h, dbuf.ptr, h.ctypes.data, h.nbytes))
+        step()
+        k3cuda.check(L.k3cuda_memcpy_d2h(ctx.h, ho.ctypes.data, src_ptr, nb))
+
+    ms_e2e = timed_e2e(ctx, D, e2e_step, args.steps, args.warmup)
     hbm, tf, src = peaks()
+    per = ms_compute / 1e3 / args.steps
     alg = prefill_bytes(T, Hl, d)
-    per = ms_max / 1e3 / args.steps
-    name = "kda_prefill_config3" if varlen else "kda_prefill_config2"
-    if not varlen and args.tokens:
-        name = f"kda_prefill_T{T}_reduced"
-    line = {
-        "metric": f"KDA chunked prefill tokens/s ({name})", "value": T * args.steps / (ms_max / 1e3),
-        "unit": "tokens/s", "n_gpus": D.world, "steps": args.steps, "warmup": args.warmup,
-        "ms_per_step": ms_max / args.steps, "higher_is_better": True,
-        "scaling": "strong" if varlen else "weak", "vs_baseline": None, "dtype": "bf16",
-        "data": "synthetic (seeded numpy: BASELINE config distributions)",
-        "config": {"workload": name, "tokens": T, "heads_total": H_total, "heads_per_gpu": Hl,
-                   "d": d, "chunk": 64, "parallelism": f"head-shard x{R}" if varlen else "replica",
-                   "allgather": "fused into the prefill (peer stores)" if gather else False,
+    name = cfg["name"] if not tokens else f"kda_prefill_T{T}_reduced"
+    rec = {
+        "metric": f"KDA chunked prefill tokens/s ({name})",
+        "value": T * args.steps / (ms / 1e3), "unit": "tokens/s", "n_gpus": R,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms / args.steps,
+        "ms_per_step_compute_only": ms_compute / args.steps,
+        "value_compute_only": T * args.steps / (ms_compute / 1e3),
+        "higher_is_better": True, "scaling": "strong", "dtype": "mixed",
+        "config": {"workload": name, "tokens": T, "sequences": nseq, "heads_total": H_total,
+                   "heads_per_gpu": Hl, "d": d, "chunk": 64,
+                   "io": "bf16 q/k/v/o, fp32 g/beta/state",
+                   "parallelism": f"head-shard x{R}" + (", output exchange fused into the "
+                                                        "prefill (peer stores over NVLink)"
+                                                        if gather else ""),
                    "l2": "inputs larger than L2"},
+        "e2e": {"value": T * args.steps / (ms_e2e / 1e3), "unit": "tokens/s",
+                "h2d_bytes_per_step": int(sum(h.nbytes for _, h in h2d)),
+                "d2h_bytes_per_step": int(nb)},
         "roofline": {"bound": "hbm", "achieved": alg / per / 1e9, "peak": hbm, "unit": "GB/s",
-                     "frac": alg / per / 1e9 / hbm, "peak_source": src,
-                     "traffic": (profile_traffic("kda_prefill_config2.md")
-                                 if not varlen and not args.tokens else None),
-                     "algorithmic_bytes_per_launch": alg},
-        "gpu_launches": int(ctx.launches() - l0), "clocks": clocks,
+                     "frac": alg / per / 1e9 / hbm, "peak_source": src, "traffic": None,
+                     "algorithmic_bytes_per_launch": alg,
+                     "basis": "compute-only time of this rank's heads"},
+        "gpu_launches": launches, "clocks": clocks,
     }
+    if check:
+        rec["check"] = check
     ctx.close()
-    return line
+    if cpu_c is not None:
+        rec["cpu_baseline"] = cpu_prefill_baseline(cpu_c, H_total)
+    return rec
 
 
 # -------------------------------------------------------------------------- mla
-def bench_mla(args, D: Dist):
+def cpu_mla_baseline(c, budget_s=5.0, nb=2):
+    """The absorbed restatement of the reference's decode attention loop (k3_ops.c:381-411,
+    oracle/k3_oracle.c orc_mla_absorbed_decode: fp64 dots and sum, expf) over `nb` of the
+    config-4 sequences, all 128 heads, OpenMP over (sequence, head), for about budget_s s."""
+    from oracle import oracle
+    f = W.bf16_to_f32
+    args_ = [np.ascontiguousarray(f(c[x][:nb])) for x in ("q_nope", "q_rope", "latent", "rope")]
+    args_ += [f(c["w_uk"]), f(c["w_uv"])]
+    lens = np.ascontiguousarray(c["ctx_lens"][:nb])
+    nth = oracle.max_threads()
+    calls, t0 = 0, time.perf_counter()
+    while True:
+        oracle.mla_absorbed_decode(*args_, lens, c["scale"], nthreads=nth)
+        calls += 1
+        el = time.perf_counter() - t0
+        if el >= budget_s:
+            break
+    return {"value": nb * calls / el, "unit": "tokens/s", "cores": nth, "kind": "port",
+            "sample": f"{calls} passes over {nb} of the 64 sequences (8192 positions, 128 heads) "
+                      f"through the C restatement of the reference's attention loop"}
+
+
+def mla_record(args, D: Dist, cpu=True):
+    """64 sequences split evenly over the ranks (no collective)."""
     import k3cuda
-    ctx = k3cuda.Context(D.local)
-    B, ctxlen, H = 64, 8192, 128
+    R = D.world
+    B_all, ctxlen, H = 64, 8192, 128
+    B = B_all // R
     c = W.mla_config4(seed=D.rank, B=B, ctx=ctxlen, H=H)
+    ctx = k3cuda.Context(D.local)
     d = [ctx.upload(c[x]) for x in ("q_nope", "q_rope", "latent", "rope", "w_uk", "w_uv")]
     out = ctx.empty((B, H, 128), np.uint16)
     nws = ctx.mla_decode_workspace(c["ctx_lens"], H)
@@ -445,46 +589,56 @@ def bench_mla(args, D: Dist):
         ctx.mla_decode(out, *d, c["ctx_lens"], ctxlen, H, c["scale"], ws, nws,
                        out_dtype=k3cuda.BF16)
 
-    for _ in range(args.warmup):
+    ms, launches, clocks = timed(ctx, D, step, args.steps, args.warmup)
+    # e2e: the step's queries in from page-locked memory, the output back (the latent cache
+    # is resident device state, like the KDA recurrent state)
+    hqn, hqr = ctx.pinned(c["q_nope"].shape, np.uint16), ctx.pinned(c["q_rope"].shape, np.uint16)
+    hqn[...], hqr[...] = c["q_nope"], c["q_rope"]
+    ho = ctx.pinned((B, H, 128), np.uint16)
+    L = k3cuda.lib()
+
+    def e2e_step():
+        k3cuda.check(L.k3cuda_memcpy_h2d(ctx.h, d[0].ptr, hqn.ctypes.data, hqn.nbytes))
+        k3cuda.check(L.k3cuda_memcpy_h2d(ctx.h, d[1].ptr, hqr.ctypes.data, hqr.nbytes))
         step()
-    ctx.sync()
-    clk = ClockSampler(D.local)
-    clk.start()
-    time.sleep(0.3)
-    D.barrier()
-    ctx.sync()
-    l0 = ctx.launches()
-    t0 = clk.mark()
-    ctx.record(0)
-    for _ in range(args.steps):
-        step()
-    ctx.record(1)
-    ctx.sync()
-    t1 = clk.mark()
-    D.barrier()
-    ms_max = D.max(ctx.elapsed_ms(0, 1))
-    clocks = clk.stop(t0, t1)
+        k3cuda.check(L.k3cuda_memcpy_d2h(ctx.h, ho.ctypes.data, out.ptr, ho.nbytes))
+
+    ms_e2e = timed_e2e(ctx, D, e2e_step, args.steps, args.warmup)
     hbm, tf, src = peaks()
-    per = ms_max / 1e3 / args.steps
+    per = ms / 1e3 / args.steps
     alg = mla_bytes(B, ctxlen, H)
-    line = {
+    rec = {
         "metric": "MLA absorbed decode tokens/s (BASELINE config 4)",
-        "value": B * args.steps * D.world / (ms_max / 1e3), "unit": "tokens/s",
-        "n_gpus": D.world, "steps": args.steps, "warmup": args.warmup,
-        "ms_per_step": ms_max / args.steps, "higher_is_better": True, "scaling": "weak",
-        "vs_baseline": None, "dtype": "bf16",
-        "data": "synthetic (seeded numpy: BASELINE config-4 distributions)",
-        "config": {"workload": "mla_decode_config4", "batch_per_gpu": B, "ctx": ctxlen,
-                   "heads": H, "parallelism": f"batch-shard x{D.world}",
-                   "l2": "inputs larger than L2 (604 MB latent+rope cache)"},
+        "value": B_all * args.steps / (ms / 1e3), "unit": "tokens/s", "n_gpus": R,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms / args.steps,
+        "higher_is_better": True, "scaling": "strong", "dtype": "mixed",
+        "config": {"workload": "mla_decode_config4", "batch": B_all, "batch_per_gpu": B,
+                   "ctx": ctxlen, "heads": H, "io": "bf16 q/cache/W_UK/W_UV/out, fp32 softmax",
+                   "parallelism": f"batch-shard x{R} (no collective)",
+                   "l2": "inputs larger than L2 (latent+rope cache)"},
+        "e2e": {"value": B_all * args.steps / (ms_e2e / 1e3), "unit": "tokens/s",
+                "h2d_bytes_per_step": int(hqn.nbytes + hqr.nbytes),
+                "d2h_bytes_per_step": int(ho.nbytes)},
         "roofline": {"bound": "hbm", "achieved": alg / per / 1e9, "peak": hbm, "unit": "GB/s",
-                     "frac": alg / per / 1e9 / hbm, "peak_source": src, "traffic": profile_traffic("mla_attend_config4.md"),
+                     "frac": alg / per / 1e9 / hbm, "peak_source": src, "traffic": None,
                      "algorithmic_bytes_per_launch": alg,
                      "tensor_tflops": mla_flops(B, ctxlen, H) / per / 1e12},
-        "gpu_launches": int(ctx.launches() - l0), "clocks": clocks,
+        "gpu_launches": launches, "clocks": clocks,
     }
     ctx.close()
-    return line
+    if cpu and R == 1 and D.rank == 0 and not args.no_cpu_baseline:
+        rec["cpu_baseline"] = cpu_mla_baseline(c)
+    return rec
+
+
+def guarded(fn, *a, **kw):
+    """A sub-record that failed on this rank is reported, not raised: the headline line still
+    prints. (Every rank runs the same steps, so a failure in a collective ends on every rank
+    under the communicator's deadline.)"""
+    try:
+        return fn(*a, **kw)
+    except Exception as e:  # noqa: BLE001
+        return {"error": f"{type(e).__name__}: {e}"}
 
 
 # ------------------------------------------------------------------------ layer
@@ -975,20 +1129,16 @@ def bench_mla_prefill(args, D: Dist):
 
 
 # -------------------------------------------------------------- reference arm
-def bench_reference(args, D: Dist):
-    """The reference's own C (oracle/_ref/libk3ref.so, unmodified k3_ops.c) on the host
-    cores, same workload, metric and unit as our arm. Rank 0 only."""
+def ref_decode_step_sampler(args):
+    """The reference's k3_kda_step over config 1, each step a sample of the batch sized so
+    the whole run stays within a couple of minutes."""
     from oracle import oracle
-    if not oracle.ref_available():
-        return {"impl": "reference", "unavailable": "oracle/_ref/libk3ref.so was not built"}
     B, H, d = DECODE_B, DECODE_H, DECODE_D
     c = W.kda_config1(B=B, H=H, d=d)
     nth = oracle.ref().k3ref_max_threads()
     S = c["state"].copy()
-    # bound each step to a sample of the batch when a full step would make the run long
     t0 = time.perf_counter()
-    _, S1 = oracle.kda_decode(S, c["q"], c["k"], c["v"], c["g"], c["beta"], use_ref=True,
-                              nthreads=nth)
+    oracle.kda_decode(S, c["q"], c["k"], c["v"], c["g"], c["beta"], use_ref=True, nthreads=nth)
     full = time.perf_counter() - t0
     total = args.steps + args.warmup
     frac = min(1.0, 120.0 / max(full * total, 1e-9))
@@ -1003,21 +1153,67 @@ def bench_reference(args, D: Dist):
         _, Ss = oracle.kda_decode(Ss, sub["q"], sub["k"], sub["v"], sub["g"], sub["beta"],
                                   use_ref=True, nthreads=nth)
     el = time.perf_counter() - t0
-    value = nb * args.steps / el
-    return {
-        "impl": "reference",
-        "metric": "KDA recurrent decode tokens/s (BASELINE config 1: B=256, H=32, d=128)",
-        "value": value, "unit": "tokens/s", "n_gpus": D.world, "steps": args.steps,
-        "warmup": args.warmup, "ms_per_step": el * 1e3 / args.steps, "higher_is_better": True,
-        "scaling": "weak", "vs_baseline": None, "dtype": "fp32", "data": "synthetic",
-        "config": {"workload": "kda_decode_config1", "batch_per_gpu": B, "heads": H, "d_k": d,
-                   "d_v": d},
-        "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": nth, "kind": "reference",
-                         "sample": f"{nb} of {B} sequences x {H} heads per step through the "
-                                   f"reference k3_kda_step (OpenMP over streams)"},
-        "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0,
-                "d2h_bytes_per_step": 0},
-    }
+    return nb * args.steps / el, el, nth, (f"{nb} of {B} sequences x {H} heads per step "
+                                            f"through the reference k3_kda_step (OpenMP over "
+                                            f"streams)")
+
+
+def bench_reference(args, D: Dist):
+    """The reference's own C on the host cores (oracle/_ref/libk3ref.so, its unmodified
+    k3_ops.c; for config 4 the C restatement of its attention loop), for the same workload,
+    metric and unit as our arm. Rank 0 only."""
+    from oracle import oracle
+    if not oracle.ref_available():
+        return {"impl": "reference", "unavailable": "oracle/_ref/libk3ref.so was not built"}
+    wl = args.workload
+    base = {"impl": "reference", "n_gpus": D.world, "steps": args.steps, "warmup": args.warmup,
+            "higher_is_better": True, "vs_baseline": None, "dtype": "mixed",
+            "data": "synthetic", "unit": "tokens/s"}
+    if wl == "decode":
+        value, el, nth, sample = ref_decode_step_sampler(args)
+        line = dict(base, metric="KDA recurrent decode tokens/s (BASELINE config 1: B=256, "
+                                 "H=32, d=128)",
+                    value=value, ms_per_step=el * 1e3 / args.steps, scaling="weak",
+                    config=decode_config(DECODE_B, DECODE_H, DECODE_D))
+        cpu = {"value": value, "unit": "tokens/s", "cores": nth, "kind": "reference",
+               "sample": sample}
+        if not args.no_subrecords:
+            for key, which in (("prefill_cfg2", "cfg2"), ("varlen_cfg3", "cfg3")):
+                H = PREFILL[which]["H"]
+                cb = cpu_prefill_baseline(prefill_sample(which), H)
+                line[key] = {"metric": f"KDA chunked prefill tokens/s "
+                                       f"({PREFILL[which]['name']})",
+                             "value": cb["value"], "unit": "tokens/s", "cpu_baseline": cb}
+            cb = cpu_mla_baseline(W.mla_config4(B=2))
+            line["mla_cfg4"] = {"metric": "MLA absorbed decode tokens/s (BASELINE config 4)",
+                                "value": cb["value"], "unit": "tokens/s", "cpu_baseline": cb}
+    elif wl in ("prefill", "varlen"):
+        which = "cfg2" if wl == "prefill" else "cfg3"
+        H = PREFILL[which]["H"]
+        budget = 2.0 * max(1, args.steps) / 10
+        cpu = cpu_prefill_baseline(prefill_sample(which), H, budget_s=budget)
+        value = cpu["value"]
+        T = args.tokens or (32768 if which == "cfg2" else int(W.config3_cu_seqlens()[-1]))
+        line = dict(base, metric=f"KDA chunked prefill tokens/s ({PREFILL[which]['name']})",
+                    value=value, ms_per_step=T / value * 1e3, scaling="strong",
+                    config={"workload": PREFILL[which]["name"], "tokens": T, "heads_total": H,
+                            "d": 128, "chunk": 64})
+    elif wl == "mla":
+        c = W.mla_config4(B=2)
+        cpu = cpu_mla_baseline(c, budget_s=2.0 * max(1, args.steps) / 10)
+        value = cpu["value"]
+        line = dict(base, metric="MLA absorbed decode tokens/s (BASELINE config 4)",
+                    value=value, ms_per_step=64 / value * 1e3, scaling="strong",
+                    config={"workload": "mla_decode_config4", "batch": 64, "ctx": 8192,
+                            "heads": 128})
+    else:
+        return {"impl": "reference",
+                "unavailable": f"the reference arm covers decode, prefill, varlen and mla; "
+                               f"{wl} is timed beside our arm as its cpu_baseline"}
+    line["cpu_baseline"] = cpu
+    line["e2e"] = {"value": line["value"], "unit": "tokens/s", "h2d_bytes_per_step": 0,
+                   "d2h_bytes_per_step": 0}
+    return line
 
 
 def main():
@@ -1032,6 +1228,8 @@ def main():
                     help="mla_layer: positions already in the cache before the new tokens")
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-subrecords", action="store_true",
+                    help="decode: print the headline alone, without the config-2/3/4 records")
     ap.add_argument("--tokens", type=int, default=None,
                     help="prefill: sequence length in place of config 2's 32768 (a small case "
                          "for kernel profiling; not a headline number); layer: tokens per call")
@@ -1045,8 +1243,16 @@ def main():
         return
     if args.workload == "decode":
         line = bench_decode(args, D)
+        if not args.no_subrecords:
+            # the other BASELINE configurations, each a record of its own in the same line
+            line["prefill_cfg2"] = guarded(prefill_record, args, D, "cfg2")
+            line["varlen_cfg3"] = guarded(prefill_record, args, D, "cfg3")
+            line["mla_cfg4"] = guarded(mla_record, args, D)
     elif args.workload in ("prefill", "varlen"):
-        line = bench_prefill(args, D, varlen=args.workload == "varlen")
+        which = "cfg2" if args.workload == "prefill" else "cfg3"
+        line = prefill_record(args, D, which, tokens=args.tokens)
+        line["vs_baseline"] = None
+        line["data"] = "synthetic (seeded numpy: BASELINE config distributions)"
     elif args.workload == "layer":
         line = bench_layer(args, D)
     elif args.workload == "mla_prefill":
@@ -1056,7 +1262,9 @@ def main():
     elif args.workload == "mla_layer":
         line = bench_mla_layer(args, D)
     else:
-        line = bench_mla(args, D)
+        line = mla_record(args, D)
+        line["vs_baseline"] = None
+        line["data"] = "synthetic (seeded numpy: BASELINE config-4 distributions)"
     if D.rank == 0:
         if args.workload == "decode" and D.world == 1 and not args.no_cpu_baseline:
             line["cpu_baseline"] = cpu_decode_baseline(DECODE_B, DECODE_H, DECODE_D)

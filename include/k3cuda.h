@@ -56,8 +56,21 @@ int  k3cuda_shutdown(k3cuda_ctx *ctx);
 /* Message of the last failure on this thread ("" when none). Never NULL. */
 const char *k3cuda_last_error(void);
 int  k3cuda_device_count(int *count);
-/* Wait for all work issued on the context's stream. */
+/* Wait for all work issued on the context's stream. Returns K3CUDA_ERR_TIMEOUT when a
+ * kernel's bounded device-side wait gave up (the kernel skipped its work and returned; the
+ * context stays usable). With a communicator the wait runs under its deadline
+ * (k3cuda_comm_set_timeout) and ends the communicator on a peer's failure. */
 int  k3cuda_sync(k3cuda_ctx *ctx);
+/* Bound of every device-side wait (mbarrier, peer flag) in this context's kernels, in SM
+ * clock cycles; cycles <= 0 restores the default 2^31 (about a second at 1.9 GHz). A wait
+ * that runs out records its code in the context's error word, the kernel drains its own
+ * copies, frees its tensor memory and returns, and the next k3cuda_sync reports
+ * K3CUDA_ERR_TIMEOUT. Applies to kernels launched after the call. */
+int  k3cuda_set_wait_limit(k3cuda_ctx *ctx, long long cycles);
+/* Launch one kernel that waits on a barrier nothing completes, under the bound above: the
+ * timeout path (error word, K3CUDA_ERR_TIMEOUT from the next k3cuda_sync) exercised
+ * without a fault, a trap or an unbounded spin. Takes as long as the bound. */
+int  k3cuda_wait_selftest(k3cuda_ctx *ctx);
 /* The context's cudaStream_t, as an opaque pointer (for callers that order their own
  * work against this library's). */
 void *k3cuda_stream(k3cuda_ctx *ctx);
@@ -187,6 +200,13 @@ int k3cuda_kda_prefill_noalloc(k3cuda_ctx *ctx, float *state, void *o, const voi
  * comments at :83-90), any H <= 128. */
 int k3cuda_mla_decode_workspace(const int *ctx_lens, int B, int H, int dl, int dv,
                                 size_t *bytes);
+/* Host-only view of the attention work plan for B queries when the device offers
+ * max_clusters two-SM clusters (a B200 offers 74): the number of (query, context range)
+ * segments and of clusters it uses, and the workspace that exact plan needs at H = 128.
+ * k3cuda_mla_decode_workspace returns a size that covers the plan for every cluster count,
+ * so a buffer sized by it fits on any part. */
+int k3cuda_mla_plan_stats(const int *ctx_lens, int B, int max_clusters, int *segments,
+                          int *clusters, size_t *bytes);
 int k3cuda_mla_decode(k3cuda_ctx *ctx, void *out, int out_dtype, const void *q_nope,
                       const void *q_rope, const void *latent, const void *rope,
                       const void *w_uk, const void *w_uv, const int *ctx_lens, int B,
@@ -252,8 +272,15 @@ int k3cuda_mla_layer(k3cuda_ctx *ctx, float *out, const float *x, const k3cuda_m
  * (libnccl.so.2); without it these return K3CUDA_ERR_NCCL. */
 #define K3CUDA_UNIQUE_ID_BYTES 128
 int k3cuda_comm_unique_id(unsigned char id[K3CUDA_UNIQUE_ID_BYTES]);
+/* Collective. The communicator is non-blocking: every host wait on it (this call, the
+ * fences of the gathered prefill, k3cuda_sync) polls NCCL's asynchronous error under a
+ * deadline. A peer that leaves, stalls or fails ends the wait with ncclCommAbort and
+ * K3CUDA_ERR_TIMEOUT or K3CUDA_ERR_NCCL, instead of a hang; afterwards the context's
+ * single-GPU calls keep working and its collective calls return K3CUDA_ERR_STATE. */
 int k3cuda_comm_init(k3cuda_ctx *ctx, int nranks, int rank,
                      const unsigned char id[K3CUDA_UNIQUE_ID_BYTES]);
+/* Deadline of those waits in milliseconds (default 60000). */
+int k3cuda_comm_set_timeout(k3cuda_ctx *ctx, int ms);
 /* full d [T][nranks*H_local][dv] <- every rank's local d [T][H_local][dv] (rank r owns
  * heads r*H_local .. r*H_local+H_local-1). workspace d >= nranks*T*H_local*dv elements
  * of `dtype` (k3cuda_allgather_heads_workspace). */

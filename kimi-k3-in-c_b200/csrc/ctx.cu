@@ -7,8 +7,23 @@
 #include <mutex>
 
 #include "internal.cuh"
+#include "sm100.cuh"
 
 namespace k3 {
+
+// One CTA waits on a barrier that nothing arrives on, under the context's wait bound: the
+// timeout path of every pipelined kernel (error word set, the kernel returns) without a
+// fault, a trap or an unbounded spin.
+__global__ void wait_selftest(unsigned *err) {
+    using namespace sm100;
+    __shared__ __align__(8) uint64_t bar;
+    if (threadIdx.x == 0) {
+        mbar_init(&bar, 1);
+        fence_barrier_init();
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) mbar_wait(&bar, 0, err, 0x5E1Fu);
+}
 
 static thread_local char g_err[1024] = "";
 
@@ -126,6 +141,8 @@ int k3cuda_init(int device, k3cuda_ctx **out) {
     }
     if (e == cudaSuccess) e = cudaMalloc((void **)&c->err_word, 256);
     if (e == cudaSuccess) e = cudaMemset(c->err_word, 0, 256);
+    if (e == cudaSuccess) e = cudaEventCreateWithFlags(&c->ev_fence, cudaEventDisableTiming);
+    c->comm_timeout_ms = 60000;
     if (e != cudaSuccess) {
         k3cuda_shutdown(c);  // releases whatever was created (every member starts out null)
         return set_error(K3CUDA_ERR_CUDA, "context creation failed: %s", cudaGetErrorString(e));
@@ -153,6 +170,7 @@ int k3cuda_shutdown(k3cuda_ctx *ctx) {
             if (ctx->pin_ev[i]) cudaEventDestroy(ctx->pin_ev[i]);
         cudaFreeHost(ctx->pin);
     }
+    if (ctx->ev_fence) cudaEventDestroy(ctx->ev_fence);
     if (ctx->ev_fork) cudaEventDestroy(ctx->ev_fork);
     if (ctx->ev_join) cudaEventDestroy(ctx->ev_join);
     if (ctx->aux) cudaStreamDestroy(ctx->aux);
@@ -175,6 +193,11 @@ int k3cuda_shutdown(k3cuda_ctx *ctx) {
 int k3cuda_sync(k3cuda_ctx *ctx) {
     int rc = enter(ctx);
     if (rc) return rc;
+    if (ctx->nccl_comm) {
+        // the stream may hold collectives: wait under the communicator's deadline
+        rc = comm_wait_stream(ctx);
+        if (rc) return rc;
+    }
     K3_CUDA_TRY(cudaStreamSynchronize(ctx->stream));
     // a kernel whose bounded wait gave up leaves its code in the error word
     unsigned code = 0;
@@ -187,6 +210,25 @@ int k3cuda_sync(k3cuda_ctx *ctx) {
 }
 
 void *k3cuda_stream(k3cuda_ctx *ctx) { return ctx ? (void *)ctx->stream : nullptr; }
+
+int k3cuda_set_wait_limit(k3cuda_ctx *ctx, long long cycles) {
+    int rc = enter(ctx);
+    if (rc) return rc;
+    // byte 8 of the error block, read by every bounded wait (stream-ordered, so kernels
+    // already queued keep the bound they were launched under)
+    const long long v = cycles > 0 ? cycles : 0;
+    K3_CUDA_TRY(cudaMemcpyAsync((char *)ctx->err_word + 8, &v, sizeof v, cudaMemcpyHostToDevice,
+                                ctx->stream));
+    K3_CUDA_TRY(cudaStreamSynchronize(ctx->stream));
+    return K3CUDA_OK;
+}
+
+int k3cuda_wait_selftest(k3cuda_ctx *ctx) {
+    int rc = enter(ctx);
+    if (rc) return rc;
+    wait_selftest<<<1, 32, 0, ctx->stream>>>(ctx->err_word);
+    return after_launch(ctx, "wait_selftest");
+}
 
 int k3cuda_malloc(k3cuda_ctx *ctx, void **dptr, size_t bytes) {
     int rc = enter(ctx);

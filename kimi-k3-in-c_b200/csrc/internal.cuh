@@ -20,6 +20,9 @@ struct k3cuda_ctx {
     // NCCL (opaque; see comm.cu)
     void *nccl_comm;
     int nranks, rank;
+    int comm_timeout_ms;        // host deadline of every wait that involves the communicator
+    int comm_failed;            // the communicator was aborted (a peer left or timed out)
+    cudaEvent_t ev_fence;       // completion of the last cross-rank fence
     // every rank's registered [T][H][dv] output, mapped into this process (comm.cu)
     void *full_out[K3CUDA_MAX_RANKS];
     void *full_base[K3CUDA_MAX_RANKS];   // peer allocations opened by IPC (to close)
@@ -91,6 +94,12 @@ int set_smem(const void *func, int bytes);
 template <typename F> inline int set_smem(F *func, int bytes) {
     return set_smem(reinterpret_cast<const void *>(func), bytes);
 }
+
+// Multi-rank state (comm.cu). comm_wait_stream: wait for the context's stream under the
+// communicator's deadline, polling NCCL's asynchronous error; a deadline that passes or an
+// error aborts the communicator (K3CUDA_ERR_TIMEOUT / K3CUDA_ERR_NCCL). Returns K3CUDA_OK
+// at once when the context has no communicator.
+int comm_wait_stream(k3cuda_ctx *ctx);
 
 // Record an error message for the calling thread; returns `code`.
 int set_error(int code, const char *fmt, ...);

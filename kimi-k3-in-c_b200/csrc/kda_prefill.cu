@@ -411,7 +411,9 @@ extern "C" int k3cuda_kda_prefill(k3cuda_ctx *ctx, float *state, void *o, const 
 
 // ------------------------------------------------- head-sharded prefill, gathered output
 namespace k3 {
-int comm_fence(k3cuda_ctx *ctx);  // comm.cu: a one-int all-reduce ordering all ranks
+// comm.cu: a one-int all-reduce ordering all ranks (wait_host: the host also waits for it,
+// under the communicator's deadline)
+int comm_fence(k3cuda_ctx *ctx, bool wait_host);
 // comm.cu: copy this rank's heads of its full buffer into every peer's full buffer
 int comm_push_heads(k3cuda_ctx *ctx, int T, int head0, int H_local, int H_total, int dv);
 }
@@ -424,6 +426,8 @@ extern "C" int k3cuda_kda_prefill_gathered(k3cuda_ctx *ctx, float *state, const 
                                            size_t workspace_bytes) {
     int rc = enter(ctx);
     if (rc) return rc;
+    if (ctx->comm_failed)
+        return set_error(K3CUDA_ERR_STATE, "the communicator was aborted after a failure");
     if (!ctx->nccl_comm || !ctx->full_out[ctx->rank])
         return set_error(K3CUDA_ERR_STATE,
                          "kda_prefill_gathered: k3cuda_comm_init and k3cuda_comm_register_full "
@@ -453,8 +457,11 @@ extern "C" int k3cuda_kda_prefill_gathered(k3cuda_ctx *ctx, float *state, const 
     go.n = 1;
     go.head0 = ctx->rank * H_local;
     go.H_total = ctx->nranks * H_local;
-    // every rank is done with the previous contents of its buffer before anyone writes
-    rc = comm_fence(ctx);
+    // every rank is done with the previous contents of its buffer before anyone writes; the
+    // host sees this fence complete before it enqueues any peer store, so a peer that has
+    // gone (or stalled past the deadline) ends the call with an error, never with a store
+    // into a buffer whose owner has left
+    rc = comm_fence(ctx, true);
     if (rc) return rc;
     if (T > 0 && n_seq > 0) {
         long long nc = 0;
@@ -467,7 +474,7 @@ extern "C" int k3cuda_kda_prefill_gathered(k3cuda_ctx *ctx, float *state, const 
         if (rc) return rc;
     }
     // and every rank's writes into every buffer are complete before anyone reads one
-    return comm_fence(ctx);
+    return comm_fence(ctx, false);
 }
 
 // ------------------------------------------------------------- allocation-free variant

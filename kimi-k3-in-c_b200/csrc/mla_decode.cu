@@ -969,6 +969,17 @@ static size_t mla_ws_bytes(const MlaPlan &p, int B, int H) {
 
 constexpr int MLA_MAX_CLUSTERS = 74;  // 148 SMs of a B200, two per cluster
 
+// Workspace for B queries whatever cluster count the run plans with (it uses
+// min(MLA_MAX_CLUSTERS, SMs / 2)): clusters take contiguous ranges of the (query, tile) line,
+// so each cluster boundary splits at most one query and a plan has at most
+// B + clusters - 1 segments; mla_ws_bytes grows with the segment and cluster counts only.
+static size_t mla_ws_bound(int B, int H) {
+    MlaPlan p;
+    p.segs.resize((size_t)B + MLA_MAX_CLUSTERS - 1);
+    p.cl_begin.resize((size_t)MLA_MAX_CLUSTERS + 1);
+    return mla_ws_bytes(p, B, H);
+}
+
 }  // namespace k3
 
 using namespace k3;
@@ -980,9 +991,21 @@ extern "C" int k3cuda_mla_decode_workspace(const int *ctx_lens, int B, int H, in
         return set_error(K3CUDA_ERR_UNSUPPORTED, "mla_decode: dl=%d dv=%d not built", dl, dv);
     for (int b = 0; b < B; b++)
         K3_ARG_CHECK(ctx_lens[b] >= 1, "ctx_lens[%d]=%d must be >= 1", b, ctx_lens[b]);
+    *bytes = mla_ws_bound(B, H);
+    return K3CUDA_OK;
+}
+
+extern "C" int k3cuda_mla_plan_stats(const int *ctx_lens, int B, int max_clusters, int *segments,
+                                     int *clusters, size_t *bytes) {
+    K3_ARG_CHECK(ctx_lens && B >= 1 && max_clusters >= 1 && segments && clusters && bytes,
+                 "bad MLA plan query");
+    for (int b = 0; b < B; b++)
+        K3_ARG_CHECK(ctx_lens[b] >= 1, "ctx_lens[%d]=%d must be >= 1", b, ctx_lens[b]);
     MlaPlan p;
-    mla_plan(ctx_lens, B, MLA_MAX_CLUSTERS, p);
-    *bytes = mla_ws_bytes(p, B, H);
+    mla_plan(ctx_lens, B, std::min(MLA_MAX_CLUSTERS, max_clusters), p);
+    *segments = (int)p.segs.size();
+    *clusters = p.ncl;
+    *bytes = mla_ws_bytes(p, B, MLA_HP);
     return K3CUDA_OK;
 }
 
@@ -1167,11 +1190,8 @@ int mla_attend_kvb(k3cuda_ctx *ctx, float *acc, const void *q_nope, const void *
 }
 
 size_t mla_attend_kvb_workspace(int T, int cached, int H) {
-    std::vector<int> lens((size_t)T);
-    for (int t = 0; t < T; t++) lens[(size_t)t] = cached + t + 1;
-    MlaPlan p;
-    mla_plan(lens.data(), T, MLA_MAX_CLUSTERS, p);
-    return mla_ws_bytes(p, T, H);
+    (void)cached;
+    return mla_ws_bound(T, H);
 }
 }  // namespace k3
 

@@ -11,8 +11,9 @@
 //     address by 32 B; the next 64-element K block is a separate [rows x 128 B] region.
 //   * MN-major operand (M/N contiguous): an atom covers 64 M/N values x 8 K rows; atoms are
 //     stacked along K every 1024 B (SBO) and along M/N by LBO bytes.
-//   * Every wait is bounded: a wait that does not complete within ~2^31 SM cycles (about a
-//     second) records `code` in the kernel's error word and returns false, and the kernel
+//   * Every wait is bounded: a wait that does not complete within the context's bound
+//     (k3cuda_set_wait_limit; 2^31 SM cycles, about a second, by default) records `code` in
+//     the kernel's error word and returns false, and the kernel
 //     then skips the rest of its work, waits (bounded) for its own copies, frees TMEM and
 //     exits. No wait can hang the GPU.
 #pragma once
@@ -103,6 +104,14 @@ __device__ __forceinline__ bool mbar_try_wait_cluster(uint64_t *bar, uint32_t pa
 
 constexpr long long kWaitCycles = 1ll << 31;
 
+// The error block of a context (256 bytes of device memory): word 0 holds the code of the
+// first wait that gave up, the 64-bit value at byte 8 the bound of every wait in SM clock
+// cycles (k3cuda_set_wait_limit; kWaitCycles, about a second, when it is not positive).
+__device__ __forceinline__ long long wait_limit(const unsigned *err) {
+    const long long lim = *(const volatile long long *)(err + 2);
+    return lim > 0 ? lim : kWaitCycles;
+}
+
 // Bounded wait; on timeout records `code` in *err (first error wins) and returns false.
 // try_wait blocks in hardware for a while before returning false, so the loop spins slowly;
 // the error word (another role's timeout) and the clock are only checked every 64 tries,
@@ -112,11 +121,12 @@ __device__ __forceinline__ bool mbar_wait_impl(uint64_t *bar, uint32_t parity, u
                                                unsigned code) {
     if (kCluster ? mbar_try_wait_cluster(bar, parity) : mbar_try_wait(bar, parity)) return true;
     const long long t0 = clock64();
+    const long long lim = wait_limit(err);
     for (uint32_t i = 1;; i++) {
         if (kCluster ? mbar_try_wait_cluster(bar, parity) : mbar_try_wait(bar, parity)) return true;
         if ((i & 63) == 0) {
             if (*(volatile unsigned *)err) return false;
-            if (clock64() - t0 > kWaitCycles) {
+            if (clock64() - t0 > lim) {
                 atomicCAS(err, 0u, code);
                 return false;
             }

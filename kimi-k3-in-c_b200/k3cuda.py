@@ -22,6 +22,7 @@ OK, ERR_ARG, ERR_CUDA, ERR_UNSUPPORTED, ERR_WORKSPACE, ERR_NCCL, ERR_TIMEOUT, ER
 F32, BF16 = 0, 1
 GATE_LOG, GATE_ALPHA = 0, 1
 MAX_EVENTS = 64
+NOALLOC_SCRATCH_BYTES = 64 << 20   # K3CUDA_NOALLOC_SCRATCH_BYTES
 
 # Every symbol include/k3cuda.h declares, with (restype, argtypes).
 _vp, _i, _f, _sz = C.c_void_p, C.c_int, C.c_float, C.c_size_t
@@ -33,6 +34,8 @@ SIGNATURES = {
     "k3cuda_device_count": (_i, [_ip]),
     "k3cuda_sync": (_i, [_vp]),
     "k3cuda_stream": (_vp, [_vp]),
+    "k3cuda_set_wait_limit": (_i, [_vp, C.c_longlong]),
+    "k3cuda_wait_selftest": (_i, [_vp]),
     "k3cuda_malloc": (_i, [_vp, C.POINTER(_vp), _sz]),
     "k3cuda_free": (_i, [_vp, _vp]),
     "k3cuda_host_alloc": (_i, [_vp, C.POINTER(_vp), _sz]),
@@ -56,6 +59,7 @@ SIGNATURES = {
     "k3cuda_kda_prefill_noalloc": (_i, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _ip, _i, _i, _i,
                                         _i, _f, _i, _i, _i]),
     "k3cuda_mla_decode_workspace": (_i, [_ip, _i, _i, _i, _i, C.POINTER(_sz)]),
+    "k3cuda_mla_plan_stats": (_i, [_ip, _i, _i, _ip, _ip, C.POINTER(_sz)]),
     "k3cuda_mla_decode": (_i, [_vp, _vp, _i, _vp, _vp, _vp, _vp, _vp, _vp, _ip, _i, _i, _i, _i,
                                _i, _i, _i, _f, _vp, _sz]),
     "k3cuda_mla_attend": (_i, [_vp, _vp, _i, _vp, _vp, _vp, _vp, _vp, _vp, _ip, _ip, _i, _i, _i,
@@ -66,6 +70,7 @@ SIGNATURES = {
                               _i, _i, _vp, _sz]),
     "k3cuda_comm_unique_id": (_i, [C.c_char_p]),
     "k3cuda_comm_init": (_i, [_vp, _i, _i, C.c_char_p]),
+    "k3cuda_comm_set_timeout": (_i, [_vp, _i]),
     "k3cuda_allgather_heads_workspace": (_i, [_i, _i, _i, _i, _i, C.POINTER(_sz)]),
     "k3cuda_allgather_heads": (_i, [_vp, _vp, _vp, _i, _i, _i, _i, _vp, _sz]),
     "k3cuda_comm_register_full": (_i, [_vp, _vp, _sz]),
@@ -377,6 +382,15 @@ class Context:
                                      _ptr(workspace), int(workspace_bytes)))
 
     # multi-GPU -------------------------------------------------------------------
+    def set_wait_limit(self, cycles: int):
+        check(lib().k3cuda_set_wait_limit(self.h, int(cycles)))
+
+    def wait_selftest(self):
+        check(lib().k3cuda_wait_selftest(self.h))
+
+    def comm_set_timeout(self, ms: int):
+        check(lib().k3cuda_comm_set_timeout(self.h, int(ms)))
+
     def comm_init(self, nranks: int, rank: int, uid: bytes):
         check(lib().k3cuda_comm_init(self.h, int(nranks), int(rank), uid))
 
@@ -467,3 +481,7 @@ class DeviceBuffer:
 
     def zero(self):
         check(lib().k3cuda_memset(self.ctx.h, self.ptr, 0, self.nbytes))
+
+    def fill(self, byte: int):
+        """Set every byte to `byte` (asynchronous, on the context's stream)."""
+        check(lib().k3cuda_memset(self.ctx.h, self.ptr, int(byte), self.nbytes))

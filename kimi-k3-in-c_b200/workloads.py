@@ -80,10 +80,21 @@ def kda_config1(seed: int = 0, B: int = 256, H: int = 32, d: int = 128):
     return t
 
 
-def kda_config2(seed: int = 0, T: int = 32768, H: int = 32, d: int = 128):
-    """Config 2: one long sequence, bf16 q,k,v."""
-    rng = np.random.default_rng(seed)
-    t = kda_tokens(rng, T, H, d, d, bf16=True)
+def kda_tokens_by_head(seed: int, T: int, H: int, dk: int, dv: int, bf16: bool,
+                       heads: slice | None = None):
+    """kda_tokens with one generator per head (seeded [seed, h]), so that any slice of
+    heads -- a rank's head shard -- is drawn on its own and equals the same columns of the
+    whole draw. Returns q, k, v [T, Hs, d], g [T, Hs, dk], beta [T, Hs]."""
+    hs = range(H)[heads] if heads is not None else range(H)
+    parts = [kda_tokens(np.random.default_rng([seed, h]), T, 1, dk, dv, bf16) for h in hs]
+    return {x: np.ascontiguousarray(np.concatenate([p[x] for p in parts], axis=1))
+            for x in ("q", "k", "v", "g", "beta")}
+
+
+def kda_config2(seed: int = 0, T: int = 32768, H: int = 32, d: int = 128,
+                heads: slice | None = None):
+    """Config 2: one long sequence, bf16 q,k,v (`heads`: only that slice of the heads)."""
+    t = kda_tokens_by_head(seed, T, H, d, d, True, heads)
     t["cu_seqlens"] = np.array([0, T], np.int32)
     return t
 
@@ -93,14 +104,19 @@ def varlen_lengths(seed: int = 0, nseq: int = 16, lo: int = 512, hi: int = 8192)
     return rng.integers(lo, hi + 1, size=nseq).astype(np.int64)
 
 
-def kda_config3(seed: int = 0, nseq: int = 16, H: int = 64, d: int = 128, lo: int = 512,
-                hi: int = 8192):
-    """Config 3: packed variable-length batch, lengths ~ U[lo, hi] (seeded)."""
+def config3_cu_seqlens(seed: int = 0, nseq: int = 16, lo: int = 512, hi: int = 8192):
     lens = varlen_lengths(seed, nseq, lo, hi)
     cu = np.zeros(nseq + 1, np.int32)
     cu[1:] = np.cumsum(lens)
-    rng = np.random.default_rng(seed + 1)
-    t = kda_tokens(rng, int(cu[-1]), H, d, d, bf16=True)
+    return cu
+
+
+def kda_config3(seed: int = 0, nseq: int = 16, H: int = 64, d: int = 128, lo: int = 512,
+                hi: int = 8192, heads: slice | None = None):
+    """Config 3: packed variable-length batch, lengths ~ U[lo, hi] (seeded); `heads`: only
+    that slice of the heads."""
+    cu = config3_cu_seqlens(seed, nseq, lo, hi)
+    t = kda_tokens_by_head(seed + 1, int(cu[-1]), H, d, d, True, heads)
     t["cu_seqlens"] = cu
     return t
 

@@ -143,26 +143,24 @@ def test_bench_unit_counts():
     assert b.mla_prefill_flops(4096, 128) == 2_474_471_587_840
 
 
-def _mla_plan_segments(lens, H=128):
-    """Segments of the MLA attention work plan, recovered from the workspace query (host-only):
-    the partial buffer holds one [H][516] fp32 block per segment."""
+def _mla_plan(lens, max_clusters=74):
+    """(segments, clusters, exact workspace at H = 128) of the MLA attention work plan."""
+    L = k3cuda.lib()
+    arr = np.ascontiguousarray(lens, np.int32)
+    ns, nc, nb = C.c_int(), C.c_int(), C.c_size_t()
+    k3cuda.check(L.k3cuda_mla_plan_stats(arr.ctypes.data_as(C.POINTER(C.c_int)), len(arr),
+                                         int(max_clusters), C.byref(ns), C.byref(nc),
+                                         C.byref(nb)))
+    return ns.value, nc.value, nb.value
+
+
+def _mla_ws_query(lens, H=128):
     L = k3cuda.lib()
     arr = np.ascontiguousarray(lens, np.int32)
     n = C.c_size_t()
     k3cuda.check(L.k3cuda_mla_decode_workspace(arr.ctypes.data_as(C.POINTER(C.c_int)), len(arr),
                                                H, 512, 128, C.byref(n)))
-    B = len(arr)
-    a = lambda x: (x + 255) // 256 * 256  # noqa: E731
-    nt = int(sum((int(v) + 63) // 64 for v in arr))
-    ncl = max(1, min(74, (nt + 3) // 4))
-    fixed = a((ncl + 1) * 4) + a((B + 1) * 4) + 2 * a(B * 4) + a(B * 128 * 576 * 2) + \
-        a(B * H * 2 * 512 * 2)
-    rest = n.value - fixed
-    per = H * 516 * 4
-    for nseg in range(max(0, rest // (per + 16) - 2), rest // per + 2):
-        if a(nseg * 16) + a(nseg * per) == rest:
-            return nseg, ncl
-    raise AssertionError(f"workspace {n.value} does not decompose")
+    return n.value
 
 
 def test_mla_work_plan_segments():
@@ -170,9 +168,14 @@ def test_mla_work_plan_segments():
     every query gets at least one segment and a cluster boundary splits at most one query, so
     B <= segments <= B + clusters - 1 -- for a causal prefill (4096 queries of 1..4096
     positions, where the plan weighs each segment as extra tiles), for config 4 and for one
-    long query (spread over 32 clusters by equal tile counts)."""
-    for lens in (np.arange(1, 4097), np.full(64, 8192), np.array([8192])):
-        nseg, ncl = _mla_plan_segments(lens)
-        assert len(lens) <= nseg <= len(lens) + ncl - 1, (len(lens), nseg, ncl)
-    nseg, ncl = _mla_plan_segments(np.array([8192]))
+    long query (spread over 32 clusters by equal tile counts), on a full B200 and on parts
+    with fewer SMs. The workspace query covers the plan of every cluster count."""
+    for lens in (np.arange(1, 4097), np.full(64, 8192), np.array([8192]), np.array([1, 70, 3])):
+        q = _mla_ws_query(lens)
+        for mc in (74, 66, 37, 8, 1):
+            nseg, ncl, need = _mla_plan(lens, mc)
+            assert ncl <= mc
+            assert len(lens) <= nseg <= len(lens) + ncl - 1, (len(lens), nseg, ncl, mc)
+            assert need <= q, (len(lens), mc, need, q)
+    nseg, ncl, _ = _mla_plan(np.array([8192]))
     assert ncl == 32 and nseg == 32
