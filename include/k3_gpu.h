@@ -43,6 +43,26 @@ void k3g_mla_attend(float *acc, const float *q, const float *latent, const float
                     const float *kv_b, float scale, int H, int qn, int qr, int kv_lora,
                     int vh, int P);
 
+/* Model configuration, field for field K3Cfg (include/k3/k3.h:73-120): same order, same
+ * types, so a K3Cfg pointer can be passed by cast. The drop-ins read hidden and rms_eps, the
+ * KDA fields (kda_heads, kda_head_dim, conv_k, gate_lb) and the MLA fields (n_heads, q_lora,
+ * kv_lora, qk_nope, qk_rope, v_head). */
+typedef struct {
+    int   hidden, n_layers, vocab;
+    float rms_eps;
+    int   kda_heads, kda_head_dim, conv_k;
+    float gate_lb;
+    int   n_heads, q_lora, kv_lora, qk_nope, qk_rope, v_head, mla_out_gate;
+    int   n_experts, topk, n_shared, latent, moe_inter;
+    float routed_scale;
+    int   moe_renorm, latent_norm;
+    int   first_dense, dense_inter;
+    int   attn_res_block;
+    float situ_b1, situ_b2;
+    int   n_full_attn;
+    int  *full_attn;
+} k3g_cfg;
+
 /* Host weights of one KDA layer, field for field K3KdaW (include/k3/k3.h:449-463): same
  * order, same types, so a K3KdaW pointer can be passed by cast. wdt: 0 fp32, 1 bf16. */
 typedef struct {
@@ -58,16 +78,58 @@ typedef struct {
     int          wdt;
 } k3g_kda_weights;
 
-/* Replaces k3_kda_layer (src/core/k3_ops.c:864-951) for host buffers: out, x [T][E]; state
- * [H*D*D + 3*H*D*(K-1)] updated in place (NULL: fresh sequence, as the reference). E, H, D,
- * K, gate_lb and rms_eps are the K3Cfg fields hidden, kda_heads, kda_head_dim, conv_k,
- * gate_lb and rms_eps. The recurrence runs on fp32 operands. The layer's weights are copied
- * to the device on the first call that sees them (keyed by the address of w->q) and kept
- * until k3g_shutdown: the reference never changes a loaded layer's weights. A caller that
- * frees a layer and loads another (whose q may land at the same address) calls
- * k3g_shutdown in between. */
-void k3g_kda_layer(float *out, const float *x, const k3g_kda_weights *w, int T, int E, int H,
-                   int D, int K, float gate_lb, float rms_eps, float *state);
+/* Host weights of one MLA layer, field for field K3MlaW (include/k3/k3.h:203-210); g may be
+ * NULL (no output gate). */
+typedef struct {
+    const void  *q_a, *q_b;
+    const void  *kv_a, *kv_b;
+    const void  *o, *g;
+    const float *q_a_norm, *kv_a_norm;
+    int          wdt;
+} k3g_mla_weights;
+
+/* Replaces k3_kda_layer (include/k3/k3.h:468-469, src/core/k3_ops.c:864-951), same
+ * signature: out, x [T][hidden]; state [H*D*D + 3*H*D*(conv_k-1)] updated in place (NULL:
+ * a fresh sequence, nothing kept, as the reference). scratch is accepted and not touched
+ * (the device work uses device workspaces), so a buffer sized by k3_kda_scratch may be
+ * passed as before. The recurrence runs on fp32 operands. The layer's weights are copied to
+ * the device on the first call that sees them and reused while the same host arrays come
+ * back: the copy is keyed by the address of w->q, the layer geometry and wdt, and a
+ * fingerprint of sampled bytes of every weight array, so a layer freed and another loaded
+ * at the same address is noticed and copied again. */
+void k3g_kda_layer(float *out, const float *x, const k3g_kda_weights *w, const k3g_cfg *c,
+                   int T, float *state, float *scratch);
+
+/* Replaces k3_mla_cached (include/k3/k3.h:219-221, src/core/k3_ops.c:321-424), same
+ * signature and contract: T tokens at positions cached .. cached+T-1 of one sequence;
+ * kvc [cap][n_heads*(qk_nope+v_head)] and ropec [cap][qk_rope] carry the cache between calls
+ * (kvc == NULL: no cache, the T tokens attend among themselves, as k3_mla); a position at or
+ * past cap aborts with the reference's message (k3_ops.c:333-334). scratch is accepted and
+ * not touched.
+ * The cache lives on the device as the compressed latent: bf16 rows with the tensor-core
+ * attention at the released head geometry (qk_nope 128, qk_rope 64, kv_lora 512, v_head
+ * 128), fp32 rows with the fp32 CUDA-core attention for any other geometry (or everywhere
+ * with K3G_MLA_F32=1 in the environment). The host buffers stay the record of the cache, in
+ * the latent form: row p of kvc holds position p's normalised latent (its first kv_lora
+ * floats, exactly the device row widened to fp32; the rest of the row is not written), and
+ * row p of ropec its rope slot, as the reference stores it. So kvc must be at least kv_lora
+ * floats wide, and a cache written by these drop-ins is not the reference's expanded form
+ * (do not hand one to the CPU k3_mla_cached, or the reverse). The device copy is keyed by
+ * kvc: rows the device does not hold (a copied or reloaded buffer, a new kvc) are uploaded
+ * from the host rows before the call. The last row before `cached` is checked against what
+ * the device holds; a caller that rewrites earlier rows of the same buffer in place calls
+ * k3g_mla_cache_forget(kvc) first. */
+void k3g_mla_cached(float *out, const float *x, const k3g_mla_weights *w, const k3g_cfg *c,
+                    int T, float *scratch, float *kvc, float *ropec, int cached, int cap);
+/* Drop the device copy of the cache whose host rows are kvc (the next call re-uploads). */
+void k3g_mla_cache_forget(const float *kvc);
+
+/* Both layer drop-ins honour K3G_TOKENWISE=1 in the environment: a call of T > 1 tokens
+ * runs as T consecutive one-token calls. Results then do not depend on how a sequence is
+ * cut into calls -- the property the reference's prefix-reuse gate demands bit for bit
+ * (tests/unit/k3_model.c:431-441) -- at the cost of prefill speed (no chunked recurrence,
+ * no GEMM projections). By default a multi-token call runs the chunked prefill and GEMMs,
+ * equal to the token-by-token result within the stated tolerance, not bit for bit. */
 
 /* State file for device-resident state (--save-state / --load-state of the reference,
  * src/cli/k3_state.c:102-270). The header is the reference's K3StateHdr byte for byte

@@ -265,6 +265,22 @@ int k3cuda_mla_layer(k3cuda_ctx *ctx, float *out, const float *x, const k3cuda_m
                      float rms_eps, void *latent, void *rope, int cached, int cap,
                      void *workspace, size_t workspace_bytes);
 
+/* k3_mla_cached (src/core/k3_ops.c:321-424) for ANY head geometry -- the reference's own
+ * test models use qk_nope 24, qk_rope 8, kv_lora 32, v_head 16 -- with an fp32 cache:
+ * latent d [cap][dl] fp32 and rope d [cap][dr] fp32 (the layer writes the T new rows at
+ * cached.., then attends causally). The attention is the absorbed form on CUDA cores in
+ * fp32 (scores, softmax, accumulation), so results stay within fp32 rounding of the
+ * reference instead of a bf16 bound; k3cuda_mla_layer is the tensor-core path for the
+ * released geometry. Weights as k3cuda_mla_layer (fp32 or bf16 by wdt). Supported: E,
+ * q_lora and H*dv multiples of 8, dl <= 1024, dr <= 256, cached + T <= cap. workspace d:
+ * k3cuda_mla_layer_f32_workspace() bytes. */
+int k3cuda_mla_layer_f32_workspace(int T, int E, int H, int q_lora, int dn, int dr, int dl,
+                                   int dv, int wdt, size_t *bytes);
+int k3cuda_mla_layer_f32(k3cuda_ctx *ctx, float *out, const float *x,
+                         const k3cuda_mla_weights *w, int T, int E, int H, int q_lora, int dn,
+                         int dr, int dl, int dv, float rms_eps, float *latent, float *rope,
+                         int cached, int cap, void *workspace, size_t workspace_bytes);
+
 /* ------------------------------------------------- multi-GPU: head-sharded output */
 /* The reference is single-process (no communicator exists in it). Head sharding adds
  * one exchange: each rank computes H_local = H / nranks heads of [T][H][dv] and the

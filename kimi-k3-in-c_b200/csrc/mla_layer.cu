@@ -273,3 +273,231 @@ extern "C" int k3cuda_mla_layer(k3cuda_ctx *ctx, float *out, const float *x,
     if ((rc = after_launch(ctx, "mla_gate"))) return rc;
     return project(ctx, out, ot, ots, w->o, wdt, T, HV, E);
 }
+
+// ---------------------------------------------------------- any head geometry, fp32 cache
+// k3_mla_cached for head widths other than the released 128/64/512/128 (the reference's
+// own test models use 24/8/32/16): the cache is fp32 latent + rope rows, the attention is
+// the absorbed form on CUDA cores with fp32 arithmetic throughout, so the layer stays
+// within fp32 rounding of the reference rather than inside a bf16 bound.
+namespace k3 {
+
+constexpr int MG_WARPS = 8;
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+    for (int o = 16; o; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+}
+
+// latent[pos0 + t] = kv_a_norm * ct[t][0:dl] / sqrt(mean(ct[t][0:dl]^2) + eps) (sum of squares
+// in double, as k3_rmsnorm) and rope[pos0 + t] = ct[t][dl:dl+dr] (k3_ops.c:363-366); one
+// block per token
+__global__ void mla_append_f32(float *__restrict__ latent, float *__restrict__ rope,
+                               const float *__restrict__ ct, const float *__restrict__ wn,
+                               int dl, int dr, int pos0, float eps) {
+    __shared__ double red[32];
+    const int t = blockIdx.x;
+    const float *c = ct + (size_t)t * (dl + dr);
+    double ss = 0.0;
+    for (int i = threadIdx.x; i < dl; i += blockDim.x) ss = fma((double)c[i], (double)c[i], ss);
+#pragma unroll
+    for (int o = 16; o; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
+    __syncthreads();
+    if (threadIdx.x < 32) {
+        double v = threadIdx.x < blockDim.x / 32 ? red[threadIdx.x] : 0.0;
+#pragma unroll
+        for (int o = 16; o; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+        if (threadIdx.x == 0) red[0] = v;
+    }
+    __syncthreads();
+    const float inv = (float)(1.0 / sqrt(red[0] / (double)dl + (double)eps));
+    float *lr = latent + (size_t)(pos0 + t) * dl;
+    float *rr = rope + (size_t)(pos0 + t) * dr;
+    for (int i = threadIdx.x; i < dl; i += blockDim.x) lr[i] = wn[i] * c[i] * inv;
+    for (int i = threadIdx.x; i < dr; i += blockDim.x) rr[i] = c[dl + i];
+}
+
+// acc[t][h][0:dv] for query t at position cached + t and head h (block (t, h), 8 warps):
+//   qa = W_UK[h]^T q_nope                      (W_UK[h] = kv_b rows h*(dn+dv) .. +dn)
+//   score[s] = (qa . latent[s] + q_rope . rope[s]) * scale,   s = 0 .. cached + t
+//   o_lat = sum_s softmax(score)[s] latent[s];  acc = W_UV[h] o_lat  (the next dv rows)
+// the attention of k3_ops.c:381-411 with kv_b's per-head blocks factored through the latent
+// (a warp walks every 8th position with its own running max / sum / o_lat, and the warps
+// merge at the end). Dynamic shared memory: (dl + dr + 8 dl + 16) floats.
+template <typename WT>
+__global__ void mla_attend_f32(float *__restrict__ acc, const float *__restrict__ q,
+                               const WT *__restrict__ kv_b, const float *__restrict__ latent,
+                               const float *__restrict__ rope, int H, int dn, int dr, int dl,
+                               int dv, int cached, float scale) {
+    extern __shared__ float sm[];
+    const int t = blockIdx.x, h = blockIdx.y;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    float *qa = sm, *qrs = qa + dl, *ow = qrs + dr, *mw = ow + MG_WARPS * dl;
+    const float *qt = q + ((size_t)t * H + h) * (dn + dr);
+    const WT *wuk = kv_b + (size_t)h * (dn + dv) * dl;
+    const WT *wuv = wuk + (size_t)dn * dl;
+    for (int j = threadIdx.x; j < dl; j += blockDim.x) {
+        float s = 0.f;
+        for (int i = 0; i < dn; i++) s = fmaf(qt[i], io<WT>::ld(wuk + (size_t)i * dl + j), s);
+        qa[j] = s;
+    }
+    for (int i = threadIdx.x; i < dr; i += blockDim.x) qrs[i] = qt[dn + i];
+    for (int i = threadIdx.x; i < MG_WARPS * dl; i += blockDim.x) ow[i] = 0.f;
+    __syncthreads();
+    const int P = cached + t + 1;
+    float m = -INFINITY, l = 0.f;
+    float *o = ow + warp * dl;
+    for (int s = warp; s < P; s += MG_WARPS) {
+        const float *ls = latent + (size_t)s * dl;
+        const float *rs = rope + (size_t)s * dr;
+        float d = 0.f;
+        for (int i = lane; i < dl; i += 32) d = fmaf(qa[i], ls[i], d);
+        for (int i = lane; i < dr; i += 32) d = fmaf(qrs[i], rs[i], d);
+        d = warp_sum(d) * scale;
+        const float mn = fmaxf(m, d);
+        const float corr = expf(m - mn), p = expf(d - mn);
+        l = l * corr + p;
+        for (int i = lane; i < dl; i += 32) o[i] = fmaf(o[i], corr, p * ls[i]);
+        m = mn;
+    }
+    if (lane == 0) {
+        mw[2 * warp] = m;
+        mw[2 * warp + 1] = l;
+    }
+    __syncthreads();
+    float M = -INFINITY;
+    for (int w = 0; w < MG_WARPS; w++)
+        if (mw[2 * w + 1] > 0.f) M = fmaxf(M, mw[2 * w]);
+    float L = 0.f;
+    for (int w = 0; w < MG_WARPS; w++)
+        if (mw[2 * w + 1] > 0.f) L += mw[2 * w + 1] * expf(mw[2 * w] - M);
+    const float invL = 1.0f / L;
+    for (int i = threadIdx.x; i < dl; i += blockDim.x) {
+        float v = 0.f;
+        for (int w = 0; w < MG_WARPS; w++)
+            if (mw[2 * w + 1] > 0.f) v = fmaf(ow[w * dl + i], expf(mw[2 * w] - M), v);
+        qa[i] = v * invL;  // o_lat (qa is no longer needed)
+    }
+    __syncthreads();
+    for (int j = warp; j < dv; j += MG_WARPS) {
+        float s = 0.f;
+        for (int i = lane; i < dl; i += 32) s = fmaf(io<WT>::ld(wuv + (size_t)j * dl + i), qa[i], s);
+        s = warp_sum(s);
+        if (lane == 0) acc[((size_t)t * H + h) * dv + j] = s;
+    }
+}
+
+struct MlaF32Plan {
+    size_t ql, ct, gb, q, acc, ot, xs, qls, ots, total;
+    bool split;
+};
+
+static void plan_f32(int T, int E, int H, int q_lora, int dn, int dr, int dl, int dv, int wdt,
+                     MlaF32Plan *p) {
+    size_t off = 0;
+    auto take = [&](size_t b) { const size_t o = off; off += al256(b); return o; };
+    const size_t HV = (size_t)H * dv, HQ = (size_t)H * (dn + dr);
+    p->split = T > PROJ_MAXT && wdt == K3CUDA_BF16;
+    p->ql = take((size_t)T * q_lora * 4);
+    p->ct = take((size_t)T * (dl + dr) * 4);
+    p->gb = take((size_t)T * HV * 4);
+    p->q = take((size_t)T * HQ * 4);
+    p->acc = take((size_t)T * HV * 4);
+    p->ot = take((size_t)T * HV * 4);
+    p->xs = p->split ? take((size_t)2 * T * E * 2) : 0;
+    p->qls = p->split ? take((size_t)2 * T * q_lora * 2) : 0;
+    p->ots = p->split ? take((size_t)2 * T * HV * 2) : 0;
+    p->total = off;
+}
+
+static int shape_f32_ok(int T, int E, int H, int q_lora, int dn, int dr, int dl, int dv, int wdt,
+                        int cached, int cap) {
+    K3_ARG_CHECK(T >= 0 && H >= 1 && dn >= 1 && dr >= 0 && dv >= 1 && cached >= 0 && cap >= 1,
+                 "mla_layer_f32: bad shape T=%d H=%d dn=%d dr=%d dv=%d cached=%d cap=%d", T, H,
+                 dn, dr, dv, cached, cap);
+    K3_ARG_CHECK(wdt == K3CUDA_F32 || wdt == K3CUDA_BF16, "mla_layer_f32: bad wdt %d", wdt);
+    if (E < 8 || E % 8 || q_lora < 8 || q_lora % 8 || (H * dv) % 8 || dl < 1 || dl > 1024 ||
+        dr > 256)
+        return set_error(K3CUDA_ERR_UNSUPPORTED,
+                         "mla_layer_f32: E=%d q_lora=%d H*dv=%d (multiples of 8), dl=%d "
+                         "(<= 1024), dr=%d (<= 256) not supported", E, q_lora, H * dv, dl, dr);
+    if ((long long)cached + T > cap)
+        return set_error(K3CUDA_ERR_ARG, "mla_layer_f32: position %lld past the cache (cap %d)",
+                         (long long)cached + T - 1, cap);
+    return K3CUDA_OK;
+}
+
+}  // namespace k3
+
+extern "C" int k3cuda_mla_layer_f32_workspace(int T, int E, int H, int q_lora, int dn, int dr,
+                                              int dl, int dv, int wdt, size_t *bytes) {
+    K3_ARG_CHECK(bytes, "null bytes");
+    int rc = shape_f32_ok(T, E, H, q_lora, dn, dr, dl, dv, wdt, 0, T > 0 ? T : 1);
+    if (rc) return rc;
+    MlaF32Plan p;
+    plan_f32(T, E, H, q_lora, dn, dr, dl, dv, wdt, &p);
+    *bytes = p.total;
+    return K3CUDA_OK;
+}
+
+extern "C" int k3cuda_mla_layer_f32(k3cuda_ctx *ctx, float *out, const float *x,
+                                    const k3cuda_mla_weights *w, int T, int E, int H, int q_lora,
+                                    int dn, int dr, int dl, int dv, float rms_eps, float *latent,
+                                    float *rope, int cached, int cap, void *workspace,
+                                    size_t workspace_bytes) {
+    int rc = enter(ctx);
+    if (rc) return rc;
+    K3_ARG_CHECK(w, "mla_layer_f32: null weights");
+    if ((rc = shape_f32_ok(T, E, H, q_lora, dn, dr, dl, dv, w->wdt, cached, cap))) return rc;
+    if (T == 0) return K3CUDA_OK;
+    K3_ARG_CHECK(out && x && w->q_a && w->q_b && w->kv_a && w->kv_b && w->o && w->q_a_norm &&
+                 w->kv_a_norm && latent && (rope || dr == 0), "mla_layer_f32: null pointer");
+    const void *al[] = {out, x, w->q_a, w->q_b, w->kv_a, w->o};
+    for (const void *p : al)
+        K3_ARG_CHECK(aligned(p, 16), "mla_layer_f32: x, out and the projections must be 16-byte "
+                                     "aligned");
+    K3_ARG_CHECK(!w->g || aligned(w->g, 16), "mla_layer_f32: g must be 16-byte aligned");
+    MlaF32Plan pl;
+    plan_f32(T, E, H, q_lora, dn, dr, dl, dv, w->wdt, &pl);
+    if (workspace_bytes < pl.total || !workspace)
+        return set_error(K3CUDA_ERR_WORKSPACE, "mla_layer_f32: workspace %zu < %zu bytes",
+                         workspace_bytes, pl.total);
+    K3_ARG_CHECK(aligned(workspace, 256), "mla_layer_f32: workspace must be 256-byte aligned");
+    char *ws = (char *)workspace;
+    const int wdt = w->wdt, HV = H * dv, HQ = H * (dn + dr);
+    float *ql = (float *)(ws + pl.ql), *ct = (float *)(ws + pl.ct), *gb = (float *)(ws + pl.gb);
+    float *q = (float *)(ws + pl.q), *acc = (float *)(ws + pl.acc), *ot = (float *)(ws + pl.ot);
+    __nv_bfloat16 *xs = pl.split ? (__nv_bfloat16 *)(ws + pl.xs) : nullptr;
+    __nv_bfloat16 *qls = pl.split ? (__nv_bfloat16 *)(ws + pl.qls) : nullptr;
+    __nv_bfloat16 *ots = pl.split ? (__nv_bfloat16 *)(ws + pl.ots) : nullptr;
+    if (pl.split && (rc = split(ctx, xs, x, (long long)T * E))) return rc;
+    if ((rc = project(ctx, ql, x, xs, w->q_a, wdt, T, E, q_lora))) return rc;
+    if ((rc = project(ctx, ct, x, xs, w->kv_a, wdt, T, E, dl + dr))) return rc;
+    if (w->g && (rc = project(ctx, gb, x, xs, w->g, wdt, T, E, HV))) return rc;
+    rmsnorm_rows<<<T, 256, 0, ctx->stream>>>(ql, w->q_a_norm, q_lora, rms_eps);
+    if ((rc = after_launch(ctx, "rmsnorm_rows"))) return rc;
+    if (pl.split && (rc = split(ctx, qls, ql, (long long)T * q_lora))) return rc;
+    if ((rc = project(ctx, q, ql, qls, w->q_b, wdt, T, q_lora, HQ))) return rc;
+    mla_append_f32<<<T, 256, 0, ctx->stream>>>(latent, rope, ct, w->kv_a_norm, dl, dr, cached,
+                                                rms_eps);
+    if ((rc = after_launch(ctx, "mla_append_f32"))) return rc;
+    const float scale = 1.0f / sqrtf((float)(dn + dr));
+    const int smem = (int)((size_t)(dl + dr + MG_WARPS * dl + 2 * MG_WARPS) * sizeof(float));
+    if (wdt == K3CUDA_BF16) {
+        if ((rc = set_smem(mla_attend_f32<__nv_bfloat16>, smem))) return rc;
+        mla_attend_f32<__nv_bfloat16><<<dim3(T, H), 32 * MG_WARPS, smem, ctx->stream>>>(
+            acc, q, (const __nv_bfloat16 *)w->kv_b, latent, rope, H, dn, dr, dl, dv, cached,
+            scale);
+    } else {
+        if ((rc = set_smem(mla_attend_f32<float>, smem))) return rc;
+        mla_attend_f32<float><<<dim3(T, H), 32 * MG_WARPS, smem, ctx->stream>>>(
+            acc, q, (const float *)w->kv_b, latent, rope, H, dn, dr, dl, dv, cached, scale);
+    }
+    if ((rc = after_launch(ctx, "mla_attend_f32"))) return rc;
+    const long long n = (long long)T * HV;
+    mla_gate<<<grid_for(ctx, n), 256, 0, ctx->stream>>>(ot, ots, ots ? ots + n : nullptr, acc,
+                                                       w->g ? gb : nullptr, n);
+    if ((rc = after_launch(ctx, "mla_gate"))) return rc;
+    return project(ctx, out, ot, ots, w->o, wdt, T, HV, E);
+}

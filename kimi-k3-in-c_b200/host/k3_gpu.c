@@ -190,79 +190,397 @@ void k3g_mla_attend(float *acc, const float *q, const float *latent, const float
     free(hlat); free(hrope);
 }
 
-/* Device copies of KDA layer weights, one allocation per layer, keyed by the host w->q. */
+/* ----------------------------------------------------------- device weight copies */
+/* One device allocation per layer's weights, reused while the same host arrays come back.
+ * The key is the address of the layer's first weight, its geometry and wdt, plus a
+ * fingerprint of sampled bytes of every array (three 256-byte windows each: start, middle,
+ * end), so a layer freed and another loaded at the same address is copied again. */
 #define K3G_MAX_LAYERS 256
+#define K3G_MAX_ARRAYS 14
 typedef struct {
     const void *key;
+    int geom[8];
+    uint64_t fp;
     void *block;
-    k3cuda_kda_weights d;
+    const void *dst[K3G_MAX_ARRAYS];
 } LayerW;
 static LayerW g_lw[K3G_MAX_LAYERS];
 static int g_nlw = 0;
 
 static size_t a256(size_t x) { return (x + 255) & ~(size_t)255; }
 
-static const k3cuda_kda_weights *layer_weights(const k3g_kda_weights *w, int E, int H, int D,
-                                               int K)
+static uint64_t fnv(uint64_t h, const void *p, size_t n)
 {
-    for (int i = 0; i < g_nlw; i++)
-        if (g_lw[i].key == w->q) return &g_lw[i].d;
-    if (g_nlw == K3G_MAX_LAYERS) {
-        fprintf(stderr, "k3_gpu: FATAL, more than %d KDA layers\n", K3G_MAX_LAYERS);
-        abort();
+    const unsigned char *b = (const unsigned char *)p;
+    for (size_t i = 0; i < n; i++) h = (h ^ b[i]) * 0x100000001b3ULL;
+    return h;
+}
+
+static uint64_t fingerprint(const void *const *src, const size_t *bytes, int n)
+{
+    uint64_t h = 0xcbf29ce484222325ULL;
+    for (int i = 0; i < n; i++) {
+        if (!src[i] || !bytes[i]) continue;
+        const size_t win = bytes[i] < 256 ? bytes[i] : 256;
+        const char *a = (const char *)src[i];
+        h = fnv(h, a, win);
+        h = fnv(h, a + (bytes[i] - win) / 2, win);
+        h = fnv(h, a + bytes[i] - win, win);
     }
+    return h;
+}
+
+/* Device copies of n host arrays (NULL entries stay NULL); returns the device pointers. */
+static const void *const *device_weights(const void *const *src, const size_t *bytes, int n,
+                                         const int geom[8])
+{
+    const uint64_t fp = fingerprint(src, bytes, n);
+    LayerW *L = NULL;
+    for (int i = 0; i < g_nlw; i++)
+        if (g_lw[i].key == src[0]) {
+            if (!memcmp(g_lw[i].geom, geom, sizeof g_lw[i].geom) && g_lw[i].fp == fp)
+                return g_lw[i].dst;
+            L = &g_lw[i];  /* same address, other weights: copy again into this slot */
+            ok(k3cuda_free(ctx(), L->block), "k3cuda_free (stale layer weights)");
+            L->block = NULL;
+            break;
+        }
+    if (!L) {
+        if (g_nlw == K3G_MAX_LAYERS) {
+            fprintf(stderr, "k3_gpu: FATAL, more than %d layers' weights\n", K3G_MAX_LAYERS);
+            abort();
+        }
+        L = &g_lw[g_nlw++];
+    }
+    size_t total = 0;
+    for (int i = 0; i < n; i++) total += a256(bytes[i]);
+    ok(k3cuda_malloc(ctx(), &L->block, total), "k3cuda_malloc (layer weights)");
+    size_t off = 0;
+    for (int i = 0; i < n; i++) {
+        L->dst[i] = NULL;
+        if (!src[i]) continue;
+        L->dst[i] = (char *)L->block + off;
+        ok(k3cuda_memcpy_h2d(ctx(), (void *)L->dst[i], src[i], bytes[i]), "upload layer weights");
+        off += a256(bytes[i]);
+    }
+    L->key = src[0];
+    memcpy(L->geom, geom, sizeof L->geom);
+    L->fp = fp;
+    return L->dst;
+}
+
+static int tokenwise(void)
+{
+    const char *e = getenv("K3G_TOKENWISE");
+    return e && e[0] == '1';
+}
+
+/* ------------------------------------------------------------------------ KDA layer */
+void k3g_kda_layer(float *out, const float *x, const k3g_kda_weights *w, const k3g_cfg *c,
+                   int T, float *state, float *scratch)
+{
+    (void)scratch;
+    if (T <= 0) return;
+    const int E = c->hidden, H = c->kda_heads, D = c->kda_head_dim, K = c->conv_k;
     const size_t P = (size_t)H * D, es = w->wdt == 1 ? 2 : 4;
     const void *src[14] = {w->q, w->k, w->v, w->q_conv, w->k_conv, w->v_conv, w->f_a, w->f_b,
                            w->A_log, w->dt_bias, w->b, w->g, w->o_norm, w->o};
     const size_t bytes[14] = {P * E * es, P * E * es, P * E * es, P * K * 4, P * K * 4,
                               P * K * 4, (size_t)D * E * es, P * D * es, (size_t)H * 4, P * 4,
                               (size_t)H * E * es, P * E * es, (size_t)D * 4, (size_t)E * P * es};
-    size_t total = 0;
-    for (int i = 0; i < 14; i++) total += a256(bytes[i]);
-    LayerW *L = &g_lw[g_nlw];
-    ok(k3cuda_malloc(ctx(), &L->block, total), "k3cuda_malloc (layer weights)");
-    const void *dst[14];
-    size_t off = 0;
-    for (int i = 0; i < 14; i++) {
+    for (int i = 0; i < 14; i++)
         if (!src[i]) {
             fprintf(stderr, "k3_gpu: FATAL, KDA layer weight %d is NULL\n", i);
             abort();
         }
-        dst[i] = (char *)L->block + off;
-        ok(k3cuda_memcpy_h2d(ctx(), (void *)dst[i], src[i], bytes[i]), "upload layer weights");
-        off += a256(bytes[i]);
-    }
-    L->d.q = dst[0]; L->d.k = dst[1]; L->d.v = dst[2];
-    L->d.q_conv = (const float *)dst[3]; L->d.k_conv = (const float *)dst[4];
-    L->d.v_conv = (const float *)dst[5];
-    L->d.f_a = dst[6]; L->d.f_b = dst[7];
-    L->d.A_log = (const float *)dst[8]; L->d.dt_bias = (const float *)dst[9];
-    L->d.b = dst[10]; L->d.g = dst[11]; L->d.o_norm = (const float *)dst[12]; L->d.o = dst[13];
-    L->d.wdt = w->wdt == 1 ? K3CUDA_BF16 : K3CUDA_F32;
-    L->key = w->q;
-    g_nlw++;
-    return &L->d;
-}
+    const int geom[8] = {1, E, H, D, K, w->wdt, 0, 0};
+    const void *const *d = device_weights(src, bytes, 14, geom);
+    k3cuda_kda_weights dw;
+    dw.q = d[0]; dw.k = d[1]; dw.v = d[2];
+    dw.q_conv = (const float *)d[3]; dw.k_conv = (const float *)d[4];
+    dw.v_conv = (const float *)d[5];
+    dw.f_a = d[6]; dw.f_b = d[7];
+    dw.A_log = (const float *)d[8]; dw.dt_bias = (const float *)d[9];
+    dw.b = d[10]; dw.g = d[11]; dw.o_norm = (const float *)d[12]; dw.o = d[13];
+    dw.wdt = w->wdt == 1 ? K3CUDA_BF16 : K3CUDA_F32;
 
-void k3g_kda_layer(float *out, const float *x, const k3g_kda_weights *w, int T, int E, int H,
-                   int D, int K, float gate_lb, float rms_eps, float *state)
-{
-    if (T <= 0) return;
-    const k3cuda_kda_weights *dw = layer_weights(w, E, H, D, K);
     const size_t xb = (size_t)T * E * 4;
     const size_t sb = ((size_t)H * D * D + 3 * (size_t)H * D * (K - 1)) * 4;
     float *dx = (float *)put(B_Q, x, xb);
     float *dout = (float *)dev(B_O, xb);
-    float *dS = NULL;
-    if (state) dS = (float *)put(B_S, state, sb);
+    float *dS = (float *)dev(B_S, sb);
+    if (state) ok(k3cuda_memcpy_h2d(ctx(), dS, state, sb), "upload state");
+    const int steps = tokenwise() ? T : 1, Tc = tokenwise() ? 1 : T;
+    /* a fresh sequence over several one-token calls still carries its state between them */
+    if (!state && steps > 1) ok(k3cuda_memset(ctx(), dS, 0, sb), "zero state");
     size_t ws = 0;
-    ok(k3cuda_kda_layer_workspace(T, E, H, D, K, dw->wdt, K3CUDA_F32, &ws), "layer workspace");
+    ok(k3cuda_kda_layer_workspace(Tc, E, H, D, K, dw.wdt, K3CUDA_F32, &ws), "layer workspace");
     void *dws = dev(B_WS, ws);
-    ok(k3cuda_kda_layer(ctx(), dout, dx, dw, T, E, H, D, K, gate_lb, rms_eps, dS, K3CUDA_F32,
-                        dws, ws),
-       "k3cuda_kda_layer");
+    for (int s = 0; s < steps; s++)
+        ok(k3cuda_kda_layer(ctx(), dout + (size_t)s * Tc * E, dx + (size_t)s * Tc * E, &dw, Tc,
+                            E, H, D, K, c->gate_lb, c->rms_eps,
+                            (state || steps > 1) ? dS : NULL, K3CUDA_F32, dws, ws),
+           "k3cuda_kda_layer");
     get(out, dout, xb);
     if (state) get(state, dS, sb);
+}
+
+/* ------------------------------------------------------------------------ MLA layer */
+/* The device copy of one caller cache (keyed by its host kvc; NULL: the per-call cache of
+ * an uncached call). valid: host rows [0, valid) are on the device; rowhash[p]: FNV-1a of
+ * host row p (latent then rope) as last written or uploaded. */
+#define K3G_MAX_CACHES 256
+typedef struct {
+    const float *key;
+    int cap, H, dl, dr, kvw, f32, valid;
+    void *lat, *rope;
+    uint64_t *rowhash;
+} MlaCache;
+static MlaCache g_mc[K3G_MAX_CACHES];
+static int g_nmc = 0;
+
+static void mla_cache_free(MlaCache *m)
+{
+    if (m->lat) k3cuda_free(ctx(), m->lat);
+    if (m->rope) k3cuda_free(ctx(), m->rope);
+    free(m->rowhash);
+    memset(m, 0, sizeof *m);
+}
+
+void k3g_mla_cache_forget(const float *kvc)
+{
+    for (int i = 0; i < g_nmc; i++)
+        if (g_mc[i].key == kvc && kvc) g_mc[i].valid = 0;
+}
+
+static uint64_t row_hash(const float *lat, const float *rope, int dl, int dr)
+{
+    uint64_t h = fnv(0xcbf29ce484222325ULL, lat, (size_t)dl * 4);
+    return fnv(h, rope, (size_t)dr * 4);
+}
+
+static MlaCache *mla_cache(const float *key, int cap, int H, int dl, int dr, int kvw, int f32)
+{
+    MlaCache *m = NULL;
+    for (int i = 0; i < g_nmc; i++)
+        if (g_mc[i].key == key) { m = &g_mc[i]; break; }
+    if (m && (m->cap < cap || m->H != H || m->dl != dl || m->dr != dr || m->kvw != kvw ||
+              m->f32 != f32 || (key && m->cap != cap))) {
+        mla_cache_free(m);  /* geometry changed: start this slot over */
+        m->key = key;
+    }
+    if (!m) {
+        if (g_nmc == K3G_MAX_CACHES) {
+            fprintf(stderr, "k3_gpu: FATAL, more than %d MLA caches\n", K3G_MAX_CACHES);
+            abort();
+        }
+        m = &g_mc[g_nmc++];
+        memset(m, 0, sizeof *m);
+        m->key = key;
+    }
+    if (!m->lat) {
+        const size_t es = f32 ? 4 : 2;
+        ok(k3cuda_malloc(ctx(), &m->lat, (size_t)cap * dl * es), "k3cuda_malloc (MLA latent)");
+        ok(k3cuda_malloc(ctx(), &m->rope, (size_t)cap * (dr ? dr : 1) * es),
+           "k3cuda_malloc (MLA rope)");
+        m->rowhash = (uint64_t *)calloc((size_t)cap, sizeof(uint64_t));
+        if (!m->rowhash) {
+            fprintf(stderr, "k3_gpu: FATAL, out of host memory\n");
+            abort();
+        }
+        m->cap = cap; m->H = H; m->dl = dl; m->dr = dr; m->kvw = kvw; m->f32 = f32;
+        m->valid = 0;
+    }
+    return m;
+}
+
+static uint16_t *stage16(size_t n)
+{
+    static uint16_t *buf = NULL;
+    static size_t have = 0;
+    if (have < n) {
+        free(buf);
+        buf = (uint16_t *)malloc(n * 2);
+        if (!buf) {
+            fprintf(stderr, "k3_gpu: FATAL, out of host memory\n");
+            abort();
+        }
+        have = n;
+    }
+    return buf;
+}
+
+/* host rows [p0, p1) of kvc (first dl floats) / ropec -> the device cache */
+static void mla_rows_up(MlaCache *m, const float *kvc, const float *ropec, int p0, int p1)
+{
+    const int dl = m->dl, dr = m->dr, n = p1 - p0;
+    if (n <= 0) return;
+    if (m->f32) {
+        float *lat = (float *)malloc((size_t)n * dl * 4 + 4);
+        if (!lat) { fprintf(stderr, "k3_gpu: FATAL, out of host memory\n"); abort(); }
+        for (int r = 0; r < n; r++)
+            memcpy(lat + (size_t)r * dl, kvc + (size_t)(p0 + r) * m->kvw, (size_t)dl * 4);
+        ok(k3cuda_memcpy_h2d(ctx(), (float *)m->lat + (size_t)p0 * dl, lat, (size_t)n * dl * 4),
+           "upload latent rows");
+        if (dr)
+            ok(k3cuda_memcpy_h2d(ctx(), (float *)m->rope + (size_t)p0 * dr,
+                                 ropec + (size_t)p0 * dr, (size_t)n * dr * 4),
+               "upload rope rows");
+        ok(k3cuda_sync(ctx()), "k3cuda_sync");
+        free(lat);
+    } else {
+        /* the host rows are bf16 values widened exactly, so this rounding is exact */
+        uint16_t *h = stage16((size_t)n * (dl + dr));
+        for (int r = 0; r < n; r++) {
+            for (int i = 0; i < dl; i++) h[(size_t)r * dl + i] = bf16(kvc[(size_t)(p0 + r) * m->kvw + i]);
+            for (int i = 0; i < dr; i++)
+                h[(size_t)n * dl + (size_t)r * dr + i] = bf16(ropec[(size_t)(p0 + r) * dr + i]);
+        }
+        ok(k3cuda_memcpy_h2d(ctx(), (uint16_t *)m->lat + (size_t)p0 * dl, h, (size_t)n * dl * 2),
+           "upload latent rows");
+        if (dr)
+            ok(k3cuda_memcpy_h2d(ctx(), (uint16_t *)m->rope + (size_t)p0 * dr, h + (size_t)n * dl,
+                                 (size_t)n * dr * 2),
+               "upload rope rows");
+        ok(k3cuda_sync(ctx()), "k3cuda_sync");
+    }
+    for (int p = p0; p < p1; p++)
+        m->rowhash[p] = row_hash(kvc + (size_t)p * m->kvw, ropec + (size_t)p * dr, dl, dr);
+}
+
+/* device rows [p0, p1) -> host kvc (first dl floats of each row) / ropec */
+static void mla_rows_down(MlaCache *m, float *kvc, float *ropec, int p0, int p1)
+{
+    const int dl = m->dl, dr = m->dr, n = p1 - p0;
+    if (n <= 0) return;
+    if (m->f32) {
+        float *lat = (float *)malloc((size_t)n * dl * 4 + 4);
+        if (!lat) { fprintf(stderr, "k3_gpu: FATAL, out of host memory\n"); abort(); }
+        ok(k3cuda_memcpy_d2h(ctx(), lat, (float *)m->lat + (size_t)p0 * dl, (size_t)n * dl * 4),
+           "download latent rows");
+        if (dr)
+            ok(k3cuda_memcpy_d2h(ctx(), ropec + (size_t)p0 * dr, (float *)m->rope + (size_t)p0 * dr,
+                                 (size_t)n * dr * 4),
+               "download rope rows");
+        ok(k3cuda_sync(ctx()), "k3cuda_sync");
+        for (int r = 0; r < n; r++)
+            memcpy(kvc + (size_t)(p0 + r) * m->kvw, lat + (size_t)r * dl, (size_t)dl * 4);
+        free(lat);
+    } else {
+        uint16_t *h = stage16((size_t)n * (dl + dr));
+        ok(k3cuda_memcpy_d2h(ctx(), h, (uint16_t *)m->lat + (size_t)p0 * dl, (size_t)n * dl * 2),
+           "download latent rows");
+        if (dr)
+            ok(k3cuda_memcpy_d2h(ctx(), h + (size_t)n * dl, (uint16_t *)m->rope + (size_t)p0 * dr,
+                                 (size_t)n * dr * 2),
+               "download rope rows");
+        ok(k3cuda_sync(ctx()), "k3cuda_sync");
+        for (int r = 0; r < n; r++) {
+            for (int i = 0; i < dl; i++) {
+                const uint32_t u = (uint32_t)h[(size_t)r * dl + i] << 16;
+                memcpy(kvc + (size_t)(p0 + r) * m->kvw + i, &u, 4);
+            }
+            for (int i = 0; i < dr; i++) {
+                const uint32_t u = (uint32_t)h[(size_t)n * dl + (size_t)r * dr + i] << 16;
+                memcpy(ropec + (size_t)(p0 + r) * dr + i, &u, 4);
+            }
+        }
+    }
+    for (int p = p0; p < p1; p++)
+        m->rowhash[p] = row_hash(kvc + (size_t)p * m->kvw, ropec + (size_t)p * dr, dl, dr);
+}
+
+void k3g_mla_cached(float *out, const float *x, const k3g_mla_weights *w, const k3g_cfg *c,
+                    int T, float *scratch, float *kvc, float *ropec, int cached, int cap)
+{
+    (void)scratch;
+    if (T <= 0) return;
+    const int E = c->hidden, H = c->n_heads, QL = c->q_lora, dn = c->qk_nope, dr = c->qk_rope;
+    const int dl = c->kv_lora, dv = c->v_head, kvw = H * (dn + dv);
+    if (!kvc) {
+        cached = 0;
+        cap = T;
+    } else {
+        const long last = (long)cached + T - 1;
+        if (last >= cap) {
+            fprintf(stderr,
+                    "k3_gpu: FATAL, MLA KV cache position is %ld, which exceeds the limit of "
+                    "%ld.\n    Aborting rather than returning without writing the output "
+                    "buffer.\n", last, (long)cap - 1);
+            abort();
+        }
+        if (kvw < dl || !ropec) {
+            fprintf(stderr, "k3_gpu: FATAL, MLA cache rows of %d floats cannot hold the %d-wide "
+                            "latent (or ropec is NULL)\n", kvw, dl);
+            abort();
+        }
+    }
+    const char *fe = getenv("K3G_MLA_F32");
+    const int released = dn == 128 && dr == 64 && dl == 512 && dv == 128 && H <= 128 &&
+                         E % 8 == 0 && QL % 8 == 0;
+    const int f32 = !released || (fe && fe[0] == '1');
+    MlaCache *m = mla_cache(kvc, cap, H, dl, dr, kvw, f32);
+    if (kvc) {
+        /* the host rows are the record: check the last one before `cached` and upload what
+         * the device does not hold */
+        if (cached > 0 && m->valid >= cached &&
+            m->rowhash[cached - 1] != row_hash(kvc + (size_t)(cached - 1) * kvw,
+                                               ropec + (size_t)(cached - 1) * dr, dl, dr))
+            m->valid = 0;
+        if (m->valid < cached) mla_rows_up(m, kvc, ropec, m->valid, cached);
+    }
+    /* weights */
+    const size_t es = w->wdt == 1 ? 2 : 4;
+    const void *src[8] = {w->q_a, w->q_b, w->kv_a, w->kv_b, w->o, w->g, w->q_a_norm,
+                          w->kv_a_norm};
+    const size_t bytes[8] = {(size_t)QL * E * es, (size_t)H * (dn + dr) * QL * es,
+                             (size_t)(dl + dr) * E * es, (size_t)kvw * dl * es,
+                             (size_t)E * H * dv * es, w->g ? (size_t)H * dv * E * es : 0,
+                             (size_t)QL * 4, (size_t)dl * 4};
+    for (int i = 0; i < 8; i++)
+        if (!src[i] && i != 5) {
+            fprintf(stderr, "k3_gpu: FATAL, MLA layer weight %d is NULL\n", i);
+            abort();
+        }
+    const int geom[8] = {2, E, H, QL, dn, dr, dl, dv + 1000 * w->wdt};
+    const void *const *d = device_weights(src, bytes, 8, geom);
+    k3cuda_mla_weights dw;
+    dw.q_a = d[0]; dw.q_b = d[1]; dw.kv_a = d[2]; dw.kv_b = d[3]; dw.o = d[4]; dw.g = d[5];
+    dw.q_a_norm = (const float *)d[6]; dw.kv_a_norm = (const float *)d[7];
+    dw.wdt = w->wdt == 1 ? K3CUDA_BF16 : K3CUDA_F32;
+
+    const size_t xb = (size_t)T * E * 4;
+    float *dx = (float *)put(B_Q, x, xb);
+    float *dout = (float *)dev(B_O, xb);
+    const int steps = tokenwise() ? T : 1, Tc = tokenwise() ? 1 : T;
+    size_t ws = 0, ws_max = 0;
+    for (int s = 0; s < steps; s++) {
+        if (f32)
+            ok(k3cuda_mla_layer_f32_workspace(Tc, E, H, QL, dn, dr, dl, dv, dw.wdt, &ws),
+               "mla layer workspace");
+        else
+            ok(k3cuda_mla_layer_workspace(Tc, E, H, QL, cached + s * Tc, dw.wdt, &ws),
+               "mla layer workspace");
+        if (ws > ws_max) ws_max = ws;
+    }
+    void *dws = dev(B_WS, ws_max);
+    for (int s = 0; s < steps; s++) {
+        const size_t off = (size_t)s * Tc * E;
+        if (f32)
+            ok(k3cuda_mla_layer_f32(ctx(), dout + off, dx + off, &dw, Tc, E, H, QL, dn, dr, dl, dv,
+                                    c->rms_eps, (float *)m->lat, (float *)m->rope,
+                                    cached + s * Tc, cap, dws, ws_max),
+               "k3cuda_mla_layer_f32");
+        else
+            ok(k3cuda_mla_layer(ctx(), dout + off, dx + off, &dw, Tc, E, H, QL, dn, dr, dl, dv,
+                                c->rms_eps, m->lat, m->rope, cached + s * Tc, cap, dws, ws_max),
+               "k3cuda_mla_layer");
+    }
+    get(out, dout, xb);
+    if (kvc) {
+        mla_rows_down(m, kvc, ropec, cached, cached + T);
+        m->valid = cached + T;
+    }
 }
 
 void k3g_shutdown(void)
@@ -270,6 +588,8 @@ void k3g_shutdown(void)
     if (!g_ctx) return;
     for (int i = 0; i < g_nlw; i++) k3cuda_free(g_ctx, g_lw[i].block);
     g_nlw = 0;
+    for (int i = 0; i < g_nmc; i++) mla_cache_free(&g_mc[i]);
+    g_nmc = 0;
     for (int i = 0; i < B_N; i++) {
         if (g_buf[i].ptr) k3cuda_free(g_ctx, g_buf[i].ptr);
         g_buf[i].ptr = NULL;

@@ -68,6 +68,10 @@ SIGNATURES = {
     "k3cuda_mla_layer_workspace": (_i, [_i, _i, _i, _i, _i, _i, C.POINTER(_sz)]),
     "k3cuda_mla_layer": (_i, [_vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _i, _i, _f, _vp, _vp,
                               _i, _i, _vp, _sz]),
+    "k3cuda_mla_layer_f32_workspace": (_i, [_i, _i, _i, _i, _i, _i, _i, _i, _i,
+                                            C.POINTER(_sz)]),
+    "k3cuda_mla_layer_f32": (_i, [_vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _i, _i, _f, _vp,
+                                  _vp, _i, _i, _vp, _sz]),
     "k3cuda_comm_unique_id": (_i, [C.c_char_p]),
     "k3cuda_comm_init": (_i, [_vp, _i, _i, C.c_char_p]),
     "k3cuda_comm_set_timeout": (_i, [_vp, _i]),
@@ -101,6 +105,19 @@ class MlaWeights(C.Structure):
                 ("g", _vp), ("q_a_norm", _vp), ("kv_a_norm", _vp), ("wdt", _i)]
 
 
+class Cfg(C.Structure):
+    """k3g_cfg: field for field the reference's K3Cfg (include/k3/k3.h:73-120)."""
+    _fields_ = [("hidden", _i), ("n_layers", _i), ("vocab", _i), ("rms_eps", _f),
+                ("kda_heads", _i), ("kda_head_dim", _i), ("conv_k", _i), ("gate_lb", _f),
+                ("n_heads", _i), ("q_lora", _i), ("kv_lora", _i), ("qk_nope", _i),
+                ("qk_rope", _i), ("v_head", _i), ("mla_out_gate", _i), ("n_experts", _i),
+                ("topk", _i), ("n_shared", _i), ("latent", _i), ("moe_inter", _i),
+                ("routed_scale", _f), ("moe_renorm", _i), ("latent_norm", _i),
+                ("first_dense", _i), ("dense_inter", _i), ("attn_res_block", _i),
+                ("situ_b1", _f), ("situ_b2", _f), ("n_full_attn", _i),
+                ("full_attn", C.POINTER(_i))]
+
+
 KDA_WEIGHT_NAMES = ("q", "k", "v", "q_conv", "k_conv", "v_conv", "f_a", "f_b", "A_log",
                     "dt_bias", "b", "g", "o_norm", "o")
 
@@ -110,7 +127,9 @@ GPU_SIGNATURES = {
     "k3g_kda_step": (None, [_fp, _fp, _fp, _fp, _fp, _fp, _f, _i, _i]),
     "k3g_kda_recurrence": (None, [_fp, _fp, _fp, _fp, _fp, _fp, _fp, _i, _i, _i]),
     "k3g_mla_attend": (None, [_fp, _fp, _fp, _fp, _fp, _f, _i, _i, _i, _i, _i, _i]),
-    "k3g_kda_layer": (None, [_fp, _fp, _vp, _i, _i, _i, _i, _i, _f, _f, _fp]),
+    "k3g_kda_layer": (None, [_fp, _fp, _vp, _vp, _i, _fp, _fp]),
+    "k3g_mla_cached": (None, [_fp, _fp, _vp, _vp, _i, _fp, _fp, _fp, _i, _i]),
+    "k3g_mla_cache_forget": (None, [_fp]),
     "k3g_state_save": (_i, [C.c_char_p, _ip, _ip, _i, _vp, C.c_int64, _i, _vp, _vp, _i, _i, _i,
                             _i, _i]),
     "k3g_state_load": (_i, [C.c_char_p, _ip, _ip, _i, _ip, _vp, C.c_int64, _i, _vp, _vp, _i, _i,
@@ -380,6 +399,20 @@ class Context:
                                      int(H), int(q_lora), 128, 64, 512, 128, float(rms_eps),
                                      _ptr(latent), _ptr(rope), int(cached), int(cap),
                                      _ptr(workspace), int(workspace_bytes)))
+
+    def mla_layer_f32_workspace(self, T, E, H, q_lora, dn, dr, dl, dv, wdt) -> int:
+        return _ws_query(lib().k3cuda_mla_layer_f32_workspace, int(T), int(E), int(H),
+                         int(q_lora), int(dn), int(dr), int(dl), int(dv), int(wdt))
+
+    def mla_layer_f32(self, out, x, weights, wdt, T, E, H, q_lora, dn, dr, dl, dv, rms_eps,
+                      latent, rope, cached, cap, workspace, workspace_bytes):
+        """Any head geometry, fp32 latent/rope cache (k3cuda_mla_layer_f32)."""
+        w = MlaWeights(**{n: _ptr(weights.get(n)) for n, _ in MlaWeights._fields_[:-1]},
+                       wdt=int(wdt))
+        check(lib().k3cuda_mla_layer_f32(self.h, _ptr(out), _ptr(x), C.byref(w), int(T), int(E),
+                                         int(H), int(q_lora), int(dn), int(dr), int(dl), int(dv),
+                                         float(rms_eps), _ptr(latent), _ptr(rope), int(cached),
+                                         int(cap), _ptr(workspace), int(workspace_bytes)))
 
     # multi-GPU -------------------------------------------------------------------
     def set_wait_limit(self, cycles: int):

@@ -5,6 +5,7 @@ argument order, abort-on-failure. They are checked on the reference's fixtures e
 the reference's tests/unit/test_ops.c drives k3_kda_step (t_recur, :310-350).
 """
 import ctypes as C
+import os
 
 import numpy as np
 import pytest
@@ -14,6 +15,7 @@ import workloads as W
 
 pytestmark = pytest.mark.gpu
 fp = C.POINTER(C.c_float)
+W_GOLDEN_TOL = os.path.join(os.path.dirname(__file__), "golden", "manifest_tolerance.npz")
 
 
 def P(a):
@@ -117,11 +119,17 @@ def test_kda_layer_dropin_on_reference_fixture(golden, name):
     x = np.ascontiguousarray(d["in"][0], np.float32)
     out = np.zeros((T, E), np.float32)
     state = np.zeros(H * D * D + 3 * H * D * (K - 1), np.float32)
-    G.k3g_kda_layer(P(out), P(x), C.byref(w), T, E, H, D, K, float(d["lower_bound"]),
-                    float(d["rms_eps"]), P(state))
+    c = k3cuda.Cfg(hidden=E, kda_heads=H, kda_head_dim=D, conv_k=K,
+                   gate_lb=float(d["lower_bound"]), rms_eps=float(d["rms_eps"]))
+    scratch = np.zeros(16, np.float32)  # accepted, not touched
+    G.k3g_kda_layer(P(out), P(x), C.byref(w), C.byref(c), T, P(state), P(scratch))
     G.k3g_shutdown()
     assert W.rel_fro(out, d["out"][0]) < 2e-3
     assert W.rel_fro(state[: H * D * D], d["state_out"].ravel()) < 2e-3
+    # and at the reference's own elementwise bar (its MANIFEST: atol + rtol * |want|)
+    tol = np.load(W_GOLDEN_TOL)
+    lim = float(tol["fp32_abs"]) + float(tol["fp32_rel"]) * np.abs(d["out"][0])
+    assert np.all(np.abs(out - d["out"][0]) <= lim)
 
 
 def test_kda_layer_dropin_bf16_weights_decode_loop():
@@ -135,10 +143,12 @@ def test_kda_layer_dropin_bf16_weights_decode_loop():
     w, keep, used = _host_weights(W.kda_layer_weights(rng, E, H, D, K), 1)
     s_gpu = (0.1 * rng.standard_normal(H * D * D + 3 * H * D * (K - 1))).astype(np.float32)
     s_orc = s_gpu.copy()
+    c = k3cuda.Cfg(hidden=E, kda_heads=H, kda_head_dim=D, conv_k=K, gate_lb=-5.0,
+                   rms_eps=1e-5)
     for T in (12, 1, 1, 1, 1):
         x = rng.standard_normal((T, E)).astype(np.float32)
         out = np.zeros((T, E), np.float32)
-        G.k3g_kda_layer(P(out), P(x), C.byref(w), T, E, H, D, K, -5.0, 1e-5, P(s_gpu))
+        G.k3g_kda_layer(P(out), P(x), C.byref(w), C.byref(c), T, P(s_gpu), None)
         want = oracle.kda_layer(x, used, H, D, K, -5.0, 1e-5, s_orc)
         assert W.rel_fro(out, want) < 2e-3, T
     G.k3g_shutdown()
