@@ -335,8 +335,9 @@ int k3cuda_kda_prefill_gathered(k3cuda_ctx *ctx, float *state, const void *q, co
  * 265-291, and k3_matmul_bf16, :1122-1227, each one row). Products of the fp32 activation
  * and the weight are exact and summed in fp32 (the reference sums in double; the
  * difference is inside fp32 rounding of the result). T <= 8 streams every weight row once
- * (HBM-bound); T > 8 is a cuBLAS GEMM (loaded at run time), and for bf16 weights x is split
- * into bf16 hi + lo halves so the product keeps near-fp32 accuracy. Requires in % 8 == 0
+ * (HBM-bound); T > 8 is a GEMM: for bf16 weights with in % 64 == 0 on tcgen05 with x split
+ * into bf16 hi + lo halves (both halves' products accumulate in fp32, so the product keeps
+ * near-fp32 accuracy), otherwise on the CUDA cores in fp32. Requires in % 8 == 0
  * and 16-byte aligned x, W, y. workspace d: k3cuda_matmul_workspace() bytes (0 when
  * T <= 8 or W is fp32). */
 int k3cuda_matmul_workspace(int T, int in, int wdt, size_t *bytes);
@@ -353,7 +354,7 @@ int k3cuda_matmul(k3cuda_ctx *ctx, float *y, const float *x, const void *W, int 
  * (:1394-1799) for T activation rows: y d [T][rows] fp32 = x d [T][in] fp32 times W^T,
  * never materialising W when T <= 4, group == 32 and in % 32 == 0 (products exact, each
  * 32-element group summed in fp32 then scaled, groups summed in fp32); otherwise W is
- * expanded to bf16 in the workspace and multiplied by cuBLAS against x's bf16 hi + lo
+ * expanded to bf16 in the workspace and multiplied on tcgen05 against x's bf16 hi + lo
  * halves. Requirements of the reference: in even, group <= 64. */
 int k3cuda_mxfp4_dequant(k3cuda_ctx *ctx, void *out, int out_dtype,
                          const unsigned char *packed, const unsigned char *scales, int rows,

@@ -153,14 +153,12 @@ int k3cuda_init(int device, k3cuda_ctx **out) {
 }
 
 int k3cuda_comm_destroy_internal(k3cuda_ctx *ctx);  // comm.cu
-void k3cuda_blas_destroy_internal(k3cuda_ctx *ctx);  // kda_layer.cu
 
 int k3cuda_shutdown(k3cuda_ctx *ctx) {
     if (!ctx) return K3CUDA_OK;
     cudaSetDevice(ctx->device);
     if (ctx->stream) cudaStreamSynchronize(ctx->stream);
     k3cuda_comm_destroy_internal(ctx);
-    k3cuda_blas_destroy_internal(ctx);
     for (int i = 0; i < K3CUDA_MAX_EVENTS; i++)
         if (ctx->events[i]) cudaEventDestroy(ctx->events[i]);
     if (ctx->flush_buf) cudaFree(ctx->flush_buf);

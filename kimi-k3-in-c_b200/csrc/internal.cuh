@@ -29,7 +29,6 @@ struct k3cuda_ctx {
     size_t full_bytes;
     int *sync_word;             // device int for the cross-rank ordering all-reduce
     void *peer_table;           // device copy of the peers' full-buffer addresses
-    void *blas;                 // cuBLAS handle of the projections (kda_layer.cu), lazily made
     cudaStream_t aux;           // side stream for work that overlaps the main stream's
     cudaEvent_t ev_fork, ev_join;  // (forked from and joined back into `stream`)
     // page-locked ring for the small per-call host tables (stage_h2d)
@@ -57,9 +56,9 @@ struct GatherOut {
 
 namespace k3 {
 
-// Projections (kda_layer.cu). split: hi = bf16(x), lo = bf16(x - hi) into xs [2][n].
-// gemm: y [T][out] = x [T][in] W^T through cuBLAS; W fp32 (SGEMM) or bf16 (two bf16
-// GEMMs over xs, the bf16 split of x).
+// Projections. split (kda_layer.cu): hi = bf16(x), lo = bf16(x - hi) into xs [2][n].
+// gemm (gemm.cu): y [T][out] = x [T][in] W^T; W bf16 on tcgen05 over xs (the bf16 split of
+// x), or fp32 (and untiled shapes) on the CUDA cores.
 int split(k3cuda_ctx *ctx, __nv_bfloat16 *xs, const float *x, long long n);
 int gemm(k3cuda_ctx *ctx, float *y, const float *x, const __nv_bfloat16 *xs, const void *W,
          int wdt, int T, int in, int out);

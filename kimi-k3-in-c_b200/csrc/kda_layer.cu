@@ -3,82 +3,26 @@
 // (k3_mmw, include/k3/k3.h:290-296) it is built from.
 //
 //   step (reference line)                         where it runs here
-//   1   q, k, v, b, f_a, f_b projections (:877-886)  matvec_rows (T <= 8) or cuBLAS (T > 8)
+//   1   q, k, v, b, f_a, f_b projections (:877-886)  matvec_rows (T <= 8) or gemm (T > 8)
 //   2   ShortConv + SiLU, history carried (:889-892)  kda_layer_pre, one launch for
 //   3   L2 on q and k per head, eps 1e-6 (:895-899)   steps 2-5
 //   4/5 beta = sigmoid, decay chain (:902-906)
 //   6   recurrence, q * D^-0.5 (:908-938)           k3cuda_kda_decode / k3cuda_kda_prefill
 //   7/8 head RMSNorm, then * sigmoid(g x) (:941-947) kda_layer_post (g x is formed in step 1)
-//   9   o_proj (:948)                               matvec_rows or cuBLAS
+//   9   o_proj (:948)                               matvec_rows or gemm
 //
 // Projections. Activations are fp32 as in the reference, weights fp32 or bf16 (the wdt tag).
 // With T <= 8 tokens every weight is used at most 8 times, so a projection is weight
 // streaming: matvec_rows reads each weight row once with 16-byte streaming loads and forms
 // the T dot products from exact fp32 products summed in fp32, bound by HBM. The first
 // projections of the layer (q, k, v, g, b, f_a all read the same x) go out as ONE launch
-// over a table of weight matrices. With T > 8 a projection is a GEMM and goes to cuBLAS
-// (opened with dlopen, like NCCL): fp32 weights through SGEMM; bf16 weights with the fp32
-// activations split into bf16 hi + lo halves (x = hi + lo to 2^-16 relative), two bf16
-// GEMMs accumulating into one fp32 result, so x is not rounded to bf16.
-#include <cublas_v2.h>  // types and enumerators only: the library is opened with dlopen
-#include <dlfcn.h>
-
-#include <mutex>
-
+// over a table of weight matrices. With T > 8 a projection is a GEMM (gemm.cu): bf16
+// weights on tcgen05 with the fp32 activations split into bf16 hi + lo halves (x = hi + lo
+// to 2^-16 relative) whose products accumulate into one fp32 tile, so x is not rounded to
+// bf16; fp32 weights on the CUDA cores.
 #include "internal.cuh"
 
 namespace k3 {
-
-// ------------------------------------------------------------------------- cuBLAS
-struct BlasApi {
-    void *handle = nullptr;
-    cublasStatus_t (*Create)(cublasHandle_t *) = nullptr;
-    cublasStatus_t (*Destroy)(cublasHandle_t) = nullptr;
-    cublasStatus_t (*SetStream)(cublasHandle_t, cudaStream_t) = nullptr;
-    cublasStatus_t (*Sgemm)(cublasHandle_t, cublasOperation_t, cublasOperation_t, int, int,
-                            int, const float *, const float *, int, const float *, int,
-                            const float *, float *, int) = nullptr;
-    cublasStatus_t (*GemmEx)(cublasHandle_t, cublasOperation_t, cublasOperation_t, int, int,
-                             int, const void *, const void *, cudaDataType, int, const void *,
-                             cudaDataType, int, const void *, void *, cudaDataType, int,
-                             cublasComputeType_t, cublasGemmAlgo_t) = nullptr;
-};
-static BlasApi g_blas;
-static std::mutex g_blas_mu;
-
-static int blas_load() {
-    std::lock_guard<std::mutex> lk(g_blas_mu);
-    if (g_blas.handle) return K3CUDA_OK;
-    void *h = dlopen("libcublas.so.12", RTLD_NOW | RTLD_GLOBAL);
-    if (!h) h = dlopen("/usr/local/cuda/lib64/libcublas.so.12", RTLD_NOW | RTLD_GLOBAL);
-    if (!h) return set_error(K3CUDA_ERR_UNSUPPORTED, "cannot load libcublas.so.12: %s", dlerror());
-#define K3_SYM(field, name)                                                              \
-    g_blas.field = (decltype(g_blas.field))dlsym(h, name);                               \
-    if (!g_blas.field) return set_error(K3CUDA_ERR_UNSUPPORTED, "libcublas lacks %s", name);
-    K3_SYM(Create, "cublasCreate_v2");
-    K3_SYM(Destroy, "cublasDestroy_v2");
-    K3_SYM(SetStream, "cublasSetStream_v2");
-    K3_SYM(Sgemm, "cublasSgemm_v2");
-    K3_SYM(GemmEx, "cublasGemmEx");
-#undef K3_SYM
-    g_blas.handle = h;
-    return K3CUDA_OK;
-}
-
-static int blas_handle(k3cuda_ctx *ctx, cublasHandle_t *out) {
-    int rc = blas_load();
-    if (rc) return rc;
-    if (!ctx->blas) {
-        cublasHandle_t hd = nullptr;
-        if (g_blas.Create(&hd) != CUBLAS_STATUS_SUCCESS)
-            return set_error(K3CUDA_ERR_CUDA, "cublasCreate failed");
-        ctx->blas = hd;
-    }
-    if (g_blas.SetStream((cublasHandle_t)ctx->blas, ctx->stream) != CUBLAS_STATUS_SUCCESS)
-        return set_error(K3CUDA_ERR_CUDA, "cublasSetStream failed");
-    *out = (cublasHandle_t)ctx->blas;
-    return K3CUDA_OK;
-}
 
 // sigmoid with the fast exponential and the hardware reciprocal (rcp.approx, no slow
 // path): within a few ulp of 1 / (1 + expf(-x)) (the reference's sigmoidf_), and exactly 0
@@ -322,33 +266,6 @@ int split(k3cuda_ctx *ctx, __nv_bfloat16 *xs, const float *x, long long n) {
     const int blocks = (int)(want < 8LL * ctx->sm_count ? want : 8LL * ctx->sm_count);
     split_bf16<<<blocks, 256, 0, ctx->stream>>>(xs, xs + n, x, n);
     return after_launch(ctx, "split_bf16");
-}
-
-// y [T][out] = x [T][in] W^T through cuBLAS (column-major: y^T = W^T' x^T with W read
-// transposed). xs = the bf16 hi/lo split of x ([2][T][in]) when W is bf16.
-int gemm(k3cuda_ctx *ctx, float *y, const float *x, const __nv_bfloat16 *xs,
-                const void *W, int wdt, int T, int in, int out) {
-    cublasHandle_t h = nullptr;
-    int rc = blas_handle(ctx, &h);
-    if (rc) return rc;
-    const float one = 1.f, zero = 0.f;
-    cublasStatus_t st;
-    if (wdt == K3CUDA_F32) {
-        st = g_blas.Sgemm(h, CUBLAS_OP_T, CUBLAS_OP_N, out, T, in, &one, (const float *)W, in, x,
-                          in, &zero, y, out);
-    } else {
-        st = g_blas.GemmEx(h, CUBLAS_OP_T, CUBLAS_OP_N, out, T, in, &one, W, CUDA_R_16BF, in, xs,
-                           CUDA_R_16BF, in, &zero, y, CUDA_R_32F, out, CUBLAS_COMPUTE_32F,
-                           CUBLAS_GEMM_DEFAULT);
-        if (st == CUBLAS_STATUS_SUCCESS)
-            st = g_blas.GemmEx(h, CUBLAS_OP_T, CUBLAS_OP_N, out, T, in, &one, W, CUDA_R_16BF, in,
-                               xs + (size_t)T * in, CUDA_R_16BF, in, &one, y, CUDA_R_32F, out,
-                               CUBLAS_COMPUTE_32F, CUBLAS_GEMM_DEFAULT);
-    }
-    if (st != CUBLAS_STATUS_SUCCESS)
-        return set_error(K3CUDA_ERR_CUDA, "cuBLAS GEMM %dx%dx%d failed (status %d)", T, out, in,
-                         (int)st);
-    return K3CUDA_OK;
 }
 
 // ------------------------------------------------------------ vector lane access
@@ -794,10 +711,7 @@ static int layer_core(k3cuda_ctx *ctx, float *out, const float *x, const k3cuda_
 
 using namespace k3;
 
-extern "C" void k3cuda_blas_destroy_internal(k3cuda_ctx *ctx) {
-    if (ctx && ctx->blas && g_blas.Destroy) g_blas.Destroy((cublasHandle_t)ctx->blas);
-    if (ctx) ctx->blas = nullptr;
-}
+
 
 extern "C" int k3cuda_matmul_workspace(int T, int in, int wdt, size_t *bytes) {
     K3_ARG_CHECK(bytes && T >= 0 && in >= 0, "bad matmul workspace query");

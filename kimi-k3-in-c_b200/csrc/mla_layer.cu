@@ -10,7 +10,8 @@
 //   causal attention, scale (qk_nope+qk_rope)^-0.5 (:381-411) mla_attend_kvb (absorbed form)
 //   acc *= sigmoid(g x) (when g), out = o acc (:413-420)      mla_gate; projection
 //
-// Projections go through the same streaming / cuBLAS paths as the KDA layer (kda_layer.cu).
+// Projections go through the same streaming / GEMM paths as the KDA layer (kda_layer.cu,
+// gemm.cu).
 #include "internal.cuh"
 
 namespace k3 {

@@ -13,8 +13,9 @@
 // scale folding).
 //
 // More rows of x (a prefill's tokens routed to one expert): the weights are expanded to
-// bf16 (exact: 3 significant bits and an fp32-range exponent) and multiplied by cuBLAS
-// against x split into bf16 hi + lo halves, the same near-fp32 scheme as the bf16 trunk.
+// bf16 (exact: 3 significant bits and an fp32-range exponent) and multiplied on tcgen05
+// (gemm.cu) against x split into bf16 hi + lo halves, the same near-fp32 scheme as the bf16
+// trunk.
 #include <cuda_fp16.h>
 
 #include "internal.cuh"

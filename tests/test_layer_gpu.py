@@ -47,10 +47,13 @@ def _run_layer(ctx, dev, wdt, x, H, D, K, lb, eps, state, io):
 
 @pytest.mark.parametrize("wdt", [0, 1])
 @pytest.mark.parametrize("T,n_in,n_out", [(1, 128, 96), (2, 1024, 300), (8, 7168, 130),
-                                          (9, 256, 96), (40, 1024, 300)])
+                                          (9, 256, 96), (40, 1024, 300), (128, 64, 256),
+                                          (129, 7168, 700), (300, 1536, 40), (1000, 512, 1031),
+                                          (33, 16, 64), (77, 200, 99)])
 def test_matmul_matches_double(ctx, wdt, T, n_in, n_out):
-    """y = x W^T for the matvec kernel (T <= 8) and the cuBLAS path (T > 8), fp32 and bf16
-    weights, row counts that leave partial row groups, against float64."""
+    """y = x W^T for the matvec kernel (T <= 8) and the GEMMs (T > 8: tcgen05 over x's bf16
+    hi/lo halves for bf16 weights with in % 64 == 0, the CUDA-core kernel for fp32 weights
+    and other widths), fp32 and bf16 weights, partial token and row tiles, against float64."""
     import k3cuda
     rng = np.random.default_rng(T * 7 + n_out + wdt)
     x = rng.standard_normal((T, n_in)).astype(np.float32)
@@ -101,7 +104,7 @@ def test_layer_matches_reference_fixture(ctx, golden, name):
 @pytest.mark.parametrize("wdt", [0, 1])
 def test_layer_carried_state_matches_oracle(ctx, wdt, io):
     """D = 128 over a sequence of calls carrying the state (recurrent and conv history):
-    prefill lengths on the cuBLAS path (70, 130, 9), decode (1), and calls shorter than the
+    prefill lengths on the GEMM path (70, 130, 9), decode (1), and calls shorter than the
     conv history (1, 2) on the matvec path; every output and the final state."""
     rng = np.random.default_rng(60 + 2 * wdt + io)
     E, H, D, K = 256, 2, 128, 4
