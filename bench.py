@@ -543,6 +543,17 @@ def prefill_record(args, D: Dist, which, tokens=None, cpu=True):
     }
     if check:
         rec["check"] = check
+    if gather:
+        # the exchange: every rank receives the other ranks' heads of the whole output; its
+        # floor is those bytes over one GPU's NVLink ingress (the measured 770 GB/s peer copy)
+        recv = (R - 1) * T * Hl * d * 2
+        t_x = max(ms - ms_compute, 1e-6) / 1e3 / args.steps
+        rec["exchange"] = {"bytes_received_per_gpu": recv, "ms_per_step": t_x * 1e3,
+                           "achieved_gbs": recv / t_x / 1e9, "peak_gbs": 770.0,
+                           "frac": recv / t_x / 1e9 / 770.0,
+                           "floor_ms": recv / 770e9 * 1e3,
+                           "basis": "time with the exchange minus compute-only time; peak = "
+                                    "measured NVLink peer copy per direction per GPU"}
     ctx.close()
     if cpu_c is not None:
         rec["cpu_baseline"] = cpu_prefill_baseline(cpu_c, H_total)
@@ -578,6 +589,9 @@ def mla_record(args, D: Dist, cpu=True):
     R = D.world
     B_all, ctxlen, H = 64, 8192, 128
     B = B_all // R
+    if getattr(args, "batch", None):  # a rank's share of a larger job, for profiling
+        B = args.batch
+        B_all = B * R
     c = W.mla_config4(seed=D.rank, B=B, ctx=ctxlen, H=H)
     ctx = k3cuda.Context(D.local)
     d = [ctx.upload(c[x]) for x in ("q_nope", "q_rope", "latent", "rope", "w_uk", "w_uv")]
@@ -1230,6 +1244,9 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-subrecords", action="store_true",
                     help="decode: print the headline alone, without the config-2/3/4 records")
+    ap.add_argument("--batch", type=int, default=None,
+                    help="mla: sequences per GPU in place of 64 / N (a profiling case: the "
+                         "per-GPU share of config 4 at more GPUs)")
     ap.add_argument("--tokens", type=int, default=None,
                     help="prefill: sequence length in place of config 2's 32768 (a small case "
                          "for kernel profiling; not a headline number); layer: tokens per call")

@@ -36,8 +36,10 @@ __device__ __forceinline__ bool all_wait(uint64_t *bar, uint32_t parity, unsigne
     return __all_sync(0xffffffffu, mbar_wait(bar, parity, err, code));
 }
 
-// CTA (n, m): tokens [128 m, +128) x weight rows [256 n, +256). Rows past T or out are
-// zero-filled by TMA and never stored.
+// CTA (m, n): tokens [128 m, +128) x weight rows [256 n, +256). The token tiles vary
+// fastest, so the CTAs that share a weight tile run together and the weight streams from
+// DRAM about once (x, a few tens of MB, stays in L2). Rows past T or out are zero-filled
+// by TMA and never stored.
 __global__ void __launch_bounds__(128, 1)
 proj_gemm_tc(const __grid_constant__ GemmMaps maps, float *__restrict__ y, int T, int in,
              int out, unsigned *__restrict__ err) {
@@ -45,7 +47,7 @@ proj_gemm_tc(const __grid_constant__ GemmMaps maps, float *__restrict__ y, int T
     uint8_t *sm = (uint8_t *)(((uintptr_t)smraw + 1023) & ~(uintptr_t)1023);
     __shared__ uint64_t bar_full[GT_NS], bar_empty[GT_NS], bar_mma;
     __shared__ uint32_t tslot;
-    const int n0 = blockIdx.x * GT_N, t0 = blockIdx.y * GT_M;
+    const int t0 = blockIdx.x * GT_M, n0 = blockIdx.y * GT_N;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int KB = in / GT_K;
     if (tid == 0) {
@@ -199,7 +201,7 @@ int gemm(k3cuda_ctx *ctx, float *y, const float *x, const __nv_bfloat16 *xs, con
                               GT_K, GT_N);
         if (rc) return rc;
         if ((rc = set_smem(proj_gemm_tc, GT_SMEM))) return rc;
-        const dim3 grid((out + GT_N - 1) / GT_N, (T + GT_M - 1) / GT_M);
+        const dim3 grid((T + GT_M - 1) / GT_M, (out + GT_N - 1) / GT_N);
         proj_gemm_tc<<<grid, 128, GT_SMEM, ctx->stream>>>(maps, y, T, in, out, ctx->err_word);
         return after_launch(ctx, "proj_gemm_tc");
     }

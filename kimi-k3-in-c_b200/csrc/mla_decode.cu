@@ -755,7 +755,10 @@ template <typename OUT>
 __global__ void __launch_bounds__(256)
 mla_project_small(const __nv_bfloat16 *__restrict__ olat2, const __nv_bfloat16 *__restrict__ w_uv,
                   long long uv_head_elems, OUT *__restrict__ out, int B, int H) {
-    __shared__ float os[MLA_SMALL_B][MLA_DL];
+    // o_lat rows with one pad float after every 16: lane l reads elements 16 l .. 16 l + 15,
+    // at 17 l .. 17 l + 15, so the 32 lanes of a read fall in 32 different banks
+    constexpr int OSW = MLA_DL + MLA_DL / 16;
+    __shared__ float os[MLA_SMALL_B][OSW];
     pdl_trigger();
     const int h = blockIdx.x, z = blockIdx.y, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int j0 = 16 * z + 2 * warp;
@@ -769,8 +772,9 @@ mla_project_small(const __nv_bfloat16 *__restrict__ olat2, const __nv_bfloat16 *
     pdl_wait();  // the weights above are never written by the chain; o_lat is
     for (int e = tid; e < B * MLA_DL; e += 256) {
         const __nv_bfloat16 *src = olat2 + ((size_t)(e / MLA_DL) * H + h) * 2 * MLA_DL;
-        os[e / MLA_DL][e % MLA_DL] =
-            __bfloat162float(src[e % MLA_DL]) + __bfloat162float(src[MLA_DL + e % MLA_DL]);
+        const int c = e % MLA_DL;
+        os[e / MLA_DL][c + c / 16] =
+            __bfloat162float(src[c]) + __bfloat162float(src[MLA_DL + c]);
     }
     __syncthreads();
 #pragma unroll
@@ -788,7 +792,7 @@ mla_project_small(const __nv_bfloat16 *__restrict__ olat2, const __nv_bfloat16 *
         for (int b = 0; b < B; b++) {
             float v = 0.f;
 #pragma unroll
-            for (int x = 0; x < 16; x++) v = fmaf(os[b][16 * lane + x], wf[x], v);
+            for (int x = 0; x < 16; x++) v = fmaf(os[b][17 * lane + x], wf[x], v);
 #pragma unroll
             for (int o = 16; o; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
             if (lane == 0) io<OUT>::st(out + ((size_t)b * H + h) * MLA_DV + j0 + r, v);
