@@ -179,3 +179,41 @@ def test_mla_work_plan_segments():
             assert need <= q, (len(lens), mc, need, q)
     nseg, ncl, _ = _mla_plan(np.array([8192]))
     assert ncl == 32 and nseg == 32
+
+
+def test_dropin_structs_match_the_reference_layout(tmp_path):
+    """k3g_cfg / k3g_kda_weights / k3g_mla_weights are K3Cfg / K3KdaW / K3MlaW field for field
+    (the drop-ins are called through a cast): compile-time checks against the reference's own
+    header, when a reference checkout is available to compile against."""
+    import shutil
+    import subprocess
+    ref = os.environ.get("K3_REFERENCE_DIR", "/root/reference")
+    hdr = os.path.join(ref, "include", "k3", "k3.h")
+    if not os.path.isfile(hdr) or not shutil.which("gcc"):
+        pytest.skip("no reference checkout to compile against")
+    src = tmp_path / "layout.c"
+    fields = {"K3Cfg": ("k3g_cfg", ["hidden", "n_layers", "vocab", "rms_eps", "kda_heads",
+                                    "kda_head_dim", "conv_k", "gate_lb", "n_heads", "q_lora",
+                                    "kv_lora", "qk_nope", "qk_rope", "v_head", "mla_out_gate",
+                                    "n_experts", "topk", "n_shared", "latent", "moe_inter",
+                                    "routed_scale", "moe_renorm", "latent_norm", "first_dense",
+                                    "dense_inter", "attn_res_block", "situ_b1", "situ_b2",
+                                    "n_full_attn", "full_attn"]),
+              "K3KdaW": ("k3g_kda_weights", ["q", "k", "v", "q_conv", "k_conv", "v_conv", "f_a",
+                                             "f_b", "A_log", "dt_bias", "b", "g", "o_norm", "o",
+                                             "wdt"]),
+              "K3MlaW": ("k3g_mla_weights", ["q_a", "q_b", "kv_a", "kv_b", "o", "g", "q_a_norm",
+                                             "kv_a_norm", "wdt"])}
+    lines = ["#include <stddef.h>", '#include "k3.h"', '#include "k3_gpu.h"']
+    for ref_t, (our_t, names) in fields.items():
+        lines.append(f'_Static_assert(sizeof({ref_t}) == sizeof({our_t}), "{ref_t} size");')
+        for n in names:
+            lines.append(f"_Static_assert(offsetof({ref_t}, {n}) == offsetof({our_t}, {n}) && "
+                         f"sizeof((({ref_t} *)0)->{n}) == sizeof((({our_t} *)0)->{n}), "
+                         f'"{ref_t}.{n}");')
+    src.write_text("\n".join(lines) + "\n")
+    inc = [f"-I{ref}/include", f"-I{ref}/include/k3", f"-I{ref}/third_party",
+           f"-I{os.path.join(ROOT, 'include')}"]
+    r = subprocess.run(["gcc", "-std=gnu99", "-fsyntax-only", *inc, str(src)],
+                       capture_output=True, text=True)
+    assert r.returncode == 0, r.stderr
