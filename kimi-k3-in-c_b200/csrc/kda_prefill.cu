@@ -30,6 +30,8 @@
 
 #include <string.h>
 
+#include <algorithm>
+
 #include "internal.cuh"
 
 namespace k3 {
@@ -293,8 +295,12 @@ static int count_chunks(const int *cu, int n_seq, long long *nc) {
     return K3CUDA_OK;
 }
 
+// chunk table, then the sequences' first-chunk offsets [n_seq + 1] and the sequences in
+// descending chunk count [n_seq] (the order the tensor-core scan takes them: the longest
+// chains start first and the short ones fill in behind them)
 static size_t table_bytes(long long nc, int n_seq) {
-    return align256((size_t)nc * sizeof(ChunkDesc)) + align256((size_t)(n_seq + 1) * sizeof(int));
+    return align256((size_t)nc * sizeof(ChunkDesc)) +
+           align256((size_t)(2 * n_seq + 1) * sizeof(int));
 }
 
 template <typename IO, int DK>
@@ -304,7 +310,7 @@ static int run_prefill(k3cuda_ctx *ctx, float *state, void *o, const void *q, co
                        void *workspace, const GatherOut *go = nullptr) {
     using L = PrefillLayout<DK>;
     std::vector<ChunkDesc> table((size_t)nc);
-    std::vector<int> c0((size_t)n_seq + 1);
+    std::vector<int> c0((size_t)2 * n_seq + 1);
     long long c = 0;
     for (int n = 0; n < n_seq; n++) {
         c0[n] = (int)c;
@@ -314,6 +320,14 @@ static int run_prefill(k3cuda_ctx *ctx, float *state, void *o, const void *q, co
         }
     }
     c0[n_seq] = (int)c;
+    {
+        std::vector<int> ord((size_t)n_seq);
+        for (int n = 0; n < n_seq; n++) ord[(size_t)n] = n;
+        std::stable_sort(ord.begin(), ord.end(), [&](int a, int b) {
+            return c0[(size_t)a + 1] - c0[(size_t)a] > c0[(size_t)b + 1] - c0[(size_t)b];
+        });
+        for (int n = 0; n < n_seq; n++) c0[(size_t)n_seq + 1 + n] = ord[(size_t)n];
+    }
     char *wsb = (char *)workspace;
     ChunkDesc *d_table = (ChunkDesc *)wsb;
     int *d_c0 = (int *)(wsb + align256((size_t)nc * sizeof(ChunkDesc)));
@@ -322,7 +336,7 @@ static int run_prefill(k3cuda_ctx *ctx, float *state, void *o, const void *q, co
         // the chunk table and the sequence offsets are adjacent: one image, one copy
         std::vector<unsigned char> img(table_bytes(nc, n_seq), 0);
         if (nc > 0) memcpy(img.data(), table.data(), (size_t)nc * sizeof(ChunkDesc));
-        memcpy(img.data() + ((char *)d_c0 - wsb), c0.data(), (size_t)(n_seq + 1) * sizeof(int));
+        memcpy(img.data() + ((char *)d_c0 - wsb), c0.data(), c0.size() * sizeof(int));
         if (int rc = stage_h2d(ctx, wsb, img.data(), img.size())) return rc;
     }
     if constexpr (std::is_same<IO, __nv_bfloat16>::value && DK == 128) {

@@ -775,7 +775,8 @@ __device__ __forceinline__ bool warp_wait_all(uint64_t *bar, uint32_t parity, un
 template <int DVT>
 __global__ void __launch_bounds__(192, 1)
 kda_scan_tc(const __grid_constant__ ScanMaps maps, const TcChunk *__restrict__ chunks,
-            const int *__restrict__ seq_chunk0, const uint8_t *__restrict__ ws,
+            const int *__restrict__ seq_chunk0, const int *__restrict__ seq_order,
+            const uint8_t *__restrict__ ws,
             float *__restrict__ state, __nv_bfloat16 *__restrict__ o, int H,
             const __grid_constant__ GatherOut go, unsigned *__restrict__ err) {
     using C = ScanCfg<DVT>;
@@ -785,7 +786,9 @@ kda_scan_tc(const __grid_constant__ ScanMaps maps, const TcChunk *__restrict__ c
     __shared__ uint64_t op_full[2], op_empty[2], s_done, o_done[2], s16_ready;
     __shared__ uint32_t tslot;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const int slice = blockIdx.x % NT, h = (blockIdx.x / NT) % H, n = blockIdx.x / (NT * H);
+    // sequences in descending chunk count: the longest chains are scheduled first
+    const int slice = blockIdx.x % NT, h = (blockIdx.x / NT) % H;
+    const int n = seq_order[blockIdx.x / (NT * H)];
     const int c0 = seq_chunk0[n], nc = seq_chunk0[n + 1] - c0;
     const int col0 = DVT * slice;
     constexpr uint32_t TM_S = 0, TM_O = DVT;
@@ -1014,7 +1017,8 @@ kda_scan_tc(const __grid_constant__ ScanMaps maps, const TcChunk *__restrict__ c
 size_t prefill_tc_block_bytes() { return WB_BYTES; }
 
 // Launch both phases. `blocks` has room for nc * H blocks of WB_BYTES; d_table / d_c0 are
-// the device copies of the chunk table and of the per-sequence first-chunk index.
+// the device copies of the chunk table and of the per-sequence first-chunk index [n_seq + 1],
+// followed by the sequences in descending chunk count [n_seq].
 int run_prefill_tc(k3cuda_ctx *ctx, float *state, void *o, const void *q, const void *k,
                    const void *v, const float *gate, const float *beta, int total_tokens,
                    int n_seq, int H, float q_scale, int gate_is_log, long long nc,
@@ -1055,14 +1059,14 @@ int run_prefill_tc(k3cuda_ctx *ctx, float *state, void *o, const void *q, const 
         using C = ScanCfg<128>;
         if (int rc_ = set_smem(kda_scan_tc<128>, C::SMEM)) return rc_;
         kda_scan_tc<128><<<(unsigned)((long long)n_seq * H), 192, C::SMEM, ctx->stream>>>(
-            sm, (const TcChunk *)d_table, d_c0, b, state, (__nv_bfloat16 *)o, H, gout,
-            ctx->err_word);
+            sm, (const TcChunk *)d_table, d_c0, d_c0 + n_seq + 1, b, state, (__nv_bfloat16 *)o,
+            H, gout, ctx->err_word);
     } else {
         using C = ScanCfg<64>;
         if (int rc_ = set_smem(kda_scan_tc<64>, C::SMEM)) return rc_;
         kda_scan_tc<64><<<(unsigned)((long long)n_seq * H * 2), 192, C::SMEM, ctx->stream>>>(
-            sm, (const TcChunk *)d_table, d_c0, b, state, (__nv_bfloat16 *)o, H, gout,
-            ctx->err_word);
+            sm, (const TcChunk *)d_table, d_c0, d_c0 + n_seq + 1, b, state, (__nv_bfloat16 *)o,
+            H, gout, ctx->err_word);
     }
     return after_launch(ctx, "kda_scan_tc");
 }
