@@ -187,7 +187,11 @@ def test_dropin_structs_match_the_reference_layout(tmp_path):
     header, when a reference checkout is available to compile against."""
     import shutil
     import subprocess
-    ref = os.environ.get("K3_REFERENCE_DIR", "/root/reference")
+    ref = os.environ.get("K3_REFERENCE_DIR", "")
+    rec = os.path.join(ROOT, "oracle", "_ref", "refdir.txt")  # where the oracle was built from
+    if not ref and os.path.exists(rec):
+        with open(rec) as f:
+            ref = f.read().strip()
     hdr = os.path.join(ref, "include", "k3", "k3.h")
     if not os.path.isfile(hdr) or not shutil.which("gcc"):
         pytest.skip("no reference checkout to compile against")
