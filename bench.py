@@ -440,21 +440,25 @@ def prefill_record(args, D: Dist, which, tokens=None, cpu=True):
     cu = c["cu_seqlens"]
     T, nseq = int(cu[-1]), len(cu) - 1
     ctx = k3cuda.Context(D.local)
-    bf = W.f32_to_bf16
-    hq, hk, hv = (ctx.pinned((T, Hl, d), np.uint16) for _ in range(3))
+    f32 = getattr(args, "io", "bf16") == "f32"  # fp32 q/k/v/o: the CUDA-core chunk kernels
+    if f32 and R > 1:
+        raise ValueError("--io f32 runs on one GPU (the gathered exchange is bf16)")
+    et = np.float32 if f32 else np.uint16
+    cv = (lambda a: a) if f32 else W.f32_to_bf16
+    hq, hk, hv = (ctx.pinned((T, Hl, d), et) for _ in range(3))
     hg = ctx.pinned((T, Hl, d), np.float32)
     hb = ctx.pinned((T, Hl), np.float32)
-    hq[...], hk[...], hv[...], hg[...], hb[...] = bf(c["q"]), bf(c["k"]), bf(c["v"]), c["g"], c["beta"]
+    hq[...], hk[...], hv[...], hg[...], hb[...] = cv(c["q"]), cv(c["k"]), cv(c["v"]), c["g"], c["beta"]
     cpu_c = c if (cpu and R == 1 and D.rank == 0 and not args.no_cpu_baseline) else None
     del c
-    dq, dk, dv = (ctx.empty((T, Hl, d), np.uint16) for _ in range(3))
+    dq, dk, dv = (ctx.empty((T, Hl, d), et) for _ in range(3))
     dg, db = ctx.empty((T, Hl, d), np.float32), ctx.empty((T, Hl), np.float32)
     h2d = [(dq, hq), (dk, hk), (dv, hv), (dg, hg), (db, hb)]
     L = k3cuda.lib()
     for dbuf, h in h2d:
         k3cuda.check(L.k3cuda_memcpy_h2d(ctx.h, dbuf.ptr, h.ctypes.data, h.nbytes))
     dS = ctx.empty((nseq, Hl, d, d), np.float32)
-    dloc = ctx.empty((T, Hl, d), np.uint16)
+    dloc = ctx.empty((T, Hl, d), et)
     nws = ctx.kda_prefill_workspace(cu, Hl, d, d)
     ws = ctx.empty((nws,), np.uint8)
     qs = 1.0 / np.sqrt(np.float32(d))
@@ -465,9 +469,11 @@ def prefill_record(args, D: Dist, which, tokens=None, cpu=True):
         dfull = ctx.empty((T, H_total, d), np.uint16)
         ctx.comm_register_full(dfull)
 
+    io = k3cuda.F32 if f32 else k3cuda.BF16
+
     def step_local():
         dS.zero()
-        ctx.kda_prefill(dS, dloc, dq, dk, dv, dg, db, cu, Hl, d, d, qs, ws, nws)
+        ctx.kda_prefill(dS, dloc, dq, dk, dv, dg, db, cu, Hl, d, d, qs, ws, nws, io_dtype=io)
 
     def step_gather():
         dS.zero()
@@ -516,8 +522,11 @@ def prefill_record(args, D: Dist, which, tokens=None, cpu=True):
     ms_e2e = timed_e2e(ctx, D, e2e_step, args.steps, args.warmup)
     hbm, tf, src = peaks()
     per = ms_compute / 1e3 / args.steps
-    alg = prefill_bytes(T, Hl, d)
+    # fp32 q, k, v and o move twice the bytes of bf16 ones
+    alg = prefill_bytes(T, Hl, d) + (4 * T * Hl * d * 2 if f32 else 0)
     name = cfg["name"] if not tokens else f"kda_prefill_T{T}_reduced"
+    if f32:
+        name += "_fp32io"
     rec = {
         "metric": f"KDA chunked prefill tokens/s ({name})",
         "value": T * args.steps / (ms / 1e3), "unit": "tokens/s", "n_gpus": R,
@@ -527,7 +536,8 @@ def prefill_record(args, D: Dist, which, tokens=None, cpu=True):
         "higher_is_better": True, "scaling": "strong", "dtype": "mixed",
         "config": {"workload": name, "tokens": T, "sequences": nseq, "heads_total": H_total,
                    "heads_per_gpu": Hl, "d": d, "chunk": 64,
-                   "io": "bf16 q/k/v/o, fp32 g/beta/state",
+                   "io": ("fp32 q/k/v/o/g/beta/state (CUDA-core chunk kernels)" if f32 else
+                          "bf16 q/k/v/o, fp32 g/beta/state"),
                    "parallelism": f"head-shard x{R}" + (", output exchange fused into the "
                                                         "prefill (peer stores over NVLink)"
                                                         if gather else ""),
@@ -1244,6 +1254,9 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-subrecords", action="store_true",
                     help="decode: print the headline alone, without the config-2/3/4 records")
+    ap.add_argument("--io", default="bf16", choices=["bf16", "f32"],
+                    help="prefill / varlen: the q/k/v/o element type (f32: the CUDA-core chunk "
+                         "kernels the fp32 drop-ins use; one GPU)")
     ap.add_argument("--batch", type=int, default=None,
                     help="mla: sequences per GPU in place of 64 / N (a profiling case: the "
                          "per-GPU share of config 4 at more GPUs)")
