@@ -14,7 +14,7 @@
 //   kda_chunk_intra  one CTA per (chunk, head), all chunks in parallel: G, Akk, Aqk with
 //                    16-token sub-block anchors, M = (I + Akk)^-1 diag(beta) by forward
 //                    substitution, and the scaled operands Qtil, Ktil, Kbar, e^G_C.
-//   kda_chunk_scan   one CTA per (sequence, head, 16-column slice of d_v): walks the
+//   kda_chunk_scan   one CTA per (sequence, head, 32-column slice of d_v): walks the
 //                    sequence's chunks in order with its state slice in shared memory:
 //                    X = V - Ktil S; Delta = M X; O = Qtil S + Aqk Delta;
 //                    S = e^G_C S + Kbar^T Delta.
@@ -45,7 +45,7 @@ size_t prefill_tc_block_bytes();
 
 constexpr int KC = 64;        // chunk length
 constexpr int KSUB = 16;      // anchor sub-block
-constexpr int SCAN_DVT = 16;  // d_v columns per scan CTA
+constexpr int SCAN_NC = 32;   // d_v columns per scan CTA
 
 struct ChunkDesc {
     int seq;    // sequence index
@@ -72,6 +72,11 @@ __device__ __forceinline__ float load_gate(const float *p, int gate_is_log) {
 }
 
 // ---------------------------------------------------------------------------- intra
+// One CTA per (chunk, head), 256 threads. Rows of the [KC][DK] tiles are padded to DK + 4
+// floats: the Akk / Aqk products read sixteen different rows of Kh at once, which then fall in
+// different banks. (I + Akk)^-1 is formed blockwise on 16 x 16 blocks: the four diagonal blocks
+// by forward substitution (one lane per column, no barrier between rows), then the blocks below
+// the diagonal, one block diagonal at a time, from T_ij = -T_ii sum_{k=j}^{i-1} A_ik T_kj.
 template <typename IO, int DK>
 __global__ void __launch_bounds__(256, 1)
 kda_chunk_intra(const ChunkDesc *__restrict__ chunks, const IO *__restrict__ q,
@@ -79,42 +84,57 @@ kda_chunk_intra(const ChunkDesc *__restrict__ chunks, const IO *__restrict__ q,
                 const float *__restrict__ beta, float *__restrict__ ws, int H, float q_scale,
                 int gate_is_log) {
     using L = PrefillLayout<DK>;
+    constexpr int LP = DK + 4, NB = KC / KSUB;
     extern __shared__ __align__(16) float sm[];
-    float *sk = sm;                     // [KC][DK]  k
-    float *sq = sk + KC * DK;           // [KC][DK]  q * q_scale
-    float *sG = sq + KC * DK;           // [KC][DK]  cumulative log decay
-    float *sKh = sG + KC * DK;          // [KC][DK]  k_s e^(G_r - G_s) for the current anchor r
-    float *sKa = sKh + KC * DK;         // [KSUB][DK] k_t e^(G_t - G_r)
-    float *sQa = sKa + KSUB * DK;       // [KSUB][DK] q_t e^(G_t - G_r)
-    float *sA = sQa + KSUB * DK;        // [KC][KC]  Akk (beta-scaled, strictly lower)
+    float *sk = sm;                     // [KC][LP]  k
+    float *sq = sk + KC * LP;           // [KC][LP]  q * q_scale
+    float *sG = sq + KC * LP;           // [KC][LP]  cumulative log decay
+    float *sKh = sG + KC * LP;          // [KC][LP]  k_s e^(G_r - G_s) for the current anchor r
+    float *sKa = sKh + KC * LP;         // [KSUB][LP] k_t e^(G_t - G_r)
+    float *sQa = sKa + KSUB * LP;       // [KSUB][LP] q_t e^(G_t - G_r)
+    float *sA = sQa + KSUB * LP;        // [KC][KC]  Akk (beta-scaled, strictly lower)
     float *sAq = sA + KC * KC;          // [KC][KC]  Aqk (lower incl. diagonal)
     float *sT = sAq + KC * KC;          // [KC][KC]  (I + Akk)^-1
     float *sb = sT + KC * KC;           // [KC]      beta
+    float *sP = sKh;                    // [NB-1][KSUB][KSUB] block products (Kh is dead then)
 
     const ChunkDesc cd = chunks[blockIdx.x];
     const int h = blockIdx.y, tid = threadIdx.x;
     float *out = ws + ((size_t)blockIdx.x * H + h) * L::floats;
 
-    for (int e = tid; e < KC * DK; e += 256) {
-        const int t = e / DK, i = e - t * DK;
-        float kv = 0.f, qv = 0.f, gv = 0.f;
-        if (t < cd.len) {
-            const size_t off = ((size_t)(cd.t0 + t) * H + h) * DK + i;
-            kv = io<IO>::ld(k + off);
-            qv = io<IO>::ld(q + off) * q_scale;
-            gv = load_gate(gate + off, gate_is_log);
+    {
+        // every load of a batch is issued before its shared stores
+        constexpr int BATCH = 8;
+        for (int e0 = 0; e0 < KC * DK; e0 += 256 * BATCH) {
+            float kv[BATCH], qv[BATCH], gv[BATCH];
+#pragma unroll
+            for (int u = 0; u < BATCH; u++) {
+                const int e = e0 + u * 256 + tid, t = e / DK, i = e - t * DK;
+                kv[u] = qv[u] = gv[u] = 0.f;
+                if (t < cd.len) {
+                    const size_t off = ((size_t)(cd.t0 + t) * H + h) * DK + i;
+                    kv[u] = io<IO>::ld(k + off);
+                    qv[u] = io<IO>::ld(q + off) * q_scale;
+                    gv[u] = load_gate(gate + off, gate_is_log);
+                }
+            }
+#pragma unroll
+            for (int u = 0; u < BATCH; u++) {
+                const int e = e0 + u * 256 + tid, t = e / DK, i = e - t * DK;
+                sk[t * LP + i] = kv[u];
+                sq[t * LP + i] = qv[u];
+                sG[t * LP + i] = gv[u];
+            }
         }
-        sk[e] = kv;
-        sq[e] = qv;
-        sG[e] = gv;
     }
     if (tid < KC) sb[tid] = tid < cd.len ? beta[(size_t)(cd.t0 + tid) * H + h] : 0.f;
     __syncthreads();
     if (tid < DK) {
         float acc = 0.f;
+#pragma unroll 16
         for (int t = 0; t < KC; t++) {
-            acc += sG[t * DK + tid];
-            sG[t * DK + tid] = acc;
+            acc += sG[t * LP + tid];
+            sG[t * LP + tid] = acc;
         }
     }
     __syncthreads();
@@ -122,164 +142,362 @@ kda_chunk_intra(const ChunkDesc *__restrict__ chunks, const IO *__restrict__ q,
     // scaled operands for the scan (full-chunk anchor at the chunk start)
     for (int e = tid; e < KC * DK; e += 256) {
         const int t = e / DK, i = e - t * DK;
-        const float G = sG[e], GC = sG[(KC - 1) * DK + i];
+        const float G = sG[t * LP + i], GC = sG[(KC - 1) * LP + i];
         const float eg = expf(G);
-        out[L::qt + e] = sq[e] * eg;
-        out[L::kt + e] = sk[e] * eg;
-        out[L::kb + e] = sk[e] * expf(GC - G);
+        out[L::qt + e] = sq[t * LP + i] * eg;
+        out[L::kt + e] = sk[t * LP + i] * eg;
+        out[L::kb + e] = sk[t * LP + i] * expf(GC - G);
     }
-    if (tid < DK) out[L::gc + tid] = expf(sG[(KC - 1) * DK + tid]);
+    if (tid < DK) out[L::gc + tid] = expf(sG[(KC - 1) * LP + tid]);
 
-    // Akk / Aqk, one 16-row sub-block at a time
-    for (int a = 0; a < KC / KSUB; a++) {
+    // Akk / Aqk, one 16-row sub-block at a time; thread (tl, ss) = (tid / 16, tid % 16) forms
+    // row r0 + tl against the columns ss + 16 m, m = 0..a
+#pragma unroll
+    for (int a = 0; a < NB; a++) {
         const int r0 = a * KSUB, ncol = r0 + KSUB;
         int big = 0;
         for (int e = tid; e < ncol * DK; e += 256) {
             const int s = e / DK, i = e - s * DK;
-            const float ex = sG[r0 * DK + i] - sG[e];
+            const float ex = sG[r0 * LP + i] - sG[s * LP + i];
             big |= ex > 80.f;
-            sKh[e] = sk[e] * expf(fminf(ex, 80.f));
+            sKh[s * LP + i] = sk[s * LP + i] * expf(fminf(ex, 80.f));
         }
         for (int e = tid; e < KSUB * DK; e += 256) {
-            const int t = r0 + e / DK, i = e % DK;
-            const float f = expf(sG[t * DK + i] - sG[r0 * DK + i]);
-            sKa[e] = sk[t * DK + i] * f;
-            sQa[e] = sq[t * DK + i] * f;
+            const int tl = e / DK, i = e - tl * DK, t = r0 + tl;
+            const float f = expf(sG[t * LP + i] - sG[r0 * LP + i]);
+            sKa[tl * LP + i] = sk[t * LP + i] * f;
+            sQa[tl * LP + i] = sq[t * LP + i] * f;
         }
         big = __syncthreads_or(big);
-        for (int e = tid; e < KSUB * KC; e += 256) {
-            const int tl = e / KC, s = e - tl * KC, t = r0 + tl;
-            float akk = 0.f, aqk = 0.f;
-            if (s <= t) {
+        const int tl = tid / 16, ss = tid % 16, t = r0 + tl;
+        float akk[NB], aqk[NB];
+#pragma unroll
+        for (int m = 0; m < NB; m++) akk[m] = aqk[m] = 0.f;
+#pragma unroll 2
+        for (int i = 0; i < DK; i += 4) {
+            const float4 ka = *reinterpret_cast<const float4 *>(sKa + tl * LP + i);
+            const float4 qa = *reinterpret_cast<const float4 *>(sQa + tl * LP + i);
+#pragma unroll
+            for (int m = 0; m <= a; m++) {
+                const float4 kh = *reinterpret_cast<const float4 *>(sKh + (ss + 16 * m) * LP + i);
+                akk[m] += ka.x * kh.x;
+                akk[m] += ka.y * kh.y;
+                akk[m] += ka.z * kh.z;
+                akk[m] += ka.w * kh.w;
+                aqk[m] += qa.x * kh.x;
+                aqk[m] += qa.y * kh.y;
+                aqk[m] += qa.z * kh.z;
+                aqk[m] += qa.w * kh.w;
+            }
+        }
+#pragma unroll
+        for (int m = 0; m < NB; m++) {
+            const int s = ss + 16 * m;
+            float vk = 0.f, vq = 0.f;
+            if (m <= a && s <= t) {
+                vk = akk[m];
+                vq = aqk[m];
                 if (big && s >= r0) {
+                    vk = vq = 0.f;
                     for (int i = 0; i < DK; i++) {
-                        const float f = expf(sG[t * DK + i] - sG[s * DK + i]) * sk[s * DK + i];
-                        akk += sk[t * DK + i] * f;
-                        aqk += sq[t * DK + i] * f;
-                    }
-                } else {
-                    const float *ka = sKa + tl * DK, *qa = sQa + tl * DK, *kh = sKh + s * DK;
-                    for (int i = 0; i < DK; i++) {
-                        akk += ka[i] * kh[i];
-                        aqk += qa[i] * kh[i];
+                        const float f = expf(sG[t * LP + i] - sG[s * LP + i]) * sk[s * LP + i];
+                        vk += sk[t * LP + i] * f;
+                        vq += sq[t * LP + i] * f;
                     }
                 }
             }
-            sA[t * KC + s] = s < t ? sb[t] * akk : 0.f;
-            sAq[t * KC + s] = aqk;
+            sA[t * KC + s] = s < t ? sb[t] * vk : 0.f;
+            sAq[t * KC + s] = vq;
         }
         __syncthreads();
     }
 
-    // T = (I + Akk)^-1 by forward substitution, row by row; M = T diag(beta)
-    for (int e = tid; e < KC * KC; e += 256) sT[e] = (e / KC == e % KC) ? 1.f : 0.f;
-    __syncthreads();
-    for (int t = 1; t < KC; t++) {
-        if (tid < t) {
-            const int s = tid;
+    // diagonal blocks of T = (I + Akk)^-1: warp d, lane c < 16 owns column 16 d + c of block d
+    if (tid < 32 * NB && tid % 32 < KSUB) {
+        const int d = tid / 32, c = tid % 32, b0 = d * KSUB;
+        float col[KSUB];
+#pragma unroll
+        for (int r = 0; r < KSUB; r++) {
             float acc = 0.f;
-            for (int j = s; j < t; j++) acc += sA[t * KC + j] * sT[j * KC + s];
-            sT[t * KC + s] = -acc;
+#pragma unroll
+            for (int j = 0; j < r; j++)
+                if (j >= c) acc += sA[(b0 + r) * KC + b0 + j] * col[j];
+            col[r] = r == c ? 1.f : (r > c ? -acc : 0.f);
+        }
+#pragma unroll
+        for (int r = 0; r < KSUB; r++) sT[(b0 + r) * KC + b0 + c] = col[r];
+    }
+    __syncthreads();
+    // blocks below the diagonal, one block diagonal (delta = i - j) at a time
+    for (int delta = 1; delta < NB; delta++) {
+        const int nblk = NB - delta;
+        for (int e = tid; e < nblk * KSUB * KSUB; e += 256) {
+            const int bj = e / (KSUB * KSUB), r = (e / KSUB) % KSUB, c = e % KSUB;
+            const int bi = bj + delta;
+            float acc = 0.f;
+            for (int x = bj * KSUB; x < bi * KSUB; x++)
+                acc += sA[(bi * KSUB + r) * KC + x] * sT[x * KC + bj * KSUB + c];
+            sP[e] = acc;
+        }
+        __syncthreads();
+        for (int e = tid; e < nblk * KSUB * KSUB; e += 256) {
+            const int bj = e / (KSUB * KSUB), r = (e / KSUB) % KSUB, c = e % KSUB;
+            const int bi = bj + delta;
+            const float *P = sP + bj * KSUB * KSUB;
+            float acc = 0.f;
+#pragma unroll
+            for (int x = 0; x < KSUB; x++)
+                acc += sT[(bi * KSUB + r) * KC + bi * KSUB + x] * P[x * KSUB + c];
+            sT[(bi * KSUB + r) * KC + bj * KSUB + c] = -acc;
         }
         __syncthreads();
     }
+    // M = T diag(beta) (zero above the diagonal blocks), and Aqk
     for (int e = tid; e < KC * KC; e += 256) {
-        const int s = e % KC;
-        out[L::m + e] = sT[e] * sb[s];
+        const int t = e / KC, s = e % KC;
+        out[L::m + e] = t / KSUB < s / KSUB ? 0.f : sT[e] * sb[s];
         out[L::aqk + e] = sAq[e];
     }
 }
 
 // ----------------------------------------------------------------------------- scan
+// 16-byte asynchronous copies global -> shared (cp.async): the next chunk's operands stream in
+// while the current chunk computes. A wait_group waits only for this thread's own copies, which
+// complete without any condition on other threads, so no wait here needs a bound.
+__device__ __forceinline__ void cp_async16(float *dst, const float *src) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(
+                     (uint32_t)__cvta_generic_to_shared(dst)),
+                 "l"(src)
+                 : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() {
+    asm volatile("cp.async.commit_group;" ::: "memory");
+}
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+    asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+
+// rows x cols floats (row stride cols in global) into shared rows of stride ld, 256 threads
+template <int ROWS, int COLS, int LD>
+__device__ __forceinline__ void stage_rows(float *dst, const float *src, int tid) {
+    constexpr int Q = COLS / 4;
+#pragma unroll
+    for (int e = tid; e < ROWS * Q; e += 256) {
+        const int r = e / Q, c = e - r * Q;
+        cp_async16(dst + r * LD + 4 * c, src + r * COLS + 4 * c);
+    }
+}
+
+__device__ __forceinline__ void fma4(float (&acc)[4], float a, const float4 &b) {
+    acc[0] += a * b.x;
+    acc[1] += a * b.y;
+    acc[2] += a * b.z;
+    acc[3] += a * b.w;
+}
+
+template <typename IO>
+__device__ __forceinline__ void load4(float (&x)[4], const IO *p) {
+#pragma unroll
+    for (int u = 0; u < 4; u++) x[u] = io<IO>::ld(p + u);
+}
+
+// One CTA per (sequence, head, 32-column slice of d_v), 256 threads. Thread (tx, ty) =
+// (tid % 8, tid / 8) owns columns 4tx..4tx+3 of the slice, the token pair (ty, 63 - ty) in the
+// token phases (the pair's triangular sums in M X and Aqk Delta have 65 terms for every ty,
+// so the eight warps finish those phases together) and state rows (DK/32) ty .. of the update.
+// Operands: Qtil / Ktil rows padded to DK + 4 floats and M / Aqk rows to 68, so the four rows
+// a warp reads at once fall in different banks. Per chunk the copies are three groups, each
+// issued as soon as the phase that read the previous chunk's copy has ended:
+//   G1 = Ktil, Qtil (read in phase A)   G2 = M (phase B)   G3 = Aqk, Kbar, e^G_C (phase C/D)
+// Sums run in the recurrence's order (over i, then over s, ascending), as in the oracle.
 template <typename IO, int DK>
 __global__ void __launch_bounds__(256, 1)
 kda_chunk_scan(const ChunkDesc *__restrict__ chunks, const int *__restrict__ seq_chunk0,
-               const IO *__restrict__ v, const float *__restrict__ ws, float *__restrict__ state,
-               IO *__restrict__ o, int H) {
+               const int *__restrict__ seq_order, const IO *__restrict__ v,
+               const float *__restrict__ ws, float *__restrict__ state, IO *__restrict__ o,
+               int H) {
     using L = PrefillLayout<DK>;
-    constexpr int DV = DK, NT = DV / SCAN_DVT;
+    constexpr int DV = DK, NT = DV / SCAN_NC, LK = DK + 4, LM = KC + 4, RS = DK / 32;
+    static_assert(RS == 2 || RS == 4, "state rows per thread");
     extern __shared__ __align__(16) float sm[];
-    float *sQt = sm;                    // [KC][DK]
-    float *sKt = sQt + KC * DK;         // [KC][DK]
-    float *sKb = sKt + KC * DK;         // [KC][DK]
-    float *sM = sKb + KC * DK;          // [KC][KC]
-    float *sAq = sM + KC * KC;          // [KC][KC]
-    float *sS = sAq + KC * KC;          // [DK][SCAN_DVT]
-    float *sX = sS + DK * SCAN_DVT;     // [KC][SCAN_DVT]
-    float *sD = sX + KC * SCAN_DVT;     // [KC][SCAN_DVT]
-    float *sGc = sD + KC * SCAN_DVT;    // [DK]
+    float *sKt = sm;                    // [KC][LK]  Ktil
+    float *sQt = sKt + KC * LK;         // [KC][LK]  Qtil
+    float *sKb = sQt + KC * LK;         // [KC][DK]  Kbar
+    float *sM = sKb + KC * DK;          // [KC][LM]  M = (I + Akk)^-1 diag(beta)
+    float *sAq = sM + KC * LM;          // [KC][LM]  Aqk
+    float *sGc = sAq + KC * LM;         // [DK]      e^G_C
+    float *sS = sGc + DK;               // [DK][SCAN_NC]  state slice
+    float *sX = sS + DK * SCAN_NC;      // [KC][SCAN_NC]  V - Ktil S
+    float *sD = sX + KC * SCAN_NC;      // [KC][SCAN_NC]  Delta
 
     const int tile = blockIdx.x % NT;
     const int h = (blockIdx.x / NT) % H;
-    const int n = blockIdx.x / (NT * H);
-    const int tid = threadIdx.x, j = tid % SCAN_DVT, r = tid / SCAN_DVT;  // r in 0..15
+    const int n = seq_order[blockIdx.x / (NT * H)];
+    const int tid = threadIdx.x, w = tid / 32, tx = tid % 8, ty = tid / 8;
+    const int ta = ty, tb = KC - 1 - ty, cj = 4 * tx, col0 = tile * SCAN_NC + cj;
     const int c0 = seq_chunk0[n], c1 = seq_chunk0[n + 1];
-    const int col0 = tile * SCAN_DVT;
     float *Sg = state ? state + ((size_t)n * H + h) * DK * DV : nullptr;
 
-    for (int e = tid; e < DK * SCAN_DVT; e += 256) {
-        const int i = e / SCAN_DVT, jj = e % SCAN_DVT;
-        sS[e] = Sg ? Sg[(size_t)i * DV + col0 + jj] : 0.f;
+    float sreg[RS][4];
+#pragma unroll
+    for (int r = 0; r < RS; r++) {
+        const int i = RS * ty + r;
+#pragma unroll
+        for (int u = 0; u < 4; u++) sreg[r][u] = Sg ? Sg[(size_t)i * DV + col0 + u] : 0.f;
+        *reinterpret_cast<float4 *>(sS + i * SCAN_NC + cj) =
+            make_float4(sreg[r][0], sreg[r][1], sreg[r][2], sreg[r][3]);
     }
+
+    auto block = [&](int c) { return ws + ((size_t)c * H + h) * L::floats; };
+    auto issue_g1 = [&](int c) {
+        const float *b = block(c);
+        stage_rows<KC, DK, LK>(sKt, b + L::kt, tid);
+        stage_rows<KC, DK, LK>(sQt, b + L::qt, tid);
+    };
+    auto issue_g2 = [&](int c) { stage_rows<KC, KC, LM>(sM, block(c) + L::m, tid); };
+    auto issue_g3 = [&](int c) {
+        const float *b = block(c);
+        stage_rows<KC, KC, LM>(sAq, b + L::aqk, tid);
+        stage_rows<KC, DK, DK>(sKb, b + L::kb, tid);
+        stage_rows<1, DK, DK>(sGc, b + L::gc, tid);
+    };
+    if (c0 < c1) issue_g1(c0);
+    cp_async_commit();
+    if (c0 < c1) issue_g2(c0);
+    cp_async_commit();
+
     for (int c = c0; c < c1; c++) {
         const ChunkDesc cd = chunks[c];
-        const float *blk = ws + ((size_t)c * H + h) * L::floats;
+        float xa[4] = {0.f, 0.f, 0.f, 0.f}, xb[4] = {0.f, 0.f, 0.f, 0.f};
+        if (ta < cd.len) load4<IO>(xa, v + ((size_t)(cd.t0 + ta) * H + h) * DV + col0);
+        if (tb < cd.len) load4<IO>(xb, v + ((size_t)(cd.t0 + tb) * H + h) * DV + col0);
+        cp_async_wait<1>();  // G1(c)
+        __syncthreads();     // ... for every thread; the previous chunk's phase C/D is over
+        issue_g3(c);
+        cp_async_commit();
+
+        // phase A: Ktil S and Qtil S for tokens ta and tb
+        float ka[4] = {0.f, 0.f, 0.f, 0.f}, kb[4] = {0.f, 0.f, 0.f, 0.f};
+        float qa[4] = {0.f, 0.f, 0.f, 0.f}, qb[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll 4
+        for (int i = 0; i < DK; i += 4) {
+            const float4 Ka = *reinterpret_cast<const float4 *>(sKt + ta * LK + i);
+            const float4 Kb = *reinterpret_cast<const float4 *>(sKt + tb * LK + i);
+            const float4 Qa = *reinterpret_cast<const float4 *>(sQt + ta * LK + i);
+            const float4 Qb = *reinterpret_cast<const float4 *>(sQt + tb * LK + i);
+            const float ka_[4] = {Ka.x, Ka.y, Ka.z, Ka.w}, kb_[4] = {Kb.x, Kb.y, Kb.z, Kb.w};
+            const float qa_[4] = {Qa.x, Qa.y, Qa.z, Qa.w}, qb_[4] = {Qb.x, Qb.y, Qb.z, Qb.w};
+#pragma unroll
+            for (int u = 0; u < 4; u++) {
+                const float4 s = *reinterpret_cast<const float4 *>(sS + (i + u) * SCAN_NC + cj);
+                fma4(ka, ka_[u], s);
+                fma4(kb, kb_[u], s);
+                fma4(qa, qa_[u], s);
+                fma4(qb, qb_[u], s);
+            }
+        }
+#pragma unroll
+        for (int u = 0; u < 4; u++) {
+            xa[u] -= ka[u];
+            xb[u] -= kb[u];
+        }
+        *reinterpret_cast<float4 *>(sX + ta * SCAN_NC + cj) = make_float4(xa[0], xa[1], xa[2], xa[3]);
+        *reinterpret_cast<float4 *>(sX + tb * SCAN_NC + cj) = make_float4(xb[0], xb[1], xb[2], xb[3]);
+        cp_async_wait<1>();  // G2(c)
         __syncthreads();
-        for (int e = tid; e < KC * DK / 4; e += 256) {
-            reinterpret_cast<float4 *>(sQt)[e] = reinterpret_cast<const float4 *>(blk + L::qt)[e];
-            reinterpret_cast<float4 *>(sKt)[e] = reinterpret_cast<const float4 *>(blk + L::kt)[e];
-            reinterpret_cast<float4 *>(sKb)[e] = reinterpret_cast<const float4 *>(blk + L::kb)[e];
+        if (c + 1 < c1) issue_g1(c + 1);
+        cp_async_commit();
+
+        // phase B: Delta = M X; M is lower triangular, so token t sums s = 0..t (the entries
+        // above the diagonal are zeros and the last group of four stops at t's group)
+        float da[4] = {0.f, 0.f, 0.f, 0.f}, db[4] = {0.f, 0.f, 0.f, 0.f};
+        for (int q = 0; q < KC / 4 - w; q++) {
+            const int s = 4 * q;
+            const float4 Mb = *reinterpret_cast<const float4 *>(sM + tb * LM + s);
+            const float mb_[4] = {Mb.x, Mb.y, Mb.z, Mb.w};
+            float4 x[4];
+#pragma unroll
+            for (int u = 0; u < 4; u++)
+                x[u] = *reinterpret_cast<const float4 *>(sX + (s + u) * SCAN_NC + cj);
+#pragma unroll
+            for (int u = 0; u < 4; u++) fma4(db, mb_[u], x[u]);
+            if (q <= w) {
+                const float4 Ma = *reinterpret_cast<const float4 *>(sM + ta * LM + s);
+                const float ma_[4] = {Ma.x, Ma.y, Ma.z, Ma.w};
+#pragma unroll
+                for (int u = 0; u < 4; u++) fma4(da, ma_[u], x[u]);
+            }
         }
-        for (int e = tid; e < KC * KC / 4; e += 256) {
-            reinterpret_cast<float4 *>(sM)[e] = reinterpret_cast<const float4 *>(blk + L::m)[e];
-            reinterpret_cast<float4 *>(sAq)[e] = reinterpret_cast<const float4 *>(blk + L::aqk)[e];
-        }
-        if (tid < DK) sGc[tid] = blk[L::gc + tid];
-        // X = V - Ktil S
-        for (int t = r; t < KC; t += 16) {
-            float vv = 0.f;
-            if (t < cd.len) vv = io<IO>::ld(v + ((size_t)(cd.t0 + t) * H + h) * DV + col0 + j);
-            sX[t * SCAN_DVT + j] = vv;
-        }
+        *reinterpret_cast<float4 *>(sD + ta * SCAN_NC + cj) = make_float4(da[0], da[1], da[2], da[3]);
+        *reinterpret_cast<float4 *>(sD + tb * SCAN_NC + cj) = make_float4(db[0], db[1], db[2], db[3]);
+        cp_async_wait<1>();  // G3(c)
         __syncthreads();
-        for (int t = r; t < KC; t += 16) {
-            float acc = 0.f;
-            const float *kt = sKt + t * DK;
-            for (int i = 0; i < DK; i++) acc += kt[i] * sS[i * SCAN_DVT + j];
-            sX[t * SCAN_DVT + j] -= acc;
+        if (c + 1 < c1) issue_g2(c + 1);
+        cp_async_commit();
+
+        // phase C: O = Qtil S + Aqk Delta (Aqk lower triangular with its diagonal)
+        for (int q = 0; q < KC / 4 - w; q++) {
+            const int s = 4 * q;
+            const float4 Ab = *reinterpret_cast<const float4 *>(sAq + tb * LM + s);
+            const float ab_[4] = {Ab.x, Ab.y, Ab.z, Ab.w};
+            float4 d[4];
+#pragma unroll
+            for (int u = 0; u < 4; u++)
+                d[u] = *reinterpret_cast<const float4 *>(sD + (s + u) * SCAN_NC + cj);
+#pragma unroll
+            for (int u = 0; u < 4; u++) fma4(qb, ab_[u], d[u]);
+            if (q <= w) {
+                const float4 Aa = *reinterpret_cast<const float4 *>(sAq + ta * LM + s);
+                const float aa_[4] = {Aa.x, Aa.y, Aa.z, Aa.w};
+#pragma unroll
+                for (int u = 0; u < 4; u++) fma4(qa, aa_[u], d[u]);
+            }
         }
-        __syncthreads();
-        // Delta = M X  (M lower triangular)
-        for (int t = r; t < KC; t += 16) {
-            float acc = 0.f;
-            const float *m = sM + t * KC;
-            for (int s = 0; s <= t; s++) acc += m[s] * sX[s * SCAN_DVT + j];
-            sD[t * SCAN_DVT + j] = acc;
+        if (ta < cd.len) {
+            IO *op = o + ((size_t)(cd.t0 + ta) * H + h) * DV + col0;
+#pragma unroll
+            for (int u = 0; u < 4; u++) io<IO>::st(op + u, qa[u]);
         }
-        __syncthreads();
-        // O = Qtil S + Aqk Delta
-        for (int t = r; t < cd.len; t += 16) {
-            float acc = 0.f;
-            const float *qt = sQt + t * DK;
-            for (int i = 0; i < DK; i++) acc += qt[i] * sS[i * SCAN_DVT + j];
-            const float *aq = sAq + t * KC;
-            for (int s = 0; s <= t; s++) acc += aq[s] * sD[s * SCAN_DVT + j];
-            io<IO>::st(o + ((size_t)(cd.t0 + t) * H + h) * DV + col0 + j, acc);
+        if (tb < cd.len) {
+            IO *op = o + ((size_t)(cd.t0 + tb) * H + h) * DV + col0;
+#pragma unroll
+            for (int u = 0; u < 4; u++) io<IO>::st(op + u, qb[u]);
         }
-        __syncthreads();
-        // S = e^G_C S + Kbar^T Delta
-        for (int i = r; i < DK; i += 16) {
-            float acc = sGc[i] * sS[i * SCAN_DVT + j];
-            for (int s = 0; s < KC; s++) acc += sKb[s * DK + i] * sD[s * SCAN_DVT + j];
-            sS[i * SCAN_DVT + j] = acc;
+
+        // phase D: S = e^G_C S + Kbar^T Delta for state rows RS ty .. RS ty + RS - 1
+#pragma unroll
+        for (int r = 0; r < RS; r++) {
+            const float g = sGc[RS * ty + r];
+#pragma unroll
+            for (int u = 0; u < 4; u++) sreg[r][u] = g * sreg[r][u];
         }
+#pragma unroll 4
+        for (int s = 0; s < KC; s++) {
+            const float4 d = *reinterpret_cast<const float4 *>(sD + s * SCAN_NC + cj);
+            float kbar[RS];
+            if constexpr (RS == 4) {
+                const float4 k4 = *reinterpret_cast<const float4 *>(sKb + s * DK + 4 * ty);
+                kbar[0] = k4.x, kbar[1] = k4.y, kbar[2] = k4.z, kbar[3] = k4.w;
+            } else {
+                const float2 k2 = *reinterpret_cast<const float2 *>(sKb + s * DK + 2 * ty);
+                kbar[0] = k2.x, kbar[1] = k2.y;
+            }
+#pragma unroll
+            for (int r = 0; r < RS; r++) fma4(sreg[r], kbar[r], d);
+        }
+#pragma unroll
+        for (int r = 0; r < RS; r++)
+            *reinterpret_cast<float4 *>(sS + (RS * ty + r) * SCAN_NC + cj) =
+                make_float4(sreg[r][0], sreg[r][1], sreg[r][2], sreg[r][3]);
     }
-    __syncthreads();
+    cp_async_wait<0>();
     if (Sg)
-        for (int e = tid; e < DK * SCAN_DVT; e += 256) {
-            const int i = e / SCAN_DVT, jj = e % SCAN_DVT;
-            Sg[(size_t)i * DV + col0 + jj] = sS[e];
-        }
+#pragma unroll
+        for (int r = 0; r < RS; r++)
+#pragma unroll
+            for (int u = 0; u < 4; u++)
+                Sg[(size_t)(RS * ty + r) * DV + col0 + u] = sreg[r][u];
 }
 
 static size_t align256(size_t x) { return (x + 255) & ~(size_t)255; }
@@ -347,7 +565,7 @@ static int run_prefill(k3cuda_ctx *ctx, float *state, void *o, const void *q, co
     }
     if (nc > 0) {
         const size_t smem1 =
-            ((size_t)4 * KC * DK + 2 * KSUB * DK + 3 * KC * KC + KC) * sizeof(float);
+            ((size_t)4 * KC * (DK + 4) + 2 * KSUB * (DK + 4) + 3 * KC * KC + KC) * sizeof(float);
         if (int rc_ = set_smem(kda_chunk_intra<IO, DK>, (int)smem1)) return rc_;
         dim3 g1((unsigned)nc, (unsigned)H);
         kda_chunk_intra<IO, DK><<<g1, 256, smem1, ctx->stream>>>(
@@ -355,13 +573,13 @@ static int run_prefill(k3cuda_ctx *ctx, float *state, void *o, const void *q, co
         int rc = after_launch(ctx, "kda_chunk_intra");
         if (rc) return rc;
     }
-    const size_t smem2 = ((size_t)3 * KC * DK + 2 * KC * KC + DK * SCAN_DVT + 2 * KC * SCAN_DVT +
-                          DK) * sizeof(float);
+    const size_t smem2 = ((size_t)2 * KC * (DK + 4) + KC * DK + 2 * KC * (KC + 4) + DK +
+                          DK * SCAN_NC + 2 * KC * SCAN_NC) * sizeof(float);
     if (int rc_ = set_smem(kda_chunk_scan<IO, DK>, (int)smem2)) return rc_;
-    const long long nblk = (long long)n_seq * H * (DK / SCAN_DVT);
+    const long long nblk = (long long)n_seq * H * (DK / SCAN_NC);
     if (nblk > 0) {
         kda_chunk_scan<IO, DK><<<(unsigned)nblk, 256, smem2, ctx->stream>>>(
-            d_table, d_c0, (const IO *)v, blocks, state, (IO *)o, H);
+            d_table, d_c0, d_c0 + n_seq + 1, (const IO *)v, blocks, state, (IO *)o, H);
         return after_launch(ctx, "kda_chunk_scan");
     }
     (void)L::floats;
