@@ -72,101 +72,105 @@ __device__ __forceinline__ float load_gate(const float *p, int gate_is_log) {
 }
 
 // ---------------------------------------------------------------------------- intra
-// One CTA per (chunk, head), 256 threads. Rows of the [KC][DK] tiles are padded to DK + 4
-// floats: the Akk / Aqk products read sixteen different rows of Kh at once, which then fall in
-// different banks. (I + Akk)^-1 is formed blockwise on 16 x 16 blocks: the four diagonal blocks
-// by forward substitution (one lane per column, no barrier between rows), then the blocks below
-// the diagonal, one block diagonal at a time, from T_ij = -T_ii sum_{k=j}^{i-1} A_ik T_kj.
+// One CTA per (chunk, head), 256 threads, two CTAs per SM. Thread (ic, grp) = (tid % DK,
+// tid / DK) owns channel ic of the tokens [TG grp, TG grp + TG) and keeps their k and q in
+// registers; shared memory holds G, the anchored operands of the current sub-block and Akk
+// (about 101 KB at d_k = 128). Rows are padded to DK + 4 floats: the Akk / Aqk products read
+// sixteen different rows of Kh at once, which then fall in different banks. Aqk goes straight
+// to the workspace. (I + Akk)^-1 is formed blockwise on 16 x 16 blocks: the four diagonal
+// blocks by forward substitution (one lane per column, no barrier between rows), then the
+// blocks below the diagonal, one block diagonal at a time, from
+// T_ij = -T_ii sum_{k=j}^{i-1} A_ik T_kj.
 template <typename IO, int DK>
-__global__ void __launch_bounds__(256, 1)
+__global__ void __launch_bounds__(256, 2)
 kda_chunk_intra(const ChunkDesc *__restrict__ chunks, const IO *__restrict__ q,
                 const IO *__restrict__ k, const float *__restrict__ gate,
                 const float *__restrict__ beta, float *__restrict__ ws, int H, float q_scale,
                 int gate_is_log) {
     using L = PrefillLayout<DK>;
-    constexpr int LP = DK + 4, NB = KC / KSUB;
+    constexpr int LP = DK + 4, NB = KC / KSUB, NG = 256 / DK, TG = KC / NG;
     extern __shared__ __align__(16) float sm[];
-    float *sk = sm;                     // [KC][LP]  k
-    float *sq = sk + KC * LP;           // [KC][LP]  q * q_scale
-    float *sG = sq + KC * LP;           // [KC][LP]  cumulative log decay
-    float *sKh = sG + KC * LP;          // [KC][LP]  k_s e^(G_r - G_s) for the current anchor r
+    float *sG = sm;                     // [KC][LP]   cumulative log decay
+    float *sKh = sG + KC * LP;          // [KC][LP]   k_s e^(G_r - G_s) for the current anchor r
     float *sKa = sKh + KC * LP;         // [KSUB][LP] k_t e^(G_t - G_r)
     float *sQa = sKa + KSUB * LP;       // [KSUB][LP] q_t e^(G_t - G_r)
-    float *sA = sQa + KSUB * LP;        // [KC][KC]  Akk (beta-scaled, strictly lower)
-    float *sAq = sA + KC * KC;          // [KC][KC]  Aqk (lower incl. diagonal)
-    float *sT = sAq + KC * KC;          // [KC][KC]  (I + Akk)^-1
-    float *sb = sT + KC * KC;           // [KC]      beta
-    float *sP = sKh;                    // [NB-1][KSUB][KSUB] block products (Kh is dead then)
+    float *sA = sQa + KSUB * LP;        // [KC][KC]   Akk (beta-scaled, strictly lower)
+    float *sb = sA + KC * KC;           // [KC]       beta
+    float *sTot = sb + KC;              // [NG][DK]   decay sum of each token group
+    float *sT = sKh;                    // [KC][KC]   (I + Akk)^-1 (Kh is dead by then)
+    float *sP = sKh + KC * KC;          // [NB-1][KSUB][KSUB] block products
 
     const ChunkDesc cd = chunks[blockIdx.x];
     const int h = blockIdx.y, tid = threadIdx.x;
+    const int ic = tid % DK, grp = tid / DK, tg0 = grp * TG;
     float *out = ws + ((size_t)blockIdx.x * H + h) * L::floats;
 
+    float kr[TG], qr[TG];
     {
-        // every load of a batch is issued before its shared stores
-        constexpr int BATCH = 8;
-        for (int e0 = 0; e0 < KC * DK; e0 += 256 * BATCH) {
-            float kv[BATCH], qv[BATCH], gv[BATCH];
+        float gr[TG];
 #pragma unroll
-            for (int u = 0; u < BATCH; u++) {
-                const int e = e0 + u * 256 + tid, t = e / DK, i = e - t * DK;
-                kv[u] = qv[u] = gv[u] = 0.f;
-                if (t < cd.len) {
-                    const size_t off = ((size_t)(cd.t0 + t) * H + h) * DK + i;
-                    kv[u] = io<IO>::ld(k + off);
-                    qv[u] = io<IO>::ld(q + off) * q_scale;
-                    gv[u] = load_gate(gate + off, gate_is_log);
-                }
-            }
-#pragma unroll
-            for (int u = 0; u < BATCH; u++) {
-                const int e = e0 + u * 256 + tid, t = e / DK, i = e - t * DK;
-                sk[t * LP + i] = kv[u];
-                sq[t * LP + i] = qv[u];
-                sG[t * LP + i] = gv[u];
+        for (int u = 0; u < TG; u++) {
+            const int t = tg0 + u;
+            kr[u] = qr[u] = gr[u] = 0.f;
+            if (t < cd.len) {
+                const size_t off = ((size_t)(cd.t0 + t) * H + h) * DK + ic;
+                kr[u] = io<IO>::ld(k + off);
+                qr[u] = io<IO>::ld(q + off) * q_scale;
+                gr[u] = load_gate(gate + off, gate_is_log);
             }
         }
-    }
-    if (tid < KC) sb[tid] = tid < cd.len ? beta[(size_t)(cd.t0 + tid) * H + h] : 0.f;
-    __syncthreads();
-    if (tid < DK) {
         float acc = 0.f;
-#pragma unroll 16
-        for (int t = 0; t < KC; t++) {
-            acc += sG[t * LP + tid];
-            sG[t * LP + tid] = acc;
+#pragma unroll
+        for (int u = 0; u < TG; u++) {
+            acc += gr[u];
+            gr[u] = acc;
         }
+        sTot[grp * DK + ic] = acc;
+        if (tid < KC) sb[tid] = tid < cd.len ? beta[(size_t)(cd.t0 + tid) * H + h] : 0.f;
+        __syncthreads();
+        float base = 0.f;
+        for (int g2 = 0; g2 < grp; g2++) base += sTot[g2 * DK + ic];
+#pragma unroll
+        for (int u = 0; u < TG; u++) sG[(tg0 + u) * LP + ic] = gr[u] + base;
     }
     __syncthreads();
 
     // scaled operands for the scan (full-chunk anchor at the chunk start)
-    for (int e = tid; e < KC * DK; e += 256) {
-        const int t = e / DK, i = e - t * DK;
-        const float G = sG[t * LP + i], GC = sG[(KC - 1) * LP + i];
-        const float eg = expf(G);
-        out[L::qt + e] = sq[t * LP + i] * eg;
-        out[L::kt + e] = sk[t * LP + i] * eg;
-        out[L::kb + e] = sk[t * LP + i] * expf(GC - G);
+    {
+        const float GC = sG[(KC - 1) * LP + ic];
+#pragma unroll
+        for (int u = 0; u < TG; u++) {
+            const int t = tg0 + u;
+            const float G = sG[t * LP + ic];
+            const float eg = expf(G);
+            out[L::qt + t * DK + ic] = qr[u] * eg;
+            out[L::kt + t * DK + ic] = kr[u] * eg;
+            out[L::kb + t * DK + ic] = kr[u] * expf(GC - G);
+        }
+        if (tid < DK) out[L::gc + tid] = expf(GC);
     }
-    if (tid < DK) out[L::gc + tid] = expf(sG[(KC - 1) * LP + tid]);
 
     // Akk / Aqk, one 16-row sub-block at a time; thread (tl, ss) = (tid / 16, tid % 16) forms
     // row r0 + tl against the columns ss + 16 m, m = 0..a
 #pragma unroll
     for (int a = 0; a < NB; a++) {
         const int r0 = a * KSUB, ncol = r0 + KSUB;
+        const float Gr = sG[r0 * LP + ic];
         int big = 0;
-        for (int e = tid; e < ncol * DK; e += 256) {
-            const int s = e / DK, i = e - s * DK;
-            const float ex = sG[r0 * LP + i] - sG[s * LP + i];
-            big |= ex > 80.f;
-            sKh[s * LP + i] = sk[s * LP + i] * expf(fminf(ex, 80.f));
-        }
-        for (int e = tid; e < KSUB * DK; e += 256) {
-            const int tl = e / DK, i = e - tl * DK, t = r0 + tl;
-            const float f = expf(sG[t * LP + i] - sG[r0 * LP + i]);
-            sKa[tl * LP + i] = sk[t * LP + i] * f;
-            sQa[tl * LP + i] = sq[t * LP + i] * f;
+#pragma unroll
+        for (int u = 0; u < TG; u++) {
+            const int s = tg0 + u;
+            if (s < ncol) {
+                const float Gs = sG[s * LP + ic];
+                const float ex = Gr - Gs;
+                big |= ex > 80.f;
+                sKh[s * LP + ic] = kr[u] * expf(fminf(ex, 80.f));
+                if (s >= r0) {
+                    const float f = expf(Gs - Gr);
+                    sKa[(s - r0) * LP + ic] = kr[u] * f;
+                    sQa[(s - r0) * LP + ic] = qr[u] * f;
+                }
+            }
         }
         big = __syncthreads_or(big);
         const int tl = tid / 16, ss = tid % 16, t = r0 + tl;
@@ -198,16 +202,22 @@ kda_chunk_intra(const ChunkDesc *__restrict__ chunks, const IO *__restrict__ q,
                 vk = akk[m];
                 vq = aqk[m];
                 if (big && s >= r0) {
+                    // exact path from the inputs (k and q are zero past the chunk's tokens)
                     vk = vq = 0.f;
-                    for (int i = 0; i < DK; i++) {
-                        const float f = expf(sG[t * LP + i] - sG[s * LP + i]) * sk[s * LP + i];
-                        vk += sk[t * LP + i] * f;
-                        vq += sq[t * LP + i] * f;
+                    if (t < cd.len) {
+                        const size_t ot = ((size_t)(cd.t0 + t) * H + h) * DK;
+                        const size_t os = ((size_t)(cd.t0 + s) * H + h) * DK;
+                        for (int i = 0; i < DK; i++) {
+                            const float f =
+                                expf(sG[t * LP + i] - sG[s * LP + i]) * io<IO>::ld(k + os + i);
+                            vk += io<IO>::ld(k + ot + i) * f;
+                            vq += io<IO>::ld(q + ot + i) * q_scale * f;
+                        }
                     }
                 }
             }
             sA[t * KC + s] = s < t ? sb[t] * vk : 0.f;
-            sAq[t * KC + s] = vq;
+            out[L::aqk + t * KC + s] = vq;
         }
         __syncthreads();
     }
@@ -252,11 +262,10 @@ kda_chunk_intra(const ChunkDesc *__restrict__ chunks, const IO *__restrict__ q,
         }
         __syncthreads();
     }
-    // M = T diag(beta) (zero above the diagonal blocks), and Aqk
+    // M = T diag(beta), zero above the diagonal blocks
     for (int e = tid; e < KC * KC; e += 256) {
         const int t = e / KC, s = e % KC;
         out[L::m + e] = t / KSUB < s / KSUB ? 0.f : sT[e] * sb[s];
-        out[L::aqk + e] = sAq[e];
     }
 }
 
@@ -564,8 +573,8 @@ static int run_prefill(k3cuda_ctx *ctx, float *state, void *o, const void *q, co
                               gate_is_log, nc, d_table, d_c0, blocks, go);
     }
     if (nc > 0) {
-        const size_t smem1 =
-            ((size_t)4 * KC * (DK + 4) + 2 * KSUB * (DK + 4) + 3 * KC * KC + KC) * sizeof(float);
+        const size_t smem1 = ((size_t)2 * KC * (DK + 4) + 2 * KSUB * (DK + 4) + KC * KC + KC +
+                              256) * sizeof(float);
         if (int rc_ = set_smem(kda_chunk_intra<IO, DK>, (int)smem1)) return rc_;
         dim3 g1((unsigned)nc, (unsigned)H);
         kda_chunk_intra<IO, DK><<<g1, 256, smem1, ctx->stream>>>(
