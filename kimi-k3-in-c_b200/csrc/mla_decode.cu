@@ -855,7 +855,7 @@ mla_merge(const float *__restrict__ part, const int *__restrict__ slot0,
         float M = -INFINITY;
         for (int s = s0 + tid; s < s1; s += 128) M = fmaxf(M, base[s * stride + MLA_DL]);
 #pragma unroll
-        for (int o = 16; o; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
+        for (int sh = 16; sh; sh >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, sh));
         if ((tid & 31) == 0) red[0][tid >> 5] = M;
         __syncthreads();
         M = fmaxf(fmaxf(red[0][0], red[0][1]), fmaxf(red[0][2], red[0][3]));
@@ -863,7 +863,7 @@ mla_merge(const float *__restrict__ part, const int *__restrict__ slot0,
         for (int s = s0 + tid; s < s1; s += 128)
             L += exp2f(base[s * stride + MLA_DL] - M) * base[s * stride + MLA_DL + 1];
 #pragma unroll
-        for (int o = 16; o; o >>= 1) L += __shfl_xor_sync(0xffffffffu, L, o);
+        for (int sh = 16; sh; sh >>= 1) L += __shfl_xor_sync(0xffffffffu, L, sh);
         if ((tid & 31) == 0) red[1][tid >> 5] = L;
         __syncthreads();
         const float invL = 1.f / ((red[1][0] + red[1][1]) + (red[1][2] + red[1][3]));
