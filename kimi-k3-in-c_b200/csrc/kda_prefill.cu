@@ -33,6 +33,7 @@
 #include <algorithm>
 
 #include "internal.cuh"
+#include "sm100.cuh"
 
 namespace k3 {
 
@@ -53,6 +54,28 @@ struct ChunkDesc {
     int len;    // tokens in this chunk (1..64)
     int pad;
 };
+
+// The block of one (chunk, head) for the tensor-core fp32 scan (d = 128; same size as the
+// fp32 block below): every operand as a hi plane bf16(x) and a lo plane bf16(x - hi), each
+// laid out as the 128-byte-swizzled shared-memory image the scan's MMAs read, so that one
+// untiled bulk copy per group stages it. Byte offsets:
+constexpr int W32_KQH = 0;        // [Qtil; Ktil] [128 rows][128 i], two K-blocks of [128][64]
+constexpr int W32_KQL = 32768;
+constexpr int W32_MH = 65536;     // M = (I + Akk)^-1 diag(beta) [64 t][64 s], K-major
+constexpr int W32_ML = 73728;
+constexpr int W32_AH = 81920;     // Aqk [64 t][64 s], K-major
+constexpr int W32_AL = 90112;
+constexpr int W32_KBH = 98304;    // Kbar [64 t][128 i], two blocks [64 t][64 i] (MN-major A)
+constexpr int W32_KBL = 114688;
+constexpr int W32_G = 131072;     // Gamma = e^(G_C) [128] fp32
+constexpr int W32_BYTES = 131584;
+
+// hi / lo halves of x at byte `off` of the planes `hi` and `lo` of block `b`
+__device__ __forceinline__ void put_split(uint8_t *b, int hi, int lo, uint32_t off, float x) {
+    const __nv_bfloat16 xh = __float2bfloat16_rn(x);
+    *reinterpret_cast<__nv_bfloat16 *>(b + hi + off) = xh;
+    *reinterpret_cast<__nv_bfloat16 *>(b + lo + off) = __float2bfloat16_rn(x - __bfloat162float(xh));
+}
 
 template <int DK>
 struct PrefillLayout {
@@ -81,7 +104,7 @@ __device__ __forceinline__ float load_gate(const float *p, int gate_is_log) {
 // blocks by forward substitution (one lane per column, no barrier between rows), then the
 // blocks below the diagonal, one block diagonal at a time, from
 // T_ij = -T_ii sum_{k=j}^{i-1} A_ik T_kj.
-template <typename IO, int DK>
+template <typename IO, int DK, bool TC32 = false>
 __global__ void __launch_bounds__(256, 2)
 kda_chunk_intra(const ChunkDesc *__restrict__ chunks, const IO *__restrict__ q,
                 const IO *__restrict__ k, const float *__restrict__ gate,
@@ -104,6 +127,8 @@ kda_chunk_intra(const ChunkDesc *__restrict__ chunks, const IO *__restrict__ q,
     const int h = blockIdx.y, tid = threadIdx.x;
     const int ic = tid % DK, grp = tid / DK, tg0 = grp * TG;
     float *out = ws + ((size_t)blockIdx.x * H + h) * L::floats;
+    uint8_t *ob = reinterpret_cast<uint8_t *>(out);  // the same block, as the TC32 layout
+    static_assert(!TC32 || (DK == 128 && L::floats * 4 == W32_BYTES), "TC32 block layout");
 
     float kr[TG], qr[TG];
     {
@@ -143,11 +168,24 @@ kda_chunk_intra(const ChunkDesc *__restrict__ chunks, const IO *__restrict__ q,
             const int t = tg0 + u;
             const float G = sG[t * LP + ic];
             const float eg = expf(G);
-            out[L::qt + t * DK + ic] = qr[u] * eg;
-            out[L::kt + t * DK + ic] = kr[u] * eg;
-            out[L::kb + t * DK + ic] = kr[u] * expf(GC - G);
+            if constexpr (TC32) {
+                const uint32_t kq = (ic >> 6) * 16384 + sm100::swz_elem(t, ic & 63);
+                put_split(ob, W32_KQH, W32_KQL, kq, qr[u] * eg);         // row t
+                put_split(ob, W32_KQH, W32_KQL, kq + 8192, kr[u] * eg);  // row 64 + t
+                put_split(ob, W32_KBH, W32_KBL, (ic >> 6) * 8192 + sm100::swz_elem(t, ic & 63),
+                          kr[u] * expf(GC - G));
+            } else {
+                out[L::qt + t * DK + ic] = qr[u] * eg;
+                out[L::kt + t * DK + ic] = kr[u] * eg;
+                out[L::kb + t * DK + ic] = kr[u] * expf(GC - G);
+            }
         }
-        if (tid < DK) out[L::gc + tid] = expf(GC);
+        if (tid < DK) {
+            if constexpr (TC32)
+                reinterpret_cast<float *>(ob + W32_G)[tid] = expf(GC);
+            else
+                out[L::gc + tid] = expf(GC);
+        }
     }
 
     // Akk / Aqk, one 16-row sub-block at a time; thread (tl, ss) = (tid / 16, tid % 16) forms
@@ -217,7 +255,10 @@ kda_chunk_intra(const ChunkDesc *__restrict__ chunks, const IO *__restrict__ q,
                 }
             }
             sA[t * KC + s] = s < t ? sb[t] * vk : 0.f;
-            out[L::aqk + t * KC + s] = vq;
+            if constexpr (TC32)
+                put_split(ob, W32_AH, W32_AL, sm100::swz_elem(t, s), vq);
+            else
+                out[L::aqk + t * KC + s] = vq;
         }
         __syncthreads();
     }
@@ -265,7 +306,11 @@ kda_chunk_intra(const ChunkDesc *__restrict__ chunks, const IO *__restrict__ q,
     // M = T diag(beta), zero above the diagonal blocks
     for (int e = tid; e < KC * KC; e += 256) {
         const int t = e / KC, s = e % KC;
-        out[L::m + e] = t / KSUB < s / KSUB ? 0.f : sT[e] * sb[s];
+        const float mv = t / KSUB < s / KSUB ? 0.f : sT[e] * sb[s];
+        if constexpr (TC32)
+            put_split(ob, W32_MH, W32_ML, sm100::swz_elem(t, s), mv);
+        else
+            out[L::m + e] = mv;
     }
 }
 
@@ -509,6 +554,318 @@ kda_chunk_scan(const ChunkDesc *__restrict__ chunks, const int *__restrict__ seq
                 Sg[(size_t)(RS * ty + r) * DV + col0 + u] = sreg[r][u];
 }
 
+// ------------------------------------------------------------ scan on tcgen05 (fp32 I/O)
+// Shared-memory plan of kda_scan_tc32 (bytes from a 1024-aligned base). The operand groups
+// keep the offsets of the workspace block, so each is one bulk copy.
+struct Scan32 {
+    static constexpr int KQ = W32_KQH, KQ_BYTES = 65536;   // [Qtil; Ktil] hi, lo
+    static constexpr int M = W32_MH, M_BYTES = 16384;      // M hi, lo
+    static constexpr int KA = W32_AH, KA_BYTES = 49152;    // Aqk hi, lo; Kbar hi, lo
+    static constexpr int S16H = 131072, S16L = 147456;     // state [128 i][64 j], MN-major
+    static constexpr int XH = 163840, XL = 172032;         // X = V - Ktil S [64 s][64 j]
+    static constexpr int DH = 180224, DL = 188416;         // Delta = M X [64 s][64 j]
+    static constexpr int BYTES = 196608, SMEM = BYTES + 1024;
+    static constexpr uint32_t TM_Y = 0, TM_D = 128, TM_S = 192, TM_COLS = 256;
+};
+static_assert(Scan32::SMEM <= 232448, "tc32 scan shared memory");
+static_assert(W32_KQL == W32_KQH + 32768 && W32_AH + Scan32::KA_BYTES == W32_G,
+              "operand groups are contiguous in the workspace block");
+
+template <bool VEC>
+__device__ __forceinline__ void ld_row64(float *dst, const float *src) {
+    if constexpr (VEC) {
+#pragma unroll
+        for (int c = 0; c < 64; c += 4) {
+            const float4 x = *reinterpret_cast<const float4 *>(src + c);
+            dst[c] = x.x, dst[c + 1] = x.y, dst[c + 2] = x.z, dst[c + 3] = x.w;
+        }
+    } else {
+#pragma unroll
+        for (int c = 0; c < 64; c++) dst[c] = src[c];
+    }
+}
+template <bool VEC>
+__device__ __forceinline__ void st_row64(float *dst, const float *src) {
+    if constexpr (VEC) {
+#pragma unroll
+        for (int c = 0; c < 64; c += 4)
+            *reinterpret_cast<float4 *>(dst + c) =
+                make_float4(src[c], src[c + 1], src[c + 2], src[c + 3]);
+    } else {
+#pragma unroll
+        for (int c = 0; c < 64; c++) dst[c] = src[c];
+    }
+}
+// bf16 hi and lo halves of a 64-value row into row r of two MN-major [rows][64] tiles
+__device__ __forceinline__ void put_row_split(uint8_t *hi, uint8_t *lo, int r, const float *x) {
+#pragma unroll
+    for (int c = 0; c < 8; c++) {
+        float h[8], l[8];
+        const uint4 ph = sm100::pack_bf8(x + 8 * c);
+        sm100::unpack_bf8(ph, h);
+#pragma unroll
+        for (int u = 0; u < 8; u++) l[u] = x[8 * c + u] - h[u];
+        sm100::st16s(hi + sm100::swz(r, c), ph);
+        sm100::st16s(lo + sm100::swz(r, c), sm100::pack_bf8(l));
+    }
+}
+
+// Chunk scan in the direct form on tcgen05, for fp32 q/k/v/o at d_k = d_v = 128, with
+// fp32-level products: every operand is a bf16 pair hi + lo and every product is three MMAs
+// (hi.hi + hi.lo + lo.hi, fp32 accumulation in TMEM), which leaves about 2^-16 relative error
+// per product instead of bf16's 2^-8. One CTA per (sequence, head, 64-column half of d_v);
+// the fp32 state half lives in TMEM. Per chunk:
+//   Y  = [Qtil; Ktil] S16         (M=128: rows 0-63 Qtil S, rows 64-127 Ktil S)
+//   X  = V - (Ktil S)             compute warps 2-3 (TMEM lanes 64-127), bf16 hi/lo to smem
+//   D  = M X                      (M=64)
+//   S' = Gamma S + Kbar^T D       (M=128, into the state accumulator, already scaled)
+//   O  = Qtil S + Aqk D           (into rows 0-63 of Y; the M=128 A operand's rows 64-127
+//                                 read the next shared tile and land on Y's dead Ktil S rows)
+// then S' is copied to S16 (hi/lo) and scaled by the next Gamma in TMEM. Warps 0-3: thread
+// i owns TMEM lane i; warp 4: bulk-copy producer; warp 5: TMEM allocation and MMA issue. Y is
+// double-buffered in TMEM so that a chunk's outputs are read while the next chunk runs.
+template <bool VEC>
+__global__ void __launch_bounds__(192, 1)
+kda_scan_tc32(const ChunkDesc *__restrict__ chunks, const int *__restrict__ seq_chunk0,
+              const int *__restrict__ seq_order, const uint8_t *__restrict__ ws,
+              const float *__restrict__ v, float *__restrict__ state, float *__restrict__ o,
+              int H, unsigned *__restrict__ err) {
+    using namespace sm100;
+    using C = Scan32;
+    extern __shared__ uint8_t smraw[];
+    uint8_t *sm = (uint8_t *)(((uintptr_t)smraw + 1023) & ~(uintptr_t)1023);
+    __shared__ uint64_t kq_full, kq_empty, m_full, m_empty, ka_full, ka_empty;
+    __shared__ uint64_t y_done, x_ready, dx_done, d_ready, s_done, o_done, s16_ready, mma_fin;
+    __shared__ uint32_t tslot;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int half = blockIdx.x & 1, h = (blockIdx.x >> 1) % H;
+    const int n = seq_order[blockIdx.x / (2 * H)];
+    const int c0 = seq_chunk0[n], nc = seq_chunk0[n + 1] - c0;
+    const int col0 = 64 * half;
+    auto block = [&](int j) { return ws + ((size_t)(c0 + j) * H + h) * W32_BYTES; };
+
+    if (tid == 0) {
+        mbar_init(&kq_full, 1);
+        mbar_init(&kq_empty, 1);
+        mbar_init(&m_full, 1);
+        mbar_init(&m_empty, 1);
+        mbar_init(&ka_full, 1);
+        mbar_init(&ka_empty, 1);
+        mbar_init(&y_done, 1);
+        mbar_init(&x_ready, 128);
+        mbar_init(&dx_done, 1);
+        mbar_init(&d_ready, 128);
+        mbar_init(&s_done, 1);
+        mbar_init(&o_done, 1);
+        mbar_init(&s16_ready, 128);
+        mbar_init(&mma_fin, 1);
+        fence_barrier_init();
+    }
+    if (warp == 5) tmem_alloc(&tslot, C::TM_COLS);
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tb = tslot;
+
+    if (warp == 4) {
+        if (lane == 0) {
+            int last_kq = -1, last_m = -1, last_ka = -1;
+            for (int j = 0; j < nc; j++) {
+                const uint8_t *b = block(j);
+                const uint32_t pe = (j - 1) & 1;
+                if (j > 0 && !mbar_wait(&kq_empty, pe, err, 0x701)) break;
+                mbar_expect_tx(&kq_full, C::KQ_BYTES);
+                bulk_load(sm + C::KQ, b + W32_KQH, C::KQ_BYTES, &kq_full);
+                last_kq = j;
+                if (j > 0 && !mbar_wait(&m_empty, pe, err, 0x702)) break;
+                mbar_expect_tx(&m_full, C::M_BYTES);
+                bulk_load(sm + C::M, b + W32_MH, C::M_BYTES, &m_full);
+                last_m = j;
+                if (j > 0 && !mbar_wait(&ka_empty, pe, err, 0x703)) break;
+                mbar_expect_tx(&ka_full, C::KA_BYTES);
+                bulk_load(sm + C::KA, b + W32_AH, C::KA_BYTES, &ka_full);
+                last_ka = j;
+            }
+            // copies still in flight are waited for (bounded) before the CTA may exit
+            if (last_kq >= 0) mbar_wait_quiet(&kq_full, last_kq & 1);
+            if (last_m >= 0) mbar_wait_quiet(&m_full, last_m & 1);
+            if (last_ka >= 0) mbar_wait_quiet(&ka_full, last_ka & 1);
+        }
+    } else if (warp == 5) {
+        if (lane == 0) {
+            constexpr uint32_t id_y = idesc_f16(128, 64, false, true);
+            constexpr uint32_t id_d = idesc_f16(64, 64, false, true);
+            constexpr uint32_t id_s = idesc_f16(128, 64, true, true);
+            const uint64_t dk = sdesc_kmajor(smem_u32(sm));
+            const uint64_t d8 = sdesc_mnmajor(smem_u32(sm), 8192);
+            const uint64_t d16 = sdesc_mnmajor(smem_u32(sm), 16384);
+            bool issued = false;
+            for (int j = 0; j < nc; j++) {
+                const uint32_t par = j & 1, yb = tb + C::TM_Y + 64 * (j & 1);
+                // Y = [Qtil; Ktil] . S16
+                if (!mbar_wait(&kq_full, par, err, 0x704)) break;
+                if (!mbar_wait(&s16_ready, par, err, 0x705)) break;
+                tc_fence_after();
+#pragma unroll
+                for (int p = 0; p < 3; p++) {
+                    const int a = C::KQ + (p == 2 ? 32768 : 0), b = p == 1 ? C::S16L : C::S16H;
+#pragma unroll
+                    for (int ks = 0; ks < 8; ks++)
+                        mma_bf16_ss(yb, dk + ((a + (ks >> 2) * 16384 + (ks & 3) * 32) >> 4),
+                                    d16 + ((b + ks * 2048) >> 4), id_y, (p | ks) ? 1u : 0u);
+                }
+                issued = true;
+                mma_commit(&y_done);
+                mma_commit(&kq_empty);
+                // D = M . X
+                if (!mbar_wait(&m_full, par, err, 0x706)) break;
+                if (!mbar_wait(&x_ready, par, err, 0x707)) break;
+                tc_fence_after();
+#pragma unroll
+                for (int p = 0; p < 3; p++) {
+                    const int a = p == 2 ? W32_ML : W32_MH, b = p == 1 ? C::XL : C::XH;
+#pragma unroll
+                    for (int ks = 0; ks < 4; ks++)
+                        mma_bf16_ss(tb + C::TM_D, dk + ((a + ks * 32) >> 4),
+                                    d8 + ((b + ks * 2048) >> 4), id_d, (p | ks) ? 1u : 0u);
+                }
+                mma_commit(&dx_done);
+                mma_commit(&m_empty);
+                // S += Kbar^T . D, then O (rows 0-63 of Y) += Aqk . D
+                if (!mbar_wait(&ka_full, par, err, 0x708)) break;
+                if (!mbar_wait(&d_ready, par, err, 0x709)) break;
+                tc_fence_after();
+#pragma unroll
+                for (int p = 0; p < 3; p++) {
+                    const int a = p == 2 ? W32_KBL : W32_KBH, b = p == 1 ? C::DL : C::DH;
+#pragma unroll
+                    for (int ks = 0; ks < 4; ks++)
+                        mma_bf16_ss(tb + C::TM_S, d8 + ((a + ks * 2048) >> 4),
+                                    d8 + ((b + ks * 2048) >> 4), id_s, 1u);
+                }
+                mma_commit(&s_done);
+#pragma unroll
+                for (int p = 0; p < 3; p++) {
+                    const int a = p == 2 ? W32_AL : W32_AH, b = p == 1 ? C::DL : C::DH;
+#pragma unroll
+                    for (int ks = 0; ks < 4; ks++)
+                        mma_bf16_ss(yb, dk + ((a + ks * 32) >> 4), d8 + ((b + ks * 2048) >> 4),
+                                    id_y, 1u);
+                }
+                mma_commit(&o_done);
+                mma_commit(&ka_empty);
+            }
+            // every MMA issued (an aborted loop included) completes before TMEM is freed
+            if (issued) {
+                mma_commit(&mma_fin);
+                mbar_wait_quiet(&mma_fin, 0);
+            }
+        }
+    } else if (nc > 0) {
+        // ----------------------------------------------------------- compute warps
+        const int i = tid;  // TMEM lane: state row i; Y row i; D row 16 warp + lane (lane < 16)
+        const uint32_t lq = (uint32_t)(32 * warp) << 16;
+        float *Sg = state ? state + (((size_t)n * H + h) * 128 + i) * 128 + col0 : nullptr;
+        auto gamma = [&](int jj) {
+            return jj < nc ? reinterpret_cast<const float *>(block(jj) + W32_G)[i] : 0.f;
+        };
+        float s[64];
+        auto tmem_row = [&](uint32_t col, float *dst) {
+            tmem_ld32(tb + lq + col, dst);
+            tmem_ld32(tb + lq + col + 32, dst + 32);
+            tmem_wait_ld();
+        };
+        // S16 <- S (hi, lo); TMEM state <- gam * S
+        auto publish = [&](float gam) {
+            put_row_split(sm + C::S16H, sm + C::S16L, i, s);
+#pragma unroll
+            for (int c = 0; c < 64; c += 16) {
+                float x[16];
+#pragma unroll
+                for (int u = 0; u < 16; u++) x[u] = s[c + u] * gam;
+                tmem_st16(tb + lq + C::TM_S + c, x);
+            }
+            tmem_wait_st();
+            fence_async_shared();
+            tc_fence_before();
+            mbar_arrive(&s16_ready);
+        };
+        if (Sg) {
+            ld_row64<VEC>(s, Sg);
+        } else {
+#pragma unroll
+            for (int c = 0; c < 64; c++) s[c] = 0.f;
+        }
+        publish(gamma(0));
+        float gam1 = gamma(1), gam2 = gamma(2);
+        bool ok = true;
+        for (int j = 0; j < nc && ok; j++) {
+            const ChunkDesc cd = chunks[c0 + j];
+            const uint32_t par = j & 1, yb = C::TM_Y + 64 * (j & 1);
+            // X = V - Ktil S (token t = i - 64 on warps 2-3); V is loaded before the wait
+            float x[64];
+            const int t = i - 64;
+            if (warp >= 2) {
+                if (t < cd.len) {
+                    ld_row64<VEC>(x, v + ((size_t)(cd.t0 + t) * H + h) * 128 + col0);
+                } else {
+#pragma unroll
+                    for (int c = 0; c < 64; c++) x[c] = 0.f;
+                }
+            }
+            if (!(ok = warp_wait_all(&y_done, par, err, 0x70a))) break;
+            tc_fence_after();
+            if (warp >= 2) {
+                float y[64];
+                tmem_row(yb, y);
+#pragma unroll
+                for (int c = 0; c < 64; c++) x[c] -= y[c];
+                put_row_split(sm + C::XH, sm + C::XL, t, x);
+            }
+            fence_async_shared();
+            tc_fence_before();
+            mbar_arrive(&x_ready);
+            // D rows to shared memory (row 16 warp + lane on lanes 0-15)
+            if (!(ok = warp_wait_all(&dx_done, par, err, 0x70b))) break;
+            tc_fence_after();
+            {
+                float dd[64];
+                tmem_row(C::TM_D, dd);
+                if (lane < 16) put_row_split(sm + C::DH, sm + C::DL, 16 * warp + lane, dd);
+            }
+            fence_async_shared();
+            tc_fence_before();
+            mbar_arrive(&d_ready);
+            // the updated state: next chunk's S16 and Gamma-scaled TMEM copy, or the result
+            if (!(ok = warp_wait_all(&s_done, par, err, 0x70c))) break;
+            tc_fence_after();
+            tmem_row(C::TM_S, s);
+            if (j + 1 < nc) {
+                publish(gam1);
+                gam1 = gam2;
+                gam2 = gamma(j + 3);
+            } else if (Sg) {
+                st_row64<VEC>(Sg, s);
+            }
+            // outputs of the chunk (rows 0-63 of Y: warps 0-1)
+            if (!(ok = warp_wait_all(&o_done, par, err, 0x70d))) break;
+            tc_fence_after();
+            if (warp < 2) {
+                float y[64];
+                tmem_row(yb, y);
+                if (i < cd.len) st_row64<VEC>(o + ((size_t)(cd.t0 + i) * H + h) * 128 + col0, y);
+            }
+            tc_fence_before();
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 5) {
+        __syncwarp();
+        tmem_dealloc(tb, C::TM_COLS);
+    }
+}
+
 static size_t align256(size_t x) { return (x + 255) & ~(size_t)255; }
 
 static int count_chunks(const int *cu, int n_seq, long long *nc) {
@@ -572,9 +929,30 @@ static int run_prefill(k3cuda_ctx *ctx, float *state, void *o, const void *q, co
         return run_prefill_tc(ctx, state, o, q, k, v, gate, beta, cu[n_seq], n_seq, H, q_scale,
                               gate_is_log, nc, d_table, d_c0, blocks, go);
     }
+    const size_t smem1 = ((size_t)2 * KC * (DK + 4) + 2 * KSUB * (DK + 4) + KC * KC + KC + 256) *
+                         sizeof(float);
+    if constexpr (std::is_same<IO, float>::value && DK == 128) {
+        // fp32 q/k/v/o at d = 128: fp32 intra-chunk kernel writing bf16 hi/lo operands, scan on
+        // the tensor cores
+        if (nc == 0) return K3CUDA_OK;
+        if (int rc_ = set_smem(kda_chunk_intra<float, 128, true>, (int)smem1)) return rc_;
+        kda_chunk_intra<float, 128, true><<<dim3((unsigned)nc, (unsigned)H), 256, smem1,
+                                            ctx->stream>>>(d_table, (const float *)q,
+                                                           (const float *)k, gate, beta, blocks,
+                                                           H, q_scale, gate_is_log);
+        if (int rc_ = after_launch(ctx, "kda_chunk_intra")) return rc_;
+        const bool vec = aligned(v, 16) && aligned(o, 16) && (!state || aligned(state, 16));
+        const unsigned nblk32 = (unsigned)((long long)n_seq * H * 2);
+        auto launch = [&](auto kern) {
+            if (int rc_ = set_smem(kern, Scan32::SMEM)) return rc_;
+            kern<<<nblk32, 192, Scan32::SMEM, ctx->stream>>>(
+                d_table, d_c0, d_c0 + n_seq + 1, (const uint8_t *)blocks, (const float *)v, state,
+                (float *)o, H, ctx->err_word);
+            return after_launch(ctx, "kda_scan_tc32");
+        };
+        return vec ? launch(kda_scan_tc32<true>) : launch(kda_scan_tc32<false>);
+    }
     if (nc > 0) {
-        const size_t smem1 = ((size_t)2 * KC * (DK + 4) + 2 * KSUB * (DK + 4) + KC * KC + KC +
-                              256) * sizeof(float);
         if (int rc_ = set_smem(kda_chunk_intra<IO, DK>, (int)smem1)) return rc_;
         dim3 g1((unsigned)nc, (unsigned)H);
         kda_chunk_intra<IO, DK><<<g1, 256, smem1, ctx->stream>>>(

@@ -72,12 +72,6 @@ struct TcChunk {
     int seq, t0, len, pad;
 };
 
-// byte offset of the 16-byte chunk `c` (0..7) of row `r` in a 128-byte-swizzled tile whose
-// base is 1024-byte aligned
-__device__ __forceinline__ uint32_t swz(int r, int c) {
-    return (uint32_t)(r * 128 + (((c ^ r) & 7) << 4));
-}
-
 // fp32 [64][128] G tile, 16-byte units XOR-swizzled within each 128-byte group so that both
 // a channel-per-thread pass (fixed t) and a token-per-thread pass (fixed channels) are free
 // of bank conflicts
@@ -90,22 +84,6 @@ __device__ __forceinline__ int gsw(int t, int i) {
 __device__ __forceinline__ float ex2(float x) { return ex2_approx(x); }
 constexpr float kLog2e = 1.4426950408889634f;
 
-__device__ __forceinline__ uint32_t pack_bf2(float a, float b) {
-    const __nv_bfloat162 p = __floats2bfloat162_rn(a, b);
-    return *reinterpret_cast<const uint32_t *>(&p);
-}
-__device__ __forceinline__ uint4 pack_bf8(const float *v) {
-    return make_uint4(pack_bf2(v[0], v[1]), pack_bf2(v[2], v[3]), pack_bf2(v[4], v[5]),
-                      pack_bf2(v[6], v[7]));
-}
-__device__ __forceinline__ void unpack_bf8(uint4 u, float *v) {
-    const uint32_t w[4] = {u.x, u.y, u.z, u.w};
-#pragma unroll
-    for (int i = 0; i < 4; i++) {
-        v[2 * i] = __uint_as_float(w[i] << 16);
-        v[2 * i + 1] = __uint_as_float(w[i] & 0xffff0000u);
-    }
-}
 __device__ __forceinline__ void ld_g8(const float *Gs, int t, int i0, float *v) {
     const float4 a = *reinterpret_cast<const float4 *>(Gs + gsw(t, i0));
     const float4 b = *reinterpret_cast<const float4 *>(Gs + gsw(t, i0 + 4));
@@ -116,7 +94,6 @@ __device__ __forceinline__ void ld_f8(const float *p, float *v) {
     const float4 b = reinterpret_cast<const float4 *>(p)[1];
     v[0] = a.x, v[1] = a.y, v[2] = a.z, v[3] = a.w, v[4] = b.x, v[5] = b.y, v[6] = b.z, v[7] = b.w;
 }
-__device__ __forceinline__ void st16s(uint8_t *p, uint4 v) { *reinterpret_cast<uint4 *>(p) = v; }
 
 struct PrepMaps {
     CUtensorMap q, k, v, g;         // inputs (loads)
@@ -763,11 +740,6 @@ struct ScanCfg {
 };
 static_assert(ScanCfg<128>::SMEM <= 232448 && ScanCfg<64>::SMEM <= 232448, "scan shared memory");
 
-__device__ __forceinline__ bool warp_wait_all(uint64_t *bar, uint32_t parity, unsigned *err,
-                                              unsigned code) {
-    const bool ok = mbar_wait(bar, parity, err, code);
-    return __all_sync(0xffffffffu, ok);
-}
 
 // One CTA per (sequence, head, DVT-column slice of d_v). Warps 0-3: thread i owns state row i
 // (TMEM lane i) and, for the M=64 output tile, token row 16 w + lane of lanes 0-15; warp 4:

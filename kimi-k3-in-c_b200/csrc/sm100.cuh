@@ -19,6 +19,7 @@
 #pragma once
 
 #include <cuda.h>
+#include <cuda_bf16.h>
 #include <stdint.h>
 
 namespace k3 {
@@ -144,6 +145,13 @@ __device__ __forceinline__ bool mbar_wait_cluster(uint64_t *bar, uint32_t parity
     return mbar_wait_impl<true>(bar, parity, err, code);
 }
 
+// Bounded wait by a whole warp; true only if every lane's wait completed.
+__device__ __forceinline__ bool warp_wait_all(uint64_t *bar, uint32_t parity, unsigned *err,
+                                              unsigned code) {
+    const bool ok = mbar_wait(bar, parity, err, code);
+    return __all_sync(0xffffffffu, ok);
+}
+
 // Bounded wait that reports nothing (used only to drain a CTA's own loads on exit).
 __device__ __forceinline__ bool mbar_wait_quiet(uint64_t *bar, uint32_t parity) {
     const long long t0 = clock64();
@@ -152,7 +160,47 @@ __device__ __forceinline__ bool mbar_wait_quiet(uint64_t *bar, uint32_t parity) 
     return true;
 }
 
+// ------------------------------------------------------------------ SW128 tiles, bf16
+// byte offset of the 16-byte chunk `c` (0..7) of row `r` in a 128-byte-swizzled tile whose
+// base is 1024-byte aligned
+__device__ __forceinline__ uint32_t swz(int r, int c) {
+    return (uint32_t)(r * 128 + (((c ^ r) & 7) << 4));
+}
+// byte offset of bf16 element (r, c), c < 64, of such a tile
+__device__ __forceinline__ uint32_t swz_elem(int r, int c) {
+    return swz(r, c >> 3) + (uint32_t)(c & 7) * 2;
+}
+
+__device__ __forceinline__ uint32_t pack_bf2(float a, float b) {
+    const __nv_bfloat162 p = __floats2bfloat162_rn(a, b);
+    return *reinterpret_cast<const uint32_t *>(&p);
+}
+__device__ __forceinline__ uint4 pack_bf8(const float *v) {
+    return make_uint4(pack_bf2(v[0], v[1]), pack_bf2(v[2], v[3]), pack_bf2(v[4], v[5]),
+                      pack_bf2(v[6], v[7]));
+}
+__device__ __forceinline__ void unpack_bf8(uint4 u, float *v) {
+    const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+    for (int i = 0; i < 4; i++) {
+        v[2 * i] = __uint_as_float(w[i] << 16);
+        v[2 * i + 1] = __uint_as_float(w[i] & 0xffff0000u);
+    }
+}
+__device__ __forceinline__ void st16s(uint8_t *p, uint4 v) { *reinterpret_cast<uint4 *>(p) = v; }
+
 // ------------------------------------------------------------------------------ TMA
+// Untiled bulk copy of `bytes` (a multiple of 16; both addresses 16-byte aligned) from global
+// memory into this CTA's shared memory, completing on `bar` (transaction bytes).
+__device__ __forceinline__ void bulk_load(void *dst, const void *src, uint32_t bytes,
+                                          uint64_t *bar) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::
+            "r"(smem_u32(dst)),
+        "l"(src), "r"(bytes), "r"(smem_u32(bar))
+        : "memory");
+}
+
 // 2-D tiled load of box (c0 = inner, c1 = outer) into shared memory, completing on `bar`
 // (transaction bytes). The destination is this CTA's own shared memory.
 __device__ __forceinline__ void tma_load_2d(void *dst, const CUtensorMap *map, uint64_t *bar,

@@ -287,11 +287,13 @@ def test_prefill_without_state_and_alpha_gate(ctx):
     assert W.rel_fro(o1, o_ref) < TOL_F32 and W.rel_fro(o2, o_ref) < TOL_F32
 
 
-def test_prefill_extreme_decay_takes_the_exact_path(ctx):
+@pytest.mark.parametrize("d", [64, 128])
+def test_prefill_extreme_decay_takes_the_exact_path(ctx, d):
     """Channels decaying by e^-30 per token overflow a 15-token anchor; the kernel must form
-    those sub-block entries directly and still match."""
+    those sub-block entries directly and still match (fp32; d = 128 runs the tensor-core
+    scan on the intra-chunk kernel's hi/lo operands)."""
     rng = np.random.default_rng(9)
-    H, d, T = 2, 64, 128
+    H, T = 2, 128
     t = W.kda_tokens(rng, T, H, d, d, bf16=False)
     t["g"][:, :, :8] = -30.0
     t["g"][:, :, 8:16] = 0.0  # alpha == 1 exactly: perfect retention is legitimate
@@ -300,6 +302,34 @@ def test_prefill_extreme_decay_takes_the_exact_path(ctx):
     o_ref, S_ref = oracle.kda_recurrence(t["q"], t["k"], t["v"], t["g"], t["beta"], cu)
     assert np.all(np.isfinite(o)) and np.all(np.isfinite(S))
     assert W.rel_fro(o, o_ref) < TOL_F32 and W.rel_fro(S, S_ref) < TOL_F32
+
+
+# fp32 q/k/v/o at d = 128 run the tensor-core scan with every operand split into bf16 hi + lo
+# (three MMAs per product): about 2^-16 relative error per product, so this bar sits far
+# below what single bf16 operands reach (~4e-3) and far above fp32 rounding.
+TOL_SPLIT = 1e-4
+
+
+def test_prefill_varlen_ragged_fp32_tensor_core(ctx):
+    """fp32 I/O, d = 128: empty, single-token, exact-chunk and partial-chunk sequences with a
+    nonzero initial state, every sequence checked on its own at the split-precision bar."""
+    rng = np.random.default_rng(41)
+    H, d = 3, 128
+    cu = np.concatenate([[0], np.cumsum(RAGGED)]).astype(np.int32)
+    t = W.kda_tokens(rng, int(cu[-1]), H, d, d, bf16=False)
+    S0 = rng.standard_normal((len(RAGGED), H, d, d), dtype=np.float32) * np.float32(0.05)
+    o, S = run_prefill(ctx, t["q"], t["k"], t["v"], t["g"], t["beta"], cu, S0=S0,
+                       io=k3cuda.F32)
+    o_ref, S_ref = oracle.kda_recurrence(t["q"], t["k"], t["v"], t["g"], t["beta"], cu, state=S0,
+                                         nthreads=oracle.max_threads())
+    assert W.rel_fro(o, o_ref) < TOL_SPLIT
+    assert W.rel_fro(S, S_ref) < TOL_SPLIT
+    for n in range(len(RAGGED)):
+        a, b = cu[n], cu[n + 1]
+        if b > a:
+            assert W.rel_fro(o[a:b], o_ref[a:b]) < TOL_SPLIT, n
+        assert W.rel_fro(S[n], S_ref[n]) < TOL_SPLIT, n
+    assert np.array_equal(S[0], S0[0]) and np.array_equal(S[5], S0[5])  # empty: untouched
 
 
 def test_prefill_extreme_decay_bf16_tensor_core(ctx):
