@@ -59,7 +59,9 @@ struct ChunkDesc {
 // fp32 block below): every operand as a hi plane bf16(x) and a lo plane bf16(x - hi), each
 // laid out as the 128-byte-swizzled shared-memory image the scan's MMAs read, so that one
 // untiled bulk copy per group stages it. Byte offsets:
-constexpr int W32_KQH = 0;        // [Qtil; Ktil] [128 rows][128 i], two K-blocks of [128][64]
+constexpr int W32_KQH = 0;        // [Qtil | Ktil] [128 rows][128 i], two K-blocks of [128][64]
+                                  // (rows interleaved by sixteen: 32 q + l, l < 16, is Qtil
+                                  // row 16 q + l; 32 q + 16 + l is Ktil row 16 q + l)
 constexpr int W32_KQL = 32768;
 constexpr int W32_MH = 65536;     // M = (I + Akk)^-1 diag(beta) [64 t][64 s], K-major
 constexpr int W32_ML = 73728;
@@ -169,9 +171,11 @@ kda_chunk_intra(const ChunkDesc *__restrict__ chunks, const IO *__restrict__ q,
             const float G = sG[t * LP + ic];
             const float eg = expf(G);
             if constexpr (TC32) {
-                const uint32_t kq = (ic >> 6) * 16384 + sm100::swz_elem(t, ic & 63);
-                put_split(ob, W32_KQH, W32_KQL, kq, qr[u] * eg);         // row t
-                put_split(ob, W32_KQH, W32_KQL, kq + 8192, kr[u] * eg);  // row 64 + t
+                // Qtil row t at A row 32 (t / 16) + t % 16, Ktil row t sixteen rows after it
+                const int rq = 32 * (t >> 4) + (t & 15);
+                const uint32_t kq = (ic >> 6) * 16384 + sm100::swz_elem(rq, ic & 63);
+                put_split(ob, W32_KQH, W32_KQL, kq, qr[u] * eg);
+                put_split(ob, W32_KQH, W32_KQL, kq + 16 * 128, kr[u] * eg);
                 put_split(ob, W32_KBH, W32_KBL, (ic >> 6) * 8192 + sm100::swz_elem(t, ic & 63),
                           kr[u] * expf(GC - G));
             } else {
@@ -558,7 +562,7 @@ kda_chunk_scan(const ChunkDesc *__restrict__ chunks, const int *__restrict__ seq
 // Shared-memory plan of kda_scan_tc32 (bytes from a 1024-aligned base). The operand groups
 // keep the offsets of the workspace block, so each is one bulk copy.
 struct Scan32 {
-    static constexpr int KQ = W32_KQH, KQ_BYTES = 65536;   // [Qtil; Ktil] hi, lo
+    static constexpr int KQ = W32_KQH, KQ_BYTES = 65536;   // [Qtil | Ktil] hi, lo
     static constexpr int M = W32_MH, M_BYTES = 16384;      // M hi, lo
     static constexpr int KA = W32_AH, KA_BYTES = 49152;    // Aqk hi, lo; Kbar hi, lo
     static constexpr int S16H = 131072, S16L = 147456;     // state [128 i][64 j], MN-major
@@ -566,47 +570,54 @@ struct Scan32 {
     static constexpr int DH = 180224, DL = 188416;         // Delta = M X [64 s][64 j]
     static constexpr int BYTES = 196608, SMEM = BYTES + 1024;
     static constexpr uint32_t TM_Y = 0, TM_D = 128, TM_S = 192, TM_COLS = 256;
+    static constexpr int THREADS = 320;                    // 8 compute warps, producer, MMA
 };
 static_assert(Scan32::SMEM <= 232448, "tc32 scan shared memory");
 static_assert(W32_KQL == W32_KQH + 32768 && W32_AH + Scan32::KA_BYTES == W32_G,
               "operand groups are contiguous in the workspace block");
 
+__device__ __forceinline__ void prefetch_l2(const void *p) {
+    asm volatile("prefetch.global.L2 [%0];" ::"l"(p));
+}
+
 template <bool VEC>
-__device__ __forceinline__ void ld_row64(float *dst, const float *src) {
+__device__ __forceinline__ void ld_row32(float *dst, const float *src) {
     if constexpr (VEC) {
 #pragma unroll
-        for (int c = 0; c < 64; c += 4) {
+        for (int c = 0; c < 32; c += 4) {
             const float4 x = *reinterpret_cast<const float4 *>(src + c);
             dst[c] = x.x, dst[c + 1] = x.y, dst[c + 2] = x.z, dst[c + 3] = x.w;
         }
     } else {
 #pragma unroll
-        for (int c = 0; c < 64; c++) dst[c] = src[c];
+        for (int c = 0; c < 32; c++) dst[c] = src[c];
     }
 }
 template <bool VEC>
-__device__ __forceinline__ void st_row64(float *dst, const float *src) {
+__device__ __forceinline__ void st_row32(float *dst, const float *src) {
     if constexpr (VEC) {
 #pragma unroll
-        for (int c = 0; c < 64; c += 4)
+        for (int c = 0; c < 32; c += 4)
             *reinterpret_cast<float4 *>(dst + c) =
                 make_float4(src[c], src[c + 1], src[c + 2], src[c + 3]);
     } else {
 #pragma unroll
-        for (int c = 0; c < 64; c++) dst[c] = src[c];
+        for (int c = 0; c < 32; c++) dst[c] = src[c];
     }
 }
-// bf16 hi and lo halves of a 64-value row into row r of two MN-major [rows][64] tiles
-__device__ __forceinline__ void put_row_split(uint8_t *hi, uint8_t *lo, int r, const float *x) {
+// bf16 hi and lo halves of 32 values into columns [32 hf, 32 hf + 32) of row r of two
+// MN-major [rows][64] tiles
+__device__ __forceinline__ void put_half_split(uint8_t *hi, uint8_t *lo, int r, int hf,
+                                               const float *x) {
 #pragma unroll
-    for (int c = 0; c < 8; c++) {
+    for (int c = 0; c < 4; c++) {
         float h[8], l[8];
         const uint4 ph = sm100::pack_bf8(x + 8 * c);
         sm100::unpack_bf8(ph, h);
 #pragma unroll
         for (int u = 0; u < 8; u++) l[u] = x[8 * c + u] - h[u];
-        sm100::st16s(hi + sm100::swz(r, c), ph);
-        sm100::st16s(lo + sm100::swz(r, c), sm100::pack_bf8(l));
+        sm100::st16s(hi + sm100::swz(r, 4 * hf + c), ph);
+        sm100::st16s(lo + sm100::swz(r, 4 * hf + c), sm100::pack_bf8(l));
     }
 }
 
@@ -615,17 +626,20 @@ __device__ __forceinline__ void put_row_split(uint8_t *hi, uint8_t *lo, int r, c
 // (hi.hi + hi.lo + lo.hi, fp32 accumulation in TMEM), which leaves about 2^-16 relative error
 // per product instead of bf16's 2^-8. One CTA per (sequence, head, 64-column half of d_v);
 // the fp32 state half lives in TMEM. Per chunk:
-//   Y  = [Qtil; Ktil] S16         (M=128: rows 0-63 Qtil S, rows 64-127 Ktil S)
-//   X  = V - (Ktil S)             compute warps 2-3 (TMEM lanes 64-127), bf16 hi/lo to smem
+//   Y  = [Qtil | Ktil] S16        (M=128; the A rows interleave by sixteen: row 32 q + l is
+//                                 Qtil row 16 q + l for l < 16 and Ktil row 16 q + l - 16
+//                                 otherwise, so every TMEM lane quarter holds 16 rows of each)
+//   X  = V - (Ktil S)             lanes 16-31 of every quarter, bf16 hi/lo to shared memory
 //   D  = M X                      (M=64)
 //   S' = Gamma S + Kbar^T D       (M=128, into the state accumulator, already scaled)
-//   O  = Qtil S + Aqk D           (into rows 0-63 of Y; the M=128 A operand's rows 64-127
-//                                 read the next shared tile and land on Y's dead Ktil S rows)
-// then S' is copied to S16 (hi/lo) and scaled by the next Gamma in TMEM. Warps 0-3: thread
-// i owns TMEM lane i; warp 4: bulk-copy producer; warp 5: TMEM allocation and MMA issue. Y is
-// double-buffered in TMEM so that a chunk's outputs are read while the next chunk runs.
+//   O  = Qtil S + Aqk D           (M=64 into Y's columns: an M=64 accumulator's row 16 q + l
+//                                 is lane 32 q + l, exactly where Y holds Qtil S)
+// then S' is copied to S16 (hi/lo) and scaled by the next Gamma in TMEM. Warps 0-7 compute:
+// warp w reads lane quarter w % 4, columns [32 (w / 4), +32); warp 8: bulk-copy producer;
+// warp 9: TMEM allocation and MMA issue. Y is double-buffered in TMEM so that a chunk's
+// outputs are read while the next chunk runs.
 template <bool VEC>
-__global__ void __launch_bounds__(192, 1)
+__global__ void __launch_bounds__(Scan32::THREADS, 1)
 kda_scan_tc32(const ChunkDesc *__restrict__ chunks, const int *__restrict__ seq_chunk0,
               const int *__restrict__ seq_order, const uint8_t *__restrict__ ws,
               const float *__restrict__ v, float *__restrict__ state, float *__restrict__ o,
@@ -642,6 +656,7 @@ kda_scan_tc32(const ChunkDesc *__restrict__ chunks, const int *__restrict__ seq_
     const int n = seq_order[blockIdx.x / (2 * H)];
     const int c0 = seq_chunk0[n], nc = seq_chunk0[n + 1] - c0;
     const int col0 = 64 * half;
+    constexpr uint32_t NCOMP = 256;
     auto block = [&](int j) { return ws + ((size_t)(c0 + j) * H + h) * W32_BYTES; };
 
     if (tid == 0) {
@@ -652,22 +667,22 @@ kda_scan_tc32(const ChunkDesc *__restrict__ chunks, const int *__restrict__ seq_
         mbar_init(&ka_full, 1);
         mbar_init(&ka_empty, 1);
         mbar_init(&y_done, 1);
-        mbar_init(&x_ready, 128);
+        mbar_init(&x_ready, NCOMP);
         mbar_init(&dx_done, 1);
-        mbar_init(&d_ready, 128);
+        mbar_init(&d_ready, NCOMP);
         mbar_init(&s_done, 1);
         mbar_init(&o_done, 1);
-        mbar_init(&s16_ready, 128);
+        mbar_init(&s16_ready, NCOMP);
         mbar_init(&mma_fin, 1);
         fence_barrier_init();
     }
-    if (warp == 5) tmem_alloc(&tslot, C::TM_COLS);
+    if (warp == 9) tmem_alloc(&tslot, C::TM_COLS);
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
     const uint32_t tb = tslot;
 
-    if (warp == 4) {
+    if (warp == 8) {
         if (lane == 0) {
             int last_kq = -1, last_m = -1, last_ka = -1;
             for (int j = 0; j < nc; j++) {
@@ -691,10 +706,10 @@ kda_scan_tc32(const ChunkDesc *__restrict__ chunks, const int *__restrict__ seq_
             if (last_m >= 0) mbar_wait_quiet(&m_full, last_m & 1);
             if (last_ka >= 0) mbar_wait_quiet(&ka_full, last_ka & 1);
         }
-    } else if (warp == 5) {
+    } else if (warp == 9) {
         if (lane == 0) {
             constexpr uint32_t id_y = idesc_f16(128, 64, false, true);
-            constexpr uint32_t id_d = idesc_f16(64, 64, false, true);
+            constexpr uint32_t id_m = idesc_f16(64, 64, false, true);
             constexpr uint32_t id_s = idesc_f16(128, 64, true, true);
             const uint64_t dk = sdesc_kmajor(smem_u32(sm));
             const uint64_t d8 = sdesc_mnmajor(smem_u32(sm), 8192);
@@ -702,7 +717,7 @@ kda_scan_tc32(const ChunkDesc *__restrict__ chunks, const int *__restrict__ seq_
             bool issued = false;
             for (int j = 0; j < nc; j++) {
                 const uint32_t par = j & 1, yb = tb + C::TM_Y + 64 * (j & 1);
-                // Y = [Qtil; Ktil] . S16
+                // Y = [Qtil | Ktil] . S16
                 if (!mbar_wait(&kq_full, par, err, 0x704)) break;
                 if (!mbar_wait(&s16_ready, par, err, 0x705)) break;
                 tc_fence_after();
@@ -727,11 +742,11 @@ kda_scan_tc32(const ChunkDesc *__restrict__ chunks, const int *__restrict__ seq_
 #pragma unroll
                     for (int ks = 0; ks < 4; ks++)
                         mma_bf16_ss(tb + C::TM_D, dk + ((a + ks * 32) >> 4),
-                                    d8 + ((b + ks * 2048) >> 4), id_d, (p | ks) ? 1u : 0u);
+                                    d8 + ((b + ks * 2048) >> 4), id_m, (p | ks) ? 1u : 0u);
                 }
                 mma_commit(&dx_done);
                 mma_commit(&m_empty);
-                // S += Kbar^T . D, then O (rows 0-63 of Y) += Aqk . D
+                // S += Kbar^T . D, then O (the Qtil rows of Y) += Aqk . D
                 if (!mbar_wait(&ka_full, par, err, 0x708)) break;
                 if (!mbar_wait(&d_ready, par, err, 0x709)) break;
                 tc_fence_after();
@@ -750,7 +765,7 @@ kda_scan_tc32(const ChunkDesc *__restrict__ chunks, const int *__restrict__ seq_
 #pragma unroll
                     for (int ks = 0; ks < 4; ks++)
                         mma_bf16_ss(yb, dk + ((a + ks * 32) >> 4), d8 + ((b + ks * 2048) >> 4),
-                                    id_y, 1u);
+                                    id_m, 1u);
                 }
                 mma_commit(&o_done);
                 mma_commit(&ka_empty);
@@ -763,23 +778,25 @@ kda_scan_tc32(const ChunkDesc *__restrict__ chunks, const int *__restrict__ seq_
         }
     } else if (nc > 0) {
         // ----------------------------------------------------------- compute warps
-        const int i = tid;  // TMEM lane: state row i; Y row i; D row 16 warp + lane (lane < 16)
-        const uint32_t lq = (uint32_t)(32 * warp) << 16;
-        float *Sg = state ? state + (((size_t)n * H + h) * 128 + i) * 128 + col0 : nullptr;
+        const int q = warp & 3, hf = warp >> 2;          // lane quarter, column half
+        const int i = 32 * q + lane;                     // TMEM lane: state row i
+        const int r16 = 16 * q + (lane & 15);            // token row of this lane's Y / D / O
+        const uint32_t lq = ((uint32_t)(32 * q) << 16) + 32 * hf;
+        float *Sg = state ? state + (((size_t)n * H + h) * 128 + i) * 128 + col0 + 32 * hf
+                          : nullptr;
         auto gamma = [&](int jj) {
             return jj < nc ? reinterpret_cast<const float *>(block(jj) + W32_G)[i] : 0.f;
         };
-        float s[64];
+        float s[32];
         auto tmem_row = [&](uint32_t col, float *dst) {
             tmem_ld32(tb + lq + col, dst);
-            tmem_ld32(tb + lq + col + 32, dst + 32);
             tmem_wait_ld();
         };
         // S16 <- S (hi, lo); TMEM state <- gam * S
         auto publish = [&](float gam) {
-            put_row_split(sm + C::S16H, sm + C::S16L, i, s);
+            put_half_split(sm + C::S16H, sm + C::S16L, i, hf, s);
 #pragma unroll
-            for (int c = 0; c < 64; c += 16) {
+            for (int c = 0; c < 32; c += 16) {
                 float x[16];
 #pragma unroll
                 for (int u = 0; u < 16; u++) x[u] = s[c + u] * gam;
@@ -791,47 +808,64 @@ kda_scan_tc32(const ChunkDesc *__restrict__ chunks, const int *__restrict__ seq_
             mbar_arrive(&s16_ready);
         };
         if (Sg) {
-            ld_row64<VEC>(s, Sg);
+            ld_row32<VEC>(s, Sg);
         } else {
 #pragma unroll
-            for (int c = 0; c < 64; c++) s[c] = 0.f;
+            for (int c = 0; c < 32; c++) s[c] = 0.f;
         }
         publish(gamma(0));
         float gam1 = gamma(1), gam2 = gamma(2);
+        const bool krow = lane >= 16;  // this lane's Y row is Ktil S (else Qtil S)
+        auto vrow = [&](const ChunkDesc &c) {
+            return v + ((size_t)(c.t0 + r16) * H + h) * 128 + col0 + 32 * hf;
+        };
+        // the chunk table runs one chunk ahead and V two (into L2), so that the V rows a
+        // chunk subtracts are on chip when its Y is ready
+        ChunkDesc cd_next = chunks[c0];
+        if (krow && nc > 1) {
+            const ChunkDesc c1 = chunks[c0 + 1];
+            if (r16 < c1.len) prefetch_l2(vrow(c1));
+        }
         bool ok = true;
         for (int j = 0; j < nc && ok; j++) {
-            const ChunkDesc cd = chunks[c0 + j];
+            const ChunkDesc cd = cd_next;
+            if (j + 1 < nc) cd_next = chunks[c0 + j + 1];
             const uint32_t par = j & 1, yb = C::TM_Y + 64 * (j & 1);
-            // X = V - Ktil S (token t = i - 64 on warps 2-3); V is loaded before the wait
-            float x[64];
-            const int t = i - 64;
-            if (warp >= 2) {
-                if (t < cd.len) {
-                    ld_row64<VEC>(x, v + ((size_t)(cd.t0 + t) * H + h) * 128 + col0);
+            // X = V - Ktil S; V is loaded before the wait
+            float x[32];
+            if (krow) {
+                if (r16 < cd.len) {
+                    ld_row32<VEC>(x, vrow(cd));
                 } else {
 #pragma unroll
-                    for (int c = 0; c < 64; c++) x[c] = 0.f;
+                    for (int c = 0; c < 32; c++) x[c] = 0.f;
+                }
+                if (j + 2 < nc) {
+                    const ChunkDesc c2 = chunks[c0 + j + 2];
+                    if (r16 < c2.len) prefetch_l2(vrow(c2));
                 }
             }
             if (!(ok = warp_wait_all(&y_done, par, err, 0x70a))) break;
             tc_fence_after();
-            if (warp >= 2) {
-                float y[64];
+            {
+                float y[32];
                 tmem_row(yb, y);
+                if (krow) {
 #pragma unroll
-                for (int c = 0; c < 64; c++) x[c] -= y[c];
-                put_row_split(sm + C::XH, sm + C::XL, t, x);
+                    for (int c = 0; c < 32; c++) x[c] -= y[c];
+                    put_half_split(sm + C::XH, sm + C::XL, r16, hf, x);
+                }
             }
             fence_async_shared();
             tc_fence_before();
             mbar_arrive(&x_ready);
-            // D rows to shared memory (row 16 warp + lane on lanes 0-15)
+            // D rows to shared memory (row 16 q + lane on lanes 0-15)
             if (!(ok = warp_wait_all(&dx_done, par, err, 0x70b))) break;
             tc_fence_after();
             {
-                float dd[64];
+                float dd[32];
                 tmem_row(C::TM_D, dd);
-                if (lane < 16) put_row_split(sm + C::DH, sm + C::DL, 16 * warp + lane, dd);
+                if (!krow) put_half_split(sm + C::DH, sm + C::DL, r16, hf, dd);
             }
             fence_async_shared();
             tc_fence_before();
@@ -845,22 +879,23 @@ kda_scan_tc32(const ChunkDesc *__restrict__ chunks, const int *__restrict__ seq_
                 gam1 = gam2;
                 gam2 = gamma(j + 3);
             } else if (Sg) {
-                st_row64<VEC>(Sg, s);
+                st_row32<VEC>(Sg, s);
             }
-            // outputs of the chunk (rows 0-63 of Y: warps 0-1)
+            // outputs of the chunk (the Qtil rows of Y, lanes 0-15)
             if (!(ok = warp_wait_all(&o_done, par, err, 0x70d))) break;
             tc_fence_after();
-            if (warp < 2) {
-                float y[64];
+            {
+                float y[32];
                 tmem_row(yb, y);
-                if (i < cd.len) st_row64<VEC>(o + ((size_t)(cd.t0 + i) * H + h) * 128 + col0, y);
+                if (!krow && r16 < cd.len)
+                    st_row32<VEC>(o + ((size_t)(cd.t0 + r16) * H + h) * 128 + col0 + 32 * hf, y);
             }
             tc_fence_before();
         }
     }
     tc_fence_before();
     __syncthreads();
-    if (warp == 5) {
+    if (warp == 9) {
         __syncwarp();
         tmem_dealloc(tb, C::TM_COLS);
     }
@@ -945,7 +980,7 @@ static int run_prefill(k3cuda_ctx *ctx, float *state, void *o, const void *q, co
         const unsigned nblk32 = (unsigned)((long long)n_seq * H * 2);
         auto launch = [&](auto kern) {
             if (int rc_ = set_smem(kern, Scan32::SMEM)) return rc_;
-            kern<<<nblk32, 192, Scan32::SMEM, ctx->stream>>>(
+            kern<<<nblk32, Scan32::THREADS, Scan32::SMEM, ctx->stream>>>(
                 d_table, d_c0, d_c0 + n_seq + 1, (const uint8_t *)blocks, (const float *)v, state,
                 (float *)o, H, ctx->err_word);
             return after_launch(ctx, "kda_scan_tc32");
