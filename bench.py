@@ -440,7 +440,7 @@ def prefill_record(args, D: Dist, which, tokens=None, cpu=True):
     cu = c["cu_seqlens"]
     T, nseq = int(cu[-1]), len(cu) - 1
     ctx = k3cuda.Context(D.local)
-    f32 = getattr(args, "io", "bf16") == "f32"  # fp32 q/k/v/o: the CUDA-core chunk kernels
+    f32 = getattr(args, "io", "bf16") == "f32"  # fp32 q/k/v/o: the path the C99 drop-ins take
     if f32 and R > 1:
         raise ValueError("--io f32 runs on one GPU (the gathered exchange is bf16)")
     et = np.float32 if f32 else np.uint16
@@ -536,7 +536,8 @@ def prefill_record(args, D: Dist, which, tokens=None, cpu=True):
         "higher_is_better": True, "scaling": "strong", "dtype": "mixed",
         "config": {"workload": name, "tokens": T, "sequences": nseq, "heads_total": H_total,
                    "heads_per_gpu": Hl, "d": d, "chunk": 64,
-                   "io": ("fp32 q/k/v/o/g/beta/state (CUDA-core chunk kernels)" if f32 else
+                   "io": ("fp32 q/k/v/o/g/beta/state (fp32 intra-chunk kernel, tcgen05 "
+                          "scan on bf16 hi/lo operands)" if f32 else
                           "bf16 q/k/v/o, fp32 g/beta/state"),
                    "parallelism": f"head-shard x{R}" + (", output exchange fused into the "
                                                         "prefill (peer stores over NVLink)"
@@ -1255,8 +1256,8 @@ def main():
     ap.add_argument("--no-subrecords", action="store_true",
                     help="decode: print the headline alone, without the config-2/3/4 records")
     ap.add_argument("--io", default="bf16", choices=["bf16", "f32"],
-                    help="prefill / varlen: the q/k/v/o element type (f32: the CUDA-core chunk "
-                         "kernels the fp32 drop-ins use; one GPU)")
+                    help="prefill / varlen: the q/k/v/o element type (f32: the path the fp32 "
+                         "drop-ins use; one GPU)")
     ap.add_argument("--batch", type=int, default=None,
                     help="mla: sequences per GPU in place of 64 / N (a profiling case: the "
                          "per-GPU share of config 4 at more GPUs)")

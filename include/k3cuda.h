@@ -155,7 +155,11 @@ int k3cuda_kda_decode_host(k3cuda_ctx *ctx, float *state, void *o, const void *q
  *               [n_streams]
  *   chunk       64 (the only chunk size built)
  * Supported: dk == dv == 64 or 128. workspace must hold k3cuda_kda_prefill_workspace()
- * bytes (device memory, 256-byte aligned). */
+ * bytes (device memory, 256-byte aligned). Arithmetic: bf16 I/O at d = 128 runs on the
+ * tensor cores with bf16 operands and fp32 accumulation; fp32 I/O at d = 128 runs its
+ * chunk-local algebra in fp32 and the scan on the tensor cores with every operand split
+ * into bf16 hi + lo (about 2^-16 relative error per product); d = 64 runs in fp32 on the
+ * CUDA cores. */
 int k3cuda_kda_prefill_workspace(const int *cu_seqlens, int n_seq, int H, int dk, int dv,
                                  int chunk, size_t *bytes);
 int k3cuda_kda_prefill(k3cuda_ctx *ctx, float *state, void *o, const void *q,

@@ -10,14 +10,18 @@
 // with Ktil_t = e^G_t k_t, Qtil_t = e^G_t q_t (q pre-multiplied by q_scale) and
 // Kbar_s = e^(G_C - G_s) k_s. Every factor above is <= 1, so nothing overflows.
 //
-// Two kernels:
-//   kda_chunk_intra  one CTA per (chunk, head), all chunks in parallel: G, Akk, Aqk with
-//                    16-token sub-block anchors, M = (I + Akk)^-1 diag(beta) by forward
-//                    substitution, and the scaled operands Qtil, Ktil, Kbar, e^G_C.
-//   kda_chunk_scan   one CTA per (sequence, head, 32-column slice of d_v): walks the
-//                    sequence's chunks in order with its state slice in shared memory:
+// Kernels (bf16 q/k/v/o at d = 128 take kda_prefill_tc.cu instead):
+//   kda_chunk_intra  one CTA per (chunk, head), all chunks in parallel, fp32: G, Akk, Aqk
+//                    with 16-token sub-block anchors, M = (I + Akk)^-1 diag(beta) by blocked
+//                    forward substitution, and the scaled operands Qtil, Ktil, Kbar, e^G_C.
+//   kda_scan_tc32    fp32 I/O at d = 128: one CTA per (sequence, head, 64-column half of d_v)
+//                    walks the sequence's chunks on tcgen05 with the state half in TMEM,
+//                    every operand a bf16 hi + lo pair (three MMAs per product):
 //                    X = V - Ktil S; Delta = M X; O = Qtil S + Aqk Delta;
 //                    S = e^G_C S + Kbar^T Delta.
+//   kda_chunk_scan   d = 64: the same steps on the CUDA cores, one CTA per (sequence, head,
+//                    32-column slice of d_v) with its state slice in registers and shared
+//                    memory.
 // Columns of the state are independent in every step, which is what lets the scan split
 // d_v across CTAs with no communication.
 //

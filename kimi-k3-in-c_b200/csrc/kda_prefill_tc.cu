@@ -43,8 +43,8 @@
 //
 // Operand precision: every tensor-core operand is bf16 and every accumulation fp32; the
 // state itself stays fp32 (Gamma is applied in fp32, and only the products with P and Q'
-// see its bf16 copy). fp32 I/O keeps the CUDA-core path of kda_prefill.cu, which is exact
-// to fp32 rounding.
+// see its bf16 copy). fp32 I/O takes kda_prefill.cu's fp32 intra-chunk kernel and its
+// tensor-core scan over bf16 hi + lo operands (fp32-level products).
 #include <vector>
 
 #include "internal.cuh"
