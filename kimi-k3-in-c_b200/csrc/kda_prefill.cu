@@ -701,6 +701,9 @@ kda_scan_tc32(const ChunkDesc *__restrict__ chunks, const int *__restrict__ seq_
                 bulk_load(sm + C::M, b + W32_MH, C::M_BYTES, &m_full);
                 last_m = j;
                 if (j > 0 && !mbar_wait(&ka_empty, pe, err, 0x703)) break;
+                // and after this chunk's Y products, so that the copy does not compete with
+                // them for shared memory (it is first read by the chunk's state update)
+                if (!mbar_wait(&kq_empty, j & 1, err, 0x70e)) break;
                 mbar_expect_tx(&ka_full, C::KA_BYTES);
                 bulk_load(sm + C::KA, b + W32_AH, C::KA_BYTES, &ka_full);
                 last_ka = j;
