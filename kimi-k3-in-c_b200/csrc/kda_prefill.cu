@@ -138,16 +138,24 @@ kda_chunk_intra(const ChunkDesc *__restrict__ chunks, const IO *__restrict__ q,
 
     float kr[TG], qr[TG];
     {
+        // every load in flight at once: rows past the chunk's end read its last row (in
+        // bounds) and are zeroed afterwards
         float gr[TG];
+        {
+            const size_t o0 = ((size_t)cd.t0 * H + h) * DK + ic, rs = (size_t)H * DK;
 #pragma unroll
-        for (int u = 0; u < TG; u++) {
-            const int t = tg0 + u;
-            kr[u] = qr[u] = gr[u] = 0.f;
-            if (t < cd.len) {
-                const size_t off = ((size_t)(cd.t0 + t) * H + h) * DK + ic;
+            for (int u = 0; u < TG; u++) {
+                const size_t off = o0 + (size_t)min(tg0 + u, cd.len - 1) * rs;
                 kr[u] = io<IO>::ld(k + off);
-                qr[u] = io<IO>::ld(q + off) * q_scale;
-                gr[u] = load_gate(gate + off, gate_is_log);
+                qr[u] = io<IO>::ld(q + off);
+                gr[u] = gate[off];
+            }
+#pragma unroll
+            for (int u = 0; u < TG; u++) {
+                const bool in = tg0 + u < cd.len;
+                kr[u] = in ? kr[u] : 0.f;
+                qr[u] = in ? qr[u] * q_scale : 0.f;
+                gr[u] = in ? (gate_is_log ? gr[u] : logf(gr[u])) : 0.f;
             }
         }
         float acc = 0.f;
