@@ -332,6 +332,44 @@ def test_prefill_varlen_ragged_fp32_tensor_core(ctx):
     assert np.array_equal(S[0], S0[0]) and np.array_equal(S[5], S0[5])  # empty: untouched
 
 
+def test_prefill_fp32_unaligned_pointers_match_aligned(ctx):
+    """fp32 v, o and state 4 bytes off a 16-byte boundary (the tensor-core scan then takes
+    its scalar-access form): the results equal the aligned call's bit for bit."""
+    rng = np.random.default_rng(43)
+    H, d = 2, 128
+    cu = np.array([0, 100, 100, 230], np.int32)
+    T = int(cu[-1])
+    t = W.kda_tokens(rng, T, H, d, d, bf16=False)
+    S0 = rng.standard_normal((3, H, d, d), dtype=np.float32) * np.float32(0.05)
+    o_al, S_al = run_prefill(ctx, t["q"], t["k"], t["v"], t["g"], t["beta"], cu, S0=S0,
+                             io=k3cuda.F32)
+    L = k3cuda.lib()
+
+    def shifted(a):  # a device copy of `a` starting 4 bytes past a 16-byte boundary
+        a = np.ascontiguousarray(a, np.float32)
+        buf = ctx.empty((a.size + 4,), np.float32)
+        k3cuda.check(L.k3cuda_memcpy_h2d(ctx.h, buf.ptr + 4, a.ctypes.data, a.nbytes))
+        return buf, buf.ptr + 4
+
+    def fetch(p, shape):
+        out = np.empty(shape, np.float32)
+        k3cuda.check(L.k3cuda_memcpy_d2h(ctx.h, out.ctypes.data, p, out.nbytes))
+        return out
+
+    dq, dk_, dg, db = (ctx.upload(np.ascontiguousarray(t[x], np.float32))
+                       for x in ("q", "k", "g", "beta"))
+    vb, vp = shifted(t["v"])
+    sb, sp = shifted(S0)
+    ob, op = shifted(np.zeros((T, H, d), np.float32))
+    nws = ctx.kda_prefill_workspace(cu, H, d, d)
+    ws = ctx.empty((nws,), np.uint8)
+    ctx.kda_prefill(sp, op, dq, dk_, vp, dg, db, cu, H, d, d, 1.0 / np.sqrt(np.float32(d)), ws,
+                    nws, k3cuda.F32)
+    ctx.sync()
+    assert np.array_equal(fetch(op, (T, H, d)), o_al)
+    assert np.array_equal(fetch(sp, S0.shape), S_al)
+
+
 def test_prefill_extreme_decay_bf16_tensor_core(ctx):
     """The same overflow case through the tensor-core path (bf16, d=128): the flagged
     sub-blocks' columns of Akk/Aqk are recomputed exactly inside the intra-chunk kernel."""
