@@ -401,6 +401,22 @@ def test_prefill_alpha_gate_bf16_tensor_core(ctx):
     assert W.rel_fro(o, o_ref) < TOL_BF16 and W.rel_fro(S, S_ref) < TOL_BF16
 
 
+def test_prefill_config2_length_fp32_tensor_core(ctx):
+    """fp32 I/O over config 2's sequence length (512 chunks in one tensor-core scan, the state
+    carried as bf16 hi/lo between chunks): the split-precision error does not grow along the
+    chain."""
+    rng = np.random.default_rng(2)
+    T, H, d = 32768, 2, 128
+    t = W.kda_tokens(rng, T, H, d, d, bf16=False)
+    cu = np.array([0, T], np.int32)
+    o, S = run_prefill(ctx, t["q"], t["k"], t["v"], t["g"], t["beta"], cu, io=k3cuda.F32)
+    o_ref, S_ref = oracle.kda_recurrence(t["q"], t["k"], t["v"], t["g"], t["beta"], cu,
+                                         nthreads=oracle.max_threads())
+    assert W.rel_fro(o, o_ref) < TOL_SPLIT and W.rel_fro(S, S_ref) < TOL_SPLIT
+    # and the last chunk on its own
+    assert W.rel_fro(o[-64:], o_ref[-64:]) < TOL_SPLIT
+
+
 def test_prefill_config2_shape_reduced_heads(ctx):
     """BASELINE config 2's sequence length (T=32768, 512 chunks in one scan) at 2 heads."""
     rng = np.random.default_rng(0)
