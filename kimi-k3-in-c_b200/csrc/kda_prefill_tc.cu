@@ -32,7 +32,7 @@
 //       cores; W = M Ktil, U = M V (M as bf16 hi + lo); P = -Kbar^T W (M=128, N=128,
 //       K=64) and Aqk W on tcgen05. Writes P, Kbar, U, Q', Aqk (bf16; Aqk also its
 //       bf16 remainder) and Gamma (fp32).
-//   kda_scan_tc   one CTA per (sequence, head, 64- or 128-column slice of d_v). The fp32 state
+//   kda_scan_tc   one CTA per (sequence, head, 64-column half of d_v). The fp32 state
 //       slice lives in TMEM; per chunk the compute warps write its bf16 copy S16 to shared
 //       memory and scale the TMEM copy by Gamma (read two chunks ahead from the workspace),
 //       then one thread issues
@@ -718,8 +718,9 @@ struct ScanMaps {
     CUtensorMap p, kb, u, qp, a, al;
 };
 
-// Shared-memory plan of kda_scan_tc for DVT state columns per CTA (64: two CTAs per head,
-// 128: one). Operand stage (bytes from a 1024-aligned base):
+// Shared-memory plan of kda_scan_tc for DVT state columns per CTA (the launch uses 64: two
+// CTAs per head; 128, one CTA per head, also fits and measured slower). Operand stage (bytes
+// from a 1024-aligned base):
 template <int DVT>
 struct ScanCfg {
     static constexpr int P = 0;                      // P    [128][128]: 2 k-blocks [128][64]
@@ -1024,22 +1025,14 @@ int run_prefill_tc(k3cuda_ctx *ctx, float *state, void *o, const void *q, const 
     if (rc) return rc;
 
     ScanMaps sm{pm.p, pm.kb, pm.u, pm.qp, pm.a, pm.al};
-    // Few (sequence, head) pairs: two CTAs per head halve each chunk's chain; enough of them
-    // to fill the GPU: one CTA per head, half the operand traffic.
-    const bool wide = (long long)n_seq * H >= ctx->sm_count;
-    if (wide) {
-        using C = ScanCfg<128>;
-        if (int rc_ = set_smem(kda_scan_tc<128>, C::SMEM)) return rc_;
-        kda_scan_tc<128><<<(unsigned)((long long)n_seq * H), 192, C::SMEM, ctx->stream>>>(
-            sm, (const TcChunk *)d_table, d_c0, d_c0 + n_seq + 1, b, state, (__nv_bfloat16 *)o,
-            H, gout, ctx->err_word);
-    } else {
-        using C = ScanCfg<64>;
-        if (int rc_ = set_smem(kda_scan_tc<64>, C::SMEM)) return rc_;
-        kda_scan_tc<64><<<(unsigned)((long long)n_seq * H * 2), 192, C::SMEM, ctx->stream>>>(
-            sm, (const TcChunk *)d_table, d_c0, d_c0 + n_seq + 1, b, state, (__nv_bfloat16 *)o,
-            H, gout, ctx->err_word);
-    }
+    // Two CTAs per head (64 state columns each): every chunk's chain is half as long as with
+    // whole 128-column rows, which also pack the GPU more finely when there are many
+    // (sequence, head) pairs (config 3: 6.05 ms with whole rows, 5.98 ms with halves)
+    using C = ScanCfg<64>;
+    if (int rc_ = set_smem(kda_scan_tc<64>, C::SMEM)) return rc_;
+    kda_scan_tc<64><<<(unsigned)((long long)n_seq * H * 2), 192, C::SMEM, ctx->stream>>>(
+        sm, (const TcChunk *)d_table, d_c0, d_c0 + n_seq + 1, b, state, (__nv_bfloat16 *)o, H,
+        gout, ctx->err_word);
     return after_launch(ctx, "kda_scan_tc");
 }
 

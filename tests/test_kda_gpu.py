@@ -253,8 +253,8 @@ def test_prefill_varlen_ragged_bf16(ctx, d):
 
 
 def test_prefill_many_streams_bf16(ctx):
-    """Enough (sequence, head) streams that the tensor-core scan takes whole 128-column
-    state rows per CTA (the config-3 shape class), ragged lengths, nonzero initial state."""
+    """Many (sequence, head) streams (the config-3 shape class: more scan CTAs than SMs),
+    ragged lengths, nonzero initial state."""
     rng = np.random.default_rng(17)
     H, d = 16, 128
     lens = [1, 64, 100, 130, 7, 0, 257, 64, 65, 33]
