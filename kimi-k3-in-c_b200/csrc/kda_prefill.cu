@@ -95,11 +95,6 @@ struct PrefillLayout {
     static constexpr size_t floats = aqk + (size_t)KC * KC;
 };
 
-__device__ __forceinline__ float load_gate(const float *p, int gate_is_log) {
-    const float x = *p;
-    return gate_is_log ? x : logf(x);
-}
-
 // ---------------------------------------------------------------------------- intra
 // One CTA per (chunk, head), 256 threads, two CTAs per SM. Thread (ic, grp) = (tid % DK,
 // tid / DK) owns channel ic of the tokens [TG grp, TG grp + TG) and keeps their k and q in
@@ -109,7 +104,9 @@ __device__ __forceinline__ float load_gate(const float *p, int gate_is_log) {
 // to the workspace. (I + Akk)^-1 is formed blockwise on 16 x 16 blocks: the four diagonal
 // blocks by forward substitution (one lane per column, no barrier between rows), then the
 // blocks below the diagonal, one block diagonal at a time, from
-// T_ij = -T_ii sum_{k=j}^{i-1} A_ik T_kj.
+// T_ij = -T_ii sum_{k=j}^{i-1} A_ik T_kj. With TC32 (fp32 I/O at d = 128) the block is written
+// in the tensor-core scan's layout (every operand as bf16 hi/lo planes, swizzled as its shared
+// memory image); otherwise as fp32 for kda_chunk_scan.
 template <typename IO, int DK, bool TC32 = false>
 __global__ void __launch_bounds__(256, 2)
 kda_chunk_intra(const ChunkDesc *__restrict__ chunks, const IO *__restrict__ q,
