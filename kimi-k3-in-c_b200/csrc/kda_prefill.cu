@@ -970,15 +970,15 @@ static int run_prefill(k3cuda_ctx *ctx, float *state, void *o, const void *q, co
         memcpy(img.data() + ((char *)d_c0 - wsb), c0.data(), c0.size() * sizeof(int));
         if (int rc = stage_h2d(ctx, wsb, img.data(), img.size())) return rc;
     }
+    const size_t smem1 = ((size_t)2 * KC * (DK + 4) + 2 * KSUB * (DK + 4) + KC * KC + KC + 256) *
+                         sizeof(float);
     if constexpr (std::is_same<IO, __nv_bfloat16>::value && DK == 128) {
         // bf16 operands on the tensor cores (every operand bf16, accumulation fp32)
+        (void)smem1;
         if (nc == 0) return K3CUDA_OK;
         return run_prefill_tc(ctx, state, o, q, k, v, gate, beta, cu[n_seq], n_seq, H, q_scale,
                               gate_is_log, nc, d_table, d_c0, blocks, go);
-    }
-    const size_t smem1 = ((size_t)2 * KC * (DK + 4) + 2 * KSUB * (DK + 4) + KC * KC + KC + 256) *
-                         sizeof(float);
-    if constexpr (std::is_same<IO, float>::value && DK == 128) {
+    } else if constexpr (std::is_same<IO, float>::value && DK == 128) {
         // fp32 q/k/v/o at d = 128: fp32 intra-chunk kernel writing bf16 hi/lo operands, scan on
         // the tensor cores
         if (nc == 0) return K3CUDA_OK;
@@ -998,26 +998,28 @@ static int run_prefill(k3cuda_ctx *ctx, float *state, void *o, const void *q, co
             return after_launch(ctx, "kda_scan_tc32");
         };
         return vec ? launch(kda_scan_tc32<true>) : launch(kda_scan_tc32<false>);
+    } else {
+        // d = 64: both kernels on the CUDA cores
+        if (nc > 0) {
+            if (int rc_ = set_smem(kda_chunk_intra<IO, DK>, (int)smem1)) return rc_;
+            dim3 g1((unsigned)nc, (unsigned)H);
+            kda_chunk_intra<IO, DK><<<g1, 256, smem1, ctx->stream>>>(
+                d_table, (const IO *)q, (const IO *)k, gate, beta, blocks, H, q_scale, gate_is_log);
+            int rc = after_launch(ctx, "kda_chunk_intra");
+            if (rc) return rc;
+        }
+        const size_t smem2 = ((size_t)2 * KC * (DK + 4) + KC * DK + 2 * KC * (KC + 4) + DK +
+                              DK * SCAN_NC + 2 * KC * SCAN_NC) * sizeof(float);
+        if (int rc_ = set_smem(kda_chunk_scan<IO, DK>, (int)smem2)) return rc_;
+        const long long nblk = (long long)n_seq * H * (DK / SCAN_NC);
+        if (nblk > 0) {
+            kda_chunk_scan<IO, DK><<<(unsigned)nblk, 256, smem2, ctx->stream>>>(
+                d_table, d_c0, d_c0 + n_seq + 1, (const IO *)v, blocks, state, (IO *)o, H);
+            return after_launch(ctx, "kda_chunk_scan");
+        }
+        (void)L::floats;
+        return K3CUDA_OK;
     }
-    if (nc > 0) {
-        if (int rc_ = set_smem(kda_chunk_intra<IO, DK>, (int)smem1)) return rc_;
-        dim3 g1((unsigned)nc, (unsigned)H);
-        kda_chunk_intra<IO, DK><<<g1, 256, smem1, ctx->stream>>>(
-            d_table, (const IO *)q, (const IO *)k, gate, beta, blocks, H, q_scale, gate_is_log);
-        int rc = after_launch(ctx, "kda_chunk_intra");
-        if (rc) return rc;
-    }
-    const size_t smem2 = ((size_t)2 * KC * (DK + 4) + KC * DK + 2 * KC * (KC + 4) + DK +
-                          DK * SCAN_NC + 2 * KC * SCAN_NC) * sizeof(float);
-    if (int rc_ = set_smem(kda_chunk_scan<IO, DK>, (int)smem2)) return rc_;
-    const long long nblk = (long long)n_seq * H * (DK / SCAN_NC);
-    if (nblk > 0) {
-        kda_chunk_scan<IO, DK><<<(unsigned)nblk, 256, smem2, ctx->stream>>>(
-            d_table, d_c0, d_c0 + n_seq + 1, (const IO *)v, blocks, state, (IO *)o, H);
-        return after_launch(ctx, "kda_chunk_scan");
-    }
-    (void)L::floats;
-    return K3CUDA_OK;
 }
 
 }  // namespace k3
