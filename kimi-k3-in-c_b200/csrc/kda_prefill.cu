@@ -50,6 +50,9 @@ size_t prefill_tc_block_bytes();
 
 constexpr int KC = 64;        // chunk length
 constexpr int KSUB = 16;      // anchor sub-block
+constexpr float kLog2eF = 1.4426950408889634f;
+// largest growth factor 2^x the anchored form admits inside a sub-block (e^80, in log2 units)
+constexpr float kAnchorLog2 = 80.f * kLog2eF;
 constexpr int SCAN_NC = 32;   // d_v columns per scan CTA
 
 struct ChunkDesc {
@@ -96,7 +99,8 @@ struct PrefillLayout {
 };
 
 // ---------------------------------------------------------------------------- intra
-// One CTA per (chunk, head), 256 threads, two CTAs per SM. Thread (ic, grp) = (tid % DK,
+// One CTA per (chunk, head), 256 threads, two CTAs per SM. G is kept in log2 units, so every
+// exponential below is one 2^x on the special-function unit. Thread (ic, grp) = (tid % DK,
 // tid / DK) owns channel ic of the tokens [TG grp, TG grp + TG) and keeps their k and q in
 // registers; shared memory holds G, the anchored operands of the current sub-block and Akk
 // (about 101 KB at d_k = 128). Rows are padded to DK + 4 floats: the Akk / Aqk products read
@@ -152,7 +156,8 @@ kda_chunk_intra(const ChunkDesc *__restrict__ chunks, const IO *__restrict__ q,
                 const bool in = tg0 + u < cd.len;
                 kr[u] = in ? kr[u] : 0.f;
                 qr[u] = in ? qr[u] * q_scale : 0.f;
-                gr[u] = in ? (gate_is_log ? gr[u] : logf(gr[u])) : 0.f;
+                // G in log2 units: every use below is 2^(difference of G values)
+                gr[u] = in ? (gate_is_log ? gr[u] * kLog2eF : log2f(gr[u])) : 0.f;
             }
         }
         float acc = 0.f;
@@ -178,7 +183,7 @@ kda_chunk_intra(const ChunkDesc *__restrict__ chunks, const IO *__restrict__ q,
         for (int u = 0; u < TG; u++) {
             const int t = tg0 + u;
             const float G = sG[t * LP + ic];
-            const float eg = expf(G);
+            const float eg = sm100::ex2_approx(G);
             if constexpr (TC32) {
                 // Qtil row t at A row 32 (t / 16) + t % 16, Ktil row t sixteen rows after it
                 const int rq = 32 * (t >> 4) + (t & 15);
@@ -186,18 +191,18 @@ kda_chunk_intra(const ChunkDesc *__restrict__ chunks, const IO *__restrict__ q,
                 put_split(ob, W32_KQH, W32_KQL, kq, qr[u] * eg);
                 put_split(ob, W32_KQH, W32_KQL, kq + 16 * 128, kr[u] * eg);
                 put_split(ob, W32_KBH, W32_KBL, (ic >> 6) * 8192 + sm100::swz_elem(t, ic & 63),
-                          kr[u] * expf(GC - G));
+                          kr[u] * sm100::ex2_approx(GC - G));
             } else {
                 out[L::qt + t * DK + ic] = qr[u] * eg;
                 out[L::kt + t * DK + ic] = kr[u] * eg;
-                out[L::kb + t * DK + ic] = kr[u] * expf(GC - G);
+                out[L::kb + t * DK + ic] = kr[u] * sm100::ex2_approx(GC - G);
             }
         }
         if (tid < DK) {
             if constexpr (TC32)
-                reinterpret_cast<float *>(ob + W32_G)[tid] = expf(GC);
+                reinterpret_cast<float *>(ob + W32_G)[tid] = sm100::ex2_approx(GC);
             else
-                out[L::gc + tid] = expf(GC);
+                out[L::gc + tid] = sm100::ex2_approx(GC);
         }
     }
 
@@ -214,10 +219,10 @@ kda_chunk_intra(const ChunkDesc *__restrict__ chunks, const IO *__restrict__ q,
             if (s < ncol) {
                 const float Gs = sG[s * LP + ic];
                 const float ex = Gr - Gs;
-                big |= ex > 80.f;
-                sKh[s * LP + ic] = kr[u] * expf(fminf(ex, 80.f));
+                big |= ex > kAnchorLog2;
+                sKh[s * LP + ic] = kr[u] * sm100::ex2_approx(fminf(ex, kAnchorLog2));
                 if (s >= r0) {
-                    const float f = expf(Gs - Gr);
+                    const float f = sm100::ex2_approx(Gs - Gr);
                     sKa[(s - r0) * LP + ic] = kr[u] * f;
                     sQa[(s - r0) * LP + ic] = qr[u] * f;
                 }
@@ -260,7 +265,8 @@ kda_chunk_intra(const ChunkDesc *__restrict__ chunks, const IO *__restrict__ q,
                         const size_t os = ((size_t)(cd.t0 + s) * H + h) * DK;
                         for (int i = 0; i < DK; i++) {
                             const float f =
-                                expf(sG[t * LP + i] - sG[s * LP + i]) * io<IO>::ld(k + os + i);
+                                sm100::ex2_approx(sG[t * LP + i] - sG[s * LP + i]) *
+                                io<IO>::ld(k + os + i);
                             vk += io<IO>::ld(k + ot + i) * f;
                             vq += io<IO>::ld(q + ot + i) * q_scale * f;
                         }
