@@ -63,8 +63,9 @@ def decode_bytes(B, H, d):
     return state + qkv + gate + out
 
 
-def prefill_bytes(T, H, d):
-    return 3 * T * H * d * 2 + T * H * d * 4 + T * H * 4 + T * H * d * 2
+def prefill_bytes(T, H, d, eb=2):
+    """q, k, v in and o out at `eb` bytes per element, fp32 g and beta."""
+    return 4 * T * H * d * eb + T * H * d * 4 + T * H * 4
 
 
 def mla_bytes(B, ctx, H):
@@ -523,7 +524,7 @@ def prefill_record(args, D: Dist, which, tokens=None, cpu=True):
     hbm, tf, src = peaks()
     per = ms_compute / 1e3 / args.steps
     # fp32 q, k, v and o move twice the bytes of bf16 ones
-    alg = prefill_bytes(T, Hl, d) + (4 * T * Hl * d * 2 if f32 else 0)
+    alg = prefill_bytes(T, Hl, d, 4 if f32 else 2)
     name = cfg["name"] if not tokens else f"kda_prefill_T{T}_reduced"
     if f32:
         name += "_fp32io"

@@ -131,8 +131,9 @@ def test_bench_unit_counts():
     spec.loader.exec_module(b)
     # config 1: fp32 state read + written, bf16 q, k, v, o, fp32 g and beta
     assert b.decode_bytes(256, 32, 128) == 1_086_357_504
-    # config 2: 1536 B per (token, head)
-    assert b.prefill_bytes(32768, 32, 128) == 1_614_807_040 == 32768 * 32 * 1536 + 32768 * 32 * 4
+    # config 2: 1540 B per (token, head) with bf16 q, k, v, o; 2564 B with fp32 ones
+    assert b.prefill_bytes(32768, 32, 128) == 1_614_807_040 == 32768 * 32 * 1540
+    assert b.prefill_bytes(32768, 32, 128, 4) == 2_688_548_864 == 32768 * 32 * 2564
     assert b.mla_bytes(64, 8192, 128) == 642_777_088
     assert b.layer_bytes(1, 7168, 96, 128, 4) == 900_685_824
     assert b.layer_flops(4096, 7168, 96, 128) == 2 * 4096 * (4 * 12288 * 7168 + 96 * 7168 +
